@@ -1,0 +1,181 @@
+/*
+ * llattn.h — C ABI of libllattn.so, the sm_100a kernels of the fused
+ * local + latent attention block (LocalLatentAttention of
+ * Fenix46/local-latent-attention, models.py:61-462).
+ *
+ * Plain C: device pointers, sizes and a stream handle. No torch types.
+ * The caller owns every buffer (outputs, saved tensors and the backward
+ * workspace); the library never allocates or frees device memory and keeps
+ * no device state between calls. Every entry point returns 0 on success and
+ * a nonzero llattn_status otherwise; llattn_last_error() then describes the
+ * failure (thread-local string). Argument errors are detected on the host
+ * before any launch.
+ *
+ * Reference interfaces replaced (paths within the reference project):
+ *   llattn_pool_fwd / llattn_pool_bwd
+ *       LocalLatentAttention._pool_to_latents      models.py:159-214
+ *       LocalLatentAttention._pool_query_blocks    models.py:216-230
+ *   llattn_fwd
+ *       kernels/llattn_op.py:34-84   _call_fwd (launch of llattn_fwd_kernel)
+ *       with the math of models.py:232-305 (local) and :355-438 (latent,
+ *       r_out, gate, mix) — the PyTorch module is the semantic target.
+ *   llattn_bwd
+ *       kernels/llattn_op.py:87-181  _call_bwd (dq and dkv kernels), with
+ *       exact autograd of the same math.
+ *   llattn_bwd_workspace_bytes
+ *       replaces the zero-initialised fp32 grad buffers allocated by
+ *       kernels/llattn_op.py:102-110.
+ */
+#ifndef LLATTN_H_
+#define LLATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LLATTN_VERSION 1
+
+#if defined(__GNUC__)
+#define LLATTN_API __attribute__((visibility("default")))
+#else
+#define LLATTN_API
+#endif
+
+typedef enum llattn_dtype {
+  LLATTN_F32 = 0,  /* activations fp32: exact SIMT path (fp32 FMA)        */
+  LLATTN_BF16 = 1  /* activations bf16: tcgen05 tensor-core path, fp32 acc */
+} llattn_dtype;
+
+typedef enum llattn_status {
+  LLATTN_OK = 0,
+  LLATTN_ERR_ARG = 1,       /* bad shape, pointer, stride or dtype          */
+  LLATTN_ERR_ALIGN = 2,     /* pointer not aligned as the kernel requires   */
+  LLATTN_ERR_LAUNCH = 3,    /* cudaLaunch / cudaFuncSetAttribute failure    */
+  LLATTN_ERR_WORKSPACE = 4, /* workspace too small                          */
+  LLATTN_ERR_DEVICE = 5     /* device-side check failed (debug builds)      */
+} llattn_status;
+
+/* Block hyper-parameters: the ModelConfig fields the block reads
+ * (models.py:21-37) plus the batch geometry of one call. */
+typedef struct llattn_dims {
+  int32_t batch;           /* B                                            */
+  int32_t seq_len;         /* T                                            */
+  int32_t n_heads;         /* H;  d_model = H * head_dim                   */
+  int32_t head_dim;        /* hd                                           */
+  int32_t latent_heads;    /* Lh                                           */
+  int32_t latent_head_dim; /* ldh; latent_d_model = Lh * ldh               */
+  int32_t window;          /* local_window W (> 0)                         */
+  int32_t local_block;     /* local_block_size (default 256)              */
+  int32_t latent_tokens;   /* latent_tokens Nl (upper bound on chunks)    */
+  int32_t query_block;     /* latent_query_block_size; <= 1 = token-wise  */
+  int32_t dtype;           /* llattn_dtype of activations                 */
+  float gate_bias;         /* added to the local gate logit (0 = reference) */
+} llattn_dims;
+
+/* Quantities derived from llattn_dims exactly as models.py derives them. */
+typedef struct llattn_geom {
+  int32_t chunk;        /* cs  = ceil(T / min(Nl, T))          models.py:175-183 */
+  int32_t n_chunks;     /* Nc  = ceil(T / cs)                                  */
+  int32_t local_span;   /* bsL = min(T, max(W, local_block))   models.py:249   */
+  int32_t qblock;       /* bs  = min(T, QB) if QB > 1 else 1   models.py:218   */
+  int32_t n_qrows;      /* Tq  = ceil(T / bs)                                  */
+} llattn_geom;
+
+/* Forward of the attention core (everything between the projections):
+ *   local  = windowed causal softmax(q k^T / sqrt(hd)) v   (per head)
+ *   lat    = causal-chunk softmax(rq gk^T / sqrt(ldh)) gv  (per latent head)
+ *   remote = lat W_rout^T + b_rout (broadcast per query block)
+ *   w      = sigmoid(local.g_l + gate_bias - remote.g_r)
+ *   mixed  = w local + (1 - w) remote
+ * Layouts (row-major, element strides implied):
+ *   qkv      [B, T, 3, H, hd]  dtype   (the qkv_proj output, un-split)
+ *   rq       [B, Tq, Lh, ldh]  dtype   (the rq_proj output)
+ *   gkv      [B, Nc, 2, Lh, ldh] dtype (the rkv_proj output of pooled x)
+ *   w_rout   [H*hd, Lh*ldh]    dtype;  b_rout [H*hd] fp32
+ *   g_local, g_remote [hd] fp32
+ * Outputs: mixed [B, T, H*hd] dtype. Saved for backward: local_out
+ * [B, T, H*hd] dtype, lse [B, H, T] fp32, lat [B, Tq, Lh*ldh] dtype,
+ * lat_lse [B, Lh, Tq] fp32. */
+typedef struct llattn_fwd_args {
+  llattn_dims dims;
+  const void* qkv;
+  const void* rq;
+  const void* gkv;
+  const void* w_rout;
+  const float* b_rout;
+  const float* g_local;
+  const float* g_remote;
+  void* mixed;
+  void* local_out;
+  float* lse;
+  void* lat;
+  float* lat_lse;
+} llattn_fwd_args;
+
+/* Backward of llattn_fwd. Inputs are the forward inputs, the saved tensors
+ * and dmixed [B, T, H*hd] dtype. Outputs (all fully overwritten):
+ *   dqkv [B, T, 3, H, hd] dtype, drq [B, Tq, Lh, ldh] dtype,
+ *   dgkv [B, Nc, 2, Lh, ldh] dtype, dw_rout [H*hd, Lh*ldh] fp32,
+ *   db_rout [H*hd] fp32, dg_local [hd] fp32, dg_remote [hd] fp32.
+ * workspace: device buffer of at least llattn_bwd_workspace_bytes(&dims)
+ * bytes, 256-byte aligned; its contents need no initialisation. */
+typedef struct llattn_bwd_args {
+  llattn_dims dims;
+  const void* qkv;
+  const void* rq;
+  const void* gkv;
+  const void* w_rout;
+  const float* b_rout;
+  const float* g_local;
+  const float* g_remote;
+  const void* local_out;
+  const float* lse;
+  const void* lat;
+  const float* lat_lse;
+  const void* dmixed;
+  void* dqkv;
+  void* drq;
+  void* dgkv;
+  float* dw_rout;
+  float* db_rout;
+  float* dg_local;
+  float* dg_remote;
+  void* workspace;
+  size_t workspace_bytes;
+} llattn_bwd_args;
+
+/* Pool modes of llattn_pool_fwd / llattn_pool_bwd. */
+typedef enum llattn_pool_mode {
+  LLATTN_POOL_CHUNKS = 0, /* chunk means of x over cs tokens, last partial
+                             chunk over its true count   (models.py:159-214) */
+  LLATTN_POOL_QBLOCKS = 1 /* query-block means over bs tokens, zero padding
+                             counted                     (models.py:216-230) */
+} llattn_pool_mode;
+
+LLATTN_API int llattn_version(void);
+LLATTN_API const char* llattn_last_error(void);
+
+/* Fills *out from *dims. Returns LLATTN_ERR_ARG for inconsistent dims. */
+LLATTN_API int llattn_geometry(const llattn_dims* dims, llattn_geom* out);
+
+/* Workspace needed by llattn_bwd for these dims (0 on bad dims). */
+LLATTN_API size_t llattn_bwd_workspace_bytes(const llattn_dims* dims);
+
+/* x [B, T, d] dtype -> pooled [B, rows, d] dtype, rows = Nc or Tq. */
+LLATTN_API int llattn_pool_fwd(const llattn_dims* dims, int mode, const void* x,
+                    void* pooled, int64_t d, void* stream);
+/* dpooled [B, rows, d] -> dx [B, T, d] (overwritten). */
+LLATTN_API int llattn_pool_bwd(const llattn_dims* dims, int mode, const void* dpooled,
+                    void* dx, int64_t d, void* stream);
+
+LLATTN_API int llattn_fwd(const llattn_fwd_args* args, void* stream);
+LLATTN_API int llattn_bwd(const llattn_bwd_args* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLATTN_H_ */

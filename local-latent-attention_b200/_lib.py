@@ -1,0 +1,106 @@
+"""ctypes binding of libllattn.so (the C ABI declared in include/llattn.h).
+
+The library is built in-tree by ``csrc/build.py``; loading fails loudly when
+it is missing — there is no fallback implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libllattn.so")
+
+F32, BF16 = 0, 1
+POOL_CHUNKS, POOL_QBLOCKS = 0, 1
+
+EXPORTED = (
+    "llattn_version", "llattn_last_error", "llattn_geometry", "llattn_bwd_workspace_bytes",
+    "llattn_pool_fwd", "llattn_pool_bwd", "llattn_fwd", "llattn_bwd",
+)
+
+
+class Dims(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32), ("seq_len", ctypes.c_int32), ("n_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("latent_heads", ctypes.c_int32),
+        ("latent_head_dim", ctypes.c_int32), ("window", ctypes.c_int32),
+        ("local_block", ctypes.c_int32), ("latent_tokens", ctypes.c_int32),
+        ("query_block", ctypes.c_int32), ("dtype", ctypes.c_int32), ("gate_bias", ctypes.c_float),
+    ]
+
+
+class Geom(ctypes.Structure):
+    _fields_ = [("chunk", ctypes.c_int32), ("n_chunks", ctypes.c_int32),
+                ("local_span", ctypes.c_int32), ("qblock", ctypes.c_int32),
+                ("n_qrows", ctypes.c_int32)]
+
+
+_vp = ctypes.c_void_p
+_fp = ctypes.c_void_p  # float* passed as raw addresses
+
+
+class FwdArgs(ctypes.Structure):
+    _fields_ = [("dims", Dims), ("qkv", _vp), ("rq", _vp), ("gkv", _vp), ("w_rout", _vp),
+                ("b_rout", _fp), ("g_local", _fp), ("g_remote", _fp), ("mixed", _vp),
+                ("local_out", _vp), ("lse", _fp), ("lat", _vp), ("lat_lse", _fp)]
+
+
+class BwdArgs(ctypes.Structure):
+    _fields_ = [("dims", Dims), ("qkv", _vp), ("rq", _vp), ("gkv", _vp), ("w_rout", _vp),
+                ("b_rout", _fp), ("g_local", _fp), ("g_remote", _fp), ("local_out", _vp),
+                ("lse", _fp), ("lat", _vp), ("lat_lse", _fp), ("dmixed", _vp), ("dqkv", _vp),
+                ("drq", _vp), ("dgkv", _vp), ("dw_rout", _fp), ("db_rout", _fp),
+                ("dg_local", _fp), ("dg_remote", _fp), ("workspace", _vp),
+                ("workspace_bytes", ctypes.c_size_t)]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libllattn.so once; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with "
+                "`python local-latent-attention_b200/csrc/build.py` (or __graft_entry__.build())")
+        L = ctypes.CDLL(LIB_PATH)
+        L.llattn_version.restype = ctypes.c_int
+        L.llattn_last_error.restype = ctypes.c_char_p
+        L.llattn_geometry.argtypes = [ctypes.POINTER(Dims), ctypes.POINTER(Geom)]
+        L.llattn_geometry.restype = ctypes.c_int
+        L.llattn_bwd_workspace_bytes.argtypes = [ctypes.POINTER(Dims)]
+        L.llattn_bwd_workspace_bytes.restype = ctypes.c_size_t
+        for name in ("llattn_pool_fwd", "llattn_pool_bwd"):
+            fn = getattr(L, name)
+            fn.argtypes = [ctypes.POINTER(Dims), ctypes.c_int, _vp, _vp, ctypes.c_int64, _vp]
+            fn.restype = ctypes.c_int
+        L.llattn_fwd.argtypes = [ctypes.POINTER(FwdArgs), _vp]
+        L.llattn_fwd.restype = ctypes.c_int
+        L.llattn_bwd.argtypes = [ctypes.POINTER(BwdArgs), _vp]
+        L.llattn_bwd.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = lib().llattn_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what} failed (status {rc}): {msg}")
+
+
+def make_dims(batch, seq_len, n_heads=1, head_dim=1, latent_heads=1, latent_head_dim=1,
+              window=1, local_block=256, latent_tokens=1, query_block=0, dtype=F32,
+              gate_bias=0.0) -> Dims:
+    return Dims(int(batch), int(seq_len), int(n_heads), int(head_dim), int(latent_heads),
+                int(latent_head_dim), int(window), int(local_block), int(latent_tokens),
+                int(query_block), int(dtype), float(gate_bias))
+
+
+def geometry(dims: Dims) -> Geom:
+    g = Geom()
+    check(lib().llattn_geometry(ctypes.byref(dims), ctypes.byref(g)), "llattn_geometry")
+    return g

@@ -1,0 +1,266 @@
+// C ABI of libllattn (declared in include/llattn.h): host-side validation,
+// geometry, backward workspace layout and kernel dispatch. No allocation, no
+// host synchronisation, no global device state.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace llattn {
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return LLATTN_OK;
+  return fail(LLATTN_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// models.py:175-183 (cs, Nc), :249 (bsL), :216-219 (bs, Tq).
+int make_geom(const llattn_dims* d, Geom* g) {
+  if (!d) return fail(LLATTN_ERR_ARG, "dims is NULL");
+  if (d->batch < 1 || d->seq_len < 1) return fail(LLATTN_ERR_ARG, "batch and seq_len must be >= 1");
+  if (d->seq_len > 65535) return fail(LLATTN_ERR_ARG, "seq_len %d exceeds 65535", d->seq_len);
+  if (d->n_heads < 1 || d->head_dim < 1 || d->head_dim > 128)
+    return fail(LLATTN_ERR_ARG, "n_heads >= 1 and 1 <= head_dim <= 128 required (head_dim=%d)", d->head_dim);
+  if (d->latent_heads < 1 || d->latent_head_dim < 1 || d->latent_head_dim > 64)
+    return fail(LLATTN_ERR_ARG, "latent_heads >= 1 and 1 <= latent_head_dim <= 64 required");
+  if (d->latent_heads * d->latent_head_dim > 128)
+    return fail(LLATTN_ERR_ARG, "latent_d_model = %d exceeds 128", d->latent_heads * d->latent_head_dim);
+  if (d->window < 1) return fail(LLATTN_ERR_ARG, "local_window must be positive");
+  if (d->latent_tokens < 1) return fail(LLATTN_ERR_ARG, "latent_tokens must be positive");
+  if (d->dtype != LLATTN_F32 && d->dtype != LLATTN_BF16) return fail(LLATTN_ERR_ARG, "unknown dtype %d", d->dtype);
+  if ((int64_t)d->n_heads * d->head_dim > (1 << 20)) return fail(LLATTN_ERR_ARG, "d_model too large");
+  const int T = d->seq_len;
+  g->B = d->batch;
+  g->T = T;
+  g->H = d->n_heads;
+  g->hd = d->head_dim;
+  g->d = d->n_heads * d->head_dim;
+  g->Lh = d->latent_heads;
+  g->ldh = d->latent_head_dim;
+  g->Ld = d->latent_heads * d->latent_head_dim;
+  g->W = d->window;
+  g->bsL = std::min(T, std::max(d->window, d->local_block));
+  const int target = std::min(d->latent_tokens, T);
+  g->cs = cdiv(T, target);
+  g->Nc = cdiv(T, g->cs);
+  g->qbs = d->query_block > 1 ? std::min(T, d->query_block) : 1;
+  g->Tq = cdiv(T, g->qbs);
+  g->gate_bias = d->gate_bias;
+  g->scale = 1.0f / sqrtf((float)g->hd);
+  g->lat_scale = 1.0f / sqrtf((float)g->ldh);
+  return LLATTN_OK;
+}
+
+// Backward workspace, every region 256-byte aligned.
+struct BwdLayout {
+  size_t dl, delta, drow, dlat, lat_delta, dg_part, dg_sum, dw_part, dgkv_part, total;
+  int gate_tok, n_gate_cta, n_split_w, n_split_lat;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+BwdLayout bwd_layout(const Geom& g, int elt) {
+  BwdLayout L;
+  L.gate_tok = 16;
+  L.n_gate_cta = g.B * cdiv(g.T, L.gate_tok);
+  const int rows = g.B * g.Tq;
+  L.n_split_w = std::max(1, std::min(cdiv(rows, 32), cdiv(2 * 148, cdiv(g.d, 32))));
+  const int lat_ctas = g.B * g.Lh * cdiv(g.Nc, 64);
+  L.n_split_lat = std::max(1, std::min(cdiv(g.Tq, 32), cdiv(2 * 148, lat_ctas)));
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
+  const size_t BTd = (size_t)g.B * g.T * g.d;
+  L.dl = take(BTd * elt);
+  L.delta = take(sizeof(float) * g.B * g.H * g.T);
+  L.drow = take(sizeof(float) * BTd);
+  L.dlat = take(sizeof(float) * (size_t)rows * g.Ld);
+  L.lat_delta = take(sizeof(float) * (size_t)g.B * g.Lh * g.Tq);
+  L.dg_part = take(sizeof(float) * (size_t)L.n_gate_cta * 2 * g.hd);
+  L.dg_sum = take(sizeof(float) * 2 * g.hd);
+  L.dw_part = take(sizeof(float) * (size_t)L.n_split_w * g.d * (g.Ld + 1));
+  L.dgkv_part = take(sizeof(float) * (size_t)L.n_split_lat * g.B * g.Nc * 2 * g.Ld);
+  L.total = off;
+  return L;
+}
+
+bool al(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+template <typename T>
+int run_fwd(const Geom& g, const llattn_fwd_args* a, cudaStream_t s) {
+  const T* qkv = static_cast<const T*>(a->qkv);
+  int rc = check_launch(launch_latent_fwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv),
+                                             static_cast<T*>(a->lat), a->lat_lse, s),
+                        "latent_fwd");
+  if (rc) return rc;
+  if (sm100::fwd_supported(g, sizeof(T))) {
+    rc = check_launch(sm100::launch_local_fwd(g, a->qkv, a->local_out, a->lse, s), "local_fwd_sm100");
+  } else {
+    rc = check_launch(launch_local_fwd_simt<T>(g, qkv, static_cast<T*>(a->local_out), a->lse, s),
+                      "local_fwd_simt");
+  }
+  if (rc) return rc;
+  return check_launch(launch_gate_fwd<T>(g, static_cast<const T*>(a->local_out), static_cast<const T*>(a->lat),
+                                         static_cast<const T*>(a->w_rout), a->b_rout, a->g_local, a->g_remote,
+                                         static_cast<T*>(a->mixed), s),
+                      "gate_fwd");
+}
+
+template <typename T>
+int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
+  const BwdLayout L = bwd_layout(g, sizeof(T));
+  char* ws = static_cast<char*>(a->workspace);
+  T* dl = reinterpret_cast<T*>(ws + L.dl);
+  float* delta = reinterpret_cast<float*>(ws + L.delta);
+  float* drow = reinterpret_cast<float*>(ws + L.drow);
+  float* dlat = reinterpret_cast<float*>(ws + L.dlat);
+  float* lat_delta = reinterpret_cast<float*>(ws + L.lat_delta);
+  float* dg_part = reinterpret_cast<float*>(ws + L.dg_part);
+  float* dg_sum = reinterpret_cast<float*>(ws + L.dg_sum);
+  float* dw_part = reinterpret_cast<float*>(ws + L.dw_part);
+  float* dgkv_part = reinterpret_cast<float*>(ws + L.dgkv_part);
+  const T* lat = static_cast<const T*>(a->lat);
+  const T* w_rout = static_cast<const T*>(a->w_rout);
+
+  int rc = check_launch(
+      launch_gate_bwd<T>(g, static_cast<const T*>(a->local_out), lat, w_rout, a->b_rout, a->g_local, a->g_remote,
+                         static_cast<const T*>(a->dmixed), dl, delta, drow, dg_part, L.gate_tok, s),
+      "gate_bwd");
+  if (rc) return rc;
+  if (sm100::bwd_supported(g, sizeof(T))) {
+    rc = check_launch(sm100::launch_local_bwd(g, a->qkv, dl, a->lse, delta, a->dqkv, s), "local_bwd_sm100");
+  } else {
+    rc = check_launch(launch_local_bwd_simt<T>(g, static_cast<const T*>(a->qkv), dl, a->lse, delta,
+                                               static_cast<T*>(a->dqkv), s),
+                      "local_bwd_simt");
+  }
+  if (rc) return rc;
+  rc = check_launch(launch_rout_bwd<T>(g, drow, lat, w_rout, dlat, dw_part, L.n_split_w, s), "rout_bwd");
+  if (rc) return rc;
+  rc = check_launch(launch_reduce_rows(dw_part, L.n_split_w, (int64_t)g.d * g.Ld, a->dw_rout, s), "reduce_dw");
+  if (rc) return rc;
+  rc = check_launch(launch_reduce_rows(dw_part + (size_t)L.n_split_w * g.d * g.Ld, L.n_split_w, g.d, a->db_rout, s),
+                    "reduce_db");
+  if (rc) return rc;
+  // dg partials are [cta][2*hd] (local half, remote half)
+  rc = check_launch(launch_reduce_rows(dg_part, L.n_gate_cta, 2 * g.hd, dg_sum, s), "reduce_dg");
+  if (rc) return rc;
+  rc = check_launch(cudaMemcpyAsync(a->dg_local, dg_sum, sizeof(float) * g.hd, cudaMemcpyDeviceToDevice, s),
+                    "copy dg_local");
+  if (rc) return rc;
+  rc = check_launch(cudaMemcpyAsync(a->dg_remote, dg_sum + g.hd, sizeof(float) * g.hd,
+                                    cudaMemcpyDeviceToDevice, s),
+                    "copy dg_remote");
+  if (rc) return rc;
+  rc = check_launch(launch_latent_bwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv), lat,
+                                         a->lat_lse, dlat, static_cast<T*>(a->drq), dgkv_part, L.n_split_lat,
+                                         lat_delta, s),
+                    "latent_bwd");
+  if (rc) return rc;
+  return check_launch(launch_latent_reduce<T>(g, dgkv_part, L.n_split_lat, static_cast<T*>(a->dgkv), s),
+                      "latent_reduce");
+}
+
+}  // namespace
+}  // namespace llattn
+
+using namespace llattn;
+
+extern "C" {
+
+int llattn_version(void) { return LLATTN_VERSION; }
+
+const char* llattn_last_error(void) { return g_err; }
+
+int llattn_geometry(const llattn_dims* dims, llattn_geom* out) {
+  Geom g;
+  int rc = make_geom(dims, &g);
+  if (rc) return rc;
+  if (!out) return fail(LLATTN_ERR_ARG, "out is NULL");
+  out->chunk = g.cs;
+  out->n_chunks = g.Nc;
+  out->local_span = g.bsL;
+  out->qblock = g.qbs;
+  out->n_qrows = g.Tq;
+  return LLATTN_OK;
+}
+
+size_t llattn_bwd_workspace_bytes(const llattn_dims* dims) {
+  Geom g;
+  if (make_geom(dims, &g)) return 0;
+  return bwd_layout(g, dims->dtype == LLATTN_BF16 ? 2 : 4).total;
+}
+
+int llattn_pool_fwd(const llattn_dims* dims, int mode, const void* x, void* pooled, int64_t d, void* stream) {
+  Geom g;
+  int rc = make_geom(dims, &g);
+  if (rc) return rc;
+  if (!x || !pooled) return fail(LLATTN_ERR_ARG, "pool_fwd: NULL pointer");
+  if (mode != LLATTN_POOL_CHUNKS && mode != LLATTN_POOL_QBLOCKS) return fail(LLATTN_ERR_ARG, "bad pool mode");
+  if (d < 1) return fail(LLATTN_ERR_ARG, "pool_fwd: d must be >= 1");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dims->dtype == LLATTN_BF16)
+    return check_launch(launch_pool_fwd<bf16>(g, mode, (const bf16*)x, (bf16*)pooled, d, s), "pool_fwd");
+  return check_launch(launch_pool_fwd<float>(g, mode, (const float*)x, (float*)pooled, d, s), "pool_fwd");
+}
+
+int llattn_pool_bwd(const llattn_dims* dims, int mode, const void* dpooled, void* dx, int64_t d, void* stream) {
+  Geom g;
+  int rc = make_geom(dims, &g);
+  if (rc) return rc;
+  if (!dpooled || !dx) return fail(LLATTN_ERR_ARG, "pool_bwd: NULL pointer");
+  if (mode != LLATTN_POOL_CHUNKS && mode != LLATTN_POOL_QBLOCKS) return fail(LLATTN_ERR_ARG, "bad pool mode");
+  if (d < 1) return fail(LLATTN_ERR_ARG, "pool_bwd: d must be >= 1");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dims->dtype == LLATTN_BF16)
+    return check_launch(launch_pool_bwd<bf16>(g, mode, (const bf16*)dpooled, (bf16*)dx, d, s), "pool_bwd");
+  return check_launch(launch_pool_bwd<float>(g, mode, (const float*)dpooled, (float*)dx, d, s), "pool_bwd");
+}
+
+int llattn_fwd(const llattn_fwd_args* a, void* stream) {
+  if (!a) return fail(LLATTN_ERR_ARG, "args is NULL");
+  Geom g;
+  int rc = make_geom(&a->dims, &g);
+  if (rc) return rc;
+  if (!a->qkv || !a->rq || !a->gkv || !a->w_rout || !a->b_rout || !a->g_local || !a->g_remote || !a->mixed ||
+      !a->local_out || !a->lse || !a->lat || !a->lat_lse)
+    return fail(LLATTN_ERR_ARG, "llattn_fwd: NULL pointer in args");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a->dims.dtype == LLATTN_BF16) return run_fwd<bf16>(g, a, s);
+  return run_fwd<float>(g, a, s);
+}
+
+int llattn_bwd(const llattn_bwd_args* a, void* stream) {
+  if (!a) return fail(LLATTN_ERR_ARG, "args is NULL");
+  Geom g;
+  int rc = make_geom(&a->dims, &g);
+  if (rc) return rc;
+  if (!a->qkv || !a->rq || !a->gkv || !a->w_rout || !a->b_rout || !a->g_local || !a->g_remote ||
+      !a->local_out || !a->lse || !a->lat || !a->lat_lse || !a->dmixed || !a->dqkv || !a->drq || !a->dgkv ||
+      !a->dw_rout || !a->db_rout || !a->dg_local || !a->dg_remote)
+    return fail(LLATTN_ERR_ARG, "llattn_bwd: NULL pointer in args");
+  const size_t need = bwd_layout(g, a->dims.dtype == LLATTN_BF16 ? 2 : 4).total;
+  if (!a->workspace || a->workspace_bytes < need)
+    return fail(LLATTN_ERR_WORKSPACE, "llattn_bwd: workspace of %zu bytes needed, %zu given", need,
+                a->workspace_bytes);
+  if (!al(a->workspace, 256)) return fail(LLATTN_ERR_ALIGN, "llattn_bwd: workspace must be 256-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a->dims.dtype == LLATTN_BF16) return run_bwd<bf16>(g, a, s);
+  return run_bwd<float>(g, a, s);
+}
+
+}  // extern "C"

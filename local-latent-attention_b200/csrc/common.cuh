@@ -1,0 +1,124 @@
+// Shared device helpers of libllattn: geometry, masks, dtype conversion.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "llattn.h"
+
+namespace llattn {
+
+using bf16 = __nv_bfloat16;
+
+// Geometry of one call, derived once on the host (see api.cu: make_geom).
+// Every size the kernels need, in the reference's terms:
+//   d = H*hd, Ld = Lh*ldh, bsL = local query-block span (models.py:249),
+//   cs/Nc = latent chunk size/count (models.py:175-183),
+//   qbs/Tq = latent query block size/row count (models.py:216-219; 1/T when
+//   queries are token-wise).
+struct Geom {
+  int B, T, H, hd, d, Lh, ldh, Ld;
+  int W, bsL, cs, Nc, qbs, Tq;
+  float gate_bias;
+  float scale;      // 1/sqrt(hd)
+  float lat_scale;  // 1/sqrt(ldh)
+};
+
+__host__ __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+// First key visible from query t (inclusive); the last is t-1. Mask of
+// models.py:245-292: 0 < t-j <= W and j >= max(0, qs(t)-W+1), where qs(t) is
+// the first row of t's bsL-block.
+__host__ __device__ __forceinline__ int local_lo(const Geom& g, int t) {
+  int qs = (t / g.bsL) * g.bsL;
+  int lo = t - g.W;
+  int lo2 = qs - g.W + 1;
+  lo = lo > lo2 ? lo : lo2;
+  return lo > 0 ? lo : 0;
+}
+
+__host__ __device__ __forceinline__ bool local_visible(const Geom& g, int t, int j) {
+  return j < t && j >= local_lo(g, t);
+}
+
+// Latent chunk count visible from latent query row r (chunks j < qid(r)),
+// models.py:208-212, 227-229, 363-365.
+__host__ __device__ __forceinline__ int row_qid(const Geom& g, int r) {
+  int t = r * g.qbs;
+  int c = t / g.cs;
+  return c < g.Nc - 1 ? c : g.Nc - 1;
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<bf16>(bf16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ bf16 from_f<bf16>(float v) { return __float2bfloat16_rn(v); }
+
+template <typename T>
+__device__ __forceinline__ float ldf(const T* p) { return to_f<T>(*p); }
+template <typename T>
+__device__ __forceinline__ void stf(T* p, float v) { *p = from_f<T>(v); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Launch helpers implemented per .cu file; all return cudaError_t of the
+// launch so api.cu can turn it into a status.
+template <typename T>
+cudaError_t launch_pool_fwd(const Geom& g, int mode, const T* x, T* out, int64_t d, cudaStream_t s);
+template <typename T>
+cudaError_t launch_pool_bwd(const Geom& g, int mode, const T* dout, T* dx, int64_t d, cudaStream_t s);
+
+template <typename T>
+cudaError_t launch_latent_fwd(const Geom& g, const T* rq, const T* gkv, T* lat, float* lat_lse,
+                              cudaStream_t s);
+// Latent backward: drq (direct) and per-row-split partials of dgk/dgv.
+template <typename T>
+cudaError_t launch_latent_bwd(const Geom& g, const T* rq, const T* gkv, const T* lat,
+                              const float* lat_lse, const float* dlat, T* drq, float* dgkv_part,
+                              int n_split, float* delta_ws, cudaStream_t s);
+template <typename T>
+cudaError_t launch_latent_reduce(const Geom& g, const float* dgkv_part, int n_split, T* dgkv,
+                                 cudaStream_t s);
+
+template <typename T>
+cudaError_t launch_local_fwd_simt(const Geom& g, const T* qkv, T* local_out, float* lse,
+                                  cudaStream_t s);
+template <typename T>
+cudaError_t launch_local_bwd_simt(const Geom& g, const T* qkv, const T* dl, const float* lse,
+                                  const float* delta, T* dqkv, cudaStream_t s);
+
+template <typename T>
+cudaError_t launch_gate_fwd(const Geom& g, const T* local_out, const T* lat, const T* w_rout,
+                            const float* b_rout, const float* g_local, const float* g_remote,
+                            T* mixed, cudaStream_t s);
+template <typename T>
+cudaError_t launch_gate_bwd(const Geom& g, const T* local_out, const T* lat, const T* w_rout,
+                            const float* b_rout, const float* g_local, const float* g_remote,
+                            const T* dmixed, T* dl, float* delta, float* drow, float* dg_part,
+                            int tok_per_cta, cudaStream_t s);
+template <typename T>
+cudaError_t launch_rout_bwd(const Geom& g, const float* drow, const T* lat, const T* w_rout,
+                            float* dlat, float* dw_part, int n_split, cudaStream_t s);
+cudaError_t launch_reduce_rows(const float* part, int n_part, int64_t n, float* out,
+                               cudaStream_t s);
+
+}  // namespace llattn

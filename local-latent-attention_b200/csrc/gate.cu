@@ -1,0 +1,315 @@
+// Remote projection, gate and mix (models.py:392-438), forward and backward,
+// plus the backward of the r_out projection. Exact fp32 path (SIMT FMAs).
+//
+//   remote[t] = lat[row(t)] W_rout^T + b_rout            (row(t) = t / qbs)
+//   w_h       = sigmoid(local_h.g_l + gate_bias - remote_h.g_r)
+//   mixed_h   = w_h local_h + (1 - w_h) remote_h
+// Backward, per token and head, with dm = dmixed_h:
+//   ds = (dm.(local_h - remote_h)) w (1 - w)
+//   dlocal  = w dm + ds g_l          (written for the local-branch backward)
+//   dremote = (1 - w) dm - ds g_r    (fp32, reduced over query blocks later)
+//   dg_l += ds local_h,  dg_r -= ds remote_h
+//   D_h = dlocal.local_h             (the local backward's row term)
+#include <math.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace llattn {
+namespace {
+
+constexpr int NT = 128;
+
+template <typename T>
+__device__ __forceinline__ void remote_row(const Geom& g, const float* slat, const T* __restrict__ w_rout,
+                                           const float* __restrict__ b_rout, float* sR) {
+  for (int c = threadIdx.x; c < g.d; c += NT) {
+    const T* wr = w_rout + (int64_t)c * g.Ld;
+    float a = b_rout[c];
+    for (int k = 0; k < g.Ld; ++k) a = fmaf(slat[k], to_f<T>(wr[k]), a);
+    sR[c] = a;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NT) gate_fwd_kernel(Geom g, const T* __restrict__ local_out,
+                                                      const T* __restrict__ lat,
+                                                      const T* __restrict__ w_rout,
+                                                      const float* __restrict__ b_rout,
+                                                      const float* __restrict__ gl,
+                                                      const float* __restrict__ gr,
+                                                      T* __restrict__ mixed) {
+  extern __shared__ float smem_gf[];
+  float* sR = smem_gf;
+  float* sL = sR + g.d;
+  float* slat = sL + g.d;
+  float* sw = slat + g.Ld;
+  const int t = blockIdx.x, b = blockIdx.y, r = t / g.qbs;
+  const int64_t row = (int64_t)b * g.T + t;
+  for (int k = threadIdx.x; k < g.Ld; k += NT) slat[k] = to_f<T>(lat[((int64_t)b * g.Tq + r) * g.Ld + k]);
+  for (int c = threadIdx.x; c < g.d; c += NT) sL[c] = to_f<T>(local_out[row * g.d + c]);
+  __syncthreads();
+  remote_row<T>(g, slat, w_rout, b_rout, sR);
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (int h = warp; h < g.H; h += NT / 32) {
+    float sl = 0.f, sr = 0.f;
+    for (int e = lane; e < g.hd; e += 32) {
+      sl = fmaf(sL[h * g.hd + e], gl[e], sl);
+      sr = fmaf(sR[h * g.hd + e], gr[e], sr);
+    }
+    sl = warp_sum(sl);
+    sr = warp_sum(sr);
+    if (lane == 0) sw[h] = 1.f / (1.f + expf(-(sl + g.gate_bias - sr)));
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < g.d; c += NT) {
+    const float w = sw[c / g.hd];
+    mixed[row * g.d + c] = from_f<T>(w * sL[c] + (1.f - w) * sR[c]);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NT) gate_bwd_kernel(
+    Geom g, const T* __restrict__ local_out, const T* __restrict__ lat, const T* __restrict__ w_rout,
+    const float* __restrict__ b_rout, const float* __restrict__ gl, const float* __restrict__ gr,
+    const T* __restrict__ dmixed, T* __restrict__ dl, float* __restrict__ delta,
+    float* __restrict__ drow, float* __restrict__ dg_part, int tok_per_cta) {
+  extern __shared__ float smem_gb[];
+  float* sR = smem_gb;
+  float* sL = sR + g.d;
+  float* sdm = sL + g.d;
+  float* slat = sdm + g.d;
+  float* sds = slat + g.Ld;
+  const int b = blockIdx.y;
+  const int ta = blockIdx.x * tok_per_cta, tb = min(g.T, ta + tok_per_cta);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  float agl = 0.f, agr = 0.f;  // thread e = threadIdx.x (hd <= 128)
+  for (int t = ta; t < tb; ++t) {
+    const int r = t / g.qbs;
+    const int64_t row = (int64_t)b * g.T + t;
+    __syncthreads();
+    for (int k = threadIdx.x; k < g.Ld; k += NT) slat[k] = to_f<T>(lat[((int64_t)b * g.Tq + r) * g.Ld + k]);
+    for (int c = threadIdx.x; c < g.d; c += NT) {
+      sL[c] = to_f<T>(local_out[row * g.d + c]);
+      sdm[c] = to_f<T>(dmixed[row * g.d + c]);
+    }
+    __syncthreads();
+    remote_row<T>(g, slat, w_rout, b_rout, sR);
+    __syncthreads();
+    for (int h = warp; h < g.H; h += NT / 32) {
+      const float* L = sL + h * g.hd;
+      const float* R = sR + h * g.hd;
+      const float* dm = sdm + h * g.hd;
+      float sl = 0.f, sr = 0.f, dw = 0.f;
+      for (int e = lane; e < g.hd; e += 32) {
+        sl = fmaf(L[e], gl[e], sl);
+        sr = fmaf(R[e], gr[e], sr);
+        dw = fmaf(dm[e], L[e] - R[e], dw);
+      }
+      sl = warp_sum(sl);
+      sr = warp_sum(sr);
+      dw = warp_sum(dw);
+      const float w = 1.f / (1.f + expf(-(sl + g.gate_bias - sr)));
+      const float ds = dw * w * (1.f - w);
+      float dsum = 0.f;
+      for (int e = lane; e < g.hd; e += 32) {
+        const float dlv = w * dm[e] + ds * gl[e];
+        const T dlt = from_f<T>(dlv);
+        dl[row * g.d + h * g.hd + e] = dlt;
+        dsum = fmaf(to_f<T>(dlt), L[e], dsum);
+        drow[row * g.d + h * g.hd + e] = (1.f - w) * dm[e] - ds * gr[e];
+      }
+      dsum = warp_sum(dsum);
+      if (lane == 0) {
+        sds[h] = ds;
+        delta[((int64_t)b * g.H + h) * g.T + t] = dsum;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < g.hd) {
+      const int e = threadIdx.x;
+      for (int h = 0; h < g.H; ++h) {
+        agl = fmaf(sds[h], sL[h * g.hd + e], agl);
+        agr = fmaf(-sds[h], sR[h * g.hd + e], agr);
+      }
+    }
+  }
+  if (threadIdx.x < g.hd) {
+    float* dst = dg_part + ((int64_t)b * gridDim.x + blockIdx.x) * 2 * g.hd;
+    dst[threadIdx.x] = agl;
+    dst[g.hd + threadIdx.x] = agr;
+  }
+}
+
+// dlat[row] = (sum over the row's tokens of dremote) . W_rout
+template <int LM>
+__global__ void __launch_bounds__(256) rout_dlat_kernel(Geom g, const float* __restrict__ drow,
+                                                        const void* __restrict__ w_rout_v, int w_bf16,
+                                                        float* __restrict__ dlat) {
+  extern __shared__ float smem_rd[];
+  float(*sdr)[64 + 1] = reinterpret_cast<float(*)[64 + 1]>(smem_rd);  // [32 rows][64 c]
+  float(*sw)[LM + 1] = reinterpret_cast<float(*)[LM + 1]>(sdr + 32);  // [64 c][LM]
+  const int tid = threadIdx.x, ri = tid / 8, kg = tid % 8;
+  const int R0 = blockIdx.x * 32;  // flattened (b, r) rows
+  const int n_rows = g.B * g.Tq;
+  float acc[LM / 8];
+#pragma unroll
+  for (int u = 0; u < LM / 8; ++u) acc[u] = 0.f;
+  for (int c0 = 0; c0 < g.d; c0 += 64) {
+    __syncthreads();
+    for (int idx = tid; idx < 32 * 64; idx += 256) {
+      const int i = idx / 64, cc = idx % 64, R = R0 + i, c = c0 + cc;
+      float a = 0.f;
+      if (R < n_rows && c < g.d) {
+        const int b = R / g.Tq, r = R % g.Tq;
+        const int t1 = min(g.T, (r + 1) * g.qbs);
+        for (int t = r * g.qbs; t < t1; ++t) a += drow[((int64_t)b * g.T + t) * g.d + c];
+      }
+      sdr[i][cc] = a;
+    }
+    for (int idx = tid; idx < 64 * LM; idx += 256) {
+      const int cc = idx / LM, k = idx % LM, c = c0 + cc;
+      float v = 0.f;
+      if (c < g.d && k < g.Ld) {
+        const int64_t o = (int64_t)c * g.Ld + k;
+        v = w_bf16 ? __bfloat162float(reinterpret_cast<const bf16*>(w_rout_v)[o])
+                   : reinterpret_cast<const float*>(w_rout_v)[o];
+      }
+      sw[cc][k] = v;
+    }
+    __syncthreads();
+    for (int cc = 0; cc < 64; ++cc) {
+      const float a = sdr[ri][cc];
+#pragma unroll
+      for (int u = 0; u < LM / 8; ++u) acc[u] = fmaf(a, sw[cc][kg + 8 * u], acc[u]);
+    }
+  }
+  const int R = R0 + ri;
+  if (R < n_rows) {
+#pragma unroll
+    for (int u = 0; u < LM / 8; ++u) {
+      const int k = kg + 8 * u;
+      if (k < g.Ld) dlat[(int64_t)R * g.Ld + k] = acc[u];
+    }
+  }
+}
+
+// partial dW_rout[c, k] and db_rout[c] over one split of the (b, r) rows.
+template <typename T, int LM>
+__global__ void __launch_bounds__(256) rout_dw_kernel(Geom g, const float* __restrict__ drow,
+                                                      const T* __restrict__ lat,
+                                                      float* __restrict__ dw_part,
+                                                      float* __restrict__ db_part, int n_split) {
+  __shared__ float sdr[32][32 + 1];
+  __shared__ float sl[32][LM + 1];
+  const int tid = threadIdx.x, ci = tid / 8, kg = tid % 8;
+  const int c0 = blockIdx.x * 32, split = blockIdx.y;
+  const int n_rows = g.B * g.Tq;
+  const int per = cdiv(cdiv(n_rows, n_split), 32) * 32;
+  const int Ra = split * per, Rb = min(n_rows, Ra + per);
+  float acc[LM / 8], adb = 0.f;
+#pragma unroll
+  for (int u = 0; u < LM / 8; ++u) acc[u] = 0.f;
+  for (int R0 = Ra; R0 < Rb; R0 += 32) {
+    __syncthreads();
+    for (int idx = tid; idx < 32 * 32; idx += 256) {
+      const int i = idx / 32, cc = idx % 32, R = R0 + i, c = c0 + cc;
+      float a = 0.f;
+      if (R < Rb && c < g.d) {
+        const int b = R / g.Tq, r = R % g.Tq;
+        const int t1 = min(g.T, (r + 1) * g.qbs);
+        for (int t = r * g.qbs; t < t1; ++t) a += drow[((int64_t)b * g.T + t) * g.d + c];
+      }
+      sdr[i][cc] = a;
+    }
+    for (int idx = tid; idx < 32 * LM; idx += 256) {
+      const int i = idx / LM, k = idx % LM, R = R0 + i;
+      sl[i][k] = (R < Rb && k < g.Ld) ? to_f<T>(lat[(int64_t)R * g.Ld + k]) : 0.f;
+    }
+    __syncthreads();
+    for (int i = 0; i < 32; ++i) {
+      const float a = sdr[i][ci];
+      adb += a;
+#pragma unroll
+      for (int u = 0; u < LM / 8; ++u) acc[u] = fmaf(a, sl[i][kg + 8 * u], acc[u]);
+    }
+  }
+  const int c = c0 + ci;
+  if (c < g.d) {
+    float* dst = dw_part + (int64_t)split * g.d * g.Ld + (int64_t)c * g.Ld;
+#pragma unroll
+    for (int u = 0; u < LM / 8; ++u) {
+      const int k = kg + 8 * u;
+      if (k < g.Ld) dst[k] = acc[u];
+    }
+    if (kg == 0) db_part[(int64_t)split * g.d + c] = adb;
+  }
+}
+
+template <typename T, int LM>
+cudaError_t rout_bwd_lm(const Geom& g, const float* drow, const T* lat, const T* w_rout, float* dlat,
+                        float* dw_part, int n_split, cudaStream_t s) {
+  const size_t sm = sizeof(float) * (32 * 65 + 64 * (LM + 1));
+  cudaError_t e = cudaFuncSetAttribute(rout_dlat_kernel<LM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sm);
+  if (e != cudaSuccess) return e;
+  const int n_rows = g.B * g.Tq;
+  rout_dlat_kernel<LM><<<cdiv(n_rows, 32), 256, sm, s>>>(g, drow, w_rout, sizeof(T) == 2, dlat);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  float* db_part = dw_part + (int64_t)n_split * g.d * g.Ld;
+  dim3 grid(cdiv(g.d, 32), n_split);
+  rout_dw_kernel<T, LM><<<grid, 256, 0, s>>>(g, drow, lat, dw_part, db_part, n_split);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+template <typename T>
+cudaError_t launch_gate_fwd(const Geom& g, const T* local_out, const T* lat, const T* w_rout,
+                            const float* b_rout, const float* g_local, const float* g_remote, T* mixed,
+                            cudaStream_t s) {
+  const size_t sm = sizeof(float) * (2 * g.d + g.Ld + g.H);
+  cudaError_t e = cudaFuncSetAttribute(gate_fwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  if (e != cudaSuccess) return e;
+  dim3 grid(g.T, g.B);
+  gate_fwd_kernel<T><<<grid, NT, sm, s>>>(g, local_out, lat, w_rout, b_rout, g_local, g_remote, mixed);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_gate_bwd(const Geom& g, const T* local_out, const T* lat, const T* w_rout,
+                            const float* b_rout, const float* g_local, const float* g_remote,
+                            const T* dmixed, T* dl, float* delta, float* drow, float* dg_part,
+                            int tok_per_cta, cudaStream_t s) {
+  const size_t sm = sizeof(float) * (3 * g.d + g.Ld + g.H);
+  cudaError_t e = cudaFuncSetAttribute(gate_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  if (e != cudaSuccess) return e;
+  dim3 grid(cdiv(g.T, tok_per_cta), g.B);
+  gate_bwd_kernel<T><<<grid, NT, sm, s>>>(g, local_out, lat, w_rout, b_rout, g_local, g_remote, dmixed, dl,
+                                          delta, drow, dg_part, tok_per_cta);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_rout_bwd(const Geom& g, const float* drow, const T* lat, const T* w_rout, float* dlat,
+                            float* dw_part, int n_split, cudaStream_t s) {
+  if (g.Ld <= 64) return rout_bwd_lm<T, 64>(g, drow, lat, w_rout, dlat, dw_part, n_split, s);
+  return rout_bwd_lm<T, 128>(g, drow, lat, w_rout, dlat, dw_part, n_split, s);
+}
+
+#define INST(T)                                                                                          \
+  template cudaError_t launch_gate_fwd<T>(const Geom&, const T*, const T*, const T*, const float*,        \
+                                          const float*, const float*, T*, cudaStream_t);                  \
+  template cudaError_t launch_gate_bwd<T>(const Geom&, const T*, const T*, const T*, const float*,        \
+                                          const float*, const float*, const T*, T*, float*, float*,       \
+                                          float*, int, cudaStream_t);                                     \
+  template cudaError_t launch_rout_bwd<T>(const Geom&, const float*, const T*, const T*, float*, float*,  \
+                                          int, cudaStream_t);
+INST(float)
+INST(bf16)
+#undef INST
+
+}  // namespace llattn

@@ -1,0 +1,19 @@
+// Tensor-core (tcgen05 + TMA) kernels of the local branch for bf16
+// activations on sm_100a. The SIMT kernels of local_simt.cu cover the rest.
+#pragma once
+
+#include "common.cuh"
+
+namespace llattn {
+namespace sm100 {
+
+// True when the tcgen05 forward / backward kernels handle this geometry.
+bool fwd_supported(const Geom& g, int elt_bytes);
+bool bwd_supported(const Geom& g, int elt_bytes);
+
+cudaError_t launch_local_fwd(const Geom& g, const void* qkv, void* local_out, float* lse, cudaStream_t s);
+cudaError_t launch_local_bwd(const Geom& g, const void* qkv, const void* dl, const float* lse,
+                             const float* delta, void* dqkv, cudaStream_t s);
+
+}  // namespace sm100
+}  // namespace llattn

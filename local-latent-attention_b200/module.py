@@ -1,0 +1,168 @@
+"""Drop-in attention module backed by libllattn's sm_100a kernels.
+
+``LocalLatentAttentionB200(config)`` has exactly the parameters, state_dict
+keys and shapes of the reference's PyTorch ``LocalLatentAttention``
+(models.py:61-96) — fused ``qkv_proj``, ``rq_proj``, ``rkv_proj``, ``r_out``,
+``out`` (all with bias) and the shared ``gate_local``/``gate_remote``
+``Linear(head_dim, 1, bias=False)`` — so checkpoints interchange, and the
+same forward math (models.py:307-462). The projections stay cuBLAS GEMMs;
+pooling and everything between the projections run in the custom ops of
+``ops.py``.
+
+``build_attention(config)`` is the module switch of models.py:465-488: with
+``config.use_triton_kernel`` set it returns this module.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+from torch import Tensor
+
+from . import ops
+
+
+class LocalLatentAttentionB200(nn.Module):
+    def __init__(self, config) -> None:
+        super().__init__()
+        assert config.d_model % config.n_heads == 0
+        assert config.latent_d_model % config.latent_heads == 0
+        self.d_model = config.d_model
+        self.n_heads = config.n_heads
+        self.head_dim = config.d_model // config.n_heads
+        self.window = config.local_window
+        self.local_block_size = config.local_block_size
+        self.latent_tokens = config.latent_tokens
+        self.latent_heads = config.latent_heads
+        self.latent_d_model = config.latent_d_model
+        self.latent_head_dim = config.latent_d_model // config.latent_heads
+        self.latent_query_block_size = max(0, config.latent_query_block_size)
+        self.qkv_proj = nn.Linear(config.d_model, 3 * config.d_model)
+        self.rq_proj = nn.Linear(config.d_model, config.latent_d_model)
+        self.rkv_proj = nn.Linear(config.d_model, 2 * config.latent_d_model)
+        self.r_out = nn.Linear(config.latent_d_model, config.d_model)
+        self.out = nn.Linear(config.d_model, config.d_model)
+        self.gate_local = nn.Linear(self.head_dim, 1, bias=False)
+        self.gate_remote = nn.Linear(self.head_dim, 1, bias=False)
+        self.dropout = nn.Dropout(config.dropout)
+        self._n_layers = getattr(config, "n_layers", 1)
+        # Added to the local gate logit; 0 reproduces the reference. Not a
+        # parameter and not saved, so state_dicts stay interchangeable.
+        self.gate_bias = 0.0
+        self.profile_enabled = False
+        self.profile_totals: dict[str, float] = {}
+        self.profile_steps = 0
+        self._profile_events: list = []
+
+    # models.py:98-129: checkpoints with split q/k/v or rk/rv projections load
+    # into the fused layout.
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys,
+                              unexpected_keys, error_msgs) -> None:
+        def fuse(new: str, olds: tuple[str, ...]) -> None:
+            for kind in ("weight", "bias"):
+                key = f"{prefix}{new}.{kind}"
+                old_keys = [f"{prefix}{o}.{kind}" for o in olds]
+                if key not in state_dict and all(k in state_dict for k in old_keys):
+                    state_dict[key] = torch.cat([state_dict.pop(k) for k in old_keys], dim=0)
+
+        fuse("qkv_proj", ("q_proj", "k_proj", "v_proj"))
+        fuse("rkv_proj", ("rk_proj", "rv_proj"))
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys,
+                                      unexpected_keys, error_msgs)
+
+    # --- profiling API of models.py:131-157 --------------------------------
+    def set_profile(self, enabled: bool) -> None:
+        self.profile_enabled = enabled
+        self.profile_totals = {}
+        self.profile_steps = 0
+        self._profile_events = []
+
+    def _drain_profile(self) -> None:
+        for ev, geo in self._profile_events:
+            ev[-1].synchronize()
+            qkv = ev[0].elapsed_time(ev[1])
+            pool = ev[1].elapsed_time(ev[2])
+            core = ev[2].elapsed_time(ev[3])
+            total = ev[0].elapsed_time(ev[4])
+            for k, v in (("total_ms", total), ("qkv_ms", qkv), ("pool_ms", pool),
+                         ("local_attention_ms", core), ("latent_attention_ms", 0.0),
+                         ("gate_mix_ms", 0.0)):
+                self.profile_totals[k] = self.profile_totals.get(k, 0.0) + v
+            for k, v in geo.items():
+                self.profile_totals[k] = self.profile_totals.get(k, 0.0) + v
+            self.profile_steps += 1
+        self._profile_events = []
+
+    def get_profile_stats(self) -> dict[str, float]:
+        """Same keys as the reference. The fused op times local + latent +
+        gate together: its time is reported as local_attention_ms and the
+        latent/gate entries are 0. gate_mean is not computed (NaN): the fused
+        op does not materialise the gate weights."""
+        if not self.profile_enabled:
+            return {}
+        self._drain_profile()
+        if self.profile_steps == 0:
+            return {}
+        n = self.profile_steps
+        t = self.profile_totals
+        return {
+            "profile_local_latent_total_ms": t["total_ms"] / n,
+            "profile_qkv_ms": t["qkv_ms"] / n,
+            "profile_pool_ms": t["pool_ms"] / n,
+            "profile_local_attention_ms": t["local_attention_ms"] / n,
+            "profile_latent_attention_ms": t["latent_attention_ms"] / n,
+            "profile_gate_mix_ms": t["gate_mix_ms"] / n,
+            "profile_gate_mean": float("nan"),
+            "profile_seq_len": t["seq_len"] / n,
+            "profile_local_block_size": t["local_block_size"] / n,
+            "profile_latent_count": t["latent_count"] / n,
+            "profile_latent_chunk_size": t["chunk_size"] / n,
+            "profile_latent_query_block_size": t["latent_query_block_size"] / n,
+        }
+
+    def forward(self, x: Tensor) -> Tensor:
+        if self.training and self.dropout.p > 0:
+            raise NotImplementedError("LocalLatentAttentionB200 does not implement attention dropout")
+        B, T, d = x.shape
+        prof = self.profile_enabled and x.is_cuda
+        if prof:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+            ev[0].record()
+        qkv = self.qkv_proj(x)
+        if prof:
+            ev[1].record()
+        pooled = ops.pool_chunks(x, self.latent_tokens)
+        gkv = self.rkv_proj(pooled)
+        if self.latent_query_block_size > 1:
+            qsrc = ops.pool_query_blocks(x, self.latent_tokens, self.latent_query_block_size)
+        else:
+            qsrc = x
+        rq = self.rq_proj(qsrc)
+        if prof:
+            ev[2].record()
+        mixed = ops.llattn_attention(
+            qkv, rq, gkv, self.r_out.weight, self.r_out.bias, self.gate_local.weight,
+            self.gate_remote.weight, n_heads=self.n_heads, latent_heads=self.latent_heads,
+            window=self.window, local_block_size=self.local_block_size,
+            latent_tokens=self.latent_tokens, latent_query_block_size=self.latent_query_block_size,
+            gate_bias=self.gate_bias)
+        if prof:
+            ev[3].record()
+        y = self.out(mixed)
+        if prof:
+            ev[4].record()
+            geo = ops.geometry(T, self.latent_tokens, self.latent_query_block_size, self.window,
+                               self.local_block_size)
+            self._profile_events.append((ev, {
+                "seq_len": T, "local_block_size": geo["local_span"],
+                "latent_count": geo["n_chunks"], "chunk_size": geo["chunk"],
+                "latent_query_block_size": geo["qblock"]}))
+        return y
+
+
+def build_attention(config) -> nn.Module:
+    """The module switch of models.py:465-488: ``use_triton_kernel`` selects
+    the B200 kernels, otherwise the caller's own PyTorch module is expected,
+    so this always returns the B200 module (the reference constructor takes
+    the same ModelConfig)."""
+    return LocalLatentAttentionB200(config)

@@ -1,0 +1,286 @@
+"""torch custom ops over libllattn.so: pooling and the fused attention core.
+
+``llattn_b200::pool_fwd/pool_bwd`` and ``llattn_b200::attn_fwd/attn_bwd`` are
+registered with ``torch.library.custom_op`` for CUDA only, with fake (meta)
+implementations for tracing and ``register_autograd`` for the backward. They
+launch on torch's current stream, allocate every output and the backward
+workspace through torch, and raise ``RuntimeError`` with the library's
+message on any argument error. There is no CPU implementation: calling them
+on CPU tensors is an error.
+
+Reference API mirrored: ``LLAttnFunction.apply`` of
+``kernels/llattn_op.py:184-238`` — the forward saves the local-branch
+logsumexp and the branch outputs, the backward returns one gradient per
+tensor input. The math is that of the PyTorch module (models.py:307-462).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+_DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
+
+
+def geometry(seq_len: int, latent_tokens: int, query_block: int, window: int = 1,
+             local_block: int = 256) -> dict:
+    """Derived sizes, as models.py derives them (cs/Nc :175-183, bsL :249,
+    bs/Tq :216-219). Pure Python so fake tensors need no library call."""
+    target = min(latent_tokens, seq_len)
+    cs = math.ceil(seq_len / target)
+    qbs = min(seq_len, query_block) if query_block > 1 else 1
+    return {"chunk": cs, "n_chunks": math.ceil(seq_len / cs),
+            "local_span": min(seq_len, max(window, local_block)),
+            "qblock": qbs, "n_qrows": math.ceil(seq_len / qbs)}
+
+
+def _ptr(t: Tensor) -> int:
+    return t.data_ptr()
+
+
+def _stream(t: Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _dtype_code(t: Tensor) -> int:
+    if t.dtype not in _DT:
+        raise RuntimeError(f"llattn: unsupported dtype {t.dtype} (float32 or bfloat16)")
+    return _DT[t.dtype]
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError("llattn: " + msg)
+
+
+# --------------------------------------------------------------------------
+# pooling (K1): models.py:159-214 (chunks) and :216-230 (query blocks)
+
+@torch.library.custom_op("llattn_b200::pool_fwd", mutates_args=(), device_types="cuda")
+def pool_fwd(x: Tensor, latent_tokens: int, query_block: int, mode: int) -> Tensor:
+    _require(x.dim() == 3 and x.is_contiguous(), "pool_fwd expects a contiguous [B, T, d] tensor")
+    B, T, d = x.shape
+    geo = geometry(T, latent_tokens, query_block)
+    rows = geo["n_chunks"] if mode == _lib.POOL_CHUNKS else geo["n_qrows"]
+    out = torch.empty(B, rows, d, dtype=x.dtype, device=x.device)
+    dims = _lib.make_dims(B, T, latent_tokens=latent_tokens, query_block=query_block,
+                          dtype=_dtype_code(x))
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().llattn_pool_fwd(ctypes.byref(dims), mode, _ptr(x), _ptr(out), d,
+                                              _stream(x)), "llattn_pool_fwd")
+    return out
+
+
+@pool_fwd.register_fake
+def _pool_fwd_fake(x, latent_tokens, query_block, mode):
+    B, T, d = x.shape
+    geo = geometry(T, latent_tokens, query_block)
+    rows = geo["n_chunks"] if mode == _lib.POOL_CHUNKS else geo["n_qrows"]
+    return x.new_empty(B, rows, d)
+
+
+@torch.library.custom_op("llattn_b200::pool_bwd", mutates_args=(), device_types="cuda")
+def pool_bwd(dpooled: Tensor, seq_len: int, latent_tokens: int, query_block: int, mode: int) -> Tensor:
+    _require(dpooled.dim() == 3 and dpooled.is_contiguous(), "pool_bwd expects a contiguous gradient")
+    B, _, d = dpooled.shape
+    dx = torch.empty(B, seq_len, d, dtype=dpooled.dtype, device=dpooled.device)
+    dims = _lib.make_dims(B, seq_len, latent_tokens=latent_tokens, query_block=query_block,
+                          dtype=_dtype_code(dpooled))
+    with torch.cuda.device(dpooled.device):
+        _lib.check(_lib.lib().llattn_pool_bwd(ctypes.byref(dims), mode, _ptr(dpooled), _ptr(dx), d,
+                                              _stream(dpooled)), "llattn_pool_bwd")
+    return dx
+
+
+@pool_bwd.register_fake
+def _pool_bwd_fake(dpooled, seq_len, latent_tokens, query_block, mode):
+    B, _, d = dpooled.shape
+    return dpooled.new_empty(B, seq_len, d)
+
+
+def _pool_setup(ctx, inputs, output):
+    x, latent_tokens, query_block, mode = inputs
+    ctx.cfg = (x.shape[1], latent_tokens, query_block, mode)
+
+
+def _pool_backward(ctx, grad):
+    return pool_bwd(grad.contiguous(), *ctx.cfg), None, None, None
+
+
+pool_fwd.register_autograd(_pool_backward, setup_context=_pool_setup)
+
+
+def pool_chunks(x: Tensor, latent_tokens: int) -> Tensor:
+    """Chunk means of x [B,T,d] -> [B,Nc,d] (models.py:159-214)."""
+    return pool_fwd(x.contiguous(), latent_tokens, 0, _lib.POOL_CHUNKS)
+
+
+def pool_query_blocks(x: Tensor, latent_tokens: int, query_block: int) -> Tensor:
+    """Zero-padded query-block means of x [B,T,d] -> [B,Tq,d] (models.py:216-230)."""
+    return pool_fwd(x.contiguous(), latent_tokens, query_block, _lib.POOL_QBLOCKS)
+
+
+# --------------------------------------------------------------------------
+# fused attention core: local + latent + r_out + gate + mix
+
+def _core_dims(qkv: Tensor, w_rout: Tensor, n_heads: int, latent_heads: int, window: int,
+               local_block: int, latent_tokens: int, query_block: int, gate_bias: float):
+    B, T, three_d = qkv.shape
+    d = three_d // 3
+    _require(three_d == 3 * d and d % n_heads == 0, "qkv last dim must be 3 * n_heads * head_dim")
+    Ld = w_rout.shape[1]
+    _require(Ld % latent_heads == 0, "latent_d_model must be divisible by latent_heads")
+    return _lib.make_dims(B, T, n_heads, d // n_heads, latent_heads, Ld // latent_heads, window,
+                          local_block, latent_tokens, query_block, _dtype_code(qkv), gate_bias)
+
+
+def _check_core_inputs(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, dims, geo):
+    dt = qkv.dtype
+    B, T = dims.batch, dims.seq_len
+    d, Ld = dims.n_heads * dims.head_dim, dims.latent_heads * dims.latent_head_dim
+    for name, t, shape, want in (
+        ("qkv", qkv, (B, T, 3 * d), dt), ("rq", rq, (B, geo["n_qrows"], Ld), dt),
+        ("gkv", gkv, (B, geo["n_chunks"], 2 * Ld), dt), ("w_rout", w_rout, (d, Ld), dt),
+        ("b_rout", b_rout, (d,), torch.float32), ("g_local", g_local, (dims.head_dim,), torch.float32),
+        ("g_remote", g_remote, (dims.head_dim,), torch.float32),
+    ):
+        _require(tuple(t.shape) == shape, f"{name} has shape {tuple(t.shape)}, expected {shape}")
+        _require(t.dtype == want, f"{name} has dtype {t.dtype}, expected {want}")
+        _require(t.is_contiguous(), f"{name} must be contiguous")
+        _require(t.device == qkv.device, f"{name} is on {t.device}, expected {qkv.device}")
+
+
+@torch.library.custom_op("llattn_b200::attn_fwd", mutates_args=(), device_types="cuda")
+def attn_fwd(qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tensor, b_rout: Tensor,
+             g_local: Tensor, g_remote: Tensor, n_heads: int, latent_heads: int, window: int,
+             local_block: int, latent_tokens: int, query_block: int,
+             gate_bias: float) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    dims = _core_dims(qkv, w_rout, n_heads, latent_heads, window, local_block, latent_tokens,
+                      query_block, gate_bias)
+    geo = geometry(dims.seq_len, latent_tokens, query_block, window, local_block)
+    _check_core_inputs(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, dims, geo)
+    B, T, H = dims.batch, dims.seq_len, dims.n_heads
+    d, Ld, Tq = H * dims.head_dim, w_rout.shape[1], geo["n_qrows"]
+    kw = dict(device=qkv.device)
+    mixed = torch.empty(B, T, d, dtype=qkv.dtype, **kw)
+    local_out = torch.empty(B, T, d, dtype=qkv.dtype, **kw)
+    lse = torch.empty(B, H, T, dtype=torch.float32, **kw)
+    lat = torch.empty(B, Tq, Ld, dtype=qkv.dtype, **kw)
+    lat_lse = torch.empty(B, latent_heads, Tq, dtype=torch.float32, **kw)
+    args = _lib.FwdArgs(dims, _ptr(qkv), _ptr(rq), _ptr(gkv), _ptr(w_rout), _ptr(b_rout),
+                        _ptr(g_local), _ptr(g_remote), _ptr(mixed), _ptr(local_out), _ptr(lse),
+                        _ptr(lat), _ptr(lat_lse))
+    with torch.cuda.device(qkv.device):
+        _lib.check(_lib.lib().llattn_fwd(ctypes.byref(args), _stream(qkv)), "llattn_fwd")
+    return mixed, local_out, lse, lat, lat_lse
+
+
+@attn_fwd.register_fake
+def _attn_fwd_fake(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, n_heads, latent_heads, window,
+                   local_block, latent_tokens, query_block, gate_bias):
+    B, T, three_d = qkv.shape
+    d = three_d // 3
+    Tq = geometry(T, latent_tokens, query_block)["n_qrows"]
+    f32 = torch.float32
+    return (qkv.new_empty(B, T, d), qkv.new_empty(B, T, d), qkv.new_empty(B, n_heads, T, dtype=f32),
+            qkv.new_empty(B, Tq, w_rout.shape[1]), qkv.new_empty(B, latent_heads, Tq, dtype=f32))
+
+
+@torch.library.custom_op("llattn_b200::attn_bwd", mutates_args=(), device_types="cuda")
+def attn_bwd(dmixed: Tensor, qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tensor, b_rout: Tensor,
+             g_local: Tensor, g_remote: Tensor, local_out: Tensor, lse: Tensor, lat: Tensor,
+             lat_lse: Tensor, n_heads: int, latent_heads: int, window: int, local_block: int,
+             latent_tokens: int, query_block: int,
+             gate_bias: float) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    dims = _core_dims(qkv, w_rout, n_heads, latent_heads, window, local_block, latent_tokens,
+                      query_block, gate_bias)
+    _require(dmixed.shape == local_out.shape and dmixed.dtype == qkv.dtype and dmixed.is_contiguous(),
+             "dmixed must be a contiguous [B, T, d] tensor of the activation dtype")
+    d, hd = dims.n_heads * dims.head_dim, dims.head_dim
+    kw = dict(device=qkv.device)
+    dqkv = torch.empty_like(qkv)
+    drq = torch.empty_like(rq)
+    dgkv = torch.empty_like(gkv)
+    dw = torch.empty(w_rout.shape, dtype=torch.float32, **kw)
+    db = torch.empty(d, dtype=torch.float32, **kw)
+    dgl = torch.empty(hd, dtype=torch.float32, **kw)
+    dgr = torch.empty(hd, dtype=torch.float32, **kw)
+    ws_bytes = _lib.lib().llattn_bwd_workspace_bytes(ctypes.byref(dims))
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, **kw)
+    args = _lib.BwdArgs(dims, _ptr(qkv), _ptr(rq), _ptr(gkv), _ptr(w_rout), _ptr(b_rout),
+                        _ptr(g_local), _ptr(g_remote), _ptr(local_out), _ptr(lse), _ptr(lat),
+                        _ptr(lat_lse), _ptr(dmixed), _ptr(dqkv), _ptr(drq), _ptr(dgkv), _ptr(dw),
+                        _ptr(db), _ptr(dgl), _ptr(dgr), _ptr(ws), ws.numel())
+    with torch.cuda.device(qkv.device):
+        _lib.check(_lib.lib().llattn_bwd(ctypes.byref(args), _stream(qkv)), "llattn_bwd")
+    return dqkv, drq, dgkv, dw, db, dgl, dgr
+
+
+@attn_bwd.register_fake
+def _attn_bwd_fake(dmixed, qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, local_out, lse, lat,
+                   lat_lse, *cfg):
+    f32 = torch.float32
+    return (torch.empty_like(qkv), torch.empty_like(rq), torch.empty_like(gkv),
+            w_rout.new_empty(w_rout.shape, dtype=f32), b_rout.new_empty(b_rout.shape, dtype=f32),
+            g_local.new_empty(g_local.shape, dtype=f32), g_remote.new_empty(g_remote.shape, dtype=f32))
+
+
+def _attn_setup(ctx, inputs, output):
+    qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, *cfg = inputs
+    _, local_out, lse, lat, lat_lse = output
+    ctx.save_for_backward(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, local_out, lse, lat,
+                          lat_lse)
+    ctx.cfg = cfg
+
+
+def _attn_backward(ctx, dmixed, _d_local, _d_lse, _d_lat, _d_lat_lse):
+    saved = ctx.saved_tensors
+    qkv = saved[0]
+    if dmixed is None:
+        dmixed = torch.zeros_like(saved[7])
+    dqkv, drq, dgkv, dw, db, dgl, dgr = attn_bwd(dmixed.to(qkv.dtype).contiguous(), *saved, *ctx.cfg)
+    return (dqkv, drq, dgkv, dw.to(saved[3].dtype), db, dgl, dgr) + (None,) * 7
+
+
+attn_fwd.register_autograd(_attn_backward, setup_context=_attn_setup)
+
+
+def llattn_attention(qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tensor, b_rout: Tensor,
+                     g_local: Tensor, g_remote: Tensor, *, n_heads: int, latent_heads: int,
+                     window: int, local_block_size: int, latent_tokens: int,
+                     latent_query_block_size: int = 0, gate_bias: float = 0.0) -> Tensor:
+    """Differentiable attention core between the projections -> mixed [B,T,d].
+
+    qkv [B,T,3d] (qkv_proj output), rq [B,Tq,Ld] (rq_proj output),
+    gkv [B,Nc,2Ld] (rkv_proj output of the chunk means), r_out weight/bias,
+    gate vectors [hd]. The activation dtype is qkv's (float32 -> exact SIMT
+    kernels, bfloat16 -> tcgen05 kernels); the other tensors are cast to it,
+    bias and gates to float32, under autograd."""
+    dt = qkv.dtype
+    outs = attn_fwd(qkv.contiguous(), rq.to(dt).contiguous(), gkv.to(dt).contiguous(),
+                    w_rout.to(dt).contiguous(), b_rout.float().contiguous(),
+                    g_local.float().reshape(-1).contiguous(), g_remote.float().reshape(-1).contiguous(),
+                    n_heads, latent_heads, window, local_block_size, latent_tokens,
+                    latent_query_block_size, float(gate_bias))
+    return outs[0]
+
+
+class LLAttnFunction:
+    """Name-compatible entry of the reference's autograd op
+    (kernels/llattn_op.py:184-238). ``apply`` takes the PyTorch module's
+    tensors (see ``llattn_attention``), not the Triton path's per-head
+    Q/K/V/GQ/GK/GV layout, because the PyTorch module is the semantic target."""
+
+    @staticmethod
+    def apply(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, n_heads, latent_heads, window,
+              local_block_size, latent_tokens, latent_query_block_size=0, gate_bias=0.0):
+        return llattn_attention(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, n_heads=n_heads,
+                                latent_heads=latent_heads, window=window,
+                                local_block_size=local_block_size, latent_tokens=latent_tokens,
+                                latent_query_block_size=latent_query_block_size,
+                                gate_bias=gate_bias)

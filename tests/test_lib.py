@@ -1,0 +1,97 @@
+"""The C-ABI library: it loads, exports every symbol include/llattn.h
+declares, and its host-side logic (geometry, workspace sizing, argument
+validation) behaves — no kernel launches, so no GPU needed."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+import llattn_b200
+from llattn_b200 import _lib, ops
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    with open(os.path.join(ROOT, "include", "llattn.h")) as fh:
+        text = fh.read()
+    return re.findall(r"LLATTN_API\s+[\w\s\*]+?\b(llattn_\w+)\s*\(", text)
+
+
+def test_header_declares_the_binding_symbols():
+    assert sorted(declared_symbols()) == sorted(_lib.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    for name in declared_symbols():
+        assert hasattr(L, name), name
+    assert L.llattn_version() == 1
+
+
+@pytest.mark.parametrize("T,Nl,QB,W,LBS", [
+    (512, 16, 0, 128, 256), (2048, 64, 0, 256, 256), (16384, 256, 64, 512, 256),
+    (37, 5, 8, 6, 10), (1, 4, 0, 4, 256), (20, 64, 0, 5, 8), (5, 3, 8, 3, 4),
+    (32805, 512, 0, 1024, 256), (8191, 32, 0, 64, 256), (130, 128, 0, 64, 256),
+])
+def test_geometry_matches_reference_formulas(T, Nl, QB, W, LBS):
+    g = _lib.geometry(_lib.make_dims(2, T, window=W, local_block=LBS, latent_tokens=Nl,
+                                     query_block=QB))
+    py = ops.geometry(T, Nl, QB, W, LBS)
+    assert (g.chunk, g.n_chunks, g.local_span, g.qblock, g.n_qrows) == (
+        py["chunk"], py["n_chunks"], py["local_span"], py["qblock"], py["n_qrows"])
+    import llattn_oracle as O
+    assert (g.chunk, g.n_chunks) == O.chunk_layout(T, Nl)
+
+
+@pytest.mark.parametrize("bad,msg", [
+    (dict(seq_len=0), "seq_len"), (dict(head_dim=256), "head_dim"), (dict(window=0), "local_window"),
+    (dict(latent_tokens=0), "latent_tokens"), (dict(dtype=7), "dtype"),
+    (dict(latent_head_dim=128), "latent_head_dim"),
+])
+def test_bad_dims_are_rejected_on_the_host(bad, msg):
+    kw = dict(batch=2, seq_len=64, n_heads=2, head_dim=16, latent_heads=2, latent_head_dim=4,
+              window=8, local_block=16, latent_tokens=8)
+    kw.update(bad)
+    dims = _lib.make_dims(**kw)
+    g = _lib.Geom()
+    rc = _lib.lib().llattn_geometry(ctypes.byref(dims), ctypes.byref(g))
+    assert rc == 1
+    assert msg in _lib.lib().llattn_last_error().decode()
+    assert _lib.lib().llattn_bwd_workspace_bytes(ctypes.byref(dims)) == 0
+
+
+def test_entry_points_reject_null_args_without_launching():
+    L = _lib.lib()
+    assert L.llattn_fwd(None, None) == 1
+    assert L.llattn_bwd(None, None) == 1
+    args = _lib.FwdArgs()
+    args.dims = _lib.make_dims(1, 8, 1, 8, 1, 4, 4, 256, 2)
+    assert L.llattn_fwd(ctypes.byref(args), None) == 1
+    assert "NULL" in L.llattn_last_error().decode()
+
+
+def test_workspace_grows_with_problem():
+    small = _lib.make_dims(1, 64, 2, 16, 2, 4, 8, 16, 8, dtype=_lib.BF16)
+    big = _lib.make_dims(16, 2048, 12, 128, 2, 32, 256, 256, 64, dtype=_lib.BF16)
+    L = _lib.lib()
+    a = L.llattn_bwd_workspace_bytes(ctypes.byref(small))
+    b = L.llattn_bwd_workspace_bytes(ctypes.byref(big))
+    assert 0 < a < b and b % 256 == 0
+
+
+def test_bwd_rejects_small_workspace():
+    import torch  # noqa: F401
+    dims = _lib.make_dims(1, 8, 1, 8, 1, 4, 4, 256, 2)
+    args = _lib.BwdArgs()
+    args.dims = dims
+    fake = 256  # never dereferenced: validation fails first
+    for name, _ in _lib.BwdArgs._fields_:
+        if name not in ("dims", "workspace", "workspace_bytes"):
+            setattr(args, name, fake)
+    args.workspace = fake
+    args.workspace_bytes = 16
+    assert _lib.lib().llattn_bwd(ctypes.byref(args), None) == 4
+    assert "workspace" in _lib.lib().llattn_last_error().decode()

@@ -1,0 +1,66 @@
+"""Host-side checks of the drop-in module and ops (CPU only)."""
+
+import pytest
+import torch
+
+import llattn_b200
+import llattn_oracle as O
+from parity import model_config
+
+
+def cfg():
+    return O.BlockCfg(d_model=32, n_heads=2, local_window=8, local_block_size=16,
+                      latent_tokens=8, latent_d_model=8, latent_heads=2)
+
+
+def test_state_dict_matches_reference_names_and_shapes():
+    m = llattn_b200.LocalLatentAttentionB200(model_config(cfg()))
+    ref = O.init_params(cfg())
+    sd = m.state_dict()
+    assert sorted(sd) == sorted(ref)
+    for k in ref:
+        assert sd[k].shape == ref[k].shape, k
+
+
+def test_loads_reference_state_dict_and_legacy_split_keys():
+    c = cfg()
+    m = llattn_b200.LocalLatentAttentionB200(model_config(c))
+    ref = O.init_params(c, seed=3)
+    m.load_state_dict(ref)
+    assert torch.equal(m.qkv_proj.weight, ref["qkv_proj.weight"])
+    legacy = dict(ref)
+    d = c.d_model
+    w, b = legacy.pop("qkv_proj.weight"), legacy.pop("qkv_proj.bias")
+    for i, n in enumerate(("q_proj", "k_proj", "v_proj")):
+        legacy[n + ".weight"] = w[i * d:(i + 1) * d]
+        legacy[n + ".bias"] = b[i * d:(i + 1) * d]
+    w, b = legacy.pop("rkv_proj.weight"), legacy.pop("rkv_proj.bias")
+    L = c.latent_d_model
+    legacy["rk_proj.weight"], legacy["rv_proj.weight"] = w[:L], w[L:]
+    legacy["rk_proj.bias"], legacy["rv_proj.bias"] = b[:L], b[L:]
+    m2 = llattn_b200.LocalLatentAttentionB200(model_config(c))
+    m2.load_state_dict(legacy)
+    for k, v in ref.items():
+        assert torch.equal(m2.state_dict()[k], v), k
+
+
+def test_ops_have_no_cpu_path():
+    x = torch.randn(2, 16, 8)
+    with pytest.raises(Exception):
+        llattn_b200.ops.pool_chunks(x, 4)
+
+
+def test_profile_api_present():
+    m = llattn_b200.LocalLatentAttentionB200(model_config(cfg()))
+    m.set_profile(True)
+    assert m.get_profile_stats() == {}
+    m.set_profile(False)
+    assert m.get_profile_stats() == {}
+
+
+def test_dropout_in_training_is_rejected():
+    c = model_config(cfg())
+    c.dropout = 0.1
+    m = llattn_b200.LocalLatentAttentionB200(c).train()
+    with pytest.raises(NotImplementedError):
+        m(torch.randn(1, 4, 32))

@@ -1,0 +1,149 @@
+"""Parity of the CUDA path (through the C ABI, via the torch ops and the
+drop-in module) against the CPU oracle and the reference's golden vectors.
+
+Tolerances: max|a-b|/max|b| <= 1e-4 for float32 activations and 2e-2 for
+bfloat16 (inputs and weights rounded to bf16, oracle in float64)."""
+
+import os
+
+import pytest
+import torch
+
+import llattn_oracle as O
+from parity import (TOL, b200_block, bf16_round_params, compare, make_cfg, oracle_block,
+                    rel_err)
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+SMALL = torch.load(os.path.join(GOLDEN, "small_f64.pt"))
+
+
+@pytest.mark.parametrize("name", sorted(SMALL))
+def test_golden_small_fp32(name):
+    case = SMALL[name]
+    _, _, cfg = make_cfg(case["dims"])
+    p32 = {k: v.float() for k, v in case["params"].items()}
+    got = b200_block(p32, case["x"].float(), case["g"].float(), cfg, case["gate_bias"], torch.float32)
+    compare(got, (case["y"], case["dx"], case["grads"]), TOL[torch.float32], name)
+
+
+@pytest.mark.parametrize("name", sorted(SMALL))
+def test_golden_small_bf16(name):
+    case = SMALL[name]
+    _, _, cfg = make_cfg(case["dims"])
+    p = bf16_round_params(case["params"])
+    x = case["x"].to(torch.bfloat16).float()
+    g = case["g"].to(torch.bfloat16).float()
+    ref = oracle_block(p, x, g, cfg, case["gate_bias"])
+    got = b200_block(p, x, g, cfg, case["gate_bias"], torch.bfloat16)
+    compare(got, ref, TOL[torch.bfloat16], name)
+
+
+def test_cfg1_fp32_against_reference_golden():
+    case = torch.load(os.path.join(GOLDEN, "cfg1_f32.pt"))
+    B, T, cfg = make_cfg(case["dims"])
+    params = O.init_params(cfg, 0, torch.float32)
+    torch.manual_seed(0)  # same draw order as the golden generator: weights, then x, then g
+    O.init_params(cfg, 0)
+    x = torch.randn(B, T, cfg.d_model)
+    g = torch.randn(B, T, cfg.d_model)
+    got = b200_block(params, x, g, cfg, 0.0, torch.float32)
+    errs = compare(got, (case["y"], case["dx"], case["grads"]), TOL[torch.float32], "cfg1")
+    print("cfg1 fp32 errors", errs)
+
+
+def _block_case(dims, seed=0, gate_bias=0.0, dtype=torch.bfloat16, oracle_dtype=torch.float64):
+    B, T, cfg = make_cfg(dims)
+    params = O.init_params(cfg, seed)
+    gen = torch.Generator().manual_seed(seed + 1)
+    x = torch.randn(B, T, cfg.d_model, generator=gen)
+    g = torch.randn(B, T, cfg.d_model, generator=gen)
+    if dtype == torch.bfloat16:
+        params = bf16_round_params(params)
+        x = x.to(torch.bfloat16).float()
+        g = g.to(torch.bfloat16).float()
+    ref = oracle_block(params, x, g, cfg, gate_bias, oracle_dtype)
+    got = b200_block(params, x, g, cfg, gate_bias, dtype)
+    return compare(got, ref, TOL[dtype], str(dims))
+
+
+# bf16 shapes exercising the tensor-core path: head_dim 64/128, ragged T,
+# window below/above the block span, block-pooled queries, saturated gates.
+BF16_CASES = [
+    dict(B=2, T=640, d_model=256, n_heads=2, local_window=256, latent_tokens=64, latent_d_model=64),
+    dict(B=1, T=1000, d_model=512, n_heads=4, local_window=128, latent_tokens=32, latent_d_model=64),
+    dict(B=2, T=515, d_model=256, n_heads=4, local_window=64, latent_tokens=32, latent_d_model=64),
+    dict(B=1, T=1337, d_model=256, n_heads=2, local_window=300, local_block_size=200,
+         latent_tokens=48, latent_d_model=64, latent_query_block_size=64),
+    dict(B=1, T=2100, d_model=256, n_heads=2, local_window=1024, latent_tokens=512,
+         latent_d_model=64),
+    dict(B=3, T=129, d_model=384, n_heads=3, local_window=16, local_block_size=32,
+         latent_tokens=16, latent_d_model=32, latent_heads=2),
+]
+
+
+@pytest.mark.parametrize("idx", range(len(BF16_CASES)))
+def test_block_bf16_shapes(idx):
+    dims = dict(BF16_CASES[idx])
+    dims.setdefault("latent_heads", 2)
+    print(_block_case(dims))
+
+
+@pytest.mark.parametrize("bias", [8.0, -8.0])
+def test_block_bf16_saturated_gate(bias):
+    dims = dict(B=2, T=600, d_model=256, n_heads=2, local_window=128, latent_tokens=32,
+                latent_d_model=64, latent_heads=2)
+    print(_block_case(dims, gate_bias=bias))
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_block_fp32_head_dims(hd):
+    dims = dict(B=1, T=700, d_model=2 * hd, n_heads=2, local_window=200, latent_tokens=32,
+                latent_d_model=32, latent_heads=2)
+    print(_block_case(dims, dtype=torch.float32))
+
+
+def test_cfg2_width_bf16_two_sequences():
+    """cfg2 shape (T2048 d1536 H12 W256 Nl64 Ld64) on 2 sequences vs the oracle."""
+    dims = dict(B=2, T=2048, d_model=1536, n_heads=12, local_window=256, latent_tokens=64,
+                latent_d_model=64, latent_heads=2)
+    print(_block_case(dims, oracle_dtype=torch.float32))
+
+
+def test_cfg3_bf16_one_sequence():
+    """cfg3 shape (T16384 d1024 H8 W512 Nl256 Ld64 QB64) on one sequence."""
+    dims = dict(B=1, T=16384, d_model=1024, n_heads=8, local_window=512, latent_tokens=256,
+                latent_d_model=64, latent_heads=2, latent_query_block_size=64)
+    print(_block_case(dims, oracle_dtype=torch.float32))
+
+
+def test_pool_ops_match_oracle():
+    import llattn_b200
+
+    for T, Nl, QB in ((37, 5, 8), (2048, 64, 0), (1000, 33, 64)):
+        x = torch.randn(2, T, 96)
+        cs, _ = O.chunk_layout(T, Nl)
+        ref = O.pool_chunks(x.double(), cs)
+        got = llattn_b200.ops.pool_chunks(x.cuda(), Nl)
+        assert rel_err(got, ref) < 1e-6
+        if QB:
+            bs, _ = O.query_block_layout(T, QB)
+            refq, _ = O.pool_query_blocks(x.double(), bs, O.chunk_ids(T, cs, O.chunk_layout(T, Nl)[1]))
+            gotq = llattn_b200.ops.pool_query_blocks(x.cuda(), Nl, QB)
+            assert rel_err(gotq, refq) < 1e-6
+
+
+def test_deterministic_fwd_bwd():
+    """No atomics anywhere: two runs are bitwise equal."""
+    dims = dict(B=2, T=777, d_model=256, n_heads=2, local_window=256, latent_tokens=32,
+                latent_d_model=64, latent_heads=2)
+    B, T, cfg = make_cfg(dims)
+    params = O.init_params(cfg, 0)
+    x = torch.randn(B, T, cfg.d_model)
+    g = torch.randn(B, T, cfg.d_model)
+    a = b200_block(params, x, g, cfg, 0.0, torch.bfloat16)
+    b = b200_block(params, x, g, cfg, 0.0, torch.bfloat16)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    for k in a[2]:
+        assert torch.equal(a[2][k], b[2][k]), k
