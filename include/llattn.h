@@ -158,6 +158,13 @@ typedef enum llattn_pool_mode {
 LLATTN_API int llattn_version(void);
 LLATTN_API const char* llattn_last_error(void);
 
+/* Device fault word of the current device (0 = none): set by a tensor-core
+ * kernel whose bounded wait on a barrier ran out, after which that kernel
+ * abandoned its work and returned. Synchronises with the device; for tests
+ * and diagnostics, not for the hot path. reset != 0 clears it. No
+ * counterpart in the reference (its Triton kernels have no waits). */
+LLATTN_API unsigned llattn_fault_status(int reset);
+
 /* Fills *out from *dims. Returns LLATTN_ERR_ARG for inconsistent dims. */
 LLATTN_API int llattn_geometry(const llattn_dims* dims, llattn_geom* out);
 

@@ -16,7 +16,7 @@ F32, BF16 = 0, 1
 POOL_CHUNKS, POOL_QBLOCKS = 0, 1
 
 EXPORTED = (
-    "llattn_version", "llattn_last_error", "llattn_geometry", "llattn_bwd_workspace_bytes",
+    "llattn_version", "llattn_last_error", "llattn_fault_status", "llattn_geometry", "llattn_bwd_workspace_bytes",
     "llattn_pool_fwd", "llattn_pool_bwd", "llattn_fwd", "llattn_bwd",
 )
 
@@ -70,6 +70,8 @@ def lib() -> ctypes.CDLL:
         L = ctypes.CDLL(LIB_PATH)
         L.llattn_version.restype = ctypes.c_int
         L.llattn_last_error.restype = ctypes.c_char_p
+        L.llattn_fault_status.argtypes = [ctypes.c_int]
+        L.llattn_fault_status.restype = ctypes.c_uint
         L.llattn_geometry.argtypes = [ctypes.POINTER(Dims), ctypes.POINTER(Geom)]
         L.llattn_geometry.restype = ctypes.c_int
         L.llattn_bwd_workspace_bytes.argtypes = [ctypes.POINTER(Dims)]

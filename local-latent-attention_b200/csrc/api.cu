@@ -184,6 +184,8 @@ extern "C" {
 
 int llattn_version(void) { return LLATTN_VERSION; }
 
+unsigned llattn_fault_status(int reset) { return sm100::read_fault_word(reset != 0); }
+
 const char* llattn_last_error(void) { return g_err; }
 
 int llattn_geometry(const llattn_dims* dims, llattn_geom* out) {

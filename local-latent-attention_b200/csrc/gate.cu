@@ -61,12 +61,18 @@ __global__ void __launch_bounds__(NT) gate_fwd_kernel(Geom g, const T* __restric
     }
     sl = warp_sum(sl);
     sr = warp_sum(sr);
-    if (lane == 0) sw[h] = 1.f / (1.f + expf(-(sl + g.gate_bias - sr)));
+    if (lane == 0) {
+      // both weights computed directly: 1 - w would lose the small one's
+      // precision when the gate saturates
+      const float x = sl + g.gate_bias - sr;
+      sw[2 * h] = 1.f / (1.f + expf(-x));
+      sw[2 * h + 1] = 1.f / (1.f + expf(x));
+    }
   }
   __syncthreads();
   for (int c = threadIdx.x; c < g.d; c += NT) {
-    const float w = sw[c / g.hd];
-    mixed[row * g.d + c] = from_f<T>(w * sL[c] + (1.f - w) * sR[c]);
+    const int h = c / g.hd;
+    mixed[row * g.d + c] = from_f<T>(sw[2 * h] * sL[c] + sw[2 * h + 1] * sR[c]);
   }
 }
 
@@ -111,15 +117,17 @@ __global__ void __launch_bounds__(NT) gate_bwd_kernel(
       sl = warp_sum(sl);
       sr = warp_sum(sr);
       dw = warp_sum(dw);
-      const float w = 1.f / (1.f + expf(-(sl + g.gate_bias - sr)));
-      const float ds = dw * w * (1.f - w);
+      const float x = sl + g.gate_bias - sr;
+      const float w = 1.f / (1.f + expf(-x));
+      const float wr = 1.f / (1.f + expf(x));
+      const float ds = dw * w * wr;
       float dsum = 0.f;
       for (int e = lane; e < g.hd; e += 32) {
         const float dlv = w * dm[e] + ds * gl[e];
         const T dlt = from_f<T>(dlv);
         dl[row * g.d + h * g.hd + e] = dlt;
         dsum = fmaf(to_f<T>(dlt), L[e], dsum);
-        drow[row * g.d + h * g.hd + e] = (1.f - w) * dm[e] - ds * gr[e];
+        drow[row * g.d + h * g.hd + e] = wr * dm[e] - ds * gr[e];
       }
       dsum = warp_sum(dsum);
       if (lane == 0) {
@@ -271,7 +279,7 @@ template <typename T>
 cudaError_t launch_gate_fwd(const Geom& g, const T* local_out, const T* lat, const T* w_rout,
                             const float* b_rout, const float* g_local, const float* g_remote, T* mixed,
                             cudaStream_t s) {
-  const size_t sm = sizeof(float) * (2 * g.d + g.Ld + g.H);
+  const size_t sm = sizeof(float) * (2 * g.d + g.Ld + 2 * g.H);
   cudaError_t e = cudaFuncSetAttribute(gate_fwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
   dim3 grid(g.T, g.B);

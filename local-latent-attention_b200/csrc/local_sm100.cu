@@ -1,16 +1,388 @@
-// Placeholder until the tcgen05 kernels land: every geometry uses SIMT.
+// Local branch on the 5th-generation tensor cores (sm_100a): windowed causal
+// attention with the reference's blockwise mask (models.py:232-305), bf16 in,
+// fp32 accumulation in TMEM, head_dim 64 or 128.
+//
+// Forward, one CTA per (batch, head, 128-query tile), 6 warps:
+//   warp 0     TMA producer: Q tile once, then K/V tiles of 128 keys into a
+//              2-stage ring (tensor map over the qkv projection output
+//              [B, T, 3, H, hd] read in place, 128-byte swizzle, OOB -> 0)
+//   warp 1     TMEM allocator + single-thread tcgen05.mma issuer:
+//              S_j = Q K_j^T (M128 N128, K = hd) into one of two TMEM S
+//              buffers, then O += P_j V_j (M128 N=hd, K = 128 keys)
+//   warps 2-5  softmax: thread r owns query row r = TMEM lane r. Reads S_j
+//              from TMEM, applies the window mask and online softmax (exp2),
+//              writes P_j (bf16, swizzled K-major) to shared memory, rescales
+//              O in TMEM when the running max moves, and finally writes the
+//              normalised row and its logsumexp.
+// Key tiles start at lo(q0) (the first key any row of the tile sees), so a
+// tile of 128 rows with window W touches ceil((127 + W) / 128) key tiles.
+//
+// Every wait is bounded (mbar_wait): on timeout the kernel records a fault
+// bit in g_fault_word, tells the other warps to stop, frees its TMEM and
+// returns; the host reads the word with llattn_fault_status().
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include <cstdlib>
+#include <mutex>
+
 #include "sm100.cuh"
+#include "sm100_ptx.cuh"
 
 namespace llattn {
 namespace sm100 {
-bool fwd_supported(const Geom&, int) { return false; }
-bool bwd_supported(const Geom&, int) { return false; }
-cudaError_t launch_local_fwd(const Geom&, const void*, void*, float*, cudaStream_t) {
-  return cudaErrorNotSupported;
+
+__device__ unsigned int g_fault_word = 0;
+
+namespace {
+
+using namespace ptx;
+
+constexpr int BM = 128;  // query rows per tile (= TMEM lanes)
+constexpr int BN = 128;  // keys per tile
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+enum Fault : unsigned {
+  kFaultProducer = 1u, kFaultMma = 2u, kFaultSoftmax = 4u, kFaultEpilogue = 8u,
+};
+
+__device__ __forceinline__ void raise_fault(unsigned bit, volatile int* abort) {
+  atomicOr(&g_fault_word, bit);
+  *abort = 1;
 }
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+template <int HD>
+struct FwdLayout {
+  static constexpr int PANEL = BM * 128;       // 128 rows x 128 bytes (64 bf16)
+  static constexpr int TILE = BM * HD * 2;      // one 128-row tile of hd columns
+  static constexpr int Q = 0;
+  static constexpr int K = Q + TILE;            // 2 stages
+  static constexpr int V = K + 2 * TILE;        // 2 stages
+  static constexpr int P = V + 2 * TILE;        // 128 x 128 bf16
+  static constexpr int BAR = P + BM * BN * 2;
+  static constexpr int BYTES = BAR + 128;
+};
+
+// Barrier slots in the BAR region.
+enum { B_Q = 0, B_K = 1, B_V = 3, B_KVE = 5, B_S = 7, B_P = 9, B_O = 10, N_BARS = 11 };
+
+template <int HD>
+__global__ void __launch_bounds__(192, 1)
+    local_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, Geom g, bf16* __restrict__ local_out,
+                        float* __restrict__ lse_out) {
+  using L = FwdLayout<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + N_BARS);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int q0 = qt * BM;
+  const int qlast = min(q0 + BM - 1, g.T - 1);
+  const int kbase = local_lo(g, q0);
+  const int khi = qlast - 1;
+  const int nk = khi >= kbase ? (khi - kbase + BN) / BN : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[B_Q], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[B_K + s], 1);
+      mbar_init(&bars[B_V + s], 1);
+      mbar_init(&bars[B_KVE + s], 1);
+      mbar_init(&bars[B_S + s], 1);
+    }
+    mbar_init(&bars[B_P], BM);
+    mbar_init(&bars[B_O], 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS0 = tmem, tS1 = tmem + 128, tO = tmem + 256;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && nk > 0) {
+      prefetch_tmap(&tm_qkv);
+      mbar_expect_tx(&bars[B_Q], L::TILE);
+#pragma unroll
+      for (int p = 0; p < HD / 64; ++p)
+        tma_load_4d(&tm_qkv, &bars[B_Q], smem + L::Q + p * L::PANEL, p * 64, h, q0, b);
+      for (int j = 0; j < nk; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&bars[B_KVE + s], ((j >> 1) - 1) & 1, abort)) {
+          raise_fault(kFaultProducer, abort);
+          break;
+        }
+        const int k0 = kbase + j * BN;
+        mbar_expect_tx(&bars[B_K + s], L::TILE);
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p)
+          tma_load_4d(&tm_qkv, &bars[B_K + s], smem + L::K + s * L::TILE + p * L::PANEL, p * 64, g.H + h, k0, b);
+        mbar_expect_tx(&bars[B_V + s], L::TILE);
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p)
+          tma_load_4d(&tm_qkv, &bars[B_V + s], smem + L::V + s * L::TILE + p * L::PANEL, p * 64, 2 * g.H + h,
+                      k0, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && nk > 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(BM, BN, false, false);
+      constexpr uint32_t idO = idesc_bf16_f32(BM, HD, false, true);
+      const uint32_t q_addr = smem_u32(smem + L::Q);
+      const uint32_t p_addr = smem_u32(smem + L::P);
+      bool ok = mbar_wait(&bars[B_Q], 0, abort);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&bars[B_K + s], (j >> 1) & 1, abort)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + L::K + s * L::TILE);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk / 4) * L::PANEL + (kk % 4) * 32;
+          mma_bf16(s ? tS1 : tS0, desc_sw128(q_addr + off, 16, 1024), desc_sw128(k_addr + off, 16, 1024), idS,
+                   kk > 0);
+        }
+        mma_commit(&bars[B_S + s]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < nk; ++j) {
+        if (j + 1 < nk && !(ok = issue_s(j + 1))) break;
+        if (!(ok = mbar_wait(&bars[B_P], j & 1, abort))) break;
+        if (!(ok = mbar_wait(&bars[B_V + (j & 1)], (j >> 1) & 1, abort))) break;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + L::V + (j & 1) * L::TILE);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t a = desc_sw128(p_addr + (kk / 4) * L::PANEL + (kk % 4) * 32, 16, 1024);
+          const uint64_t bdesc = desc_sw128(v_addr + kk * 16 * 128, L::PANEL, 1024);
+          mma_bf16(tO, a, bdesc, idO, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&bars[B_KVE + (j & 1)]);
+        mma_commit(&bars[B_O]);
+      }
+      if (!ok) raise_fault(kFaultMma, abort);
+    }
+  } else {
+    // ---------------- softmax / epilogue (warps 2..5) ----------------
+    const int row = 32 * (warp & 3) + lane;
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const int t = q0 + row;
+    const bool valid = t < g.T;
+    const int lo = valid ? local_lo(g, t) : 0x7fffffff;
+    const float sc = g.scale * kLog2e;
+    float m = -INFINITY, l = 0.f;
+    uint8_t* prow = smem + L::P + row * 128;
+    bool ok = true;
+    for (int j = 0; j < nk; ++j) {
+      const int s = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_S + s], (j >> 1) & 1, abort));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t tsrc = (s ? tS1 : tS0) + lane_off;
+      const int c_lo = lo - (kbase + j * BN);  // visible columns: [c_lo, c_hi)
+      const int c_hi = t - (kbase + j * BN);
+      // pass 1: masked row max
+      float mx = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tsrc + cc * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int c = cc * 32 + i;
+          if (c >= c_lo && c < c_hi) mx = fmaxf(mx, __uint_as_float(r[i]));
+        }
+      }
+      const float m_new = fmaxf(m, mx * sc);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = exp2f(m - m_use);
+      // P buffer and O are free once PV_{j-1} has completed
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_O], (j - 1) & 1, abort));
+        if (!ok) break;
+      }
+      tc_fence_after();
+      // pass 2: p = exp2(s*sc - m), bf16, swizzled store (chunk c of 8 keys
+      // goes to panel c/8, 16-byte slot (c%8) ^ (row%8))
+      float psum = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tsrc + cc * 32, r);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c = cc * 32 + 2 * i;
+          const float p0 = (c >= c_lo && c < c_hi) ? exp2f(__uint_as_float(r[2 * i]) * sc - m_use) : 0.f;
+          const float p1 =
+              (c + 1 >= c_lo && c + 1 < c_hi) ? exp2f(__uint_as_float(r[2 * i + 1]) * sc - m_use) : 0.f;
+          psum += p0 + p1;
+          pk[i] = pack_bf16(p0, p1);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = cc * 4 + q;
+          const int slot = (chunk & 7) ^ (row & 7);
+          uint4 v = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          *reinterpret_cast<uint4*>(prow + (chunk >> 3) * L::PANEL + slot * 16) = v;
+        }
+      }
+      fence_async_smem();
+      l = l * alpha + psum;
+      m = m_new;
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int cc = 0; cc < HD / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tO + lane_off + cc * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(tO + lane_off + cc * 32, r);
+        }
+        tmem_st_wait();
+      }
+      tc_fence_before();
+      mbar_arrive(&bars[B_P]);
+    }
+    if (!ok) raise_fault(kFaultSoftmax, abort);
+    // epilogue: O / l -> bf16 row, logsumexp (natural log)
+    if (ok && nk > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_O], (nk - 1) & 1, abort));
+    if (!ok) {
+      raise_fault(kFaultEpilogue, abort);
+    } else if (valid) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      bf16* dst = local_out + ((int64_t)b * g.T + t) * g.d + (int64_t)h * HD;
+#pragma unroll
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        uint32_t r[32];
+        if (nk > 0) {
+          tmem_ld32(tO + lane_off + cc * 32, r);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * inv, __uint_as_float(r[2 * i + 1]) * inv);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
+                                                                        pk[4 * q + 3]);
+      }
+      lse_out[((int64_t)b * g.H + h) * g.T + t] = l > 0.f ? (m + log2f(l)) * kLn2 : INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// [B, T, S, H, hd] bf16 viewed as 4-D (hd, S*H, T, B); box (64, 1, 128, 1).
+bool make_rows_map(CUtensorMap* map, const void* base, int B, int T, int slots_x_heads, int hd) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)hd, (cuuint64_t)slots_x_heads, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)hd * 2, (cuuint64_t)slots_x_heads * hd * 2,
+                           (cuuint64_t)T * slots_x_heads * hd * 2};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool force_simt() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("LLATTN_FORCE_SIMT");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+template <int HD>
+cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, cudaStream_t s) {
+  CUtensorMap tm;
+  if (!make_rows_map(&tm, qkv, g.B, g.T, 3 * g.H, HD)) return cudaErrorInvalidValue;
+  const int smem = FwdLayout<HD>::BYTES + 1024;
+  cudaError_t e = cudaFuncSetAttribute(local_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(cdiv(g.T, BM), g.H, g.B);
+  local_fwd_tc_kernel<HD><<<grid, 192, smem, s>>>(tm, g, static_cast<bf16*>(local_out), lse);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool fwd_supported(const Geom& g, int elt_bytes) {
+  return !force_simt() && elt_bytes == 2 && (g.hd == 64 || g.hd == 128) && get_encode() != nullptr;
+}
+
+bool bwd_supported(const Geom&, int) { return false; }
+
+cudaError_t launch_local_fwd(const Geom& g, const void* qkv, void* local_out, float* lse, cudaStream_t s) {
+  if (((uintptr_t)qkv & 15) || ((uintptr_t)local_out & 15)) return cudaErrorMisalignedAddress;
+  if (g.hd == 64) return fwd_hd<64>(g, qkv, local_out, lse, s);
+  return fwd_hd<128>(g, qkv, local_out, lse, s);
+}
+
 cudaError_t launch_local_bwd(const Geom&, const void*, const void*, const float*, const float*, void*,
                              cudaStream_t) {
   return cudaErrorNotSupported;
 }
+
+unsigned read_fault_word(bool reset) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbol(&v, g_fault_word, sizeof(v));
+  if (reset) {
+    unsigned z = 0;
+    cudaMemcpyToSymbol(g_fault_word, &z, sizeof(z));
+  }
+  return v;
+}
+
 }  // namespace sm100
 }  // namespace llattn

@@ -15,5 +15,9 @@ cudaError_t launch_local_fwd(const Geom& g, const void* qkv, void* local_out, fl
 cudaError_t launch_local_bwd(const Geom& g, const void* qkv, const void* dl, const float* lse,
                              const float* delta, void* dqkv, cudaStream_t s);
 
+// Reads (and optionally clears) the device fault word of the current device:
+// bits set by a tensor-core kernel whose bounded wait ran out.
+unsigned read_fault_word(bool reset);
+
 }  // namespace sm100
 }  // namespace llattn
