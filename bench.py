@@ -1,0 +1,407 @@
+"""Benchmark of the LocalLatentAttention block on B200 (one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config cfg2|cfg3|cfg1] [--no-cpu-baseline]
+
+A step is one forward + backward of the drop-in block (LocalLatentAttentionB200:
+cuBLAS projections + the libllattn kernels) over one batch of the configured
+shape, bf16, with a seeded synthetic input and upstream gradient. Default
+workload: cfg2 (B16 T2048 d1536 H12 W256 Nl64 Ld64 Lh2, token-wise latent
+queries). Under torchrun each rank runs its own batch (weak scaling) and
+all-reduces the block's parameter gradients with NCCL (all_reduce_mean), the
+data-parallel exchange of the reference's DDP training.
+
+Keys beyond the base contract:
+  e2e           same metric through the public module API with the step's
+                inputs (x, upstream grad) copied from pinned host memory and
+                dx copied back, inside the timed region
+  roofline      dominant kernel: algorithmic FLOPs (local branch: 4*hd*P fwd,
+                8*hd*P bwd, P = visible query/key pairs) or bytes per launch
+                over its CUDA-event time in the timed region, against
+                MEASURED_PEAKS.json; traffic from the committed ncu summary
+  cpu_baseline  the CPU oracle (a restatement of the reference PyTorch block)
+                on the host cores, bounded sample
+  kernels       per-kernel-group event times (ms per step) and launch counts
+  clocks        nvidia-smi samples taken during the timed region
+
+--impl reference times the reference's CPU implementation of the path (the
+oracle port of models.py's LocalLatentAttention, autocast bf16, all host
+threads) on a bounded sample; under torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    "cfg1": dict(B=2, T=512, d_model=256, n_heads=4, local_window=128, local_block_size=256,
+                 latent_tokens=16, latent_d_model=32, latent_heads=2, latent_query_block_size=0),
+    "cfg2": dict(B=16, T=2048, d_model=1536, n_heads=12, local_window=256, local_block_size=256,
+                 latent_tokens=64, latent_d_model=64, latent_heads=2, latent_query_block_size=0),
+    "cfg3": dict(B=2, T=16384, d_model=1024, n_heads=8, local_window=512, local_block_size=256,
+                 latent_tokens=256, latent_d_model=64, latent_heads=2, latent_query_block_size=64),
+}
+METRIC = "llattn fwd+bwd tokens/s/GPU (bf16, T=2048)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=12.0)
+    return p.parse_args()
+
+
+def block_cfg(name):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import llattn_oracle as O
+
+    d = dict(CONFIGS[name])
+    B, T = d.pop("B"), d.pop("T")
+    return B, T, O.BlockCfg(**d)
+
+
+def config_json(name, n_gpus):
+    c = CONFIGS[name]
+    return {"workload": f"LocalLatentAttention block fwd+bwd ({name})", "global_batch": c["B"] * n_gpus,
+            "seq_len": c["T"], "d_model": c["d_model"], "n_heads": c["n_heads"],
+            "local_window": c["local_window"], "latent_tokens": c["latent_tokens"],
+            "latent_d_model": c["latent_d_model"], "latent_heads": c["latent_heads"],
+            "latent_query_block_size": c["latent_query_block_size"],
+            "parallelism": f"dp{n_gpus}", "l2": "inputs larger than L2 (qkv alone > 126 MB)"}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle = restatement of the reference PyTorch block)
+
+def cpu_time_block(name, seconds, steps=None, warmup=1):
+    import torch
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import llattn_oracle as O
+
+    B, T, cfg = block_cfg(name)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    Bs = 1  # bounded sample: one sequence of the workload per iteration
+    params = {k: v.requires_grad_(True) for k, v in O.init_params(cfg, 0).items()}
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(Bs, T, cfg.d_model, generator=gen).requires_grad_(True)
+    g = torch.randn(Bs, T, cfg.d_model, generator=gen)
+
+    def one():
+        with torch.autocast("cpu", dtype=torch.bfloat16):
+            y = O.block_forward(params, x, cfg)
+        y.float().backward(g)
+
+    for _ in range(warmup):
+        one()
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+        if steps is not None and len(times) >= steps:
+            break
+        if steps is None and time.perf_counter() - t_start > seconds and len(times) >= 2:
+            break
+    per = statistics.median(times)
+    sample = (f"{len(times)} iterations of 1 x {T}-token sequence of {name} (oracle restatement of "
+              f"models.py LocalLatentAttention, autocast bf16, fwd+bwd), median")
+    return Bs * T / per, threads, sample, per
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    tok_s, threads, sample, per = cpu_time_block(args.config, 0, steps=args.steps, warmup=args.warmup)
+    import platform
+
+    cpu = platform.processor() or "cpu"
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    cpu = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    out = {"impl": "reference", "metric": METRIC, "value": round(tok_s, 1), "unit": "tokens/s",
+           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded randn)",
+           "config": config_json(args.config, 1),
+           "cpu_baseline": {"value": round(tok_s, 1), "unit": "tokens/s", "cores": threads,
+                            "kind": "port", "sample": sample, "cpu": cpu},
+           "e2e": {"value": round(tok_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            p = json.load(fh)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def load_traffic():
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as fh:
+            return json.load(fh)
+    except (OSError, ValueError):
+        return {}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import llattn_b200
+    import llattn_oracle as O
+    from llattn_b200 import _lib
+    from parity import model_config
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    B, T, cfg = block_cfg(args.config)
+    m = llattn_b200.LocalLatentAttentionB200(model_config(cfg))
+    m.load_state_dict(O.init_params(cfg, 0))
+    m = m.to(device=dev, dtype=torch.bfloat16)
+    params = [p for p in m.parameters()]
+    gen = torch.Generator().manual_seed(1 + rank)
+    x_h = torch.randn(B, T, cfg.d_model, generator=gen).to(torch.bfloat16).pin_memory()
+    g_h = torch.randn(B, T, cfg.d_model, generator=gen).to(torch.bfloat16).pin_memory()
+    dx_h = torch.empty_like(x_h).pin_memory()
+    x = x_h.to(dev).requires_grad_(True)
+    g = g_h.to(dev)
+    flat = torch.empty(sum(p.numel() for p in params), dtype=torch.bfloat16, device=dev)
+
+    def step():
+        for p in params:
+            p.grad = None
+        x.grad = None
+        y = m(x)
+        y.backward(g)
+        if world > 1:
+            # data-parallel exchange: one flat bucket, all_reduce_mean
+            torch.cat([p.grad.reshape(-1) for p in params], out=flat)
+            dist.all_reduce(flat)
+            flat.div_(world)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    _lib.profile_enable(True)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    kern = _lib.profile_read()
+    _lib.profile_enable(False)
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+
+    # end to end through the public module: pinned host inputs in, dx out
+    for _ in range(2):
+        x.data.copy_(x_h, non_blocking=True)
+        g.copy_(g_h, non_blocking=True)
+        step()
+        dx_h.copy_(x.grad, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(args.steps):
+        x.data.copy_(x_h, non_blocking=True)
+        g.copy_(g_h, non_blocking=True)
+        step()
+        dx_h.copy_(x.grad, non_blocking=True)
+    e3.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = e2.elapsed_time(e3) / args.steps
+
+    t = torch.tensor([ms, ms_e2e], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_e2e = t.tolist()
+    tokens = B * T * world
+    value = tokens / (ms / 1e3)
+    e2e_value = tokens / (ms_e2e / 1e3)
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    # roofline of the dominant kernel group
+    hbm, tflops, peak_kind = load_peaks()
+    P = O.local_pairs(T, cfg.local_window, cfg.local_block_size) * B * cfg.n_heads
+    hd = cfg.head_dim
+    d = cfg.d_model
+    alg = {  # per launch-group call: (amount, unit)
+        "local_fwd": (4.0 * hd * P, "flop"),
+        "local_bwd": (8.0 * hd * P, "flop"),
+        "gate_fwd": ((2 * B * T * d + B * T * d + 2 * d * cfg.latent_d_model) * 2.0, "byte"),
+        "gate_bwd": ((3 * B * T * d) * 2.0 + B * T * d * 4.0, "byte"),
+        "pool_fwd": (B * T * d * 2.0, "byte"),
+        "pool_bwd": (B * T * d * 2.0, "byte"),
+    }
+    per_step = {k: (v[0] / args.steps, v[1] / args.steps) for k, v in kern.items() if v[1] > 0}
+    top = max(per_step, key=lambda k: per_step[k][0])
+    calls = max(1, round(kern[top][1] / args.steps / {"local_bwd": 2, "rout_bwd": 2, "reduce": 3,
+                                                      "latent_bwd": 3}.get(top, 1)))
+    avg_ms = kern[top][0] / args.steps / calls
+    roof = None
+    if top in alg:
+        amount, unit = alg[top]
+        if unit == "flop":
+            ach = amount / (avg_ms / 1e3) / 1e12
+            roof = {"kernel": top, "bound": "tensor", "achieved": round(ach, 2), "peak": tflops,
+                    "unit": "TFLOP/s", "frac": round(ach / tflops, 4), "peak_kind": peak_kind}
+        else:
+            ach = amount / (avg_ms / 1e3) / 1e9
+            roof = {"kernel": top, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm,
+                    "unit": "GB/s", "frac": round(ach / hbm, 4), "peak_kind": peak_kind}
+        tr = load_traffic().get(f"{top}:{args.config}")
+        roof["traffic"] = tr
+        roof["avg_launch_ms"] = round(avg_ms, 4)
+    # also the local branch as a whole (fwd + bwd), the BASELINE target
+    local_ms = sum(per_step.get(k, (0, 0))[0] for k in ("local_fwd", "local_bwd"))
+    local_branch = None
+    if local_ms > 0:
+        ach = 12.0 * hd * P / (local_ms / 1e3) / 1e12
+        local_branch = {"ms": round(local_ms, 4), "achieved": round(ach, 2), "unit": "TFLOP/s",
+                        "frac": round(ach / tflops, 4), "flops": 12.0 * hd * P}
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        tok_s, threads, sample, _ = cpu_time_block(args.config, args.cpu_seconds)
+        cpu = {"value": round(tok_s, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": sample}
+
+    launches = int(sum(v[1] for v in kern.values()))
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded randn inputs and upstream grad; reference default init)",
+        "config": config_json(args.config, world),
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": 2 * x_h.numel() * 2, "d2h_bytes_per_step": dx_h.numel() * 2,
+                "ms_per_step": round(ms_e2e, 4)},
+        "roofline": roof,
+        "local_branch": local_branch,
+        "cpu_baseline": cpu,
+        "gpu_launches": launches,
+        "kernels": {k: {"ms_per_step": round(v[0], 4), "launches_per_step": v[1]} for k, v in per_step.items()},
+        "clocks": clk,
+    }
+    print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

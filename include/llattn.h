@@ -181,6 +181,16 @@ LLATTN_API int llattn_pool_bwd(const llattn_dims* dims, int mode, const void* dp
 LLATTN_API int llattn_fwd(const llattn_fwd_args* args, void* stream);
 LLATTN_API int llattn_bwd(const llattn_bwd_args* args, void* stream);
 
+/* Per-kernel timing with CUDA events on the launching stream, the native
+ * side of the module's set_profile/get_profile_stats (models.py:131-157,
+ * which times phases with host syncs instead). enable != 0 turns it on;
+ * every call resets the totals and returns the number of kernel groups.
+ * llattn_profile_read synchronises on the recorded events and fills, per
+ * group id < n, the summed milliseconds and launch counts. */
+LLATTN_API int llattn_profile_enable(int enable);
+LLATTN_API int llattn_profile_read(double* ms, long long* launches, int n);
+LLATTN_API const char* llattn_profile_name(int id);
+
 #ifdef __cplusplus
 }
 #endif

@@ -18,6 +18,7 @@ POOL_CHUNKS, POOL_QBLOCKS = 0, 1
 EXPORTED = (
     "llattn_version", "llattn_last_error", "llattn_fault_status", "llattn_geometry", "llattn_bwd_workspace_bytes",
     "llattn_pool_fwd", "llattn_pool_bwd", "llattn_fwd", "llattn_bwd",
+    "llattn_profile_enable", "llattn_profile_read", "llattn_profile_name",
 )
 
 
@@ -84,8 +85,30 @@ def lib() -> ctypes.CDLL:
         L.llattn_fwd.restype = ctypes.c_int
         L.llattn_bwd.argtypes = [ctypes.POINTER(BwdArgs), _vp]
         L.llattn_bwd.restype = ctypes.c_int
+        L.llattn_profile_enable.argtypes = [ctypes.c_int]
+        L.llattn_profile_enable.restype = ctypes.c_int
+        L.llattn_profile_read.argtypes = [ctypes.POINTER(ctypes.c_double),
+                                          ctypes.POINTER(ctypes.c_longlong), ctypes.c_int]
+        L.llattn_profile_read.restype = ctypes.c_int
+        L.llattn_profile_name.argtypes = [ctypes.c_int]
+        L.llattn_profile_name.restype = ctypes.c_char_p
         _lib = L
     return _lib
+
+
+def profile_enable(on: bool) -> None:
+    """Turn per-kernel event timing on/off (and reset the totals)."""
+    lib().llattn_profile_enable(1 if on else 0)
+
+
+def profile_read() -> dict:
+    """{kernel group: (total ms, launches)} since the last profile_enable."""
+    L = lib()
+    n = 16
+    ms = (ctypes.c_double * n)()
+    cnt = (ctypes.c_longlong * n)()
+    k = L.llattn_profile_read(ms, cnt, n)
+    return {L.llattn_profile_name(i).decode(): (ms[i], cnt[i]) for i in range(k)}
 
 
 def check(rc: int, what: str) -> None:

@@ -9,6 +9,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "profile.cuh"
 #include "sm100.cuh"
 
 namespace llattn {
@@ -103,17 +104,25 @@ bool al(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
 template <typename T>
 int run_fwd(const Geom& g, const llattn_fwd_args* a, cudaStream_t s) {
   const T* qkv = static_cast<const T*>(a->qkv);
-  int rc = check_launch(launch_latent_fwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv),
+  int rc;
+  {
+    prof::Scope ps(prof::LATENT_FWD, s);
+    rc = check_launch(launch_latent_fwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv),
                                              static_cast<T*>(a->lat), a->lat_lse, s),
                         "latent_fwd");
+  }
   if (rc) return rc;
+  {
+  prof::Scope ps(prof::LOCAL_FWD, s);
   if (sm100::fwd_supported(g, sizeof(T))) {
     rc = check_launch(sm100::launch_local_fwd(g, a->qkv, a->local_out, a->lse, s), "local_fwd_sm100");
   } else {
     rc = check_launch(launch_local_fwd_simt<T>(g, qkv, static_cast<T*>(a->local_out), a->lse, s),
                       "local_fwd_simt");
   }
+  }
   if (rc) return rc;
+  prof::Scope ps(prof::GATE_FWD, s);
   return check_launch(launch_gate_fwd<T>(g, static_cast<const T*>(a->local_out), static_cast<const T*>(a->lat),
                                          static_cast<const T*>(a->w_rout), a->b_rout, a->g_local, a->g_remote,
                                          static_cast<T*>(a->mixed), s),
@@ -136,11 +145,17 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
   const T* lat = static_cast<const T*>(a->lat);
   const T* w_rout = static_cast<const T*>(a->w_rout);
 
-  int rc = check_launch(
+  int rc;
+  {
+  prof::Scope ps(prof::GATE_BWD, s);
+  rc = check_launch(
       launch_gate_bwd<T>(g, static_cast<const T*>(a->local_out), lat, w_rout, a->b_rout, a->g_local, a->g_remote,
                          static_cast<const T*>(a->dmixed), dl, delta, drow, dg_part, L.gate_tok, s),
       "gate_bwd");
+  }
   if (rc) return rc;
+  {
+  prof::Scope ps(prof::LOCAL_BWD, s, 2);
   if (sm100::bwd_supported(g, sizeof(T))) {
     rc = check_launch(sm100::launch_local_bwd(g, a->qkv, dl, a->lse, delta, a->dqkv, s), "local_bwd_sm100");
   } else {
@@ -148,9 +163,15 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
                                                static_cast<T*>(a->dqkv), s),
                       "local_bwd_simt");
   }
+  }
   if (rc) return rc;
+  {
+  prof::Scope ps(prof::ROUT_BWD, s, 2);
   rc = check_launch(launch_rout_bwd<T>(g, drow, lat, w_rout, dlat, dw_part, L.n_split_w, s), "rout_bwd");
+  }
   if (rc) return rc;
+  {
+  prof::Scope ps(prof::REDUCE, s, 3);
   rc = check_launch(launch_reduce_rows(dw_part, L.n_split_w, (int64_t)g.d * g.Ld, a->dw_rout, s), "reduce_dw");
   if (rc) return rc;
   rc = check_launch(launch_reduce_rows(dw_part + (size_t)L.n_split_w * g.d * g.Ld, L.n_split_w, g.d, a->db_rout, s),
@@ -165,7 +186,9 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
   rc = check_launch(cudaMemcpyAsync(a->dg_remote, dg_sum + g.hd, sizeof(float) * g.hd,
                                     cudaMemcpyDeviceToDevice, s),
                     "copy dg_remote");
+  }
   if (rc) return rc;
+  prof::Scope ps(prof::LATENT_BWD, s, 3);
   rc = check_launch(launch_latent_bwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv), lat,
                                          a->lat_lse, dlat, static_cast<T*>(a->drq), dgkv_part, L.n_split_lat,
                                          lat_delta, s),
@@ -215,6 +238,7 @@ int llattn_pool_fwd(const llattn_dims* dims, int mode, const void* x, void* pool
   if (mode != LLATTN_POOL_CHUNKS && mode != LLATTN_POOL_QBLOCKS) return fail(LLATTN_ERR_ARG, "bad pool mode");
   if (d < 1) return fail(LLATTN_ERR_ARG, "pool_fwd: d must be >= 1");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  prof::Scope ps(prof::POOL_FWD, s);
   if (dims->dtype == LLATTN_BF16)
     return check_launch(launch_pool_fwd<bf16>(g, mode, (const bf16*)x, (bf16*)pooled, d, s), "pool_fwd");
   return check_launch(launch_pool_fwd<float>(g, mode, (const float*)x, (float*)pooled, d, s), "pool_fwd");
@@ -228,6 +252,7 @@ int llattn_pool_bwd(const llattn_dims* dims, int mode, const void* dpooled, void
   if (mode != LLATTN_POOL_CHUNKS && mode != LLATTN_POOL_QBLOCKS) return fail(LLATTN_ERR_ARG, "bad pool mode");
   if (d < 1) return fail(LLATTN_ERR_ARG, "pool_bwd: d must be >= 1");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  prof::Scope ps(prof::POOL_BWD, s);
   if (dims->dtype == LLATTN_BF16)
     return check_launch(launch_pool_bwd<bf16>(g, mode, (const bf16*)dpooled, (bf16*)dx, d, s), "pool_bwd");
   return check_launch(launch_pool_bwd<float>(g, mode, (const float*)dpooled, (float*)dx, d, s), "pool_bwd");

@@ -32,6 +32,9 @@
 namespace llattn {
 namespace sm100 {
 
+// Nonzero once any tensor-core kernel gave up on a wait; every later wait
+// (in any CTA) then returns at once, so a broken launch ends within about a
+// second instead of timing out CTA by CTA.
 __device__ unsigned int g_fault_word = 0;
 
 namespace {
@@ -104,6 +107,7 @@ __global__ void __launch_bounds__(192, 1)
     fence_barrier_init();
   }
   if (warp == 1) {
+    __syncwarp();
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -116,6 +120,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0 && nk > 0) {
+      int issued = 0;
       prefetch_tmap(&tm_qkv);
       mbar_expect_tx(&bars[B_Q], L::TILE);
 #pragma unroll
@@ -123,7 +128,7 @@ __global__ void __launch_bounds__(192, 1)
         tma_load_4d(&tm_qkv, &bars[B_Q], smem + L::Q + p * L::PANEL, p * 64, h, q0, b);
       for (int j = 0; j < nk; ++j) {
         const int s = j & 1;
-        if (j >= 2 && !mbar_wait(&bars[B_KVE + s], ((j >> 1) - 1) & 1, abort)) {
+        if (j >= 2 && !mbar_wait(&bars[B_KVE + s], ((j >> 1) - 1) & 1, abort, &g_fault_word)) {
           raise_fault(kFaultProducer, abort);
           break;
         }
@@ -137,6 +142,18 @@ __global__ void __launch_bounds__(192, 1)
         for (int p = 0; p < HD / 64; ++p)
           tma_load_4d(&tm_qkv, &bars[B_V + s], smem + L::V + s * L::TILE + p * L::PANEL, p * 64, 2 * g.H + h,
                       k0, b);
+        issued = j + 1;
+      }
+      if (*abort) {
+        // leave no bulk copy writing into shared memory after exit: wait
+        // (bounded, ignoring the abort flags) for the last loads issued
+        volatile int none = 0;
+        volatile unsigned gnone = 0;
+        mbar_wait(&bars[B_Q], 0, &none, &gnone, 100000000ull);
+        for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j) {
+          mbar_wait(&bars[B_K + (j & 1)], (j >> 1) & 1, &none, &gnone, 100000000ull);
+          mbar_wait(&bars[B_V + (j & 1)], (j >> 1) & 1, &none, &gnone, 100000000ull);
+        }
       }
     }
   } else if (warp == 1) {
@@ -146,10 +163,10 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t idO = idesc_bf16_f32(BM, HD, false, true);
       const uint32_t q_addr = smem_u32(smem + L::Q);
       const uint32_t p_addr = smem_u32(smem + L::P);
-      bool ok = mbar_wait(&bars[B_Q], 0, abort);
+      bool ok = mbar_wait(&bars[B_Q], 0, abort, &g_fault_word);
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
-        if (!mbar_wait(&bars[B_K + s], (j >> 1) & 1, abort)) return false;
+        if (!mbar_wait(&bars[B_K + s], (j >> 1) & 1, abort, &g_fault_word)) return false;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + L::K + s * L::TILE);
 #pragma unroll
@@ -164,8 +181,8 @@ __global__ void __launch_bounds__(192, 1)
       if (ok) ok = issue_s(0);
       for (int j = 0; ok && j < nk; ++j) {
         if (j + 1 < nk && !(ok = issue_s(j + 1))) break;
-        if (!(ok = mbar_wait(&bars[B_P], j & 1, abort))) break;
-        if (!(ok = mbar_wait(&bars[B_V + (j & 1)], (j >> 1) & 1, abort))) break;
+        if (!(ok = mbar_wait(&bars[B_P], j & 1, abort, &g_fault_word))) break;
+        if (!(ok = mbar_wait(&bars[B_V + (j & 1)], (j >> 1) & 1, abort, &g_fault_word))) break;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(smem + L::V + (j & 1) * L::TILE);
 #pragma unroll
@@ -192,7 +209,7 @@ __global__ void __launch_bounds__(192, 1)
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
       const int s = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_S + s], (j >> 1) & 1, abort));
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_S + s], (j >> 1) & 1, abort, &g_fault_word));
       if (!ok) break;
       tc_fence_after();
       const uint32_t tsrc = (s ? tS1 : tS0) + lane_off;
@@ -216,7 +233,7 @@ __global__ void __launch_bounds__(192, 1)
       const float alpha = exp2f(m - m_use);
       // P buffer and O are free once PV_{j-1} has completed
       if (j > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_O], (j - 1) & 1, abort));
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_O], (j - 1) & 1, abort, &g_fault_word));
         if (!ok) break;
       }
       tc_fence_after();
@@ -265,14 +282,16 @@ __global__ void __launch_bounds__(192, 1)
       mbar_arrive(&bars[B_P]);
     }
     if (!ok) raise_fault(kFaultSoftmax, abort);
-    // epilogue: O / l -> bf16 row, logsumexp (natural log)
-    if (ok && nk > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_O], (nk - 1) & 1, abort));
+    // epilogue: O / l -> bf16 row, logsumexp (natural log). The TMEM loads
+    // are warp-collective (.sync.aligned): every lane executes them, rows
+    // past T only skip the stores.
+    if (ok && nk > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_O], (nk - 1) & 1, abort, &g_fault_word));
     if (!ok) {
       raise_fault(kFaultEpilogue, abort);
-    } else if (valid) {
+    } else {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      bf16* dst = local_out + ((int64_t)b * g.T + t) * g.d + (int64_t)h * HD;
+      bf16* dst = local_out + ((int64_t)b * g.T + (valid ? t : 0)) * g.d + (int64_t)h * HD;
 #pragma unroll
       for (int cc = 0; cc < HD / 32; ++cc) {
         uint32_t r[32];
@@ -287,17 +306,20 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i)
           pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * inv, __uint_as_float(r[2 * i + 1]) * inv);
+        if (valid) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
-                                                                        pk[4 * q + 3]);
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        }
       }
-      lse_out[((int64_t)b * g.H + h) * g.T + t] = l > 0.f ? (m + log2f(l)) * kLn2 : INFINITY;
+      if (valid) lse_out[((int64_t)b * g.H + h) * g.T + t] = l > 0.f ? (m + log2f(l)) * kLn2 : INFINITY;
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();  // lane 0 issued the MMAs alone; dealloc is warp-collective
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -334,13 +356,11 @@ bool make_rows_map(CUtensorMap* map, const void* base, int B, int T, int slots_x
   return r == CUDA_SUCCESS;
 }
 
+// LLATTN_FORCE_SIMT=1 routes bf16 through the SIMT kernels (used by the tests
+// to compare the two implementations of the same math).
 bool force_simt() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = std::getenv("LLATTN_FORCE_SIMT");
-    v = (e && e[0] == '1') ? 1 : 0;
-  }
-  return v == 1;
+  const char* e = std::getenv("LLATTN_FORCE_SIMT");
+  return e && e[0] == '1';
 }
 
 template <int HD>

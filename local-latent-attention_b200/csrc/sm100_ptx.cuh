@@ -54,16 +54,18 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Bounded wait: gives up after ~`limit_ns` of wall time or when *abort is
-// set by another warp; returns false then. Never spins forever.
+// Bounded wait: gives up after ~`limit_ns` of wall time, or as soon as
+// *abort (this CTA) or *global_abort (any CTA of any launch) is nonzero;
+// returns false then. Never spins forever.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          uint64_t limit_ns = 2000000000ull) {
+                                          volatile unsigned* global_abort,
+                                          uint64_t limit_ns = 1000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
-      if (*abort) return false;
+      if (*abort || *global_abort) return false;
       if (globaltimer_ns() - t0 > limit_ns) return false;
     }
   }

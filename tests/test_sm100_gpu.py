@@ -1,0 +1,88 @@
+"""The tcgen05 (sm_100a tensor-core) local-branch kernels against the exact
+SIMT kernels of the same math and against the oracle, on bf16 inputs.
+
+Both implementations run through the C ABI (torch op -> llattn_fwd/bwd); the
+SIMT one is selected with LLATTN_FORCE_SIMT=1. After every launch the
+device fault word (bounded waits that ran out) must be 0."""
+
+import math
+import os
+
+import pytest
+import torch
+
+import llattn_oracle as O
+from parity import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _fault():
+    from llattn_b200 import _lib
+    return _lib.lib().llattn_fault_status(1)
+
+
+def _inputs(B, T, H, hd, Lh=2, ldh=32, Nl=32, QB=0, seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    d, Ld = H * hd, Lh * ldh
+    cs, nc = O.chunk_layout(T, Nl)
+    tq = math.ceil(T / min(T, QB)) if QB > 1 else T
+    f = lambda *s: torch.randn(*s, generator=gen)
+    return dict(qkv=f(B, T, 3 * d), rq=f(B, tq, Ld), gkv=f(B, nc, 2 * Ld), w=f(d, Ld) / math.sqrt(Ld),
+                b=f(d) * 0.1, gl=f(hd) / math.sqrt(hd), gr=f(hd) / math.sqrt(hd))
+
+
+def _run_fwd(inp, H, Lh, W, LBS, Nl, QB, force_simt):
+    import llattn_b200
+
+    os.environ["LLATTN_FORCE_SIMT"] = "1" if force_simt else "0"
+    try:
+        dev = {k: v.cuda().to(torch.bfloat16 if k in ("qkv", "rq", "gkv", "w") else torch.float32)
+               for k, v in inp.items()}
+        outs = torch.ops.llattn_b200.attn_fwd(dev["qkv"], dev["rq"], dev["gkv"], dev["w"], dev["b"],
+                                              dev["gl"], dev["gr"], H, Lh, W, LBS, Nl, QB, 0.0)
+        torch.cuda.synchronize()
+    finally:
+        os.environ["LLATTN_FORCE_SIMT"] = "0"
+    return [o.cpu() for o in outs]
+
+
+FWD_CASES = [
+    # B, T, H, hd, W, LBS
+    (1, 256, 1, 128, 256, 256),
+    (1, 300, 2, 64, 128, 256),
+    (2, 1000, 2, 128, 256, 256),
+    (1, 777, 3, 64, 300, 200),
+    (1, 2100, 1, 128, 1024, 256),
+    (2, 129, 2, 128, 16, 32),
+    (1, 1, 1, 128, 4, 256),
+    (1, 4096, 2, 128, 512, 256),
+]
+
+
+@pytest.mark.parametrize("case", FWD_CASES)
+def test_local_fwd_tc_matches_simt(case):
+    B, T, H, hd, W, LBS = case
+    inp = _inputs(B, T, H, hd)
+    tc = _run_fwd(inp, H, 2, W, LBS, 32, 0, False)
+    assert _fault() == 0
+    ref = _run_fwd(inp, H, 2, W, LBS, 32, 0, True)
+    # local_out (bf16) and lse
+    assert rel_err(tc[1].float(), ref[1].float()) < 1e-2, rel_err(tc[1].float(), ref[1].float())
+    fin = torch.isfinite(ref[2])
+    assert torch.equal(fin, torch.isfinite(tc[2]))
+    if fin.any():
+        assert (tc[2][fin] - ref[2][fin]).abs().max().item() < 1e-3
+    assert rel_err(tc[0].float(), ref[0].float()) < 1e-2
+
+
+def test_local_fwd_tc_against_oracle():
+    B, T, H, hd, W, LBS = 1, 700, 2, 128, 256, 256
+    inp = _inputs(B, T, H, hd)
+    tc = _run_fwd(inp, H, 2, W, LBS, 32, 0, False)
+    assert _fault() == 0
+    qkv = inp["qkv"].to(torch.bfloat16).double()
+    q, k, v = qkv.view(B, T, 3, H, hd).unbind(2)
+    ref = O.local_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), W, LBS)
+    got = tc[1].view(B, T, H, hd).transpose(1, 2)
+    assert rel_err(got, ref) < 2e-2
