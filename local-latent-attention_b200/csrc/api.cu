@@ -154,15 +154,19 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
       "gate_bwd");
   }
   if (rc) return rc;
-  {
-  prof::Scope ps(prof::LOCAL_BWD, s, 2);
   if (sm100::bwd_supported(g, sizeof(T))) {
-    rc = check_launch(sm100::launch_local_bwd(g, a->qkv, dl, a->lse, delta, a->dqkv, s), "local_bwd_sm100");
+    {
+      prof::Scope ps(prof::LOCAL_DQ, s);
+      rc = check_launch(sm100::launch_local_dq(g, a->qkv, dl, a->lse, delta, a->dqkv, s), "local_dq_sm100");
+    }
+    if (rc) return rc;
+    prof::Scope ps(prof::LOCAL_DKV, s);
+    rc = check_launch(sm100::launch_local_dkv(g, a->qkv, dl, a->lse, delta, a->dqkv, s), "local_dkv_sm100");
   } else {
+    prof::Scope ps(prof::LOCAL_BWD, s, 2);
     rc = check_launch(launch_local_bwd_simt<T>(g, static_cast<const T*>(a->qkv), dl, a->lse, delta,
                                                static_cast<T*>(a->dqkv), s),
                       "local_bwd_simt");
-  }
   }
   if (rc) return rc;
   {

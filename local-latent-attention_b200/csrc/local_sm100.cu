@@ -23,6 +23,7 @@
 #include <cudaTypedefs.h>
 #include <math.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <mutex>
 
@@ -325,6 +326,8 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+#include "local_sm100_bwd.cuh"
+
 // ---------------------------------------------------------------------------
 // host side
 
@@ -341,14 +344,14 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// [B, T, S, H, hd] bf16 viewed as 4-D (hd, S*H, T, B); box (64, 1, 128, 1).
-bool make_rows_map(CUtensorMap* map, const void* base, int B, int T, int slots_x_heads, int hd) {
+// [B, T, S, H, hd] bf16 viewed as 4-D (hd, S*H, T, B); box (64, 1, rows, 1).
+bool make_rows_map(CUtensorMap* map, const void* base, int B, int T, int slots_x_heads, int hd, int rows = 128) {
   auto enc = get_encode();
   if (!enc) return false;
   cuuint64_t dims[4] = {(cuuint64_t)hd, (cuuint64_t)slots_x_heads, (cuuint64_t)T, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)hd * 2, (cuuint64_t)slots_x_heads * hd * 2,
                            (cuuint64_t)T * slots_x_heads * hd * 2};
-  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -367,11 +370,42 @@ template <int HD>
 cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, cudaStream_t s) {
   CUtensorMap tm;
   if (!make_rows_map(&tm, qkv, g.B, g.T, 3 * g.H, HD)) return cudaErrorInvalidValue;
-  const int smem = FwdLayout<HD>::BYTES + 1024;
+  // at least 116 KB so a second CTA never shares the SM (and its TMEM)
+  const int smem = std::max(FwdLayout<HD>::BYTES + 1024, 116 * 1024);
   cudaError_t e = cudaFuncSetAttribute(local_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.T, BM), g.H, g.B);
   local_fwd_tc_kernel<HD><<<grid, 192, smem, s>>>(tm, g, static_cast<bf16*>(local_out), lse);
+  return cudaGetLastError();
+}
+
+template <int HD>
+cudaError_t dq_hd(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta, void* dqkv,
+                  cudaStream_t s) {
+  CUtensorMap q128, q64, do128;
+  if (!make_rows_map(&q128, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_rows_map(&q64, qkv, g.B, g.T, 3 * g.H, HD, 64) ||
+      !make_rows_map(&do128, dl, g.B, g.T, g.H, HD, 128))
+    return cudaErrorInvalidValue;
+  const int smem = std::max(DqLayout<HD>::BYTES + 1024, 116 * 1024);
+  cudaError_t e = cudaFuncSetAttribute(local_dq_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(cdiv(g.T, BM), g.H, g.B);
+  local_dq_tc_kernel<HD><<<grid, 192, smem, s>>>(q128, q64, do128, g, lse, delta, static_cast<bf16*>(dqkv));
+  return cudaGetLastError();
+}
+
+template <int HD>
+cudaError_t dkv_hd(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta, void* dqkv,
+                   cudaStream_t s) {
+  CUtensorMap q128, q64, do64;
+  if (!make_rows_map(&q128, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_rows_map(&q64, qkv, g.B, g.T, 3 * g.H, HD, 64) ||
+      !make_rows_map(&do64, dl, g.B, g.T, g.H, HD, 64))
+    return cudaErrorInvalidValue;
+  const int smem = std::max(DkvLayout<HD>::BYTES + 1024, 116 * 1024);
+  cudaError_t e = cudaFuncSetAttribute(local_dkv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(cdiv(g.T, BM), g.H, g.B);
+  local_dkv_tc_kernel<HD><<<grid, 192, smem, s>>>(q128, q64, do64, g, lse, delta, static_cast<bf16*>(dqkv));
   return cudaGetLastError();
 }
 
@@ -381,7 +415,7 @@ bool fwd_supported(const Geom& g, int elt_bytes) {
   return !force_simt() && elt_bytes == 2 && (g.hd == 64 || g.hd == 128) && get_encode() != nullptr;
 }
 
-bool bwd_supported(const Geom&, int) { return false; }
+bool bwd_supported(const Geom& g, int elt_bytes) { return fwd_supported(g, elt_bytes); }
 
 cudaError_t launch_local_fwd(const Geom& g, const void* qkv, void* local_out, float* lse, cudaStream_t s) {
   if (((uintptr_t)qkv & 15) || ((uintptr_t)local_out & 15)) return cudaErrorMisalignedAddress;
@@ -389,9 +423,18 @@ cudaError_t launch_local_fwd(const Geom& g, const void* qkv, void* local_out, fl
   return fwd_hd<128>(g, qkv, local_out, lse, s);
 }
 
-cudaError_t launch_local_bwd(const Geom&, const void*, const void*, const float*, const float*, void*,
-                             cudaStream_t) {
-  return cudaErrorNotSupported;
+cudaError_t launch_local_dq(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta,
+                            void* dqkv, cudaStream_t s) {
+  if (((uintptr_t)qkv & 15) || ((uintptr_t)dl & 15) || ((uintptr_t)dqkv & 15)) return cudaErrorMisalignedAddress;
+  if (g.hd == 64) return dq_hd<64>(g, qkv, dl, lse, delta, dqkv, s);
+  return dq_hd<128>(g, qkv, dl, lse, delta, dqkv, s);
+}
+
+cudaError_t launch_local_dkv(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta,
+                             void* dqkv, cudaStream_t s) {
+  if (((uintptr_t)qkv & 15) || ((uintptr_t)dl & 15) || ((uintptr_t)dqkv & 15)) return cudaErrorMisalignedAddress;
+  if (g.hd == 64) return dkv_hd<64>(g, qkv, dl, lse, delta, dqkv, s);
+  return dkv_hd<128>(g, qkv, dl, lse, delta, dqkv, s);
 }
 
 unsigned read_fault_word(bool reset) {

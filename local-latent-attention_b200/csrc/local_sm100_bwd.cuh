@@ -1,0 +1,520 @@
+// Backward of the tensor-core local branch (included by local_sm100.cu, which
+// provides the fault word, the tensor-map helpers and the ptx wrappers).
+//
+// With s = scale q.k, P = exp(s - lse) on visible pairs, dO = dlocal (the
+// gate backward's gradient of the local output), D = rowsum(dO * O):
+//   dS = P (dO.v - D),  dq = scale sum_j dS k_j,  dk_j = scale sum_t dS q_t,
+//   dv_j = sum_t P dO_t.
+// Two kernels, no atomics, deterministic:
+//   dq  : one CTA per (b, h, 128-query tile); loops over 64-key tiles.
+//   dkv : one CTA per (b, h, 128-key tile); loops over 64-query tiles
+//         t in [k0+1, k0+127+W].
+// Both keep the two score-like tiles (S and dP) of the current inner tile in
+// TMEM, double-buffered, so the softmax warps of tile j overlap the MMAs of
+// tile j+1.
+
+// ---------------------------------------------------------------------------
+// dq
+
+template <int HD>
+struct DqLayout {
+  static constexpr int BNK = 64;                  // keys per inner tile
+  static constexpr int QPANEL = BM * 128;          // 128-row panel (16 KB)
+  static constexpr int KPANEL = BNK * 128;         // 64-row panel (8 KB)
+  static constexpr int QTILE = BM * HD * 2;
+  static constexpr int KTILE = BNK * HD * 2;
+  static constexpr int Q = 0;
+  static constexpr int DO = Q + QTILE;
+  static constexpr int K = DO + QTILE;             // 2 stages
+  static constexpr int V = K + 2 * KTILE;          // 2 stages
+  static constexpr int DS = V + 2 * KTILE;         // 2 buffers of 128 x 64 bf16
+  static constexpr int BAR = DS + 2 * BM * BNK * 2;
+  static constexpr int BYTES = BAR + 256;
+};
+
+enum { DQ_Q = 0, DQ_K = 1, DQ_V = 3, DQ_KVE = 5, DQ_SP = 7, DQ_DS = 9, DQ_DQ = 11, DQ_NB = 13 };
+
+template <int HD>
+__global__ void __launch_bounds__(192, 1)
+    local_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv128, const __grid_constant__ CUtensorMap tm_qkv64,
+                       const __grid_constant__ CUtensorMap tm_do128, Geom g, const float* __restrict__ lse,
+                       const float* __restrict__ delta, bf16* __restrict__ dqkv) {
+  using L = DqLayout<HD>;
+  constexpr int BNK = L::BNK;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + DQ_NB);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int q0 = blockIdx.x * BM;
+  const int qlast = min(q0 + BM - 1, g.T - 1);
+  const int kbase = local_lo(g, q0);
+  const int khi = qlast - 1;
+  const int nk = khi >= kbase ? (khi - kbase + BNK) / BNK : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[DQ_Q], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[DQ_K + s], 1);
+      mbar_init(&bars[DQ_V + s], 1);
+      mbar_init(&bars[DQ_KVE + s], 1);
+      mbar_init(&bars[DQ_SP + s], 1);
+      mbar_init(&bars[DQ_DS + s], BM);
+      mbar_init(&bars[DQ_DQ + s], 1);
+    }
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // S buffers at columns [0,64) and [64,128); dP at [128,192) and [192,256)
+  const uint32_t tDQ = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0 && nk > 0) {
+      int issued = 0;
+      prefetch_tmap(&tm_qkv128);
+      prefetch_tmap(&tm_qkv64);
+      prefetch_tmap(&tm_do128);
+      mbar_expect_tx(&bars[DQ_Q], 2 * L::QTILE);
+#pragma unroll
+      for (int p = 0; p < HD / 64; ++p) {
+        tma_load_4d(&tm_qkv128, &bars[DQ_Q], smem + L::Q + p * L::QPANEL, p * 64, h, q0, b);
+        tma_load_4d(&tm_do128, &bars[DQ_Q], smem + L::DO + p * L::QPANEL, p * 64, h, q0, b);
+      }
+      for (int j = 0; j < nk; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&bars[DQ_KVE + s], ((j >> 1) - 1) & 1, abort, &g_fault_word)) {
+          raise_fault(kFaultProducer, abort);
+          break;
+        }
+        const int k0 = kbase + j * BNK;
+        mbar_expect_tx(&bars[DQ_K + s], L::KTILE);
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p)
+          tma_load_4d(&tm_qkv64, &bars[DQ_K + s], smem + L::K + s * L::KTILE + p * L::KPANEL, p * 64, g.H + h, k0,
+                      b);
+        mbar_expect_tx(&bars[DQ_V + s], L::KTILE);
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p)
+          tma_load_4d(&tm_qkv64, &bars[DQ_V + s], smem + L::V + s * L::KTILE + p * L::KPANEL, p * 64,
+                      2 * g.H + h, k0, b);
+        issued = j + 1;
+      }
+      if (*abort) {
+        volatile int none = 0;
+        volatile unsigned gnone = 0;
+        mbar_wait(&bars[DQ_Q], 0, &none, &gnone, 100000000ull);
+        for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j) {
+          mbar_wait(&bars[DQ_K + (j & 1)], (j >> 1) & 1, &none, &gnone, 100000000ull);
+          mbar_wait(&bars[DQ_V + (j & 1)], (j >> 1) & 1, &none, &gnone, 100000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nk > 0) {
+      constexpr uint32_t idSP = idesc_bf16_f32(BM, BNK, false, false);  // Q K^T, dO V^T
+      constexpr uint32_t idDQ = idesc_bf16_f32(BM, HD, false, true);    // dS K (K MN-major)
+      const uint32_t q_addr = smem_u32(smem + L::Q), do_addr = smem_u32(smem + L::DO);
+      bool ok = mbar_wait(&bars[DQ_Q], 0, abort, &g_fault_word);
+      auto issue_sp = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&bars[DQ_K + s], (j >> 1) & 1, abort, &g_fault_word)) return false;
+        if (!mbar_wait(&bars[DQ_V + s], (j >> 1) & 1, abort, &g_fault_word)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + L::K + s * L::KTILE);
+        const uint32_t v_addr = smem_u32(smem + L::V + s * L::KTILE);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t aoff = (kk / 4) * L::QPANEL + (kk % 4) * 32;
+          const uint32_t boff = (kk / 4) * L::KPANEL + (kk % 4) * 32;
+          mma_bf16(tmem + s * BNK, desc_sw128(q_addr + aoff, 16, 1024), desc_sw128(k_addr + boff, 16, 1024), idSP,
+                   kk > 0);
+          mma_bf16(tmem + 128 + s * BNK, desc_sw128(do_addr + aoff, 16, 1024), desc_sw128(v_addr + boff, 16, 1024),
+                   idSP, kk > 0);
+        }
+        mma_commit(&bars[DQ_SP + s]);
+        return true;
+      };
+      if (ok) ok = issue_sp(0);
+      for (int j = 0; ok && j < nk; ++j) {
+        if (j + 1 < nk && !(ok = issue_sp(j + 1))) break;
+        const int s = j & 1;
+        if (!(ok = mbar_wait(&bars[DQ_DS + s], (j >> 1) & 1, abort, &g_fault_word))) break;
+        tc_fence_after();
+        const uint32_t ds_addr = smem_u32(smem + L::DS + s * BM * BNK * 2);
+        const uint32_t k_addr = smem_u32(smem + L::K + s * L::KTILE);
+#pragma unroll
+        for (int kk = 0; kk < BNK / 16; ++kk)
+          mma_bf16(tDQ, desc_sw128(ds_addr + kk * 32, 16, 1024), desc_sw128(k_addr + kk * 2048, L::KPANEL, 1024),
+                   idDQ, (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&bars[DQ_DQ + s]);
+        mma_commit(&bars[DQ_KVE + s]);
+      }
+      if (!ok) raise_fault(kFaultMma, abort);
+    }
+  } else {
+    const int row = 32 * (warp & 3) + lane;
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const int t = q0 + row;
+    const bool valid = t < g.T;
+    const int lo = valid ? local_lo(g, t) : 0x7fffffff;
+    const float sc = g.scale * kLog2e;
+    const float lse2 = valid ? lse[((int64_t)b * g.H + h) * g.T + t] * kLog2e : INFINITY;
+    const float dt = valid ? delta[((int64_t)b * g.H + h) * g.T + t] : 0.f;
+    bool ok = true;
+    for (int j = 0; j < nk; ++j) {
+      const int s = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[DQ_SP + s], (j >> 1) & 1, abort, &g_fault_word));
+      if (ok && j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(&bars[DQ_DQ + s], ((j >> 1) - 1) & 1, abort,
+                                                                 &g_fault_word));
+      if (!ok) break;
+      tc_fence_after();
+      const int k0 = kbase + j * BNK;
+      const int c_lo = lo - k0, c_hi = t - k0;
+      uint8_t* dsrow = smem + L::DS + s * BM * BNK * 2 + row * 128;
+#pragma unroll
+      for (int cc = 0; cc < BNK / 32; ++cc) {
+        uint32_t rs[32], rp[32];
+        tmem_ld32(tmem + lane_off + s * BNK + cc * 32, rs);
+        tmem_ld32(tmem + lane_off + 128 + s * BNK + cc * 32, rp);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float v[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int c = cc * 32 + 2 * i + u;
+            const float p = (c >= c_lo && c < c_hi) ? exp2f(__uint_as_float(rs[2 * i + u]) * sc - lse2) : 0.f;
+            v[u] = p * (__uint_as_float(rp[2 * i + u]) - dt);
+          }
+          pk[i] = pack_bf16(v[0], v[1]);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = cc * 4 + q;
+          const int slot = (chunk & 7) ^ (row & 7);
+          *reinterpret_cast<uint4*>(dsrow + slot * 16) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
+                                                                    pk[4 * q + 3]);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars[DQ_DS + s]);
+    }
+    if (!ok) raise_fault(kFaultSoftmax, abort);
+    if (ok && nk > 0)
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[DQ_DQ + ((nk - 1) & 1)], ((nk - 1) >> 1) & 1, abort,
+                                             &g_fault_word));
+    if (!ok) {
+      raise_fault(kFaultEpilogue, abort);
+    } else {
+      tc_fence_after();
+      bf16* dst = dqkv + ((int64_t)b * g.T + (valid ? t : 0)) * 3 * g.d + (int64_t)h * HD;
+#pragma unroll
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        uint32_t r[32];
+        if (nk > 0) {
+          tmem_ld32(tDQ + lane_off + cc * 32, r);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * g.scale, __uint_as_float(r[2 * i + 1]) * g.scale);
+        if (valid) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dk, dv
+
+template <int HD>
+struct DkvLayout {
+  static constexpr int BNQ = 64;                   // queries per inner tile
+  static constexpr int KPANEL = BM * 128;          // 128-key panel (16 KB)
+  static constexpr int QPANEL = BNQ * 128;         // 64-query panel (8 KB)
+  static constexpr int KTILE = BM * HD * 2;
+  static constexpr int QTILE = BNQ * HD * 2;
+  static constexpr int K = 0;
+  static constexpr int V = K + KTILE;
+  static constexpr int Q = V + KTILE;              // 2 stages
+  static constexpr int DO = Q + 2 * QTILE;         // 2 stages
+  static constexpr int PT = DO + 2 * QTILE;        // 2 buffers of 128 x 64 bf16
+  static constexpr int DST = PT + 2 * BM * BNQ * 2;
+  static constexpr int VEC = DST + 2 * BM * BNQ * 2;  // per softmax warp: {lse2, D, lo}[64]
+  static constexpr int BAR = VEC + 4 * 3 * BNQ * 4;
+  static constexpr int BYTES = BAR + 256;
+};
+
+enum { KV_KV = 0, KV_QD = 1, KV_QDE = 3, KV_SP = 5, KV_PD = 7, KV_DKV = 9, KV_NB = 11 };
+
+template <int HD>
+__global__ void __launch_bounds__(192, 1)
+    local_dkv_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv128, const __grid_constant__ CUtensorMap tm_qkv64,
+                        const __grid_constant__ CUtensorMap tm_do64, Geom g, const float* __restrict__ lse,
+                        const float* __restrict__ delta, bf16* __restrict__ dqkv) {
+  using L = DkvLayout<HD>;
+  constexpr int BNQ = L::BNQ;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + KV_NB);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int k0 = blockIdx.x * BM;
+  const int tfirst = k0 + 1;
+  const int tlast = min(g.T - 1, k0 + BM - 1 + g.W);
+  const int nq = tlast >= tfirst ? (tlast - tfirst + BNQ) / BNQ : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[KV_KV], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[KV_QD + s], 1);
+      mbar_init(&bars[KV_QDE + s], 1);
+      mbar_init(&bars[KV_SP + s], 1);
+      mbar_init(&bars[KV_PD + s], BM);
+      mbar_init(&bars[KV_DKV + s], 1);
+    }
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // S^T at [0,64) / [64,128), dP^T at [128,192) / [192,256), dV, dK after
+  const uint32_t tDV = tmem + 256, tDK = tmem + 256 + HD;
+
+  if (warp == 0) {
+    if (lane == 0 && nq > 0) {
+      int issued = 0;
+      prefetch_tmap(&tm_qkv128);
+      prefetch_tmap(&tm_qkv64);
+      prefetch_tmap(&tm_do64);
+      mbar_expect_tx(&bars[KV_KV], 2 * L::KTILE);
+#pragma unroll
+      for (int p = 0; p < HD / 64; ++p) {
+        tma_load_4d(&tm_qkv128, &bars[KV_KV], smem + L::K + p * L::KPANEL, p * 64, g.H + h, k0, b);
+        tma_load_4d(&tm_qkv128, &bars[KV_KV], smem + L::V + p * L::KPANEL, p * 64, 2 * g.H + h, k0, b);
+      }
+      for (int i = 0; i < nq; ++i) {
+        const int s = i & 1;
+        if (i >= 2 && !mbar_wait(&bars[KV_QDE + s], ((i >> 1) - 1) & 1, abort, &g_fault_word)) {
+          raise_fault(kFaultProducer, abort);
+          break;
+        }
+        const int t0 = tfirst + i * BNQ;
+        mbar_expect_tx(&bars[KV_QD + s], 2 * L::QTILE);
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p) {
+          tma_load_4d(&tm_qkv64, &bars[KV_QD + s], smem + L::Q + s * L::QTILE + p * L::QPANEL, p * 64, h, t0, b);
+          tma_load_4d(&tm_do64, &bars[KV_QD + s], smem + L::DO + s * L::QTILE + p * L::QPANEL, p * 64, h, t0, b);
+        }
+        issued = i + 1;
+      }
+      if (*abort) {
+        volatile int none = 0;
+        volatile unsigned gnone = 0;
+        mbar_wait(&bars[KV_KV], 0, &none, &gnone, 100000000ull);
+        for (int i = issued - 2 < 0 ? 0 : issued - 2; i < issued; ++i)
+          mbar_wait(&bars[KV_QD + (i & 1)], (i >> 1) & 1, &none, &gnone, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nq > 0) {
+      constexpr uint32_t idSP = idesc_bf16_f32(BM, BNQ, false, false);  // K Q^T, V dO^T
+      constexpr uint32_t idKV = idesc_bf16_f32(BM, HD, false, true);    // P^T dO, dS^T Q
+      const uint32_t k_addr = smem_u32(smem + L::K), v_addr = smem_u32(smem + L::V);
+      bool ok = mbar_wait(&bars[KV_KV], 0, abort, &g_fault_word);
+      auto issue_sp = [&](int i) -> bool {
+        const int s = i & 1;
+        if (!mbar_wait(&bars[KV_QD + s], (i >> 1) & 1, abort, &g_fault_word)) return false;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(smem + L::Q + s * L::QTILE);
+        const uint32_t do_addr = smem_u32(smem + L::DO + s * L::QTILE);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t aoff = (kk / 4) * L::KPANEL + (kk % 4) * 32;
+          const uint32_t boff = (kk / 4) * L::QPANEL + (kk % 4) * 32;
+          mma_bf16(tmem + s * BNQ, desc_sw128(k_addr + aoff, 16, 1024), desc_sw128(q_addr + boff, 16, 1024), idSP,
+                   kk > 0);
+          mma_bf16(tmem + 128 + s * BNQ, desc_sw128(v_addr + aoff, 16, 1024), desc_sw128(do_addr + boff, 16, 1024),
+                   idSP, kk > 0);
+        }
+        mma_commit(&bars[KV_SP + s]);
+        return true;
+      };
+      if (ok) ok = issue_sp(0);
+      for (int i = 0; ok && i < nq; ++i) {
+        if (i + 1 < nq && !(ok = issue_sp(i + 1))) break;
+        const int s = i & 1;
+        if (!(ok = mbar_wait(&bars[KV_PD + s], (i >> 1) & 1, abort, &g_fault_word))) break;
+        tc_fence_after();
+        const uint32_t pt_addr = smem_u32(smem + L::PT + s * BM * BNQ * 2);
+        const uint32_t dst_addr = smem_u32(smem + L::DST + s * BM * BNQ * 2);
+        const uint32_t q_addr = smem_u32(smem + L::Q + s * L::QTILE);
+        const uint32_t do_addr = smem_u32(smem + L::DO + s * L::QTILE);
+#pragma unroll
+        for (int kk = 0; kk < BNQ / 16; ++kk) {
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          mma_bf16(tDV, desc_sw128(pt_addr + kk * 32, 16, 1024), desc_sw128(do_addr + kk * 2048, L::QPANEL, 1024),
+                   idKV, acc);
+          mma_bf16(tDK, desc_sw128(dst_addr + kk * 32, 16, 1024), desc_sw128(q_addr + kk * 2048, L::QPANEL, 1024),
+                   idKV, acc);
+        }
+        mma_commit(&bars[KV_DKV + s]);
+        mma_commit(&bars[KV_QDE + s]);
+      }
+      if (!ok) raise_fault(kFaultMma, abort);
+    }
+  } else {
+    const int row = 32 * (warp & 3) + lane;
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const int j = k0 + row;            // this thread's key
+    const bool valid = j < g.T;
+    const float sc = g.scale * kLog2e;
+    // each softmax warp keeps its own copy of the query-tile vectors, so the
+    // four warps never wait on one another
+    float* v_lse = reinterpret_cast<float*>(smem + L::VEC) + (warp & 3) * 3 * BNQ;
+    float* v_d = v_lse + BNQ;
+    int* v_lo = reinterpret_cast<int*>(v_d + BNQ);
+    const float* lse_b = lse + ((int64_t)b * g.H + h) * g.T;
+    const float* d_b = delta + ((int64_t)b * g.H + h) * g.T;
+    bool ok = true;
+    for (int i = 0; i < nq; ++i) {
+      const int s = i & 1;
+      const int t0 = tfirst + i * BNQ;
+      __syncwarp();
+      for (int c = lane; c < BNQ; c += 32) {
+        const int t = t0 + c;
+        const bool tv = t <= tlast;
+        v_lse[c] = tv ? lse_b[t] * kLog2e : INFINITY;
+        v_d[c] = tv ? d_b[t] : 0.f;
+        v_lo[c] = tv ? local_lo(g, t) : 0x7fffffff;
+      }
+      __syncwarp();
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_SP + s], (i >> 1) & 1, abort, &g_fault_word));
+      if (ok && i >= 2) ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_DKV + s], ((i >> 1) - 1) & 1, abort,
+                                                                 &g_fault_word));
+      if (!ok) break;
+      tc_fence_after();
+      uint8_t* ptrow = smem + L::PT + s * BM * BNQ * 2 + row * 128;
+      uint8_t* dsrow = smem + L::DST + s * BM * BNQ * 2 + row * 128;
+#pragma unroll
+      for (int cc = 0; cc < BNQ / 32; ++cc) {
+        uint32_t rs[32], rp[32];
+        tmem_ld32(tmem + lane_off + s * BNQ + cc * 32, rs);
+        tmem_ld32(tmem + lane_off + 128 + s * BNQ + cc * 32, rp);
+        tmem_ld_wait();
+        uint32_t pp[16], pd[16];
+#pragma unroll
+        for (int i2 = 0; i2 < 16; ++i2) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int c = cc * 32 + 2 * i2 + u;
+            const int t = t0 + c;
+            const bool vis = valid && j < t && j >= v_lo[c];
+            const float p = vis ? exp2f(__uint_as_float(rs[2 * i2 + u]) * sc - v_lse[c]) : 0.f;
+            pv[u] = p;
+            dv[u] = p * (__uint_as_float(rp[2 * i2 + u]) - v_d[c]);
+          }
+          pp[i2] = pack_bf16(pv[0], pv[1]);
+          pd[i2] = pack_bf16(dv[0], dv[1]);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = cc * 4 + q;
+          const int slot = (chunk & 7) ^ (row & 7);
+          *reinterpret_cast<uint4*>(ptrow + slot * 16) = make_uint4(pp[4 * q], pp[4 * q + 1], pp[4 * q + 2],
+                                                                    pp[4 * q + 3]);
+          *reinterpret_cast<uint4*>(dsrow + slot * 16) = make_uint4(pd[4 * q], pd[4 * q + 1], pd[4 * q + 2],
+                                                                    pd[4 * q + 3]);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars[KV_PD + s]);
+    }
+    if (!ok) raise_fault(kFaultSoftmax, abort);
+    if (ok && nq > 0)
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_DKV + ((nq - 1) & 1)], ((nq - 1) >> 1) & 1, abort,
+                                             &g_fault_word));
+    if (!ok) {
+      raise_fault(kFaultEpilogue, abort);
+    } else {
+      tc_fence_after();
+      bf16* dst = dqkv + ((int64_t)b * g.T + (valid ? j : 0)) * 3 * g.d + (int64_t)h * HD;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {  // 0: dk (slot 1), 1: dv (slot 2)
+        const uint32_t tsrc = (which == 0 ? tDK : tDV) + lane_off;
+        const float mul = which == 0 ? g.scale : 1.f;
+        bf16* out = dst + (1 + which) * g.d;
+#pragma unroll
+        for (int cc = 0; cc < HD / 32; ++cc) {
+          uint32_t r[32];
+          if (nq > 0) {
+            tmem_ld32(tsrc + cc * 32, r);
+            tmem_ld_wait();
+          } else {
+#pragma unroll
+            for (int i2 = 0; i2 < 32; ++i2) r[i2] = 0u;
+          }
+          uint32_t pk[16];
+#pragma unroll
+          for (int i2 = 0; i2 < 16; ++i2)
+            pk[i2] = pack_bf16(__uint_as_float(r[2 * i2]) * mul, __uint_as_float(r[2 * i2 + 1]) * mul);
+          if (valid) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(out + cc * 32 + q * 8) =
+                  make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}

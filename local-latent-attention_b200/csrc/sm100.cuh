@@ -12,7 +12,11 @@ bool fwd_supported(const Geom& g, int elt_bytes);
 bool bwd_supported(const Geom& g, int elt_bytes);
 
 cudaError_t launch_local_fwd(const Geom& g, const void* qkv, void* local_out, float* lse, cudaStream_t s);
-cudaError_t launch_local_bwd(const Geom& g, const void* qkv, const void* dl, const float* lse,
+// dq into slot 0 of dqkv; dk, dv into slots 1 and 2. dl = gradient of the
+// local output [B, T, H, hd] bf16; delta = rowsum(dl * local_out) [B, H, T].
+cudaError_t launch_local_dq(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta,
+                            void* dqkv, cudaStream_t s);
+cudaError_t launch_local_dkv(const Geom& g, const void* qkv, const void* dl, const float* lse,
                              const float* delta, void* dqkv, cudaStream_t s);
 
 // Reads (and optionally clears) the device fault word of the current device:

@@ -86,3 +86,53 @@ def test_local_fwd_tc_against_oracle():
     ref = O.local_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), W, LBS)
     got = tc[1].view(B, T, H, hd).transpose(1, 2)
     assert rel_err(got, ref) < 2e-2
+
+
+def _run_fwd_bwd(inp, H, Lh, W, LBS, Nl, QB, force_simt, seed=5):
+    os.environ["LLATTN_FORCE_SIMT"] = "1" if force_simt else "0"
+    try:
+        dev = {k: v.cuda().to(torch.bfloat16 if k in ("qkv", "rq", "gkv", "w") else torch.float32)
+               for k, v in inp.items()}
+        outs = torch.ops.llattn_b200.attn_fwd(dev["qkv"], dev["rq"], dev["gkv"], dev["w"], dev["b"],
+                                              dev["gl"], dev["gr"], H, Lh, W, LBS, Nl, QB, 0.0)
+        gen = torch.Generator().manual_seed(seed)
+        dm = torch.randn(outs[0].shape, generator=gen).to(torch.bfloat16).cuda()
+        grads = torch.ops.llattn_b200.attn_bwd(dm, dev["qkv"], dev["rq"], dev["gkv"], dev["w"], dev["b"],
+                                               dev["gl"], dev["gr"], outs[1], outs[2], outs[3], outs[4],
+                                               H, Lh, W, LBS, Nl, QB, 0.0)
+        torch.cuda.synchronize()
+    finally:
+        os.environ["LLATTN_FORCE_SIMT"] = "0"
+    return [o.cpu() for o in outs], [g_.cpu() for g_ in grads]
+
+
+BWD_CASES = [
+    # B, T, H, hd, W, LBS
+    (1, 256, 1, 128, 256, 256),
+    (1, 300, 2, 64, 128, 256),
+    (2, 1000, 2, 128, 256, 256),
+    (1, 777, 3, 64, 300, 200),
+    (1, 2100, 1, 128, 1024, 256),
+    (2, 129, 2, 128, 16, 32),
+    (1, 1, 1, 128, 4, 256),
+    (1, 4096, 2, 128, 512, 256),
+]
+
+
+@pytest.mark.parametrize("case", BWD_CASES)
+def test_local_bwd_tc_matches_simt(case):
+    B, T, H, hd, W, LBS = case
+    inp = _inputs(B, T, H, hd)
+    _, gt = _run_fwd_bwd(inp, H, 2, W, LBS, 32, 0, False)
+    assert _fault() == 0
+    _, gr = _run_fwd_bwd(inp, H, 2, W, LBS, 32, 0, True)
+    names = ["dqkv", "drq", "dgkv", "dw_rout", "db_rout", "dg_local", "dg_remote"]
+    d = H * hd
+    for name, a, b_ in zip(names, gt, gr):
+        if name == "dqkv":
+            for slot, sname in enumerate(("dq", "dk", "dv")):
+                x = a.view(B, T, 3, d)[:, :, slot].float()
+                y = b_.view(B, T, 3, d)[:, :, slot].float()
+                assert rel_err(x, y) < 2e-2, (sname, rel_err(x, y))
+        else:
+            assert rel_err(a.float(), b_.float()) < 2e-2, (name, rel_err(a.float(), b_.float()))
