@@ -335,6 +335,8 @@ def run_ours(args):
     alg = {  # per launch-group call: (amount, unit)
         "local_fwd": (4.0 * hd * P, "flop"),
         "local_bwd": (8.0 * hd * P, "flop"),
+        "local_dq": (4.0 * hd * P, "flop"),   # dP and dS.K (recompute of S not counted)
+        "local_dkv": (4.0 * hd * P, "flop"),  # dV and dK
         "gate_fwd": ((2 * B * T * d + B * T * d + 2 * d * cfg.latent_d_model) * 2.0, "byte"),
         "gate_bwd": ((3 * B * T * d) * 2.0 + B * T * d * 4.0, "byte"),
         "pool_fwd": (B * T * d * 2.0, "byte"),
@@ -360,7 +362,7 @@ def run_ours(args):
         roof["traffic"] = tr
         roof["avg_launch_ms"] = round(avg_ms, 4)
     # also the local branch as a whole (fwd + bwd), the BASELINE target
-    local_ms = sum(per_step.get(k, (0, 0))[0] for k in ("local_fwd", "local_bwd"))
+    local_ms = sum(per_step.get(k, (0, 0))[0] for k in ("local_fwd", "local_bwd", "local_dq", "local_dkv"))
     local_branch = None
     if local_ms > 0:
         ach = 12.0 * hd * P / (local_ms / 1e3) / 1e12
