@@ -181,6 +181,28 @@ LLATTN_API int llattn_pool_bwd(const llattn_dims* dims, int mode, const void* dp
 LLATTN_API int llattn_fwd(const llattn_fwd_args* args, void* stream);
 LLATTN_API int llattn_bwd(const llattn_bwd_args* args, void* stream);
 
+/* Backward without a caller-provided workspace. For callers that cannot
+ * allocate device memory themselves: hosts that hand the library only
+ * preallocated tensors from their own pool and forbid cudaMalloc, or loops
+ * where an allocation (and its possible synchronisation) is not allowed.
+ * No counterpart in the reference (its Triton backward allocates its fp32
+ * grad buffers with torch on every call).
+ *
+ * Same arguments and results as llattn_bwd; args->workspace and
+ * workspace_bytes are ignored. The scratch is a fixed array of
+ * LLATTN_BWD_NOALLOC_SCRATCH_BYTES (32 MiB) inside the library, reserved on
+ * every GPU that loads the library until the process exits. Dims whose
+ * llattn_bwd_workspace_bytes exceeds that are rejected with
+ * LLATTN_ERR_WORKSPACE (one 8192-token sequence of d_model 256 in bf16 needs
+ * 21 MiB and fits; a 16 x 2048-token batch of d_model 1536 needs 307 MiB and
+ * does not). The first call on each device looks up the array's device address (with that device current), so make that first call before
+ * any stream capture. All calls on a device share the one array: calls that
+ * can overlap on the GPU (different streams, or other threads) race and
+ * corrupt each other's results — serialise them. Nothing in it needs clearing
+ * between calls; it allocates and frees nothing. */
+#define LLATTN_BWD_NOALLOC_SCRATCH_BYTES (32u << 20)
+LLATTN_API int llattn_bwd_noalloc(const llattn_bwd_args* args, void* stream);
+
 /* Per-kernel timing with CUDA events on the launching stream, the native
  * side of the module's set_profile/get_profile_stats (models.py:131-157,
  * which times phases with host syncs instead). enable != 0 turns it on;

@@ -14,10 +14,11 @@ LIB_PATH = os.path.join(_HERE, "libllattn.so")
 
 F32, BF16 = 0, 1
 POOL_CHUNKS, POOL_QBLOCKS = 0, 1
+BWD_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 EXPORTED = (
     "llattn_version", "llattn_last_error", "llattn_fault_status", "llattn_geometry", "llattn_bwd_workspace_bytes",
-    "llattn_pool_fwd", "llattn_pool_bwd", "llattn_fwd", "llattn_bwd",
+    "llattn_pool_fwd", "llattn_pool_bwd", "llattn_fwd", "llattn_bwd", "llattn_bwd_noalloc",
     "llattn_profile_enable", "llattn_profile_read", "llattn_profile_name",
 )
 
@@ -85,6 +86,8 @@ def lib() -> ctypes.CDLL:
         L.llattn_fwd.restype = ctypes.c_int
         L.llattn_bwd.argtypes = [ctypes.POINTER(BwdArgs), _vp]
         L.llattn_bwd.restype = ctypes.c_int
+        L.llattn_bwd_noalloc.argtypes = [ctypes.POINTER(BwdArgs), _vp]
+        L.llattn_bwd_noalloc.restype = ctypes.c_int
         L.llattn_profile_enable.argtypes = [ctypes.c_int]
         L.llattn_profile_enable.restype = ctypes.c_int
         L.llattn_profile_read.argtypes = [ctypes.POINTER(ctypes.c_double),

@@ -7,6 +7,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "profile.cuh"
@@ -292,6 +293,51 @@ int llattn_bwd(const llattn_bwd_args* a, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a->dims.dtype == LLATTN_BF16) return run_bwd<bf16>(g, a, s);
   return run_bwd<float>(g, a, s);
+}
+
+// ---------------------------------------------------------------------------
+// llattn_bwd_noalloc: the backward for callers that must not allocate device
+// memory themselves. Its workspace is this file-scope array, reserved on every
+// GPU that loads the library for the life of the process.
+static __device__ __align__(256) unsigned char g_bwd_noalloc_scratch[LLATTN_BWD_NOALLOC_SCRATCH_BYTES];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64];  // device address of the array, per device
+
+int llattn_bwd_noalloc(const llattn_bwd_args* a, void* stream) {
+  if (!a) return fail(LLATTN_ERR_ARG, "args is NULL");
+  Geom g;
+  int rc = make_geom(&a->dims, &g);
+  if (rc) return rc;
+  const size_t need = bwd_layout(g, a->dims.dtype == LLATTN_BF16 ? 2 : 4).total;
+  if (need > (size_t)LLATTN_BWD_NOALLOC_SCRATCH_BYTES)
+    return fail(LLATTN_ERR_WORKSPACE,
+                "llattn_bwd_noalloc: these dims need %zu bytes of scratch, more than its fixed %zu bytes; "
+                "use llattn_bwd with a caller-provided workspace",
+                need, (size_t)LLATTN_BWD_NOALLOC_SCRATCH_BYTES);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(LLATTN_ERR_LAUNCH, "llattn_bwd_noalloc: no usable current device");
+  void* ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      // once per device, with that device current: the host-side symbol is
+      // only a stand-in, the kernels need the array's device address
+      cudaError_t e = cudaGetSymbolAddress(&g_noalloc_ptr[dev], g_bwd_noalloc_scratch);
+      if (e != cudaSuccess) {
+        g_noalloc_ptr[dev] = nullptr;
+        return fail(LLATTN_ERR_LAUNCH, "llattn_bwd_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      }
+    }
+    ptr = g_noalloc_ptr[dev];
+  }
+  // Same kernels as llattn_bwd; every workspace region is fully written before
+  // it is read, so the array's previous contents never need clearing.
+  llattn_bwd_args b = *a;
+  b.workspace = ptr;
+  b.workspace_bytes = (size_t)LLATTN_BWD_NOALLOC_SCRATCH_BYTES;
+  return llattn_bwd(&b, stream);
 }
 
 }  // extern "C"
