@@ -113,16 +113,20 @@ int run_fwd(const Geom& g, const llattn_fwd_args* a, cudaStream_t s) {
                         "latent_fwd");
   }
   if (rc) return rc;
+  const bool tc = sm100::fwd_supported(g, sizeof(T));
+  const bool fused = tc && sm100::gate_fusable(g);
   {
   prof::Scope ps(prof::LOCAL_FWD, s);
-  if (sm100::fwd_supported(g, sizeof(T))) {
-    rc = check_launch(sm100::launch_local_fwd(g, a->qkv, a->local_out, a->lse, s), "local_fwd_sm100");
+  if (tc) {
+    sm100::GateEpilogue ep{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    if (fused) ep = {a->lat, a->w_rout, a->b_rout, a->g_local, a->g_remote, a->mixed};
+    rc = check_launch(sm100::launch_local_fwd(g, a->qkv, a->local_out, a->lse, ep, s), "local_fwd_sm100");
   } else {
     rc = check_launch(launch_local_fwd_simt<T>(g, qkv, static_cast<T*>(a->local_out), a->lse, s),
                       "local_fwd_simt");
   }
   }
-  if (rc) return rc;
+  if (rc || fused) return rc;
   prof::Scope ps(prof::GATE_FWD, s);
   return check_launch(launch_gate_fwd<T>(g, static_cast<const T*>(a->local_out), static_cast<const T*>(a->lat),
                                          static_cast<const T*>(a->w_rout), a->b_rout, a->g_local, a->g_remote,

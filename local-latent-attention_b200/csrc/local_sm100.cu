@@ -68,17 +68,21 @@ struct FwdLayout {
   static constexpr int K = Q + TILE;            // 2 stages
   static constexpr int V = K + 2 * TILE;        // 2 stages
   static constexpr int P = V + 2 * TILE;        // 128 x 128 bf16
+  // the fused gate's lat tile (128 x 64 bf16) and W_rout slice (hd x 64 bf16)
+  // live in the P region: the R MMA reads them before P_0 is written
+  static constexpr int LAT = P;
+  static constexpr int WR = P + BM * 128;
   static constexpr int BAR = P + BM * BN * 2;
   static constexpr int BYTES = BAR + 128;
 };
 
 // Barrier slots in the BAR region.
-enum { B_Q = 0, B_K = 1, B_V = 3, B_KVE = 5, B_S = 7, B_P = 9, B_O = 10, N_BARS = 11 };
+enum { B_Q = 0, B_K = 1, B_V = 3, B_KVE = 5, B_S = 7, B_P = 9, B_O = 10, B_LW = 11, B_R = 12, N_BARS = 13 };
 
 template <int HD>
 __global__ void __launch_bounds__(192, 1)
     local_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, Geom g, bf16* __restrict__ local_out,
-                        float* __restrict__ lse_out) {
+                        float* __restrict__ lse_out, GateEpilogue ep) {
   using L = FwdLayout<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -104,6 +108,8 @@ __global__ void __launch_bounds__(192, 1)
     }
     mbar_init(&bars[B_P], BM);
     mbar_init(&bars[B_O], 1);
+    mbar_init(&bars[B_LW], BM);
+    mbar_init(&bars[B_R], 1);
     *abort = 0;
     fence_barrier_init();
   }
@@ -116,7 +122,8 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS0 = tmem, tS1 = tmem + 128, tO = tmem + 256;
+  const uint32_t tS0 = tmem, tS1 = tmem + 128, tO = tmem + 256, tR = tmem + 256 + HD;
+  const bool fuse = ep.lat != nullptr;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -159,12 +166,26 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0 && nk > 0) {
+    if (lane == 0 && (nk > 0 || fuse)) {
       constexpr uint32_t idS = idesc_bf16_f32(BM, BN, false, false);
       constexpr uint32_t idO = idesc_bf16_f32(BM, HD, false, true);
       const uint32_t q_addr = smem_u32(smem + L::Q);
       const uint32_t p_addr = smem_u32(smem + L::P);
-      bool ok = mbar_wait(&bars[B_Q], 0, abort, &g_fault_word);
+      bool ok = true;
+      if (fuse) {
+        // remote tile R = lat_tile (128 x 64) . W_h^T (64 x hd), K-major both
+        ok = mbar_wait(&bars[B_LW], 0, abort, &g_fault_word);
+        if (ok) {
+          tc_fence_after();
+          constexpr uint32_t idR = idesc_bf16_f32(BM, HD, false, false);
+          const uint32_t la = smem_u32(smem + L::LAT), wa = smem_u32(smem + L::WR);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16(tR, desc_sw128(la + kk * 32, 16, 1024), desc_sw128(wa + kk * 32, 16, 1024), idR, kk > 0);
+          mma_commit(&bars[B_R]);
+        }
+      }
+      if (ok && nk > 0) ok = mbar_wait(&bars[B_Q], 0, abort, &g_fault_word);
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
         if (!mbar_wait(&bars[B_K + s], (j >> 1) & 1, abort, &g_fault_word)) return false;
@@ -179,7 +200,7 @@ __global__ void __launch_bounds__(192, 1)
         mma_commit(&bars[B_S + s]);
         return true;
       };
-      if (ok) ok = issue_s(0);
+      if (ok && nk > 0) ok = issue_s(0);
       for (int j = 0; ok && j < nk; ++j) {
         if (j + 1 < nk && !(ok = issue_s(j + 1))) break;
         if (!(ok = mbar_wait(&bars[B_P], j & 1, abort, &g_fault_word))) break;
@@ -208,7 +229,28 @@ __global__ void __launch_bounds__(192, 1)
     float m = -INFINITY, l = 0.f;
     uint8_t* prow = smem + L::P + row * 128;
     bool ok = true;
-    for (int j = 0; j < nk; ++j) {
+    if (fuse) {
+      // row `row` of the lat tile: latent output of this token's query row;
+      // rows < hd also copy one row of W_rout's head slice. 128-byte rows,
+      // 16-byte chunk c stored at slot c ^ (row % 8) (128-byte swizzle).
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.lat) +
+                                                        ((int64_t)b * g.Tq + (valid ? t / g.qbs : 0)) * 64);
+      uint8_t* dl_ = smem + L::LAT + row * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dl_ + ((c ^ (row & 7)) * 16)) = src[c];
+      if (row < HD) {
+        const uint4* wsrc = reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.w_rout) +
+                                                           ((int64_t)h * HD + row) * 64);
+        uint8_t* wd = smem + L::WR + row * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(wd + ((c ^ (row & 7)) * 16)) = wsrc[c];
+      }
+      fence_async_smem();
+      mbar_arrive(&bars[B_LW]);
+      // P_0 overwrites this region: wait until the R MMA has read it
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_R], 0, abort, &g_fault_word));
+    }
+    for (int j = 0; ok && j < nk; ++j) {
       const int s = j & 1;
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_S + s], (j >> 1) & 1, abort, &g_fault_word));
       if (!ok) break;
@@ -293,6 +335,60 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       bf16* dst = local_out + ((int64_t)b * g.T + (valid ? t : 0)) * g.d + (int64_t)h * HD;
+      if (fuse) {
+        // pass A: gate logits from the bf16-rounded local row (the value
+        // stored for the backward) and the remote row
+        const float* bh = ep.b_rout + (int64_t)h * HD;
+        float sl = 0.f, sr = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < HD / 32; ++cc) {
+          uint32_t ro[32], rr[32];
+          if (nk > 0) tmem_ld32(tO + lane_off + cc * 32, ro);
+          tmem_ld32(tR + lane_off + cc * 32, rr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int c = cc * 32 + i;
+            const float lv = nk > 0 ? __bfloat162float(__float2bfloat16_rn(__uint_as_float(ro[i]) * inv)) : 0.f;
+            sl = fmaf(lv, __ldg(ep.g_local + c), sl);
+            sr = fmaf(__uint_as_float(rr[i]) + __ldg(bh + c), __ldg(ep.g_remote + c), sr);
+          }
+        }
+        const float x = sl + g.gate_bias - sr;
+        const float wl = 1.f / (1.f + expf(-x));
+        const float wr = 1.f / (1.f + expf(x));
+        bf16* mdst = static_cast<bf16*>(ep.mixed) + ((int64_t)b * g.T + (valid ? t : 0)) * g.d + (int64_t)h * HD;
+        // pass B: local_out and mixed
+#pragma unroll
+        for (int cc = 0; cc < HD / 32; ++cc) {
+          uint32_t ro[32], rr[32];
+          if (nk > 0) tmem_ld32(tO + lane_off + cc * 32, ro);
+          tmem_ld32(tR + lane_off + cc * 32, rr);
+          tmem_ld_wait();
+          uint32_t pl[16], pm[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float lv[2], mv[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int c = cc * 32 + 2 * i + u;
+              lv[u] = nk > 0 ? __bfloat162float(__float2bfloat16_rn(__uint_as_float(ro[2 * i + u]) * inv)) : 0.f;
+              mv[u] = wl * lv[u] + wr * (__uint_as_float(rr[2 * i + u]) + __ldg(bh + c));
+            }
+            pl[i] = pack_bf16(lv[0], lv[1]);
+            pm[i] = pack_bf16(mv[0], mv[1]);
+          }
+          if (valid) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) = make_uint4(pl[4 * q], pl[4 * q + 1], pl[4 * q + 2],
+                                                                            pl[4 * q + 3]);
+              *reinterpret_cast<uint4*>(mdst + cc * 32 + q * 8) =
+                  make_uint4(pm[4 * q], pm[4 * q + 1], pm[4 * q + 2], pm[4 * q + 3]);
+            }
+          }
+        }
+      } else {
 #pragma unroll
       for (int cc = 0; cc < HD / 32; ++cc) {
         uint32_t r[32];
@@ -313,6 +409,7 @@ __global__ void __launch_bounds__(192, 1)
             *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) =
                 make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
+      }
       }
       if (valid) lse_out[((int64_t)b * g.H + h) * g.T + t] = l > 0.f ? (m + log2f(l)) * kLn2 : INFINITY;
     }
@@ -367,7 +464,8 @@ bool force_simt() {
 }
 
 template <int HD>
-cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, cudaStream_t s) {
+cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, const GateEpilogue& ep,
+                   cudaStream_t s) {
   CUtensorMap tm;
   if (!make_rows_map(&tm, qkv, g.B, g.T, 3 * g.H, HD)) return cudaErrorInvalidValue;
   // at least 116 KB so a second CTA never shares the SM (and its TMEM)
@@ -375,7 +473,7 @@ cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, 
   cudaError_t e = cudaFuncSetAttribute(local_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.T, BM), g.H, g.B);
-  local_fwd_tc_kernel<HD><<<grid, 192, smem, s>>>(tm, g, static_cast<bf16*>(local_out), lse);
+  local_fwd_tc_kernel<HD><<<grid, 192, smem, s>>>(tm, g, static_cast<bf16*>(local_out), lse, ep);
   return cudaGetLastError();
 }
 
@@ -417,10 +515,16 @@ bool fwd_supported(const Geom& g, int elt_bytes) {
 
 bool bwd_supported(const Geom& g, int elt_bytes) { return fwd_supported(g, elt_bytes); }
 
-cudaError_t launch_local_fwd(const Geom& g, const void* qkv, void* local_out, float* lse, cudaStream_t s) {
+bool gate_fusable(const Geom& g) { return g.Ld == 64; }
+
+cudaError_t launch_local_fwd(const Geom& g, const void* qkv, void* local_out, float* lse, const GateEpilogue& ep,
+                             cudaStream_t s) {
   if (((uintptr_t)qkv & 15) || ((uintptr_t)local_out & 15)) return cudaErrorMisalignedAddress;
-  if (g.hd == 64) return fwd_hd<64>(g, qkv, local_out, lse, s);
-  return fwd_hd<128>(g, qkv, local_out, lse, s);
+  if (ep.lat && (g.Ld != 64 || ((uintptr_t)ep.lat & 15) || ((uintptr_t)ep.w_rout & 15) ||
+                 ((uintptr_t)ep.mixed & 15)))
+    return cudaErrorMisalignedAddress;
+  if (g.hd == 64) return fwd_hd<64>(g, qkv, local_out, lse, ep, s);
+  return fwd_hd<128>(g, qkv, local_out, lse, ep, s);
 }
 
 cudaError_t launch_local_dq(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta,

@@ -11,7 +11,23 @@ namespace sm100 {
 bool fwd_supported(const Geom& g, int elt_bytes);
 bool bwd_supported(const Geom& g, int elt_bytes);
 
-cudaError_t launch_local_fwd(const Geom& g, const void* qkv, void* local_out, float* lse, cudaStream_t s);
+// Remote projection + gate + mix fused into the forward epilogue
+// (models.py:392-438): remote_h = lat[t/qbs] W_rout[h]^T + b_rout[h] as one
+// more tcgen05 MMA, then w = sigmoid(local.g_l + bias - remote.g_r) and
+// mixed = w local + (1-w) remote per row. lat == nullptr: not fused (the
+// caller runs the separate gate kernel). Needs latent_d_model == 64.
+struct GateEpilogue {
+  const void* lat;       // [B, Tq, 64] bf16
+  const void* w_rout;    // [d, 64] bf16
+  const float* b_rout;   // [d]
+  const float* g_local;  // [hd]
+  const float* g_remote; // [hd]
+  void* mixed;           // [B, T, d] bf16
+};
+bool gate_fusable(const Geom& g);
+
+cudaError_t launch_local_fwd(const Geom& g, const void* qkv, void* local_out, float* lse, const GateEpilogue& ep,
+                             cudaStream_t s);
 // dq into slot 0 of dqkv; dk, dv into slots 1 and 2. dl = gradient of the
 // local output [B, T, H, hd] bf16; delta = rowsum(dl * local_out) [B, H, T].
 cudaError_t launch_local_dq(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta,
