@@ -63,6 +63,7 @@ def parse():
     p.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--batch", type=int, default=0, help="override the config's batch (small profiling runs)")
     return p.parse_args()
 
 
@@ -243,6 +244,9 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev)
 
     B, T, cfg = block_cfg(args.config)
+    if args.batch:
+        B = args.batch
+        CONFIGS[args.config] = dict(CONFIGS[args.config], B=B)
     m = llattn_b200.LocalLatentAttentionB200(model_config(cfg))
     m.load_state_dict(O.init_params(cfg, 0))
     m = m.to(device=dev, dtype=torch.bfloat16)

@@ -70,7 +70,7 @@ int make_geom(const llattn_dims* d, Geom* g) {
 
 // Backward workspace, every region 256-byte aligned.
 struct BwdLayout {
-  size_t dl, delta, drow, dlat, lat_delta, dg_part, dg_sum, dw_part, dgkv_part, total;
+  size_t dl, delta, drow, dlat, dlat_tok, lat_delta, dg_part, dg_sum, dw_part, dgkv_part, total;
   int gate_tok, n_gate_cta, n_split_w, n_split_lat;
 };
 
@@ -81,7 +81,8 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
   L.gate_tok = 16;
   L.n_gate_cta = g.B * cdiv(g.T, L.gate_tok);
   const int rows = g.B * g.Tq;
-  L.n_split_w = std::max(1, std::min(cdiv(rows, 32), cdiv(2 * 148, cdiv(g.d, 32))));
+  // token splits of the dW_rout reduction (enough CTAs to fill the GPU)
+  L.n_split_w = std::max(1, std::min(cdiv(g.B * g.T, 64), cdiv(2 * 148, cdiv(g.d, 128))));
   const int lat_ctas = g.B * g.Lh * cdiv(g.Nc, 64);
   L.n_split_lat = std::max(1, std::min(cdiv(g.Tq, 32), cdiv(2 * 148, lat_ctas)));
   size_t off = 0;
@@ -91,6 +92,7 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
   L.delta = take(sizeof(float) * g.B * g.H * g.T);
   L.drow = take(sizeof(float) * BTd);
   L.dlat = take(sizeof(float) * (size_t)rows * g.Ld);
+  L.dlat_tok = take(sizeof(float) * (size_t)g.B * g.T * g.Ld);
   L.lat_delta = take(sizeof(float) * (size_t)g.B * g.Lh * g.Tq);
   L.dg_part = take(sizeof(float) * (size_t)L.n_gate_cta * 2 * g.hd);
   L.dg_sum = take(sizeof(float) * 2 * g.hd);
@@ -150,7 +152,46 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
   const T* lat = static_cast<const T*>(a->lat);
   const T* w_rout = static_cast<const T*>(a->w_rout);
 
+  const bool tc = sm100::bwd_supported(g, sizeof(T)) && sm100::gate_fusable(g);
+  int n_dg = L.n_gate_cta;
   int rc;
+  if (tc) {
+    // tensor-core path: gate backward (also dlat, dR bf16, dg partials), then
+    // the local backward, then the dW_rout / db_rout GEMM from dR
+    bf16* dr = reinterpret_cast<bf16*>(drow);
+    float* dlat_tok = reinterpret_cast<float*>(ws + L.dlat_tok);
+    n_dg = sm100::gate_bwd_ctas(g);
+    {
+      prof::Scope ps(prof::GATE_BWD, s);
+      sm100::GateBwd gb{a->local_out, a->lat,   a->w_rout, a->b_rout, a->g_local, a->g_remote,
+                        a->dmixed,    dl,       delta,     dr,        dlat_tok,   dg_part};
+      rc = check_launch(sm100::launch_gate_bwd(g, gb, s), "gate_bwd_sm100");
+    }
+    if (rc) return rc;
+    {
+      prof::Scope ps(prof::LOCAL_DQ, s);
+      rc = check_launch(sm100::launch_local_dq(g, a->qkv, dl, a->lse, delta, a->dqkv, s), "local_dq_sm100");
+    }
+    if (rc) return rc;
+    {
+      prof::Scope ps(prof::LOCAL_DKV, s);
+      rc = check_launch(sm100::launch_local_dkv(g, a->qkv, dl, a->lse, delta, a->dqkv, s), "local_dkv_sm100");
+    }
+    if (rc) return rc;
+    {
+      prof::Scope ps(prof::ROUT_BWD, s, g.qbs > 1 ? 2 : 1);
+      rc = check_launch(sm100::launch_rout_dw(g, dr, a->lat, dw_part, dw_part + (size_t)L.n_split_w * g.d * g.Ld,
+                                              L.n_split_w, s),
+                        "rout_dw_sm100");
+      if (rc) return rc;
+      if (g.qbs > 1) {
+        rc = check_launch(sm100::launch_dlat_rowsum(g, dlat_tok, dlat, s), "dlat_rowsum");
+        if (rc) return rc;
+      } else {
+        dlat = dlat_tok;
+      }
+    }
+  } else {
   {
   prof::Scope ps(prof::GATE_BWD, s);
   rc = check_launch(
@@ -179,6 +220,7 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
   rc = check_launch(launch_rout_bwd<T>(g, drow, lat, w_rout, dlat, dw_part, L.n_split_w, s), "rout_bwd");
   }
   if (rc) return rc;
+  }
   {
   prof::Scope ps(prof::REDUCE, s, 3);
   rc = check_launch(launch_reduce_rows(dw_part, L.n_split_w, (int64_t)g.d * g.Ld, a->dw_rout, s), "reduce_dw");
@@ -187,7 +229,7 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
                     "reduce_db");
   if (rc) return rc;
   // dg partials are [cta][2*hd] (local half, remote half)
-  rc = check_launch(launch_reduce_rows(dg_part, L.n_gate_cta, 2 * g.hd, dg_sum, s), "reduce_dg");
+  rc = check_launch(launch_reduce_rows(dg_part, n_dg, 2 * g.hd, dg_sum, s), "reduce_dg");
   if (rc) return rc;
   rc = check_launch(cudaMemcpyAsync(a->dg_local, dg_sum, sizeof(float) * g.hd, cudaMemcpyDeviceToDevice, s),
                     "copy dg_local");

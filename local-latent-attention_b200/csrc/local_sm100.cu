@@ -424,6 +424,7 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 #include "local_sm100_bwd.cuh"
+#include "gate_sm100.cuh"
 
 // ---------------------------------------------------------------------------
 // host side
@@ -458,6 +459,19 @@ bool make_rows_map(CUtensorMap* map, const void* base, int B, int T, int slots_x
 
 // LLATTN_FORCE_SIMT=1 routes bf16 through the SIMT kernels (used by the tests
 // to compare the two implementations of the same math).
+// bf16 matrix [rows, cols] (cols contiguous) with box (64 cols, 64 rows).
+bool make_2d_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool force_simt() {
   const char* e = std::getenv("LLATTN_FORCE_SIMT");
   return e && e[0] == '1';
@@ -507,7 +521,45 @@ cudaError_t dkv_hd(const Geom& g, const void* qkv, const void* dl, const float* 
   return cudaGetLastError();
 }
 
+template <int HD>
+cudaError_t gate_bwd_hd(const Geom& g, const GateBwd& a, cudaStream_t s) {
+  const int smem = std::max(GbLayout<HD>::BYTES + 1024, 116 * 1024);
+  cudaError_t e = cudaFuncSetAttribute(gate_bwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(cdiv(g.T, BM), g.B);
+  gate_bwd_tc_kernel<HD><<<grid, 192, smem, s>>>(
+      g, static_cast<const bf16*>(a.local_out), static_cast<const bf16*>(a.lat), static_cast<const bf16*>(a.w_rout),
+      a.b_rout, a.g_local, a.g_remote, static_cast<const bf16*>(a.dmixed), static_cast<bf16*>(a.dl), a.delta,
+      static_cast<bf16*>(a.dr), a.dlat_tok, a.dg_part);
+  return cudaGetLastError();
+}
+
 }  // namespace
+
+int gate_bwd_ctas(const Geom& g) { return g.B * cdiv(g.T, BM); }
+
+cudaError_t launch_gate_bwd(const Geom& g, const GateBwd& a, cudaStream_t s) {
+  if (g.hd == 64) return gate_bwd_hd<64>(g, a, s);
+  return gate_bwd_hd<128>(g, a, s);
+}
+
+cudaError_t launch_rout_dw(const Geom& g, const void* dr, const void* lat, float* dw_part, float* db_part,
+                           int n_split, cudaStream_t s) {
+  CUtensorMap tm;
+  if (!make_2d_map(&tm, dr, (int64_t)g.B * g.T, g.d)) return cudaErrorInvalidValue;
+  const int smem = std::max(DwLayout::BYTES + 1024, 116 * 1024);
+  cudaError_t e = cudaFuncSetAttribute(rout_dw_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(cdiv(g.d, 128), n_split);
+  rout_dw_tc_kernel<<<grid, 192, smem, s>>>(tm, g, static_cast<const bf16*>(lat), dw_part, db_part, n_split);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dlat_rowsum(const Geom& g, const float* dlat_tok, float* dlat, cudaStream_t s) {
+  const int64_t n = (int64_t)g.B * g.Tq * 64;
+  dlat_rowsum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(g, dlat_tok, dlat);
+  return cudaGetLastError();
+}
 
 bool fwd_supported(const Geom& g, int elt_bytes) {
   return !force_simt() && elt_bytes == 2 && (g.hd == 64 || g.hd == 128) && get_encode() != nullptr;

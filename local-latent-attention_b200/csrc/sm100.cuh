@@ -35,6 +35,21 @@ cudaError_t launch_local_dq(const Geom& g, const void* qkv, const void* dl, cons
 cudaError_t launch_local_dkv(const Geom& g, const void* qkv, const void* dl, const float* lse,
                              const float* delta, void* dqkv, cudaStream_t s);
 
+// Gate / r_out backward on tensor cores (needs gate_fusable): writes dl
+// (bf16 [B,T,d]), delta [B,H,T], dr (bf16 [B,T,d]), dlat_tok (fp32 [B,T,64])
+// and dg_part ([gate_bwd_ctas][2*hd], dg_local half then dg_remote half).
+struct GateBwd {
+  const void* local_out; const void* lat; const void* w_rout; const float* b_rout; const float* g_local;
+  const float* g_remote; const void* dmixed; void* dl; float* delta; void* dr; float* dlat_tok; float* dg_part;
+};
+int gate_bwd_ctas(const Geom& g);
+cudaError_t launch_gate_bwd(const Geom& g, const GateBwd& a, cudaStream_t s);
+// dW_rout / db_rout partials over n_split token ranges: dw_part [n_split][d*64],
+// db_part [n_split][d]; dr bf16 [B*T, d] (d a multiple of 64), lat [B,Tq,64].
+cudaError_t launch_rout_dw(const Geom& g, const void* dr, const void* lat, float* dw_part, float* db_part,
+                           int n_split, cudaStream_t s);
+cudaError_t launch_dlat_rowsum(const Geom& g, const float* dlat_tok, float* dlat, cudaStream_t s);
+
 // Reads (and optionally clears) the device fault word of the current device:
 // bits set by a tensor-core kernel whose bounded wait ran out.
 unsigned read_fault_word(bool reset);
