@@ -16,15 +16,19 @@
 
 template <int HD>
 struct GbLayout {
+  static constexpr int TILE = BM * HD * 2;         // 128 rows x HD bf16 (HD/64 panels of 16 KB)
   static constexpr int LAT = 0;                    // 128 x 64 bf16
-  static constexpr int W = LAT + BM * 128;         // 2 x (HD x 64 bf16)
-  static constexpr int DR = W + 2 * HD * 128;      // 2 x (128 x HD bf16)
-  static constexpr int RED = DR + 2 * BM * HD * 2; // 4 warps x 2 x HD floats
-  static constexpr int BAR = RED + 4 * 2 * HD * 4;
+  static constexpr int W = LAT + BM * 128;         // per group: HD x 64 bf16
+  static constexpr int LT = W + 2 * HD * 128;      // per group: local_out tile of the head
+  static constexpr int DM = LT + 2 * TILE;         // per group: dmixed tile, overwritten by dR
+  static constexpr int RED = DM + 2 * TILE;        // 8 warps x 2 x HD floats
+  static constexpr int BAR = RED + 8 * 2 * HD * 4;
   static constexpr int BYTES = BAR + 256;
 };
 
-enum { GB_W = 0, GB_R = 2, GB_DR = 4, GB_DL = 6, GB_NB = 8 };
+// per group g (0/1): W ready, R computed, dR tile ready, dlat MMA done,
+// L/dmixed tiles loaded
+enum { GB_W = 0, GB_R = 2, GB_DR = 4, GB_DL = 6, GB_F = 8, GB_NB = 10 };
 
 // Sum of v[c] over the 32 lanes for column c = lane (recursive halving).
 __device__ __forceinline__ float butterfly32(float (&v)[32], int lane) {
@@ -51,9 +55,12 @@ __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   }
 }
 
+// Warps: 0 idle, 1 = TMEM + MMA issuer, 2-5 = group 0 (even heads),
+// 6-9 = group 1 (odd heads); in a group thread = token row = TMEM lane.
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
-    gate_bwd_tc_kernel(Geom g, const bf16* __restrict__ local_out, const bf16* __restrict__ lat,
+__global__ void __launch_bounds__(320, 1)
+    gate_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_dm,
+                       Geom g, const bf16* __restrict__ local_out, const bf16* __restrict__ lat,
                        const bf16* __restrict__ w_rout, const float* __restrict__ b_rout,
                        const float* __restrict__ gl, const float* __restrict__ gr, const bf16* __restrict__ dmixed,
                        bf16* __restrict__ dl, float* __restrict__ delta, bf16* __restrict__ dr,
@@ -74,6 +81,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&bars[GB_R + s], 1);
       mbar_init(&bars[GB_DR + s], BM);
       mbar_init(&bars[GB_DL + s], 1);
+      mbar_init(&bars[GB_F + s], 1);
     }
     *abort = 0;
     fence_barrier_init();
@@ -86,16 +94,47 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // R_h buffers at [0,HD) and [HD,2HD); dlat at 256
+  const uint32_t tmem = *tmem_slot;  // R of group g at [g*HD, (g+1)*HD); dlat at 256
   const uint32_t tDL = tmem + 256;
   float* red = reinterpret_cast<float*>(smem + L::RED);
 
-  if (warp == 1) {
+  if (warp == 0) {
+    // TMA producer: local_out and dmixed tiles of head h into group h&1's
+    // buffers, once that group's previous head has been fully consumed
+    // (its dlat MMA, which reads the dR tile in the dmixed buffer, is done)
+    if (lane == 0) {
+      prefetch_tmap(&tm_lo);
+      prefetch_tmap(&tm_dm);
+      int issued = 0;
+      for (int h = 0; h < H; ++h) {
+        const int grp = h & 1, n = h >> 1;
+        if (n >= 1 && !mbar_wait(&bars[GB_DL + grp], (n - 1) & 1, abort, &g_fault_word)) {
+          raise_fault(kFaultProducer, abort);
+          break;
+        }
+        mbar_expect_tx(&bars[GB_F + grp], 2 * L::TILE);
+        const int row0 = b * g.T + t0;
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p) {
+          tma_load_2d(&tm_lo, &bars[GB_F + grp], smem + L::LT + grp * L::TILE + p * (BM * 128), h * HD + p * 64, row0);
+          tma_load_2d(&tm_dm, &bars[GB_F + grp], smem + L::DM + grp * L::TILE + p * (BM * 128), h * HD + p * 64, row0);
+        }
+        issued = h + 1;
+      }
+      if (*abort) {
+        volatile int none = 0;
+        volatile unsigned gnone = 0;
+        for (int h = issued - 2 < 0 ? 0 : issued - 2; h < issued; ++h)
+          mbar_wait(&bars[GB_F + (h & 1)], (h >> 1) & 1, &none, &gnone, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idR = idesc_bf16_f32(BM, HD, false, false);  // lat . W_h^T
       constexpr uint32_t idL = idesc_bf16_f32(BM, 64, false, true);   // dR_h . W_h
       const uint32_t la = smem_u32(smem + L::LAT);
       bool ok = true;
+      // head h belongs to group h&1 and is that group's (h>>1)-th head
       auto issue_r = [&](int h) -> bool {
         const int s = h & 1;
         if (!mbar_wait(&bars[GB_W + s], (h >> 1) & 1, abort, &g_fault_word)) return false;
@@ -109,82 +148,91 @@ __global__ void __launch_bounds__(192, 1)
         return true;
       };
       ok = issue_r(0);
+      if (ok && H > 1) ok = issue_r(1);
       for (int h = 0; ok && h < H; ++h) {
-        if (h + 1 < H && !(ok = issue_r(h + 1))) break;
         const int s = h & 1;
         if (!(ok = mbar_wait(&bars[GB_DR + s], (h >> 1) & 1, abort, &g_fault_word))) break;
         tc_fence_after();
-        const uint32_t da = smem_u32(smem + L::DR + s * BM * HD * 2);
+        const uint32_t da = smem_u32(smem + L::DM + s * L::TILE);
         const uint32_t wa = smem_u32(smem + L::W + s * HD * 128);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
           mma_bf16(tDL, desc_sw128(da + (kk / 4) * (BM * 128) + (kk % 4) * 32, 16, 1024),
                    desc_sw128(wa + kk * 2048, 0, 1024), idL, (h > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&bars[GB_DL + s]);
+        if (h + 2 < H && !(ok = issue_r(h + 2))) break;
       }
       if (!ok) raise_fault(kFaultMma, abort);
     }
   } else if (warp >= 2) {
+    const int grp = (warp - 2) >> 2;
     const int row = 32 * (warp & 3) + lane;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
     const int t = t0 + row;
     const bool valid = t < g.T;
     const int64_t tok = (int64_t)b * g.T + (valid ? t : 0);
-    // lat row of this token, 128-byte swizzled rows
-    {
+    if (grp == 0) {  // lat row of this token, 128-byte swizzled rows
       const uint4* src = reinterpret_cast<const uint4*>(lat + ((int64_t)b * g.Tq + (valid ? t / g.qbs : 0)) * 64);
       uint8_t* d = smem + L::LAT + row * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(d + ((c ^ (row & 7)) * 16)) = src[c];
     }
-    auto write_w = [&](int h) {
+    auto write_w = [&](int h) {  // into this group's W buffer
       if (row < HD) {
         const uint4* src = reinterpret_cast<const uint4*>(w_rout + ((int64_t)h * HD + row) * 64);
-        uint8_t* d = smem + L::W + (h & 1) * HD * 128 + row * 128;
+        uint8_t* d = smem + L::W + grp * HD * 128 + row * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(d + ((c ^ (row & 7)) * 16)) = src[c];
       }
       fence_async_smem();
-      mbar_arrive(&bars[GB_W + (h & 1)]);
+      mbar_arrive(&bars[GB_W + grp]);
     };
-    write_w(0);
-    // per-warp dg accumulators in shared memory; lane owns column cc*32+lane
-    float* wred = red + (warp & 3) * 2 * HD;
+    float* wred = red + (warp - 2) * 2 * HD;  // lane owns columns cc*32+lane
     for (int e = lane; e < 2 * HD; e += 32) wred[e] = 0.f;
     bool ok = true;
-    for (int h = 0; h < H; ++h) {
-      const int s = h & 1;
-      if (h >= 1) {  // dlat MMA of head h-1 done: W[(h+1)&1] and DR[s] are free
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_DL + ((h - 1) & 1)], ((h - 1) >> 1) & 1, abort,
-                                               &g_fault_word));
-        if (!ok) break;
-      }
-      if (h + 1 < H) write_w(h + 1);
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_R + s], (h >> 1) & 1, abort, &g_fault_word));
+    if (grp < H) write_w(grp);
+    // tile rows: 16-byte chunk c of this row sits at panel c/8, slot (c%8)^(row%8)
+    auto chunk_ptr = [&](uint8_t* tile, int c) -> uint4* {
+      return reinterpret_cast<uint4*>(tile + (c >> 3) * (BM * 128) + row * 128 + (((c & 7) ^ (row & 7)) * 16));
+    };
+    const float4* gl4 = reinterpret_cast<const float4*>(gl);
+    const float4* gr4 = reinterpret_cast<const float4*>(gr);
+    for (int h = grp; h < H; h += 2) {
+      const int n = h >> 1;  // this group's n-th head
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_R + grp], n & 1, abort, &g_fault_word));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_F + grp], n & 1, abort, &g_fault_word));
       if (!ok) break;
       tc_fence_after();
-      const bf16* lrow = local_out + tok * g.d + (int64_t)h * HD;
-      const bf16* mrow = dmixed + tok * g.d + (int64_t)h * HD;
-      const float* bh = b_rout + (int64_t)h * HD;
+      const uint32_t tR = tmem + grp * HD + lane_off;
+      uint8_t* lt = smem + L::LT + grp * L::TILE;
+      uint8_t* dmt = smem + L::DM + grp * L::TILE;
+      const float4* bh4 = reinterpret_cast<const float4*>(b_rout + (int64_t)h * HD);
       // pass 1: gate logits and dw
       float sl = 0.f, sr = 0.f, dw = 0.f;
-#pragma unroll
+#pragma unroll 1
       for (int cc = 0; cc < HD / 32; ++cc) {
         uint32_t rr[32];
-        tmem_ld32(tmem + lane_off + s * HD + cc * 32, rr);
+        tmem_ld32(tR + cc * 32, rr);
         tmem_ld_wait();
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           float lv[8], mv[8];
-          unpack8(reinterpret_cast<const uint4*>(lrow + cc * 32)[q], lv);
-          unpack8(reinterpret_cast<const uint4*>(mrow + cc * 32)[q], mv);
+          unpack8(*chunk_ptr(lt, cc * 4 + q), lv);
+          unpack8(*chunk_ptr(dmt, cc * 4 + q), mv);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int c = cc * 32 + q * 8 + i;
-            const float rv = __uint_as_float(rr[q * 8 + i]) + __ldg(bh + c);
-            sl = fmaf(lv[i], __ldg(gl + c), sl);
-            sr = fmaf(rv, __ldg(gr + c), sr);
-            dw = fmaf(mv[i], lv[i] - rv, dw);
+          for (int i4 = 0; i4 < 2; ++i4) {
+            const int c4 = (cc * 32 + q * 8) / 4 + i4;
+            const float4 bb = __ldg(bh4 + c4), ga = __ldg(gl4 + c4), gb = __ldg(gr4 + c4);
+            const float bv[4] = {bb.x, bb.y, bb.z, bb.w}, gav[4] = {ga.x, ga.y, ga.z, ga.w};
+            const float gbv[4] = {gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int i = i4 * 4 + k;
+              const float rv = __uint_as_float(rr[q * 8 + i]) + bv[k];
+              sl = fmaf(lv[i], gav[k], sl);
+              sr = fmaf(rv, gbv[k], sr);
+              dw = fmaf(mv[i], lv[i] - rv, dw);
+            }
           }
         }
       }
@@ -192,86 +240,99 @@ __global__ void __launch_bounds__(192, 1)
       const float w = 1.f / (1.f + expf(-x));
       const float wr = 1.f / (1.f + expf(x));
       const float ds = valid ? dw * w * wr : 0.f;
-      // pass 2: dL, D, dR, dg
+      // pass 2: dL, D, dR (written over dmixed in the tile: same thread, same
+      // bytes, after reading them), dg
       float dsum = 0.f;
-      uint8_t* drow_s = smem + L::DR + s * BM * HD * 2 + row * 128;
+      const int64_t gofs = tok * g.d + (int64_t)h * HD;
 #pragma unroll 1
       for (int cc = 0; cc < HD / 32; ++cc) {
         uint32_t rr[32];
-        tmem_ld32(tmem + lane_off + s * HD + cc * 32, rr);
+        tmem_ld32(tR + cc * 32, rr);
         tmem_ld_wait();
         float al[32];
         uint32_t pdl[16], pdr[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           float lv[8], mv[8];
-          unpack8(reinterpret_cast<const uint4*>(lrow + cc * 32)[q], lv);
-          unpack8(reinterpret_cast<const uint4*>(mrow + cc * 32)[q], mv);
+          unpack8(*chunk_ptr(lt, cc * 4 + q), lv);
+          unpack8(*chunk_ptr(dmt, cc * 4 + q), mv);
 #pragma unroll
-          for (int i = 0; i < 8; i += 2) {
-            float dlv[2], drv[2];
+          for (int i4 = 0; i4 < 2; ++i4) {
+            const int c4 = (cc * 32 + q * 8) / 4 + i4;
+            const float4 ga = __ldg(gl4 + c4), gb = __ldg(gr4 + c4);
+            const float gav[4] = {ga.x, ga.y, ga.z, ga.w}, gbv[4] = {gb.x, gb.y, gb.z, gb.w};
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int c = cc * 32 + q * 8 + i + u;
-              const float rv = __uint_as_float(rr[q * 8 + i + u]) + __ldg(bh + c);
-              const float a = __bfloat162float(__float2bfloat16_rn(w * mv[i + u] + ds * __ldg(gl + c)));
-              dlv[u] = a;
-              dsum = fmaf(a, lv[i + u], dsum);
-              drv[u] = wr * mv[i + u] - ds * __ldg(gr + c);
-              al[q * 8 + i + u] = ds * lv[i + u];
+            for (int k = 0; k < 4; k += 2) {
+              float dlv[2], drv[2];
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                const int i = i4 * 4 + k + u;
+                const float a = __bfloat162float(__float2bfloat16_rn(w * mv[i] + ds * gav[k + u]));
+                dlv[u] = a;
+                dsum = fmaf(a, lv[i], dsum);
+                drv[u] = valid ? wr * mv[i] - ds * gbv[k + u] : 0.f;
+                al[q * 8 + i] = ds * lv[i];
+              }
+              pdl[(q * 8 + i4 * 4 + k) / 2] = pack_bf16(dlv[0], dlv[1]);
+              pdr[(q * 8 + i4 * 4 + k) / 2] = pack_bf16(drv[0], drv[1]);
             }
-            pdl[(q * 8 + i) / 2] = pack_bf16(dlv[0], dlv[1]);
-            pdr[(q * 8 + i) / 2] = pack_bf16(drv[0], drv[1]);
           }
+          *chunk_ptr(dmt, cc * 4 + q) = make_uint4(pdr[4 * q], pdr[4 * q + 1], pdr[4 * q + 2], pdr[4 * q + 3]);
         }
         if (valid) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const uint4 vl = make_uint4(pdl[4 * q], pdl[4 * q + 1], pdl[4 * q + 2], pdl[4 * q + 3]);
-            const uint4 vr = make_uint4(pdr[4 * q], pdr[4 * q + 1], pdr[4 * q + 2], pdr[4 * q + 3]);
-            reinterpret_cast<uint4*>(dl + tok * g.d + (int64_t)h * HD + cc * 32)[q] = vl;
-            reinterpret_cast<uint4*>(dr + tok * g.d + (int64_t)h * HD + cc * 32)[q] = vr;
+            reinterpret_cast<uint4*>(dl + gofs + cc * 32)[q] =
+                make_uint4(pdl[4 * q], pdl[4 * q + 1], pdl[4 * q + 2], pdl[4 * q + 3]);
+            reinterpret_cast<uint4*>(dr + gofs + cc * 32)[q] =
+                make_uint4(pdr[4 * q], pdr[4 * q + 1], pdr[4 * q + 2], pdr[4 * q + 3]);
           }
-        }
-        // dR row into the swizzled A tile (rows past T hold zeros)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = cc * 4 + q;  // 16-byte chunk along HD
-          const uint4 vr = valid ? make_uint4(pdr[4 * q], pdr[4 * q + 1], pdr[4 * q + 2], pdr[4 * q + 3])
-                                 : make_uint4(0u, 0u, 0u, 0u);
-          *reinterpret_cast<uint4*>(drow_s + (chunk >> 3) * (BM * 128) + ((chunk & 7) ^ (row & 7)) * 16) = vr;
         }
         wred[cc * 32 + lane] += butterfly32(al, lane);
         {
           float ar[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ar[i] = -ds * (__uint_as_float(rr[i]) + __ldg(bh + cc * 32 + i));
+          for (int i4 = 0; i4 < 8; ++i4) {
+            const float4 bb = __ldg(bh4 + cc * 8 + i4);
+            ar[4 * i4] = -ds * (__uint_as_float(rr[4 * i4]) + bb.x);
+            ar[4 * i4 + 1] = -ds * (__uint_as_float(rr[4 * i4 + 1]) + bb.y);
+            ar[4 * i4 + 2] = -ds * (__uint_as_float(rr[4 * i4 + 2]) + bb.z);
+            ar[4 * i4 + 3] = -ds * (__uint_as_float(rr[4 * i4 + 3]) + bb.w);
+          }
           wred[HD + cc * 32 + lane] += butterfly32(ar, lane);
         }
       }
       if (valid) delta[((int64_t)b * H + h) * g.T + t] = dsum;
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(&bars[GB_DR + s]);
+      mbar_arrive(&bars[GB_DR + grp]);
+      // W buffer reuse: the dlat MMA of head h must have read it
+      if (h + 2 < H) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_DL + grp], n & 1, abort, &g_fault_word));
+        if (!ok) break;
+        write_w(h + 2);
+      }
     }
     if (!ok) raise_fault(kFaultSoftmax, abort);
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_DL + ((H - 1) & 1)], ((H - 1) >> 1) & 1, abort,
-                                                   &g_fault_word));
-    if (!ok) {
-      raise_fault(kFaultEpilogue, abort);
-    } else {
-      tc_fence_after();
+    if (grp == 0) {
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_DL + ((H - 1) & 1)], ((H - 1) >> 1) & 1, abort,
+                                                     &g_fault_word));
+      if (!ok) {
+        raise_fault(kFaultEpilogue, abort);
+      } else {
+        tc_fence_after();
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        uint32_t r[32];
-        tmem_ld32(tDL + lane_off + cc * 32, r);
-        tmem_ld_wait();
-        if (valid) {
-          float4* d = reinterpret_cast<float4*>(dlat_tok + tok * 64 + cc * 32);
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tDL + lane_off + cc * 32, r);
+          tmem_ld_wait();
+          if (valid) {
+            float4* d = reinterpret_cast<float4*>(dlat_tok + tok * 64 + cc * 32);
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            d[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
-                               __uint_as_float(r[4 * q + 3]));
+            for (int q = 0; q < 8; ++q)
+              d[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                 __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+          }
         }
       }
     }
@@ -279,8 +340,10 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   // partial [cta][2*HD] (dg_l half, dg_r half) summed over the compute warps
-  for (int e = threadIdx.x; e < 2 * HD; e += 192) {
-    const float v = red[e] + red[2 * HD + e] + red[4 * HD + e] + red[6 * HD + e];
+  for (int e = threadIdx.x; e < 2 * HD; e += blockDim.x) {
+    float v = 0.f;
+#pragma unroll
+    for (int w8 = 0; w8 < 8; ++w8) v += red[w8 * 2 * HD + e];
     dg_part[((int64_t)b * gridDim.x + blockIdx.x) * 2 * HD + e] = v;
   }
   if (warp == 1) {

@@ -459,13 +459,13 @@ bool make_rows_map(CUtensorMap* map, const void* base, int B, int T, int slots_x
 
 // LLATTN_FORCE_SIMT=1 routes bf16 through the SIMT kernels (used by the tests
 // to compare the two implementations of the same math).
-// bf16 matrix [rows, cols] (cols contiguous) with box (64 cols, 64 rows).
-bool make_2d_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols) {
+// bf16 matrix [rows, cols] (cols contiguous) with box (64 cols, box_rows rows).
+bool make_2d_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows = 64) {
   auto enc = get_encode();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {64, 64};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -502,7 +502,7 @@ cudaError_t dq_hd(const Geom& g, const void* qkv, const void* dl, const float* l
   cudaError_t e = cudaFuncSetAttribute(local_dq_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.T, BM), g.H, g.B);
-  local_dq_tc_kernel<HD><<<grid, 192, smem, s>>>(q128, q64, do128, g, lse, delta, static_cast<bf16*>(dqkv));
+  local_dq_tc_kernel<HD><<<grid, 320, smem, s>>>(q128, q64, do128, g, lse, delta, static_cast<bf16*>(dqkv));
   return cudaGetLastError();
 }
 
@@ -517,18 +517,22 @@ cudaError_t dkv_hd(const Geom& g, const void* qkv, const void* dl, const float* 
   cudaError_t e = cudaFuncSetAttribute(local_dkv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.T, BM), g.H, g.B);
-  local_dkv_tc_kernel<HD><<<grid, 192, smem, s>>>(q128, q64, do64, g, lse, delta, static_cast<bf16*>(dqkv));
+  local_dkv_tc_kernel<HD><<<grid, 320, smem, s>>>(q128, q64, do64, g, lse, delta, static_cast<bf16*>(dqkv));
   return cudaGetLastError();
 }
 
 template <int HD>
 cudaError_t gate_bwd_hd(const Geom& g, const GateBwd& a, cudaStream_t s) {
+  CUtensorMap tlo, tdm;
+  if (!make_2d_map(&tlo, a.local_out, (int64_t)g.B * g.T, g.d, 128) ||
+      !make_2d_map(&tdm, a.dmixed, (int64_t)g.B * g.T, g.d, 128))
+    return cudaErrorInvalidValue;
   const int smem = std::max(GbLayout<HD>::BYTES + 1024, 116 * 1024);
   cudaError_t e = cudaFuncSetAttribute(gate_bwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.T, BM), g.B);
-  gate_bwd_tc_kernel<HD><<<grid, 192, smem, s>>>(
-      g, static_cast<const bf16*>(a.local_out), static_cast<const bf16*>(a.lat), static_cast<const bf16*>(a.w_rout),
+  gate_bwd_tc_kernel<HD><<<grid, 320, smem, s>>>(
+      tlo, tdm, g, static_cast<const bf16*>(a.local_out), static_cast<const bf16*>(a.lat), static_cast<const bf16*>(a.w_rout),
       a.b_rout, a.g_local, a.g_remote, static_cast<const bf16*>(a.dmixed), static_cast<bf16*>(a.dl), a.delta,
       static_cast<bf16*>(a.dr), a.dlat_tok, a.dg_part);
   return cudaGetLastError();

@@ -35,7 +35,7 @@ struct DqLayout {
 enum { DQ_Q = 0, DQ_K = 1, DQ_V = 3, DQ_KVE = 5, DQ_SP = 7, DQ_DS = 9, DQ_DQ = 11, DQ_NB = 13 };
 
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     local_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv128, const __grid_constant__ CUtensorMap tm_qkv64,
                        const __grid_constant__ CUtensorMap tm_do128, Geom g, const float* __restrict__ lse,
                        const float* __restrict__ delta, bf16* __restrict__ dqkv) {
@@ -62,7 +62,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&bars[DQ_V + s], 1);
       mbar_init(&bars[DQ_KVE + s], 1);
       mbar_init(&bars[DQ_SP + s], 1);
-      mbar_init(&bars[DQ_DS + s], BM);
+      mbar_init(&bars[DQ_DS + s], 2 * BM);
       mbar_init(&bars[DQ_DQ + s], 1);
     }
     *abort = 0;
@@ -164,6 +164,9 @@ __global__ void __launch_bounds__(192, 1)
       if (!ok) raise_fault(kFaultMma, abort);
     }
   } else {
+    // warps 2..9: row = TMEM lane; warps w and w+4 share a lane quarter and
+    // split the columns (half 0 / half 1), two warps per scheduler
+    const int half = (warp - 2) >> 2;
     const int row = 32 * (warp & 3) + lane;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
     const int t = q0 + row;
@@ -183,8 +186,8 @@ __global__ void __launch_bounds__(192, 1)
       const int k0 = kbase + j * BNK;
       const int c_lo = lo - k0, c_hi = t - k0;
       uint8_t* dsrow = smem + L::DS + s * BM * BNK * 2 + row * 128;
-#pragma unroll
-      for (int cc = 0; cc < BNK / 32; ++cc) {
+      {
+        const int cc = half;  // this warp's 32 of the tile's 64 key columns
         uint32_t rs[32], rp[32];
         tmem_ld32(tmem + lane_off + s * BNK + cc * 32, rs);
         tmem_ld32(tmem + lane_off + 128 + s * BNK + cc * 32, rp);
@@ -223,7 +226,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       bf16* dst = dqkv + ((int64_t)b * g.T + (valid ? t : 0)) * 3 * g.d + (int64_t)h * HD;
 #pragma unroll
-      for (int cc = 0; cc < HD / 32; ++cc) {
+      for (int cc = half * (HD / 64); cc < (half + 1) * (HD / 64); ++cc) {
         uint32_t r[32];
         if (nk > 0) {
           tmem_ld32(tDQ + lane_off + cc * 32, r);
@@ -270,15 +273,15 @@ struct DkvLayout {
   static constexpr int DO = Q + 2 * QTILE;         // 2 stages
   static constexpr int PT = DO + 2 * QTILE;        // 2 buffers of 128 x 64 bf16
   static constexpr int DST = PT + 2 * BM * BNQ * 2;
-  static constexpr int VEC = DST + 2 * BM * BNQ * 2;  // per softmax warp: {lse2, D, lo}[64]
-  static constexpr int BAR = VEC + 4 * 3 * BNQ * 4;
+  static constexpr int VEC = DST + 2 * BM * BNQ * 2;  // per compute warp: {lse2, D}[32]
+  static constexpr int BAR = VEC + 8 * 2 * 32 * 4;
   static constexpr int BYTES = BAR + 256;
 };
 
 enum { KV_KV = 0, KV_QD = 1, KV_QDE = 3, KV_SP = 5, KV_PD = 7, KV_DKV = 9, KV_NB = 11 };
 
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     local_dkv_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv128, const __grid_constant__ CUtensorMap tm_qkv64,
                         const __grid_constant__ CUtensorMap tm_do64, Geom g, const float* __restrict__ lse,
                         const float* __restrict__ delta, bf16* __restrict__ dqkv) {
@@ -303,7 +306,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&bars[KV_QD + s], 1);
       mbar_init(&bars[KV_QDE + s], 1);
       mbar_init(&bars[KV_SP + s], 1);
-      mbar_init(&bars[KV_PD + s], BM);
+      mbar_init(&bars[KV_PD + s], 2 * BM);
       mbar_init(&bars[KV_DKV + s], 1);
     }
     *abort = 0;
@@ -404,16 +407,19 @@ __global__ void __launch_bounds__(192, 1)
       if (!ok) raise_fault(kFaultMma, abort);
     }
   } else {
+    // warps 2..9: row = TMEM lane = key; warps w and w+4 split the columns
+    const int half = (warp - 2) >> 2;
     const int row = 32 * (warp & 3) + lane;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
     const int j = k0 + row;            // this thread's key
     const bool valid = j < g.T;
     const float sc = g.scale * kLog2e;
-    // each softmax warp keeps its own copy of the query-tile vectors, so the
-    // four warps never wait on one another
-    float* v_lse = reinterpret_cast<float*>(smem + L::VEC) + (warp & 3) * 3 * BNQ;
-    float* v_d = v_lse + BNQ;
-    int* v_lo = reinterpret_cast<int*>(v_d + BNQ);
+    // queries that see key j form one range: t in (j, j+W] with qs(t) <= j+W-1,
+    // i.e. t < the end of the bsL-block holding j+W-1 (mask of models.py:286-292)
+    const int t_hi = min(min(j + g.W, ((j + g.W - 1) / g.bsL + 1) * g.bsL - 1), g.T - 1);  // inclusive
+    // per-warp copy of lse2 and D for this warp's 32 query columns
+    float* v_lse = reinterpret_cast<float*>(smem + L::VEC) + (warp - 2) * 64;
+    float* v_d = v_lse + 32;
     const float* lse_b = lse + ((int64_t)b * g.H + h) * g.T;
     const float* d_b = delta + ((int64_t)b * g.H + h) * g.T;
     bool ok = true;
@@ -421,12 +427,11 @@ __global__ void __launch_bounds__(192, 1)
       const int s = i & 1;
       const int t0 = tfirst + i * BNQ;
       __syncwarp();
-      for (int c = lane; c < BNQ; c += 32) {
-        const int t = t0 + c;
+      {
+        const int t = t0 + half * 32 + lane;
         const bool tv = t <= tlast;
-        v_lse[c] = tv ? lse_b[t] * kLog2e : INFINITY;
-        v_d[c] = tv ? d_b[t] : 0.f;
-        v_lo[c] = tv ? local_lo(g, t) : 0x7fffffff;
+        v_lse[lane] = tv ? lse_b[t] * kLog2e : INFINITY;
+        v_d[lane] = tv ? d_b[t] : 0.f;
       }
       __syncwarp();
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_SP + s], (i >> 1) & 1, abort, &g_fault_word));
@@ -436,8 +441,9 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       uint8_t* ptrow = smem + L::PT + s * BM * BNQ * 2 + row * 128;
       uint8_t* dsrow = smem + L::DST + s * BM * BNQ * 2 + row * 128;
-#pragma unroll
-      for (int cc = 0; cc < BNQ / 32; ++cc) {
+      const int c_lo = j + 1 - t0 - half * 32, c_hi = valid ? t_hi - t0 - half * 32 + 1 : -1;  // in [0, 32)
+      {
+        const int cc = half;
         uint32_t rs[32], rp[32];
         tmem_ld32(tmem + lane_off + s * BNQ + cc * 32, rs);
         tmem_ld32(tmem + lane_off + 128 + s * BNQ + cc * 32, rp);
@@ -448,12 +454,11 @@ __global__ void __launch_bounds__(192, 1)
           float pv[2], dv[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
-            const int c = cc * 32 + 2 * i2 + u;
-            const int t = t0 + c;
-            const bool vis = valid && j < t && j >= v_lo[c];
-            const float p = vis ? exp2f(__uint_as_float(rs[2 * i2 + u]) * sc - v_lse[c]) : 0.f;
+            const int c = 2 * i2 + u;
+            const bool vis = c >= c_lo && c < c_hi;
+            const float p = vis ? exp2f(__uint_as_float(rs[c]) * sc - v_lse[c]) : 0.f;
             pv[u] = p;
-            dv[u] = p * (__uint_as_float(rp[2 * i2 + u]) - v_d[c]);
+            dv[u] = p * (__uint_as_float(rp[c]) - v_d[c]);
           }
           pp[i2] = pack_bf16(pv[0], pv[1]);
           pd[i2] = pack_bf16(dv[0], dv[1]);
@@ -481,8 +486,8 @@ __global__ void __launch_bounds__(192, 1)
     } else {
       tc_fence_after();
       bf16* dst = dqkv + ((int64_t)b * g.T + (valid ? j : 0)) * 3 * g.d + (int64_t)h * HD;
-#pragma unroll
-      for (int which = 0; which < 2; ++which) {  // 0: dk (slot 1), 1: dv (slot 2)
+      {
+        const int which = half;  // half 0 writes dk (slot 1), half 1 dv (slot 2)
         const uint32_t tsrc = (which == 0 ? tDK : tDV) + lane_off;
         const float mul = which == 0 ? g.scale : 1.f;
         bf16* out = dst + (1 + which) * g.d;
