@@ -72,15 +72,17 @@ struct FwdLayout {
   // live in the P region: the R MMA reads them before P_0 is written
   static constexpr int LAT = P;
   static constexpr int WR = P + BM * 128;
-  static constexpr int BAR = P + BM * BN * 2;
-  static constexpr int BYTES = BAR + 128;
+  static constexpr int XCH = P + BM * BN * 2;   // half-pair exchange, 2 x 2 x 128 x 2 floats
+  static constexpr int BAR = XCH + 2 * 2 * BM * 2 * 4;
+  static constexpr int BYTES = BAR + 256;
 };
 
 // Barrier slots in the BAR region.
-enum { B_Q = 0, B_K = 1, B_V = 3, B_KVE = 5, B_S = 7, B_P = 9, B_O = 10, B_LW = 11, B_R = 12, N_BARS = 13 };
+enum { B_Q = 0, B_K = 1, B_V = 3, B_KVE = 5, B_S = 7, B_P = 9, B_O = 10, B_LW = 11, B_R = 12, B_X = 13,
+       N_BARS = 17 };
 
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     local_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, Geom g, bf16* __restrict__ local_out,
                         float* __restrict__ lse_out, GateEpilogue ep) {
   using L = FwdLayout<HD>;
@@ -106,9 +108,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&bars[B_KVE + s], 1);
       mbar_init(&bars[B_S + s], 1);
     }
-    mbar_init(&bars[B_P], BM);
+    mbar_init(&bars[B_P], 2 * BM);
     mbar_init(&bars[B_O], 1);
-    mbar_init(&bars[B_LW], BM);
+    mbar_init(&bars[B_LW], 2 * BM);
+    for (int q = 0; q < 4; ++q) mbar_init(&bars[B_X + q], 64);
     mbar_init(&bars[B_R], 1);
     *abort = 0;
     fence_barrier_init();
@@ -219,26 +222,46 @@ __global__ void __launch_bounds__(192, 1)
       if (!ok) raise_fault(kFaultMma, abort);
     }
   } else {
-    // ---------------- softmax / epilogue (warps 2..5) ----------------
-    const int row = 32 * (warp & 3) + lane;
-    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    // ---------------- softmax / epilogue (warps 2..9) ----------------
+    // Row r = TMEM lane r is shared by warps w and w+4 (same lane quarter):
+    // half 0 owns key columns [0,64) and O columns [0,hd/2), half 1 the rest.
+    // The pair exchanges row maxima / sums through shared memory guarded by
+    // a per-quarter mbarrier (64 arrivals per use, bounded waits).
+    const int half = (warp - 2) >> 2, quarter = warp & 3;
+    const int row = 32 * quarter + lane;
+    const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
     const int t = q0 + row;
     const bool valid = t < g.T;
     const int lo = valid ? local_lo(g, t) : 0x7fffffff;
     const float sc = g.scale * kLog2e;
-    float m = -INFINITY, l = 0.f;
+    float m = -INFINITY, l = 0.f;  // l: this half's partial row sum
     uint8_t* prow = smem + L::P + row * 128;
+    float* xch = reinterpret_cast<float*>(smem + L::XCH);  // [2 bufs][2 halves][128 rows][2]
+    int xuse = 0;
+    // publish (a, b) for this row, receive the partner half's pair
+    auto exchange = [&](float a, float bv, float& pa, float& pb) -> bool {
+      float* mine = xch + (((xuse & 1) * 2 + half) * BM + row) * 2;
+      float* other = xch + (((xuse & 1) * 2 + (half ^ 1)) * BM + row) * 2;
+      mine[0] = a;
+      mine[1] = bv;
+      mbar_arrive(&bars[B_X + quarter]);
+      const bool okx = __all_sync(0xffffffffu, mbar_wait(&bars[B_X + quarter], xuse & 1, abort, &g_fault_word));
+      pa = other[0];
+      pb = other[1];
+      ++xuse;
+      return okx;
+    };
     bool ok = true;
     if (fuse) {
-      // row `row` of the lat tile: latent output of this token's query row;
-      // rows < hd also copy one row of W_rout's head slice. 128-byte rows,
-      // 16-byte chunk c stored at slot c ^ (row % 8) (128-byte swizzle).
-      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.lat) +
-                                                        ((int64_t)b * g.Tq + (valid ? t / g.qbs : 0)) * 64);
-      uint8_t* dl_ = smem + L::LAT + row * 128;
+      // row `row` of the lat tile (half 0) and of W_rout's head slice (half 1,
+      // rows < hd): 128-byte rows, 16-byte chunk c at slot c ^ (row % 8)
+      if (half == 0) {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.lat) +
+                                                          ((int64_t)b * g.Tq + (valid ? t / g.qbs : 0)) * 64);
+        uint8_t* dl_ = smem + L::LAT + row * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dl_ + ((c ^ (row & 7)) * 16)) = src[c];
-      if (row < HD) {
+        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dl_ + ((c ^ (row & 7)) * 16)) = src[c];
+      } else if (row < HD) {
         const uint4* wsrc = reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.w_rout) +
                                                            ((int64_t)h * HD + row) * 64);
         uint8_t* wd = smem + L::WR + row * 128;
@@ -255,13 +278,13 @@ __global__ void __launch_bounds__(192, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_S + s], (j >> 1) & 1, abort, &g_fault_word));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t tsrc = (s ? tS1 : tS0) + lane_off;
-      const int c_lo = lo - (kbase + j * BN);  // visible columns: [c_lo, c_hi)
-      const int c_hi = t - (kbase + j * BN);
-      // pass 1: masked row max
+      const uint32_t tsrc = (s ? tS1 : tS0) + lane_off + half * 64;
+      const int c_lo = lo - (kbase + j * BN) - half * 64;  // visible columns of this half: [c_lo, c_hi)
+      const int c_hi = t - (kbase + j * BN) - half * 64;
+      // pass 1: masked row max over this half's 64 columns, then both halves
       float mx = -INFINITY;
 #pragma unroll
-      for (int cc = 0; cc < BN / 32; ++cc) {
+      for (int cc = 0; cc < 2; ++cc) {
         uint32_t r[32];
         tmem_ld32(tsrc + cc * 32, r);
         tmem_ld_wait();
@@ -271,6 +294,9 @@ __global__ void __launch_bounds__(192, 1)
           if (c >= c_lo && c < c_hi) mx = fmaxf(mx, __uint_as_float(r[i]));
         }
       }
+      float pmx, unused;
+      if (!(ok = exchange(mx, 0.f, pmx, unused))) break;
+      mx = fmaxf(mx, pmx);
       const float m_new = fmaxf(m, mx * sc);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
       const float alpha = exp2f(m - m_use);
@@ -280,11 +306,10 @@ __global__ void __launch_bounds__(192, 1)
         if (!ok) break;
       }
       tc_fence_after();
-      // pass 2: p = exp2(s*sc - m), bf16, swizzled store (chunk c of 8 keys
-      // goes to panel c/8, 16-byte slot (c%8) ^ (row%8))
+      // pass 2: p = exp2(s*sc - m), bf16, swizzled store into panel `half`
       float psum = 0.f;
 #pragma unroll
-      for (int cc = 0; cc < BN / 32; ++cc) {
+      for (int cc = 0; cc < 2; ++cc) {
         uint32_t r[32];
         tmem_ld32(tsrc + cc * 32, r);
         tmem_ld_wait();
@@ -302,8 +327,8 @@ __global__ void __launch_bounds__(192, 1)
         for (int q = 0; q < 4; ++q) {
           const int chunk = cc * 4 + q;
           const int slot = (chunk & 7) ^ (row & 7);
-          uint4 v = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          *reinterpret_cast<uint4*>(prow + (chunk >> 3) * L::PANEL + slot * 16) = v;
+          *reinterpret_cast<uint4*>(prow + half * L::PANEL + slot * 16) =
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
       fence_async_smem();
@@ -311,13 +336,14 @@ __global__ void __launch_bounds__(192, 1)
       m = m_new;
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-        for (int cc = 0; cc < HD / 32; ++cc) {
+        for (int cc = 0; cc < HD / 64; ++cc) {
           uint32_t r[32];
-          tmem_ld32(tO + lane_off + cc * 32, r);
+          const uint32_t ta = tO + lane_off + half * (HD / 2) + cc * 32;
+          tmem_ld32(ta, r);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(tO + lane_off + cc * 32, r);
+          tmem_st32(ta, r);
         }
         tmem_st_wait();
       }
@@ -325,93 +351,115 @@ __global__ void __launch_bounds__(192, 1)
       mbar_arrive(&bars[B_P]);
     }
     if (!ok) raise_fault(kFaultSoftmax, abort);
-    // epilogue: O / l -> bf16 row, logsumexp (natural log). The TMEM loads
-    // are warp-collective (.sync.aligned): every lane executes them, rows
-    // past T only skip the stores.
+    // epilogue. The TMEM loads are warp-collective (.sync.aligned): every
+    // lane executes them, rows past T only skip the stores.
     if (ok && nk > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[B_O], (nk - 1) & 1, abort, &g_fault_word));
+    float pl = 0.f, unused2;
+    if (ok) ok = exchange(l, 0.f, pl, unused2);
     if (!ok) {
       raise_fault(kFaultEpilogue, abort);
     } else {
       tc_fence_after();
+      l += pl;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      bf16* dst = local_out + ((int64_t)b * g.T + (valid ? t : 0)) * g.d + (int64_t)h * HD;
+      const int c0 = half * (HD / 2);  // this half's O columns
+      bf16* dst = local_out + ((int64_t)b * g.T + (valid ? t : 0)) * g.d + (int64_t)h * HD + c0;
       if (fuse) {
         // pass A: gate logits from the bf16-rounded local row (the value
-        // stored for the backward) and the remote row
-        const float* bh = ep.b_rout + (int64_t)h * HD;
+        // stored for the backward) and the remote row, halves combined
+        const float4* bh4 = reinterpret_cast<const float4*>(ep.b_rout + (int64_t)h * HD + c0);
+        const float4* gl4 = reinterpret_cast<const float4*>(ep.g_local + c0);
+        const float4* gr4 = reinterpret_cast<const float4*>(ep.g_remote + c0);
         float sl = 0.f, sr = 0.f;
 #pragma unroll
-        for (int cc = 0; cc < HD / 32; ++cc) {
+        for (int cc = 0; cc < HD / 64; ++cc) {
           uint32_t ro[32], rr[32];
-          if (nk > 0) tmem_ld32(tO + lane_off + cc * 32, ro);
-          tmem_ld32(tR + lane_off + cc * 32, rr);
+          if (nk > 0) tmem_ld32(tO + lane_off + c0 + cc * 32, ro);
+          tmem_ld32(tR + lane_off + c0 + cc * 32, rr);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = cc * 32 + i;
-            const float lv = nk > 0 ? __bfloat162float(__float2bfloat16_rn(__uint_as_float(ro[i]) * inv)) : 0.f;
-            sl = fmaf(lv, __ldg(ep.g_local + c), sl);
-            sr = fmaf(__uint_as_float(rr[i]) + __ldg(bh + c), __ldg(ep.g_remote + c), sr);
+          for (int i4 = 0; i4 < 8; ++i4) {
+            const float4 bb = __ldg(bh4 + cc * 8 + i4), ga = __ldg(gl4 + cc * 8 + i4), gb = __ldg(gr4 + cc * 8 + i4);
+            const float bv[4] = {bb.x, bb.y, bb.z, bb.w}, gav[4] = {ga.x, ga.y, ga.z, ga.w};
+            const float gbv[4] = {gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int i = 4 * i4 + k;
+              const float lv = nk > 0 ? __bfloat162float(__float2bfloat16_rn(__uint_as_float(ro[i]) * inv)) : 0.f;
+              sl = fmaf(lv, gav[k], sl);
+              sr = fmaf(__uint_as_float(rr[i]) + bv[k], gbv[k], sr);
+            }
           }
         }
-        const float x = sl + g.gate_bias - sr;
-        const float wl = 1.f / (1.f + expf(-x));
-        const float wr = 1.f / (1.f + expf(x));
-        bf16* mdst = static_cast<bf16*>(ep.mixed) + ((int64_t)b * g.T + (valid ? t : 0)) * g.d + (int64_t)h * HD;
-        // pass B: local_out and mixed
+        float psl, psr;
+        if (!exchange(sl, sr, psl, psr)) {
+          raise_fault(kFaultEpilogue, abort);
+        } else {
+          const float x = sl + psl + g.gate_bias - (sr + psr);
+          const float wl = 1.f / (1.f + expf(-x));
+          const float wr = 1.f / (1.f + expf(x));
+          bf16* mdst =
+              static_cast<bf16*>(ep.mixed) + ((int64_t)b * g.T + (valid ? t : 0)) * g.d + (int64_t)h * HD + c0;
+          // pass B: local_out and mixed
 #pragma unroll
-        for (int cc = 0; cc < HD / 32; ++cc) {
-          uint32_t ro[32], rr[32];
-          if (nk > 0) tmem_ld32(tO + lane_off + cc * 32, ro);
-          tmem_ld32(tR + lane_off + cc * 32, rr);
-          tmem_ld_wait();
-          uint32_t pl[16], pm[16];
+          for (int cc = 0; cc < HD / 64; ++cc) {
+            uint32_t ro[32], rr[32];
+            if (nk > 0) tmem_ld32(tO + lane_off + c0 + cc * 32, ro);
+            tmem_ld32(tR + lane_off + c0 + cc * 32, rr);
+            tmem_ld_wait();
+            uint32_t plk[16], pm[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float lv[2], mv[2];
+            for (int i4 = 0; i4 < 8; ++i4) {
+              const float4 bb = __ldg(bh4 + cc * 8 + i4);
+              const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+              float lv[4], mv[4];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int c = cc * 32 + 2 * i + u;
-              lv[u] = nk > 0 ? __bfloat162float(__float2bfloat16_rn(__uint_as_float(ro[2 * i + u]) * inv)) : 0.f;
-              mv[u] = wl * lv[u] + wr * (__uint_as_float(rr[2 * i + u]) + __ldg(bh + c));
+              for (int k = 0; k < 4; ++k) {
+                const int i = 4 * i4 + k;
+                lv[k] = nk > 0 ? __bfloat162float(__float2bfloat16_rn(__uint_as_float(ro[i]) * inv)) : 0.f;
+                mv[k] = wl * lv[k] + wr * (__uint_as_float(rr[i]) + bv[k]);
+              }
+              plk[2 * i4] = pack_bf16(lv[0], lv[1]);
+              plk[2 * i4 + 1] = pack_bf16(lv[2], lv[3]);
+              pm[2 * i4] = pack_bf16(mv[0], mv[1]);
+              pm[2 * i4 + 1] = pack_bf16(mv[2], mv[3]);
             }
-            pl[i] = pack_bf16(lv[0], lv[1]);
-            pm[i] = pack_bf16(mv[0], mv[1]);
-          }
-          if (valid) {
+            if (valid) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) = make_uint4(pl[4 * q], pl[4 * q + 1], pl[4 * q + 2],
-                                                                            pl[4 * q + 3]);
-              *reinterpret_cast<uint4*>(mdst + cc * 32 + q * 8) =
-                  make_uint4(pm[4 * q], pm[4 * q + 1], pm[4 * q + 2], pm[4 * q + 3]);
+              for (int q = 0; q < 4; ++q) {
+                *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) =
+                    make_uint4(plk[4 * q], plk[4 * q + 1], plk[4 * q + 2], plk[4 * q + 3]);
+                *reinterpret_cast<uint4*>(mdst + cc * 32 + q * 8) =
+                    make_uint4(pm[4 * q], pm[4 * q + 1], pm[4 * q + 2], pm[4 * q + 3]);
+              }
             }
           }
         }
       } else {
 #pragma unroll
-      for (int cc = 0; cc < HD / 32; ++cc) {
-        uint32_t r[32];
-        if (nk > 0) {
-          tmem_ld32(tO + lane_off + cc * 32, r);
-          tmem_ld_wait();
-        } else {
+        for (int cc = 0; cc < HD / 64; ++cc) {
+          uint32_t r[32];
+          if (nk > 0) {
+            tmem_ld32(tO + lane_off + c0 + cc * 32, r);
+            tmem_ld_wait();
+          } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = 0u;
-        }
-        uint32_t pk[16];
+            for (int i = 0; i < 32; ++i) r[i] = 0u;
+          }
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * inv, __uint_as_float(r[2 * i + 1]) * inv);
-        if (valid) {
+          for (int i = 0; i < 16; ++i)
+            pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * inv, __uint_as_float(r[2 * i + 1]) * inv);
+          if (valid) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) =
+                  make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
         }
       }
-      }
-      if (valid) lse_out[((int64_t)b * g.H + h) * g.T + t] = l > 0.f ? (m + log2f(l)) * kLn2 : INFINITY;
+      if (valid && half == 0)
+        lse_out[((int64_t)b * g.H + h) * g.T + t] = l > 0.f ? (m + log2f(l)) * kLn2 : INFINITY;
     }
   }
   tc_fence_before();
@@ -487,7 +535,7 @@ cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, 
   cudaError_t e = cudaFuncSetAttribute(local_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.T, BM), g.H, g.B);
-  local_fwd_tc_kernel<HD><<<grid, 192, smem, s>>>(tm, g, static_cast<bf16*>(local_out), lse, ep);
+  local_fwd_tc_kernel<HD><<<grid, 320, smem, s>>>(tm, g, static_cast<bf16*>(local_out), lse, ep);
   return cudaGetLastError();
 }
 
