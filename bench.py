@@ -64,6 +64,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--batch", type=int, default=0, help="override the config's batch (small profiling runs)")
+    p.add_argument("--workload", default="block", choices=["block", "lm"],
+                   help="block: the attention block fwd+bwd (default); lm: cfg4 LM training step")
+    p.add_argument("--layers", type=int, default=24, help="lm: decoder layers (cfg4: 24)")
     return p.parse_args()
 
 
@@ -233,6 +236,7 @@ def run_ours(args):
     import llattn_b200
     import llattn_oracle as O
     from llattn_b200 import _lib
+    from llattn_b200 import dist as D
     from parity import model_config
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -268,8 +272,7 @@ def run_ours(args):
         if world > 1:
             # data-parallel exchange: one flat bucket, all_reduce_mean
             torch.cat([p.grad.reshape(-1) for p in params], out=flat)
-            dist.all_reduce(flat)
-            flat.div_(world)
+            D.all_reduce_mean(flat)
 
     def barrier():
         if world > 1:
@@ -401,10 +404,117 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+LM_METRIC = "LM train tok/s (bf16, T=2048, cfg4 0.55B-class, AdamW, DDP)"
+
+
+def run_lm(args):
+    """cfg4: LocalLatentLM (24 x d1536 H12 W256 Nl64 Ld64, d_ff 4096, V32000,
+    tied embeddings), B16 x T2048 per GPU, bf16 autocast, fused AdamW, DDP
+    gradient all-reduce over NCCL (bucketed, overlapping the backward)."""
+    import torch
+    import torch.distributed as dist
+
+    import llattn_b200  # noqa: F401
+    from llattn_b200 import _lib
+    from llattn_b200 import dist as D
+    from llattn_b200.lm import LocalLatentLM, ModelConfig, build_optimizer, train_step
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    device = D.setup_distributed("nccl") if world > 1 else torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    rank = D.get_rank()
+    B = args.batch or 16
+    T = 2048
+    cfg = ModelConfig(vocab_size=32000, max_seq_len=T, d_model=1536, n_heads=12, n_layers=args.layers, d_ff=4096,
+                      local_window=256, latent_tokens=64, latent_d_model=64, latent_heads=2)
+    torch.manual_seed(0)  # identical init on every rank (DDP also broadcasts rank 0's)
+    model = LocalLatentLM(cfg).to(device)
+    n_params = sum(p.numel() for p in model.parameters())
+    if world > 1:
+        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[device.index], bucket_cap_mb=100,
+                                                          gradient_as_bucket_view=True)
+    opt = build_optimizer(model)
+    gen = torch.Generator().manual_seed(1000 + rank)
+    data_h = torch.randint(0, cfg.vocab_size, (B, T + 1), generator=gen, dtype=torch.int64).pin_memory()
+    data = data_h.to(device)
+    ids, tgt = data[:, :-1].contiguous(), data[:, 1:].contiguous()
+
+    for _ in range(args.warmup):
+        train_step(model, opt, ids, tgt)
+    torch.cuda.synchronize()
+    D.barrier()
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    time.sleep(0.3)
+    _lib.profile_enable(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        loss = train_step(model, opt, ids, tgt)
+    e1.record()
+    torch.cuda.synchronize()
+    D.barrier()
+    kern = _lib.profile_read()
+    _lib.profile_enable(False)
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    # end to end: the step's tokens copied from pinned host memory, loss read back
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(args.steps):
+        data.copy_(data_h, non_blocking=True)
+        loss = train_step(model, opt, data[:, :-1], data[:, 1:])
+        loss_h.copy_(loss, non_blocking=True)
+    e3.record()
+    torch.cuda.synchronize()
+    ms_e2e = e2.elapsed_time(e3) / args.steps
+    t = torch.tensor([ms, ms_e2e], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_e2e = t.tolist()
+    if rank == 0:
+        hbm, tflops, peak_kind = load_peaks()
+        sustained = tflops
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+                sustained = json.load(fh).get("bf16_tflops_sustained", tflops)
+        except (OSError, ValueError):
+            pass
+        tokens = B * T * world
+        n_nonemb = n_params - cfg.vocab_size * cfg.d_model - T * cfg.d_model
+        flops_tok = 6 * n_nonemb + 6 * cfg.vocab_size * cfg.d_model
+        ach = flops_tok * tokens / (ms / 1e3) / 1e12
+        per_step = {k: (v[0] / args.steps, v[1] / args.steps) for k, v in kern.items() if v[1] > 0}
+        out = {
+            "metric": LM_METRIC, "value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded uniform tokens in [0, 32000))",
+            "config": {"workload": "LocalLatentLM training step (cfg4)", "model": "LocalLatentLM 0.55B-class",
+                       "n_layers": cfg.n_layers, "params": n_params, "global_batch": B * world, "seq_len": T,
+                       "parallelism": f"dp{world}", "l2": "inputs and activations larger than L2"},
+            "e2e": {"value": round(tokens / (ms_e2e / 1e3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": data_h.numel() * 8, "d2h_bytes_per_step": 4},
+            "roofline": {"kernel": "whole step (6N FLOPs/token model)", "bound": "tensor",
+                         "achieved": round(ach / world, 1), "peak": sustained, "unit": "TFLOP/s",
+                         "frac": round(ach / world / sustained, 4), "peak_kind": peak_kind + " sustained",
+                         "traffic": None},
+            "gpu_launches": int(sum(v[1] for v in kern.values())),
+            "kernels": {k: {"ms_per_step": round(v[0], 4), "launches_per_step": v[1]} for k, v in per_step.items()},
+            "final_loss": float(loss.item()),
+            "clocks": clk,
+        }
+        print(json.dumps(out), flush=True)
+    D.cleanup_distributed()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "lm":
+        run_lm(args)
     else:
         run_ours(args)
 

@@ -132,19 +132,13 @@ __global__ void __launch_bounds__(256) latent_bwd_rows_kernel(
   }
   if (tid < kRowsBwd) {
     const int r = r0 + tid;
-    float dsum = 0.f;
     if (r < g.Tq) {
-      for (int e = 0; e < g.ldh; ++e)
-        dsum += dlat[(int64_t)(b * g.Tq + r) * g.Ld + lh * g.ldh + e] *
-                to_f<T>(lat[(int64_t)(b * g.Tq + r) * g.Ld + lh * g.ldh + e]);
       s_lse[tid] = lat_lse[(int64_t)(b * g.Lh + lh) * g.Tq + r];
       s_qid[tid] = row_qid(g, r);
-      delta_ws[(int64_t)(b * g.Lh + lh) * g.Tq + r] = dsum;
     } else {
       s_lse[tid] = INFINITY;
       s_qid[tid] = 0;
     }
-    s_delta[tid] = dsum;
   }
   const int max_qid = row_qid(g, min(r0 + kRowsBwd - 1, g.Tq - 1));
   // thread -> (row ri, 4-key subset kc) for dS; (row ri, e-subset ec) for drq
@@ -153,6 +147,47 @@ __global__ void __launch_bounds__(256) latent_bwd_rows_kernel(
   float acc[EPT];
 #pragma unroll
   for (int u = 0; u < EPT; ++u) acc[u] = 0.f;
+
+  // delta = dlat . lat, taken as sum_j P_j (dlat . gv_j) in fp32 rather than
+  // from the stored (rounded) lat: with long chunks the pooled values are
+  // nearly equal and dS = P (dlat.gv_j - delta) cancels, so delta must be
+  // consistent with P to working precision
+  float dpart = 0.f;
+  for (int j0 = 0; j0 < max_qid; j0 += kKeyTile) {
+    __syncthreads();
+    for (int idx = tid; idx < kKeyTile * L; idx += 256) {
+      const int jj = idx / L, e = idx % L, j = j0 + jj;
+      float kv = 0.f, vv = 0.f;
+      if (j < g.Nc && e < g.ldh) {
+        const int64_t base = ((int64_t)(b * g.Nc + j) * 2 * g.Lh + lh) * g.ldh + e;
+        kv = to_f<T>(gkv[base]);
+        vv = to_f<T>(gkv[base + (int64_t)g.Lh * g.ldh]);
+      }
+      s_k[jj][e] = kv;
+      s_v[jj][e] = vv;
+    }
+    __syncthreads();
+    const float lse = s_lse[ri];
+    const int qid = s_qid[ri];
+    for (int u = 0; u < kKeyTile / 4; ++u) {
+      const int jj = kc + 4 * u;
+      if (j0 + jj < qid) {
+        float sd = 0.f, dp = 0.f;
+#pragma unroll
+        for (int e = 0; e < L; ++e) {
+          sd = fmaf(s_rq[ri][e], s_k[jj][e], sd);
+          dp = fmaf(s_dl[ri][e], s_v[jj][e], dp);
+        }
+        dpart = fmaf(expf(sd * g.lat_scale - lse), dp, dpart);
+      }
+    }
+  }
+  dpart += __shfl_xor_sync(0xffffffffu, dpart, 1);
+  dpart += __shfl_xor_sync(0xffffffffu, dpart, 2);
+  if (kc == 0) {
+    s_delta[ri] = dpart;
+    if (r0 + ri < g.Tq) delta_ws[(int64_t)(b * g.Lh + lh) * g.Tq + r0 + ri] = dpart;
+  }
 
   for (int j0 = 0; j0 < max_qid; j0 += kKeyTile) {
     __syncthreads();

@@ -147,3 +147,45 @@ def test_deterministic_fwd_bwd():
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
     for k in a[2]:
         assert torch.equal(a[2][k], b[2][k]), k
+
+
+# cfg5 edge sweep (bf16): T in {1024, 4096, 8192, 32768} with ragged
+# companions (T % chunk != 0), head_dim {64, 128}, window {64, 1024},
+# n_latents {32, 512}, gate bias +8 / -8. Two heads per case keep the CPU
+# oracle within seconds at T = 32768.
+SWEEP = [
+    # T, hd, W, Nl, bias
+    (1024 + 37, 64, 64, 32, 8.0),
+    (1024, 128, 1024, 512, -8.0),
+    (4096 - 1, 128, 64, 512, 8.0),
+    (4096, 64, 1024, 32, -8.0),
+    (8192 + 37, 128, 1024, 32, 8.0),
+    (8192, 64, 64, 512, -8.0),
+    (32768, 128, 1024, 512, 8.0),
+    (32768 - 1, 64, 64, 32, -8.0),
+]
+
+
+@pytest.mark.parametrize("case", SWEEP)
+def test_cfg5_sweep(case):
+    T, hd, W, Nl, bias = case
+    dims = dict(B=1, T=T, d_model=2 * hd, n_heads=2, local_window=W, latent_tokens=Nl, latent_d_model=64,
+                latent_heads=2)
+    print(_block_case(dims, gate_bias=bias, oracle_dtype=torch.float32))
+
+
+def test_cfg2_full_batch_rows_against_oracle():
+    """cfg2 at full size (B16): all 16 sequences through the GPU block, the
+    oracle on sequences 0 and 15 (y and dx rows are per-sequence)."""
+    dims = dict(B=16, T=2048, d_model=1536, n_heads=12, local_window=256, latent_tokens=64, latent_d_model=64,
+                latent_heads=2)
+    B, T, cfg = make_cfg(dims)
+    params = bf16_round_params(O.init_params(cfg, 0))
+    gen = torch.Generator().manual_seed(7)
+    x = torch.randn(B, T, cfg.d_model, generator=gen).to(torch.bfloat16).float()
+    g = torch.randn(B, T, cfg.d_model, generator=gen).to(torch.bfloat16).float()
+    y, dx, _ = b200_block(params, x, g, cfg, 0.0, torch.bfloat16)
+    for bi in (0, 15):
+        ry, rdx, _ = oracle_block(params, x[bi:bi + 1], g[bi:bi + 1], cfg, 0.0, torch.float32)
+        assert rel_err(y[bi:bi + 1], ry) < TOL[torch.bfloat16]
+        assert rel_err(dx[bi:bi + 1], rdx) < TOL[torch.bfloat16]
