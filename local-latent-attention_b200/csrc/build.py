@@ -62,6 +62,10 @@ def _compile(name: str, fl: list[str]) -> str:
         if r.stderr.strip() and os.environ.get("LLATTN_PTXAS_V") == "1":
             sys.stderr.write(r.stderr)
         os.replace(obj + ".tmp", obj)
+        stem = name.replace(".cu", ".")
+        for old in os.listdir(BUILD):  # drop objects of earlier versions of this source
+            if old.startswith(stem) and old.endswith(".o") and os.path.join(BUILD, old) != obj:
+                os.remove(os.path.join(BUILD, old))
     return obj
 
 
