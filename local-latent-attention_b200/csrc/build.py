@@ -34,6 +34,8 @@ def flags() -> list[str]:
          "-I" + INCLUDE, "-I" + CSRC]
     if os.environ.get("LLATTN_CHECK_BOUNDS") == "1":
         f.append("-DLLATTN_CHECK_BOUNDS=1")
+    if os.environ.get("LLATTN_TRACE") == "1":
+        f.append("-DLLATTN_TRACE=1")
     if os.environ.get("LLATTN_PTXAS_V") == "1":
         f += ["-Xptxas", "-v"]
     return f

@@ -45,16 +45,6 @@ __device__ __forceinline__ float butterfly32(float (&v)[32], int lane) {
   return v[0];
 }
 
-__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
-  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 x = __bfloat1622float2(p[i]);
-    f[2 * i] = x.x;
-    f[2 * i + 1] = x.y;
-  }
-}
-
 // Warps: 0 idle, 1 = TMEM + MMA issuer, 2-5 = group 0 (even heads),
 // 6-9 = group 1 (odd heads); in a group thread = token row = TMEM lane.
 template <int HD>

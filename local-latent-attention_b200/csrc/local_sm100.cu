@@ -38,12 +38,26 @@ namespace sm100 {
 // second instead of timing out CTA by CTA.
 __device__ unsigned int g_fault_word = 0;
 
+#if defined(LLATTN_TRACE)
+// diagnostic builds only: per-CTA phase timestamps (globaltimer, ns)
+constexpr int kTraceCtas = 1024, kTraceEv = 64;
+__device__ unsigned long long g_trace[kTraceCtas][kTraceEv];
+#define LLATTN_TRACE_AT(ev)                                                                      \
+  do {                                                                                          \
+    const int cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);           \
+    if (cta_ < kTraceCtas && (ev) < kTraceEv) g_trace[cta_][(ev)] = ptx::globaltimer_ns();   \
+  } while (0)
+#else
+#define LLATTN_TRACE_AT(ev) \
+  do {                      \
+  } while (0)
+#endif
+
 namespace {
 
 using namespace ptx;
 
 constexpr int BM = 128;  // query rows per tile (= TMEM lanes)
-constexpr int BN = 128;  // keys per tile
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -61,6 +75,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 }
 
 #include "local_sm100_fwd.cuh"
+#include "local_sm100_fwd_pp.cuh"
 #include "local_sm100_bwd.cuh"
 #include "gate_sm100.cuh"
 
@@ -110,6 +125,19 @@ bool make_2d_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// bf16 [B, T, d] as 3-D (d, T, B), box (64, 128, 1), 128-byte swizzle.
+bool make_btd_map(CUtensorMap* map, const void* base, int B, int T, int d) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)d * 2, (cuuint64_t)T * d * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool force_simt() {
   const char* e = std::getenv("LLATTN_FORCE_SIMT");
   return e && e[0] == '1';
@@ -121,12 +149,25 @@ cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, 
   CUtensorMap tq, tkv;
   if (!make_rows_map(&tq, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_rows_map(&tkv, qkv, g.B, g.T, 3 * g.H, HD, 64))
     return cudaErrorInvalidValue;
-  // exactly the layout: two CTAs (and their 256 TMEM columns each) share an SM
-  const int smem = Fwd2Layout<HD>::BYTES;
-  cudaError_t e = cudaFuncSetAttribute(local_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (std::getenv("LLATTN_FWD_SINGLE") && std::getenv("LLATTN_FWD_SINGLE")[0] == '1') {
+    // one query tile per CTA, two CTAs per SM
+    const int smem = Fwd2Layout<HD>::BYTES;
+    cudaError_t e = cudaFuncSetAttribute(local_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid(cdiv(g.T, BM), g.H, g.B);
+    local_fwd_tc_kernel<HD><<<grid, 192, smem, s>>>(tq, tkv, g, static_cast<bf16*>(local_out), lse, ep);
+    return cudaGetLastError();
+  }
+  // two query tiles per CTA (ping-pong), one CTA per SM; the fused epilogue
+  // stores local_out and mixed through 3-D maps (d, T, B) that clip at T
+  CUtensorMap tlo, tmx;
+  if (!make_btd_map(&tlo, local_out, g.B, g.T, g.d) || !make_btd_map(&tmx, ep.mixed ? ep.mixed : local_out, g.B, g.T, g.d))
+    return cudaErrorInvalidValue;
+  const int smem = FwdPPLayout<HD>::BYTES;
+  cudaError_t e = cudaFuncSetAttribute(local_fwd_pp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(cdiv(g.T, BM), g.H, g.B);
-  local_fwd_tc_kernel<HD><<<grid, 192, smem, s>>>(tq, tkv, g, static_cast<bf16*>(local_out), lse, ep);
+  dim3 grid(cdiv(g.T, 2 * BM), g.H, g.B);
+  local_fwd_pp_kernel<HD><<<grid, 320, smem, s>>>(tq, tkv, tlo, tmx, g, static_cast<bf16*>(local_out), lse, ep);
   return cudaGetLastError();
 }
 
@@ -235,6 +276,12 @@ cudaError_t launch_local_dkv(const Geom& g, const void* qkv, const void* dl, con
   if (g.hd == 64) return dkv_hd<64>(g, qkv, dl, lse, delta, dqkv, s);
   return dkv_hd<128>(g, qkv, dl, lse, delta, dqkv, s);
 }
+
+#if defined(LLATTN_TRACE)
+extern "C" __attribute__((visibility("default"))) int llattn_trace_read(void* dst, size_t bytes) {
+  return (int)cudaMemcpyFromSymbol(dst, g_trace, bytes < sizeof(g_trace) ? bytes : sizeof(g_trace));
+}
+#endif
 
 unsigned read_fault_word(bool reset) {
   unsigned v = 0;

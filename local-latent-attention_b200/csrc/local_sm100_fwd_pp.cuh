@@ -1,0 +1,543 @@
+// Forward of the tensor-core local branch, two query tiles per CTA
+// ("ping-pong"; included by local_sm100.cu).
+//
+// One CTA per (batch, head, 256 queries) = query tiles A (rows q0..q0+127)
+// and B (q0+128..q0+255); 10 warps:
+//   warp 0     TMA producer: Q_A, Q_B, then the 64-key K/V tiles of the union
+//              of both tiles' key ranges, in a 2-stage ring (a key tile in
+//              the overlap is loaded once for both)
+//   warp 1     TMEM allocator (512 columns) and single-thread MMA issuer. For
+//              each key tile: S_A, S_B of the next tile, then PV_A, PV_B of
+//              this one, so one group's softmax overlaps the other's MMAs.
+//              After a group's last PV, its remote tile R = lat W_h^T goes
+//              into that group's freed S columns.
+//   warps 2-5  softmax of tile A, warps 6-9 softmax of tile B: thread = query
+//              row = TMEM lane; online softmax with the window mask, P bf16
+//              into swizzled smem, O rescale in TMEM, fused gate epilogue.
+// TMEM: S_A x2 [0,128), S_B x2 [128,256), O_A [256,256+hd), O_B after it.
+
+template <int HD>
+struct FwdPPLayout {
+  static constexpr int BNK = 64;
+  static constexpr int QPANEL = BM * 128;
+  static constexpr int KPANEL = BNK * 128;
+  static constexpr int QTILE = BM * HD * 2;
+  static constexpr int KTILE = BNK * HD * 2;
+  static constexpr int QA = 0;
+  static constexpr int QB = QA + QTILE;
+  static constexpr int NST = 3;                 // K/V ring depth
+  static constexpr int K = QB + QTILE;          // NST stages
+  static constexpr int V = K + NST * KTILE;     // NST stages
+  static constexpr int PA = V + NST * KTILE;      // 2 buffers of 128 x 64 bf16 per group
+  static constexpr int PB = PA + 2 * BM * BNK * 2;
+  static constexpr int END = PB + 2 * BM * BNK * 2;
+  // remote-tile operands (128 x 64 lat rows per group, hd x 64 W_rout slice):
+  // for hd = 128 they reuse each group's Q tile once its S MMAs are done,
+  // for hd = 64 they get their own region
+  static constexpr int LATA = HD == 128 ? QA : END;
+  static constexpr int WR = HD == 128 ? QA + BM * 128 : END + BM * 128;
+  static constexpr int LATB = HD == 128 ? QB : END + BM * 128 + HD * 128;
+  static constexpr int BAR = HD == 128 ? END : LATB + BM * 128;
+  static constexpr int BYTES = BAR + 256;
+};
+
+// per group g: S[2], P[2] (softmax arrivals), O[2] (PV done) — one barrier
+// per buffer, so a group running a tile ahead never makes a parity wait
+// ambiguous — plus LW (remote operands written) and R; shared: Q, K[2],
+// V[2], KVE[2]
+enum {
+  PP_Q = 0, PP_K = 1, PP_V = 4, PP_KVE = 7,  // K, V, KVE: + stage (3)
+  PP_LW = 10,  // + g
+  PP_S = 12,   // + 2*g + buffer
+  PP_P = 16,   // + 2*g + buffer
+  PP_O = 20,   // + 2*g + buffer
+  PP_R = 24,   // + g
+  PP_EP = 26,  // + g: epilogue tiles staged
+  PP_NB = 28
+};
+
+// The running max of a row is only moved (and O rescaled) when the new
+// maximum exceeds it by more than this many powers of two; otherwise P uses
+// the stale max and stays below 2^kRescaleLog2.
+constexpr float kRescaleLog2 = 8.f;
+
+struct PPTiles {
+  int first, last;  // key-tile range [first, last] of a query tile; last < first: none
+  __device__ bool has(int j) const { return j >= first && j <= last; }
+  __device__ int n() const { return last >= first ? last - first + 1 : 0; }
+};
+
+template <int HD>
+__global__ void __launch_bounds__(320, 1)
+    local_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kv,
+                        const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_mx, Geom g,
+                        bf16* __restrict__ local_out, float* __restrict__ lse_out, GateEpilogue ep) {
+  using L = FwdPPLayout<HD>;
+  constexpr int BNK = L::BNK;
+  extern __shared__ __align__(1024) uint8_t smem_pp[];
+  uint8_t* smem = smem_pp;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + PP_NB);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  if (smem_u32(smem) & 1023u) {
+    if (threadIdx.x == 0) atomicOr(&g_fault_word, kFaultEpilogue);
+    return;
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int q0 = blockIdx.x * 2 * BM;
+  if (threadIdx.x == 0) LLATTN_TRACE_AT(0);
+  const bool fuse = ep.lat != nullptr;
+  const bool has_b = q0 + BM < g.T;
+  const int kbase = local_lo(g, q0);  // first key of the union range
+  // key tiles [kbase + 64 j, +64) used by each query tile
+  PPTiles tA, tB;
+  {
+    const int lastA = min(q0 + BM - 1, g.T - 1) - 1;  // last key of tile A
+    tA.first = 0;
+    tA.last = lastA >= kbase ? (lastA - kbase) / BNK : -1;
+    if (has_b) {
+      const int loB = local_lo(g, q0 + BM), lastB = min(q0 + 2 * BM - 1, g.T - 1) - 1;
+      tB.first = (loB - kbase) / BNK;
+      tB.last = lastB >= loB ? (lastB - kbase) / BNK : -1;
+    } else {
+      tB.first = 0;
+      tB.last = -1;
+    }
+  }
+  const int nk = max(tA.last, tB.last) + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[PP_Q], 1);
+    for (int s = 0; s < L::NST; ++s) {
+      mbar_init(&bars[PP_K + s], 1);
+      mbar_init(&bars[PP_V + s], 1);
+      mbar_init(&bars[PP_KVE + s], 1);
+    }
+    for (int x = 0; x < 4; ++x) {
+      mbar_init(&bars[PP_S + x], 1);
+      mbar_init(&bars[PP_P + x], BM);
+      mbar_init(&bars[PP_O + x], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars[PP_LW + x], BM);
+      mbar_init(&bars[PP_R + x], 1);
+      mbar_init(&bars[PP_EP + x], BM);
+    }
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) LLATTN_TRACE_AT(1);
+
+  if (warp == 0) {
+    if (lane == 0 && nk > 0) {
+      int issued = 0;
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_kv);
+      mbar_expect_tx(&bars[PP_Q], 2 * L::QTILE);
+#pragma unroll
+      for (int p = 0; p < HD / 64; ++p) {
+        tma_load_4d(&tm_q, &bars[PP_Q], smem + L::QA + p * L::QPANEL, p * 64, h, q0, b);
+        tma_load_4d(&tm_q, &bars[PP_Q], smem + L::QB + p * L::QPANEL, p * 64, h, q0 + BM, b);
+      }
+      for (int j = 0; j < nk; ++j) {
+        const int s = j % L::NST;
+        if (j >= L::NST && !mbar_wait(&bars[PP_KVE + s], ((j / L::NST) - 1) & 1, abort, &g_fault_word)) {
+          raise_fault(kFaultProducer, abort);
+          break;
+        }
+        const int k0 = kbase + j * BNK;
+        mbar_expect_tx(&bars[PP_K + s], L::KTILE);
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p)
+          tma_load_4d(&tm_kv, &bars[PP_K + s], smem + L::K + s * L::KTILE + p * L::KPANEL, p * 64, g.H + h, k0, b);
+        mbar_expect_tx(&bars[PP_V + s], L::KTILE);
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p)
+          tma_load_4d(&tm_kv, &bars[PP_V + s], smem + L::V + s * L::KTILE + p * L::KPANEL, p * 64, 2 * g.H + h, k0,
+                      b);
+        issued = j + 1;
+      }
+      if (*abort) {
+        volatile int none = 0;
+        volatile unsigned gnone = 0;
+        mbar_wait(&bars[PP_Q], 0, &none, &gnone, 100000000ull);
+        for (int j = issued - L::NST < 0 ? 0 : issued - L::NST; j < issued; ++j) {
+          mbar_wait(&bars[PP_K + j % L::NST], (j / L::NST) & 1, &none, &gnone, 100000000ull);
+          mbar_wait(&bars[PP_V + j % L::NST], (j / L::NST) & 1, &none, &gnone, 100000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(BM, BNK, false, false);
+      constexpr uint32_t idO = idesc_bf16_f32(BM, HD, false, true);
+      constexpr uint32_t idR = idesc_bf16_f32(BM, HD, false, false);
+      const uint32_t qa = smem_u32(smem + L::QA), qb = smem_u32(smem + L::QB);
+      bool ok = true;
+      // Event-driven issue: each pass tests (without blocking) what has
+      // become ready and issues it, so neither group waits for the other.
+      //   S_x(i): K tile loaded, and S buffer i&1 free (P_x(i-2) landed,
+      //           which holds once PV_x(i-2) was issued: i <= npv + 1)
+      //   PV_x(i): P_x(i) landed and V tile loaded
+      //   R_x: after the group's last PV, once its lat / W_rout rows are in
+      // A K/V stage is released (KVE commit) once every group using the tile
+      // has issued its PV for it; releases happen in tile order.
+      int ns[2] = {0, 0}, npv[2] = {0, 0};
+      bool r_done[2] = {false, false};
+      const int nx[2] = {tA.n(), has_b ? tB.n() : 0};
+      const int first[2] = {tA.first, tB.first};
+      const bool grp_on[2] = {true, has_b};
+      int released = 0;  // tiles whose stage was released
+      if (nk > 0) ok = mbar_wait(&bars[PP_Q], 0, abort, &g_fault_word);
+      LLATTN_TRACE_AT(2);
+      uint64_t t_last = globaltimer_ns();
+      uint32_t spin = 0;
+      while (ok) {
+        bool progress = false, all_done = true;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          if (!grp_on[x]) continue;
+          // S
+          if (ns[x] < nx[x] && ns[x] <= npv[x] + 1) {
+            const int j = first[x] + ns[x], st = j % L::NST;
+            if (mbar_test_wait(&bars[PP_K + st], (j / L::NST) & 1)) {
+              tc_fence_after();
+              const uint32_t ka = smem_u32(smem + L::K + st * L::KTILE);
+              const uint32_t dst = tmem + x * 128 + (ns[x] & 1) * BNK;
+              const uint32_t q_addr = x ? qb : qa;
+#pragma unroll
+              for (int kk = 0; kk < HD / 16; ++kk)
+                mma_bf16(dst, desc_sw128(q_addr + (kk / 4) * L::QPANEL + (kk % 4) * 32, 16, 1024),
+                         desc_sw128(ka + (kk / 4) * L::KPANEL + (kk % 4) * 32, 16, 1024), idS, kk > 0);
+              mma_commit(&bars[PP_S + 2 * x + (ns[x] & 1)]);
+              ++ns[x];
+              progress = true;
+            }
+          }
+          // PV
+          if (npv[x] < ns[x]) {
+            const int i = npv[x], j = first[x] + i, st = j % L::NST;
+            if (mbar_test_wait(&bars[PP_P + 2 * x + (i & 1)], (i >> 1) & 1) &&
+                mbar_test_wait(&bars[PP_V + st], (j / L::NST) & 1)) {
+              tc_fence_after();
+              const uint32_t pa = smem_u32(smem + (x ? L::PB : L::PA) + (i & 1) * BM * BNK * 2);
+              const uint32_t va = smem_u32(smem + L::V + st * L::KTILE);
+#pragma unroll
+              for (int kk = 0; kk < BNK / 16; ++kk)
+                mma_bf16(tmem + 256 + x * HD, desc_sw128(pa + kk * 32, 16, 1024),
+                         desc_sw128(va + kk * 2048, L::KPANEL, 1024), idO, (i > 0 || kk > 0) ? 1u : 0u);
+              mma_commit(&bars[PP_O + 2 * x + (i & 1)]);
+              ++npv[x];
+              progress = true;
+            }
+          }
+          // R
+          if (fuse && !r_done[x] && npv[x] == nx[x]) {
+            if (mbar_test_wait(&bars[PP_LW + 0], 0) && (x == 0 || mbar_test_wait(&bars[PP_LW + 1], 0))) {
+              tc_fence_after();
+              const uint32_t la = smem_u32(smem + (x ? L::LATB : L::LATA)), wa = smem_u32(smem + L::WR);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_bf16(tmem + x * 128, desc_sw128(la + kk * 32, 16, 1024), desc_sw128(wa + kk * 32, 16, 1024), idR,
+                         kk > 0);
+              mma_commit(&bars[PP_R + x]);
+              r_done[x] = true;
+              progress = true;
+            }
+          }
+          if (npv[x] < nx[x] || (fuse && !r_done[x])) all_done = false;
+        }
+        // release K/V stages in tile order
+        while (released < nk) {
+          const int j = released;
+          bool used_done = true;
+#pragma unroll
+          for (int x = 0; x < 2; ++x)
+            if (grp_on[x] && j >= first[x] && j < first[x] + nx[x] && npv[x] <= j - first[x]) used_done = false;
+          if (!used_done) break;
+          mma_commit(&bars[PP_KVE + j % L::NST]);
+          ++released;
+          progress = true;
+        }
+        if (all_done && released == nk) break;
+        if (progress) {
+          t_last = globaltimer_ns();
+          spin = 0;
+        } else if ((++spin & 63u) == 0) {
+          if (*abort || g_fault_word || globaltimer_ns() - t_last > 1000000000ull) ok = false;
+        }
+      }
+      if (!ok) raise_fault(kFaultMma, abort);
+    }
+  } else {
+    const int grp = (warp - 2) >> 2;  // 0: tile A, 1: tile B
+    const PPTiles tt = grp ? tB : tA;
+    const int n_mine = tt.n();
+    const int row = 32 * (warp & 3) + lane;
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const int t = q0 + grp * BM + row;
+    const bool valid = t < g.T;
+    const int lo = valid ? local_lo(g, t) : 0x7fffffff;
+    const float sc = g.scale * kLog2e;
+    float m = -INFINITY, l = 0.f;  // m: reference max (log2 domain) of P and O
+    uint8_t* prow = smem + (grp ? L::PB : L::PA) + row * 128;
+    const uint32_t tS = tmem + grp * 128, tO = tmem + 256 + grp * HD, tR = tmem + grp * 128;
+    bool ok = true;
+    // remote-tile operands: this row's lat row (and, in group A, a row of
+    // W_rout's head slice). With hd = 128 they go into this group's Q tile,
+    // so they are written after the group's last S MMA (or after Q landed).
+    auto write_remote_operands = [&]() {
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.lat) +
+                                                        ((int64_t)b * g.Tq + (valid ? t / g.qbs : 0)) * 64);
+      uint8_t* dl_ = smem + (grp ? L::LATB : L::LATA) + row * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dl_ + ((c ^ (row & 7)) * 16)) = src[c];
+      if (grp == 0 && row < HD) {
+        const uint4* wsrc =
+            reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.w_rout) + ((int64_t)h * HD + row) * 64);
+        uint8_t* wd = smem + L::WR + row * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(wd + ((c ^ (row & 7)) * 16)) = wsrc[c];
+      }
+      fence_async_smem();
+      mbar_arrive(&bars[PP_LW + grp]);
+    };
+    if (grp == 1 && !has_b) {
+      if (fuse) {  // group A's R still waits on this group's arrival
+        if (nk > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_Q], 0, abort, &g_fault_word));
+        write_remote_operands();
+      }
+    } else {
+      for (int i = 0; ok && i < n_mine; ++i) {
+        const int j = tt.first + i;
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_S + 2 * grp + (i & 1)], (i >> 1) & 1, abort, &g_fault_word));
+        if (!ok) break;
+        if (row == 0) LLATTN_TRACE_AT(4 + grp * 24 + i);
+        tc_fence_after();
+        const uint32_t tsrc = tS + (i & 1) * BNK + lane_off;
+        const int c_lo = lo - (kbase + j * BNK);
+        const int c_hi = t - (kbase + j * BNK);
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tsrc, r0);
+        tmem_ld32(tsrc + 32, r1);
+        tmem_ld_wait();
+        // whole tile visible to every row of this warp: no per-element mask
+        const bool full = __all_sync(0xffffffffu, c_lo <= 0 && c_hi >= BNK);
+        float mx = -INFINITY;
+        if (full) {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) mx = fmaxf(mx, fmaxf(__uint_as_float(r0[q]), __uint_as_float(r1[q])));
+        } else {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) {
+            if (q >= c_lo && q < c_hi) mx = fmaxf(mx, __uint_as_float(r0[q]));
+            if (q + 32 >= c_lo && q + 32 < c_hi) mx = fmaxf(mx, __uint_as_float(r1[q]));
+          }
+        }
+        mx *= sc;
+        // move the reference max only when it grows by more than 2^8
+        const bool move = mx > m + kRescaleLog2;
+        const float m_new = move ? mx : m;
+        const float alpha = (move && m != -INFINITY) ? fast_exp2(m - m_new) : 1.f;
+        const float m_use = m_new == -INFINITY ? 0.f : m_new;
+        // P buffer (i&1) is free once PV(i-2) has read it
+        if (i >= 2) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_O + 2 * grp + (i & 1)], ((i - 2) >> 1) & 1, abort,
+                                                 &g_fault_word));
+          if (!ok) break;
+        }
+        uint8_t* pbuf = prow + (i & 1) * BM * BNK * 2;
+        float psum = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const int c = cc * 32 + 2 * q;
+            const float s0 = __uint_as_float(cc ? r1[2 * q] : r0[2 * q]);
+            const float s1 = __uint_as_float(cc ? r1[2 * q + 1] : r0[2 * q + 1]);
+            float p0 = fast_exp2(fmaf(s0, sc, -m_use));
+            float p1 = fast_exp2(fmaf(s1, sc, -m_use));
+            if (!full) {
+              p0 = (c >= c_lo && c < c_hi) ? p0 : 0.f;
+              p1 = (c + 1 >= c_lo && c + 1 < c_hi) ? p1 : 0.f;
+            }
+            psum += p0 + p1;
+            pk[q] = pack_bf16(p0, p1);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = cc * 4 + q;
+            *reinterpret_cast<uint4*>(pbuf + (((chunk & 7) ^ (row & 7)) * 16)) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
+        }
+        fence_async_smem();
+        l = l * alpha + psum;
+        m = m_new;
+        // rare: rescale O, after PV(i-1) has completed
+        if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_O + 2 * grp + ((i - 1) & 1)], ((i - 1) >> 1) & 1, abort,
+                                                 &g_fault_word));
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int cc = 0; cc < HD / 32; ++cc) {
+            uint32_t r[32];
+            tmem_ld32(tO + lane_off + cc * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q = 0; q < 32; ++q) r[q] = __float_as_uint(__uint_as_float(r[q]) * alpha);
+            tmem_st32(tO + lane_off + cc * 32, r);
+          }
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        mbar_arrive(&bars[PP_P + 2 * grp + (i & 1)]);
+        if (row == 0) LLATTN_TRACE_AT(16 + grp * 24 + i);
+      }
+      if (!ok) raise_fault(kFaultSoftmax, abort);
+      if (ok && fuse) {
+        // all of this group's S MMAs are done (or, without tiles, Q landed)
+        if (n_mine == 0 && nk > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_Q], 0, abort, &g_fault_word));
+        write_remote_operands();
+      }
+      if (ok && n_mine > 0)
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_O + 2 * grp + ((n_mine - 1) & 1)], ((n_mine - 1) >> 1) & 1,
+                                               abort, &g_fault_word));
+      if (ok && fuse) ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_R + grp], 0, abort, &g_fault_word));
+      if (row == 0) LLATTN_TRACE_AT(52 + 2 * grp);
+      if (!ok) {
+        raise_fault(kFaultEpilogue, abort);
+      } else {
+        tc_fence_after();
+        const int nk_here = n_mine;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        bf16* dst = local_out + ((int64_t)b * g.T + (valid ? t : 0)) * g.d + (int64_t)h * HD;
+        if (fuse) {
+          // one pass over TMEM: gate logits, and the bf16 local row and remote
+          // row (+ bias) staged in smem (local: this group's P buffers; remote:
+          // its Q tile, free once the remote MMAs have read the operands there)
+          if (HD == 128 && grp == 0 && has_b)  // W_rout rows in Q_A feed group B's remote MMA
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_R + 1], 0, abort, &g_fault_word));
+          uint8_t* ltile = smem + (grp ? L::PB : L::PA);
+          uint8_t* rtile = smem + (grp ? L::QB : L::QA);
+          auto tile_chunk = [&](uint8_t* tile, int c) -> uint4* {  // 16-byte chunk c of this row, SW128
+            return reinterpret_cast<uint4*>(tile + (c >> 3) * (BM * 128) + row * 128 + (((c & 7) ^ (row & 7)) * 16));
+          };
+          const float4* bh4 = reinterpret_cast<const float4*>(ep.b_rout + (int64_t)h * HD);
+          const float4* gl4 = reinterpret_cast<const float4*>(ep.g_local);
+          const float4* gr4 = reinterpret_cast<const float4*>(ep.g_remote);
+          float sl = 0.f, sr = 0.f;
+#pragma unroll 1
+          for (int cc = 0; cc < HD / 32; ++cc) {
+            uint32_t ro[32], rr[32];
+            if (nk_here > 0) tmem_ld32(tO + lane_off + cc * 32, ro);
+            tmem_ld32(tR + lane_off + cc * 32, rr);
+            tmem_ld_wait();
+            uint32_t pl[16], pr[16];
+#pragma unroll
+            for (int i4 = 0; i4 < 8; ++i4) {
+              const float4 bb = __ldg(bh4 + cc * 8 + i4), ga = __ldg(gl4 + cc * 8 + i4), gb = __ldg(gr4 + cc * 8 + i4);
+              const float bv[4] = {bb.x, bb.y, bb.z, bb.w}, gav[4] = {ga.x, ga.y, ga.z, ga.w};
+              const float gbv[4] = {gb.x, gb.y, gb.z, gb.w};
+              float lv[4], rv[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int q = 4 * i4 + k;
+                lv[k] = nk_here > 0 ? __bfloat162float(__float2bfloat16_rn(__uint_as_float(ro[q]) * inv)) : 0.f;
+                rv[k] = __uint_as_float(rr[q]) + bv[k];
+                sl = fmaf(lv[k], gav[k], sl);
+                sr = fmaf(rv[k], gbv[k], sr);
+              }
+              pl[2 * i4] = pack_bf16(lv[0], lv[1]);
+              pl[2 * i4 + 1] = pack_bf16(lv[2], lv[3]);
+              pr[2 * i4] = pack_bf16(rv[0], rv[1]);
+              pr[2 * i4 + 1] = pack_bf16(rv[2], rv[3]);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              *tile_chunk(ltile, cc * 4 + q) = make_uint4(pl[4 * q], pl[4 * q + 1], pl[4 * q + 2], pl[4 * q + 3]);
+              *tile_chunk(rtile, cc * 4 + q) = make_uint4(pr[4 * q], pr[4 * q + 1], pr[4 * q + 2], pr[4 * q + 3]);
+            }
+          }
+          const float x = sl + g.gate_bias - sr;
+          const float wl = 1.f / (1.f + expf(-x));
+          const float wr = 1.f / (1.f + expf(x));
+          // mixed = wl * local + wr * remote, in place over the remote row
+#pragma unroll 4
+          for (int c = 0; c < HD / 8; ++c) {
+            const uint4 lu = *tile_chunk(ltile, c);
+            uint4 ru = *tile_chunk(rtile, c);
+            float lf[8], rf[8];
+            unpack8(lu, lf);
+            unpack8(ru, rf);
+            ru = make_uint4(pack_bf16(wl * lf[0] + wr * rf[0], wl * lf[1] + wr * rf[1]),
+                            pack_bf16(wl * lf[2] + wr * rf[2], wl * lf[3] + wr * rf[3]),
+                            pack_bf16(wl * lf[4] + wr * rf[4], wl * lf[5] + wr * rf[5]),
+                            pack_bf16(wl * lf[6] + wr * rf[6], wl * lf[7] + wr * rf[7]));
+            *tile_chunk(rtile, c) = ru;
+          }
+          // both 128-row tiles to global by TMA (3-D maps: rows past T are clipped)
+          fence_async_smem();
+          mbar_arrive(&bars[PP_EP + grp]);
+          if (row == 0) {
+            if (mbar_wait(&bars[PP_EP + grp], 0, abort, &g_fault_word)) {
+#pragma unroll
+              for (int p = 0; p < HD / 64; ++p) {
+                tma_store_3d(&tm_lo, ltile + p * (BM * 128), h * HD + p * 64, q0 + grp * BM, b);
+                tma_store_3d(&tm_mx, rtile + p * (BM * 128), h * HD + p * 64, q0 + grp * BM, b);
+              }
+              tma_store_commit();
+              tma_store_wait_read();
+            } else {
+              raise_fault(kFaultEpilogue, abort);
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int cc = 0; cc < HD / 32; ++cc) {
+            uint32_t r[32];
+            if (nk_here > 0) {
+              tmem_ld32(tO + lane_off + cc * 32, r);
+              tmem_ld_wait();
+            } else {
+#pragma unroll
+              for (int q = 0; q < 32; ++q) r[q] = 0u;
+            }
+            uint32_t pk[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+              pk[q] = pack_bf16(__uint_as_float(r[2 * q]) * inv, __uint_as_float(r[2 * q + 1]) * inv);
+            if (valid) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) =
+                    make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+            }
+          }
+        }
+        if (valid) lse_out[((int64_t)b * g.H + h) * g.T + t] = l > 0.f ? (m + log2f(l)) * kLn2 : INFINITY;
+      }
+      if (row == 0) LLATTN_TRACE_AT(53 + 2 * grp);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) LLATTN_TRACE_AT(60);
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
