@@ -1,25 +1,17 @@
-// Local branch on the 5th-generation tensor cores (sm_100a): windowed causal
-// attention with the reference's blockwise mask (models.py:232-305), bf16 in,
-// fp32 accumulation in TMEM, head_dim 64 or 128.
+// Tensor-core (tcgen05 + TMA) kernels of the local branch and of the
+// r_out / gate backward for bf16 activations on sm_100a, and their host-side
+// launchers (tensor maps, shared-memory sizing). The kernels live in:
+//   local_sm100_fwd_pp.cuh  forward, two 128-query tiles per CTA, fused
+//                           remote projection + gate + mix epilogue
+//   local_sm100_bwd.cuh     dq (per query tile) and dk/dv (per key tile)
+//   gate_sm100.cuh          gate / r_out backward and the dW_rout GEMM
+// Windowed causal mask of the reference (models.py:232-305): key j is
+// visible from query t iff 0 < t-j <= W and j >= qs(t) - W + 1.
 //
-// Forward, one CTA per (batch, head, 128-query tile), 6 warps:
-//   warp 0     TMA producer: Q tile once, then K/V tiles of 128 keys into a
-//              2-stage ring (tensor map over the qkv projection output
-//              [B, T, 3, H, hd] read in place, 128-byte swizzle, OOB -> 0)
-//   warp 1     TMEM allocator + single-thread tcgen05.mma issuer:
-//              S_j = Q K_j^T (M128 N128, K = hd) into one of two TMEM S
-//              buffers, then O += P_j V_j (M128 N=hd, K = 128 keys)
-//   warps 2-5  softmax: thread r owns query row r = TMEM lane r. Reads S_j
-//              from TMEM, applies the window mask and online softmax (exp2),
-//              writes P_j (bf16, swizzled K-major) to shared memory, rescales
-//              O in TMEM when the running max moves, and finally writes the
-//              normalised row and its logsumexp.
-// Key tiles start at lo(q0) (the first key any row of the tile sees), so a
-// tile of 128 rows with window W touches ceil((127 + W) / 128) key tiles.
-//
-// Every wait is bounded (mbar_wait): on timeout the kernel records a fault
-// bit in g_fault_word, tells the other warps to stop, frees its TMEM and
-// returns; the host reads the word with llattn_fault_status().
+// Every wait is bounded (mbar_wait): on timeout a kernel records a fault
+// bit in g_fault_word, tells its other warps to stop, waits for its own
+// in-flight copies, frees its TMEM and returns; the host reads the word with
+// llattn_fault_status().
 #include <cudaTypedefs.h>
 #include <math.h>
 
@@ -74,7 +66,6 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-#include "local_sm100_fwd.cuh"
 #include "local_sm100_fwd_pp.cuh"
 #include "local_sm100_bwd.cuh"
 #include "gate_sm100.cuh"
@@ -149,15 +140,6 @@ cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, 
   CUtensorMap tq, tkv;
   if (!make_rows_map(&tq, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_rows_map(&tkv, qkv, g.B, g.T, 3 * g.H, HD, 64))
     return cudaErrorInvalidValue;
-  if (std::getenv("LLATTN_FWD_SINGLE") && std::getenv("LLATTN_FWD_SINGLE")[0] == '1') {
-    // one query tile per CTA, two CTAs per SM
-    const int smem = Fwd2Layout<HD>::BYTES;
-    cudaError_t e = cudaFuncSetAttribute(local_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    dim3 grid(cdiv(g.T, BM), g.H, g.B);
-    local_fwd_tc_kernel<HD><<<grid, 192, smem, s>>>(tq, tkv, g, static_cast<bf16*>(local_out), lse, ep);
-    return cudaGetLastError();
-  }
   // two query tiles per CTA (ping-pong), one CTA per SM; the fused epilogue
   // stores local_out and mixed through 3-D maps (d, T, B) that clip at T
   CUtensorMap tlo, tmx;

@@ -199,7 +199,8 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int c = cc * 32 + 2 * i + u;
-            const float p = (c >= c_lo && c < c_hi) ? exp2f(__uint_as_float(rs[2 * i + u]) * sc - lse2) : 0.f;
+            const float e = fast_exp2(fmaf(__uint_as_float(rs[2 * i + u]), sc, -lse2));
+            const float p = (c >= c_lo && c < c_hi) ? e : 0.f;
             v[u] = p * (__uint_as_float(rp[2 * i + u]) - dt);
           }
           pk[i] = pack_bf16(v[0], v[1]);
@@ -423,17 +424,23 @@ __global__ void __launch_bounds__(320, 1)
     const float* lse_b = lse + ((int64_t)b * g.H + h) * g.T;
     const float* d_b = delta + ((int64_t)b * g.H + h) * g.T;
     bool ok = true;
+    // this lane's lse2 / D for the next query tile, loaded one tile ahead
+    auto fetch = [&](int i, float& l2, float& dd) {
+      const int t = tfirst + i * BNQ + half * 32 + lane;
+      const bool tv = i < nq && t <= tlast;
+      l2 = tv ? __ldg(lse_b + t) * kLog2e : INFINITY;
+      dd = tv ? __ldg(d_b + t) : 0.f;
+    };
+    float nl2, nd;
+    fetch(0, nl2, nd);
     for (int i = 0; i < nq; ++i) {
       const int s = i & 1;
       const int t0 = tfirst + i * BNQ;
       __syncwarp();
-      {
-        const int t = t0 + half * 32 + lane;
-        const bool tv = t <= tlast;
-        v_lse[lane] = tv ? lse_b[t] * kLog2e : INFINITY;
-        v_d[lane] = tv ? d_b[t] : 0.f;
-      }
+      v_lse[lane] = nl2;
+      v_d[lane] = nd;
       __syncwarp();
+      fetch(i + 1, nl2, nd);
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_SP + s], (i >> 1) & 1, abort, &g_fault_word));
       if (ok && i >= 2) ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_DKV + s], ((i >> 1) - 1) & 1, abort,
                                                                  &g_fault_word));
@@ -456,7 +463,8 @@ __global__ void __launch_bounds__(320, 1)
           for (int u = 0; u < 2; ++u) {
             const int c = 2 * i2 + u;
             const bool vis = c >= c_lo && c < c_hi;
-            const float p = vis ? exp2f(__uint_as_float(rs[c]) * sc - v_lse[c]) : 0.f;
+            const float e = fast_exp2(fmaf(__uint_as_float(rs[c]), sc, -v_lse[c]));
+            const float p = vis ? e : 0.f;
             pv[u] = p;
             dv[u] = p * (__uint_as_float(rp[c]) - v_d[c]);
           }
