@@ -15,10 +15,12 @@ Keys beyond the base contract:
   e2e           same metric through the public module API with the step's
                 inputs (x, upstream grad) copied from pinned host memory and
                 dx copied back, inside the timed region
-  roofline      dominant kernel: algorithmic FLOPs (local branch: 4*hd*P fwd,
-                8*hd*P bwd, P = visible query/key pairs) or bytes per launch
-                over its CUDA-event time in the timed region, against
-                MEASURED_PEAKS.json; traffic from the committed ncu summary
+  roofline      dominant kernel: its algorithmic FLOPs (local branch: 4*hd*P
+                per launch, P = visible query/key pairs) and bytes per launch;
+                the bound is the roof whose ideal time is longer; achieved =
+                that amount over the kernel's CUDA-event time in the timed
+                region, against MEASURED_PEAKS.json; traffic = DRAM bytes per
+                launch from the committed full-size ncu capture
   cpu_baseline  the CPU oracle (a restatement of the reference PyTorch block)
                 on the host cores, bounded sample
   kernels       per-kernel-group event times (ms per step) and launch counts
@@ -371,15 +373,17 @@ def run_ours(args):
     P = O.local_pairs(T, cfg.local_window, cfg.local_block_size) * B * cfg.n_heads
     hd = cfg.head_dim
     d = cfg.d_model
-    alg = {  # per launch-group call: (amount, unit)
-        "local_fwd": (4.0 * hd * P, "flop"),
-        "local_bwd": (8.0 * hd * P, "flop"),
-        "local_dq": (4.0 * hd * P, "flop"),   # dP and dS.K (recompute of S not counted)
-        "local_dkv": (4.0 * hd * P, "flop"),  # dV and dK
-        "gate_fwd": ((2 * B * T * d + B * T * d + 2 * d * cfg.latent_d_model) * 2.0, "byte"),
-        "gate_bwd": ((3 * B * T * d) * 2.0 + B * T * d * 4.0, "byte"),
-        "pool_fwd": (B * T * d * 2.0, "byte"),
-        "pool_bwd": (B * T * d * 2.0, "byte"),
+    BTd2 = B * T * d * 2.0  # one [B,T,d] bf16 tensor
+    # per launch-group call: (FLOPs, bytes that must cross HBM)
+    alg = {
+        "local_fwd": (4.0 * hd * P, 3 * BTd2 + 2 * BTd2),    # qkv in; local_out, mixed out
+        "local_bwd": (8.0 * hd * P, 4 * BTd2 + 3 * BTd2),
+        "local_dq": (4.0 * hd * P, 4 * BTd2 + BTd2),        # q,k,v,dlocal in; dq out
+        "local_dkv": (4.0 * hd * P, 4 * BTd2 + 2 * BTd2),   # q,k,v,dlocal in; dk,dv out
+        "gate_fwd": (0.0, (2 * B * T * d + B * T * d + 2 * d * cfg.latent_d_model) * 2.0),
+        "gate_bwd": (0.0, 4 * BTd2),                        # local_out, dmixed in; dlocal, dR out
+        "pool_fwd": (0.0, BTd2),
+        "pool_bwd": (0.0, BTd2),
     }
     per_step = {k: (v[0] / args.steps, v[1] / args.steps) for k, v in kern.items() if v[1] > 0}
     top = max(per_step, key=lambda k: per_step[k][0])
@@ -388,16 +392,24 @@ def run_ours(args):
     avg_ms = kern[top][0] / args.steps / calls
     roof = None
     if top in alg:
-        amount, unit = alg[top]
-        if unit == "flop":
-            ach = amount / (avg_ms / 1e3) / 1e12
-            roof = {"kernel": top, "bound": "tensor", "achieved": round(ach, 2), "peak": tflops,
-                    "unit": "TFLOP/s", "frac": round(ach / tflops, 4), "peak_kind": peak_kind}
+        # the binding roof is the one whose ideal time (amount / peak) is longer
+        flops, nbytes = alg[top]
+        t_tensor = flops / (tflops * 1e12)
+        t_hbm = nbytes / (hbm * 1e9)
+        f_ach = flops / (avg_ms / 1e3) / 1e12
+        b_ach = nbytes / (avg_ms / 1e3) / 1e9
+        if t_tensor > t_hbm:
+            roof = {"kernel": top, "bound": "tensor", "achieved": round(f_ach, 2), "peak": tflops,
+                    "unit": "TFLOP/s", "frac": round(f_ach / tflops, 4), "peak_kind": peak_kind,
+                    "hbm_frac": round(b_ach / hbm, 4)}
         else:
-            ach = amount / (avg_ms / 1e3) / 1e9
-            roof = {"kernel": top, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm,
-                    "unit": "GB/s", "frac": round(ach / hbm, 4), "peak_kind": peak_kind}
-        tr = load_traffic().get(f"{top}:{args.config}")
+            roof = {"kernel": top, "bound": "hbm", "achieved": round(b_ach, 1), "peak": hbm,
+                    "unit": "GB/s", "frac": round(b_ach / hbm, 4), "peak_kind": peak_kind,
+                    "algorithmic_bytes": nbytes}
+            if flops:
+                roof["tensor_frac"] = round(f_ach / tflops, 4)
+        # measured at the config's default batch; other batches get null
+        tr = None if args.batch else load_traffic().get(f"{top}:{args.config}")
         roof["traffic"] = tr
         roof["avg_launch_ms"] = round(avg_ms, 4)
     # also the local branch as a whole (fwd + bwd), the BASELINE target
