@@ -148,7 +148,7 @@ cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, 
   const int smem = FwdPPLayout<HD>::BYTES;
   cudaError_t e = cudaFuncSetAttribute(local_fwd_pp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(cdiv(g.T, 2 * BM), g.H, g.B);
+  dim3 grid(g.H, cdiv(g.T, 2 * BM), g.B);
   local_fwd_pp_kernel<HD><<<grid, 320, smem, s>>>(tq, tkv, tlo, tmx, g, static_cast<bf16*>(local_out), lse, ep);
   return cudaGetLastError();
 }
@@ -156,30 +156,30 @@ cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, 
 template <int HD>
 cudaError_t dq_hd(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta, void* dqkv,
                   cudaStream_t s) {
-  CUtensorMap q128, q64, do128;
+  CUtensorMap q128, q64, do128, st;
   if (!make_rows_map(&q128, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_rows_map(&q64, qkv, g.B, g.T, 3 * g.H, HD, 64) ||
-      !make_rows_map(&do128, dl, g.B, g.T, g.H, HD, 128))
+      !make_rows_map(&do128, dl, g.B, g.T, g.H, HD, 128) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, HD, 128))
     return cudaErrorInvalidValue;
   const int smem = std::max(DqLayout<HD>::BYTES + 1024, 116 * 1024);
   cudaError_t e = cudaFuncSetAttribute(local_dq_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(cdiv(g.T, BM), g.H, g.B);
-  local_dq_tc_kernel<HD><<<grid, 320, smem, s>>>(q128, q64, do128, g, lse, delta, static_cast<bf16*>(dqkv));
+  dim3 grid(g.H, cdiv(g.T, BM), g.B);
+  local_dq_tc_kernel<HD><<<grid, 320, smem, s>>>(q128, q64, do128, st, g, lse, delta);
   return cudaGetLastError();
 }
 
 template <int HD>
 cudaError_t dkv_hd(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta, void* dqkv,
                    cudaStream_t s) {
-  CUtensorMap q128, q64, do64;
+  CUtensorMap q128, q64, do64, st;
   if (!make_rows_map(&q128, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_rows_map(&q64, qkv, g.B, g.T, 3 * g.H, HD, 64) ||
-      !make_rows_map(&do64, dl, g.B, g.T, g.H, HD, 64))
+      !make_rows_map(&do64, dl, g.B, g.T, g.H, HD, 64) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, HD, 128))
     return cudaErrorInvalidValue;
   const int smem = std::max(DkvLayout<HD>::BYTES + 1024, 116 * 1024);
   cudaError_t e = cudaFuncSetAttribute(local_dkv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(cdiv(g.T, BM), g.H, g.B);
-  local_dkv_tc_kernel<HD><<<grid, 320, smem, s>>>(q128, q64, do64, g, lse, delta, static_cast<bf16*>(dqkv));
+  dim3 grid(g.H, cdiv(g.T, BM), g.B);
+  local_dkv_tc_kernel<HD><<<grid, 320, smem, s>>>(q128, q64, do64, st, g, lse, delta);
   return cudaGetLastError();
 }
 

@@ -19,26 +19,28 @@
 template <int HD>
 struct DqLayout {
   static constexpr int BNK = 64;                  // keys per inner tile
+  static constexpr int NKS = 4;                    // K / V stages
   static constexpr int QPANEL = BM * 128;          // 128-row panel (16 KB)
   static constexpr int KPANEL = BNK * 128;         // 64-row panel (8 KB)
   static constexpr int QTILE = BM * HD * 2;
   static constexpr int KTILE = BNK * HD * 2;
   static constexpr int Q = 0;
   static constexpr int DO = Q + QTILE;
-  static constexpr int K = DO + QTILE;             // 2 stages
-  static constexpr int V = K + 2 * KTILE;          // 2 stages
-  static constexpr int DS = V + 2 * KTILE;         // 2 buffers of 128 x 64 bf16
-  static constexpr int BAR = DS + 2 * BM * BNK * 2;
+  static constexpr int K = DO + QTILE;             // NKS stages
+  static constexpr int V = K + NKS * KTILE;        // NKS stages
+  static constexpr int BAR = V + NKS * KTILE;
   static constexpr int BYTES = BAR + 256;
 };
 
-enum { DQ_Q = 0, DQ_K = 1, DQ_V = 3, DQ_KVE = 5, DQ_SP = 7, DQ_DS = 9, DQ_DQ = 11, DQ_NB = 13 };
+// barriers: Q/dO loaded; per K/V stage loaded (K, V) / released; per TMEM
+// buffer S,dP ready / dS written / dQ MMAs done
+enum { DQ_Q = 0, DQ_K = 1, DQ_V = 5, DQ_KVE = 9, DQ_SP = 13, DQ_DS = 15, DQ_DQ = 17, DQ_NB = 19 };
 
 template <int HD>
 __global__ void __launch_bounds__(320, 1)
     local_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv128, const __grid_constant__ CUtensorMap tm_qkv64,
-                       const __grid_constant__ CUtensorMap tm_do128, Geom g, const float* __restrict__ lse,
-                       const float* __restrict__ delta, bf16* __restrict__ dqkv) {
+                       const __grid_constant__ CUtensorMap tm_do128, const __grid_constant__ CUtensorMap tm_st,
+                       Geom g, const float* __restrict__ lse, const float* __restrict__ delta) {
   using L = DqLayout<HD>;
   constexpr int BNK = L::BNK;
   extern __shared__ uint8_t smem_raw[];
@@ -48,8 +50,9 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int q0 = blockIdx.x * BM;
+  // heads fastest: CTAs that run together cover whole token rows of qkv
+  const int h = blockIdx.x, b = blockIdx.z;
+  const int q0 = blockIdx.y * BM;
   const int qlast = min(q0 + BM - 1, g.T - 1);
   const int kbase = local_lo(g, q0);
   const int khi = qlast - 1;
@@ -57,10 +60,12 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars[DQ_Q], 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < L::NKS; ++s) {
       mbar_init(&bars[DQ_K + s], 1);
       mbar_init(&bars[DQ_V + s], 1);
       mbar_init(&bars[DQ_KVE + s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&bars[DQ_SP + s], 1);
       mbar_init(&bars[DQ_DS + s], 2 * BM);
       mbar_init(&bars[DQ_DQ + s], 1);
@@ -77,7 +82,9 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // S buffers at columns [0,64) and [64,128); dP at [128,192) and [192,256)
+  // S buffers at columns [0,64) and [64,128); dP at [128,192) and [192,256).
+  // dS (bf16) is written back over the first 16 of each 32 dP columns that
+  // produced it and feeds the dQ MMA from TMEM.
   const uint32_t tDQ = tmem + 256;
 
   if (warp == 0) {
@@ -93,8 +100,8 @@ __global__ void __launch_bounds__(320, 1)
         tma_load_4d(&tm_do128, &bars[DQ_Q], smem + L::DO + p * L::QPANEL, p * 64, h, q0, b);
       }
       for (int j = 0; j < nk; ++j) {
-        const int s = j & 1;
-        if (j >= 2 && !mbar_wait(&bars[DQ_KVE + s], ((j >> 1) - 1) & 1, abort, &g_fault_word)) {
+        const int s = j % L::NKS;
+        if (j >= L::NKS && !mbar_wait(&bars[DQ_KVE + s], ((j / L::NKS) - 1) & 1, abort, &g_fault_word)) {
           raise_fault(kFaultProducer, abort);
           break;
         }
@@ -115,9 +122,9 @@ __global__ void __launch_bounds__(320, 1)
         volatile int none = 0;
         volatile unsigned gnone = 0;
         mbar_wait(&bars[DQ_Q], 0, &none, &gnone, 100000000ull);
-        for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j) {
-          mbar_wait(&bars[DQ_K + (j & 1)], (j >> 1) & 1, &none, &gnone, 100000000ull);
-          mbar_wait(&bars[DQ_V + (j & 1)], (j >> 1) & 1, &none, &gnone, 100000000ull);
+        for (int j = issued - L::NKS < 0 ? 0 : issued - L::NKS; j < issued; ++j) {
+          mbar_wait(&bars[DQ_K + j % L::NKS], (j / L::NKS) & 1, &none, &gnone, 100000000ull);
+          mbar_wait(&bars[DQ_V + j % L::NKS], (j / L::NKS) & 1, &none, &gnone, 100000000ull);
         }
       }
     }
@@ -128,12 +135,12 @@ __global__ void __launch_bounds__(320, 1)
       const uint32_t q_addr = smem_u32(smem + L::Q), do_addr = smem_u32(smem + L::DO);
       bool ok = mbar_wait(&bars[DQ_Q], 0, abort, &g_fault_word);
       auto issue_sp = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&bars[DQ_K + s], (j >> 1) & 1, abort, &g_fault_word)) return false;
-        if (!mbar_wait(&bars[DQ_V + s], (j >> 1) & 1, abort, &g_fault_word)) return false;
+        const int s = j & 1, sk = j % L::NKS;
+        if (!mbar_wait(&bars[DQ_K + sk], (j / L::NKS) & 1, abort, &g_fault_word)) return false;
+        if (!mbar_wait(&bars[DQ_V + sk], (j / L::NKS) & 1, abort, &g_fault_word)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + L::K + s * L::KTILE);
-        const uint32_t v_addr = smem_u32(smem + L::V + s * L::KTILE);
+        const uint32_t k_addr = smem_u32(smem + L::K + sk * L::KTILE);
+        const uint32_t v_addr = smem_u32(smem + L::V + sk * L::KTILE);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t aoff = (kk / 4) * L::QPANEL + (kk % 4) * 32;
@@ -149,17 +156,19 @@ __global__ void __launch_bounds__(320, 1)
       if (ok) ok = issue_sp(0);
       for (int j = 0; ok && j < nk; ++j) {
         if (j + 1 < nk && !(ok = issue_sp(j + 1))) break;
-        const int s = j & 1;
+        const int s = j & 1, sk = j % L::NKS;
         if (!(ok = mbar_wait(&bars[DQ_DS + s], (j >> 1) & 1, abort, &g_fault_word))) break;
         tc_fence_after();
-        const uint32_t ds_addr = smem_u32(smem + L::DS + s * BM * BNK * 2);
-        const uint32_t k_addr = smem_u32(smem + L::K + s * L::KTILE);
+        const uint32_t k_addr = smem_u32(smem + L::K + sk * L::KTILE);
 #pragma unroll
-        for (int kk = 0; kk < BNK / 16; ++kk)
-          mma_bf16(tDQ, desc_sw128(ds_addr + kk * 32, 16, 1024), desc_sw128(k_addr + kk * 2048, L::KPANEL, 1024),
-                   idDQ, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BNK / 16; ++kk) {
+          // keys 16kk..16kk+15: packed in the half (kk/2) written by warp group kk/2
+          const uint32_t acol = (uint32_t)(128 + s * BNK + (kk >> 1) * 32 + (kk & 1) * 8);
+          mma_bf16_ts(tDQ, tmem + acol, desc_sw128(k_addr + kk * 2048, L::KPANEL, 1024), idDQ,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        }
         mma_commit(&bars[DQ_DQ + s]);
-        mma_commit(&bars[DQ_KVE + s]);
+        mma_commit(&bars[DQ_KVE + sk]);
       }
       if (!ok) raise_fault(kFaultMma, abort);
     }
@@ -178,14 +187,13 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
       const int s = j & 1;
+      // S(j) done implies the dQ MMA of tile j-2 (issued earlier) has
+      // finished reading the dS columns this pass overwrites
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[DQ_SP + s], (j >> 1) & 1, abort, &g_fault_word));
-      if (ok && j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(&bars[DQ_DQ + s], ((j >> 1) - 1) & 1, abort,
-                                                                 &g_fault_word));
       if (!ok) break;
       tc_fence_after();
       const int k0 = kbase + j * BNK;
       const int c_lo = lo - k0, c_hi = t - k0;
-      uint8_t* dsrow = smem + L::DS + s * BM * BNK * 2 + row * 128;
       {
         const int cc = half;  // this warp's 32 of the tile's 64 key columns
         uint32_t rs[32], rp[32];
@@ -205,15 +213,9 @@ __global__ void __launch_bounds__(320, 1)
           }
           pk[i] = pack_bf16(v[0], v[1]);
         }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = cc * 4 + q;
-          const int slot = (chunk & 7) ^ (row & 7);
-          *reinterpret_cast<uint4*>(dsrow + slot * 16) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
-                                                                    pk[4 * q + 3]);
-        }
+        tmem_st16(tmem + lane_off + 128 + s * BNK + cc * 32, pk);
+        tmem_st_wait();
       }
-      fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars[DQ_DS + s]);
     }
@@ -225,7 +227,8 @@ __global__ void __launch_bounds__(320, 1)
       raise_fault(kFaultEpilogue, abort);
     } else {
       tc_fence_after();
-      bf16* dst = dqkv + ((int64_t)b * g.T + (valid ? t : 0)) * 3 * g.d + (int64_t)h * HD;
+      // dQ staged as bf16 128-byte-swizzled 64-column panels in the (now
+      // idle) K ring, stored below by TMA (rows >= T clipped by the map)
 #pragma unroll
       for (int cc = half * (HD / 64); cc < (half + 1) * (HD / 64); ++cc) {
         uint32_t r[32];
@@ -240,13 +243,23 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i)
           pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * g.scale, __uint_as_float(r[2 * i + 1]) * g.scale);
-        if (valid) {
+        uint8_t* prow = smem + L::K + (cc >> 1) * (BM * 128) + row * 128;
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = (cc & 1) * 4 + q;
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) * 16)) =
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
+      fence_async_smem();
+    }
+    // every compute warp reaches this barrier exactly once, faulted or not
+    named_bar_sync(1, 256);
+    if (warp == 2 && lane == 0 && !*abort) {
+#pragma unroll
+      for (int p = 0; p < HD / 64; ++p) tma_store_4d(&tm_st, smem + L::K + p * (BM * 128), p * 64, h, q0, b);
+      tma_store_commit();
+      tma_store_wait_read();
     }
   }
   tc_fence_before();
@@ -264,28 +277,29 @@ __global__ void __launch_bounds__(320, 1)
 template <int HD>
 struct DkvLayout {
   static constexpr int BNQ = 64;                   // queries per inner tile
+  static constexpr int NQS = 4;                    // Q / dO stages
   static constexpr int KPANEL = BM * 128;          // 128-key panel (16 KB)
   static constexpr int QPANEL = BNQ * 128;         // 64-query panel (8 KB)
   static constexpr int KTILE = BM * HD * 2;
   static constexpr int QTILE = BNQ * HD * 2;
   static constexpr int K = 0;
   static constexpr int V = K + KTILE;
-  static constexpr int Q = V + KTILE;              // 2 stages
-  static constexpr int DO = Q + 2 * QTILE;         // 2 stages
-  static constexpr int PT = DO + 2 * QTILE;        // 2 buffers of 128 x 64 bf16
-  static constexpr int DST = PT + 2 * BM * BNQ * 2;
-  static constexpr int VEC = DST + 2 * BM * BNQ * 2;  // per compute warp: {lse2, D}[32]
+  static constexpr int Q = V + KTILE;              // NQS stages
+  static constexpr int DO = Q + NQS * QTILE;       // NQS stages
+  static constexpr int VEC = DO + NQS * QTILE;     // per compute warp: {lse2, D}[32]
   static constexpr int BAR = VEC + 8 * 2 * 32 * 4;
   static constexpr int BYTES = BAR + 256;
 };
 
-enum { KV_KV = 0, KV_QD = 1, KV_QDE = 3, KV_SP = 5, KV_PD = 7, KV_DKV = 9, KV_NB = 11 };
+// barriers: K/V loaded; per Q/dO stage loaded / released; per TMEM buffer
+// S^T,dP^T ready / P^T,dS^T written / dV,dK MMAs done
+enum { KV_KV = 0, KV_QD = 1, KV_QDE = 5, KV_SP = 9, KV_PD = 11, KV_DKV = 13, KV_NB = 15 };
 
 template <int HD>
 __global__ void __launch_bounds__(320, 1)
     local_dkv_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv128, const __grid_constant__ CUtensorMap tm_qkv64,
-                        const __grid_constant__ CUtensorMap tm_do64, Geom g, const float* __restrict__ lse,
-                        const float* __restrict__ delta, bf16* __restrict__ dqkv) {
+                        const __grid_constant__ CUtensorMap tm_do64, const __grid_constant__ CUtensorMap tm_st,
+                        Geom g, const float* __restrict__ lse, const float* __restrict__ delta) {
   using L = DkvLayout<HD>;
   constexpr int BNQ = L::BNQ;
   extern __shared__ uint8_t smem_raw[];
@@ -295,17 +309,21 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int k0 = blockIdx.x * BM;
+  // heads fastest: CTAs that run together cover whole token rows of qkv
+  const int h = blockIdx.x, b = blockIdx.z;
+  const int k0 = blockIdx.y * BM;
   const int tfirst = k0 + 1;
   const int tlast = min(g.T - 1, k0 + BM - 1 + g.W);
   const int nq = tlast >= tfirst ? (tlast - tfirst + BNQ) / BNQ : 0;
 
+  if (threadIdx.x == 0) LLATTN_TRACE_AT(0);
   if (threadIdx.x == 0) {
     mbar_init(&bars[KV_KV], 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < L::NQS; ++s) {
       mbar_init(&bars[KV_QD + s], 1);
       mbar_init(&bars[KV_QDE + s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&bars[KV_SP + s], 1);
       mbar_init(&bars[KV_PD + s], 2 * BM);
       mbar_init(&bars[KV_DKV + s], 1);
@@ -322,7 +340,10 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // S^T at [0,64) / [64,128), dP^T at [128,192) / [192,256), dV, dK after
+  if (threadIdx.x == 0) LLATTN_TRACE_AT(1);
+  // S^T at [0,64) / [64,128), dP^T at [128,192) / [192,256), dV, dK after.
+  // P^T and dS^T (bf16) are written back over the first 16 of each 32
+  // S^T / dP^T columns that produced them and feed the dV / dK MMAs from TMEM.
   const uint32_t tDV = tmem + 256, tDK = tmem + 256 + HD;
 
   if (warp == 0) {
@@ -338,8 +359,8 @@ __global__ void __launch_bounds__(320, 1)
         tma_load_4d(&tm_qkv128, &bars[KV_KV], smem + L::V + p * L::KPANEL, p * 64, 2 * g.H + h, k0, b);
       }
       for (int i = 0; i < nq; ++i) {
-        const int s = i & 1;
-        if (i >= 2 && !mbar_wait(&bars[KV_QDE + s], ((i >> 1) - 1) & 1, abort, &g_fault_word)) {
+        const int s = i % L::NQS;
+        if (i >= L::NQS && !mbar_wait(&bars[KV_QDE + s], ((i / L::NQS) - 1) & 1, abort, &g_fault_word)) {
           raise_fault(kFaultProducer, abort);
           break;
         }
@@ -356,8 +377,8 @@ __global__ void __launch_bounds__(320, 1)
         volatile int none = 0;
         volatile unsigned gnone = 0;
         mbar_wait(&bars[KV_KV], 0, &none, &gnone, 100000000ull);
-        for (int i = issued - 2 < 0 ? 0 : issued - 2; i < issued; ++i)
-          mbar_wait(&bars[KV_QD + (i & 1)], (i >> 1) & 1, &none, &gnone, 100000000ull);
+        for (int i = issued - L::NQS < 0 ? 0 : issued - L::NQS; i < issued; ++i)
+          mbar_wait(&bars[KV_QD + i % L::NQS], (i / L::NQS) & 1, &none, &gnone, 100000000ull);
       }
     }
   } else if (warp == 1) {
@@ -366,12 +387,14 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t idKV = idesc_bf16_f32(BM, HD, false, true);    // P^T dO, dS^T Q
       const uint32_t k_addr = smem_u32(smem + L::K), v_addr = smem_u32(smem + L::V);
       bool ok = mbar_wait(&bars[KV_KV], 0, abort, &g_fault_word);
+      LLATTN_TRACE_AT(2);
       auto issue_sp = [&](int i) -> bool {
-        const int s = i & 1;
-        if (!mbar_wait(&bars[KV_QD + s], (i >> 1) & 1, abort, &g_fault_word)) return false;
+        const int s = i & 1, sq = i % L::NQS;
+        if (!mbar_wait(&bars[KV_QD + sq], (i / L::NQS) & 1, abort, &g_fault_word)) return false;
+        if (i < 12) LLATTN_TRACE_AT(24 + i);
         tc_fence_after();
-        const uint32_t q_addr = smem_u32(smem + L::Q + s * L::QTILE);
-        const uint32_t do_addr = smem_u32(smem + L::DO + s * L::QTILE);
+        const uint32_t q_addr = smem_u32(smem + L::Q + sq * L::QTILE);
+        const uint32_t do_addr = smem_u32(smem + L::DO + sq * L::QTILE);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t aoff = (kk / 4) * L::KPANEL + (kk % 4) * 32;
@@ -387,23 +410,22 @@ __global__ void __launch_bounds__(320, 1)
       if (ok) ok = issue_sp(0);
       for (int i = 0; ok && i < nq; ++i) {
         if (i + 1 < nq && !(ok = issue_sp(i + 1))) break;
-        const int s = i & 1;
+        const int s = i & 1, sq = i % L::NQS;
         if (!(ok = mbar_wait(&bars[KV_PD + s], (i >> 1) & 1, abort, &g_fault_word))) break;
+        if (i < 12) LLATTN_TRACE_AT(36 + i);
         tc_fence_after();
-        const uint32_t pt_addr = smem_u32(smem + L::PT + s * BM * BNQ * 2);
-        const uint32_t dst_addr = smem_u32(smem + L::DST + s * BM * BNQ * 2);
-        const uint32_t q_addr = smem_u32(smem + L::Q + s * L::QTILE);
-        const uint32_t do_addr = smem_u32(smem + L::DO + s * L::QTILE);
+        const uint32_t q_addr = smem_u32(smem + L::Q + sq * L::QTILE);
+        const uint32_t do_addr = smem_u32(smem + L::DO + sq * L::QTILE);
 #pragma unroll
         for (int kk = 0; kk < BNQ / 16; ++kk) {
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          mma_bf16(tDV, desc_sw128(pt_addr + kk * 32, 16, 1024), desc_sw128(do_addr + kk * 2048, L::QPANEL, 1024),
-                   idKV, acc);
-          mma_bf16(tDK, desc_sw128(dst_addr + kk * 32, 16, 1024), desc_sw128(q_addr + kk * 2048, L::QPANEL, 1024),
-                   idKV, acc);
+          // queries 16kk..16kk+15: packed in the half (kk/2) written by warp group kk/2
+          const uint32_t acol = (uint32_t)(s * BNQ + (kk >> 1) * 32 + (kk & 1) * 8);
+          mma_bf16_ts(tDV, tmem + acol, desc_sw128(do_addr + kk * 2048, L::QPANEL, 1024), idKV, acc);
+          mma_bf16_ts(tDK, tmem + 128 + acol, desc_sw128(q_addr + kk * 2048, L::QPANEL, 1024), idKV, acc);
         }
         mma_commit(&bars[KV_DKV + s]);
-        mma_commit(&bars[KV_QDE + s]);
+        mma_commit(&bars[KV_QDE + sq]);
       }
       if (!ok) raise_fault(kFaultMma, abort);
     }
@@ -441,13 +463,12 @@ __global__ void __launch_bounds__(320, 1)
       v_d[lane] = nd;
       __syncwarp();
       fetch(i + 1, nl2, nd);
+      // S^T(i) done implies the dV/dK MMAs of tile i-2 (issued earlier) have
+      // finished reading the P^T / dS^T columns this pass overwrites
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_SP + s], (i >> 1) & 1, abort, &g_fault_word));
-      if (ok && i >= 2) ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_DKV + s], ((i >> 1) - 1) & 1, abort,
-                                                                 &g_fault_word));
       if (!ok) break;
+      if (row == 0 && half == 0 && i < 12) LLATTN_TRACE_AT(4 + i);
       tc_fence_after();
-      uint8_t* ptrow = smem + L::PT + s * BM * BNQ * 2 + row * 128;
-      uint8_t* dsrow = smem + L::DST + s * BM * BNQ * 2 + row * 128;
       const int c_lo = j + 1 - t0 - half * 32, c_hi = valid ? t_hi - t0 - half * 32 + 1 : -1;  // in [0, 32)
       {
         const int cc = half;
@@ -455,6 +476,7 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld32(tmem + lane_off + s * BNQ + cc * 32, rs);
         tmem_ld32(tmem + lane_off + 128 + s * BNQ + cc * 32, rp);
         tmem_ld_wait();
+        if (row == 0 && half == 0 && i < 6) LLATTN_TRACE_AT(44 + i);
         uint32_t pp[16], pd[16];
 #pragma unroll
         for (int i2 = 0; i2 < 16; ++i2) {
@@ -471,19 +493,14 @@ __global__ void __launch_bounds__(320, 1)
           pp[i2] = pack_bf16(pv[0], pv[1]);
           pd[i2] = pack_bf16(dv[0], dv[1]);
         }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = cc * 4 + q;
-          const int slot = (chunk & 7) ^ (row & 7);
-          *reinterpret_cast<uint4*>(ptrow + slot * 16) = make_uint4(pp[4 * q], pp[4 * q + 1], pp[4 * q + 2],
-                                                                    pp[4 * q + 3]);
-          *reinterpret_cast<uint4*>(dsrow + slot * 16) = make_uint4(pd[4 * q], pd[4 * q + 1], pd[4 * q + 2],
-                                                                    pd[4 * q + 3]);
-        }
+        tmem_st16(tmem + lane_off + s * BNQ + cc * 32, pp);
+        tmem_st16(tmem + lane_off + 128 + s * BNQ + cc * 32, pd);
+        tmem_st_wait();
       }
-      fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars[KV_PD + s]);
+      if (row == 0 && half == 0 && i < 12) LLATTN_TRACE_AT(16 + i);
+      if (warp == 9 && lane == 31 && i < 6) LLATTN_TRACE_AT(54 + i);
     }
     if (!ok) raise_fault(kFaultSoftmax, abort);
     if (ok && nq > 0)
@@ -493,38 +510,51 @@ __global__ void __launch_bounds__(320, 1)
       raise_fault(kFaultEpilogue, abort);
     } else {
       tc_fence_after();
-      bf16* dst = dqkv + ((int64_t)b * g.T + (valid ? j : 0)) * 3 * g.d + (int64_t)h * HD;
-      {
-        const int which = half;  // half 0 writes dk (slot 1), half 1 dv (slot 2)
-        const uint32_t tsrc = (which == 0 ? tDK : tDV) + lane_off;
-        const float mul = which == 0 ? g.scale : 1.f;
-        bf16* out = dst + (1 + which) * g.d;
+      if (row == 0 && half == 0) LLATTN_TRACE_AT(52);
+      // half 0 stages dK, half 1 dV: bf16, 128-byte-swizzled 64-column panels
+      // in the (now idle) Q/dO ring, stored below by TMA (rows >= T clipped)
+      uint8_t* stage = smem + L::Q + half * (BM * HD * 2);
+      const uint32_t tsrc = (half == 0 ? tDK : tDV) + lane_off;
+      const float mul = half == 0 ? g.scale : 1.f;
 #pragma unroll
-        for (int cc = 0; cc < HD / 32; ++cc) {
-          uint32_t r[32];
-          if (nq > 0) {
-            tmem_ld32(tsrc + cc * 32, r);
-            tmem_ld_wait();
-          } else {
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        uint32_t r[32];
+        if (nq > 0) {
+          tmem_ld32(tsrc + cc * 32, r);
+          tmem_ld_wait();
+        } else {
 #pragma unroll
-            for (int i2 = 0; i2 < 32; ++i2) r[i2] = 0u;
-          }
-          uint32_t pk[16];
+          for (int i2 = 0; i2 < 32; ++i2) r[i2] = 0u;
+        }
+        uint32_t pk[16];
 #pragma unroll
-          for (int i2 = 0; i2 < 16; ++i2)
-            pk[i2] = pack_bf16(__uint_as_float(r[2 * i2]) * mul, __uint_as_float(r[2 * i2 + 1]) * mul);
-          if (valid) {
+        for (int i2 = 0; i2 < 16; ++i2)
+          pk[i2] = pack_bf16(__uint_as_float(r[2 * i2]) * mul, __uint_as_float(r[2 * i2 + 1]) * mul);
+        uint8_t* prow = stage + (cc >> 1) * (BM * 128) + row * 128;
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              *reinterpret_cast<uint4*>(out + cc * 32 + q * 8) =
-                  make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          }
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = (cc & 1) * 4 + q;
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) * 16)) =
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
+      fence_async_smem();
+    }
+    // every compute warp reaches this barrier exactly once, faulted or not
+    named_bar_sync(1, 256);
+    if (warp == 2 && lane == 0 && !*abort) {
+#pragma unroll
+      for (int w = 0; w < 2; ++w)
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p)
+          tma_store_4d(&tm_st, smem + L::Q + w * (BM * HD * 2) + p * (BM * 128), p * 64, (1 + w) * g.H + h, k0, b);
+      tma_store_commit();
+      tma_store_wait_read();
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) LLATTN_TRACE_AT(60);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();

@@ -84,8 +84,9 @@ __global__ void __launch_bounds__(320, 1)
     return;
   }
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int q0 = blockIdx.x * 2 * BM;
+  // heads fastest: CTAs that run together cover whole token rows of qkv
+  const int h = blockIdx.x, b = blockIdx.z;
+  const int q0 = blockIdx.y * 2 * BM;
   if (threadIdx.x == 0) LLATTN_TRACE_AT(0);
   const bool fuse = ep.lat != nullptr;
   const bool has_b = q0 + BM < g.T;
