@@ -34,8 +34,9 @@ def flags() -> list[str]:
          "-I" + INCLUDE, "-I" + CSRC]
     if os.environ.get("LLATTN_CHECK_BOUNDS") == "1":
         f.append("-DLLATTN_CHECK_BOUNDS=1")
-    if os.environ.get("LLATTN_TRACE") == "1":
-        f.append("-DLLATTN_TRACE=1")
+    if os.environ.get("LLATTN_TRACE", "0") not in ("", "0"):
+        # diagnostic builds: 1 = forward, 2 = dK/dV, 3 = gate backward phase timestamps
+        f.append("-DLLATTN_TRACE=" + os.environ["LLATTN_TRACE"])
     if os.environ.get("LLATTN_PTXAS_V") == "1":
         f += ["-Xptxas", "-v"]
     return f

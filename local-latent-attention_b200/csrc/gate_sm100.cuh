@@ -14,19 +14,22 @@
 // TMA (MN-major A operand), lat tiles written by threads (MN-major B), the
 // column sums for db taken from the same shared-memory tiles.
 
+constexpr int kGateMaxHeads = 32;  // per-head gate grads kept in shared memory
+
 template <int HD>
 struct GbLayout {
   static constexpr int TILE = BM * HD * 2;         // 128 rows x HD bf16 (HD/64 panels of 16 KB)
   static constexpr int LAT = 0;                    // 128 x 64 bf16
   static constexpr int W = LAT + BM * 128;         // per group: HD x 64 bf16
-  static constexpr int LT = W + 2 * HD * 128;      // per group: local_out tile of the head
+  static constexpr int LT = W + 2 * HD * 128;      // per group: local_out tile of the head, overwritten by dL
   static constexpr int DM = LT + 2 * TILE;         // per group: dmixed tile, overwritten by dR
-  static constexpr int RED = DM + 2 * TILE;        // 8 warps x 2 x HD floats
-  static constexpr int BAR = RED + 8 * 2 * HD * 4;
+  static constexpr int RED = DM + 2 * TILE;        // 8 warps x HD floats (dg_local partials)
+  static constexpr int DSH = RED + 8 * HD * 4;     // [kGateMaxHeads][128] gate grad ds per head and row
+  static constexpr int BAR = DSH + kGateMaxHeads * BM * 4;
   static constexpr int BYTES = BAR + 256;
 };
 
-// per group g (0/1): W ready, R computed, dR tile ready, dlat MMA done,
+// per group g (0/1): W ready, R computed, dL/dR tiles ready, dlat MMA done,
 // L/dmixed tiles loaded
 enum { GB_W = 0, GB_R = 2, GB_DR = 4, GB_DL = 6, GB_F = 8, GB_NB = 10 };
 
@@ -45,16 +48,21 @@ __device__ __forceinline__ float butterfly32(float (&v)[32], int lane) {
   return v[0];
 }
 
-// Warps: 0 idle, 1 = TMEM + MMA issuer, 2-5 = group 0 (even heads),
-// 6-9 = group 1 (odd heads); in a group thread = token row = TMEM lane.
+// Warps: 0 = TMA producer (tiles in, dL/dR tiles out), 1 = TMEM + MMA issuer,
+// 2-5 = group 0 (even heads), 6-9 = group 1 (odd heads); in a group thread =
+// token row = TMEM lane.
+//
+// dg_remote needs no per-head reduction over R: with R_h = lat W_h^T + b_h,
+//   dg_r = -sum_{t,h} ds R_h = -sum_h (S1_h W_h^T + S0_h b_h),
+//   S1_h = sum_t ds[t,h] lat[t], S0_h = sum_t ds[t,h],
+// formed from ds kept in shared memory after the head loop.
 template <int HD>
 __global__ void __launch_bounds__(320, 1)
     gate_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_dm,
-                       Geom g, const bf16* __restrict__ local_out, const bf16* __restrict__ lat,
-                       const bf16* __restrict__ w_rout, const float* __restrict__ b_rout,
-                       const float* __restrict__ gl, const float* __restrict__ gr, const bf16* __restrict__ dmixed,
-                       bf16* __restrict__ dl, float* __restrict__ delta, bf16* __restrict__ dr,
-                       float* __restrict__ dlat_tok, float* __restrict__ dg_part) {
+                       const __grid_constant__ CUtensorMap tm_dl, const __grid_constant__ CUtensorMap tm_dr,
+                       Geom g, const bf16* __restrict__ lat, const bf16* __restrict__ w_rout,
+                       const float* __restrict__ b_rout, const float* __restrict__ gl, const float* __restrict__ gr,
+                       float* __restrict__ delta, float* __restrict__ dlat_tok, float* __restrict__ dg_part) {
   using L = GbLayout<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -64,7 +72,9 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int b = blockIdx.y, t0 = blockIdx.x * BM;
   const int H = g.H;
+  float* dsh = reinterpret_cast<float*>(smem + L::DSH);
 
+  if (threadIdx.x == 0) LLATTN_TRACE_K(3, 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars[GB_W + s], BM);
@@ -89,21 +99,36 @@ __global__ void __launch_bounds__(320, 1)
   float* red = reinterpret_cast<float*>(smem + L::RED);
 
   if (warp == 0) {
-    // TMA producer: local_out and dmixed tiles of head h into group h&1's
-    // buffers, once that group's previous head has been fully consumed
-    // (its dlat MMA, which reads the dR tile in the dmixed buffer, is done)
+    // TMA producer. Head h uses group h&1's buffers; before loading head h
+    // the producer stores head h-2's dL / dR tiles (written in place over the
+    // local_out / dmixed tiles; 3-D (d, T, B) maps clip rows past T), waits
+    // for its dlat MMA (reads dR) and for the stores to have read shared memory.
     if (lane == 0) {
       prefetch_tmap(&tm_lo);
       prefetch_tmap(&tm_dm);
+      const int row0 = b * g.T + t0;
       int issued = 0;
+      bool ok = true;
+      auto store_head = [&](int h) -> bool {
+        const int grp = h & 1, n = h >> 1;
+        if (!mbar_wait(&bars[GB_DR + grp], n & 1, abort, &g_fault_word)) return false;
+#pragma unroll
+        for (int p = 0; p < HD / 64; ++p) {
+          tma_store_3d(&tm_dl, smem + L::LT + grp * L::TILE + p * (BM * 128), h * HD + p * 64, t0, b);
+          tma_store_3d(&tm_dr, smem + L::DM + grp * L::TILE + p * (BM * 128), h * HD + p * 64, t0, b);
+        }
+        tma_store_commit();
+        return true;
+      };
       for (int h = 0; h < H; ++h) {
         const int grp = h & 1, n = h >> 1;
-        if (n >= 1 && !mbar_wait(&bars[GB_DL + grp], (n - 1) & 1, abort, &g_fault_word)) {
-          raise_fault(kFaultProducer, abort);
-          break;
+        if (n >= 1) {
+          if (!(ok = store_head(h - 2))) break;
+          if (!(ok = mbar_wait(&bars[GB_DL + grp], (n - 1) & 1, abort, &g_fault_word))) break;
+          tma_store_wait_read();
         }
+        if (h < 12) LLATTN_TRACE_K(3, 2 + h);
         mbar_expect_tx(&bars[GB_F + grp], 2 * L::TILE);
-        const int row0 = b * g.T + t0;
 #pragma unroll
         for (int p = 0; p < HD / 64; ++p) {
           tma_load_2d(&tm_lo, &bars[GB_F + grp], smem + L::LT + grp * L::TILE + p * (BM * 128), h * HD + p * 64, row0);
@@ -111,7 +136,10 @@ __global__ void __launch_bounds__(320, 1)
         }
         issued = h + 1;
       }
-      if (*abort) {
+      for (int h = H - 2 < 0 ? 0 : H - 2; ok && h < H; ++h) ok = store_head(h);
+      tma_store_wait_read();
+      if (!ok) {
+        raise_fault(kFaultProducer, abort);
         volatile int none = 0;
         volatile unsigned gnone = 0;
         for (int h = issued - 2 < 0 ? 0 : issued - 2; h < issued; ++h)
@@ -177,8 +205,8 @@ __global__ void __launch_bounds__(320, 1)
       fence_async_smem();
       mbar_arrive(&bars[GB_W + grp]);
     };
-    float* wred = red + (warp - 2) * 2 * HD;  // lane owns columns cc*32+lane
-    for (int e = lane; e < 2 * HD; e += 32) wred[e] = 0.f;
+    float* wred = red + (warp - 2) * HD;  // lane owns columns cc*32+lane
+    for (int e = lane; e < HD; e += 32) wred[e] = 0.f;
     bool ok = true;
     if (grp < H) write_w(grp);
     // tile rows: 16-byte chunk c of this row sits at panel c/8, slot (c%8)^(row%8)
@@ -192,6 +220,7 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_R + grp], n & 1, abort, &g_fault_word));
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_F + grp], n & 1, abort, &g_fault_word));
       if (!ok) break;
+      if (row == 0 && h < 12) LLATTN_TRACE_K(3, 14 + h);
       tc_fence_after();
       const uint32_t tR = tmem + grp * HD + lane_off;
       uint8_t* lt = smem + L::LT + grp * L::TILE;
@@ -226,26 +255,26 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       }
+      if (row == 0 && h < 12) LLATTN_TRACE_K(3, 26 + h);
       const float x = sl + g.gate_bias - sr;
       const float w = 1.f / (1.f + expf(-x));
       const float wr = 1.f / (1.f + expf(x));
       const float ds = valid ? dw * w * wr : 0.f;
-      // pass 2: dL, D, dR (written over dmixed in the tile: same thread, same
-      // bytes, after reading them), dg
+      dsh[h * BM + row] = ds;
+      // pass 2: dL over local_out and dR over dmixed in the tiles (same
+      // thread, same bytes, after reading them), D = dL.L, dg_local partial
       float dsum = 0.f;
-      const int64_t gofs = tok * g.d + (int64_t)h * HD;
 #pragma unroll 1
       for (int cc = 0; cc < HD / 32; ++cc) {
-        uint32_t rr[32];
-        tmem_ld32(tR + cc * 32, rr);
-        tmem_ld_wait();
         float al[32];
-        uint32_t pdl[16], pdr[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           float lv[8], mv[8];
-          unpack8(*chunk_ptr(lt, cc * 4 + q), lv);
-          unpack8(*chunk_ptr(dmt, cc * 4 + q), mv);
+          uint4* lp = chunk_ptr(lt, cc * 4 + q);
+          uint4* mp = chunk_ptr(dmt, cc * 4 + q);
+          unpack8(*lp, lv);
+          unpack8(*mp, mv);
+          uint32_t pdl[4], pdr[4];
 #pragma unroll
           for (int i4 = 0; i4 < 2; ++i4) {
             const int c4 = (cc * 32 + q * 8) / 4 + i4;
@@ -258,48 +287,30 @@ __global__ void __launch_bounds__(320, 1)
               for (int u = 0; u < 2; ++u) {
                 const int i = i4 * 4 + k + u;
                 const float a = __bfloat162float(__float2bfloat16_rn(w * mv[i] + ds * gav[k + u]));
-                dlv[u] = a;
+                dlv[u] = valid ? a : 0.f;
                 dsum = fmaf(a, lv[i], dsum);
                 drv[u] = valid ? wr * mv[i] - ds * gbv[k + u] : 0.f;
                 al[q * 8 + i] = ds * lv[i];
               }
-              pdl[(q * 8 + i4 * 4 + k) / 2] = pack_bf16(dlv[0], dlv[1]);
-              pdr[(q * 8 + i4 * 4 + k) / 2] = pack_bf16(drv[0], drv[1]);
+              pdl[(i4 * 4 + k) / 2] = pack_bf16(dlv[0], dlv[1]);
+              pdr[(i4 * 4 + k) / 2] = pack_bf16(drv[0], drv[1]);
             }
           }
-          *chunk_ptr(dmt, cc * 4 + q) = make_uint4(pdr[4 * q], pdr[4 * q + 1], pdr[4 * q + 2], pdr[4 * q + 3]);
-        }
-        if (valid) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            reinterpret_cast<uint4*>(dl + gofs + cc * 32)[q] =
-                make_uint4(pdl[4 * q], pdl[4 * q + 1], pdl[4 * q + 2], pdl[4 * q + 3]);
-            reinterpret_cast<uint4*>(dr + gofs + cc * 32)[q] =
-                make_uint4(pdr[4 * q], pdr[4 * q + 1], pdr[4 * q + 2], pdr[4 * q + 3]);
-          }
+          *lp = make_uint4(pdl[0], pdl[1], pdl[2], pdl[3]);
+          *mp = make_uint4(pdr[0], pdr[1], pdr[2], pdr[3]);
         }
         wred[cc * 32 + lane] += butterfly32(al, lane);
-        {
-          float ar[32];
-#pragma unroll
-          for (int i4 = 0; i4 < 8; ++i4) {
-            const float4 bb = __ldg(bh4 + cc * 8 + i4);
-            ar[4 * i4] = -ds * (__uint_as_float(rr[4 * i4]) + bb.x);
-            ar[4 * i4 + 1] = -ds * (__uint_as_float(rr[4 * i4 + 1]) + bb.y);
-            ar[4 * i4 + 2] = -ds * (__uint_as_float(rr[4 * i4 + 2]) + bb.z);
-            ar[4 * i4 + 3] = -ds * (__uint_as_float(rr[4 * i4 + 3]) + bb.w);
-          }
-          wred[HD + cc * 32 + lane] += butterfly32(ar, lane);
-        }
       }
       if (valid) delta[((int64_t)b * H + h) * g.T + t] = dsum;
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars[GB_DR + grp]);
+      if (row == 0 && h < 12) LLATTN_TRACE_K(3, 38 + h);
       // W buffer reuse: the dlat MMA of head h must have read it
       if (h + 2 < H) {
         ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_DL + grp], n & 1, abort, &g_fault_word));
         if (!ok) break;
+        if (row == 0 && h < 10) LLATTN_TRACE_K(3, 50 + h);
         write_w(h + 2);
       }
     }
@@ -329,12 +340,53 @@ __global__ void __launch_bounds__(320, 1)
   }
   tc_fence_before();
   __syncthreads();
-  // partial [cta][2*HD] (dg_l half, dg_r half) summed over the compute warps
-  for (int e = threadIdx.x; e < 2 * HD; e += blockDim.x) {
+  if (threadIdx.x == 0) LLATTN_TRACE_K(3, 60);
+  const int64_t part = ((int64_t)b * gridDim.x + blockIdx.x) * 2 * HD;
+  // dg_local partial [cta][0, HD): summed over the compute warps
+  for (int e = threadIdx.x; e < HD; e += blockDim.x) {
     float v = 0.f;
 #pragma unroll
-    for (int w8 = 0; w8 < 8; ++w8) v += red[w8 * 2 * HD + e];
-    dg_part[((int64_t)b * gridDim.x + blockIdx.x) * 2 * HD + e] = v;
+    for (int w8 = 0; w8 < 8; ++w8) v += red[w8 * HD + e];
+    dg_part[part + e] = v;
+  }
+  // dg_remote partial [cta][HD, 2HD): S1_h[e] = sum_rows ds lat[row, e] and
+  // S0_h into the (now idle) local_out tile buffer, then -sum_h S1_h W_h^T + S0_h b_h
+  float* s1 = reinterpret_cast<float*>(smem + L::LT);  // [H][64], then S0 at [H*64 + h]
+  const bool all_ok = !*abort;
+  for (int idx = threadIdx.x; idx < H * 65; idx += blockDim.x) {
+    const int h = idx / 65, e = idx % 65;
+    float v = 0.f;
+    if (all_ok) {
+      if (e < 64) {
+        const int c = e >> 3, k = e & 7;
+#pragma unroll 4
+        for (int r = 0; r < BM; ++r) {
+          const bf16* lrow = reinterpret_cast<const bf16*>(smem + L::LAT + r * 128 + ((c ^ (r & 7)) * 16));
+          v = fmaf(dsh[h * BM + r], __bfloat162float(lrow[k]), v);
+        }
+      } else {
+#pragma unroll 4
+        for (int r = 0; r < BM; ++r) v += dsh[h * BM + r];
+      }
+    }
+    s1[h * 65 + e] = v;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < HD; c += blockDim.x) {
+    float v = 0.f;
+    for (int h = 0; h < H; ++h) {
+      const uint4* wrow = reinterpret_cast<const uint4*>(w_rout + ((int64_t)h * HD + c) * 64);
+      const float* sh = s1 + h * 65;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float wv[8];
+        unpack8(__ldg(wrow + q), wv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v = fmaf(sh[q * 8 + k], wv[k], v);
+      }
+      v = fmaf(sh[64], __ldg(b_rout + (int64_t)h * HD + c), v);
+    }
+    dg_part[part + HD + c] = -v;
   }
   if (warp == 1) {
     __syncwarp();

@@ -34,14 +34,17 @@ __device__ unsigned int g_fault_word = 0;
 // diagnostic builds only: per-CTA phase timestamps (globaltimer, ns)
 constexpr int kTraceCtas = 1024, kTraceEv = 64;
 __device__ unsigned long long g_trace[kTraceCtas][kTraceEv];
-#define LLATTN_TRACE_AT(ev)                                                                      \
+// LLATTN_TRACE selects which kernel records (1 forward, 2 dK/dV, 3 gate backward)
+#define LLATTN_TRACE_K(kid, ev)                                                                 \
   do {                                                                                          \
-    const int cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);           \
-    if (cta_ < kTraceCtas && (ev) < kTraceEv) g_trace[cta_][(ev)] = ptx::globaltimer_ns();   \
+    if (LLATTN_TRACE == (kid)) {                                                                \
+      const int cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);         \
+      if (cta_ < kTraceCtas && (ev) < kTraceEv) g_trace[cta_][(ev)] = ptx::globaltimer_ns(); \
+    }                                                                                           \
   } while (0)
 #else
-#define LLATTN_TRACE_AT(ev) \
-  do {                      \
+#define LLATTN_TRACE_K(kid, ev) \
+  do {                          \
   } while (0)
 #endif
 
@@ -185,18 +188,18 @@ cudaError_t dkv_hd(const Geom& g, const void* qkv, const void* dl, const float* 
 
 template <int HD>
 cudaError_t gate_bwd_hd(const Geom& g, const GateBwd& a, cudaStream_t s) {
-  CUtensorMap tlo, tdm;
+  CUtensorMap tlo, tdm, tdl, tdr;
   if (!make_2d_map(&tlo, a.local_out, (int64_t)g.B * g.T, g.d, 128) ||
-      !make_2d_map(&tdm, a.dmixed, (int64_t)g.B * g.T, g.d, 128))
+      !make_2d_map(&tdm, a.dmixed, (int64_t)g.B * g.T, g.d, 128) || !make_btd_map(&tdl, a.dl, g.B, g.T, g.d) ||
+      !make_btd_map(&tdr, a.dr, g.B, g.T, g.d))
     return cudaErrorInvalidValue;
   const int smem = std::max(GbLayout<HD>::BYTES + 1024, 116 * 1024);
   cudaError_t e = cudaFuncSetAttribute(gate_bwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.T, BM), g.B);
-  gate_bwd_tc_kernel<HD><<<grid, 320, smem, s>>>(
-      tlo, tdm, g, static_cast<const bf16*>(a.local_out), static_cast<const bf16*>(a.lat), static_cast<const bf16*>(a.w_rout),
-      a.b_rout, a.g_local, a.g_remote, static_cast<const bf16*>(a.dmixed), static_cast<bf16*>(a.dl), a.delta,
-      static_cast<bf16*>(a.dr), a.dlat_tok, a.dg_part);
+  gate_bwd_tc_kernel<HD><<<grid, 320, smem, s>>>(tlo, tdm, tdl, tdr, g, static_cast<const bf16*>(a.lat),
+                                                 static_cast<const bf16*>(a.w_rout), a.b_rout, a.g_local, a.g_remote,
+                                                 a.delta, a.dlat_tok, a.dg_part);
   return cudaGetLastError();
 }
 
@@ -233,7 +236,7 @@ bool fwd_supported(const Geom& g, int elt_bytes) {
 
 bool bwd_supported(const Geom& g, int elt_bytes) { return fwd_supported(g, elt_bytes); }
 
-bool gate_fusable(const Geom& g) { return g.Ld == 64; }
+bool gate_fusable(const Geom& g) { return g.Ld == 64 && g.H <= kGateMaxHeads; }
 
 cudaError_t launch_local_fwd(const Geom& g, const void* qkv, void* local_out, float* lse, const GateEpilogue& ep,
                              cudaStream_t s) {

@@ -201,17 +201,24 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld32(tmem + lane_off + 128 + s * BNK + cc * 32, rp);
         tmem_ld_wait();
         uint32_t pk[16];
+        // interior tiles (all 32 keys visible from every query of the warp) skip the mask
+        const bool full = __all_sync(0xffffffffu, c_lo <= cc * 32 && c_hi >= cc * 32 + 32);
+        const uint64_t sc2 = f2_pack(sc, sc), nl2 = f2_pack(-lse2, -lse2), dt2 = f2_pack(dt, dt);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float v[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int c = cc * 32 + 2 * i + u;
-            const float e = fast_exp2(fmaf(__uint_as_float(rs[2 * i + u]), sc, -lse2));
-            const float p = (c >= c_lo && c < c_hi) ? e : 0.f;
-            v[u] = p * (__uint_as_float(rp[2 * i + u]) - dt);
+          const int c = cc * 32 + 2 * i;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(rs[2 * i]), __uint_as_float(rs[2 * i + 1])), sc2, nl2), x0, x1);
+          float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+          if (!full) {
+            p0 = (c >= c_lo && c < c_hi) ? p0 : 0.f;
+            p1 = (c + 1 >= c_lo && c + 1 < c_hi) ? p1 : 0.f;
           }
-          pk[i] = pack_bf16(v[0], v[1]);
+          float d0, d1;
+          f2_unpack(f2_mul(f2_pack(p0, p1),
+                           f2_sub(f2_pack(__uint_as_float(rp[2 * i]), __uint_as_float(rp[2 * i + 1])), dt2)),
+                    d0, d1);
+          pk[i] = pack_bf16(d0, d1);
         }
         tmem_st16(tmem + lane_off + 128 + s * BNK + cc * 32, pk);
         tmem_st_wait();
@@ -316,7 +323,7 @@ __global__ void __launch_bounds__(320, 1)
   const int tlast = min(g.T - 1, k0 + BM - 1 + g.W);
   const int nq = tlast >= tfirst ? (tlast - tfirst + BNQ) / BNQ : 0;
 
-  if (threadIdx.x == 0) LLATTN_TRACE_AT(0);
+  if (threadIdx.x == 0) LLATTN_TRACE_K(2, 0);
   if (threadIdx.x == 0) {
     mbar_init(&bars[KV_KV], 1);
     for (int s = 0; s < L::NQS; ++s) {
@@ -340,7 +347,7 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0) LLATTN_TRACE_AT(1);
+  if (threadIdx.x == 0) LLATTN_TRACE_K(2, 1);
   // S^T at [0,64) / [64,128), dP^T at [128,192) / [192,256), dV, dK after.
   // P^T and dS^T (bf16) are written back over the first 16 of each 32
   // S^T / dP^T columns that produced them and feed the dV / dK MMAs from TMEM.
@@ -387,11 +394,11 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t idKV = idesc_bf16_f32(BM, HD, false, true);    // P^T dO, dS^T Q
       const uint32_t k_addr = smem_u32(smem + L::K), v_addr = smem_u32(smem + L::V);
       bool ok = mbar_wait(&bars[KV_KV], 0, abort, &g_fault_word);
-      LLATTN_TRACE_AT(2);
+      LLATTN_TRACE_K(2, 2);
       auto issue_sp = [&](int i) -> bool {
         const int s = i & 1, sq = i % L::NQS;
         if (!mbar_wait(&bars[KV_QD + sq], (i / L::NQS) & 1, abort, &g_fault_word)) return false;
-        if (i < 12) LLATTN_TRACE_AT(24 + i);
+        if (i < 12) LLATTN_TRACE_K(2, 24 + i);
         tc_fence_after();
         const uint32_t q_addr = smem_u32(smem + L::Q + sq * L::QTILE);
         const uint32_t do_addr = smem_u32(smem + L::DO + sq * L::QTILE);
@@ -412,7 +419,7 @@ __global__ void __launch_bounds__(320, 1)
         if (i + 1 < nq && !(ok = issue_sp(i + 1))) break;
         const int s = i & 1, sq = i % L::NQS;
         if (!(ok = mbar_wait(&bars[KV_PD + s], (i >> 1) & 1, abort, &g_fault_word))) break;
-        if (i < 12) LLATTN_TRACE_AT(36 + i);
+        if (i < 12) LLATTN_TRACE_K(2, 36 + i);
         tc_fence_after();
         const uint32_t q_addr = smem_u32(smem + L::Q + sq * L::QTILE);
         const uint32_t do_addr = smem_u32(smem + L::DO + sq * L::QTILE);
@@ -446,11 +453,11 @@ __global__ void __launch_bounds__(320, 1)
     const float* lse_b = lse + ((int64_t)b * g.H + h) * g.T;
     const float* d_b = delta + ((int64_t)b * g.H + h) * g.T;
     bool ok = true;
-    // this lane's lse2 / D for the next query tile, loaded one tile ahead
+    // this lane's -lse*log2(e) / D for the next query tile, loaded one tile ahead
     auto fetch = [&](int i, float& l2, float& dd) {
       const int t = tfirst + i * BNQ + half * 32 + lane;
       const bool tv = i < nq && t <= tlast;
-      l2 = tv ? __ldg(lse_b + t) * kLog2e : INFINITY;
+      l2 = tv ? -__ldg(lse_b + t) * kLog2e : -INFINITY;
       dd = tv ? __ldg(d_b + t) : 0.f;
     };
     float nl2, nd;
@@ -467,7 +474,6 @@ __global__ void __launch_bounds__(320, 1)
       // finished reading the P^T / dS^T columns this pass overwrites
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_SP + s], (i >> 1) & 1, abort, &g_fault_word));
       if (!ok) break;
-      if (row == 0 && half == 0 && i < 12) LLATTN_TRACE_AT(4 + i);
       tc_fence_after();
       const int c_lo = j + 1 - t0 - half * 32, c_hi = valid ? t_hi - t0 - half * 32 + 1 : -1;  // in [0, 32)
       {
@@ -476,31 +482,47 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld32(tmem + lane_off + s * BNQ + cc * 32, rs);
         tmem_ld32(tmem + lane_off + 128 + s * BNQ + cc * 32, rp);
         tmem_ld_wait();
-        if (row == 0 && half == 0 && i < 6) LLATTN_TRACE_AT(44 + i);
+        if (row == 0 && half == 0 && i < 6) LLATTN_TRACE_K(2, 44 + i);
         uint32_t pp[16], pd[16];
+        // interior tiles (every key of the warp sees all 32 queries) skip the mask
+        const bool full = __all_sync(0xffffffffu, c_lo <= 0 && c_hi >= 32);
+        const float4* nl4 = reinterpret_cast<const float4*>(v_lse);
+        const float4* d4 = reinterpret_cast<const float4*>(v_d);
+        const uint64_t sc2 = f2_pack(sc, sc);
 #pragma unroll
-        for (int i2 = 0; i2 < 16; ++i2) {
-          float pv[2], dv[2];
+        for (int q4 = 0; q4 < 8; ++q4) {
+          const float4 nl = nl4[q4], dd = d4[q4];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
-            const int c = 2 * i2 + u;
-            const bool vis = c >= c_lo && c < c_hi;
-            const float e = fast_exp2(fmaf(__uint_as_float(rs[c]), sc, -v_lse[c]));
-            const float p = vis ? e : 0.f;
-            pv[u] = p;
-            dv[u] = p * (__uint_as_float(rp[c]) - v_d[c]);
+            const int c = 4 * q4 + 2 * u;
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sc2,
+                             u == 0 ? f2_pack(nl.x, nl.y) : f2_pack(nl.z, nl.w)),
+                      x0, x1);
+            float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+            if (!full) {
+              p0 = (c >= c_lo && c < c_hi) ? p0 : 0.f;
+              p1 = (c + 1 >= c_lo && c + 1 < c_hi) ? p1 : 0.f;
+            }
+            const uint64_t ds = f2_mul(f2_pack(p0, p1),
+                                       f2_sub(f2_pack(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])),
+                                              u == 0 ? f2_pack(dd.x, dd.y) : f2_pack(dd.z, dd.w)));
+            float d0, d1;
+            f2_unpack(ds, d0, d1);
+            pp[c / 2] = pack_bf16(p0, p1);
+            pd[c / 2] = pack_bf16(d0, d1);
           }
-          pp[i2] = pack_bf16(pv[0], pv[1]);
-          pd[i2] = pack_bf16(dv[0], dv[1]);
         }
+        if (row == 0 && half == 0 && i < 6) LLATTN_TRACE_K(2, 30 + i);
         tmem_st16(tmem + lane_off + s * BNQ + cc * 32, pp);
         tmem_st16(tmem + lane_off + 128 + s * BNQ + cc * 32, pd);
         tmem_st_wait();
+        if (row == 0 && half == 0 && i < 12) LLATTN_TRACE_K(2, 4 + i);
       }
       tc_fence_before();
       mbar_arrive(&bars[KV_PD + s]);
-      if (row == 0 && half == 0 && i < 12) LLATTN_TRACE_AT(16 + i);
-      if (warp == 9 && lane == 31 && i < 6) LLATTN_TRACE_AT(54 + i);
+      if (row == 0 && half == 0 && i < 12) LLATTN_TRACE_K(2, 16 + i);
+      if (warp == 9 && lane == 31 && i < 6) LLATTN_TRACE_K(2, 54 + i);
     }
     if (!ok) raise_fault(kFaultSoftmax, abort);
     if (ok && nq > 0)
@@ -510,7 +532,7 @@ __global__ void __launch_bounds__(320, 1)
       raise_fault(kFaultEpilogue, abort);
     } else {
       tc_fence_after();
-      if (row == 0 && half == 0) LLATTN_TRACE_AT(52);
+      if (row == 0 && half == 0) LLATTN_TRACE_K(2, 52);
       // half 0 stages dK, half 1 dV: bf16, 128-byte-swizzled 64-column panels
       // in the (now idle) Q/dO ring, stored below by TMA (rows >= T clipped)
       uint8_t* stage = smem + L::Q + half * (BM * HD * 2);
@@ -554,7 +576,7 @@ __global__ void __launch_bounds__(320, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) LLATTN_TRACE_AT(60);
+  if (threadIdx.x == 0) LLATTN_TRACE_K(2, 60);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();

@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(320, 1)
   // heads fastest: CTAs that run together cover whole token rows of qkv
   const int h = blockIdx.x, b = blockIdx.z;
   const int q0 = blockIdx.y * 2 * BM;
-  if (threadIdx.x == 0) LLATTN_TRACE_AT(0);
+  if (threadIdx.x == 0) LLATTN_TRACE_K(1, 0);
   const bool fuse = ep.lat != nullptr;
   const bool has_b = q0 + BM < g.T;
   const int kbase = local_lo(g, q0);  // first key of the union range
@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0) LLATTN_TRACE_AT(1);
+  if (threadIdx.x == 0) LLATTN_TRACE_K(1, 1);
 
   if (warp == 0) {
     if (lane == 0 && nk > 0) {
@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(320, 1)
       const bool grp_on[2] = {true, has_b};
       int released = 0;  // tiles whose stage was released
       if (nk > 0) ok = mbar_wait(&bars[PP_Q], 0, abort, &g_fault_word);
-      LLATTN_TRACE_AT(2);
+      LLATTN_TRACE_K(1, 2);
       uint64_t t_last = globaltimer_ns();
       uint32_t spin = 0;
       while (ok) {
@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(320, 1)
         const int j = tt.first + i;
         ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_S + 2 * grp + (i & 1)], (i >> 1) & 1, abort, &g_fault_word));
         if (!ok) break;
-        if (row == 0) LLATTN_TRACE_AT(4 + grp * 24 + i);
+        if (row == 0) LLATTN_TRACE_K(1, 4 + grp * 24 + i);
         tc_fence_after();
         const uint32_t tsrc = tS + (i & 1) * BNK + lane_off;
         const int c_lo = lo - (kbase + j * BNK);
@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc_fence_before();
         mbar_arrive(&bars[PP_P + 2 * grp + (i & 1)]);
-        if (row == 0) LLATTN_TRACE_AT(16 + grp * 24 + i);
+        if (row == 0) LLATTN_TRACE_K(1, 16 + grp * 24 + i);
       }
       if (!ok) raise_fault(kFaultSoftmax, abort);
       if (ok && fuse) {
@@ -417,7 +417,7 @@ __global__ void __launch_bounds__(320, 1)
         ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_O + 2 * grp + ((n_mine - 1) & 1)], ((n_mine - 1) >> 1) & 1,
                                                abort, &g_fault_word));
       if (ok && fuse) ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_R + grp], 0, abort, &g_fault_word));
-      if (row == 0) LLATTN_TRACE_AT(52 + 2 * grp);
+      if (row == 0) LLATTN_TRACE_K(1, 52 + 2 * grp);
       if (!ok) {
         raise_fault(kFaultEpilogue, abort);
       } else {
@@ -530,12 +530,12 @@ __global__ void __launch_bounds__(320, 1)
         }
         if (valid) lse_out[((int64_t)b * g.H + h) * g.T + t] = l > 0.f ? (m + log2f(l)) * kLn2 : INFINITY;
       }
-      if (row == 0) LLATTN_TRACE_AT(53 + 2 * grp);
+      if (row == 0) LLATTN_TRACE_K(1, 53 + 2 * grp);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) LLATTN_TRACE_AT(60);
+  if (threadIdx.x == 0) LLATTN_TRACE_K(1, 60);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
