@@ -388,7 +388,7 @@ def run_ours(args):
     per_step = {k: (v[0] / args.steps, v[1] / args.steps) for k, v in kern.items() if v[1] > 0}
     top = max(per_step, key=lambda k: per_step[k][0])
     calls = max(1, round(kern[top][1] / args.steps / {"local_bwd": 2, "rout_bwd": 2, "reduce": 3,
-                                                      "latent_bwd": 3}.get(top, 1)))
+                                                      "latent_bwd": 2}.get(top, 1)))
     avg_ms = kern[top][0] / args.steps / calls
     roof = None
     if top in alg:

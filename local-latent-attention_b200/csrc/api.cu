@@ -70,7 +70,7 @@ int make_geom(const llattn_dims* d, Geom* g) {
 
 // Backward workspace, every region 256-byte aligned.
 struct BwdLayout {
-  size_t dl, delta, drow, dlat, dlat_tok, lat_delta, dg_part, dg_sum, dw_part, dgkv_part, total;
+  size_t dl, delta, drow, dlat, dlat_tok, dg_part, dg_sum, dw_part, dgkv_part, total;
   int gate_tok, n_gate_cta, n_split_w, n_split_lat;
 };
 
@@ -83,8 +83,8 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
   const int rows = g.B * g.Tq;
   // token splits of the dW_rout reduction (enough CTAs to fill the GPU)
   L.n_split_w = std::max(1, std::min(cdiv(g.B * g.T, 64), cdiv(2 * 148, cdiv(g.d, 128))));
-  const int lat_ctas = g.B * g.Lh * cdiv(g.Nc, 64);
-  L.n_split_lat = std::max(1, std::min(cdiv(g.Tq, 32), cdiv(2 * 148, lat_ctas)));
+  // row splits of the latent backward: (b, latent head, split) CTAs, about two per SM
+  L.n_split_lat = std::max(1, std::min(cdiv(g.Tq, 64), (2 * 148) / (g.B * g.Lh)));
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
   const size_t BTd = (size_t)g.B * g.T * g.d;
@@ -93,7 +93,6 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
   L.drow = take(sizeof(float) * BTd);
   L.dlat = take(sizeof(float) * (size_t)rows * g.Ld);
   L.dlat_tok = take(sizeof(float) * (size_t)g.B * g.T * g.Ld);
-  L.lat_delta = take(sizeof(float) * (size_t)g.B * g.Lh * g.Tq);
   L.dg_part = take(sizeof(float) * (size_t)L.n_gate_cta * 2 * g.hd);
   L.dg_sum = take(sizeof(float) * 2 * g.hd);
   L.dw_part = take(sizeof(float) * (size_t)L.n_split_w * g.d * (g.Ld + 1));
@@ -144,7 +143,6 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
   float* delta = reinterpret_cast<float*>(ws + L.delta);
   float* drow = reinterpret_cast<float*>(ws + L.drow);
   float* dlat = reinterpret_cast<float*>(ws + L.dlat);
-  float* lat_delta = reinterpret_cast<float*>(ws + L.lat_delta);
   float* dg_part = reinterpret_cast<float*>(ws + L.dg_part);
   float* dg_sum = reinterpret_cast<float*>(ws + L.dg_sum);
   float* dw_part = reinterpret_cast<float*>(ws + L.dw_part);
@@ -239,10 +237,9 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
                     "copy dg_remote");
   }
   if (rc) return rc;
-  prof::Scope ps(prof::LATENT_BWD, s, 3);
-  rc = check_launch(launch_latent_bwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv), lat,
-                                         a->lat_lse, dlat, static_cast<T*>(a->drq), dgkv_part, L.n_split_lat,
-                                         lat_delta, s),
+  prof::Scope ps(prof::LATENT_BWD, s, 2);
+  rc = check_launch(launch_latent_bwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv),
+                                         a->lat_lse, dlat, static_cast<T*>(a->drq), dgkv_part, L.n_split_lat, s),
                     "latent_bwd");
   if (rc) return rc;
   return check_launch(launch_latent_reduce<T>(g, dgkv_part, L.n_split_lat, static_cast<T*>(a->dgkv), s),

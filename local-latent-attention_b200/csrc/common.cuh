@@ -90,11 +90,11 @@ cudaError_t launch_pool_bwd(const Geom& g, int mode, const T* dout, T* dx, int64
 template <typename T>
 cudaError_t launch_latent_fwd(const Geom& g, const T* rq, const T* gkv, T* lat, float* lat_lse,
                               cudaStream_t s);
-// Latent backward: drq (direct) and per-row-split partials of dgk/dgv.
+// Latent backward: drq (direct) and per-row-split partials of dgk/dgv
+// ([n_split][B][Nc][2][Ld], every entry written).
 template <typename T>
-cudaError_t launch_latent_bwd(const Geom& g, const T* rq, const T* gkv, const T* lat,
-                              const float* lat_lse, const float* dlat, T* drq, float* dgkv_part,
-                              int n_split, float* delta_ws, cudaStream_t s);
+cudaError_t launch_latent_bwd(const Geom& g, const T* rq, const T* gkv, const float* lat_lse,
+                              const float* dlat, T* drq, float* dgkv_part, int n_split, cudaStream_t s);
 template <typename T>
 cudaError_t launch_latent_reduce(const Geom& g, const float* dgkv_part, int n_split, T* dgkv,
                                  cudaStream_t s);

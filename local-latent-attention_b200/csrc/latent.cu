@@ -96,280 +96,277 @@ __global__ void __launch_bounds__(kRowsFwd) latent_fwd_kernel(Geom g, const T* _
 // delta = dlat.lat, dS = P (dP - delta):
 //   drq = lat_scale * sum_j dS gk_j,  dgk_j = lat_scale * sum_r dS rq_r,
 //   dgv_j = sum_r P dlat_r.
-// Kernel 1 (row-major CTAs) computes drq and delta. Kernel 2 (key-major CTAs,
-// rows split in n_split ranges) accumulates dgk/dgv for 64 keys in registers
-// and writes one partial per row range; a reduce sums the partials in a fixed
-// order, so the result is deterministic.
+// One kernel: a CTA owns (b, latent head, row split) and walks its 64-row
+// blocks (interleaved over the splits, so early rows with few visible chunks
+// and late rows with many spread evenly). Per row block, pass 1 sums
+// delta = sum_j P_j (dlat.gv_j) over the 64-key tiles in fp32 (not from the
+// stored, rounded lat: with long chunks the pooled values are nearly equal
+// and dS cancels, so delta must be consistent with P to working precision);
+// pass 2 forms P and dS per tile in shared memory, accumulates drq in
+// registers and adds dgk / dgv into the CTA's own partial slice (plain
+// read-modify-write by the owning thread: no atomics). A reduce sums the
+// per-split partials in a fixed order, so the result is deterministic.
+// S and dP of a 64x64 tile: each thread a 4-row x 4-key block, operands as
+// float4 from shared memory (8 FMAs per load); with a single key tile (the
+// usual case) pass 2 reuses pass 1's P and dP instead of recomputing them.
 
-constexpr int kRowsBwd = 64;
+constexpr int kLatRows = 64, kLatKeys = 64;
+constexpr float kLatLog2e = 1.4426950408889634f;
 
-template <typename T, int L>
-__global__ void __launch_bounds__(256) latent_bwd_rows_kernel(
-    Geom g, const T* __restrict__ rq, const T* __restrict__ gkv, const T* __restrict__ lat,
-    const float* __restrict__ lat_lse, const float* __restrict__ dlat, T* __restrict__ drq,
-    float* __restrict__ delta_ws) {
-  extern __shared__ float smem_rows[];
-  float(*s_rq)[L + 1] = reinterpret_cast<float(*)[L + 1]>(smem_rows);
-  float(*s_dl)[L + 1] = s_rq + kRowsBwd;
-  float(*s_k)[L + 1] = s_dl + kRowsBwd;
-  float(*s_v)[L + 1] = s_k + kKeyTile;
-  float(*s_ds)[kKeyTile + 1] = reinterpret_cast<float(*)[kKeyTile + 1]>(s_v + kKeyTile);
-  float* s_lse = reinterpret_cast<float*>(s_ds + kRowsBwd);
-  float* s_delta = s_lse + kRowsBwd;
-  int* s_qid = reinterpret_cast<int*>(s_delta + kRowsBwd);
-  const int b = blockIdx.z, lh = blockIdx.y, r0 = blockIdx.x * kRowsBwd;
+template <int L>
+struct LatBwdSmem {
+  static constexpr int LS = L + 4;          // operand row stride (floats; 16-byte rows)
+  static constexpr int PS = kLatKeys + 4;   // P / dS row stride
+  static constexpr int RQ = 0, DL = RQ + kLatRows * LS, K = DL + kLatRows * LS, V = K + kLatKeys * LS;
+  static constexpr int P = V + kLatKeys * LS, DS = P + kLatRows * PS;
+  static constexpr int LSE = DS + kLatRows * PS, DELTA = LSE + kLatRows, QID = DELTA + kLatRows;
+  static constexpr int FLOATS = QID + kLatRows;
+};
+
+// ONE: all chunk keys fit one 64-key tile (Nc <= 64): the keys are staged
+// once per CTA and the dgk / dgv accumulators stay in registers across the
+// CTA's row blocks (a single store of the partial at the end).
+template <typename T, int L, bool ONE>
+__global__ void __launch_bounds__(256, 2) latent_bwd_kernel(Geom g, const T* __restrict__ rq,
+                                                         const T* __restrict__ gkv,
+                                                         const float* __restrict__ lat_lse,
+                                                         const float* __restrict__ dlat, T* __restrict__ drq,
+                                                         float* __restrict__ part, int n_split) {
+  using S = LatBwdSmem<L>;
+  constexpr int LS = S::LS, PS = S::PS, EQ = L / 4;
+  extern __shared__ float4 smem_lat4[];
+  float* sm = reinterpret_cast<float*>(smem_lat4);
+  float *s_rq = sm + S::RQ, *s_dl = sm + S::DL, *s_k = sm + S::K, *s_v = sm + S::V;
+  float *s_p = sm + S::P, *s_ds = sm + S::DS, *s_lse = sm + S::LSE, *s_delta = sm + S::DELTA;
+  int* s_qid = reinterpret_cast<int*>(sm + S::QID);
+  const int b = blockIdx.z, lh = blockIdx.y, split = blockIdx.x;
   const int tid = threadIdx.x;
+  const float sc2 = g.lat_scale * kLatLog2e;
+  const int rg = tid >> 4, kg = tid & 15;  // S / dP block: rows 4rg + i, keys kg + 16u
+  const int own = tid >> 2, eq = tid & 3;  // drq row / dgk,dgv key, and its e-quarter
+  float* my_part = part + ((int64_t)split * g.B + b) * g.Nc * 2 * g.Ld + lh * g.ldh;
 
-  for (int idx = tid; idx < kRowsBwd * L; idx += 256) {
-    const int i = idx / L, e = idx % L, r = r0 + i;
-    float a = 0.f, dv = 0.f;
-    if (r < g.Tq && e < g.ldh) {
-      a = to_f<T>(rq[((int64_t)(b * g.Tq + r) * g.Lh + lh) * g.ldh + e]);
-      dv = dlat[(int64_t)(b * g.Tq + r) * g.Ld + lh * g.ldh + e];
-    }
-    s_rq[i][e] = a;
-    s_dl[i][e] = dv;
-  }
-  if (tid < kRowsBwd) {
-    const int r = r0 + tid;
-    if (r < g.Tq) {
-      s_lse[tid] = lat_lse[(int64_t)(b * g.Lh + lh) * g.Tq + r];
-      s_qid[tid] = row_qid(g, r);
-    } else {
-      s_lse[tid] = INFINITY;
-      s_qid[tid] = 0;
-    }
-  }
-  const int max_qid = row_qid(g, min(r0 + kRowsBwd - 1, g.Tq - 1));
-  // thread -> (row ri, 4-key subset kc) for dS; (row ri, e-subset ec) for drq
-  const int ri = tid / 4, kc = tid % 4;
-  constexpr int EPT = (L + 3) / 4;
-  float acc[EPT];
+  // this CTA's partial slice starts at zero (same thread mapping as the adds)
+  if (!ONE)
+  for (int j = own; j < g.Nc; j += kLatKeys)
 #pragma unroll
-  for (int u = 0; u < EPT; ++u) acc[u] = 0.f;
-
-  // delta = dlat . lat, taken as sum_j P_j (dlat . gv_j) in fp32 rather than
-  // from the stored (rounded) lat: with long chunks the pooled values are
-  // nearly equal and dS = P (dlat.gv_j - delta) cancels, so delta must be
-  // consistent with P to working precision
-  float dpart = 0.f;
-  for (int j0 = 0; j0 < max_qid; j0 += kKeyTile) {
-    __syncthreads();
-    for (int idx = tid; idx < kKeyTile * L; idx += 256) {
-      const int jj = idx / L, e = idx % L, j = j0 + jj;
-      float kv = 0.f, vv = 0.f;
-      if (j < g.Nc && e < g.ldh) {
-        const int64_t base = ((int64_t)(b * g.Nc + j) * 2 * g.Lh + lh) * g.ldh + e;
-        kv = to_f<T>(gkv[base]);
-        vv = to_f<T>(gkv[base + (int64_t)g.Lh * g.ldh]);
-      }
-      s_k[jj][e] = kv;
-      s_v[jj][e] = vv;
-    }
-    __syncthreads();
-    const float lse = s_lse[ri];
-    const int qid = s_qid[ri];
-    for (int u = 0; u < kKeyTile / 4; ++u) {
-      const int jj = kc + 4 * u;
-      if (j0 + jj < qid) {
-        float sd = 0.f, dp = 0.f;
-#pragma unroll
-        for (int e = 0; e < L; ++e) {
-          sd = fmaf(s_rq[ri][e], s_k[jj][e], sd);
-          dp = fmaf(s_dl[ri][e], s_v[jj][e], dp);
-        }
-        dpart = fmaf(expf(sd * g.lat_scale - lse), dp, dpart);
-      }
-    }
-  }
-  dpart += __shfl_xor_sync(0xffffffffu, dpart, 1);
-  dpart += __shfl_xor_sync(0xffffffffu, dpart, 2);
-  if (kc == 0) {
-    s_delta[ri] = dpart;
-    if (r0 + ri < g.Tq) delta_ws[(int64_t)(b * g.Lh + lh) * g.Tq + r0 + ri] = dpart;
-  }
-
-  for (int j0 = 0; j0 < max_qid; j0 += kKeyTile) {
-    __syncthreads();
-    for (int idx = tid; idx < kKeyTile * L; idx += 256) {
-      const int jj = idx / L, e = idx % L, j = j0 + jj;
-      float kv = 0.f, vv = 0.f;
-      if (j < g.Nc && e < g.ldh) {
-        const int64_t base = ((int64_t)(b * g.Nc + j) * 2 * g.Lh + lh) * g.ldh + e;
-        kv = to_f<T>(gkv[base]);
-        vv = to_f<T>(gkv[base + (int64_t)g.Lh * g.ldh]);
-      }
-      s_k[jj][e] = kv;
-      s_v[jj][e] = vv;
-    }
-    __syncthreads();
-    {
-      const float lse = s_lse[ri], dlt = s_delta[ri];
-      const int qid = s_qid[ri];
-#pragma unroll 4
-      for (int u = 0; u < kKeyTile / 4; ++u) {
-        const int jj = kc + 4 * u;
-        float sd = 0.f, dp = 0.f;
-#pragma unroll
-        for (int e = 0; e < L; ++e) {
-          sd = fmaf(s_rq[ri][e], s_k[jj][e], sd);
-          dp = fmaf(s_dl[ri][e], s_v[jj][e], dp);
-        }
-        float ds = 0.f;
-        if (j0 + jj < qid) {
-          const float p = expf(sd * g.lat_scale - lse);
-          ds = p * (dp - dlt);
-        }
-        s_ds[ri][jj] = ds;
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < EPT; ++u) {
-      const int e = kc + 4 * u;
-      if (e < L) {
-        float a = acc[u];
-        for (int jj = 0; jj < kKeyTile; ++jj) a = fmaf(s_ds[ri][jj], s_k[jj][e], a);
-        acc[u] = a;
-      }
-    }
-  }
-  const int r = r0 + ri;
-  if (r < g.Tq) {
-#pragma unroll
-    for (int u = 0; u < EPT; ++u) {
-      const int e = kc + 4 * u;
-      if (e < g.ldh)
-        drq[((int64_t)(b * g.Tq + r) * g.Lh + lh) * g.ldh + e] = from_f<T>(acc[u] * g.lat_scale);
-    }
-  }
-}
-
-constexpr int kRowsSub = 32;  // rows per inner step of the key-major kernel
-
-template <typename T, int L>
-__global__ void __launch_bounds__(256) latent_bwd_keys_kernel(
-    Geom g, const T* __restrict__ rq, const T* __restrict__ gkv, const float* __restrict__ lat_lse,
-    const float* __restrict__ dlat, const float* __restrict__ delta_ws, float* __restrict__ part,
-    int n_split) {
-  extern __shared__ float smem_keys[];
-  float(*s_k)[L + 1] = reinterpret_cast<float(*)[L + 1]>(smem_keys);
-  float(*s_v)[L + 1] = s_k + kKeyTile;
-  float(*s_rq)[L + 1] = s_v + kKeyTile;
-  float(*s_dl)[L + 1] = s_rq + kRowsSub;
-  float(*s_p)[kKeyTile + 1] = reinterpret_cast<float(*)[kKeyTile + 1]>(s_dl + kRowsSub);
-  float(*s_ds)[kKeyTile + 1] = s_p + kRowsSub;
-  float* s_lse = reinterpret_cast<float*>(s_ds + kRowsSub);
-  float* s_delta = s_lse + kRowsSub;
-  int* s_qid = reinterpret_cast<int*>(s_delta + kRowsSub);
-  const int tid = threadIdx.x;
-  const int n_ktiles = cdiv(g.Nc, kKeyTile);
-  const int kt = blockIdx.x % n_ktiles, split = blockIdx.x / n_ktiles;
-  const int b = blockIdx.z, lh = blockIdx.y, j0 = kt * kKeyTile;
-
-  for (int idx = tid; idx < kKeyTile * L; idx += 256) {
-    const int jj = idx / L, e = idx % L, j = j0 + jj;
-    float kv = 0.f, vv = 0.f;
-    if (j < g.Nc && e < g.ldh) {
-      const int64_t base = ((int64_t)(b * g.Nc + j) * 2 * g.Lh + lh) * g.ldh + e;
-      kv = to_f<T>(gkv[base]);
-      vv = to_f<T>(gkv[base + (int64_t)g.Lh * g.ldh]);
-    }
-    s_k[jj][e] = kv;
-    s_v[jj][e] = vv;
-  }
-  // rows that can see chunk j0: qid(r) > j0. qid is non-decreasing in r, so
-  // that is a suffix [r_first, Tq); find it by bisection.
-  int lo = 0, hi = g.Tq;
-  while (lo < hi) {
-    const int mid = (lo + hi) / 2;
-    if (row_qid(g, mid) > j0) hi = mid; else lo = mid + 1;
-  }
-  const int r_first = lo;
-  const int n_rows = g.Tq - r_first;
-  const int per = cdiv(cdiv(max(n_rows, 1), n_split), kRowsSub) * kRowsSub;
-  const int ra = r_first + split * per, rb = min(g.Tq, ra + per);
-
-  // accumulators: key jk = tid/4, e-subset ec = tid%4
-  const int jk = tid / 4, ec = tid % 4;
-  constexpr int EPT = (L + 3) / 4;
-  float agk[EPT], agv[EPT];
-#pragma unroll
-  for (int u = 0; u < EPT; ++u) agk[u] = agv[u] = 0.f;
-
-  for (int rs = ra; rs < rb; rs += kRowsSub) {
-    __syncthreads();
-    for (int idx = tid; idx < kRowsSub * L; idx += 256) {
-      const int i = idx / L, e = idx % L, r = rs + i;
-      float a = 0.f, dv = 0.f;
-      if (r < rb && e < g.ldh) {
-        a = to_f<T>(rq[((int64_t)(b * g.Tq + r) * g.Lh + lh) * g.ldh + e]);
-        dv = dlat[(int64_t)(b * g.Tq + r) * g.Ld + lh * g.ldh + e];
-      }
-      s_rq[i][e] = a;
-      s_dl[i][e] = dv;
-    }
-    if (tid < kRowsSub) {
-      const int r = rs + tid;
-      if (r < rb) {
-        s_lse[tid] = lat_lse[(int64_t)(b * g.Lh + lh) * g.Tq + r];
-        s_delta[tid] = delta_ws[(int64_t)(b * g.Lh + lh) * g.Tq + r];
-        s_qid[tid] = row_qid(g, r);
-      } else {
-        s_lse[tid] = INFINITY;
-        s_delta[tid] = 0.f;
-        s_qid[tid] = 0;
-      }
-    }
-    __syncthreads();
-    // 32 rows x 64 keys = 2048 pairs, 8 per thread: row = tid/8, key = tid%8 + 8u
-    {
-      const int ri = tid / 8, kc = tid % 8;
-      const float lse = s_lse[ri], dlt = s_delta[ri];
-      const int qid = s_qid[ri];
-#pragma unroll
-      for (int u = 0; u < kKeyTile / 8; ++u) {
-        const int jj = kc + 8 * u;
-        float sd = 0.f, dp = 0.f;
-#pragma unroll
-        for (int e = 0; e < L; ++e) {
-          sd = fmaf(s_rq[ri][e], s_k[jj][e], sd);
-          dp = fmaf(s_dl[ri][e], s_v[jj][e], dp);
-        }
-        float p = 0.f, ds = 0.f;
-        if (j0 + jj < qid) {
-          p = expf(sd * g.lat_scale - lse);
-          ds = p * (dp - dlt);
-        }
-        s_p[ri][jj] = p;
-        s_ds[ri][jj] = ds;
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < EPT; ++u) {
-      const int e = ec + 4 * u;
-      if (e < L) {
-        float a = agk[u], v = agv[u];
-        for (int i = 0; i < kRowsSub; ++i) {
-          a = fmaf(s_ds[i][jk], s_rq[i][e], a);
-          v = fmaf(s_p[i][jk], s_dl[i][e], v);
-        }
-        agk[u] = a;
-        agv[u] = v;
-      }
-    }
-  }
-  const int j = j0 + jk;
-  if (j < g.Nc) {
-    float* dst = part + (int64_t)split * g.B * g.Nc * 2 * g.Ld;
-#pragma unroll
-    for (int u = 0; u < EPT; ++u) {
-      const int e = ec + 4 * u;
+    for (int u = 0; u < EQ; ++u) {
+      const int e = eq * EQ + u;
       if (e < g.ldh) {
+        my_part[(int64_t)(2 * j) * g.Ld + e] = 0.f;
+        my_part[(int64_t)(2 * j + 1) * g.Ld + e] = 0.f;
+      }
+    }
+
+  auto load_keys = [&](int j0) {
+    for (int idx = tid; idx < kLatKeys * L; idx += 256) {
+      const int jj = idx / L, e = idx % L, j = j0 + jj;
+      float kv = 0.f, vv = 0.f;
+      if (j < g.Nc && e < g.ldh) {
         const int64_t base = ((int64_t)(b * g.Nc + j) * 2 * g.Lh + lh) * g.ldh + e;
-        dst[base] = agk[u] * g.lat_scale;
-        dst[base + (int64_t)g.Lh * g.ldh] = agv[u];
+        kv = to_f<T>(gkv[base]);
+        vv = to_f<T>(gkv[base + (int64_t)g.Lh * g.ldh]);
+      }
+      s_k[jj * LS + e] = kv;
+      s_v[jj * LS + e] = vv;
+    }
+  };
+  // P and dP of this thread's 4 rows (4rg + i) x 4 keys (kg + 16u) of the
+  // tile at j0 into s_p / s_ds; returns nothing, masks keys j >= qid(row).
+  // (Keys kg + 16u: the 8 lanes of a quarter warp read 8 distinct 16-byte
+  // bank groups of s_k / s_v.)
+  auto tile_pdp = [&](int j0) {
+    // S block, then dP block (fewer live registers than both at once)
+    float sa[4][4], da[4][4];
+    auto block = [&](const float* x, const float* y, float (&acc)[4][4]) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[i][u] = 0.f;
+#pragma unroll
+      for (int e = 0; e < L; e += 4) {
+        float4 a[4], k[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          a[i] = *reinterpret_cast<const float4*>(x + (4 * rg + i) * LS + e);
+          k[i] = *reinterpret_cast<const float4*>(y + (kg + 16 * i) * LS + e);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            acc[i][u] = fmaf(a[i].x, k[u].x, fmaf(a[i].y, k[u].y, fmaf(a[i].z, k[u].z, fmaf(a[i].w, k[u].w, acc[i][u]))));
+      }
+    };
+    block(s_rq, s_k, sa);
+    block(s_dl, s_v, da);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int ri = 4 * rg + i;
+      const float lse2 = s_lse[ri];
+      const int qid = s_qid[ri];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int jj = kg + 16 * u;
+        s_p[ri * PS + jj] = j0 + jj < qid ? exp2f(fmaf(sa[i][u], sc2, -lse2)) : 0.f;
+        s_ds[ri * PS + jj] = da[i][u];
+      }
+    }
+  };
+
+  // rq / dlat of a row block, loaded into registers one block ahead
+  constexpr int NPRE = kLatRows * L / 256;
+  float pre_a[NPRE], pre_d[NPRE];
+  auto prefetch_rows = [&](int rb) {
+#pragma unroll
+    for (int k = 0; k < NPRE; ++k) {
+      const int idx = tid + 256 * k, i = idx / L, e = idx % L, r = rb * kLatRows + i;
+      pre_a[k] = pre_d[k] = 0.f;
+      if (r < g.Tq && e < g.ldh) {
+        pre_a[k] = to_f<T>(rq[((int64_t)(b * g.Tq + r) * g.Lh + lh) * g.ldh + e]);
+        pre_d[k] = dlat[(int64_t)(b * g.Tq + r) * g.Ld + lh * g.ldh + e];
+      }
+    }
+  };
+  float ak1[EQ], av1[EQ];  // ONE: dgk / dgv of key `own` over all this CTA's rows
+#pragma unroll
+  for (int u = 0; u < EQ; ++u) ak1[u] = av1[u] = 0.f;
+  if (ONE) load_keys(0);
+  const int n_rb = cdiv(g.Tq, kLatRows);
+  if (split < n_rb) prefetch_rows(split);
+  for (int rb = split; rb < n_rb; rb += n_split) {
+    const int r0 = rb * kLatRows;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < NPRE; ++k) {
+      const int idx = tid + 256 * k, i = idx / L, e = idx % L;
+      s_rq[i * LS + e] = pre_a[k];
+      s_dl[i * LS + e] = pre_d[k];
+    }
+    if (rb + n_split < n_rb) prefetch_rows(rb + n_split);
+    if (tid < kLatRows) {
+      const int r = r0 + tid;
+      const bool ok = r < g.Tq;
+      s_lse[tid] = ok ? lat_lse[(int64_t)(b * g.Lh + lh) * g.Tq + r] * kLatLog2e : INFINITY;
+      s_qid[tid] = ok ? row_qid(g, r) : 0;
+      s_delta[tid] = 0.f;
+    }
+    const int jmax = row_qid(g, min(r0 + kLatRows - 1, g.Tq - 1));  // keys j < jmax are visible
+    const int n_kt = cdiv(jmax, kLatKeys);
+    // pass 1: delta = sum_j P dP (P, dP of the last tile stay in s_p / s_ds)
+    for (int kt = 0; kt < n_kt; ++kt) {
+      __syncthreads();
+      if (!ONE) {
+        load_keys(kt * kLatKeys);
+        __syncthreads();
+      }
+      tile_pdp(kt * kLatKeys);
+      // each thread sums the entries it wrote: rows 4rg+i, keys kg+16u
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ri = 4 * rg + i;
+        float dsum = 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) dsum = fmaf(s_p[ri * PS + kg + 16 * u], s_ds[ri * PS + kg + 16 * u], dsum);
+#pragma unroll
+        for (int off = 1; off < 16; off <<= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, off);
+        if (kg == 0) s_delta[ri] += dsum;
+      }
+    }
+    float aq[EQ];
+#pragma unroll
+    for (int u = 0; u < EQ; ++u) aq[u] = 0.f;
+    // pass 2: dS; drq; dgk, dgv
+    for (int kt = 0; kt < n_kt; ++kt) {
+      const int j0 = kt * kLatKeys;
+      __syncthreads();
+      if (!ONE && n_kt > 1) {  // one tile: its P, dP are still in s_p / s_ds
+        load_keys(j0);
+        __syncthreads();
+        tile_pdp(j0);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ri = 4 * rg + i;
+        const float dlt = s_delta[ri];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float* q = s_ds + ri * PS + kg + 16 * u;
+          *q = s_p[ri * PS + kg + 16 * u] * (*q - dlt);
+        }
+      }
+      __syncthreads();
+      // drq: row `own`, e-quarter eq
+#pragma unroll 4
+      for (int j = 0; j < kLatKeys; ++j) {
+        const float dsv = s_ds[own * PS + j];
+        const float* kr = s_k + j * LS + eq * EQ;
+#pragma unroll
+        for (int u = 0; u < EQ; u += 4) {
+          const float4 k4 = *reinterpret_cast<const float4*>(kr + u);
+          aq[u] = fmaf(dsv, k4.x, aq[u]);
+          aq[u + 1] = fmaf(dsv, k4.y, aq[u + 1]);
+          aq[u + 2] = fmaf(dsv, k4.z, aq[u + 2]);
+          aq[u + 3] = fmaf(dsv, k4.w, aq[u + 3]);
+        }
+      }
+      // dgk, dgv: key `own` of this tile, e-quarter eq
+      float ak[EQ], av[EQ];
+#pragma unroll
+      for (int u = 0; u < EQ; ++u) ak[u] = av[u] = 0.f;
+#pragma unroll 4
+      for (int r = 0; r < kLatRows; ++r) {
+        const float dsv = s_ds[r * PS + own], pv = s_p[r * PS + own];
+        const float* qr = s_rq + r * LS + eq * EQ;
+        const float* lr = s_dl + r * LS + eq * EQ;
+#pragma unroll
+        for (int u = 0; u < EQ; u += 4) {
+          const float4 q4 = *reinterpret_cast<const float4*>(qr + u);
+          const float4 l4 = *reinterpret_cast<const float4*>(lr + u);
+          ak[u] = fmaf(dsv, q4.x, ak[u]);
+          ak[u + 1] = fmaf(dsv, q4.y, ak[u + 1]);
+          ak[u + 2] = fmaf(dsv, q4.z, ak[u + 2]);
+          ak[u + 3] = fmaf(dsv, q4.w, ak[u + 3]);
+          av[u] = fmaf(pv, l4.x, av[u]);
+          av[u + 1] = fmaf(pv, l4.y, av[u + 1]);
+          av[u + 2] = fmaf(pv, l4.z, av[u + 2]);
+          av[u + 3] = fmaf(pv, l4.w, av[u + 3]);
+        }
+      }
+      const int j = j0 + own;
+      if (ONE) {
+#pragma unroll
+        for (int u = 0; u < EQ; ++u) {
+          ak1[u] += ak[u];
+          av1[u] += av[u];
+        }
+      } else if (j < g.Nc) {
+#pragma unroll
+        for (int u = 0; u < EQ; ++u) {
+          const int e = eq * EQ + u;
+          if (e < g.ldh) {
+            my_part[(int64_t)(2 * j) * g.Ld + e] += ak[u] * g.lat_scale;
+            my_part[(int64_t)(2 * j + 1) * g.Ld + e] += av[u];
+          }
+        }
+      }
+    }
+    const int r = r0 + own;
+    if (r < g.Tq) {
+#pragma unroll
+      for (int u = 0; u < EQ; ++u) {
+        const int e = eq * EQ + u;
+        if (e < g.ldh) drq[((int64_t)(b * g.Tq + r) * g.Lh + lh) * g.ldh + e] = from_f<T>(aq[u] * g.lat_scale);
+      }
+    }
+  }
+  if (ONE && own < g.Nc) {
+#pragma unroll
+    for (int u = 0; u < EQ; ++u) {
+      const int e = eq * EQ + u;
+      if (e < g.ldh) {
+        my_part[(int64_t)(2 * own) * g.Ld + e] = ak1[u] * g.lat_scale;
+        my_part[(int64_t)(2 * own + 1) * g.Ld + e] = av1[u];
       }
     }
   }
@@ -394,25 +391,14 @@ cudaError_t latent_fwd_l(const Geom& g, const T* rq, const T* gkv, T* lat, float
 }
 
 template <typename T, int L>
-cudaError_t latent_bwd_l(const Geom& g, const T* rq, const T* gkv, const T* lat, const float* lse,
-                         const float* dlat, T* drq, float* part, int n_split, float* delta,
-                         cudaStream_t s) {
-  const size_t sm1 = sizeof(float) * ((2 * kRowsBwd + 2 * kKeyTile) * (L + 1) +
-                                      kRowsBwd * (kKeyTile + 1) + 3 * kRowsBwd);
-  const size_t sm2 = sizeof(float) * ((2 * kKeyTile + 2 * kRowsSub) * (L + 1) +
-                                      2 * kRowsSub * (kKeyTile + 1) + 3 * kRowsSub);
-  cudaError_t e = cudaFuncSetAttribute(latent_bwd_rows_kernel<T, L>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
+cudaError_t latent_bwd_l(const Geom& g, const T* rq, const T* gkv, const float* lse, const float* dlat, T* drq,
+                         float* part, int n_split, cudaStream_t s) {
+  const int sm = (int)sizeof(float) * LatBwdSmem<L>::FLOATS;
+  auto k = g.Nc <= kLatKeys ? latent_bwd_kernel<T, L, true> : latent_bwd_kernel<T, L, false>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(latent_bwd_keys_kernel<T, L>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2);
-  if (e != cudaSuccess) return e;
-  dim3 g1(cdiv(g.Tq, kRowsBwd), g.Lh, g.B);
-  latent_bwd_rows_kernel<T, L><<<g1, 256, sm1, s>>>(g, rq, gkv, lat, lse, dlat, drq, delta);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  dim3 g2(cdiv(g.Nc, kKeyTile) * n_split, g.Lh, g.B);
-  latent_bwd_keys_kernel<T, L><<<g2, 256, sm2, s>>>(g, rq, gkv, lse, dlat, delta, part, n_split);
+  dim3 grid(n_split, g.Lh, g.B);
+  k<<<grid, 256, sm, s>>>(g, rq, gkv, lse, dlat, drq, part, n_split);
   return cudaGetLastError();
 }
 
@@ -428,16 +414,12 @@ cudaError_t launch_latent_fwd(const Geom& g, const T* rq, const T* gkv, T* lat, 
 }
 
 template <typename T>
-cudaError_t launch_latent_bwd(const Geom& g, const T* rq, const T* gkv, const T* lat,
-                              const float* lat_lse, const float* dlat, T* drq, float* dgkv_part,
-                              int n_split, float* delta_ws, cudaStream_t s) {
-  if (g.ldh <= 8)
-    return latent_bwd_l<T, 8>(g, rq, gkv, lat, lat_lse, dlat, drq, dgkv_part, n_split, delta_ws, s);
-  if (g.ldh <= 16)
-    return latent_bwd_l<T, 16>(g, rq, gkv, lat, lat_lse, dlat, drq, dgkv_part, n_split, delta_ws, s);
-  if (g.ldh <= 32)
-    return latent_bwd_l<T, 32>(g, rq, gkv, lat, lat_lse, dlat, drq, dgkv_part, n_split, delta_ws, s);
-  return latent_bwd_l<T, 64>(g, rq, gkv, lat, lat_lse, dlat, drq, dgkv_part, n_split, delta_ws, s);
+cudaError_t launch_latent_bwd(const Geom& g, const T* rq, const T* gkv, const float* lat_lse, const float* dlat,
+                              T* drq, float* dgkv_part, int n_split, cudaStream_t s) {
+  if (g.ldh <= 8) return latent_bwd_l<T, 8>(g, rq, gkv, lat_lse, dlat, drq, dgkv_part, n_split, s);
+  if (g.ldh <= 16) return latent_bwd_l<T, 16>(g, rq, gkv, lat_lse, dlat, drq, dgkv_part, n_split, s);
+  if (g.ldh <= 32) return latent_bwd_l<T, 32>(g, rq, gkv, lat_lse, dlat, drq, dgkv_part, n_split, s);
+  return latent_bwd_l<T, 64>(g, rq, gkv, lat_lse, dlat, drq, dgkv_part, n_split, s);
 }
 
 template <typename T>
@@ -458,9 +440,9 @@ cudaError_t launch_reduce_rows(const float* part, int n_part, int64_t n, float* 
 template cudaError_t launch_latent_fwd<float>(const Geom&, const float*, const float*, float*, float*, cudaStream_t);
 template cudaError_t launch_latent_fwd<bf16>(const Geom&, const bf16*, const bf16*, bf16*, float*, cudaStream_t);
 template cudaError_t launch_latent_bwd<float>(const Geom&, const float*, const float*, const float*, const float*,
-                                              const float*, float*, float*, int, float*, cudaStream_t);
-template cudaError_t launch_latent_bwd<bf16>(const Geom&, const bf16*, const bf16*, const bf16*, const float*,
-                                             const float*, bf16*, float*, int, float*, cudaStream_t);
+                                              float*, float*, int, cudaStream_t);
+template cudaError_t launch_latent_bwd<bf16>(const Geom&, const bf16*, const bf16*, const float*, const float*,
+                                             bf16*, float*, int, cudaStream_t);
 template cudaError_t launch_latent_reduce<float>(const Geom&, const float*, int, float*, cudaStream_t);
 template cudaError_t launch_latent_reduce<bf16>(const Geom&, const float*, int, bf16*, cudaStream_t);
 

@@ -104,6 +104,24 @@ bool make_rows_map(CUtensorMap* map, const void* base, int B, int T, int slots_x
   return r == CUDA_SUCCESS;
 }
 
+// [B, T, S, H, hd] bf16 viewed as 5-D (64, T, hd/64, S*H, B) with box
+// (64, rows, hd/64, 1, 1): one copy brings a whole rows x hd tile in the
+// panel-major 128-byte-swizzled layout the MMA descriptors expect (panel p at
+// p * rows * 128 bytes). Fewer, larger copies: the TMA issue rate, not
+// bandwidth, bounds a stream of 8 KB boxes.
+bool make_panel_map(CUtensorMap* map, const void* base, int B, int T, int slots_x_heads, int hd, int rows) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t row_stride = (cuuint64_t)slots_x_heads * hd * 2;
+  cuuint64_t dims[5] = {64, (cuuint64_t)T, (cuuint64_t)(hd / 64), (cuuint64_t)slots_x_heads, (cuuint64_t)B};
+  cuuint64_t strides[4] = {row_stride, 128, (cuuint64_t)hd * 2, (cuuint64_t)T * row_stride};
+  cuuint32_t box[5] = {64, (cuuint32_t)rows, (cuuint32_t)(hd / 64), 1, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // LLATTN_FORCE_SIMT=1 routes bf16 through the SIMT kernels (used by the tests
 // to compare the two implementations of the same math).
 // bf16 matrix [rows, cols] (cols contiguous) with box (64 cols, box_rows rows).
@@ -132,6 +150,19 @@ bool make_btd_map(CUtensorMap* map, const void* base, int B, int T, int d) {
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = v > 0 ? v : 148;
+  }
+  return cache[dev];
+}
+
 bool force_simt() {
   const char* e = std::getenv("LLATTN_FORCE_SIMT");
   return e && e[0] == '1';
@@ -141,7 +172,7 @@ template <int HD>
 cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, const GateEpilogue& ep,
                    cudaStream_t s) {
   CUtensorMap tq, tkv;
-  if (!make_rows_map(&tq, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_rows_map(&tkv, qkv, g.B, g.T, 3 * g.H, HD, 64))
+  if (!make_panel_map(&tq, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_panel_map(&tkv, qkv, g.B, g.T, 3 * g.H, HD, 64))
     return cudaErrorInvalidValue;
   // two query tiles per CTA (ping-pong), one CTA per SM; the fused epilogue
   // stores local_out and mixed through 3-D maps (d, T, B) that clip at T
@@ -160,8 +191,8 @@ template <int HD>
 cudaError_t dq_hd(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta, void* dqkv,
                   cudaStream_t s) {
   CUtensorMap q128, q64, do128, st;
-  if (!make_rows_map(&q128, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_rows_map(&q64, qkv, g.B, g.T, 3 * g.H, HD, 64) ||
-      !make_rows_map(&do128, dl, g.B, g.T, g.H, HD, 128) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, HD, 128))
+  if (!make_panel_map(&q128, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_panel_map(&q64, qkv, g.B, g.T, 3 * g.H, HD, 64) ||
+      !make_panel_map(&do128, dl, g.B, g.T, g.H, HD, 128) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, HD, 128))
     return cudaErrorInvalidValue;
   const int smem = std::max(DqLayout<HD>::BYTES + 1024, 116 * 1024);
   cudaError_t e = cudaFuncSetAttribute(local_dq_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -175,14 +206,15 @@ template <int HD>
 cudaError_t dkv_hd(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta, void* dqkv,
                    cudaStream_t s) {
   CUtensorMap q128, q64, do64, st;
-  if (!make_rows_map(&q128, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_rows_map(&q64, qkv, g.B, g.T, 3 * g.H, HD, 64) ||
-      !make_rows_map(&do64, dl, g.B, g.T, g.H, HD, 64) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, HD, 128))
+  if (!make_panel_map(&q128, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_panel_map(&q64, qkv, g.B, g.T, 3 * g.H, HD, 64) ||
+      !make_panel_map(&do64, dl, g.B, g.T, g.H, HD, 64) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, HD, 128))
     return cudaErrorInvalidValue;
   const int smem = std::max(DkvLayout<HD>::BYTES + 1024, 116 * 1024);
   cudaError_t e = cudaFuncSetAttribute(local_dkv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(g.H, cdiv(g.T, BM), g.B);
-  local_dkv_tc_kernel<HD><<<grid, 320, smem, s>>>(q128, q64, do64, st, g, lse, delta);
+  // persistent: one CTA per SM walks the (h, key tile, b) units
+  const int n_units = g.H * cdiv(g.T, BM) * g.B;
+  local_dkv_tc_kernel<HD><<<std::min(n_units, sm_count()), 320, smem, s>>>(q128, q64, do64, st, g, lse, delta, n_units);
   return cudaGetLastError();
 }
 

@@ -94,11 +94,8 @@ __global__ void __launch_bounds__(320, 1)
       prefetch_tmap(&tm_qkv64);
       prefetch_tmap(&tm_do128);
       mbar_expect_tx(&bars[DQ_Q], 2 * L::QTILE);
-#pragma unroll
-      for (int p = 0; p < HD / 64; ++p) {
-        tma_load_4d(&tm_qkv128, &bars[DQ_Q], smem + L::Q + p * L::QPANEL, p * 64, h, q0, b);
-        tma_load_4d(&tm_do128, &bars[DQ_Q], smem + L::DO + p * L::QPANEL, p * 64, h, q0, b);
-      }
+      tma_load_tile(&tm_qkv128, &bars[DQ_Q], smem + L::Q, q0, h, b);
+      tma_load_tile(&tm_do128, &bars[DQ_Q], smem + L::DO, q0, h, b);
       for (int j = 0; j < nk; ++j) {
         const int s = j % L::NKS;
         if (j >= L::NKS && !mbar_wait(&bars[DQ_KVE + s], ((j / L::NKS) - 1) & 1, abort, &g_fault_word)) {
@@ -107,15 +104,9 @@ __global__ void __launch_bounds__(320, 1)
         }
         const int k0 = kbase + j * BNK;
         mbar_expect_tx(&bars[DQ_K + s], L::KTILE);
-#pragma unroll
-        for (int p = 0; p < HD / 64; ++p)
-          tma_load_4d(&tm_qkv64, &bars[DQ_K + s], smem + L::K + s * L::KTILE + p * L::KPANEL, p * 64, g.H + h, k0,
-                      b);
+        tma_load_tile(&tm_qkv64, &bars[DQ_K + s], smem + L::K + s * L::KTILE, k0, g.H + h, b);
         mbar_expect_tx(&bars[DQ_V + s], L::KTILE);
-#pragma unroll
-        for (int p = 0; p < HD / 64; ++p)
-          tma_load_4d(&tm_qkv64, &bars[DQ_V + s], smem + L::V + s * L::KTILE + p * L::KPANEL, p * 64,
-                      2 * g.H + h, k0, b);
+        tma_load_tile(&tm_qkv64, &bars[DQ_V + s], smem + L::V + s * L::KTILE, k0, 2 * g.H + h, b);
         issued = j + 1;
       }
       if (*abort) {
@@ -279,7 +270,13 @@ __global__ void __launch_bounds__(320, 1)
 }
 
 // ---------------------------------------------------------------------------
-// dk, dv
+// dk, dv: persistent. Each CTA walks work units u = blockIdx.x + k * gridDim.x
+// (unit = 128 keys of one (b, h), heads fastest). The Q/dO ring and the
+// S^T/dP^T buffers run on counters that continue across units, so the next
+// unit's first query tiles load while the current one finishes; its K/V load
+// once the current unit's dK/dV, staged in the K/V region, have been stored.
+// Launch-aligned waves of non-persistent CTAs all load at once and all store
+// at once; a persistent walk spreads both over time.
 
 template <int HD>
 struct DkvLayout {
@@ -289,52 +286,67 @@ struct DkvLayout {
   static constexpr int QPANEL = BNQ * 128;         // 64-query panel (8 KB)
   static constexpr int KTILE = BM * HD * 2;
   static constexpr int QTILE = BNQ * HD * 2;
-  static constexpr int K = 0;
-  static constexpr int V = K + KTILE;
+  static constexpr int K = 0;                      // K tile, then dK staging
+  static constexpr int V = K + KTILE;              // V tile, then dV staging
   static constexpr int Q = V + KTILE;              // NQS stages
   static constexpr int DO = Q + NQS * QTILE;       // NQS stages
-  static constexpr int VEC = DO + NQS * QTILE;     // per compute warp: {lse2, D}[32]
+  static constexpr int VEC = DO + NQS * QTILE;     // per compute warp: {-lse*log2e, D}[32]
   static constexpr int BAR = VEC + 8 * 2 * 32 * 4;
   static constexpr int BYTES = BAR + 256;
 };
 
-// barriers: K/V loaded; per Q/dO stage loaded / released; per TMEM buffer
-// S^T,dP^T ready / P^T,dS^T written / dV,dK MMAs done
-enum { KV_KV = 0, KV_QD = 1, KV_QDE = 5, KV_SP = 9, KV_PD = 11, KV_DKV = 13, KV_NB = 15 };
+// barriers: K/V loaded / K,V region free again (dK, dV stores have read it);
+// per Q/dO stage loaded / released; per TMEM buffer S^T,dP^T ready /
+// P^T,dS^T written; dV,dK complete / read out of TMEM; dK,dV staged
+enum {
+  KV_KV = 0, KV_KVE = 1, KV_QD = 2, KV_QDE = 6, KV_SP = 10, KV_PD = 12, KV_ACC = 14, KV_ACCE = 15, KV_STG = 16,
+  KV_NB = 17
+};
+
+struct DkvUnit {
+  int h, k0, b, tfirst, tlast, nq;
+};
+__device__ __forceinline__ DkvUnit dkv_unit(const Geom& g, int u) {
+  DkvUnit t;
+  const int nkt = cdiv(g.T, BM);
+  t.h = u % g.H;
+  const int r = u / g.H;
+  t.k0 = (r % nkt) * BM;
+  t.b = r / nkt;
+  t.tfirst = t.k0 + 1;
+  t.tlast = min(g.T - 1, t.k0 + BM - 1 + g.W);
+  t.nq = t.tlast >= t.tfirst ? (t.tlast - t.tfirst + 64) / 64 : 0;
+  return t;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(320, 1)
     local_dkv_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv128, const __grid_constant__ CUtensorMap tm_qkv64,
                         const __grid_constant__ CUtensorMap tm_do64, const __grid_constant__ CUtensorMap tm_st,
-                        Geom g, const float* __restrict__ lse, const float* __restrict__ delta) {
+                        Geom g, const float* __restrict__ lse, const float* __restrict__ delta, int n_units) {
   using L = DkvLayout<HD>;
-  constexpr int BNQ = L::BNQ;
+  constexpr int BNQ = L::BNQ, NQS = L::NQS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + KV_NB);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // heads fastest: CTAs that run together cover whole token rows of qkv
-  const int h = blockIdx.x, b = blockIdx.z;
-  const int k0 = blockIdx.y * BM;
-  const int tfirst = k0 + 1;
-  const int tlast = min(g.T - 1, k0 + BM - 1 + g.W);
-  const int nq = tlast >= tfirst ? (tlast - tfirst + BNQ) / BNQ : 0;
 
-  if (threadIdx.x == 0) LLATTN_TRACE_K(2, 0);
   if (threadIdx.x == 0) {
     mbar_init(&bars[KV_KV], 1);
-    for (int s = 0; s < L::NQS; ++s) {
+    mbar_init(&bars[KV_KVE], 1);
+    for (int s = 0; s < NQS; ++s) {
       mbar_init(&bars[KV_QD + s], 1);
       mbar_init(&bars[KV_QDE + s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars[KV_SP + s], 1);
       mbar_init(&bars[KV_PD + s], 2 * BM);
-      mbar_init(&bars[KV_DKV + s], 1);
     }
+    mbar_init(&bars[KV_ACC], 1);
+    mbar_init(&bars[KV_ACCE], 2 * BM);
+    mbar_init(&bars[KV_STG], 2 * BM);
     *abort = 0;
     fence_barrier_init();
   }
@@ -347,58 +359,63 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0) LLATTN_TRACE_K(2, 1);
   // S^T at [0,64) / [64,128), dP^T at [128,192) / [192,256), dV, dK after.
   // P^T and dS^T (bf16) are written back over the first 16 of each 32
   // S^T / dP^T columns that produced them and feed the dV / dK MMAs from TMEM.
   const uint32_t tDV = tmem + 256, tDK = tmem + 256 + HD;
 
   if (warp == 0) {
-    if (lane == 0 && nq > 0) {
-      int issued = 0;
+    if (lane == 0) {
       prefetch_tmap(&tm_qkv128);
       prefetch_tmap(&tm_qkv64);
       prefetch_tmap(&tm_do64);
-      mbar_expect_tx(&bars[KV_KV], 2 * L::KTILE);
-#pragma unroll
-      for (int p = 0; p < HD / 64; ++p) {
-        tma_load_4d(&tm_qkv128, &bars[KV_KV], smem + L::K + p * L::KPANEL, p * 64, g.H + h, k0, b);
-        tma_load_4d(&tm_qkv128, &bars[KV_KV], smem + L::V + p * L::KPANEL, p * 64, 2 * g.H + h, k0, b);
-      }
-      for (int i = 0; i < nq; ++i) {
-        const int s = i % L::NQS;
-        if (i >= L::NQS && !mbar_wait(&bars[KV_QDE + s], ((i / L::NQS) - 1) & 1, abort, &g_fault_word)) {
-          raise_fault(kFaultProducer, abort);
-          break;
-        }
-        const int t0 = tfirst + i * BNQ;
+      prefetch_tmap(&tm_st);
+      int q = 0, n = 0, issued_q = 0, issued_kv = 0;
+      bool ok = true;
+      auto load_qd = [&](const DkvUnit& t, int i) -> bool {
+        const int gq = q + i, s = gq % NQS;
+        if (gq >= NQS && !mbar_wait(&bars[KV_QDE + s], ((gq / NQS) - 1) & 1, abort, &g_fault_word)) return false;
+        const int t0 = t.tfirst + i * BNQ;
         mbar_expect_tx(&bars[KV_QD + s], 2 * L::QTILE);
-#pragma unroll
-        for (int p = 0; p < HD / 64; ++p) {
-          tma_load_4d(&tm_qkv64, &bars[KV_QD + s], smem + L::Q + s * L::QTILE + p * L::QPANEL, p * 64, h, t0, b);
-          tma_load_4d(&tm_do64, &bars[KV_QD + s], smem + L::DO + s * L::QTILE + p * L::QPANEL, p * 64, h, t0, b);
-        }
-        issued = i + 1;
+        tma_load_tile(&tm_qkv64, &bars[KV_QD + s], smem + L::Q + s * L::QTILE, t0, t.h, t.b);
+        tma_load_tile(&tm_do64, &bars[KV_QD + s], smem + L::DO + s * L::QTILE, t0, t.h, t.b);
+        issued_q = gq + 1;
+        return true;
+      };
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++n) {
+        const DkvUnit t = dkv_unit(g, u);
+        // this unit's first query tiles may load while the previous unit finishes
+        const int pre = min(t.nq, NQS);
+        for (int i = 0; ok && i < pre; ++i) ok = load_qd(t, i);
+        if (!ok) break;
+        if (n > 0 && !(ok = mbar_wait(&bars[KV_KVE], (n - 1) & 1, abort, &g_fault_word))) break;
+        mbar_expect_tx(&bars[KV_KV], 2 * L::KTILE);
+        tma_load_tile(&tm_qkv128, &bars[KV_KV], smem + L::K, t.k0, g.H + t.h, t.b);
+        tma_load_tile(&tm_qkv128, &bars[KV_KV], smem + L::V, t.k0, 2 * g.H + t.h, t.b);
+        issued_kv = n + 1;
+        for (int i = pre; ok && i < t.nq; ++i) ok = load_qd(t, i);
+        q += t.nq;
       }
-      if (*abort) {
+      if (!ok) {
+        raise_fault(kFaultProducer, abort);
+        // let the copies already issued land before the CTA can exit
         volatile int none = 0;
         volatile unsigned gnone = 0;
-        mbar_wait(&bars[KV_KV], 0, &none, &gnone, 100000000ull);
-        for (int i = issued - L::NQS < 0 ? 0 : issued - L::NQS; i < issued; ++i)
-          mbar_wait(&bars[KV_QD + i % L::NQS], (i / L::NQS) & 1, &none, &gnone, 100000000ull);
+        if (issued_kv > 0) mbar_wait(&bars[KV_KV], (issued_kv - 1) & 1, &none, &gnone, 100000000ull);
+        for (int gq = issued_q - NQS < 0 ? 0 : issued_q - NQS; gq < issued_q; ++gq)
+          mbar_wait(&bars[KV_QD + gq % NQS], (gq / NQS) & 1, &none, &gnone, 100000000ull);
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && nq > 0) {
+    if (lane == 0) {
       constexpr uint32_t idSP = idesc_bf16_f32(BM, BNQ, false, false);  // K Q^T, V dO^T
       constexpr uint32_t idKV = idesc_bf16_f32(BM, HD, false, true);    // P^T dO, dS^T Q
       const uint32_t k_addr = smem_u32(smem + L::K), v_addr = smem_u32(smem + L::V);
-      bool ok = mbar_wait(&bars[KV_KV], 0, abort, &g_fault_word);
-      LLATTN_TRACE_K(2, 2);
-      auto issue_sp = [&](int i) -> bool {
-        const int s = i & 1, sq = i % L::NQS;
-        if (!mbar_wait(&bars[KV_QD + sq], (i / L::NQS) & 1, abort, &g_fault_word)) return false;
-        if (i < 12) LLATTN_TRACE_K(2, 24 + i);
+      int q = 0, n = 0, m = 0;  // m: units with at least one query tile
+      bool ok = true;
+      auto issue_sp = [&](int gq) -> bool {
+        const int s = gq & 1, sq = gq % NQS;
+        if (!mbar_wait(&bars[KV_QD + sq], (gq / NQS) & 1, abort, &g_fault_word)) return false;
         tc_fence_after();
         const uint32_t q_addr = smem_u32(smem + L::Q + sq * L::QTILE);
         const uint32_t do_addr = smem_u32(smem + L::DO + sq * L::QTILE);
@@ -414,25 +431,40 @@ __global__ void __launch_bounds__(320, 1)
         mma_commit(&bars[KV_SP + s]);
         return true;
       };
-      if (ok) ok = issue_sp(0);
-      for (int i = 0; ok && i < nq; ++i) {
-        if (i + 1 < nq && !(ok = issue_sp(i + 1))) break;
-        const int s = i & 1, sq = i % L::NQS;
-        if (!(ok = mbar_wait(&bars[KV_PD + s], (i >> 1) & 1, abort, &g_fault_word))) break;
-        if (i < 12) LLATTN_TRACE_K(2, 36 + i);
+      // S^T(i+1) is issued before dV/dK(i): the softmax warps wait for it
+      // next, and it may start once dV/dK(i-1) are issued (they read the
+      // P^T columns S^T(i+1) overwrites)
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++n) {
+        const DkvUnit t = dkv_unit(g, u);
+        if (!(ok = mbar_wait(&bars[KV_KV], n & 1, abort, &g_fault_word))) break;
         tc_fence_after();
-        const uint32_t q_addr = smem_u32(smem + L::Q + sq * L::QTILE);
-        const uint32_t do_addr = smem_u32(smem + L::DO + sq * L::QTILE);
+        if (t.nq > 0) {
+          ok = issue_sp(q);
+          for (int i = 0; ok && i < t.nq; ++i) {
+            const int gq = q + i, s = gq & 1, sq = gq % NQS;
+            if (i + 1 < t.nq && !(ok = issue_sp(gq + 1))) break;
+            if (!(ok = mbar_wait(&bars[KV_PD + s], (gq >> 1) & 1, abort, &g_fault_word))) break;
+            // the first dV/dK MMA overwrites the accumulators: the previous
+            // unit's epilogue must have read them
+            if (i == 0 && m > 0 && !(ok = mbar_wait(&bars[KV_ACCE], (m - 1) & 1, abort, &g_fault_word))) break;
+            tc_fence_after();
+            const uint32_t q_addr = smem_u32(smem + L::Q + sq * L::QTILE);
+            const uint32_t do_addr = smem_u32(smem + L::DO + sq * L::QTILE);
 #pragma unroll
-        for (int kk = 0; kk < BNQ / 16; ++kk) {
-          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          // queries 16kk..16kk+15: packed in the half (kk/2) written by warp group kk/2
-          const uint32_t acol = (uint32_t)(s * BNQ + (kk >> 1) * 32 + (kk & 1) * 8);
-          mma_bf16_ts(tDV, tmem + acol, desc_sw128(do_addr + kk * 2048, L::QPANEL, 1024), idKV, acc);
-          mma_bf16_ts(tDK, tmem + 128 + acol, desc_sw128(q_addr + kk * 2048, L::QPANEL, 1024), idKV, acc);
+            for (int kk = 0; kk < BNQ / 16; ++kk) {
+              const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+              // queries 16kk..16kk+15: packed in the half (kk/2) written by warp group kk/2
+              const uint32_t acol = (uint32_t)(s * BNQ + (kk >> 1) * 32 + (kk & 1) * 8);
+              mma_bf16_ts(tDV, tmem + acol, desc_sw128(do_addr + kk * 2048, L::QPANEL, 1024), idKV, acc);
+              mma_bf16_ts(tDK, tmem + 128 + acol, desc_sw128(q_addr + kk * 2048, L::QPANEL, 1024), idKV, acc);
+            }
+            mma_commit(&bars[KV_QDE + sq]);
+          }
+          if (!ok) break;
+          mma_commit(&bars[KV_ACC]);
+          ++m;
         }
-        mma_commit(&bars[KV_DKV + s]);
-        mma_commit(&bars[KV_QDE + sq]);
+        q += t.nq;
       }
       if (!ok) raise_fault(kFaultMma, abort);
     }
@@ -441,107 +473,103 @@ __global__ void __launch_bounds__(320, 1)
     const int half = (warp - 2) >> 2;
     const int row = 32 * (warp & 3) + lane;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
-    const int j = k0 + row;            // this thread's key
-    const bool valid = j < g.T;
     const float sc = g.scale * kLog2e;
-    // queries that see key j form one range: t in (j, j+W] with qs(t) <= j+W-1,
-    // i.e. t < the end of the bsL-block holding j+W-1 (mask of models.py:286-292)
-    const int t_hi = min(min(j + g.W, ((j + g.W - 1) / g.bsL + 1) * g.bsL - 1), g.T - 1);  // inclusive
-    // per-warp copy of lse2 and D for this warp's 32 query columns
     float* v_lse = reinterpret_cast<float*>(smem + L::VEC) + (warp - 2) * 64;
     float* v_d = v_lse + 32;
-    const float* lse_b = lse + ((int64_t)b * g.H + h) * g.T;
-    const float* d_b = delta + ((int64_t)b * g.H + h) * g.T;
+    int q = 0, n = 0, m = 0;
     bool ok = true;
-    // this lane's -lse*log2(e) / D for the next query tile, loaded one tile ahead
-    auto fetch = [&](int i, float& l2, float& dd) {
-      const int t = tfirst + i * BNQ + half * 32 + lane;
-      const bool tv = i < nq && t <= tlast;
-      l2 = tv ? -__ldg(lse_b + t) * kLog2e : -INFINITY;
-      dd = tv ? __ldg(d_b + t) : 0.f;
-    };
-    float nl2, nd;
-    fetch(0, nl2, nd);
-    for (int i = 0; i < nq; ++i) {
-      const int s = i & 1;
-      const int t0 = tfirst + i * BNQ;
-      __syncwarp();
-      v_lse[lane] = nl2;
-      v_d[lane] = nd;
-      __syncwarp();
-      fetch(i + 1, nl2, nd);
-      // S^T(i) done implies the dV/dK MMAs of tile i-2 (issued earlier) have
-      // finished reading the P^T / dS^T columns this pass overwrites
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_SP + s], (i >> 1) & 1, abort, &g_fault_word));
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++n) {
+      const DkvUnit t = dkv_unit(g, u);
+      const int j = t.k0 + row;  // this thread's key
+      const bool valid = j < g.T;
+      // queries that see key j form one range: t in (j, j+W] with qs(t) <= j+W-1,
+      // i.e. t < the end of the bsL-block holding j+W-1 (mask of models.py:286-292)
+      const int t_hi = min(min(j + g.W, ((j + g.W - 1) / g.bsL + 1) * g.bsL - 1), g.T - 1);  // inclusive
+      const float* lse_b = lse + ((int64_t)t.b * g.H + t.h) * g.T;
+      const float* d_b = delta + ((int64_t)t.b * g.H + t.h) * g.T;
+      // this lane's -lse*log2(e) / D for the next query tile, loaded one tile ahead
+      auto fetch = [&](int i, float& l2, float& dd) {
+        const int tq = t.tfirst + i * BNQ + half * 32 + lane;
+        const bool tv = i < t.nq && tq <= t.tlast;
+        l2 = tv ? -__ldg(lse_b + tq) * kLog2e : -INFINITY;
+        dd = tv ? __ldg(d_b + tq) : 0.f;
+      };
+      float nl2, nd;
+      fetch(0, nl2, nd);
+      for (int i = 0; i < t.nq; ++i) {
+        const int gq = q + i, s = gq & 1;
+        const int t0 = t.tfirst + i * BNQ;
+        __syncwarp();
+        v_lse[lane] = nl2;
+        v_d[lane] = nd;
+        __syncwarp();
+        fetch(i + 1, nl2, nd);
+        // S^T(gq) done implies the dV/dK MMAs of tile gq-2 (issued earlier)
+        // have finished reading the P^T / dS^T columns this pass overwrites
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_SP + s], (gq >> 1) & 1, abort, &g_fault_word));
+        if (!ok) break;
+        tc_fence_after();
+        const int c_lo = j + 1 - t0 - half * 32, c_hi = valid ? t_hi - t0 - half * 32 + 1 : -1;  // in [0, 32)
+        {
+          const int cc = half;
+          uint32_t rs[32], rp[32];
+          tmem_ld32(tmem + lane_off + s * BNQ + cc * 32, rs);
+          tmem_ld32(tmem + lane_off + 128 + s * BNQ + cc * 32, rp);
+          tmem_ld_wait();
+          uint32_t pp[16], pd[16];
+          // interior tiles (every key of the warp sees all 32 queries) skip the mask
+          const bool full = __all_sync(0xffffffffu, c_lo <= 0 && c_hi >= 32);
+          const float4* nl4 = reinterpret_cast<const float4*>(v_lse);
+          const float4* d4 = reinterpret_cast<const float4*>(v_d);
+          const uint64_t sc2 = f2_pack(sc, sc);
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 nl = nl4[q4], dd = d4[q4];
+#pragma unroll
+            for (int uu = 0; uu < 2; ++uu) {
+              const int c = 4 * q4 + 2 * uu;
+              float x0, x1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sc2,
+                               uu == 0 ? f2_pack(nl.x, nl.y) : f2_pack(nl.z, nl.w)),
+                        x0, x1);
+              float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+              if (!full) {
+                p0 = (c >= c_lo && c < c_hi) ? p0 : 0.f;
+                p1 = (c + 1 >= c_lo && c + 1 < c_hi) ? p1 : 0.f;
+              }
+              const uint64_t ds = f2_mul(f2_pack(p0, p1),
+                                         f2_sub(f2_pack(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])),
+                                                uu == 0 ? f2_pack(dd.x, dd.y) : f2_pack(dd.z, dd.w)));
+              float d0, d1;
+              f2_unpack(ds, d0, d1);
+              pp[c / 2] = pack_bf16(p0, p1);
+              pd[c / 2] = pack_bf16(d0, d1);
+            }
+          }
+          tmem_st16(tmem + lane_off + s * BNQ + cc * 32, pp);
+          tmem_st16(tmem + lane_off + 128 + s * BNQ + cc * 32, pd);
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        mbar_arrive(&bars[KV_PD + s]);
+      }
+      if (!ok) break;
+      // epilogue: dK (half 0, scaled) / dV (half 1) as bf16 128-byte-swizzled
+      // 64-column panels over the K / V tiles (free once the unit's MMAs are
+      // done), then TMA stores (rows >= T clipped by the map)
+      if (t.nq > 0)
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_ACC], m & 1, abort, &g_fault_word));
+      else  // no MMAs: only make sure the unit's K/V copy has landed before overwriting it
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_KV], n & 1, abort, &g_fault_word));
       if (!ok) break;
       tc_fence_after();
-      const int c_lo = j + 1 - t0 - half * 32, c_hi = valid ? t_hi - t0 - half * 32 + 1 : -1;  // in [0, 32)
-      {
-        const int cc = half;
-        uint32_t rs[32], rp[32];
-        tmem_ld32(tmem + lane_off + s * BNQ + cc * 32, rs);
-        tmem_ld32(tmem + lane_off + 128 + s * BNQ + cc * 32, rp);
-        tmem_ld_wait();
-        if (row == 0 && half == 0 && i < 6) LLATTN_TRACE_K(2, 44 + i);
-        uint32_t pp[16], pd[16];
-        // interior tiles (every key of the warp sees all 32 queries) skip the mask
-        const bool full = __all_sync(0xffffffffu, c_lo <= 0 && c_hi >= 32);
-        const float4* nl4 = reinterpret_cast<const float4*>(v_lse);
-        const float4* d4 = reinterpret_cast<const float4*>(v_d);
-        const uint64_t sc2 = f2_pack(sc, sc);
-#pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4) {
-          const float4 nl = nl4[q4], dd = d4[q4];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int c = 4 * q4 + 2 * u;
-            float x0, x1;
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sc2,
-                             u == 0 ? f2_pack(nl.x, nl.y) : f2_pack(nl.z, nl.w)),
-                      x0, x1);
-            float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-            if (!full) {
-              p0 = (c >= c_lo && c < c_hi) ? p0 : 0.f;
-              p1 = (c + 1 >= c_lo && c + 1 < c_hi) ? p1 : 0.f;
-            }
-            const uint64_t ds = f2_mul(f2_pack(p0, p1),
-                                       f2_sub(f2_pack(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])),
-                                              u == 0 ? f2_pack(dd.x, dd.y) : f2_pack(dd.z, dd.w)));
-            float d0, d1;
-            f2_unpack(ds, d0, d1);
-            pp[c / 2] = pack_bf16(p0, p1);
-            pd[c / 2] = pack_bf16(d0, d1);
-          }
-        }
-        if (row == 0 && half == 0 && i < 6) LLATTN_TRACE_K(2, 30 + i);
-        tmem_st16(tmem + lane_off + s * BNQ + cc * 32, pp);
-        tmem_st16(tmem + lane_off + 128 + s * BNQ + cc * 32, pd);
-        tmem_st_wait();
-        if (row == 0 && half == 0 && i < 12) LLATTN_TRACE_K(2, 4 + i);
-      }
-      tc_fence_before();
-      mbar_arrive(&bars[KV_PD + s]);
-      if (row == 0 && half == 0 && i < 12) LLATTN_TRACE_K(2, 16 + i);
-      if (warp == 9 && lane == 31 && i < 6) LLATTN_TRACE_K(2, 54 + i);
-    }
-    if (!ok) raise_fault(kFaultSoftmax, abort);
-    if (ok && nq > 0)
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_DKV + ((nq - 1) & 1)], ((nq - 1) >> 1) & 1, abort,
-                                             &g_fault_word));
-    if (!ok) {
-      raise_fault(kFaultEpilogue, abort);
-    } else {
-      tc_fence_after();
-      if (row == 0 && half == 0) LLATTN_TRACE_K(2, 52);
-      // half 0 stages dK, half 1 dV: bf16, 128-byte-swizzled 64-column panels
-      // in the (now idle) Q/dO ring, stored below by TMA (rows >= T clipped)
-      uint8_t* stage = smem + L::Q + half * (BM * HD * 2);
+      uint8_t* stage = smem + (half == 0 ? L::K : L::V);
       const uint32_t tsrc = (half == 0 ? tDK : tDV) + lane_off;
       const float mul = half == 0 ? g.scale : 1.f;
 #pragma unroll
       for (int cc = 0; cc < HD / 32; ++cc) {
         uint32_t r[32];
-        if (nq > 0) {
+        if (t.nq > 0) {
           tmem_ld32(tsrc + cc * 32, r);
           tmem_ld_wait();
         } else {
@@ -554,29 +582,41 @@ __global__ void __launch_bounds__(320, 1)
           pk[i2] = pack_bf16(__uint_as_float(r[2 * i2]) * mul, __uint_as_float(r[2 * i2 + 1]) * mul);
         uint8_t* prow = stage + (cc >> 1) * (BM * 128) + row * 128;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = (cc & 1) * 4 + q;
+        for (int qq = 0; qq < 4; ++qq) {
+          const int chunk = (cc & 1) * 4 + qq;
           *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) * 16)) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+              make_uint4(pk[4 * qq], pk[4 * qq + 1], pk[4 * qq + 2], pk[4 * qq + 3]);
         }
       }
+      if (t.nq > 0) {
+        tc_fence_before();
+        mbar_arrive(&bars[KV_ACCE]);
+        ++m;
+      }
       fence_async_smem();
-    }
-    // every compute warp reaches this barrier exactly once, faulted or not
-    named_bar_sync(1, 256);
-    if (warp == 2 && lane == 0 && !*abort) {
+      mbar_arrive(&bars[KV_STG]);
+      if (warp == 2 && lane == 0) {
+        // all 256 staging writes done -> store dK, dV; K/V region free once read
+        ok = mbar_wait(&bars[KV_STG], n & 1, abort, &g_fault_word);
+        if (ok) {
 #pragma unroll
-      for (int w = 0; w < 2; ++w)
-#pragma unroll
-        for (int p = 0; p < HD / 64; ++p)
-          tma_store_4d(&tm_st, smem + L::Q + w * (BM * HD * 2) + p * (BM * 128), p * 64, (1 + w) * g.H + h, k0, b);
-      tma_store_commit();
-      tma_store_wait_read();
+          for (int p = 0; p < HD / 64; ++p) {
+            tma_store_4d(&tm_st, smem + L::K + p * (BM * 128), p * 64, g.H + t.h, t.k0, t.b);
+            tma_store_4d(&tm_st, smem + L::V + p * (BM * 128), p * 64, 2 * g.H + t.h, t.k0, t.b);
+          }
+          tma_store_commit();
+          tma_store_wait_read();
+          mbar_arrive(&bars[KV_KVE]);
+        }
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      q += t.nq;
     }
+    if (!ok) raise_fault(kFaultSoftmax, abort);
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) LLATTN_TRACE_K(2, 60);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();

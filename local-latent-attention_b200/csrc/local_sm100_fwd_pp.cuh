@@ -145,11 +145,8 @@ __global__ void __launch_bounds__(320, 1)
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_kv);
       mbar_expect_tx(&bars[PP_Q], 2 * L::QTILE);
-#pragma unroll
-      for (int p = 0; p < HD / 64; ++p) {
-        tma_load_4d(&tm_q, &bars[PP_Q], smem + L::QA + p * L::QPANEL, p * 64, h, q0, b);
-        tma_load_4d(&tm_q, &bars[PP_Q], smem + L::QB + p * L::QPANEL, p * 64, h, q0 + BM, b);
-      }
+      tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QA, q0, h, b);
+      tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QB, q0 + BM, h, b);
       for (int j = 0; j < nk; ++j) {
         const int s = j % L::NST;
         if (j >= L::NST && !mbar_wait(&bars[PP_KVE + s], ((j / L::NST) - 1) & 1, abort, &g_fault_word)) {
@@ -158,14 +155,9 @@ __global__ void __launch_bounds__(320, 1)
         }
         const int k0 = kbase + j * BNK;
         mbar_expect_tx(&bars[PP_K + s], L::KTILE);
-#pragma unroll
-        for (int p = 0; p < HD / 64; ++p)
-          tma_load_4d(&tm_kv, &bars[PP_K + s], smem + L::K + s * L::KTILE + p * L::KPANEL, p * 64, g.H + h, k0, b);
+        tma_load_tile(&tm_kv, &bars[PP_K + s], smem + L::K + s * L::KTILE, k0, g.H + h, b);
         mbar_expect_tx(&bars[PP_V + s], L::KTILE);
-#pragma unroll
-        for (int p = 0; p < HD / 64; ++p)
-          tma_load_4d(&tm_kv, &bars[PP_V + s], smem + L::V + s * L::KTILE + p * L::KPANEL, p * 64, 2 * g.H + h, k0,
-                      b);
+        tma_load_tile(&tm_kv, &bars[PP_V + s], smem + L::V + s * L::KTILE, k0, 2 * g.H + h, b);
         issued = j + 1;
       }
       if (*abort) {
