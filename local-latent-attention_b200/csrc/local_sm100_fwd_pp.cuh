@@ -13,8 +13,14 @@
 //              into that group's freed S columns.
 //   warps 2-5  softmax of tile A, warps 6-9 softmax of tile B: thread = query
 //              row = TMEM lane; online softmax with the window mask, P bf16
-//              into swizzled smem, O rescale in TMEM, fused gate epilogue.
+//              written back over the S columns it came from (the PV MMA
+//              reads it from TMEM), O rescale in TMEM, fused gate epilogue.
 // TMEM: S_A x2 [0,128), S_B x2 [128,256), O_A [256,256+hd), O_B after it.
+// Shared memory: Q_A, Q_B, the K/V ring, and per group the remote-tile
+// operands (lat rows, a copy of the head's W_rout slice) written at kernel
+// start; in the epilogue local_out is staged over the group's Q tile and
+// mixed over its remote-operand region, so the groups never wait for each
+// other.
 
 template <int HD>
 struct FwdPPLayout {
@@ -28,17 +34,13 @@ struct FwdPPLayout {
   static constexpr int NST = 3;                 // K/V ring depth
   static constexpr int K = QB + QTILE;          // NST stages
   static constexpr int V = K + NST * KTILE;     // NST stages
-  static constexpr int PA = V + NST * KTILE;      // 2 buffers of 128 x 64 bf16 per group
-  static constexpr int PB = PA + 2 * BM * BNK * 2;
-  static constexpr int END = PB + 2 * BM * BNK * 2;
-  // remote-tile operands (128 x 64 lat rows per group, hd x 64 W_rout slice):
-  // for hd = 128 they reuse each group's Q tile once its S MMAs are done,
-  // for hd = 64 they get their own region
-  static constexpr int LATA = HD == 128 ? QA : END;
-  static constexpr int WR = HD == 128 ? QA + BM * 128 : END + BM * 128;
-  static constexpr int LATB = HD == 128 ? QB : END + BM * 128 + HD * 128;
-  static constexpr int BAR = HD == 128 ? END : LATB + BM * 128;
+  // per group x at X + x * XS: lat rows (128 x 64 bf16) then W_rout[h] (hd x 64)
+  static constexpr int X = V + NST * KTILE;
+  static constexpr int XS = BM * 128 + HD * 128;
+  static constexpr int CST = X + 2 * XS;        // b_rout[h], g_local, g_remote (hd floats each)
+  static constexpr int BAR = CST + 3 * HD * 4;
   static constexpr int BYTES = BAR + 256;
+  static_assert(XS >= QTILE, "mixed tile staged over the remote operands");
 };
 
 // per group g: S[2], P[2] (softmax arrivals), O[2] (PV done) — one barrier
@@ -179,8 +181,8 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       // Event-driven issue: each pass tests (without blocking) what has
       // become ready and issues it, so neither group waits for the other.
-      //   S_x(i): K tile loaded, and S buffer i&1 free (P_x(i-2) landed,
-      //           which holds once PV_x(i-2) was issued: i <= npv + 1)
+      //   S_x(i): K tile loaded, and S buffer i&1 free: PV_x(i-2), which
+      //           reads P_x(i-2) from those columns, issued (i <= npv + 1)
       //   PV_x(i): P_x(i) landed and V tile loaded
       //   R_x: after the group's last PV, once its lat / W_rout rows are in
       // A K/V stage is released (KVE commit) once every group using the tile
@@ -223,12 +225,13 @@ __global__ void __launch_bounds__(320, 1)
             if (mbar_test_wait(&bars[PP_P + 2 * x + (i & 1)], (i >> 1) & 1) &&
                 mbar_test_wait(&bars[PP_V + st], (j / L::NST) & 1)) {
               tc_fence_after();
-              const uint32_t pa = smem_u32(smem + (x ? L::PB : L::PA) + (i & 1) * BM * BNK * 2);
+              // P (bf16, packed two per column) over the first 32 columns of S buffer i&1
+              const uint32_t pa = tmem + x * 128 + (i & 1) * BNK;
               const uint32_t va = smem_u32(smem + L::V + st * L::KTILE);
 #pragma unroll
               for (int kk = 0; kk < BNK / 16; ++kk)
-                mma_bf16(tmem + 256 + x * HD, desc_sw128(pa + kk * 32, 16, 1024),
-                         desc_sw128(va + kk * 2048, L::KPANEL, 1024), idO, (i > 0 || kk > 0) ? 1u : 0u);
+                mma_bf16_ts(tmem + 256 + x * HD, pa + kk * 8, desc_sw128(va + kk * 2048, L::KPANEL, 1024), idO,
+                            (i > 0 || kk > 0) ? 1u : 0u);
               mma_commit(&bars[PP_O + 2 * x + (i & 1)]);
               ++npv[x];
               progress = true;
@@ -236,9 +239,9 @@ __global__ void __launch_bounds__(320, 1)
           }
           // R
           if (fuse && !r_done[x] && npv[x] == nx[x]) {
-            if (mbar_test_wait(&bars[PP_LW + 0], 0) && (x == 0 || mbar_test_wait(&bars[PP_LW + 1], 0))) {
+            if (mbar_test_wait(&bars[PP_LW + x], 0)) {
               tc_fence_after();
-              const uint32_t la = smem_u32(smem + (x ? L::LATB : L::LATA)), wa = smem_u32(smem + L::WR);
+              const uint32_t la = smem_u32(smem + L::X + x * L::XS), wa = la + BM * 128;
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)
                 mma_bf16(tmem + x * 128, desc_sw128(la + kk * 32, 16, 1024), desc_sw128(wa + kk * 32, 16, 1024), idR,
@@ -283,34 +286,36 @@ __global__ void __launch_bounds__(320, 1)
     const int lo = valid ? local_lo(g, t) : 0x7fffffff;
     const float sc = g.scale * kLog2e;
     float m = -INFINITY, l = 0.f;  // m: reference max (log2 domain) of P and O
-    uint8_t* prow = smem + (grp ? L::PB : L::PA) + row * 128;
     const uint32_t tS = tmem + grp * 128, tO = tmem + 256 + grp * HD, tR = tmem + grp * 128;
+    uint8_t* xreg = smem + L::X + grp * L::XS;  // this group's lat rows, then W_rout[h]
+    float* cst = reinterpret_cast<float*>(smem + L::CST);
     bool ok = true;
-    // remote-tile operands: this row's lat row (and, in group A, a row of
-    // W_rout's head slice). With hd = 128 they go into this group's Q tile,
-    // so they are written after the group's last S MMA (or after Q landed).
-    auto write_remote_operands = [&]() {
+    // remote-tile operands, written up front: this row's lat row, row `row`
+    // of W_rout's head slice (each group its own copy), and (group A) the
+    // per-column constants of the epilogue
+    if (fuse) {
       const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.lat) +
                                                         ((int64_t)b * g.Tq + (valid ? t / g.qbs : 0)) * 64);
-      uint8_t* dl_ = smem + (grp ? L::LATB : L::LATA) + row * 128;
+      uint8_t* dl_ = xreg + row * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dl_ + ((c ^ (row & 7)) * 16)) = src[c];
-      if (grp == 0 && row < HD) {
+      if (row < HD) {
         const uint4* wsrc =
             reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.w_rout) + ((int64_t)h * HD + row) * 64);
-        uint8_t* wd = smem + L::WR + row * 128;
+        uint8_t* wd = xreg + BM * 128 + row * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(wd + ((c ^ (row & 7)) * 16)) = wsrc[c];
+        if (grp == 0) {
+          cst[row] = ep.b_rout[(int64_t)h * HD + row];
+          cst[HD + row] = ep.g_local[row];
+          cst[2 * HD + row] = ep.g_remote[row];
+        }
       }
       fence_async_smem();
       mbar_arrive(&bars[PP_LW + grp]);
-    };
-    if (grp == 1 && !has_b) {
-      if (fuse) {  // group A's R still waits on this group's arrival
-        if (nk > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_Q], 0, abort, &g_fault_word));
-        write_remote_operands();
-      }
-    } else {
+    }
+    if (!(grp == 1 && !has_b)) {
+      const uint64_t sc2 = f2_pack(sc, sc);
       for (int i = 0; ok && i < n_mine; ++i) {
         const int j = tt.first + i;
         ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_S + 2 * grp + (i & 1)], (i >> 1) & 1, abort, &g_fault_word));
@@ -343,14 +348,11 @@ __global__ void __launch_bounds__(320, 1)
         const float m_new = move ? mx : m;
         const float alpha = (move && m != -INFINITY) ? fast_exp2(m - m_new) : 1.f;
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        // P buffer (i&1) is free once PV(i-2) has read it
-        if (i >= 2) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_O + 2 * grp + (i & 1)], ((i - 2) >> 1) & 1, abort,
-                                                 &g_fault_word));
-          if (!ok) break;
-        }
-        uint8_t* pbuf = prow + (i & 1) * BM * BNK * 2;
-        float psum = 0.f;
+        const uint64_t nm2 = f2_pack(-m_use, -m_use);
+        // P(i) goes over the S(i) columns: the PV MMA of tile i-2, the last
+        // reader of this buffer, was issued before S(i) (whose completion
+        // this thread has seen), so it is done
+        uint64_t ps2 = f2_pack(0.f, 0.f);
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
           uint32_t pk[16];
@@ -359,24 +361,21 @@ __global__ void __launch_bounds__(320, 1)
             const int c = cc * 32 + 2 * q;
             const float s0 = __uint_as_float(cc ? r1[2 * q] : r0[2 * q]);
             const float s1 = __uint_as_float(cc ? r1[2 * q + 1] : r0[2 * q + 1]);
-            float p0 = fast_exp2(fmaf(s0, sc, -m_use));
-            float p1 = fast_exp2(fmaf(s1, sc, -m_use));
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(s0, s1), sc2, nm2), x0, x1);
+            float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
             if (!full) {
               p0 = (c >= c_lo && c < c_hi) ? p0 : 0.f;
               p1 = (c + 1 >= c_lo && c + 1 < c_hi) ? p1 : 0.f;
             }
-            psum += p0 + p1;
+            ps2 = f2_add(ps2, f2_pack(p0, p1));
             pk[q] = pack_bf16(p0, p1);
           }
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int chunk = cc * 4 + q;
-            *reinterpret_cast<uint4*>(pbuf + (((chunk & 7) ^ (row & 7)) * 16)) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          }
+          tmem_st16(tsrc + cc * 16, pk);
         }
-        fence_async_smem();
-        l = l * alpha + psum;
+        float psa, psb;
+        f2_unpack(ps2, psa, psb);
+        l = l * alpha + (psa + psb);
         m = m_new;
         // rare: rescale O, after PV(i-1) has completed
         if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -393,22 +392,21 @@ __global__ void __launch_bounds__(320, 1)
             for (int q = 0; q < 32; ++q) r[q] = __float_as_uint(__uint_as_float(r[q]) * alpha);
             tmem_st32(tO + lane_off + cc * 32, r);
           }
-          tmem_st_wait();
         }
+        tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bars[PP_P + 2 * grp + (i & 1)]);
         if (row == 0) LLATTN_TRACE_K(1, 16 + grp * 24 + i);
       }
       if (!ok) raise_fault(kFaultSoftmax, abort);
-      if (ok && fuse) {
-        // all of this group's S MMAs are done (or, without tiles, Q landed)
-        if (n_mine == 0 && nk > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_Q], 0, abort, &g_fault_word));
-        write_remote_operands();
-      }
       if (ok && n_mine > 0)
         ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_O + 2 * grp + ((n_mine - 1) & 1)], ((n_mine - 1) >> 1) & 1,
                                                abort, &g_fault_word));
-      if (ok && fuse) ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_R + grp], 0, abort, &g_fault_word));
+      if (ok && fuse) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_R + grp], 0, abort, &g_fault_word));
+        // the per-column constants written by group A
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_LW + 0], 0, abort, &g_fault_word));
+      }
       if (row == 0) LLATTN_TRACE_K(1, 52 + 2 * grp);
       if (!ok) {
         raise_fault(kFaultEpilogue, abort);
@@ -418,80 +416,79 @@ __global__ void __launch_bounds__(320, 1)
         const float inv = l > 0.f ? 1.f / l : 0.f;
         bf16* dst = local_out + ((int64_t)b * g.T + (valid ? t : 0)) * g.d + (int64_t)h * HD;
         if (fuse) {
-          // one pass over TMEM: gate logits, and the bf16 local row and remote
-          // row (+ bias) staged in smem (local: this group's P buffers; remote:
-          // its Q tile, free once the remote MMAs have read the operands there)
-          if (HD == 128 && grp == 0 && has_b)  // W_rout rows in Q_A feed group B's remote MMA
-            ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_R + 1], 0, abort, &g_fault_word));
-          uint8_t* ltile = smem + (grp ? L::PB : L::PA);
-          uint8_t* rtile = smem + (grp ? L::QB : L::QA);
+          // pass 1 over TMEM: gate logits of local = bf16(O / l) and
+          // remote = R + b; pass 2: local (over this group's Q tile) and
+          // mixed = w local + (1 - w) remote (over its remote operands), then
+          // both 128-row tiles to global by TMA (3-D maps clip rows past T)
+          uint8_t* ltile = smem + (grp ? L::QB : L::QA);
+          uint8_t* mtile = xreg;
           auto tile_chunk = [&](uint8_t* tile, int c) -> uint4* {  // 16-byte chunk c of this row, SW128
             return reinterpret_cast<uint4*>(tile + (c >> 3) * (BM * 128) + row * 128 + (((c & 7) ^ (row & 7)) * 16));
           };
-          const float4* bh4 = reinterpret_cast<const float4*>(ep.b_rout + (int64_t)h * HD);
-          const float4* gl4 = reinterpret_cast<const float4*>(ep.g_local);
-          const float4* gr4 = reinterpret_cast<const float4*>(ep.g_remote);
-          float sl = 0.f, sr = 0.f;
-#pragma unroll 1
-          for (int cc = 0; cc < HD / 32; ++cc) {
+          const float4* b4 = reinterpret_cast<const float4*>(cst);
+          const float4* gl4 = reinterpret_cast<const float4*>(cst + HD);
+          const float4* gr4 = reinterpret_cast<const float4*>(cst + 2 * HD);
+          auto load_row = [&](int cc, float (&lv)[32], float (&rv)[32]) {
             uint32_t ro[32], rr[32];
             if (nk_here > 0) tmem_ld32(tO + lane_off + cc * 32, ro);
             tmem_ld32(tR + lane_off + cc * 32, rr);
             tmem_ld_wait();
-            uint32_t pl[16], pr[16];
 #pragma unroll
             for (int i4 = 0; i4 < 8; ++i4) {
-              const float4 bb = __ldg(bh4 + cc * 8 + i4), ga = __ldg(gl4 + cc * 8 + i4), gb = __ldg(gr4 + cc * 8 + i4);
-              const float bv[4] = {bb.x, bb.y, bb.z, bb.w}, gav[4] = {ga.x, ga.y, ga.z, ga.w};
-              const float gbv[4] = {gb.x, gb.y, gb.z, gb.w};
-              float lv[4], rv[4];
+              const float4 bb = b4[cc * 8 + i4];
+              const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
                 const int q = 4 * i4 + k;
-                lv[k] = nk_here > 0 ? __bfloat162float(__float2bfloat16_rn(__uint_as_float(ro[q]) * inv)) : 0.f;
-                rv[k] = __uint_as_float(rr[q]) + bv[k];
-                sl = fmaf(lv[k], gav[k], sl);
-                sr = fmaf(rv[k], gbv[k], sr);
+                lv[q] = nk_here > 0 ? __bfloat162float(__float2bfloat16_rn(__uint_as_float(ro[q]) * inv)) : 0.f;
+                rv[q] = __uint_as_float(rr[q]) + bv[k];
               }
-              pl[2 * i4] = pack_bf16(lv[0], lv[1]);
-              pl[2 * i4 + 1] = pack_bf16(lv[2], lv[3]);
-              pr[2 * i4] = pack_bf16(rv[0], rv[1]);
-              pr[2 * i4 + 1] = pack_bf16(rv[2], rv[3]);
+            }
+          };
+          float sl = 0.f, sr = 0.f;
+#pragma unroll 1
+          for (int cc = 0; cc < HD / 32; ++cc) {
+            float lv[32], rv[32];
+            load_row(cc, lv, rv);
+#pragma unroll
+            for (int i4 = 0; i4 < 8; ++i4) {
+              const float4 ga = gl4[cc * 8 + i4], gb = gr4[cc * 8 + i4];
+              sl = fmaf(lv[4 * i4], ga.x, fmaf(lv[4 * i4 + 1], ga.y, fmaf(lv[4 * i4 + 2], ga.z, fmaf(lv[4 * i4 + 3], ga.w, sl))));
+              sr = fmaf(rv[4 * i4], gb.x, fmaf(rv[4 * i4 + 1], gb.y, fmaf(rv[4 * i4 + 2], gb.z, fmaf(rv[4 * i4 + 3], gb.w, sr))));
+            }
+          }
+          if (row == 0) LLATTN_TRACE_K(1, 56 + grp);
+          const float x = sl + g.gate_bias - sr;
+          const float wl = 1.f / (1.f + expf(-x));
+          const float wr = 1.f / (1.f + expf(x));
+#pragma unroll 1
+          for (int cc = 0; cc < HD / 32; ++cc) {
+            float lv[32], rv[32];
+            load_row(cc, lv, rv);
+            uint32_t pl[16], pm[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              pl[q] = pack_bf16(lv[2 * q], lv[2 * q + 1]);
+              pm[q] = pack_bf16(wl * lv[2 * q] + wr * rv[2 * q], wl * lv[2 * q + 1] + wr * rv[2 * q + 1]);
             }
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               *tile_chunk(ltile, cc * 4 + q) = make_uint4(pl[4 * q], pl[4 * q + 1], pl[4 * q + 2], pl[4 * q + 3]);
-              *tile_chunk(rtile, cc * 4 + q) = make_uint4(pr[4 * q], pr[4 * q + 1], pr[4 * q + 2], pr[4 * q + 3]);
+              *tile_chunk(mtile, cc * 4 + q) = make_uint4(pm[4 * q], pm[4 * q + 1], pm[4 * q + 2], pm[4 * q + 3]);
             }
           }
-          const float x = sl + g.gate_bias - sr;
-          const float wl = 1.f / (1.f + expf(-x));
-          const float wr = 1.f / (1.f + expf(x));
-          // mixed = wl * local + wr * remote, in place over the remote row
-#pragma unroll 4
-          for (int c = 0; c < HD / 8; ++c) {
-            const uint4 lu = *tile_chunk(ltile, c);
-            uint4 ru = *tile_chunk(rtile, c);
-            float lf[8], rf[8];
-            unpack8(lu, lf);
-            unpack8(ru, rf);
-            ru = make_uint4(pack_bf16(wl * lf[0] + wr * rf[0], wl * lf[1] + wr * rf[1]),
-                            pack_bf16(wl * lf[2] + wr * rf[2], wl * lf[3] + wr * rf[3]),
-                            pack_bf16(wl * lf[4] + wr * rf[4], wl * lf[5] + wr * rf[5]),
-                            pack_bf16(wl * lf[6] + wr * rf[6], wl * lf[7] + wr * rf[7]));
-            *tile_chunk(rtile, c) = ru;
-          }
-          // both 128-row tiles to global by TMA (3-D maps: rows past T are clipped)
           fence_async_smem();
+          if (row == 0) LLATTN_TRACE_K(1, 58 + grp);
           mbar_arrive(&bars[PP_EP + grp]);
           if (row == 0) {
             if (mbar_wait(&bars[PP_EP + grp], 0, abort, &g_fault_word)) {
 #pragma unroll
               for (int p = 0; p < HD / 64; ++p) {
                 tma_store_3d(&tm_lo, ltile + p * (BM * 128), h * HD + p * 64, q0 + grp * BM, b);
-                tma_store_3d(&tm_mx, rtile + p * (BM * 128), h * HD + p * 64, q0 + grp * BM, b);
+                tma_store_3d(&tm_mx, mtile + p * (BM * 128), h * HD + p * 64, q0 + grp * BM, b);
               }
               tma_store_commit();
+              LLATTN_TRACE_K(1, 62 + grp);
               tma_store_wait_read();
             } else {
               raise_fault(kFaultEpilogue, abort);
