@@ -176,14 +176,23 @@ cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, 
     return cudaErrorInvalidValue;
   // two query tiles per CTA (ping-pong), one CTA per SM; the fused epilogue
   // stores local_out and mixed through 3-D maps (d, T, B) that clip at T
-  CUtensorMap tlo, tmx;
+  CUtensorMap tlo, tmx, tlat, tw;
   if (!make_btd_map(&tlo, local_out, g.B, g.T, g.d) || !make_btd_map(&tmx, ep.mixed ? ep.mixed : local_out, g.B, g.T, g.d))
     return cudaErrorInvalidValue;
+  // remote-tile operands: lat rows [B, Tq, 64] (box 64 x 128 rows) and the
+  // head's W_rout slice [d, 64] (box 64 x hd rows); unused without the fusion
+  if (ep.lat) {
+    if (!make_btd_map(&tlat, ep.lat, g.B, g.Tq, 64) || !make_2d_map(&tw, ep.w_rout, g.d, 64, HD))
+      return cudaErrorInvalidValue;
+  } else {
+    tlat = tlo;
+    tw = tlo;
+  }
   const int smem = FwdPPLayout<HD>::BYTES;
   cudaError_t e = cudaFuncSetAttribute(local_fwd_pp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(g.H, cdiv(g.T, 2 * BM), g.B);
-  local_fwd_pp_kernel<HD><<<grid, 320, smem, s>>>(tq, tkv, tlo, tmx, g, static_cast<bf16*>(local_out), lse, ep);
+  local_fwd_pp_kernel<HD><<<grid, 320, smem, s>>>(tq, tkv, tlo, tmx, tlat, tw, g, static_cast<bf16*>(local_out), lse, ep);
   return cudaGetLastError();
 }
 
@@ -274,7 +283,8 @@ cudaError_t launch_local_fwd(const Geom& g, const void* qkv, void* local_out, fl
                              cudaStream_t s) {
   if (((uintptr_t)qkv & 15) || ((uintptr_t)local_out & 15)) return cudaErrorMisalignedAddress;
   if (ep.lat && (g.Ld != 64 || ((uintptr_t)ep.lat & 15) || ((uintptr_t)ep.w_rout & 15) ||
-                 ((uintptr_t)ep.mixed & 15)))
+                 ((uintptr_t)ep.mixed & 15) || ((uintptr_t)ep.b_rout & 15) || ((uintptr_t)ep.g_local & 15) ||
+                 ((uintptr_t)ep.g_remote & 15)))
     return cudaErrorMisalignedAddress;
   if (g.hd == 64) return fwd_hd<64>(g, qkv, local_out, lse, ep, s);
   return fwd_hd<128>(g, qkv, local_out, lse, ep, s);

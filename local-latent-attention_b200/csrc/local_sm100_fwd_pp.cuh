@@ -72,7 +72,8 @@ struct PPTiles {
 template <int HD>
 __global__ void __launch_bounds__(320, 1)
     local_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kv,
-                        const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_mx, Geom g,
+                        const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_mx,
+                        const __grid_constant__ CUtensorMap tm_lat, const __grid_constant__ CUtensorMap tm_w, Geom g,
                         bf16* __restrict__ local_out, float* __restrict__ lse_out, GateEpilogue ep) {
   using L = FwdPPLayout<HD>;
   constexpr int BNK = L::BNK;
@@ -123,7 +124,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&bars[PP_O + x], 1);
     }
     for (int x = 0; x < 2; ++x) {
-      mbar_init(&bars[PP_LW + x], BM);
+      mbar_init(&bars[PP_LW + x], BM + 1);
       mbar_init(&bars[PP_R + x], 1);
       mbar_init(&bars[PP_EP + x], BM);
     }
@@ -142,13 +143,32 @@ __global__ void __launch_bounds__(320, 1)
   if (threadIdx.x == 0) LLATTN_TRACE_K(1, 1);
 
   if (warp == 0) {
-    if (lane == 0 && nk > 0) {
+    if (lane == 0 && (nk > 0 || fuse)) {
       int issued = 0;
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_kv);
-      mbar_expect_tx(&bars[PP_Q], 2 * L::QTILE);
-      tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QA, q0, h, b);
-      tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QB, q0 + BM, h, b);
+      if (fuse) {
+        // remote-tile operands: W_rout[h] for each group, the lat rows of
+        // token-wise queries (block-pooled ones are written by the threads),
+        // and the epilogue's per-column constants (with group A's barrier)
+        const bool lat_tma = g.qbs == 1;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          uint8_t* xr = smem + L::X + x * L::XS;
+          mbar_expect_tx(&bars[PP_LW + x], HD * 128 + (lat_tma ? BM * 128 : 0) + (x == 0 ? 3 * HD * 4 : 0));
+          tma_load_2d(&tm_w, &bars[PP_LW + x], xr + BM * 128, 0, h * HD);
+          if (lat_tma) tma_load_3d(&tm_lat, &bars[PP_LW + x], xr, 0, q0 + x * BM, b);
+        }
+        float* cst = reinterpret_cast<float*>(smem + L::CST);
+        bulk_load(cst, ep.b_rout + (int64_t)h * HD, HD * 4, &bars[PP_LW + 0]);
+        bulk_load(cst + HD, ep.g_local, HD * 4, &bars[PP_LW + 0]);
+        bulk_load(cst + 2 * HD, ep.g_remote, HD * 4, &bars[PP_LW + 0]);
+      }
+      if (nk > 0) {
+        mbar_expect_tx(&bars[PP_Q], 2 * L::QTILE);
+        tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QA, q0, h, b);
+        tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QB, q0 + BM, h, b);
+      }
       for (int j = 0; j < nk; ++j) {
         const int s = j % L::NST;
         if (j >= L::NST && !mbar_wait(&bars[PP_KVE + s], ((j / L::NST) - 1) & 1, abort, &g_fault_word)) {
@@ -163,9 +183,12 @@ __global__ void __launch_bounds__(320, 1)
         issued = j + 1;
       }
       if (*abort) {
+        // let the copies already issued land before the CTA can exit
         volatile int none = 0;
         volatile unsigned gnone = 0;
-        mbar_wait(&bars[PP_Q], 0, &none, &gnone, 100000000ull);
+        if (nk > 0) mbar_wait(&bars[PP_Q], 0, &none, &gnone, 100000000ull);
+        if (fuse)
+          for (int x = 0; x < 2; ++x) mbar_wait(&bars[PP_LW + x], 0, &none, &gnone, 100000000ull);
         for (int j = issued - L::NST < 0 ? 0 : issued - L::NST; j < issued; ++j) {
           mbar_wait(&bars[PP_K + j % L::NST], (j / L::NST) & 1, &none, &gnone, 100000000ull);
           mbar_wait(&bars[PP_V + j % L::NST], (j / L::NST) & 1, &none, &gnone, 100000000ull);
@@ -290,28 +313,17 @@ __global__ void __launch_bounds__(320, 1)
     uint8_t* xreg = smem + L::X + grp * L::XS;  // this group's lat rows, then W_rout[h]
     float* cst = reinterpret_cast<float*>(smem + L::CST);
     bool ok = true;
-    // remote-tile operands, written up front: this row's lat row, row `row`
-    // of W_rout's head slice (each group its own copy), and (group A) the
-    // per-column constants of the epilogue
+    // block-pooled latent queries: this row's lat row (token-wise ones and
+    // W_rout come by TMA)
     if (fuse) {
-      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.lat) +
-                                                        ((int64_t)b * g.Tq + (valid ? t / g.qbs : 0)) * 64);
-      uint8_t* dl_ = xreg + row * 128;
+      if (g.qbs != 1) {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.lat) +
+                                                          ((int64_t)b * g.Tq + (valid ? t / g.qbs : 0)) * 64);
+        uint8_t* dl_ = xreg + row * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dl_ + ((c ^ (row & 7)) * 16)) = src[c];
-      if (row < HD) {
-        const uint4* wsrc =
-            reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.w_rout) + ((int64_t)h * HD + row) * 64);
-        uint8_t* wd = xreg + BM * 128 + row * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(wd + ((c ^ (row & 7)) * 16)) = wsrc[c];
-        if (grp == 0) {
-          cst[row] = ep.b_rout[(int64_t)h * HD + row];
-          cst[HD + row] = ep.g_local[row];
-          cst[2 * HD + row] = ep.g_remote[row];
-        }
+        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dl_ + ((c ^ (row & 7)) * 16)) = src[c];
+        fence_async_smem();
       }
-      fence_async_smem();
       mbar_arrive(&bars[PP_LW + grp]);
     }
     if (!(grp == 1 && !has_b)) {
