@@ -150,18 +150,17 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       constexpr uint32_t idR = idesc_bf16_f32(BM, HD, false, false);  // lat . W_h^T
       constexpr uint32_t idL = idesc_bf16_f32(BM, 64, false, true);   // dR_h . W_h
-      const uint32_t la = smem_u32(smem + L::LAT);
+      const uint64_t dla = desc_sw128(smem_u32(smem + L::LAT), 16, 1024);
       bool ok = true;
       // head h belongs to group h&1 and is that group's (h>>1)-th head
       auto issue_r = [&](int h) -> bool {
         const int s = h & 1;
         if (!mbar_wait(&bars[GB_W + s], (h >> 1) & 1, abort, &g_fault_word)) return false;
         tc_fence_after();
-        const uint32_t wa = smem_u32(smem + L::W + s * HD * 128);
+        const uint64_t dw = desc_sw128(smem_u32(smem + L::W + s * HD * 128), 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(tmem + s * HD, desc_sw128(la + kk * 32, 16, 1024), desc_sw128(wa + kk * 32, 16, 1024), idR,
-                   kk > 0);
+          mma_bf16(tmem + s * HD, desc_add(dla, kk * 32), desc_add(dw, kk * 32), idR, kk > 0);
         mma_commit(&bars[GB_R + s]);
         return true;
       };
@@ -171,12 +170,12 @@ __global__ void __launch_bounds__(320, 1)
         const int s = h & 1;
         if (!(ok = mbar_wait(&bars[GB_DR + s], (h >> 1) & 1, abort, &g_fault_word))) break;
         tc_fence_after();
-        const uint32_t da = smem_u32(smem + L::DM + s * L::TILE);
-        const uint32_t wa = smem_u32(smem + L::W + s * HD * 128);
+        const uint64_t dda = desc_sw128(smem_u32(smem + L::DM + s * L::TILE), 16, 1024);
+        const uint64_t dwm = desc_sw128(smem_u32(smem + L::W + s * HD * 128), 0, 1024);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          mma_bf16(tDL, desc_sw128(da + (kk / 4) * (BM * 128) + (kk % 4) * 32, 16, 1024),
-                   desc_sw128(wa + kk * 2048, 0, 1024), idL, (h > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16(tDL, desc_add(dda, (kk / 4) * (BM * 128) + (kk % 4) * 32), desc_add(dwm, kk * 2048), idL,
+                   (h > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&bars[GB_DL + s]);
         if (h + 2 < H && !(ok = issue_r(h + 2))) break;
       }
@@ -477,11 +476,11 @@ __global__ void __launch_bounds__(192, 1)
         if (!(ok = mbar_wait(&bars[DW_FA + s], (i / DW_ST) & 1, abort, &g_fault_word))) break;
         if (!(ok = mbar_wait(&bars[DW_FB + s], (i / DW_ST) & 1, abort, &g_fault_word))) break;
         tc_fence_after();
-        const uint32_t aa = smem_u32(smem + L::A + s * 16384), ba = smem_u32(smem + L::B + s * 8192);
+        const uint64_t da = desc_sw128(smem_u32(smem + L::A + s * 16384), 8192, 1024);
+        const uint64_t db = desc_sw128(smem_u32(smem + L::B + s * 8192), 0, 1024);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(tmem, desc_sw128(aa + kk * 2048, 8192, 1024), desc_sw128(ba + kk * 2048, 0, 1024), id,
-                   (i > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16(tmem, desc_add(da, kk * 2048), desc_add(db, kk * 2048), id, (i > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&bars[DW_E + s]);
       }
       mma_commit(&bars[DW_DONE]);

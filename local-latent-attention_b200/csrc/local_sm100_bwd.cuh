@@ -123,23 +123,23 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0 && nk > 0) {
       constexpr uint32_t idSP = idesc_bf16_f32(BM, BNK, false, false);  // Q K^T, dO V^T
       constexpr uint32_t idDQ = idesc_bf16_f32(BM, HD, false, true);    // dS K (K MN-major)
-      const uint32_t q_addr = smem_u32(smem + L::Q), do_addr = smem_u32(smem + L::DO);
+      const uint64_t dq0 = desc_sw128(smem_u32(smem + L::Q), 16, 1024);
+      const uint64_t ddo0 = desc_sw128(smem_u32(smem + L::DO), 16, 1024);
       bool ok = mbar_wait(&bars[DQ_Q], 0, abort, &g_fault_word);
       auto issue_sp = [&](int j) -> bool {
         const int s = j & 1, sk = j % L::NKS;
         if (!mbar_wait(&bars[DQ_K + sk], (j / L::NKS) & 1, abort, &g_fault_word)) return false;
         if (!mbar_wait(&bars[DQ_V + sk], (j / L::NKS) & 1, abort, &g_fault_word)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + L::K + sk * L::KTILE);
-        const uint32_t v_addr = smem_u32(smem + L::V + sk * L::KTILE);
+        const uint64_t dk = desc_sw128(smem_u32(smem + L::K + sk * L::KTILE), 16, 1024);
+        const uint64_t dv = desc_sw128(smem_u32(smem + L::V + sk * L::KTILE), 16, 1024);
+        const uint32_t tS = tmem + s * BNK, tP = tmem + 128 + s * BNK;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t aoff = (kk / 4) * L::QPANEL + (kk % 4) * 32;
           const uint32_t boff = (kk / 4) * L::KPANEL + (kk % 4) * 32;
-          mma_bf16(tmem + s * BNK, desc_sw128(q_addr + aoff, 16, 1024), desc_sw128(k_addr + boff, 16, 1024), idSP,
-                   kk > 0);
-          mma_bf16(tmem + 128 + s * BNK, desc_sw128(do_addr + aoff, 16, 1024), desc_sw128(v_addr + boff, 16, 1024),
-                   idSP, kk > 0);
+          mma_bf16(tS, desc_add(dq0, aoff), desc_add(dk, boff), idSP, kk > 0);
+          mma_bf16(tP, desc_add(ddo0, aoff), desc_add(dv, boff), idSP, kk > 0);
         }
         mma_commit(&bars[DQ_SP + s]);
         return true;
@@ -150,13 +150,13 @@ __global__ void __launch_bounds__(320, 1)
         const int s = j & 1, sk = j % L::NKS;
         if (!(ok = mbar_wait(&bars[DQ_DS + s], (j >> 1) & 1, abort, &g_fault_word))) break;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + L::K + sk * L::KTILE);
+        const uint64_t dkm = desc_sw128(smem_u32(smem + L::K + sk * L::KTILE), L::KPANEL, 1024);
+        const uint32_t tA = tmem + 128 + s * BNK;
 #pragma unroll
         for (int kk = 0; kk < BNK / 16; ++kk) {
           // keys 16kk..16kk+15: packed in the half (kk/2) written by warp group kk/2
-          const uint32_t acol = (uint32_t)(128 + s * BNK + (kk >> 1) * 32 + (kk & 1) * 8);
-          mma_bf16_ts(tDQ, tmem + acol, desc_sw128(k_addr + kk * 2048, L::KPANEL, 1024), idDQ,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+          const uint32_t acol = (uint32_t)((kk >> 1) * 32 + (kk & 1) * 8);
+          mma_bf16_ts(tDQ, tA + acol, desc_add(dkm, kk * 2048), idDQ, (j > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(&bars[DQ_DQ + s]);
         mma_commit(&bars[DQ_KVE + sk]);
@@ -410,23 +410,23 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       constexpr uint32_t idSP = idesc_bf16_f32(BM, BNQ, false, false);  // K Q^T, V dO^T
       constexpr uint32_t idKV = idesc_bf16_f32(BM, HD, false, true);    // P^T dO, dS^T Q
-      const uint32_t k_addr = smem_u32(smem + L::K), v_addr = smem_u32(smem + L::V);
+      const uint64_t dk0 = desc_sw128(smem_u32(smem + L::K), 16, 1024);
+      const uint64_t dv0 = desc_sw128(smem_u32(smem + L::V), 16, 1024);
       int q = 0, n = 0, m = 0;  // m: units with at least one query tile
       bool ok = true;
       auto issue_sp = [&](int gq) -> bool {
         const int s = gq & 1, sq = gq % NQS;
         if (!mbar_wait(&bars[KV_QD + sq], (gq / NQS) & 1, abort, &g_fault_word)) return false;
         tc_fence_after();
-        const uint32_t q_addr = smem_u32(smem + L::Q + sq * L::QTILE);
-        const uint32_t do_addr = smem_u32(smem + L::DO + sq * L::QTILE);
+        const uint64_t dq = desc_sw128(smem_u32(smem + L::Q + sq * L::QTILE), 16, 1024);
+        const uint64_t ddo = desc_sw128(smem_u32(smem + L::DO + sq * L::QTILE), 16, 1024);
+        const uint32_t tS = tmem + s * BNQ, tP = tmem + 128 + s * BNQ;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t aoff = (kk / 4) * L::KPANEL + (kk % 4) * 32;
           const uint32_t boff = (kk / 4) * L::QPANEL + (kk % 4) * 32;
-          mma_bf16(tmem + s * BNQ, desc_sw128(k_addr + aoff, 16, 1024), desc_sw128(q_addr + boff, 16, 1024), idSP,
-                   kk > 0);
-          mma_bf16(tmem + 128 + s * BNQ, desc_sw128(v_addr + aoff, 16, 1024), desc_sw128(do_addr + boff, 16, 1024),
-                   idSP, kk > 0);
+          mma_bf16(tS, desc_add(dk0, aoff), desc_add(dq, boff), idSP, kk > 0);
+          mma_bf16(tP, desc_add(dv0, aoff), desc_add(ddo, boff), idSP, kk > 0);
         }
         mma_commit(&bars[KV_SP + s]);
         return true;
@@ -448,15 +448,16 @@ __global__ void __launch_bounds__(320, 1)
             // unit's epilogue must have read them
             if (i == 0 && m > 0 && !(ok = mbar_wait(&bars[KV_ACCE], (m - 1) & 1, abort, &g_fault_word))) break;
             tc_fence_after();
-            const uint32_t q_addr = smem_u32(smem + L::Q + sq * L::QTILE);
-            const uint32_t do_addr = smem_u32(smem + L::DO + sq * L::QTILE);
+            const uint64_t dqm = desc_sw128(smem_u32(smem + L::Q + sq * L::QTILE), L::QPANEL, 1024);
+            const uint64_t ddom = desc_sw128(smem_u32(smem + L::DO + sq * L::QTILE), L::QPANEL, 1024);
+            const uint32_t tA = tmem + s * BNQ;
 #pragma unroll
             for (int kk = 0; kk < BNQ / 16; ++kk) {
               const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
               // queries 16kk..16kk+15: packed in the half (kk/2) written by warp group kk/2
-              const uint32_t acol = (uint32_t)(s * BNQ + (kk >> 1) * 32 + (kk & 1) * 8);
-              mma_bf16_ts(tDV, tmem + acol, desc_sw128(do_addr + kk * 2048, L::QPANEL, 1024), idKV, acc);
-              mma_bf16_ts(tDK, tmem + 128 + acol, desc_sw128(q_addr + kk * 2048, L::QPANEL, 1024), idKV, acc);
+              const uint32_t acol = (uint32_t)((kk >> 1) * 32 + (kk & 1) * 8);
+              mma_bf16_ts(tDV, tA + acol, desc_add(ddom, kk * 2048), idKV, acc);
+              mma_bf16_ts(tDK, tA + 128 + acol, desc_add(dqm, kk * 2048), idKV, acc);
             }
             mma_commit(&bars[KV_QDE + sq]);
           }

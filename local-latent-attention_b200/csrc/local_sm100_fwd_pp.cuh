@@ -200,7 +200,8 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t idS = idesc_bf16_f32(BM, BNK, false, false);
       constexpr uint32_t idO = idesc_bf16_f32(BM, HD, false, true);
       constexpr uint32_t idR = idesc_bf16_f32(BM, HD, false, false);
-      const uint32_t qa = smem_u32(smem + L::QA), qb = smem_u32(smem + L::QB);
+      const uint64_t dqa0 = desc_sw128(smem_u32(smem + L::QA), 16, 1024);
+      const uint64_t dqb0 = desc_sw128(smem_u32(smem + L::QB), 16, 1024);
       bool ok = true;
       // Event-driven issue: each pass tests (without blocking) what has
       // become ready and issues it, so neither group waits for the other.
@@ -230,13 +231,13 @@ __global__ void __launch_bounds__(320, 1)
             const int j = first[x] + ns[x], st = j % L::NST;
             if (mbar_test_wait(&bars[PP_K + st], (j / L::NST) & 1)) {
               tc_fence_after();
-              const uint32_t ka = smem_u32(smem + L::K + st * L::KTILE);
+              const uint64_t dka = desc_sw128(smem_u32(smem + L::K + st * L::KTILE), 16, 1024);
               const uint32_t dst = tmem + x * 128 + (ns[x] & 1) * BNK;
-              const uint32_t q_addr = x ? qb : qa;
+              const uint64_t dqa = x ? dqb0 : dqa0;
 #pragma unroll
               for (int kk = 0; kk < HD / 16; ++kk)
-                mma_bf16(dst, desc_sw128(q_addr + (kk / 4) * L::QPANEL + (kk % 4) * 32, 16, 1024),
-                         desc_sw128(ka + (kk / 4) * L::KPANEL + (kk % 4) * 32, 16, 1024), idS, kk > 0);
+                mma_bf16(dst, desc_add(dqa, (kk / 4) * L::QPANEL + (kk % 4) * 32),
+                         desc_add(dka, (kk / 4) * L::KPANEL + (kk % 4) * 32), idS, kk > 0);
               mma_commit(&bars[PP_S + 2 * x + (ns[x] & 1)]);
               ++ns[x];
               progress = true;
@@ -249,12 +250,11 @@ __global__ void __launch_bounds__(320, 1)
                 mbar_test_wait(&bars[PP_V + st], (j / L::NST) & 1)) {
               tc_fence_after();
               // P (bf16, packed two per column) over the first 32 columns of S buffer i&1
-              const uint32_t pa = tmem + x * 128 + (i & 1) * BNK;
-              const uint32_t va = smem_u32(smem + L::V + st * L::KTILE);
+              const uint32_t pa = tmem + x * 128 + (i & 1) * BNK, to = tmem + 256 + x * HD;
+              const uint64_t dva = desc_sw128(smem_u32(smem + L::V + st * L::KTILE), L::KPANEL, 1024);
 #pragma unroll
               for (int kk = 0; kk < BNK / 16; ++kk)
-                mma_bf16_ts(tmem + 256 + x * HD, pa + kk * 8, desc_sw128(va + kk * 2048, L::KPANEL, 1024), idO,
-                            (i > 0 || kk > 0) ? 1u : 0u);
+                mma_bf16_ts(to, pa + kk * 8, desc_add(dva, kk * 2048), idO, (i > 0 || kk > 0) ? 1u : 0u);
               mma_commit(&bars[PP_O + 2 * x + (i & 1)]);
               ++npv[x];
               progress = true;
@@ -264,11 +264,11 @@ __global__ void __launch_bounds__(320, 1)
           if (fuse && !r_done[x] && npv[x] == nx[x]) {
             if (mbar_test_wait(&bars[PP_LW + x], 0)) {
               tc_fence_after();
-              const uint32_t la = smem_u32(smem + L::X + x * L::XS), wa = la + BM * 128;
+              const uint32_t la = smem_u32(smem + L::X + x * L::XS);
+              const uint64_t dla = desc_sw128(la, 16, 1024), dwa = desc_sw128(la + BM * 128, 16, 1024);
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)
-                mma_bf16(tmem + x * 128, desc_sw128(la + kk * 32, 16, 1024), desc_sw128(wa + kk * 32, 16, 1024), idR,
-                         kk > 0);
+                mma_bf16(tmem + x * 128, desc_add(dla, kk * 32), desc_add(dwa, kk * 32), idR, kk > 0);
               mma_commit(&bars[PP_R + x]);
               r_done[x] = true;
               progress = true;

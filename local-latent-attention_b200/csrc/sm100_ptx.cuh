@@ -274,6 +274,14 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uin
   return d;
 }
 
+// Descriptor of the same operand layout at `saddr + byte_off`: the start
+// address field is the low 14 bits (addr >> 4) and shared-memory addresses
+// stay below 256 KB, so the offset adds without a carry out of the field.
+// Issue loops precompute one descriptor per tile and add constant offsets:
+// a single thread issues every MMA, and recomputing full descriptors
+// between instructions throttles the issue rate.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t byte_off) { return d + (byte_off >> 4); }
+
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn, bool b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
