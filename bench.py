@@ -555,6 +555,9 @@ def run_lm(args):
 
 def main():
     args = parse()
+    # stdout carries exactly one JSON line: keep NCCL's version banner off it
+    if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+        os.environ["NCCL_DEBUG"] = "WARN"
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "lm":
