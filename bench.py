@@ -66,19 +66,32 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--batch", type=int, default=0, help="override the config's batch (small profiling runs)")
-    p.add_argument("--workload", default="block", choices=["block", "lm"],
+    p.add_argument("--workload", default="block", choices=["block", "lm", "decode"],
                    help="block: the attention block fwd+bwd (default); lm: cfg4 LM training step")
     p.add_argument("--layers", type=int, default=24, help="lm: decoder layers (cfg4: 24)")
     return p.parse_args()
 
 
 def block_cfg(name):
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import llattn_oracle as O
+    """(B, T, block ModelConfig) of a config; head_dim = d_model / n_heads."""
+    from llattn_b200.lm import ModelConfig
 
     d = dict(CONFIGS[name])
     B, T = d.pop("B"), d.pop("T")
-    return B, T, O.BlockCfg(**d)
+    return B, T, ModelConfig(max_seq_len=T, n_layers=1, dropout=0.0, **d)
+
+
+def seeded_module(cfg, device):
+    """The block with the reference constructor's default init drawn from
+    seed 0 (its layers are created in the reference's order, so the weights
+    equal the reference module's under the same seed), bf16 on `device`."""
+    import torch
+
+    import llattn_b200
+
+    torch.manual_seed(0)
+    m = llattn_b200.LocalLatentAttentionB200(cfg)
+    return m.to(device=device, dtype=torch.bfloat16)
 
 
 def config_json(name, n_gpus):
@@ -100,7 +113,9 @@ def cpu_time_block(name, seconds, steps=None, warmup=1):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import llattn_oracle as O
 
-    B, T, cfg = block_cfg(name)
+    fields = {k: v for k, v in CONFIGS[name].items() if k not in ("B", "T")}
+    T = CONFIGS[name]["T"]
+    cfg = O.BlockCfg(**fields)
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     Bs = 1  # bounded sample: one sequence of the workload per iteration
@@ -233,13 +248,10 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
 
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    sys.path.insert(0, os.path.join(ROOT, "tests"))
     import llattn_b200
-    import llattn_oracle as O
     from llattn_b200 import _lib
     from llattn_b200 import dist as D
-    from parity import model_config
+    from llattn_b200.ops import visible_pairs
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -253,9 +265,7 @@ def run_ours(args):
     if args.batch:
         B = args.batch
         CONFIGS[args.config] = dict(CONFIGS[args.config], B=B)
-    m = llattn_b200.LocalLatentAttentionB200(model_config(cfg))
-    m.load_state_dict(O.init_params(cfg, 0))
-    m = m.to(device=dev, dtype=torch.bfloat16)
+    m = seeded_module(cfg, dev)
     params = [p for p in m.parameters()]
     gen = torch.Generator().manual_seed(1 + rank)
     x_h = torch.randn(B, T, cfg.d_model, generator=gen).to(torch.bfloat16).pin_memory()
@@ -370,8 +380,8 @@ def run_ours(args):
 
     # roofline of the dominant kernel group
     hbm, tflops, peak_kind = load_peaks()
-    P = O.local_pairs(T, cfg.local_window, cfg.local_block_size) * B * cfg.n_heads
-    hd = cfg.head_dim
+    P = visible_pairs(T, cfg.local_window, cfg.local_block_size) * B * cfg.n_heads
+    hd = cfg.d_model // cfg.n_heads
     d = cfg.d_model
     BTd2 = B * T * d * 2.0  # one [B,T,d] bf16 tensor
     # per launch-group call: (FLOPs, bytes that must cross HBM)
@@ -553,6 +563,96 @@ def run_lm(args):
     D.cleanup_distributed()
 
 
+def run_decode(args):
+    """Incremental decode of the cfg2 block: B=16 sequences with a 2047-token
+    prefix in the decode caches, then one token per step through
+    LocalLatentAttentionB200.decode (qkv row, chunk means re-pooled over the
+    prefix, llattn_decode, out row). Metric: generated tokens/s; 1 GPU
+    (replicas only: each rank would decode its own sequences)."""
+    import torch
+
+    from llattn_b200 import _lib
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    B, T, cfg = block_cfg(args.config)
+    if args.batch:
+        B = args.batch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    m = seeded_module(cfg, dev).eval()
+    gen = torch.Generator().manual_seed(0)
+    T0 = T - 1
+    steps = args.steps + args.warmup
+    x = torch.randn(B, T0 + steps, cfg.d_model, generator=gen).to(device=dev, dtype=torch.bfloat16)
+    cache = m.new_decode_cache(T0 + steps)
+    m.prefill(x[:, :T0], cache)
+    for i in range(args.warmup):
+        m.decode(x[:, T0 + i:T0 + i + 1], cache)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    clocks.start()
+    time.sleep(0.3)
+    _lib.profile_enable(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.warmup, steps):
+        y = m.decode(x[:, T0 + i:T0 + i + 1], cache)
+    e1.record()
+    torch.cuda.synchronize()
+    kern = _lib.profile_read()
+    _lib.profile_enable(False)
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    # end to end: the new token's input from pinned host memory, its output row back
+    xh = x[:, -1:].cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    cache2 = m.new_decode_cache(T0 + steps)
+    m.prefill(x[:, :T0], cache2)
+    xd = torch.empty_like(x[:, :1])
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(args.steps):
+        xd.copy_(xh, non_blocking=True)
+        yd = m.decode(xd, cache2)
+        yh.copy_(yd, non_blocking=True)
+    e3.record()
+    torch.cuda.synchronize()
+    ms_e2e = e2.elapsed_time(e3) / args.steps
+    per_step = {k: (v[0] / args.steps, v[1] / args.steps) for k, v in kern.items() if v[1] > 0}
+    hbm, tflops, peak_kind = load_peaks()
+    # the decode kernel reads, per (b, h), the key/value rows of the window and
+    # the query row, plus per sequence the rq row, gk/gv and W_rout
+    Tn = T0 + steps
+    nk = min(cfg.local_window, Tn - 1)
+    Ld = cfg.latent_d_model
+    hd = cfg.d_model // cfg.n_heads
+    dec_bytes = 2.0 * B * (cfg.n_heads * (2 * nk + 1) * hd + cfg.d_model * (1 + Ld) + 2 * 64 * Ld)
+    dec_ms = per_step.get("decode", (0.0, 0))[0]
+    roof = None
+    if dec_ms > 0:
+        ach = dec_bytes / (dec_ms / 1e3) / 1e9
+        roof = {"kernel": "decode", "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(ach / hbm, 4), "peak_kind": peak_kind, "algorithmic_bytes": dec_bytes, "traffic": None,
+                "avg_launch_ms": round(dec_ms, 4)}
+    out = {
+        "metric": "llattn decode tokens/s (bf16, cfg2 block, 2047-token prefix)", "value": round(B / (ms / 1e3), 1),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded randn token inputs)",
+        "config": {"workload": "LocalLatentAttention block decode (cfg2 shapes)", "batch": B, "prefix": T0,
+                   "parallelism": "replicas only"},
+        "e2e": {"value": round(B / (ms_e2e / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": xh.numel() * 2,
+                "d2h_bytes_per_step": yh.numel() * 2},
+        "roofline": roof,
+        "gpu_launches": int(sum(v[1] for v in kern.values())),
+        "kernels": {k: {"ms_per_step": round(v[0], 4), "launches_per_step": v[1]} for k, v in per_step.items()},
+        "clocks": clk,
+    }
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse()
     # stdout carries exactly one JSON line: keep NCCL's version banner off it
@@ -562,6 +662,8 @@ def main():
         run_reference(args)
     elif args.workload == "lm":
         run_lm(args)
+    elif args.workload == "decode":
+        run_decode(args)
     else:
         run_ours(args)
 

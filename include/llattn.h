@@ -115,6 +115,31 @@ typedef struct llattn_fwd_args {
   float* lat_lse;
 } llattn_fwd_args;
 
+/* One decode step: row t = dims.seq_len - 1 of llattn_fwd's `mixed` for the
+ * dims.seq_len-token prefix (every size derived from that length, as the
+ * reference's generation loop recomputes the whole prefix each step,
+ * generate.py:188-202), computed from cached rows instead of recomputing
+ * the prefix:
+ *   qkv_cache [B, cache_len, 3, H, hd] dtype: rows 0..t of the prefix's
+ *             qkv_proj output (cache_len >= seq_len)
+ *   rq_row    [B, Lh*ldh] dtype: the rq_proj row of t's latent query (the
+ *             token's own row, or its query block's pooled row)
+ *   gkv       [B, Nc, 2, Lh, ldh] dtype: rkv_proj of the prefix's chunk means
+ *   w_rout, b_rout, g_local, g_remote as in llattn_fwd
+ * Output: mixed_row [B, H*hd] dtype. */
+typedef struct llattn_decode_args {
+  llattn_dims dims;
+  int64_t cache_len;
+  const void* qkv_cache;
+  const void* rq_row;
+  const void* gkv;
+  const void* w_rout;
+  const float* b_rout;
+  const float* g_local;
+  const float* g_remote;
+  void* mixed_row;
+} llattn_decode_args;
+
 /* Backward of llattn_fwd. Inputs are the forward inputs, the saved tensors
  * and dmixed [B, T, H*hd] dtype. Outputs (all fully overwritten):
  *   dqkv [B, T, 3, H, hd] dtype, drq [B, Tq, Lh, ldh] dtype,
@@ -179,6 +204,9 @@ LLATTN_API int llattn_pool_bwd(const llattn_dims* dims, int mode, const void* dp
                     void* dx, int64_t d, void* stream);
 
 LLATTN_API int llattn_fwd(const llattn_fwd_args* args, void* stream);
+/* Replaces nothing in the reference (its generation loop re-runs the whole
+ * forward per token, generate.py:188-202); the per-token path of that loop. */
+LLATTN_API int llattn_decode(const llattn_decode_args* args, void* stream);
 LLATTN_API int llattn_bwd(const llattn_bwd_args* args, void* stream);
 
 /* Backward without a caller-provided workspace. For callers that cannot

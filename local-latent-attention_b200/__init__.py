@@ -9,7 +9,7 @@ first use; it is built by ``csrc/build.py``.
 """
 
 from . import ops
-from .module import LocalLatentAttentionB200, build_attention
+from .module import DecodeCache, LocalLatentAttentionB200, build_attention
 from .ops import LLAttnFunction, llattn_attention
 
-__all__ = ["LocalLatentAttentionB200", "build_attention", "llattn_attention", "LLAttnFunction", "ops"]
+__all__ = ["LocalLatentAttentionB200", "DecodeCache", "build_attention", "llattn_attention", "LLAttnFunction", "ops"]

@@ -18,7 +18,7 @@ BWD_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 EXPORTED = (
     "llattn_version", "llattn_last_error", "llattn_fault_status", "llattn_geometry", "llattn_bwd_workspace_bytes",
-    "llattn_pool_fwd", "llattn_pool_bwd", "llattn_fwd", "llattn_bwd", "llattn_bwd_noalloc",
+    "llattn_pool_fwd", "llattn_pool_bwd", "llattn_fwd", "llattn_bwd", "llattn_bwd_noalloc", "llattn_decode",
     "llattn_profile_enable", "llattn_profile_read", "llattn_profile_name",
 )
 
@@ -58,6 +58,12 @@ class BwdArgs(ctypes.Structure):
                 ("workspace_bytes", ctypes.c_size_t)]
 
 
+class DecodeArgs(ctypes.Structure):
+    _fields_ = [("dims", Dims), ("cache_len", ctypes.c_int64), ("qkv_cache", _vp), ("rq_row", _vp),
+                ("gkv", _vp), ("w_rout", _vp), ("b_rout", _fp), ("g_local", _fp), ("g_remote", _fp),
+                ("mixed_row", _vp)]
+
+
 _lib = None
 
 
@@ -88,6 +94,8 @@ def lib() -> ctypes.CDLL:
         L.llattn_bwd.restype = ctypes.c_int
         L.llattn_bwd_noalloc.argtypes = [ctypes.POINTER(BwdArgs), _vp]
         L.llattn_bwd_noalloc.restype = ctypes.c_int
+        L.llattn_decode.argtypes = [ctypes.POINTER(DecodeArgs), _vp]
+        L.llattn_decode.restype = ctypes.c_int
         L.llattn_profile_enable.argtypes = [ctypes.c_int]
         L.llattn_profile_enable.restype = ctypes.c_int
         L.llattn_profile_read.argtypes = [ctypes.POINTER(ctypes.c_double),

@@ -319,6 +319,30 @@ int llattn_fwd(const llattn_fwd_args* a, void* stream) {
   return run_fwd<float>(g, a, s);
 }
 
+int llattn_decode(const llattn_decode_args* a, void* stream) {
+  if (!a) return fail(LLATTN_ERR_ARG, "args is NULL");
+  Geom g;
+  int rc = make_geom(&a->dims, &g);
+  if (rc) return rc;
+  if (!a->qkv_cache || !a->rq_row || !a->gkv || !a->w_rout || !a->b_rout || !a->g_local || !a->g_remote ||
+      !a->mixed_row)
+    return fail(LLATTN_ERR_ARG, "llattn_decode: NULL pointer in args");
+  if (a->cache_len < a->dims.seq_len)
+    return fail(LLATTN_ERR_ARG, "llattn_decode: cache_len %lld < seq_len %d", (long long)a->cache_len,
+                a->dims.seq_len);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  prof::Scope ps(prof::DECODE, s);
+  if (a->dims.dtype == LLATTN_BF16)
+    return check_launch(launch_decode<bf16>(g, a->cache_len, (const bf16*)a->qkv_cache, (const bf16*)a->rq_row,
+                                            (const bf16*)a->gkv, (const bf16*)a->w_rout, a->b_rout, a->g_local,
+                                            a->g_remote, (bf16*)a->mixed_row, s),
+                        "decode");
+  return check_launch(launch_decode<float>(g, a->cache_len, (const float*)a->qkv_cache, (const float*)a->rq_row,
+                                           (const float*)a->gkv, (const float*)a->w_rout, a->b_rout, a->g_local,
+                                           a->g_remote, (float*)a->mixed_row, s),
+                      "decode");
+}
+
 int llattn_bwd(const llattn_bwd_args* a, void* stream) {
   if (!a) return fail(LLATTN_ERR_ARG, "args is NULL");
   Geom g;

@@ -24,7 +24,7 @@ ROOT = os.path.dirname(PKG)
 INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(CSRC, "_build")
 LIB = os.path.join(PKG, "libllattn.so")
-SOURCES = ["api.cu", "pool.cu", "latent.cu", "local_simt.cu", "gate.cu", "local_sm100.cu", "profile.cu"]
+SOURCES = ["api.cu", "pool.cu", "latent.cu", "local_simt.cu", "gate.cu", "local_sm100.cu", "decode.cu", "profile.cu"]
 NVCC = os.environ.get("NVCC", shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc")
 
 

@@ -95,6 +95,12 @@ cudaError_t launch_latent_fwd(const Geom& g, const T* rq, const T* gkv, T* lat, 
 template <typename T>
 cudaError_t launch_latent_bwd(const Geom& g, const T* rq, const T* gkv, const float* lat_lse,
                               const float* dlat, T* drq, float* dgkv_part, int n_split, cudaStream_t s);
+// One decode step (decode.cu): qkv cache [B, cache_len, 3, H, hd] with rows
+// 0..T-1 filled, rq_row [B, Ld], gkv [B, Nc, 2, Ld] -> out [B, d] (row T-1).
+template <typename T>
+cudaError_t launch_decode(const Geom& g, int64_t cache_len, const T* qkv, const T* rq_row, const T* gkv,
+                          const T* w_rout, const float* b_rout, const float* g_local, const float* g_remote, T* out,
+                          cudaStream_t s);
 template <typename T>
 cudaError_t launch_latent_reduce(const Geom& g, const float* dgkv_part, int n_split, T* dgkv,
                                  cudaStream_t s);

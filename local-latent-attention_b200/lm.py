@@ -131,6 +131,65 @@ class LocalLatentLM(nn.Module):
         return self.lm_head(self.norm(x))
 
 
+    # --- generation ---------------------------------------------------------
+
+    @torch.no_grad()
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int, temperature: float = 0.0,
+                 top_k: int = 0, generator: torch.Generator | None = None,
+                 incremental: bool = True) -> torch.Tensor:
+        """Append max_new_tokens sampled tokens to input_ids [B, P] -> [B, P + n].
+
+        The loop of the reference's generate.py:188-202 (context = the last
+        max_seq_len tokens, next token from the last position's logits;
+        temperature <= 0 is greedy, top_k > 0 keeps the k largest logits).
+        With ``incremental`` each step runs only the new token through the
+        layers, the attention layers from their decode caches; once the
+        sequence outgrows max_seq_len (the context then slides and positions
+        are re-based) it falls back to the full forward, as the reference."""
+        ids = input_ids
+        caches = None
+        for _ in range(max_new_tokens):
+            T = ids.shape[1]
+            if incremental and T <= self.config.max_seq_len:
+                if caches is None:
+                    cap = min(self.config.max_seq_len, T + max_new_tokens)
+                    caches = [blk.attn.new_decode_cache(cap) for blk in self.blocks]
+                    logits = self._prefill(ids, caches)
+                else:
+                    logits = self._decode_one(ids[:, -1:], T - 1, caches)
+            else:
+                logits = self(ids[:, -self.config.max_seq_len:])[:, -1]
+            ids = torch.cat([ids, _sample(logits.float(), temperature, top_k, generator)], dim=1)
+        return ids
+
+    def _prefill(self, ids: torch.Tensor, caches) -> torch.Tensor:
+        T = ids.shape[1]
+        x = self.embedding(ids) + self.position(torch.arange(T, device=ids.device)).unsqueeze(0)
+        for blk, cache in zip(self.blocks, caches):
+            x = x + blk.attn.prefill(blk.norm1(x), cache)
+            x = x + blk.ff(blk.norm2(x))
+        return self.lm_head(self.norm(x[:, -1]))
+
+    def _decode_one(self, tok: torch.Tensor, pos: int, caches) -> torch.Tensor:
+        x = self.embedding(tok) + self.position.weight[pos].view(1, 1, -1)
+        for blk, cache in zip(self.blocks, caches):
+            x = x + blk.attn.decode(blk.norm1(x), cache)
+            x = x + blk.ff(blk.norm2(x))
+        return self.lm_head(self.norm(x[:, -1]))
+
+
+def _sample(logits: torch.Tensor, temperature: float, top_k: int, generator) -> torch.Tensor:
+    """Next token [B, 1] from last-position logits [B, V] (generate.py:42-110
+    without its repetition penalty and n-gram ban, which filter logits on the host)."""
+    if temperature <= 0.0:
+        return logits.argmax(dim=-1, keepdim=True)
+    logits = logits / temperature
+    if 0 < top_k < logits.shape[-1]:
+        kth = torch.topk(logits, top_k, dim=-1).values[:, -1:]
+        logits = logits.masked_fill(logits < kth, float("-inf"))
+    return torch.multinomial(torch.softmax(logits, dim=-1), 1, generator=generator)
+
+
 def build_optimizer(model: nn.Module, lr: float = 3e-4, weight_decay: float = 0.1):
     """AdamW(beta 0.9/0.95), decay on >= 2-D params only (train.py:851-859)."""
     decay, no_decay = [], []

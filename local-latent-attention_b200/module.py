@@ -15,11 +15,27 @@ pooling and everything between the projections run in the custom ops of
 
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import torch
 import torch.nn as nn
 from torch import Tensor
 
 from . import ops
+
+
+@dataclass
+class DecodeCache:
+    """Generation state of one LocalLatentAttentionB200 layer: the qkv_proj
+    rows [B, capacity, 3d] and the attention inputs [B, capacity, d] of every
+    token so far. The inputs are kept (not only a key/value window) because
+    the latent chunking depends on the whole prefix length
+    (models.py:175-183): chunk means are re-pooled from them each step."""
+
+    capacity: int
+    qkv: Tensor | None = None
+    x: Tensor | None = None
+    length: int = 0
 
 
 class LocalLatentAttentionB200(nn.Module):
@@ -158,6 +174,63 @@ class LocalLatentAttentionB200(nn.Module):
                 "latent_count": geo["n_chunks"], "chunk_size": geo["chunk"],
                 "latent_query_block_size": geo["qblock"]}))
         return y
+
+    # --- incremental generation ------------------------------------------
+
+    def new_decode_cache(self, capacity: int) -> DecodeCache:
+        return DecodeCache(capacity=int(capacity))
+
+    def _store(self, cache: DecodeCache, x: Tensor, qkv: Tensor) -> None:
+        B, n, d = x.shape
+        if cache.qkv is None:
+            cache.qkv = torch.empty(B, cache.capacity, qkv.shape[-1], dtype=qkv.dtype, device=x.device)
+            cache.x = torch.empty(B, cache.capacity, d, dtype=x.dtype, device=x.device)
+        if cache.length + n > cache.capacity:
+            raise RuntimeError(f"llattn: decode cache full ({cache.length} + {n} > {cache.capacity} tokens)")
+        cache.qkv[:, cache.length:cache.length + n] = qkv
+        cache.x[:, cache.length:cache.length + n] = x
+        cache.length += n
+
+    def prefill(self, x: Tensor, cache: DecodeCache) -> Tensor:
+        """Full forward of the first tokens [B, n, d] that also fills the cache."""
+        if cache.length != 0:
+            raise RuntimeError("llattn: prefill needs an empty decode cache")
+        with torch.no_grad():
+            y = self(x)
+            self._store(cache, x, self.qkv_proj(x))
+        return y
+
+    def decode(self, x: Tensor, cache: DecodeCache) -> Tensor:
+        """Outputs [B, n, d] of n new tokens [B, n, d] appended after the
+        cached prefix, one token at a time. Row i equals the last row of
+        this module's forward over the prefix extended by tokens 0..i (the
+        computation the reference's generation loop repeats per token,
+        generate.py:188-202), from the cache: qkv of one row, chunk means
+        re-pooled over the prefix (the latent geometry follows its length),
+        one ``llattn_decode`` launch."""
+        ys = []
+        with torch.no_grad():
+            for i in range(x.shape[1]):
+                xt = x[:, i:i + 1]
+                self._store(cache, xt, self.qkv_proj(xt))
+                T = cache.length
+                xs = cache.x[:, :T].contiguous()
+                gkv = self.rkv_proj(ops.pool_chunks(xs, self.latent_tokens))
+                if self.latent_query_block_size > 1:
+                    qrows = ops.pool_query_blocks(xs, self.latent_tokens, self.latent_query_block_size)
+                    qb = ops.geometry(T, self.latent_tokens, self.latent_query_block_size)["qblock"]
+                    src = qrows[:, (T - 1) // qb]
+                else:
+                    src = xt[:, 0]
+                rq_row = self.rq_proj(src)
+                mixed = ops.decode_core(
+                    cache.qkv, T, rq_row, gkv, self.r_out.weight, self.r_out.bias, self.gate_local.weight,
+                    self.gate_remote.weight, n_heads=self.n_heads, latent_heads=self.latent_heads,
+                    window=self.window, local_block_size=self.local_block_size,
+                    latent_tokens=self.latent_tokens, latent_query_block_size=self.latent_query_block_size,
+                    gate_bias=self.gate_bias)
+                ys.append(self.out(mixed))
+        return torch.stack(ys, dim=1)
 
 
 def build_attention(config) -> nn.Module:

@@ -39,6 +39,18 @@ def geometry(seq_len: int, latent_tokens: int, query_block: int, window: int = 1
             "qblock": qbs, "n_qrows": math.ceil(seq_len / qbs)}
 
 
+def visible_pairs(seq_len: int, window: int, local_block: int = 256) -> int:
+    """Visible (query, key) pairs of one (batch, head) sequence under the
+    local mask (models.py:245-292: key j visible from t iff 0 < t-j <= W and
+    j >= qs(t) - W + 1): the local branch's work is 4*hd FLOPs per pair
+    forward and 8*hd backward."""
+    bsl = min(seq_len, max(window, local_block))
+    t = torch.arange(seq_len, dtype=torch.int64)
+    qs = (t // bsl) * bsl
+    lo = torch.clamp(torch.maximum(t - window, qs - window + 1), min=0)
+    return int((t - lo).clamp(min=0).sum())
+
+
 def _ptr(t: Tensor) -> int:
     return t.data_ptr()
 
@@ -268,6 +280,44 @@ def llattn_attention(qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tensor, b_rou
                     n_heads, latent_heads, window, local_block_size, latent_tokens,
                     latent_query_block_size, float(gate_bias))
     return outs[0]
+
+
+def decode_core(qkv_cache: Tensor, seq_len: int, rq_row: Tensor, gkv: Tensor, w_rout: Tensor,
+                b_rout: Tensor, g_local: Tensor, g_remote: Tensor, *, n_heads: int, latent_heads: int,
+                window: int, local_block_size: int, latent_tokens: int,
+                latent_query_block_size: int = 0, gate_bias: float = 0.0) -> Tensor:
+    """One decode step of the attention core (no autograd) -> mixed row [B, d].
+
+    The last row (t = seq_len - 1) of ``llattn_attention`` over the
+    seq_len-token prefix whose qkv_proj rows fill qkv_cache[:, :seq_len]
+    ([B, cache_len, 3d]); rq_row [B, Ld] is the rq_proj row of t's latent
+    query and gkv [B, Nc, 2Ld] the rkv_proj output of the prefix's chunk means
+    (Nc of seq_len). Launches ``llattn_decode``; CUDA only."""
+    dt = qkv_cache.dtype
+    _require(qkv_cache.is_cuda, "decode_core needs CUDA tensors")
+    _require(qkv_cache.is_contiguous() and qkv_cache.dim() == 3, "qkv_cache must be a contiguous [B, cache_len, 3d]")
+    B, cache_len, three_d = qkv_cache.shape
+    _require(1 <= seq_len <= cache_len, f"seq_len {seq_len} outside [1, cache_len={cache_len}]")
+    d = three_d // 3
+    Ld = w_rout.shape[1]
+    dims = _lib.make_dims(B, seq_len, n_heads, d // n_heads, latent_heads, Ld // latent_heads, window,
+                          local_block_size, latent_tokens, latent_query_block_size, _dtype_code(qkv_cache),
+                          float(gate_bias))
+    geo = geometry(seq_len, latent_tokens, latent_query_block_size, window, local_block_size)
+    rq_row = rq_row.to(dt).reshape(B, Ld).contiguous()
+    gkv = gkv.to(dt).contiguous()
+    _require(tuple(gkv.shape) == (B, geo["n_chunks"], 2 * Ld),
+             f"gkv has shape {tuple(gkv.shape)}, expected {(B, geo['n_chunks'], 2 * Ld)}")
+    w = w_rout.to(dt).contiguous()
+    b = b_rout.float().contiguous()
+    gl = g_local.float().reshape(-1).contiguous()
+    gr = g_remote.float().reshape(-1).contiguous()
+    out = torch.empty(B, d, dtype=dt, device=qkv_cache.device)
+    args = _lib.DecodeArgs(dims, cache_len, _ptr(qkv_cache), _ptr(rq_row), _ptr(gkv), _ptr(w), _ptr(b),
+                           _ptr(gl), _ptr(gr), _ptr(out))
+    with torch.cuda.device(qkv_cache.device):
+        _lib.check(_lib.lib().llattn_decode(ctypes.byref(args), _stream(qkv_cache)), "llattn_decode")
+    return out
 
 
 class LLAttnFunction:

@@ -64,3 +64,38 @@ def test_dropout_in_training_is_rejected():
     m = llattn_b200.LocalLatentAttentionB200(c).train()
     with pytest.raises(NotImplementedError):
         m(torch.randn(1, 4, 32))
+
+
+def test_decode_cache_bookkeeping_and_cpu_refusal():
+    """The decode path keeps its cache on the host side consistent and, like
+    every op, refuses CPU tensors instead of falling back."""
+    import llattn_b200
+    from llattn_b200 import ops
+
+    cache = llattn_b200.DecodeCache(capacity=8)
+    assert cache.length == 0 and cache.qkv is None
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.decode_core(torch.zeros(1, 8, 3 * 64), 1, torch.zeros(1, 32), torch.zeros(1, 1, 64),
+                        torch.zeros(64, 32), torch.zeros(64), torch.zeros(16), torch.zeros(16), n_heads=4,
+                        latent_heads=2, window=4, local_block_size=8, latent_tokens=4)
+
+
+def test_seeded_construction_equals_reference_default_init():
+    """bench.py builds its block under torch.manual_seed(0); the module's
+    layers are created in the reference constructor's order, so the weights
+    are the reference module's default init (the oracle's init_params)."""
+    cfg = O.BlockCfg(d_model=128, n_heads=4, local_window=16, latent_tokens=8, latent_d_model=32)
+    torch.manual_seed(0)
+    m = llattn_b200.LocalLatentAttentionB200(model_config(cfg))
+    ref = O.init_params(cfg, 0)
+    sd = m.state_dict()
+    assert set(sd) == set(ref)
+    for k, v in ref.items():
+        assert torch.equal(sd[k], v), k
+
+
+def test_visible_pairs_matches_oracle_count():
+    from llattn_b200.ops import visible_pairs
+
+    for T, W, lbs in [(2048, 256, 256), (512, 128, 256), (16384, 512, 256), (37, 12, 16), (1, 4, 4), (300, 64, 32)]:
+        assert visible_pairs(T, W, lbs) == O.local_pairs(T, W, lbs)
