@@ -188,11 +188,26 @@ cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, 
     tlat = tlo;
     tw = tlo;
   }
-  const int smem = FwdPPLayout<HD>::BYTES;
-  cudaError_t e = cudaFuncSetAttribute(local_fwd_pp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  dim3 grid(g.H, cdiv(g.T, 2 * BM), g.B);
-  local_fwd_pp_kernel<HD><<<grid, 320, smem, s>>>(tq, tkv, tlo, tmx, tlat, tw, g, static_cast<bf16*>(local_out), lse, ep);
+  // LLATTN_FWD_PAIR=1 selects the two-tiles-per-CTA variant (one CTA per SM)
+  static const bool pair = [] {
+    const char* e = std::getenv("LLATTN_FWD_PAIR");
+    return e && e[0] == '1';
+  }();
+  if (pair) {
+    const int smem = FwdPPLayout<HD, true>::BYTES;
+    cudaError_t e = cudaFuncSetAttribute(local_fwd_pp_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid(g.H, cdiv(g.T, 2 * BM), g.B);
+    local_fwd_pp_kernel<HD, true><<<grid, FwdPPLayout<HD, true>::THREADS, smem, s>>>(
+        tq, tkv, tlo, tmx, tlat, tw, g, static_cast<bf16*>(local_out), lse, ep);
+  } else {
+    const int smem = FwdPPLayout<HD, false>::BYTES;
+    cudaError_t e = cudaFuncSetAttribute(local_fwd_pp_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid(g.H, cdiv(g.T, BM), g.B);
+    local_fwd_pp_kernel<HD, false><<<grid, FwdPPLayout<HD, false>::THREADS, smem, s>>>(
+        tq, tkv, tlo, tmx, tlat, tw, g, static_cast<bf16*>(local_out), lse, ep);
+  }
   return cudaGetLastError();
 }
 

@@ -22,7 +22,13 @@
 // mixed over its remote-operand region, so the groups never wait for each
 // other.
 
-template <int HD>
+// PAIR: two query tiles per CTA (ping-pong), 512 TMEM columns, one CTA per SM.
+// !PAIR: one query tile per CTA, 256 TMEM columns and under 113 KB of shared
+// memory, two CTAs per SM: one CTA's prologue and epilogue overlap the other's
+// main loop. The remote-tile operands then overlay the Q tile once its S MMAs
+// are done (hd 128), and the epilogue stages local_out / mixed over the K / V
+// ring.
+template <int HD, bool PAIR = true>
 struct FwdPPLayout {
   static constexpr int BNK = 64;
   static constexpr int QPANEL = BM * 128;
@@ -30,17 +36,23 @@ struct FwdPPLayout {
   static constexpr int QTILE = BM * HD * 2;
   static constexpr int KTILE = BNK * HD * 2;
   static constexpr int QA = 0;
-  static constexpr int QB = QA + QTILE;
-  static constexpr int NST = 3;                 // K/V ring depth
-  static constexpr int K = QB + QTILE;          // NST stages
+  static constexpr int QB = PAIR ? QA + QTILE : QA;
+  static constexpr int NST = PAIR ? 3 : 2;      // K/V ring depth
+  static constexpr int K = QB + QTILE;          // NST stages (QB = QA without PAIR)
   static constexpr int V = K + NST * KTILE;     // NST stages
   // per group x at X + x * XS: lat rows (128 x 64 bf16) then W_rout[h] (hd x 64)
-  static constexpr int X = V + NST * KTILE;
   static constexpr int XS = BM * 128 + HD * 128;
-  static constexpr int CST = X + 2 * XS;        // b_rout[h], g_local, g_remote (hd floats each)
-  static constexpr int BAR = CST + 3 * HD * 4;
+  static constexpr bool X_OVER_Q = !PAIR && XS <= QTILE;
+  static constexpr int X = X_OVER_Q ? QA : V + NST * KTILE;
+  static constexpr int CST = X_OVER_Q ? V + NST * KTILE : X + (PAIR ? 2 : 1) * XS;
+  static constexpr int BAR = CST + 3 * HD * 4;  // b_rout[h], g_local, g_remote (hd floats each)
   static constexpr int BYTES = BAR + 256;
-  static_assert(XS >= QTILE, "mixed tile staged over the remote operands");
+  static constexpr int TMEM_COLS = PAIR ? 512 : 256;
+  static constexpr int O_BASE = PAIR ? 256 : 128;  // O_x at O_BASE + x * hd
+  static constexpr int THREADS = PAIR ? 320 : 192;
+  static_assert(!PAIR || XS >= QTILE, "mixed tile staged over the remote operands");
+  static_assert(PAIR || NST * KTILE >= QTILE, "local_out / mixed staged over the K / V ring");
+  static_assert(PAIR || BYTES + 1024 <= 113 * 1024, "two CTAs per SM");
 };
 
 // per group g: S[2], P[2] (softmax arrivals), O[2] (PV done) — one barrier
@@ -55,7 +67,8 @@ enum {
   PP_O = 20,   // + 2*g + buffer
   PP_R = 24,   // + g
   PP_EP = 26,  // + g: epilogue tiles staged
-  PP_NB = 28
+  PP_SD = 28,  // group A's S MMAs done (!PAIR: Q free for the remote operands)
+  PP_NB = 29
 };
 
 // The running max of a row is only moved (and O rescaled) when the new
@@ -69,13 +82,13 @@ struct PPTiles {
   __device__ int n() const { return last >= first ? last - first + 1 : 0; }
 };
 
-template <int HD>
-__global__ void __launch_bounds__(320, 1)
+template <int HD, bool PAIR>
+__global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
     local_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kv,
                         const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_mx,
                         const __grid_constant__ CUtensorMap tm_lat, const __grid_constant__ CUtensorMap tm_w, Geom g,
                         bf16* __restrict__ local_out, float* __restrict__ lse_out, GateEpilogue ep) {
-  using L = FwdPPLayout<HD>;
+  using L = FwdPPLayout<HD, PAIR>;
   constexpr int BNK = L::BNK;
   extern __shared__ __align__(1024) uint8_t smem_pp[];
   uint8_t* smem = smem_pp;
@@ -89,10 +102,10 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   // heads fastest: CTAs that run together cover whole token rows of qkv
   const int h = blockIdx.x, b = blockIdx.z;
-  const int q0 = blockIdx.y * 2 * BM;
+  const int q0 = blockIdx.y * (PAIR ? 2 : 1) * BM;
   if (threadIdx.x == 0) LLATTN_TRACE_K(1, 0);
   const bool fuse = ep.lat != nullptr;
-  const bool has_b = q0 + BM < g.T;
+  const bool has_b = PAIR && q0 + BM < g.T;
   const int kbase = local_lo(g, q0);  // first key of the union range
   // key tiles [kbase + 64 j, +64) used by each query tile
   PPTiles tA, tB;
@@ -123,6 +136,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&bars[PP_P + x], BM);
       mbar_init(&bars[PP_O + x], 1);
     }
+    mbar_init(&bars[PP_SD], 1);
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars[PP_LW + x], BM + 1);
       mbar_init(&bars[PP_R + x], 1);
@@ -133,7 +147,7 @@ __global__ void __launch_bounds__(320, 1)
   }
   if (warp == 1) {
     __syncwarp();
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -147,13 +161,13 @@ __global__ void __launch_bounds__(320, 1)
       int issued = 0;
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_kv);
-      if (fuse) {
+      auto load_remote = [&]() {
         // remote-tile operands: W_rout[h] for each group, the lat rows of
         // token-wise queries (block-pooled ones are written by the threads),
         // and the epilogue's per-column constants (with group A's barrier)
         const bool lat_tma = g.qbs == 1;
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
+        for (int x = 0; x < (PAIR ? 2 : 1); ++x) {
           uint8_t* xr = smem + L::X + x * L::XS;
           mbar_expect_tx(&bars[PP_LW + x], HD * 128 + (lat_tma ? BM * 128 : 0) + (x == 0 ? 3 * HD * 4 : 0));
           tma_load_2d(&tm_w, &bars[PP_LW + x], xr + BM * 128, 0, h * HD);
@@ -163,11 +177,12 @@ __global__ void __launch_bounds__(320, 1)
         bulk_load(cst, ep.b_rout + (int64_t)h * HD, HD * 4, &bars[PP_LW + 0]);
         bulk_load(cst + HD, ep.g_local, HD * 4, &bars[PP_LW + 0]);
         bulk_load(cst + 2 * HD, ep.g_remote, HD * 4, &bars[PP_LW + 0]);
-      }
+      };
+      if (fuse && !L::X_OVER_Q) load_remote();
       if (nk > 0) {
-        mbar_expect_tx(&bars[PP_Q], 2 * L::QTILE);
+        mbar_expect_tx(&bars[PP_Q], (PAIR ? 2 : 1) * L::QTILE);
         tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QA, q0, h, b);
-        tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QB, q0 + BM, h, b);
+        if (PAIR) tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QB, q0 + BM, h, b);
       }
       for (int j = 0; j < nk; ++j) {
         const int s = j % L::NST;
@@ -182,13 +197,19 @@ __global__ void __launch_bounds__(320, 1)
         tma_load_tile(&tm_kv, &bars[PP_V + s], smem + L::V + s * L::KTILE, k0, 2 * g.H + h, b);
         issued = j + 1;
       }
+      if (fuse && L::X_OVER_Q && !*abort) {  // the remote operands go over Q once its S MMAs are done
+        if (mbar_wait(&bars[PP_SD], 0, abort, &g_fault_word))
+          load_remote();
+        else
+          raise_fault(kFaultProducer, abort);
+      }
       if (*abort) {
         // let the copies already issued land before the CTA can exit
         volatile int none = 0;
         volatile unsigned gnone = 0;
         if (nk > 0) mbar_wait(&bars[PP_Q], 0, &none, &gnone, 100000000ull);
         if (fuse)
-          for (int x = 0; x < 2; ++x) mbar_wait(&bars[PP_LW + x], 0, &none, &gnone, 100000000ull);
+          for (int x = 0; x < (PAIR ? 2 : 1); ++x) mbar_wait(&bars[PP_LW + x], 0, &none, &gnone, 100000000ull);
         for (int j = issued - L::NST < 0 ? 0 : issued - L::NST; j < issued; ++j) {
           mbar_wait(&bars[PP_K + j % L::NST], (j / L::NST) & 1, &none, &gnone, 100000000ull);
           mbar_wait(&bars[PP_V + j % L::NST], (j / L::NST) & 1, &none, &gnone, 100000000ull);
@@ -221,8 +242,13 @@ __global__ void __launch_bounds__(320, 1)
       LLATTN_TRACE_K(1, 2);
       uint64_t t_last = globaltimer_ns();
       uint32_t spin = 0;
+      bool sd_done = false;
       while (ok) {
         bool progress = false, all_done = true;
+        if (!sd_done && ns[0] == nx[0]) {  // group A's S MMAs all issued: Q_A free once they complete
+          mma_commit(&bars[PP_SD]);
+          sd_done = true;
+        }
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           if (!grp_on[x]) continue;
@@ -250,7 +276,7 @@ __global__ void __launch_bounds__(320, 1)
                 mbar_test_wait(&bars[PP_V + st], (j / L::NST) & 1)) {
               tc_fence_after();
               // P (bf16, packed two per column) over the first 32 columns of S buffer i&1
-              const uint32_t pa = tmem + x * 128 + (i & 1) * BNK, to = tmem + 256 + x * HD;
+              const uint32_t pa = tmem + x * 128 + (i & 1) * BNK, to = tmem + L::O_BASE + x * HD;
               const uint64_t dva = desc_sw128(smem_u32(smem + L::V + st * L::KTILE), L::KPANEL, 1024);
 #pragma unroll
               for (int kk = 0; kk < BNK / 16; ++kk)
@@ -309,13 +335,13 @@ __global__ void __launch_bounds__(320, 1)
     const int lo = valid ? local_lo(g, t) : 0x7fffffff;
     const float sc = g.scale * kLog2e;
     float m = -INFINITY, l = 0.f;  // m: reference max (log2 domain) of P and O
-    const uint32_t tS = tmem + grp * 128, tO = tmem + 256 + grp * HD, tR = tmem + grp * 128;
+    const uint32_t tS = tmem + grp * 128, tO = tmem + L::O_BASE + grp * HD, tR = tmem + grp * 128;
     uint8_t* xreg = smem + L::X + grp * L::XS;  // this group's lat rows, then W_rout[h]
     float* cst = reinterpret_cast<float*>(smem + L::CST);
     bool ok = true;
     // block-pooled latent queries: this row's lat row (token-wise ones and
-    // W_rout come by TMA)
-    if (fuse) {
+    // W_rout come by TMA); with the operands over Q, after its S MMAs
+    auto write_lat_rows = [&]() {
       if (g.qbs != 1) {
         const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.lat) +
                                                           ((int64_t)b * g.Tq + (valid ? t / g.qbs : 0)) * 64);
@@ -325,7 +351,8 @@ __global__ void __launch_bounds__(320, 1)
         fence_async_smem();
       }
       mbar_arrive(&bars[PP_LW + grp]);
-    }
+    };
+    if (fuse && !L::X_OVER_Q) write_lat_rows();
     if (!(grp == 1 && !has_b)) {
       const uint64_t sc2 = f2_pack(sc, sc);
       for (int i = 0; ok && i < n_mine; ++i) {
@@ -411,6 +438,10 @@ __global__ void __launch_bounds__(320, 1)
         if (row == 0) LLATTN_TRACE_K(1, 16 + grp * 24 + i);
       }
       if (!ok) raise_fault(kFaultSoftmax, abort);
+      if (ok && fuse && L::X_OVER_Q) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_SD], 0, abort, &g_fault_word));
+        if (ok) write_lat_rows();
+      }
       if (ok && n_mine > 0)
         ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_O + 2 * grp + ((n_mine - 1) & 1)], ((n_mine - 1) >> 1) & 1,
                                                abort, &g_fault_word));
@@ -432,8 +463,8 @@ __global__ void __launch_bounds__(320, 1)
           // remote = R + b; pass 2: local (over this group's Q tile) and
           // mixed = w local + (1 - w) remote (over its remote operands), then
           // both 128-row tiles to global by TMA (3-D maps clip rows past T)
-          uint8_t* ltile = smem + (grp ? L::QB : L::QA);
-          uint8_t* mtile = xreg;
+          uint8_t* ltile = PAIR ? smem + (grp ? L::QB : L::QA) : smem + L::K;
+          uint8_t* mtile = PAIR ? xreg : smem + L::V;
           auto tile_chunk = [&](uint8_t* tile, int c) -> uint4* {  // 16-byte chunk c of this row, SW128
             return reinterpret_cast<uint4*>(tile + (c >> 3) * (BM * 128) + row * 128 + (((c & 7) ^ (row & 7)) * 16));
           };
@@ -540,6 +571,6 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, L::TMEM_COLS);
   }
 }
