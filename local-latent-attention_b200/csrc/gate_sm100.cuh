@@ -14,19 +14,28 @@
 // TMA (MN-major A operand), lat tiles written by threads (MN-major B), the
 // column sums for db taken from the same shared-memory tiles.
 
-constexpr int kGateMaxHeads = 32;  // per-head gate grads kept in shared memory
+// G warp groups per CTA, each taking every G-th head with its own buffers.
+// G = 2: 512 TMEM columns, ~200 KB of shared memory, one CTA per SM.
+// G = 1: 256 TMEM columns and < 113 KB, two CTAs per SM: one CTA's head chain
+// (load, two passes, stores) overlaps the other's.
+template <int G>
+constexpr int gate_max_heads() { return G == 2 ? 32 : 24; }  // per-head ds rows kept in shared memory
+constexpr int kGateMaxHeads = 32;
 
-template <int HD>
+template <int HD, int G = 2>
 struct GbLayout {
   static constexpr int TILE = BM * HD * 2;         // 128 rows x HD bf16 (HD/64 panels of 16 KB)
   static constexpr int LAT = 0;                    // 128 x 64 bf16
   static constexpr int W = LAT + BM * 128;         // per group: HD x 64 bf16
-  static constexpr int LT = W + 2 * HD * 128;      // per group: local_out tile of the head, overwritten by dL
-  static constexpr int DM = LT + 2 * TILE;         // per group: dmixed tile, overwritten by dR
-  static constexpr int RED = DM + 2 * TILE;        // 8 warps x HD floats (dg_local partials)
-  static constexpr int DSH = RED + 8 * HD * 4;     // [kGateMaxHeads][128] gate grad ds per head and row
-  static constexpr int BAR = DSH + kGateMaxHeads * BM * 4;
+  static constexpr int LT = W + G * HD * 128;      // per group: local_out tile of the head, overwritten by dL
+  static constexpr int DM = LT + G * TILE;         // per group: dmixed tile, overwritten by dR
+  static constexpr int RED = DM + G * TILE;        // 4G warps x HD floats (dg_local partials)
+  static constexpr int DSH = RED + 4 * G * HD * 4; // [max heads][128] gate grad ds per head and row
+  static constexpr int BAR = DSH + gate_max_heads<G>() * BM * 4;
   static constexpr int BYTES = BAR + 256;
+  static constexpr int THREADS = 64 + 128 * G;
+  static constexpr int TMEM_COLS = G == 2 ? 512 : 256;
+  static_assert(G == 2 || BYTES + 1024 <= 115 * 1024, "two CTAs per SM");
 };
 
 // per group g (0/1): W ready, R computed, dL/dR tiles ready, dlat MMA done,
@@ -56,14 +65,14 @@ __device__ __forceinline__ float butterfly32(float (&v)[32], int lane) {
 //   dg_r = -sum_{t,h} ds R_h = -sum_h (S1_h W_h^T + S0_h b_h),
 //   S1_h = sum_t ds[t,h] lat[t], S0_h = sum_t ds[t,h],
 // formed from ds kept in shared memory after the head loop.
-template <int HD>
-__global__ void __launch_bounds__(320, 1)
+template <int HD, int G>
+__global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
     gate_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_dm,
                        const __grid_constant__ CUtensorMap tm_dl, const __grid_constant__ CUtensorMap tm_dr,
                        Geom g, const bf16* __restrict__ lat, const bf16* __restrict__ w_rout,
                        const float* __restrict__ b_rout, const float* __restrict__ gl, const float* __restrict__ gr,
                        float* __restrict__ delta, float* __restrict__ dlat_tok, float* __restrict__ dg_part) {
-  using L = GbLayout<HD>;
+  using L = GbLayout<HD, G>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
@@ -76,7 +85,7 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) LLATTN_TRACE_K(3, 0);
   if (threadIdx.x == 0) {
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < G; ++s) {
       mbar_init(&bars[GB_W + s], BM);
       mbar_init(&bars[GB_R + s], 1);
       mbar_init(&bars[GB_DR + s], BM);
@@ -88,19 +97,19 @@ __global__ void __launch_bounds__(320, 1)
   }
   if (warp == 1) {
     __syncwarp();
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // R of group g at [g*HD, (g+1)*HD); dlat at 256
-  const uint32_t tDL = tmem + 256;
+  const uint32_t tmem = *tmem_slot;  // R of group g at [g*HD, (g+1)*HD); dlat at G*128
+  const uint32_t tDL = tmem + G * 128;
   float* red = reinterpret_cast<float*>(smem + L::RED);
 
   if (warp == 0) {
-    // TMA producer. Head h uses group h&1's buffers; before loading head h
-    // the producer stores head h-2's dL / dR tiles (written in place over the
+    // TMA producer. Head h uses group h%G's buffers; before loading head h
+    // the producer stores head h-G's dL / dR tiles (written in place over the
     // local_out / dmixed tiles; 3-D (d, T, B) maps clip rows past T), waits
     // for its dlat MMA (reads dR) and for the stores to have read shared memory.
     if (lane == 0) {
@@ -110,7 +119,7 @@ __global__ void __launch_bounds__(320, 1)
       int issued = 0;
       bool ok = true;
       auto store_head = [&](int h) -> bool {
-        const int grp = h & 1, n = h >> 1;
+        const int grp = h % G, n = h / G;
         if (!mbar_wait(&bars[GB_DR + grp], n & 1, abort, &g_fault_word)) return false;
 #pragma unroll
         for (int p = 0; p < HD / 64; ++p) {
@@ -121,9 +130,9 @@ __global__ void __launch_bounds__(320, 1)
         return true;
       };
       for (int h = 0; h < H; ++h) {
-        const int grp = h & 1, n = h >> 1;
+        const int grp = h % G, n = h / G;
         if (n >= 1) {
-          if (!(ok = store_head(h - 2))) break;
+          if (!(ok = store_head(h - G))) break;
           if (!(ok = mbar_wait(&bars[GB_DL + grp], (n - 1) & 1, abort, &g_fault_word))) break;
           tma_store_wait_read();
         }
@@ -136,14 +145,14 @@ __global__ void __launch_bounds__(320, 1)
         }
         issued = h + 1;
       }
-      for (int h = H - 2 < 0 ? 0 : H - 2; ok && h < H; ++h) ok = store_head(h);
+      for (int h = H - G < 0 ? 0 : H - G; ok && h < H; ++h) ok = store_head(h);
       tma_store_wait_read();
       if (!ok) {
         raise_fault(kFaultProducer, abort);
         volatile int none = 0;
         volatile unsigned gnone = 0;
-        for (int h = issued - 2 < 0 ? 0 : issued - 2; h < issued; ++h)
-          mbar_wait(&bars[GB_F + (h & 1)], (h >> 1) & 1, &none, &gnone, 100000000ull);
+        for (int h = issued - G < 0 ? 0 : issued - G; h < issued; ++h)
+          mbar_wait(&bars[GB_F + h % G], (h / G) & 1, &none, &gnone, 100000000ull);
       }
     }
   } else if (warp == 1) {
@@ -154,8 +163,8 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       // head h belongs to group h&1 and is that group's (h>>1)-th head
       auto issue_r = [&](int h) -> bool {
-        const int s = h & 1;
-        if (!mbar_wait(&bars[GB_W + s], (h >> 1) & 1, abort, &g_fault_word)) return false;
+        const int s = h % G;
+        if (!mbar_wait(&bars[GB_W + s], (h / G) & 1, abort, &g_fault_word)) return false;
         tc_fence_after();
         const uint64_t dw = desc_sw128(smem_u32(smem + L::W + s * HD * 128), 16, 1024);
 #pragma unroll
@@ -164,11 +173,10 @@ __global__ void __launch_bounds__(320, 1)
         mma_commit(&bars[GB_R + s]);
         return true;
       };
-      ok = issue_r(0);
-      if (ok && H > 1) ok = issue_r(1);
+      for (int x = 0; ok && x < G && x < H; ++x) ok = issue_r(x);
       for (int h = 0; ok && h < H; ++h) {
-        const int s = h & 1;
-        if (!(ok = mbar_wait(&bars[GB_DR + s], (h >> 1) & 1, abort, &g_fault_word))) break;
+        const int s = h % G;
+        if (!(ok = mbar_wait(&bars[GB_DR + s], (h / G) & 1, abort, &g_fault_word))) break;
         tc_fence_after();
         const uint64_t dda = desc_sw128(smem_u32(smem + L::DM + s * L::TILE), 16, 1024);
         const uint64_t dwm = desc_sw128(smem_u32(smem + L::W + s * HD * 128), 0, 1024);
@@ -177,7 +185,7 @@ __global__ void __launch_bounds__(320, 1)
           mma_bf16(tDL, desc_add(dda, (kk / 4) * (BM * 128) + (kk % 4) * 32), desc_add(dwm, kk * 2048), idL,
                    (h > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&bars[GB_DL + s]);
-        if (h + 2 < H && !(ok = issue_r(h + 2))) break;
+        if (h + G < H && !(ok = issue_r(h + G))) break;
       }
       if (!ok) raise_fault(kFaultMma, abort);
     }
@@ -214,8 +222,8 @@ __global__ void __launch_bounds__(320, 1)
     };
     const float4* gl4 = reinterpret_cast<const float4*>(gl);
     const float4* gr4 = reinterpret_cast<const float4*>(gr);
-    for (int h = grp; h < H; h += 2) {
-      const int n = h >> 1;  // this group's n-th head
+    for (int h = grp; h < H; h += G) {
+      const int n = h / G;  // this group's n-th head
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_R + grp], n & 1, abort, &g_fault_word));
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_F + grp], n & 1, abort, &g_fault_word));
       if (!ok) break;
@@ -306,16 +314,16 @@ __global__ void __launch_bounds__(320, 1)
       mbar_arrive(&bars[GB_DR + grp]);
       if (row == 0 && h < 12) LLATTN_TRACE_K(3, 38 + h);
       // W buffer reuse: the dlat MMA of head h must have read it
-      if (h + 2 < H) {
+      if (h + G < H) {
         ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_DL + grp], n & 1, abort, &g_fault_word));
         if (!ok) break;
         if (row == 0 && h < 10) LLATTN_TRACE_K(3, 50 + h);
-        write_w(h + 2);
+        write_w(h + G);
       }
     }
     if (!ok) raise_fault(kFaultSoftmax, abort);
     if (grp == 0) {
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_DL + ((H - 1) & 1)], ((H - 1) >> 1) & 1, abort,
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_DL + ((H - 1) % G)], ((H - 1) / G) & 1, abort,
                                                      &g_fault_word));
       if (!ok) {
         raise_fault(kFaultEpilogue, abort);
@@ -345,7 +353,7 @@ __global__ void __launch_bounds__(320, 1)
   for (int e = threadIdx.x; e < HD; e += blockDim.x) {
     float v = 0.f;
 #pragma unroll
-    for (int w8 = 0; w8 < 8; ++w8) v += red[w8 * HD + e];
+    for (int w8 = 0; w8 < 4 * G; ++w8) v += red[w8 * HD + e];
     dg_part[part + e] = v;
   }
   // dg_remote partial [cta][HD, 2HD): S1_h[e] = sum_rows ds lat[row, e] and
@@ -390,7 +398,7 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, L::TMEM_COLS);
   }
 }
 

@@ -242,20 +242,20 @@ cudaError_t dkv_hd(const Geom& g, const void* qkv, const void* dl, const float* 
   return cudaGetLastError();
 }
 
-template <int HD>
+template <int HD, int G>
 cudaError_t gate_bwd_hd(const Geom& g, const GateBwd& a, cudaStream_t s) {
   CUtensorMap tlo, tdm, tdl, tdr;
   if (!make_2d_map(&tlo, a.local_out, (int64_t)g.B * g.T, g.d, 128) ||
       !make_2d_map(&tdm, a.dmixed, (int64_t)g.B * g.T, g.d, 128) || !make_btd_map(&tdl, a.dl, g.B, g.T, g.d) ||
       !make_btd_map(&tdr, a.dr, g.B, g.T, g.d))
     return cudaErrorInvalidValue;
-  const int smem = std::max(GbLayout<HD>::BYTES + 1024, 116 * 1024);
-  cudaError_t e = cudaFuncSetAttribute(gate_bwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const int smem = GbLayout<HD, G>::BYTES + 1024;
+  cudaError_t e = cudaFuncSetAttribute(gate_bwd_tc_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.T, BM), g.B);
-  gate_bwd_tc_kernel<HD><<<grid, 320, smem, s>>>(tlo, tdm, tdl, tdr, g, static_cast<const bf16*>(a.lat),
-                                                 static_cast<const bf16*>(a.w_rout), a.b_rout, a.g_local, a.g_remote,
-                                                 a.delta, a.dlat_tok, a.dg_part);
+  gate_bwd_tc_kernel<HD, G><<<grid, GbLayout<HD, G>::THREADS, smem, s>>>(
+      tlo, tdm, tdl, tdr, g, static_cast<const bf16*>(a.lat), static_cast<const bf16*>(a.w_rout), a.b_rout, a.g_local,
+      a.g_remote, a.delta, a.dlat_tok, a.dg_part);
   return cudaGetLastError();
 }
 
@@ -264,8 +264,13 @@ cudaError_t gate_bwd_hd(const Geom& g, const GateBwd& a, cudaStream_t s) {
 int gate_bwd_ctas(const Geom& g) { return g.B * cdiv(g.T, BM); }
 
 cudaError_t launch_gate_bwd(const Geom& g, const GateBwd& a, cudaStream_t s) {
-  if (g.hd == 64) return gate_bwd_hd<64>(g, a, s);
-  return gate_bwd_hd<128>(g, a, s);
+  // one head group per CTA, two CTAs per SM, unless the heads' ds rows do not fit
+  if (g.H <= gate_max_heads<1>()) {
+    if (g.hd == 64) return gate_bwd_hd<64, 1>(g, a, s);
+    return gate_bwd_hd<128, 1>(g, a, s);
+  }
+  if (g.hd == 64) return gate_bwd_hd<64, 2>(g, a, s);
+  return gate_bwd_hd<128, 2>(g, a, s);
 }
 
 cudaError_t launch_rout_dw(const Geom& g, const void* dr, const void* lat, float* dw_part, float* db_part,
