@@ -82,7 +82,7 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
   L.n_gate_cta = g.B * cdiv(g.T, L.gate_tok);
   const int rows = g.B * g.Tq;
   // token splits of the dW_rout reduction (enough CTAs to fill the GPU)
-  L.n_split_w = std::max(1, std::min(cdiv(g.B * g.T, 64), cdiv(2 * 148, cdiv(g.d, 128))));
+  L.n_split_w = std::max(1, std::min(cdiv(g.B * g.T, 64), (2 * 148) / cdiv(g.d, 128)));
   // row splits of the latent backward: (b, latent head, split) CTAs, about two per SM
   L.n_split_lat = std::max(1, std::min(cdiv(g.Tq, 64), (2 * 148) / (g.B * g.Lh)));
   size_t off = 0;

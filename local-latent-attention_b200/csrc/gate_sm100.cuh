@@ -409,15 +409,22 @@ constexpr int DW_ST = 4;  // pipeline stages of 64 tokens
 struct DwLayout {
   static constexpr int A = 0;                    // DW_ST x (64 tokens x 128 cols bf16) = 16 KB each
   static constexpr int B = A + DW_ST * 16384;    // DW_ST x (64 tokens x 64 bf16) = 8 KB each
-  static constexpr int BAR = B + DW_ST * 8192;
+  static constexpr int ONES = B + DW_ST * 8192;  // 16 x 64 bf16 ones: B operand of the column-sum MMA
+  static constexpr int BAR = ONES + 2048;
   static constexpr int BYTES = BAR + 256;
 };
 
 enum { DW_FA = 0, DW_FB = DW_ST, DW_E = 2 * DW_ST, DW_DONE = 3 * DW_ST, DW_NB = 3 * DW_ST + 1 };
 
-__global__ void __launch_bounds__(192, 1)
-    rout_dw_tc_kernel(const __grid_constant__ CUtensorMap tm_dr, Geom g, const bf16* __restrict__ lat,
-                      float* __restrict__ dw_part, float* __restrict__ db_part, int n_split) {
+// dW partial [128 columns of d x 64] over this split's tokens, and db as a
+// second MMA against a ones tile (D2[:, j] = sum over tokens of dR, for
+// every j): the tensor pipe does both reductions. Token-wise queries
+// (qbs = 1): the lat rows of a 64-token chunk are one TMA box; block-pooled
+// ones are gathered by the threads.
+__global__ void __launch_bounds__(192, 2)
+    rout_dw_tc_kernel(const __grid_constant__ CUtensorMap tm_dr, const __grid_constant__ CUtensorMap tm_lat, Geom g,
+                      const bf16* __restrict__ lat, float* __restrict__ dw_part, float* __restrict__ db_part,
+                      int n_split) {
   using L = DwLayout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -427,9 +434,12 @@ __global__ void __launch_bounds__(192, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int c0 = blockIdx.x * 128, split = blockIdx.y;
   const int n_tok = g.B * g.T;
+  // split boundaries are multiples of 64 tokens; the last chunk's rows past
+  // n_tok are zero-filled by the copies (or zeroed by the gathering threads)
   const int per = cdiv(cdiv(n_tok, n_split), 64) * 64;
   const int na = split * per, nb = min(n_tok, na + per);
   const int nch = nb > na ? cdiv(nb - na, 64) : 0;
+  const bool lat_tma = g.qbs == 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < DW_ST; ++s) {
@@ -441,19 +451,25 @@ __global__ void __launch_bounds__(192, 1)
     *abort = 0;
     fence_barrier_init();
   }
+  {  // ones tile, K-major 128-byte-swizzled (every element 1.0, so the swizzle is moot)
+    uint4* o = reinterpret_cast<uint4*>(smem + L::ONES);
+    for (int i = threadIdx.x; i < 2048 / 16; i += blockDim.x) o[i] = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+    fence_async_smem();
+  }
   if (warp == 1) {
     __syncwarp();
-    tmem_alloc(tmem_slot, 64);
+    tmem_alloc(tmem_slot, 128);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *tmem_slot;  // dW partial at [0, 64), column sums at [64, 80)
 
   if (warp == 0) {
     if (lane == 0 && nch > 0) {
       prefetch_tmap(&tm_dr);
+      if (lat_tma) prefetch_tmap(&tm_lat);
       int issued = 0;
       for (int i = 0; i < nch; ++i) {
         const int s = i % DW_ST;
@@ -461,11 +477,10 @@ __global__ void __launch_bounds__(192, 1)
           raise_fault(kFaultProducer, abort);
           break;
         }
-        mbar_expect_tx(&bars[DW_FA + s], 16384);
-        // rows past this split's range belong to the next split: they are
-        // loaded but zeroed out of the B tile, so they contribute nothing
+        mbar_expect_tx(&bars[DW_FA + s], 16384 + (lat_tma ? 8192 : 0));
         tma_load_2d(&tm_dr, &bars[DW_FA + s], smem + L::A + s * 16384, c0, na + i * 64);
         tma_load_2d(&tm_dr, &bars[DW_FA + s], smem + L::A + s * 16384 + 8192, c0 + 64, na + i * 64);
+        if (lat_tma) tma_load_2d(&tm_lat, &bars[DW_FA + s], smem + L::B + s * 8192, 0, na + i * 64);
         issued = i + 1;
       }
       if (*abort) {
@@ -478,34 +493,38 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     if (lane == 0 && nch > 0) {
       constexpr uint32_t id = idesc_bf16_f32(128, 64, true, true);
+      constexpr uint32_t id1 = idesc_bf16_f32(128, 16, true, false);
+      const uint64_t d1 = desc_sw128(smem_u32(smem + L::ONES), 16, 1024);
       bool ok = true;
       for (int i = 0; ok && i < nch; ++i) {
         const int s = i % DW_ST;
         if (!(ok = mbar_wait(&bars[DW_FA + s], (i / DW_ST) & 1, abort, &g_fault_word))) break;
-        if (!(ok = mbar_wait(&bars[DW_FB + s], (i / DW_ST) & 1, abort, &g_fault_word))) break;
+        if (!lat_tma && !(ok = mbar_wait(&bars[DW_FB + s], (i / DW_ST) & 1, abort, &g_fault_word))) break;
         tc_fence_after();
         const uint64_t da = desc_sw128(smem_u32(smem + L::A + s * 16384), 8192, 1024);
         const uint64_t db = desc_sw128(smem_u32(smem + L::B + s * 8192), 0, 1024);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(tmem, desc_add(da, kk * 2048), desc_add(db, kk * 2048), id, (i > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          mma_bf16(tmem, desc_add(da, kk * 2048), desc_add(db, kk * 2048), id, acc);
+          mma_bf16(tmem + 64, desc_add(da, kk * 2048), desc_add(d1, kk * 32), id1, acc);
+        }
         mma_commit(&bars[DW_E + s]);
       }
       mma_commit(&bars[DW_DONE]);
       if (!ok) raise_fault(kFaultMma, abort);
     }
   } else {
-    const int tid = threadIdx.x - 64;  // 0..127: column c0 + tid, and B-tile writer
-    float db = 0.f;
+    const int tid = threadIdx.x - 64;  // 0..127
     bool ok = true;
-    for (int i = 0; i < nch; ++i) {
-      const int s = i % DW_ST;
-      if (i >= DW_ST) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars[DW_E + s], ((i / DW_ST) - 1) & 1, abort, &g_fault_word));
-        if (!ok) break;
-      }
-      // B tile: 64 token rows of lat (row r of token n = b*T + t -> lat row b*Tq + t/qbs)
-      {
+    if (!lat_tma) {
+      for (int i = 0; i < nch; ++i) {
+        const int s = i % DW_ST;
+        if (i >= DW_ST) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars[DW_E + s], ((i / DW_ST) - 1) & 1, abort, &g_fault_word));
+          if (!ok) break;
+        }
+        // B tile: 64 token rows of lat (row r of token n = b*T + t -> lat row b*Tq + t/qbs)
         const int r = tid >> 1, half = tid & 1;
         const int n = na + i * 64 + r;
         uint8_t* d = smem + L::B + s * 8192 + r * 128;
@@ -519,22 +538,11 @@ __global__ void __launch_bounds__(192, 1)
           for (int c = half * 4; c < half * 4 + 4; ++c)
             *reinterpret_cast<uint4*>(d + ((c ^ (r & 7)) * 16)) = make_uint4(0u, 0u, 0u, 0u);
         }
+        fence_async_smem();
+        mbar_arrive(&bars[DW_FB + s]);
       }
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars[DW_FA + s], (i / DW_ST) & 1, abort, &g_fault_word));
-      if (!ok) break;
-      // db: column sum of the dR tile over its valid rows
-      {
-        const uint8_t* a = smem + L::A + s * 16384 + (tid >> 6) * 8192;
-        const int cc = tid & 63, chunk = cc >> 3, e = cc & 7;
-        const int rows = min(64, nb - (na + i * 64));
-        for (int r = 0; r < rows; ++r)
-          db += __bfloat162float(*reinterpret_cast<const bf16*>(a + r * 128 + ((chunk ^ (r & 7)) * 16) + e * 2));
-      }
-      fence_async_smem();
-      mbar_arrive(&bars[DW_FB + s]);
+      if (!ok) raise_fault(kFaultSoftmax, abort);
     }
-    if (!ok) raise_fault(kFaultSoftmax, abort);
-    const int c = c0 + tid;
     if (ok && nch > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[DW_DONE], 0, abort, &g_fault_word));
     if (!ok) {
       raise_fault(kFaultEpilogue, abort);
@@ -561,7 +569,15 @@ __global__ void __launch_bounds__(192, 1)
                 __uint_as_float(r[4 * q + 3]));
         }
       }
-      if (c < g.d) db_part[(int64_t)split * g.d + c] = db;
+      uint32_t r1[16];
+      if (nch > 0) {
+        tmem_ld16(tmem + lane_off + 64, r1);
+        tmem_ld_wait();
+      } else {
+        r1[0] = 0u;
+      }
+      if (c0 + m < g.d) db_part[(int64_t)split * g.d + c0 + m] = __uint_as_float(r1[0]);
+      (void)tid;
     }
   }
   tc_fence_before();
@@ -569,7 +585,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 64);
+    tmem_dealloc(tmem, 128);
   }
 }
 

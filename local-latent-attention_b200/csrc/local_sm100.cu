@@ -275,13 +275,19 @@ cudaError_t launch_gate_bwd(const Geom& g, const GateBwd& a, cudaStream_t s) {
 
 cudaError_t launch_rout_dw(const Geom& g, const void* dr, const void* lat, float* dw_part, float* db_part,
                            int n_split, cudaStream_t s) {
-  CUtensorMap tm;
+  CUtensorMap tm, tl;
   if (!make_2d_map(&tm, dr, (int64_t)g.B * g.T, g.d)) return cudaErrorInvalidValue;
-  const int smem = std::max(DwLayout::BYTES + 1024, 116 * 1024);
+  // token-wise queries: the lat rows of a 64-token chunk are one box of [B*Tq, 64]
+  if (g.qbs == 1) {
+    if (!make_2d_map(&tl, lat, (int64_t)g.B * g.Tq, 64, 64)) return cudaErrorInvalidValue;
+  } else {
+    tl = tm;
+  }
+  const int smem = DwLayout::BYTES + 1024;  // < 113 KB: two CTAs per SM
   cudaError_t e = cudaFuncSetAttribute(rout_dw_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.d, 128), n_split);
-  rout_dw_tc_kernel<<<grid, 192, smem, s>>>(tm, g, static_cast<const bf16*>(lat), dw_part, db_part, n_split);
+  rout_dw_tc_kernel<<<grid, 192, smem, s>>>(tm, tl, g, static_cast<const bf16*>(lat), dw_part, db_part, n_split);
   return cudaGetLastError();
 }
 
