@@ -15,81 +15,6 @@
 namespace llattn {
 namespace {
 
-constexpr int kRowsFwd = 128;  // query rows per CTA (one thread each)
-constexpr int kKeyTile = 64;   // chunk keys staged per shared-memory tile
-
-template <typename T, int L>
-__global__ void __launch_bounds__(kRowsFwd) latent_fwd_kernel(Geom g, const T* __restrict__ rq,
-                                                              const T* __restrict__ gkv,
-                                                              T* __restrict__ lat,
-                                                              float* __restrict__ lat_lse) {
-  __shared__ float sk[kKeyTile][L];
-  __shared__ float sv[kKeyTile][L];
-  const int b = blockIdx.z, lh = blockIdx.y;
-  const int r = blockIdx.x * kRowsFwd + threadIdx.x;
-  const bool valid = r < g.Tq;
-  const int qid = valid ? row_qid(g, r) : 0;
-  const int max_qid = row_qid(g, min((int)(blockIdx.x * kRowsFwd + kRowsFwd - 1), g.Tq - 1));
-
-  float q[L];
-#pragma unroll
-  for (int e = 0; e < L; ++e) {
-    q[e] = (valid && e < g.ldh)
-               ? to_f<T>(rq[((int64_t)(b * g.Tq + r) * g.Lh + lh) * g.ldh + e]) * g.lat_scale
-               : 0.f;
-  }
-  float m = -INFINITY, l = 0.f, acc[L];
-#pragma unroll
-  for (int e = 0; e < L; ++e) acc[e] = 0.f;
-
-  for (int j0 = 0; j0 < max_qid; j0 += kKeyTile) {
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < kKeyTile * L; idx += kRowsFwd) {
-      const int jj = idx / L, e = idx % L, j = j0 + jj;
-      float kv = 0.f, vv = 0.f;
-      if (j < g.Nc && e < g.ldh) {
-        const int64_t base = ((int64_t)(b * g.Nc + j) * 2 * g.Lh + lh) * g.ldh + e;
-        kv = to_f<T>(gkv[base]);
-        vv = to_f<T>(gkv[base + (int64_t)g.Lh * g.ldh]);
-      }
-      sk[jj][e] = kv;
-      sv[jj][e] = vv;
-    }
-    __syncthreads();
-    const int n = min(kKeyTile, qid - j0);
-    for (int u0 = 0; u0 < n; u0 += 16) {
-      float s[16];
-      float mx = m;
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        float dot = 0.f;
-#pragma unroll
-        for (int e = 0; e < L; ++e) dot = fmaf(q[e], sk[u0 + u][e], dot);
-        s[u] = (u0 + u < n) ? dot : -INFINITY;
-        mx = fmaxf(mx, s[u]);
-      }
-      const float corr = expf(m - mx);  // m = -inf on the first tile -> 0
-      l *= corr;
-#pragma unroll
-      for (int e = 0; e < L; ++e) acc[e] *= corr;
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const float p = expf(s[u] - mx);
-        l += p;
-#pragma unroll
-        for (int e = 0; e < L; ++e) acc[e] = fmaf(p, sv[u0 + u][e], acc[e]);
-      }
-      m = mx;
-    }
-  }
-  if (!valid) return;
-  const float inv = qid > 0 ? 1.f / l : 0.f;
-  T* dst = lat + (int64_t)(b * g.Tq + r) * g.Ld + lh * g.ldh;
-#pragma unroll
-  for (int e = 0; e < L; ++e)
-    if (e < g.ldh) dst[e] = from_f<T>(acc[e] * inv);
-  lat_lse[(int64_t)(b * g.Lh + lh) * g.Tq + r] = qid > 0 ? m + logf(l) : INFINITY;
-}
 
 // ---------------------------------------------------------------------------
 // Backward. With P = softmax(s) (s = lat_scale * rq.gk), dP = dlat.gv,
@@ -372,21 +297,185 @@ __global__ void __launch_bounds__(256, 2) latent_bwd_kernel(Geom g, const T* __r
   }
 }
 
-template <typename To>
-__global__ void reduce_parts_kernel(const float* __restrict__ part, int n_part, int64_t n,
-                                    To* __restrict__ out) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
+// Forward, blocked: a CTA per (64-row block, latent head, b), 256 threads.
+// Per 64-key tile: S = rq gk^T as 4-row x 4-key register blocks over float4
+// shared-memory operands (the layout of the backward), online softmax in
+// log2 units (row max / sum across the 16 threads of a row by shuffles), P
+// through shared memory, then O += P gv with each thread owning one row and a
+// quarter of the columns. lat_lse = m + ln(l) (natural log) as the backward
+// expects; rows that see no chunk (qid = 0) output 0 (models.py:366-373).
+template <typename T, int L>
+__global__ void __launch_bounds__(256) latent_fwd_blocked_kernel(Geom g, const T* __restrict__ rq,
+                                                                 const T* __restrict__ gkv, T* __restrict__ lat,
+                                                                 float* __restrict__ lat_lse) {
+  using S = LatBwdSmem<L>;
+  constexpr int LS = S::LS, PS = S::PS, EQ = L / 4;
+  extern __shared__ float4 smem_latf4[];
+  float* sm = reinterpret_cast<float*>(smem_latf4);
+  float *s_rq = sm + S::RQ, *s_k = sm + S::K, *s_v = sm + S::V, *s_p = sm + S::P;
+  float* s_alpha = sm + S::LSE;   // per row: rescale of the running output for this tile
+  float* s_l = sm + S::DELTA;     // per row: final normaliser
+  int* s_qid = reinterpret_cast<int*>(sm + S::QID);
+  const int b = blockIdx.z, lh = blockIdx.y, r0 = blockIdx.x * kLatRows, tid = threadIdx.x;
+  const int rg = tid >> 4, kg = tid & 15;  // S block: rows 4rg + i, keys kg + 16u
+  const int own = tid >> 2, eq = tid & 3;  // output row and e-quarter
+  const float sc2 = g.lat_scale * kLatLog2e;
+
+  for (int idx = tid; idx < kLatRows * L; idx += 256) {
+    const int i = idx / L, e = idx % L, r = r0 + i;
     float a = 0.f;
-    for (int p = 0; p < n_part; ++p) a += part[(int64_t)p * n + i];
-    out[i] = from_f<To>(a);
+    if (r < g.Tq && e < g.ldh) a = to_f<T>(rq[((int64_t)(b * g.Tq + r) * g.Lh + lh) * g.ldh + e]) * sc2;
+    s_rq[i * LS + e] = a;
+  }
+  if (tid < kLatRows) s_qid[tid] = r0 + tid < g.Tq ? row_qid(g, r0 + tid) : 0;
+  const int jmax = row_qid(g, min(r0 + kLatRows - 1, g.Tq - 1));
+  float m[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+  }
+  float acc[EQ];
+#pragma unroll
+  for (int u = 0; u < EQ; ++u) acc[u] = 0.f;
+
+  for (int j0 = 0; j0 < jmax; j0 += kLatKeys) {
+    __syncthreads();
+    for (int idx = tid; idx < kLatKeys * L; idx += 256) {
+      const int jj = idx / L, e = idx % L, j = j0 + jj;
+      float kv = 0.f, vv = 0.f;
+      if (j < g.Nc && e < g.ldh) {
+        const int64_t base = ((int64_t)(b * g.Nc + j) * 2 * g.Lh + lh) * g.ldh + e;
+        kv = to_f<T>(gkv[base]);
+        vv = to_f<T>(gkv[base + (int64_t)g.Lh * g.ldh]);
+      }
+      s_k[jj * LS + e] = kv;
+      s_v[jj * LS + e] = vv;
+    }
+    __syncthreads();
+    float sa[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) sa[i][u] = 0.f;
+#pragma unroll
+    for (int e = 0; e < L; e += 4) {
+      float4 a[4], k[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = *reinterpret_cast<const float4*>(s_rq + (4 * rg + i) * LS + e);
+        k[i] = *reinterpret_cast<const float4*>(s_k + (kg + 16 * i) * LS + e);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          sa[i][u] = fmaf(a[i].x, k[u].x, fmaf(a[i].y, k[u].y, fmaf(a[i].z, k[u].z, fmaf(a[i].w, k[u].w, sa[i][u]))));
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int ri = 4 * rg + i, qid = s_qid[ri];
+      float tm = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (j0 + kg + 16 * u >= qid) sa[i][u] = -INFINITY;
+        tm = fmaxf(tm, sa[i][u]);
+      }
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, o));
+      const float mn = fmaxf(m[i], tm);
+      const float alpha = m[i] == -INFINITY ? 0.f : exp2f(m[i] - mn);
+      float ps = 0.f;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float p = sa[i][u] == -INFINITY ? 0.f : exp2f(sa[i][u] - mn);
+        s_p[ri * PS + kg + 16 * u] = p;
+        ps += p;
+      }
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      l[i] = l[i] * alpha + ps;
+      m[i] = mn;
+      if (kg == 0) s_alpha[ri] = alpha;
+    }
+    __syncthreads();
+    const float al = s_alpha[own];
+#pragma unroll
+    for (int u = 0; u < EQ; ++u) acc[u] *= al;
+#pragma unroll 4
+    for (int j = 0; j < kLatKeys; ++j) {
+      const float p = s_p[own * PS + j];
+      const float* vr = s_v + j * LS + eq * EQ;
+#pragma unroll
+      for (int u = 0; u < EQ; u += 4) {
+        const float4 v4 = *reinterpret_cast<const float4*>(vr + u);
+        acc[u] = fmaf(p, v4.x, acc[u]);
+        acc[u + 1] = fmaf(p, v4.y, acc[u + 1]);
+        acc[u + 2] = fmaf(p, v4.z, acc[u + 2]);
+        acc[u + 3] = fmaf(p, v4.w, acc[u + 3]);
+      }
+    }
+  }
+  __syncthreads();
+  if (kg == 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = r0 + 4 * rg + i;
+      s_l[4 * rg + i] = l[i];
+      if (r < g.Tq) {
+        const bool any = s_qid[4 * rg + i] > 0;
+        lat_lse[(int64_t)(b * g.Lh + lh) * g.Tq + r] = any ? (m[i] + log2f(l[i])) * 0.6931471805599453f : INFINITY;
+      }
+    }
+  }
+  __syncthreads();
+  const int r = r0 + own;
+  if (r < g.Tq) {
+    const float inv = s_qid[own] > 0 ? 1.f / s_l[own] : 0.f;
+    T* dst = lat + (int64_t)(b * g.Tq + r) * g.Ld + lh * g.ldh;
+#pragma unroll
+    for (int u = 0; u < EQ; ++u) {
+      const int e = eq * EQ + u;
+      if (e < g.ldh) dst[e] = from_f<T>(acc[u] * inv);
+    }
+  }
+}
+
+// out[i] = sum_p part[p * n + i], p in a fixed order (deterministic). A block
+// takes 32 consecutive outputs; its 8 warps split the partials (warp w sums
+// p = w, w+8, ...) and the 8 sums are added in warp order, so long partial
+// lists do not make one thread walk them all.
+template <typename To>
+__global__ void __launch_bounds__(256) reduce_parts_kernel(const float* __restrict__ part, int n_part, int64_t n,
+                                                           To* __restrict__ out) {
+  __shared__ float red[8][33];
+  const int c = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int64_t i0 = (int64_t)blockIdx.x * 32; i0 < n; i0 += (int64_t)gridDim.x * 32) {
+    const int64_t i = i0 + c;
+    float a = 0.f;
+    if (i < n) {
+#pragma unroll 4
+      for (int p = w; p < n_part; p += 8) a += part[(int64_t)p * n + i];
+    }
+    red[w][c] = a;
+    __syncthreads();
+    if (w == 0 && i < n) {
+      float s = red[0][c];
+#pragma unroll
+      for (int k = 1; k < 8; ++k) s += red[k][c];
+      out[i] = from_f<To>(s);
+    }
+    __syncthreads();
   }
 }
 
 template <typename T, int L>
 cudaError_t latent_fwd_l(const Geom& g, const T* rq, const T* gkv, T* lat, float* lse, cudaStream_t s) {
-  dim3 grid(cdiv(g.Tq, kRowsFwd), g.Lh, g.B);
-  latent_fwd_kernel<T, L><<<grid, kRowsFwd, 0, s>>>(g, rq, gkv, lat, lse);
+  const int sm = (int)sizeof(float) * LatBwdSmem<L>::FLOATS;
+  cudaError_t e = cudaFuncSetAttribute(latent_fwd_blocked_kernel<T, L>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  if (e != cudaSuccess) return e;
+  dim3 grid(cdiv(g.Tq, kLatRows), g.Lh, g.B);
+  latent_fwd_blocked_kernel<T, L><<<grid, 256, sm, s>>>(g, rq, gkv, lat, lse);
   return cudaGetLastError();
 }
 
@@ -426,13 +515,13 @@ template <typename T>
 cudaError_t launch_latent_reduce(const Geom& g, const float* part, int n_split, T* dgkv,
                                  cudaStream_t s) {
   const int64_t n = (int64_t)g.B * g.Nc * 2 * g.Ld;
-  const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 8);
+  const int blocks = (int)std::min<int64_t>((n + 31) / 32, 148 * 8);
   reduce_parts_kernel<T><<<blocks, 256, 0, s>>>(part, n_split, n, dgkv);
   return cudaGetLastError();
 }
 
 cudaError_t launch_reduce_rows(const float* part, int n_part, int64_t n, float* out, cudaStream_t s) {
-  const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 8);
+  const int blocks = (int)std::min<int64_t>((n + 31) / 32, 148 * 8);
   reduce_parts_kernel<float><<<blocks, 256, 0, s>>>(part, n_part, n, out);
   return cudaGetLastError();
 }
