@@ -233,7 +233,7 @@ cudaError_t dkv_hd(const Geom& g, const void* qkv, const void* dl, const float* 
   if (!make_panel_map(&q128, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_panel_map(&q64, qkv, g.B, g.T, 3 * g.H, HD, 64) ||
       !make_panel_map(&do64, dl, g.B, g.T, g.H, HD, 64) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, HD, 128))
     return cudaErrorInvalidValue;
-  const int smem = std::max(DkvLayout<HD>::BYTES + 1024, 116 * 1024);
+  const int smem = DkvLayout<HD>::BYTES;  // the kernel's shared memory is 1024-byte aligned
   cudaError_t e = cudaFuncSetAttribute(local_dkv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   // persistent: one CTA per SM walks the (h, key tile, b) units

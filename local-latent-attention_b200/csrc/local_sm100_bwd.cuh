@@ -281,26 +281,30 @@ __global__ void __launch_bounds__(320, 1)
 template <int HD>
 struct DkvLayout {
   static constexpr int BNQ = 64;                   // queries per inner tile
-  static constexpr int NQS = 4;                    // Q / dO stages
+  static constexpr int NQS = 3;                    // Q / dO stages
   static constexpr int KPANEL = BM * 128;          // 128-key panel (16 KB)
   static constexpr int QPANEL = BNQ * 128;         // 64-query panel (8 KB)
   static constexpr int KTILE = BM * HD * 2;
   static constexpr int QTILE = BNQ * HD * 2;
-  static constexpr int K = 0;                      // K tile, then dK staging
-  static constexpr int V = K + KTILE;              // V tile, then dV staging
-  static constexpr int Q = V + KTILE;              // NQS stages
+  // two K/V buffers: unit n uses buffer n&1, so the next unit's K/V load
+  // while this one finishes (its dK/dV are staged over its own K/V tiles)
+  static constexpr int KV = 2 * KTILE;             // bytes of one K/V buffer
+  static constexpr int K = 0;                      // + kb * KV: K tile, then dK staging
+  static constexpr int V = K + KTILE;              // + kb * KV: V tile, then dV staging
+  static constexpr int Q = 2 * KV;                 // NQS stages
   static constexpr int DO = Q + NQS * QTILE;       // NQS stages
   static constexpr int VEC = DO + NQS * QTILE;     // per compute warp: {-lse*log2e, D}[32]
   static constexpr int BAR = VEC + 8 * 2 * 32 * 4;
   static constexpr int BYTES = BAR + 256;
+  static_assert(BYTES <= 227 * 1024, "shared memory");
 };
 
 // barriers: K/V loaded / K,V region free again (dK, dV stores have read it);
 // per Q/dO stage loaded / released; per TMEM buffer S^T,dP^T ready /
 // P^T,dS^T written; dV,dK complete / read out of TMEM; dK,dV staged
 enum {
-  KV_KV = 0, KV_KVE = 1, KV_QD = 2, KV_QDE = 6, KV_SP = 10, KV_PD = 12, KV_ACC = 14, KV_ACCE = 15, KV_STG = 16,
-  KV_NB = 17
+  KV_KV = 0, KV_KVE = 2, KV_QD = 4, KV_QDE = 8, KV_SP = 12, KV_PD = 14, KV_ACC = 16, KV_ACCE = 17, KV_STG = 18,
+  KV_NB = 19
 };
 
 struct DkvUnit {
@@ -326,16 +330,22 @@ __global__ void __launch_bounds__(320, 1)
                         Geom g, const float* __restrict__ lse, const float* __restrict__ delta, int n_units) {
   using L = DkvLayout<HD>;
   constexpr int BNQ = L::BNQ, NQS = L::NQS;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align1024(smem_raw);
+  extern __shared__ __align__(1024) uint8_t smem_dkv[];
+  uint8_t* smem = smem_dkv;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + KV_NB);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  if (smem_u32(smem) & 1023u) {  // the swizzled layouts need 1024-byte alignment
+    if (threadIdx.x == 0) atomicOr(&g_fault_word, kFaultEpilogue);
+    return;
+  }
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars[KV_KV], 1);
-    mbar_init(&bars[KV_KVE], 1);
+    for (int kb = 0; kb < 2; ++kb) {
+      mbar_init(&bars[KV_KV + kb], 1);
+      mbar_init(&bars[KV_KVE + kb], 1);
+    }
     for (int s = 0; s < NQS; ++s) {
       mbar_init(&bars[KV_QD + s], 1);
       mbar_init(&bars[KV_QDE + s], 1);
@@ -384,16 +394,14 @@ __global__ void __launch_bounds__(320, 1)
       };
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++n) {
         const DkvUnit t = dkv_unit(g, u);
-        // this unit's first query tiles may load while the previous unit finishes
-        const int pre = min(t.nq, NQS);
-        for (int i = 0; ok && i < pre; ++i) ok = load_qd(t, i);
-        if (!ok) break;
-        if (n > 0 && !(ok = mbar_wait(&bars[KV_KVE], (n - 1) & 1, abort, &g_fault_word))) break;
-        mbar_expect_tx(&bars[KV_KV], 2 * L::KTILE);
-        tma_load_tile(&tm_qkv128, &bars[KV_KV], smem + L::K, t.k0, g.H + t.h, t.b);
-        tma_load_tile(&tm_qkv128, &bars[KV_KV], smem + L::V, t.k0, 2 * g.H + t.h, t.b);
+        // K/V buffer n&1: free once unit n-2's dK/dV stores have read it
+        const int kb = n & 1;
+        if (n >= 2 && !(ok = mbar_wait(&bars[KV_KVE + kb], ((n >> 1) - 1) & 1, abort, &g_fault_word))) break;
+        mbar_expect_tx(&bars[KV_KV + kb], 2 * L::KTILE);
+        tma_load_tile(&tm_qkv128, &bars[KV_KV + kb], smem + kb * L::KV + L::K, t.k0, g.H + t.h, t.b);
+        tma_load_tile(&tm_qkv128, &bars[KV_KV + kb], smem + kb * L::KV + L::V, t.k0, 2 * g.H + t.h, t.b);
         issued_kv = n + 1;
-        for (int i = pre; ok && i < t.nq; ++i) ok = load_qd(t, i);
+        for (int i = 0; ok && i < t.nq; ++i) ok = load_qd(t, i);
         q += t.nq;
       }
       if (!ok) {
@@ -401,7 +409,8 @@ __global__ void __launch_bounds__(320, 1)
         // let the copies already issued land before the CTA can exit
         volatile int none = 0;
         volatile unsigned gnone = 0;
-        if (issued_kv > 0) mbar_wait(&bars[KV_KV], (issued_kv - 1) & 1, &none, &gnone, 100000000ull);
+        if (issued_kv > 0)
+          mbar_wait(&bars[KV_KV + ((issued_kv - 1) & 1)], ((issued_kv - 1) >> 1) & 1, &none, &gnone, 100000000ull);
         for (int gq = issued_q - NQS < 0 ? 0 : issued_q - NQS; gq < issued_q; ++gq)
           mbar_wait(&bars[KV_QD + gq % NQS], (gq / NQS) & 1, &none, &gnone, 100000000ull);
       }
@@ -410,11 +419,11 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       constexpr uint32_t idSP = idesc_bf16_f32(BM, BNQ, false, false);  // K Q^T, V dO^T
       constexpr uint32_t idKV = idesc_bf16_f32(BM, HD, false, true);    // P^T dO, dS^T Q
-      const uint64_t dk0 = desc_sw128(smem_u32(smem + L::K), 16, 1024);
-      const uint64_t dv0 = desc_sw128(smem_u32(smem + L::V), 16, 1024);
+      const uint64_t dkb0 = desc_sw128(smem_u32(smem + L::K), 16, 1024);
+      const uint64_t dvb0 = desc_sw128(smem_u32(smem + L::V), 16, 1024);
       int q = 0, n = 0, m = 0;  // m: units with at least one query tile
       bool ok = true;
-      auto issue_sp = [&](int gq) -> bool {
+      auto issue_sp = [&](int gq, uint64_t dk0, uint64_t dv0) -> bool {
         const int s = gq & 1, sq = gq % NQS;
         if (!mbar_wait(&bars[KV_QD + sq], (gq / NQS) & 1, abort, &g_fault_word)) return false;
         tc_fence_after();
@@ -436,13 +445,15 @@ __global__ void __launch_bounds__(320, 1)
       // P^T columns S^T(i+1) overwrites)
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++n) {
         const DkvUnit t = dkv_unit(g, u);
-        if (!(ok = mbar_wait(&bars[KV_KV], n & 1, abort, &g_fault_word))) break;
+        const int kb = n & 1;
+        if (!(ok = mbar_wait(&bars[KV_KV + kb], (n >> 1) & 1, abort, &g_fault_word))) break;
+        const uint64_t dk0 = desc_add(dkb0, kb * L::KV), dv0 = desc_add(dvb0, kb * L::KV);
         tc_fence_after();
         if (t.nq > 0) {
-          ok = issue_sp(q);
+          ok = issue_sp(q, dk0, dv0);
           for (int i = 0; ok && i < t.nq; ++i) {
             const int gq = q + i, s = gq & 1, sq = gq % NQS;
-            if (i + 1 < t.nq && !(ok = issue_sp(gq + 1))) break;
+            if (i + 1 < t.nq && !(ok = issue_sp(gq + 1, dk0, dv0))) break;
             if (!(ok = mbar_wait(&bars[KV_PD + s], (gq >> 1) & 1, abort, &g_fault_word))) break;
             // the first dV/dK MMA overwrites the accumulators: the previous
             // unit's epilogue must have read them
@@ -561,10 +572,10 @@ __global__ void __launch_bounds__(320, 1)
       if (t.nq > 0)
         ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_ACC], m & 1, abort, &g_fault_word));
       else  // no MMAs: only make sure the unit's K/V copy has landed before overwriting it
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_KV], n & 1, abort, &g_fault_word));
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[KV_KV + (n & 1)], (n >> 1) & 1, abort, &g_fault_word));
       if (!ok) break;
       tc_fence_after();
-      uint8_t* stage = smem + (half == 0 ? L::K : L::V);
+      uint8_t* stage = smem + (n & 1) * L::KV + (half == 0 ? L::K : L::V);
       const uint32_t tsrc = (half == 0 ? tDK : tDV) + lane_off;
       const float mul = half == 0 ? g.scale : 1.f;
 #pragma unroll
@@ -602,12 +613,12 @@ __global__ void __launch_bounds__(320, 1)
         if (ok) {
 #pragma unroll
           for (int p = 0; p < HD / 64; ++p) {
-            tma_store_4d(&tm_st, smem + L::K + p * (BM * 128), p * 64, g.H + t.h, t.k0, t.b);
-            tma_store_4d(&tm_st, smem + L::V + p * (BM * 128), p * 64, 2 * g.H + t.h, t.k0, t.b);
+            tma_store_4d(&tm_st, smem + (n & 1) * L::KV + L::K + p * (BM * 128), p * 64, g.H + t.h, t.k0, t.b);
+            tma_store_4d(&tm_st, smem + (n & 1) * L::KV + L::V + p * (BM * 128), p * 64, 2 * g.H + t.h, t.k0, t.b);
           }
           tma_store_commit();
           tma_store_wait_read();
-          mbar_arrive(&bars[KV_KVE]);
+          mbar_arrive(&bars[KV_KVE + (n & 1)]);
         }
       }
       ok = __all_sync(0xffffffffu, ok);
