@@ -3,7 +3,7 @@
 // launchers (tensor maps, shared-memory sizing). The kernels live in:
 //   local_sm100_fwd_pp.cuh  forward, two 128-query tiles per CTA, fused
 //                           remote projection + gate + mix epilogue
-//   local_sm100_bwd.cuh     dq (per query tile) and dk/dv (per key tile)
+//   local_sm100_bwd.cuh     dq (units of query tiles) and dk/dv (units of key tiles), persistent
 //   gate_sm100.cuh          gate / r_out backward and the dW_rout GEMM
 // Windowed causal mask of the reference (models.py:232-305): key j is
 // visible from query t iff 0 < t-j <= W and j >= qs(t) - W + 1.
@@ -218,11 +218,13 @@ cudaError_t dq_hd(const Geom& g, const void* qkv, const void* dl, const float* l
   if (!make_panel_map(&q128, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_panel_map(&q64, qkv, g.B, g.T, 3 * g.H, HD, 64) ||
       !make_panel_map(&do128, dl, g.B, g.T, g.H, HD, 128) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, HD, 128))
     return cudaErrorInvalidValue;
-  const int smem = std::max(DqLayout<HD>::BYTES + 1024, 116 * 1024);
-  cudaError_t e = cudaFuncSetAttribute(local_dq_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  // persistent: one CTA per SM walks the (h, query tile, b) units
+  const int smem = DqpLayout<HD>::BYTES;  // the kernel's shared memory is 1024-byte aligned
+  cudaError_t e = cudaFuncSetAttribute(local_dq_persist_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(g.H, cdiv(g.T, BM), g.B);
-  local_dq_tc_kernel<HD><<<grid, 320, smem, s>>>(q128, q64, do128, st, g, lse, delta);
+  const int n_units = g.H * cdiv(g.T, BM) * g.B;
+  local_dq_persist_kernel<HD><<<std::min(n_units, sm_count()), 320, smem, s>>>(q128, q64, do128, st, g, lse, delta,
+                                                                               n_units);
   return cudaGetLastError();
 }
 

@@ -6,70 +6,98 @@
 //   dS = P (dO.v - D),  dq = scale sum_j dS k_j,  dk_j = scale sum_t dS q_t,
 //   dv_j = sum_t P dO_t.
 // Two kernels, no atomics, deterministic:
-//   dq  : one CTA per (b, h, 128-query tile); loops over 64-key tiles.
-//   dkv : one CTA per (b, h, 128-key tile); loops over 64-query tiles
-//         t in [k0+1, k0+127+W].
+//   dq  : persistent, units of (b, h, 128-query tile); loops over 64-key tiles.
+//   dkv : persistent, units of (b, h, 128-key tile); loops over 64-query
+//         tiles t in [k0+1, k0+127+W].
 // Both keep the two score-like tiles (S and dP) of the current inner tile in
 // TMEM, double-buffered, so the softmax warps of tile j overlap the MMAs of
 // tile j+1.
 
 // ---------------------------------------------------------------------------
-// dq
+// dq, persistent: one CTA per SM walks the (h, query tile, b) units
+// u = blockIdx.x + k * gridDim.x, heads fastest. Q/dO are double-buffered by
+// unit (unit n uses buffer n&1), the K/V ring and the S/dP buffers run on
+// counters that continue across units, so the next unit's Q/dO and first
+// K/V tiles load and its first score MMAs run while this unit's dQ is read
+// out of TMEM, staged over its own (no longer read) Q tile and stored.
 
 template <int HD>
-struct DqLayout {
-  static constexpr int BNK = 64;                  // keys per inner tile
-  static constexpr int NKS = 4;                    // K / V stages
+struct DqpLayout {
+  static constexpr int BNK = 64;                   // keys per inner tile
+  static constexpr int NKS = 3;                    // K / V stages
   static constexpr int QPANEL = BM * 128;          // 128-row panel (16 KB)
   static constexpr int KPANEL = BNK * 128;         // 64-row panel (8 KB)
   static constexpr int QTILE = BM * HD * 2;
   static constexpr int KTILE = BNK * HD * 2;
-  static constexpr int Q = 0;
-  static constexpr int DO = Q + QTILE;
-  static constexpr int K = DO + QTILE;             // NKS stages
-  static constexpr int V = K + NKS * KTILE;        // NKS stages
-  static constexpr int BAR = V + NKS * KTILE;
+  static constexpr int QD = 2 * QTILE;             // one Q/dO buffer: Q (then dQ staging), dO
+  static constexpr int Q = 0;                      // + qb * QD
+  static constexpr int DO = QTILE;                 // + qb * QD
+  static constexpr int K = 2 * QD;                 // NKS stages of K, V
+  static constexpr int V = K + KTILE;
+  static constexpr int KV = 2 * KTILE;             // bytes of one K/V stage
+  static constexpr int BAR = K + NKS * KV;
   static constexpr int BYTES = BAR + 256;
+  static_assert(BYTES <= 227 * 1024, "shared memory");
 };
 
-// barriers: Q/dO loaded; per K/V stage loaded (K, V) / released; per TMEM
-// buffer S,dP ready / dS written / dQ MMAs done
-enum { DQ_Q = 0, DQ_K = 1, DQ_V = 5, DQ_KVE = 9, DQ_SP = 13, DQ_DS = 15, DQ_DQ = 17, DQ_NB = 19 };
+// barriers: per Q/dO buffer loaded / free again (dQ store has read the
+// staging); per K/V stage loaded / released; per TMEM buffer S,dP ready /
+// dS written; dQ of a unit complete; dQ staged
+enum {
+  DP_Q = 0, DP_QE = 2, DP_KV = 4, DP_KVE = 7, DP_SP = 10, DP_DS = 12, DP_ACC = 14, DP_STG = 15, DP_NB = 16
+};
+
+struct DqUnit {
+  int h, q0, b, kbase, nk;
+};
+template <int BNK>
+__device__ __forceinline__ DqUnit dq_unit(const Geom& g, int u) {
+  DqUnit t;
+  const int nqt = cdiv(g.T, BM);
+  t.h = u % g.H;
+  const int r = u / g.H;
+  t.q0 = (r % nqt) * BM;
+  t.b = r / nqt;
+  const int qlast = min(t.q0 + BM - 1, g.T - 1);
+  t.kbase = local_lo(g, t.q0);
+  const int khi = qlast - 1;
+  t.nk = khi >= t.kbase ? (khi - t.kbase + BNK) / BNK : 0;
+  return t;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(320, 1)
-    local_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv128, const __grid_constant__ CUtensorMap tm_qkv64,
-                       const __grid_constant__ CUtensorMap tm_do128, const __grid_constant__ CUtensorMap tm_st,
-                       Geom g, const float* __restrict__ lse, const float* __restrict__ delta) {
-  using L = DqLayout<HD>;
-  constexpr int BNK = L::BNK;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align1024(smem_raw);
+    local_dq_persist_kernel(const __grid_constant__ CUtensorMap tm_qkv128, const __grid_constant__ CUtensorMap tm_qkv64,
+                            const __grid_constant__ CUtensorMap tm_do128, const __grid_constant__ CUtensorMap tm_st,
+                            Geom g, const float* __restrict__ lse, const float* __restrict__ delta, int n_units) {
+  using L = DqpLayout<HD>;
+  constexpr int BNK = L::BNK, NKS = L::NKS;
+  extern __shared__ __align__(1024) uint8_t smem_dqp[];
+  uint8_t* smem = smem_dqp;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + DQ_NB);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + DP_NB);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
+  if (smem_u32(smem) & 1023u) {  // the swizzled layouts need 1024-byte alignment
+    if (threadIdx.x == 0) atomicOr(&g_fault_word, kFaultEpilogue);
+    return;
+  }
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // heads fastest: CTAs that run together cover whole token rows of qkv
-  const int h = blockIdx.x, b = blockIdx.z;
-  const int q0 = blockIdx.y * BM;
-  const int qlast = min(q0 + BM - 1, g.T - 1);
-  const int kbase = local_lo(g, q0);
-  const int khi = qlast - 1;
-  const int nk = khi >= kbase ? (khi - kbase + BNK) / BNK : 0;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars[DQ_Q], 1);
-    for (int s = 0; s < L::NKS; ++s) {
-      mbar_init(&bars[DQ_K + s], 1);
-      mbar_init(&bars[DQ_V + s], 1);
-      mbar_init(&bars[DQ_KVE + s], 1);
+    for (int qb = 0; qb < 2; ++qb) {
+      mbar_init(&bars[DP_Q + qb], 1);
+      mbar_init(&bars[DP_QE + qb], 1);
+    }
+    for (int s = 0; s < NKS; ++s) {
+      mbar_init(&bars[DP_KV + s], 1);
+      mbar_init(&bars[DP_KVE + s], 1);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars[DQ_SP + s], 1);
-      mbar_init(&bars[DQ_DS + s], 2 * BM);
-      mbar_init(&bars[DQ_DQ + s], 1);
+      mbar_init(&bars[DP_SP + s], 1);
+      mbar_init(&bars[DP_DS + s], 2 * BM);
     }
+    mbar_init(&bars[DP_ACC], 1);
+    mbar_init(&bars[DP_STG], 2 * BM);
     *abort = 0;
     fence_barrier_init();
   }
@@ -82,110 +110,174 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // S buffers at columns [0,64) and [64,128); dP at [128,192) and [192,256).
-  // dS (bf16) is written back over the first 16 of each 32 dP columns that
-  // produced it and feeds the dQ MMA from TMEM.
+  // S buffers at columns [0,64) and [64,128); dP at [128,192) and [192,256);
+  // dQ at [256, 256+HD). dS (bf16) is written back over the first 16 of each
+  // 32 dP columns that produced it and feeds the dQ MMA from TMEM. One dQ
+  // accumulator suffices: the first dQ MMA of a unit waits for that unit's
+  // first dS, which the compute warps write only after reading out the
+  // previous unit's dQ.
   const uint32_t tDQ = tmem + 256;
 
   if (warp == 0) {
-    if (lane == 0 && nk > 0) {
-      int issued = 0;
+    if (lane == 0) {
       prefetch_tmap(&tm_qkv128);
       prefetch_tmap(&tm_qkv64);
       prefetch_tmap(&tm_do128);
-      mbar_expect_tx(&bars[DQ_Q], 2 * L::QTILE);
-      tma_load_tile(&tm_qkv128, &bars[DQ_Q], smem + L::Q, q0, h, b);
-      tma_load_tile(&tm_do128, &bars[DQ_Q], smem + L::DO, q0, h, b);
-      for (int j = 0; j < nk; ++j) {
-        const int s = j % L::NKS;
-        if (j >= L::NKS && !mbar_wait(&bars[DQ_KVE + s], ((j / L::NKS) - 1) & 1, abort, &g_fault_word)) {
-          raise_fault(kFaultProducer, abort);
-          break;
+      prefetch_tmap(&tm_st);
+      int jj = 0, n = 0, issued_kv = 0, issued_q = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++n) {
+        const DqUnit t = dq_unit<BNK>(g, u);
+        const int qb = n & 1;
+        // buffer qb: free once unit n-2's dQ store has read its staging
+        if (n >= 2 && !(ok = mbar_wait(&bars[DP_QE + qb], ((n >> 1) - 1) & 1, abort, &g_fault_word))) break;
+        mbar_expect_tx(&bars[DP_Q + qb], 2 * L::QTILE);
+        tma_load_tile(&tm_qkv128, &bars[DP_Q + qb], smem + qb * L::QD + L::Q, t.q0, t.h, t.b);
+        tma_load_tile(&tm_do128, &bars[DP_Q + qb], smem + qb * L::QD + L::DO, t.q0, t.h, t.b);
+        issued_q = n + 1;
+        for (int j = 0; j < t.nk; ++j, ++jj) {
+          const int s = jj % NKS;
+          if (jj >= NKS && !(ok = mbar_wait(&bars[DP_KVE + s], ((jj / NKS) - 1) & 1, abort, &g_fault_word))) break;
+          const int k0 = t.kbase + j * BNK;
+          mbar_expect_tx(&bars[DP_KV + s], 2 * L::KTILE);
+          tma_load_tile(&tm_qkv64, &bars[DP_KV + s], smem + L::K + s * L::KV, k0, g.H + t.h, t.b);
+          tma_load_tile(&tm_qkv64, &bars[DP_KV + s], smem + L::V + s * L::KV, k0, 2 * g.H + t.h, t.b);
+          issued_kv = jj + 1;
         }
-        const int k0 = kbase + j * BNK;
-        mbar_expect_tx(&bars[DQ_K + s], L::KTILE);
-        tma_load_tile(&tm_qkv64, &bars[DQ_K + s], smem + L::K + s * L::KTILE, k0, g.H + h, b);
-        mbar_expect_tx(&bars[DQ_V + s], L::KTILE);
-        tma_load_tile(&tm_qkv64, &bars[DQ_V + s], smem + L::V + s * L::KTILE, k0, 2 * g.H + h, b);
-        issued = j + 1;
       }
-      if (*abort) {
+      if (!ok) {
+        raise_fault(kFaultProducer, abort);
+        // let the copies already issued land before the CTA can exit
         volatile int none = 0;
         volatile unsigned gnone = 0;
-        mbar_wait(&bars[DQ_Q], 0, &none, &gnone, 100000000ull);
-        for (int j = issued - L::NKS < 0 ? 0 : issued - L::NKS; j < issued; ++j) {
-          mbar_wait(&bars[DQ_K + j % L::NKS], (j / L::NKS) & 1, &none, &gnone, 100000000ull);
-          mbar_wait(&bars[DQ_V + j % L::NKS], (j / L::NKS) & 1, &none, &gnone, 100000000ull);
-        }
+        for (int q = issued_q - 2 < 0 ? 0 : issued_q - 2; q < issued_q; ++q)
+          mbar_wait(&bars[DP_Q + (q & 1)], (q >> 1) & 1, &none, &gnone, 100000000ull);
+        for (int k = issued_kv - NKS < 0 ? 0 : issued_kv - NKS; k < issued_kv; ++k)
+          mbar_wait(&bars[DP_KV + k % NKS], (k / NKS) & 1, &none, &gnone, 100000000ull);
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && nk > 0) {
+    if (lane == 0) {
       constexpr uint32_t idSP = idesc_bf16_f32(BM, BNK, false, false);  // Q K^T, dO V^T
       constexpr uint32_t idDQ = idesc_bf16_f32(BM, HD, false, true);    // dS K (K MN-major)
       const uint64_t dq0 = desc_sw128(smem_u32(smem + L::Q), 16, 1024);
       const uint64_t ddo0 = desc_sw128(smem_u32(smem + L::DO), 16, 1024);
-      bool ok = mbar_wait(&bars[DQ_Q], 0, abort, &g_fault_word);
-      auto issue_sp = [&](int j) -> bool {
-        const int s = j & 1, sk = j % L::NKS;
-        if (!mbar_wait(&bars[DQ_K + sk], (j / L::NKS) & 1, abort, &g_fault_word)) return false;
-        if (!mbar_wait(&bars[DQ_V + sk], (j / L::NKS) & 1, abort, &g_fault_word)) return false;
+      const uint64_t dk0 = desc_sw128(smem_u32(smem + L::K), 16, 1024);
+      const uint64_t dv0 = desc_sw128(smem_u32(smem + L::V), 16, 1024);
+      const uint64_t dkm0 = desc_sw128(smem_u32(smem + L::K), L::KPANEL, 1024);
+      // cursor over the (unit, key tile) items of this CTA, units without
+      // keys skipped (n still counts them: it picks the Q/dO buffer)
+      struct Cur {
+        int u, n, j;
+        DqUnit t;
+      };
+      auto skip_empty = [&](Cur& c) {
+        while (c.u < n_units && c.t.nk == 0) {
+          c.u += gridDim.x;
+          ++c.n;
+          if (c.u < n_units) c.t = dq_unit<BNK>(g, c.u);
+        }
+      };
+      auto advance = [&](Cur& c) {
+        if (++c.j < c.t.nk) return;
+        c.j = 0;
+        c.u += gridDim.x;
+        ++c.n;
+        if (c.u < n_units) c.t = dq_unit<BNK>(g, c.u);
+        skip_empty(c);
+      };
+      auto issue_sp = [&](const Cur& c, int jj) -> bool {
+        const int s = jj & 1, sk = jj % NKS, qb = c.n & 1;
+        if (c.j == 0 && !mbar_wait(&bars[DP_Q + qb], (c.n >> 1) & 1, abort, &g_fault_word)) return false;
+        if (!mbar_wait(&bars[DP_KV + sk], (jj / NKS) & 1, abort, &g_fault_word)) return false;
         tc_fence_after();
-        const uint64_t dk = desc_sw128(smem_u32(smem + L::K + sk * L::KTILE), 16, 1024);
-        const uint64_t dv = desc_sw128(smem_u32(smem + L::V + sk * L::KTILE), 16, 1024);
+        const uint64_t dq = desc_add(dq0, qb * L::QD), ddo = desc_add(ddo0, qb * L::QD);
+        const uint64_t dk = desc_add(dk0, sk * L::KV), dv = desc_add(dv0, sk * L::KV);
         const uint32_t tS = tmem + s * BNK, tP = tmem + 128 + s * BNK;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t aoff = (kk / 4) * L::QPANEL + (kk % 4) * 32;
           const uint32_t boff = (kk / 4) * L::KPANEL + (kk % 4) * 32;
-          mma_bf16(tS, desc_add(dq0, aoff), desc_add(dk, boff), idSP, kk > 0);
-          mma_bf16(tP, desc_add(ddo0, aoff), desc_add(dv, boff), idSP, kk > 0);
+          mma_bf16(tS, desc_add(dq, aoff), desc_add(dk, boff), idSP, kk > 0);
+          mma_bf16(tP, desc_add(ddo, aoff), desc_add(dv, boff), idSP, kk > 0);
         }
-        mma_commit(&bars[DQ_SP + s]);
+        mma_commit(&bars[DP_SP + s]);
         return true;
       };
-      if (ok) ok = issue_sp(0);
-      for (int j = 0; ok && j < nk; ++j) {
-        if (j + 1 < nk && !(ok = issue_sp(j + 1))) break;
-        const int s = j & 1, sk = j % L::NKS;
-        if (!(ok = mbar_wait(&bars[DQ_DS + s], (j >> 1) & 1, abort, &g_fault_word))) break;
+      Cur cur;
+      cur.u = blockIdx.x;
+      cur.n = 0;
+      cur.j = 0;
+      if (cur.u < n_units) cur.t = dq_unit<BNK>(g, cur.u);
+      skip_empty(cur);
+      bool ok = true;
+      int jj = 0;
+      if (cur.u < n_units) ok = issue_sp(cur, 0);
+      // S/dP of the next item are issued before dQ of this one: the compute
+      // warps wait for them next, and they may start once dQ of the item
+      // before is issued (it reads the dS columns they overwrite)
+      while (ok && cur.u < n_units) {
+        Cur nx = cur;
+        advance(nx);
+        if (nx.u < n_units && !(ok = issue_sp(nx, jj + 1))) break;
+        const int s = jj & 1, sk = jj % NKS;
+        if (!(ok = mbar_wait(&bars[DP_DS + s], (jj >> 1) & 1, abort, &g_fault_word))) break;
         tc_fence_after();
-        const uint64_t dkm = desc_sw128(smem_u32(smem + L::K + sk * L::KTILE), L::KPANEL, 1024);
+        const uint64_t dkm = desc_add(dkm0, sk * L::KV);
         const uint32_t tA = tmem + 128 + s * BNK;
 #pragma unroll
         for (int kk = 0; kk < BNK / 16; ++kk) {
           // keys 16kk..16kk+15: packed in the half (kk/2) written by warp group kk/2
           const uint32_t acol = (uint32_t)((kk >> 1) * 32 + (kk & 1) * 8);
-          mma_bf16_ts(tDQ, tA + acol, desc_add(dkm, kk * 2048), idDQ, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ts(tDQ, tA + acol, desc_add(dkm, kk * 2048), idDQ, (cur.j > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(&bars[DQ_DQ + s]);
-        mma_commit(&bars[DQ_KVE + sk]);
+        mma_commit(&bars[DP_KVE + sk]);
+        if (cur.j == cur.t.nk - 1) mma_commit(&bars[DP_ACC]);
+        cur = nx;
+        ++jj;
       }
       if (!ok) raise_fault(kFaultMma, abort);
     }
   } else {
-    // warps 2..9: row = TMEM lane; warps w and w+4 share a lane quarter and
-    // split the columns (half 0 / half 1), two warps per scheduler
+    // warps 2..9: row = TMEM lane = query; warps w and w+4 share a lane
+    // quarter and split the columns (half 0 / half 1), two warps per scheduler
     const int half = (warp - 2) >> 2;
     const int row = 32 * (warp & 3) + lane;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
-    const int t = q0 + row;
-    const bool valid = t < g.T;
-    const int lo = valid ? local_lo(g, t) : 0x7fffffff;
     const float sc = g.scale * kLog2e;
-    const float lse2 = valid ? lse[((int64_t)b * g.H + h) * g.T + t] * kLog2e : INFINITY;
-    const float dt = valid ? delta[((int64_t)b * g.H + h) * g.T + t] : 0.f;
+    // this row's lse*log2(e) / D, loaded one unit ahead
+    auto fetch = [&](int u, float& l2, float& dd) {
+      l2 = INFINITY;
+      dd = 0.f;
+      if (u < n_units) {
+        const DqUnit t = dq_unit<BNK>(g, u);
+        const int tq = t.q0 + row;
+        if (tq < g.T) {
+          l2 = __ldg(lse + ((int64_t)t.b * g.H + t.h) * g.T + tq) * kLog2e;
+          dd = __ldg(delta + ((int64_t)t.b * g.H + t.h) * g.T + tq);
+        }
+      }
+    };
+    float nlse2, ndt;
+    fetch(blockIdx.x, nlse2, ndt);
+    int jj = 0, n = 0, m = 0;
     bool ok = true;
-    for (int j = 0; j < nk; ++j) {
-      const int s = j & 1;
-      // S(j) done implies the dQ MMA of tile j-2 (issued earlier) has
-      // finished reading the dS columns this pass overwrites
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars[DQ_SP + s], (j >> 1) & 1, abort, &g_fault_word));
-      if (!ok) break;
-      tc_fence_after();
-      const int k0 = kbase + j * BNK;
-      const int c_lo = lo - k0, c_hi = t - k0;
-      {
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++n) {
+      const DqUnit t = dq_unit<BNK>(g, u);
+      const int qb = n & 1;
+      const float lse2 = nlse2, dt = ndt;
+      fetch(u + gridDim.x, nlse2, ndt);
+      const int tq = t.q0 + row;
+      const int lo = tq < g.T ? local_lo(g, tq) : 0x7fffffff;
+      for (int j = 0; j < t.nk; ++j, ++jj) {
+        const int s = jj & 1;
+        // S(jj) done implies the dQ MMA of item jj-2 (issued earlier) has
+        // finished reading the dS columns this pass overwrites
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[DP_SP + s], (jj >> 1) & 1, abort, &g_fault_word));
+        if (!ok) break;
+        tc_fence_after();
+        const int k0 = t.kbase + j * BNK;
+        const int c_lo = lo - k0, c_hi = tq - k0;
         const int cc = half;  // this warp's 32 of the tile's 64 key columns
         uint32_t rs[32], rp[32];
         tmem_ld32(tmem + lane_off + s * BNK + cc * 32, rs);
@@ -213,24 +305,24 @@ __global__ void __launch_bounds__(320, 1)
         }
         tmem_st16(tmem + lane_off + 128 + s * BNK + cc * 32, pk);
         tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bars[DP_DS + s]);
       }
-      tc_fence_before();
-      mbar_arrive(&bars[DQ_DS + s]);
-    }
-    if (!ok) raise_fault(kFaultSoftmax, abort);
-    if (ok && nk > 0)
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars[DQ_DQ + ((nk - 1) & 1)], ((nk - 1) >> 1) & 1, abort,
-                                             &g_fault_word));
-    if (!ok) {
-      raise_fault(kFaultEpilogue, abort);
-    } else {
+      if (!ok) break;
+      // epilogue: dQ (scaled) as bf16 128-byte-swizzled 64-column panels over
+      // the unit's Q tile (free once the unit's MMAs are done), then TMA
+      // stores (rows >= T clipped by the map)
+      if (t.nk > 0)
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[DP_ACC], m & 1, abort, &g_fault_word));
+      else  // no MMAs: only make sure the unit's Q copy has landed before overwriting it
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[DP_Q + qb], (n >> 1) & 1, abort, &g_fault_word));
+      if (!ok) break;
       tc_fence_after();
-      // dQ staged as bf16 128-byte-swizzled 64-column panels in the (now
-      // idle) K ring, stored below by TMA (rows >= T clipped by the map)
+      uint8_t* stage = smem + qb * L::QD + L::Q;
 #pragma unroll
       for (int cc = half * (HD / 64); cc < (half + 1) * (HD / 64); ++cc) {
         uint32_t r[32];
-        if (nk > 0) {
+        if (t.nk > 0) {
           tmem_ld32(tDQ + lane_off + cc * 32, r);
           tmem_ld_wait();
         } else {
@@ -241,7 +333,7 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i)
           pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * g.scale, __uint_as_float(r[2 * i + 1]) * g.scale);
-        uint8_t* prow = smem + L::K + (cc >> 1) * (BM * 128) + row * 128;
+        uint8_t* prow = stage + (cc >> 1) * (BM * 128) + row * 128;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int chunk = (cc & 1) * 4 + q;
@@ -249,16 +341,26 @@ __global__ void __launch_bounds__(320, 1)
               make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
+      if (t.nk > 0) {
+        tc_fence_before();
+        ++m;
+      }
       fence_async_smem();
-    }
-    // every compute warp reaches this barrier exactly once, faulted or not
-    named_bar_sync(1, 256);
-    if (warp == 2 && lane == 0 && !*abort) {
+      mbar_arrive(&bars[DP_STG]);
+      if (warp == 2 && lane == 0) {
+        // all 256 staging writes done -> store dQ; buffer qb free once read
+        ok = mbar_wait(&bars[DP_STG], n & 1, abort, &g_fault_word);
+        if (ok) {
 #pragma unroll
-      for (int p = 0; p < HD / 64; ++p) tma_store_4d(&tm_st, smem + L::K + p * (BM * 128), p * 64, h, q0, b);
-      tma_store_commit();
-      tma_store_wait_read();
+          for (int p = 0; p < HD / 64; ++p) tma_store_4d(&tm_st, stage + p * (BM * 128), p * 64, t.h, t.q0, t.b);
+          tma_store_commit();
+          tma_store_wait_read();
+          mbar_arrive(&bars[DP_QE + qb]);
+        }
+      }
+      ok = __all_sync(0xffffffffu, ok);
     }
+    if (!ok) raise_fault(kFaultSoftmax, abort);
   }
   tc_fence_before();
   __syncthreads();
