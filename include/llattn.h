@@ -176,8 +176,11 @@ typedef struct llattn_bwd_args {
 typedef enum llattn_pool_mode {
   LLATTN_POOL_CHUNKS = 0, /* chunk means of x over cs tokens, last partial
                              chunk over its true count   (models.py:159-214) */
-  LLATTN_POOL_QBLOCKS = 1 /* query-block means over bs tokens, zero padding
-                             counted                     (models.py:216-230) */
+  LLATTN_POOL_QBLOCKS = 1, /* query-block means over bs tokens, zero padding
+                              counted                    (models.py:216-230) */
+  LLATTN_POOL_ACCUMULATE = 16 /* or'd into llattn_pool_bwd's mode: dx += the
+                                 spread gradient instead of dx = (autograd's
+                                 sum of x's gradient contributions) */
 } llattn_pool_mode;
 
 LLATTN_API int llattn_version(void);
@@ -199,9 +202,20 @@ LLATTN_API size_t llattn_bwd_workspace_bytes(const llattn_dims* dims);
 /* x [B, T, d] dtype -> pooled [B, rows, d] dtype, rows = Nc or Tq. */
 LLATTN_API int llattn_pool_fwd(const llattn_dims* dims, int mode, const void* x,
                     void* pooled, int64_t d, void* stream);
-/* dpooled [B, rows, d] -> dx [B, T, d] (overwritten). */
+/* dpooled [B, rows, d] -> dx [B, T, d] (overwritten, or added to with
+ * LLATTN_POOL_ACCUMULATE). */
 LLATTN_API int llattn_pool_bwd(const llattn_dims* dims, int mode, const void* dpooled,
                     void* dx, int64_t d, void* stream);
+
+/* Bias gradient of a linear layer: out[c] = sum_r g[r, c] over a row-major
+ * [rows, cols] matrix of dtype (LLATTN_BF16 / LLATTN_F32), fp32
+ * accumulation in a fixed order (deterministic), out in dtype. Replaces the
+ * bias-gradient reduction of torch.nn.Linear's autograd for the block's
+ * qkv_proj / rq_proj / rkv_proj / out layers (models.py:80-84). workspace:
+ * llattn_colsum_workspace_bytes(rows, cols, dtype) bytes of device memory. */
+LLATTN_API size_t llattn_colsum_workspace_bytes(int64_t rows, int64_t cols, int dtype);
+LLATTN_API int llattn_colsum(const void* g, int64_t rows, int64_t cols, int dtype, void* out,
+                  void* workspace, size_t workspace_bytes, void* stream);
 
 LLATTN_API int llattn_fwd(const llattn_fwd_args* args, void* stream);
 /* Replaces nothing in the reference (its generation loop re-runs the whole

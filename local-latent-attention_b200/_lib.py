@@ -13,13 +13,14 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libllattn.so")
 
 F32, BF16 = 0, 1
-POOL_CHUNKS, POOL_QBLOCKS = 0, 1
+POOL_CHUNKS, POOL_QBLOCKS, POOL_ACCUMULATE = 0, 1, 16
 BWD_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 EXPORTED = (
     "llattn_version", "llattn_last_error", "llattn_fault_status", "llattn_geometry", "llattn_bwd_workspace_bytes",
     "llattn_pool_fwd", "llattn_pool_bwd", "llattn_fwd", "llattn_bwd", "llattn_bwd_noalloc", "llattn_decode",
-    "llattn_profile_enable", "llattn_profile_read", "llattn_profile_name",
+    "llattn_profile_enable", "llattn_profile_read", "llattn_profile_name", "llattn_colsum_workspace_bytes",
+    "llattn_colsum",
 )
 
 
@@ -88,6 +89,10 @@ def lib() -> ctypes.CDLL:
             fn = getattr(L, name)
             fn.argtypes = [ctypes.POINTER(Dims), ctypes.c_int, _vp, _vp, ctypes.c_int64, _vp]
             fn.restype = ctypes.c_int
+        L.llattn_colsum_workspace_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int]
+        L.llattn_colsum_workspace_bytes.restype = ctypes.c_size_t
+        L.llattn_colsum.argtypes = [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _vp, _vp, ctypes.c_size_t, _vp]
+        L.llattn_colsum.restype = ctypes.c_int
         L.llattn_fwd.argtypes = [ctypes.POINTER(FwdArgs), _vp]
         L.llattn_fwd.restype = ctypes.c_int
         L.llattn_bwd.argtypes = [ctypes.POINTER(BwdArgs), _vp]

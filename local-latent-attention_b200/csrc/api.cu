@@ -297,13 +297,34 @@ int llattn_pool_bwd(const llattn_dims* dims, int mode, const void* dpooled, void
   int rc = make_geom(dims, &g);
   if (rc) return rc;
   if (!dpooled || !dx) return fail(LLATTN_ERR_ARG, "pool_bwd: NULL pointer");
+  const int acc = (mode & LLATTN_POOL_ACCUMULATE) ? 1 : 0;
+  mode &= ~LLATTN_POOL_ACCUMULATE;
   if (mode != LLATTN_POOL_CHUNKS && mode != LLATTN_POOL_QBLOCKS) return fail(LLATTN_ERR_ARG, "bad pool mode");
   if (d < 1) return fail(LLATTN_ERR_ARG, "pool_bwd: d must be >= 1");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   prof::Scope ps(prof::POOL_BWD, s);
   if (dims->dtype == LLATTN_BF16)
-    return check_launch(launch_pool_bwd<bf16>(g, mode, (const bf16*)dpooled, (bf16*)dx, d, s), "pool_bwd");
-  return check_launch(launch_pool_bwd<float>(g, mode, (const float*)dpooled, (float*)dx, d, s), "pool_bwd");
+    return check_launch(launch_pool_bwd<bf16>(g, mode, (const bf16*)dpooled, (bf16*)dx, d, acc, s), "pool_bwd");
+  return check_launch(launch_pool_bwd<float>(g, mode, (const float*)dpooled, (float*)dx, d, acc, s), "pool_bwd");
+}
+
+size_t llattn_colsum_workspace_bytes(int64_t rows, int64_t cols, int dtype) {
+  if (rows < 1 || cols < 1 || (dtype != LLATTN_BF16 && dtype != LLATTN_F32)) return 0;
+  return sizeof(float) * (size_t)colsum_splits(rows, cols, dtype == LLATTN_BF16 ? 2 : 4) * (size_t)cols;
+}
+
+int llattn_colsum(const void* g, int64_t rows, int64_t cols, int dtype, void* out, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  if (!g || !out || !workspace) return fail(LLATTN_ERR_ARG, "colsum: NULL pointer");
+  const size_t need = llattn_colsum_workspace_bytes(rows, cols, dtype);
+  if (need == 0) return fail(LLATTN_ERR_ARG, "colsum: bad rows, cols or dtype");
+  if (cols > (int64_t)INT32_MAX / 32) return fail(LLATTN_ERR_ARG, "colsum: cols too large");
+  if (workspace_bytes < need) return fail(LLATTN_ERR_ARG, "colsum: workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  prof::Scope ps(prof::COLSUM, s, 2);
+  if (dtype == LLATTN_BF16)
+    return check_launch(launch_colsum<bf16>((const bf16*)g, rows, cols, (float*)workspace, (bf16*)out, s), "colsum");
+  return check_launch(launch_colsum<float>((const float*)g, rows, cols, (float*)workspace, (float*)out, s), "colsum");
 }
 
 int llattn_fwd(const llattn_fwd_args* a, void* stream) {

@@ -85,7 +85,16 @@ __device__ __forceinline__ float warp_max(float v) {
 template <typename T>
 cudaError_t launch_pool_fwd(const Geom& g, int mode, const T* x, T* out, int64_t d, cudaStream_t s);
 template <typename T>
-cudaError_t launch_pool_bwd(const Geom& g, int mode, const T* dout, T* dx, int64_t d, cudaStream_t s);
+cudaError_t launch_pool_bwd(const Geom& g, int mode, const T* dout, T* dx, int64_t d, int accumulate,
+                            cudaStream_t s);
+// out[c] = sum_r g[r, c] over a row-major [rows, cols] matrix; part holds
+// colsum_splits(rows, cols, sizeof(T)) x cols floats
+int colsum_splits(int64_t rows, int64_t cols, int elem_bytes);
+int sm_count();  // SMs of the current device
+template <typename T>
+cudaError_t launch_colsum(const T* g, int64_t rows, int64_t cols, float* part, T* out, cudaStream_t s);
+template <typename To>
+cudaError_t launch_reduce_parts(const float* part, int n_part, int64_t n, To* out, cudaStream_t s);
 
 template <typename T>
 cudaError_t launch_latent_fwd(const Geom& g, const T* rq, const T* gkv, T* lat, float* lat_lse,

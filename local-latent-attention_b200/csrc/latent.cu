@@ -521,10 +521,17 @@ cudaError_t launch_latent_reduce(const Geom& g, const float* part, int n_split, 
 }
 
 cudaError_t launch_reduce_rows(const float* part, int n_part, int64_t n, float* out, cudaStream_t s) {
+  return launch_reduce_parts<float>(part, n_part, n, out, s);
+}
+
+template <typename To>
+cudaError_t launch_reduce_parts(const float* part, int n_part, int64_t n, To* out, cudaStream_t s) {
   const int blocks = (int)std::min<int64_t>((n + 31) / 32, 148 * 8);
-  reduce_parts_kernel<float><<<blocks, 256, 0, s>>>(part, n_part, n, out);
+  reduce_parts_kernel<To><<<blocks, 256, 0, s>>>(part, n_part, n, out);
   return cudaGetLastError();
 }
+template cudaError_t launch_reduce_parts<float>(const float*, int, int64_t, float*, cudaStream_t);
+template cudaError_t launch_reduce_parts<bf16>(const float*, int, int64_t, bf16*, cudaStream_t);
 
 template cudaError_t launch_latent_fwd<float>(const Geom&, const float*, const float*, float*, float*, cudaStream_t);
 template cudaError_t launch_latent_fwd<bf16>(const Geom&, const bf16*, const bf16*, bf16*, float*, cudaStream_t);

@@ -150,18 +150,6 @@ bool make_btd_map(CUtensorMap* map, const void* base, int B, int T, int d) {
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int sm_count() {
-  static int cache[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int v = 0;
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    cache[dev] = v > 0 ? v : 148;
-  }
-  return cache[dev];
-}
 
 bool force_simt() {
   const char* e = std::getenv("LLATTN_FORCE_SIMT");

@@ -8,6 +8,8 @@
 // One thread owns 16 bytes of a row (8 bf16 / 4 fp32 columns) and walks the
 // chunk's tokens; consecutive threads own consecutive 16-byte columns, so each
 // token row is read fully coalesced. Accumulation is fp32.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace llattn {
@@ -93,10 +95,12 @@ __global__ void __launch_bounds__(256) pool_fwd_kernel(const T* __restrict__ x, 
 
 // dx[b,t] = dout[b, t/size] / divisor(t/size): the mean's gradient spread over
 // the row's tokens (models.py:195-199 / :223 through autograd).
+// With accumulate set, dx += that instead (one read-modify-write of dx, so
+// the other gradient contributions to x need no separate add).
 template <typename T, int V>
 __global__ void __launch_bounds__(256) pool_bwd_kernel(const T* __restrict__ dout, T* __restrict__ dx,
                                                        int T_, int64_t d, int rows, int size,
-                                                       int full_divisor) {
+                                                       int full_divisor, int accumulate) {
   const int b = blockIdx.z, t = blockIdx.y;
   const int64_t col = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * V;
   if (col >= d) return;
@@ -107,7 +111,62 @@ __global__ void __launch_bounds__(256) pool_bwd_kernel(const T* __restrict__ dou
   const float inv = 1.f / (float)cnt;
 #pragma unroll
   for (int i = 0; i < V; ++i) v[i] *= inv;
-  Vec<T, V>::store(dx + ((int64_t)b * T_ + t) * d + col, v);
+  T* dst = dx + ((int64_t)b * T_ + t) * d + col;
+  if (accumulate) {
+    float o[V];
+    Vec<T, V>::load(dst, o);
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] += o[i];
+  }
+  Vec<T, V>::store(dst, v);
+}
+
+// Column sums of a row-major [rows, cols] matrix (the bias gradient of a
+// linear layer: the sum of its output gradient over tokens), fp32
+// accumulation. Block: 32 column groups of V columns x 8 row lanes; blockIdx.y
+// takes a contiguous row range and writes its fp32 partial row to part[y].
+template <typename T, int V>
+__global__ void __launch_bounds__(256) colsum_part_kernel(const T* __restrict__ g, int64_t rows, int64_t cols,
+                                                          int64_t rows_per_split, float* __restrict__ part) {
+  __shared__ float red[8][32 * V + 1];
+  const int cg = threadIdx.x & 31, rl = threadIdx.x >> 5;
+  const int64_t col = ((int64_t)blockIdx.x * 32 + cg) * V;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_split;
+  const int64_t r1 = min(rows, r0 + rows_per_split);
+  float acc[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = 0.f;
+  if (col < cols) {
+    int64_t r = r0 + rl;
+    for (; r + 24 < r1; r += 32) {  // four rows in flight per thread
+      float v0[V], v1[V], v2[V], v3[V];
+      Vec<T, V>::load(g + r * cols + col, v0);
+      Vec<T, V>::load(g + (r + 8) * cols + col, v1);
+      Vec<T, V>::load(g + (r + 16) * cols + col, v2);
+      Vec<T, V>::load(g + (r + 24) * cols + col, v3);
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] += (v0[i] + v1[i]) + (v2[i] + v3[i]);
+    }
+    for (; r < r1; r += 8) {
+      float v0[V];
+      Vec<T, V>::load(g + r * cols + col, v0);
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] += v0[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < V; ++i) red[rl][cg * V + i] = acc[i];
+  __syncthreads();
+  // 256 threads sum the 8 row lanes of the block's 32 * V columns
+  for (int c = threadIdx.x; c < 32 * V; c += 256) {
+    const int64_t oc = (int64_t)blockIdx.x * 32 * V + c;
+    if (oc < cols) {
+      float s = red[0][c];
+#pragma unroll
+      for (int k = 1; k < 8; ++k) s += red[k][c];
+      part[(int64_t)blockIdx.y * cols + oc] = s;
+    }
+  }
 }
 
 template <typename T>
@@ -134,24 +193,78 @@ cudaError_t launch_pool_fwd(const Geom& g, int mode, const T* x, T* out, int64_t
 }
 
 template <typename T>
-cudaError_t launch_pool_bwd(const Geom& g, int mode, const T* dout, T* dx, int64_t d, cudaStream_t s) {
+cudaError_t launch_pool_bwd(const Geom& g, int mode, const T* dout, T* dx, int64_t d, int accumulate,
+                            cudaStream_t s) {
   const bool chunks = mode == LLATTN_POOL_CHUNKS;
   const int rows = chunks ? g.Nc : g.Tq;
   const int size = chunks ? g.cs : g.qbs;
   constexpr int V = vec_width<T>();
   if (d % V == 0 && aligned16(dout) && aligned16(dx)) {
     dim3 grid((unsigned)cdiv((int)(d / V), 256), g.T, g.B);
-    pool_bwd_kernel<T, V><<<grid, 256, 0, s>>>(dout, dx, g.T, d, rows, size, chunks ? 0 : 1);
+    pool_bwd_kernel<T, V><<<grid, 256, 0, s>>>(dout, dx, g.T, d, rows, size, chunks ? 0 : 1, accumulate);
   } else {
     dim3 grid((unsigned)cdiv((int)d, 256), g.T, g.B);
-    pool_bwd_kernel<T, 1><<<grid, 256, 0, s>>>(dout, dx, g.T, d, rows, size, chunks ? 0 : 1);
+    pool_bwd_kernel<T, 1><<<grid, 256, 0, s>>>(dout, dx, g.T, d, rows, size, chunks ? 0 : 1, accumulate);
   }
   return cudaGetLastError();
 }
 
+// SMs of the current device, cached per device
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = v > 0 ? v : 148;
+  }
+  return cache[dev];
+}
+
+int colsum_splits(int64_t rows, int64_t cols, int elem_bytes) {
+  const int64_t v = 16 / elem_bytes;
+  const int64_t gx = (cols + 32 * v - 1) / (32 * v);
+  // at most 8 blocks per SM (the launch takes what fits resident), at least
+  // 64 rows per block
+  int64_t splits = (148 * 8 + gx - 1) / gx;
+  splits = std::min<int64_t>(splits, (rows + 63) / 64);
+  return (int)std::max<int64_t>(splits, 1);
+}
+
+template <typename K>
+int colsum_occupancy(K kernel) {
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, 256, 0) != cudaSuccess || occ < 1) return 1;
+  return occ;
+}
+
+template <typename T>
+cudaError_t launch_colsum(const T* g, int64_t rows, int64_t cols, float* part, T* out, cudaStream_t s) {
+  constexpr int V = vec_width<T>();
+  const bool vec = cols % V == 0 && aligned16(g);
+  const int gx = vec ? cdiv((int)(cols / V), 32) : cdiv((int)cols, 32);
+  // one wave: as many row splits as fit resident beside the column groups
+  static const int occ_v = colsum_occupancy(colsum_part_kernel<T, V>);
+  static const int occ_1 = colsum_occupancy(colsum_part_kernel<T, 1>);
+  const int occ = vec ? occ_v : occ_1, sms = sm_count();
+  const int splits = std::max(1, std::min(colsum_splits(rows, cols, (int)sizeof(T)), sms * occ / gx));
+  const int64_t per = (rows + splits - 1) / splits;
+  if (vec)
+    colsum_part_kernel<T, V><<<dim3(gx, splits), 256, 0, s>>>(g, rows, cols, per, part);
+  else
+    colsum_part_kernel<T, 1><<<dim3(gx, splits), 256, 0, s>>>(g, rows, cols, per, part);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_reduce_parts<T>(part, splits, cols, out, s);
+}
+
+template cudaError_t launch_colsum<float>(const float*, int64_t, int64_t, float*, float*, cudaStream_t);
+template cudaError_t launch_colsum<bf16>(const bf16*, int64_t, int64_t, float*, bf16*, cudaStream_t);
 template cudaError_t launch_pool_fwd<float>(const Geom&, int, const float*, float*, int64_t, cudaStream_t);
 template cudaError_t launch_pool_fwd<bf16>(const Geom&, int, const bf16*, bf16*, int64_t, cudaStream_t);
-template cudaError_t launch_pool_bwd<float>(const Geom&, int, const float*, float*, int64_t, cudaStream_t);
-template cudaError_t launch_pool_bwd<bf16>(const Geom&, int, const bf16*, bf16*, int64_t, cudaStream_t);
+template cudaError_t launch_pool_bwd<float>(const Geom&, int, const float*, float*, int64_t, int, cudaStream_t);
+template cudaError_t launch_pool_bwd<bf16>(const Geom&, int, const bf16*, bf16*, int64_t, int, cudaStream_t);
 
 }  // namespace llattn

@@ -22,7 +22,7 @@ long long g_launches[N_IDS];
 
 const char* kNames[N_IDS] = {"pool_fwd", "pool_bwd", "latent_fwd", "local_fwd", "gate_fwd",
                              "gate_bwd", "local_bwd", "rout_bwd", "reduce", "latent_bwd",
-                             "local_dq", "local_dkv", "decode"};
+                             "local_dq", "local_dkv", "decode", "colsum"};
 
 void drain_locked() {
   for (auto& p : g_pending) {

@@ -10,7 +10,7 @@ namespace prof {
 
 enum Id {
   POOL_FWD = 0, POOL_BWD, LATENT_FWD, LOCAL_FWD, GATE_FWD, GATE_BWD, LOCAL_BWD, ROUT_BWD, REDUCE, LATENT_BWD,
-  LOCAL_DQ, LOCAL_DKV, DECODE,
+  LOCAL_DQ, LOCAL_DKV, DECODE, COLSUM,
   N_IDS
 };
 

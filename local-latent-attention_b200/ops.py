@@ -282,6 +282,130 @@ def llattn_attention(qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tensor, b_rou
     return outs[0]
 
 
+# --------------------------------------------------------------------------
+# whole block: projections, pooling, attention core, output projection
+
+def colsum(g: Tensor) -> Tensor:
+    """Column sums of a contiguous [rows, cols] CUDA tensor, in its dtype with
+    fp32 accumulation in a fixed order: the bias gradient of a linear layer
+    whose output gradient is g (llattn_colsum)."""
+    _require(g.dim() == 2 and g.is_contiguous() and g.is_cuda, "colsum expects a contiguous 2-D CUDA tensor")
+    rows, cols = g.shape
+    code = _dtype_code(g)
+    L = _lib.lib()
+    ws = torch.empty(max(int(L.llattn_colsum_workspace_bytes(rows, cols, code)), 16), dtype=torch.uint8,
+                     device=g.device)
+    out = torch.empty(cols, dtype=g.dtype, device=g.device)
+    with torch.cuda.device(g.device):
+        _lib.check(L.llattn_colsum(_ptr(g), rows, cols, code, _ptr(out), _ptr(ws), ws.numel(), _stream(g)),
+                   "llattn_colsum")
+    return out
+
+
+def pool_bwd_accumulate_(dx: Tensor, dpooled: Tensor, latent_tokens: int, query_block: int, mode: int) -> Tensor:
+    """dx [B,T,d] += the pooling gradient of dpooled [B,rows,d] (in place)."""
+    _require(dx.is_contiguous() and dpooled.is_contiguous() and dx.dtype == dpooled.dtype,
+             "pool_bwd_accumulate_ expects contiguous tensors of one dtype")
+    B, T, d = dx.shape
+    dims = _lib.make_dims(B, T, latent_tokens=latent_tokens, query_block=query_block, dtype=_dtype_code(dx))
+    with torch.cuda.device(dx.device):
+        _lib.check(_lib.lib().llattn_pool_bwd(ctypes.byref(dims), mode | _lib.POOL_ACCUMULATE, _ptr(dpooled),
+                                              _ptr(dx), d, _stream(dx)), "llattn_pool_bwd")
+    return dx
+
+
+class BlockFunction(torch.autograd.Function):
+    """The whole attention block (models.py:307-462 with the projections of
+    models.py:80-84) as one autograd node, so its backward can fuse what
+    autograd would run as separate kernels: x's three gradient contributions
+    accumulate in place (the rq_proj input gradient as a beta=1 GEMM into the
+    qkv_proj one, the pooling gradients through llattn_pool_bwd's accumulate
+    mode) instead of two elementwise adds, and the four bias gradients are
+    llattn_colsum reductions. Same math and the same GEMMs as autograd over
+    the separate layers; activations, weights and biases share one dtype.
+
+    Inputs: x [B,T,d], then weight/bias of qkv_proj, rq_proj, rkv_proj,
+    r_out, the gate_local / gate_remote weights [1, hd], weight/bias of out,
+    and cfg = (n_heads, latent_heads, window, local_block_size, latent_tokens,
+    latent_query_block_size, gate_bias)."""
+
+    @staticmethod
+    def forward(ctx, x, w_qkv, b_qkv, w_rq, b_rq, w_rkv, b_rkv, w_rout, b_rout, g_local, g_remote, w_out,
+                b_out, cfg):
+        n_heads, latent_heads, window, local_block, latent_tokens, query_block, gate_bias = cfg
+        B, T, d = x.shape
+        x = x.contiguous()
+        F = torch.nn.functional
+        qkv = F.linear(x, w_qkv, b_qkv)
+        pooled = pool_fwd(x, latent_tokens, 0, _lib.POOL_CHUNKS)
+        gkv = F.linear(pooled, w_rkv, b_rkv)
+        qsrc = pool_fwd(x, latent_tokens, query_block, _lib.POOL_QBLOCKS) if query_block > 1 else None
+        rq = F.linear(x if qsrc is None else qsrc, w_rq, b_rq)
+        b_rout_f = b_rout.float().contiguous()
+        gl = g_local.float().reshape(-1).contiguous()
+        gr = g_remote.float().reshape(-1).contiguous()
+        mixed, local_out, lse, lat, lat_lse = attn_fwd(
+            qkv, rq, gkv, w_rout.contiguous(), b_rout_f, gl, gr, n_heads, latent_heads, window, local_block,
+            latent_tokens, query_block, float(gate_bias))
+        y = F.linear(mixed, w_out, b_out)
+        ctx.save_for_backward(x, qkv, pooled, qsrc, rq, gkv, mixed, local_out, lse, lat, lat_lse, w_qkv, w_rq,
+                              w_rkv, w_rout, b_rout_f, gl, gr, w_out)
+        ctx.cfg = cfg
+        ctx.dtypes = (b_rout.dtype, g_local.dtype, g_local.shape, g_remote.dtype, g_remote.shape)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x, qkv, pooled, qsrc, rq, gkv, mixed, local_out, lse, lat, lat_lse, w_qkv, w_rq, w_rkv, w_rout,
+         b_rout_f, gl, gr, w_out) = ctx.saved_tensors
+        n_heads, latent_heads, window, local_block, latent_tokens, query_block, gate_bias = ctx.cfg
+        b_rout_dt, gl_dt, gl_shape, gr_dt, gr_shape = ctx.dtypes
+        need = ctx.needs_input_grad
+        B, T, d = x.shape
+        M = B * T
+        dy2 = dy.to(x.dtype).contiguous().view(M, d)
+        x2 = x.view(M, d)
+        g = [None] * 14
+        dmixed = torch.mm(dy2, w_out)
+        if need[11]:
+            g[11] = torch.mm(dy2.t(), mixed.view(M, d))
+        if need[12]:
+            g[12] = colsum(dy2)
+        dqkv, drq, dgkv, dw_rout, db_rout, dgl, dgr = attn_bwd(
+            dmixed.view(B, T, d), qkv, rq, gkv, w_rout, b_rout_f, gl, gr, local_out, lse, lat, lat_lse,
+            n_heads, latent_heads, window, local_block, latent_tokens, query_block, float(gate_bias))
+        dqkv2 = dqkv.view(M, 3 * d)
+        drq2 = drq.view(-1, drq.shape[-1])
+        dgkv2 = dgkv.view(-1, dgkv.shape[-1])
+        if need[0]:
+            dx = torch.mm(dqkv2, w_qkv)
+            if qsrc is None:
+                dx.addmm_(drq2, w_rq)
+            dx = dx.view(B, T, d)
+            if qsrc is not None:
+                pool_bwd_accumulate_(dx, torch.mm(drq2, w_rq).view(B, -1, d), latent_tokens, query_block,
+                                     _lib.POOL_QBLOCKS)
+            pool_bwd_accumulate_(dx, torch.mm(dgkv2, w_rkv).view(B, -1, d), latent_tokens, 0, _lib.POOL_CHUNKS)
+            g[0] = dx
+        if need[1]:
+            g[1] = torch.mm(dqkv2.t(), x2)
+        if need[2]:
+            g[2] = colsum(dqkv2)
+        if need[3]:
+            g[3] = torch.mm(drq2.t(), x2 if qsrc is None else qsrc.view(-1, d))
+        if need[4]:
+            g[4] = colsum(drq2)
+        if need[5]:
+            g[5] = torch.mm(dgkv2.t(), pooled.view(-1, d))
+        if need[6]:
+            g[6] = colsum(dgkv2)
+        g[7] = dw_rout.to(w_rout.dtype) if need[7] else None
+        g[8] = db_rout.to(b_rout_dt) if need[8] else None
+        g[9] = dgl.to(gl_dt).view(gl_shape) if need[9] else None
+        g[10] = dgr.to(gr_dt).view(gr_shape) if need[10] else None
+        return tuple(g)
+
+
 def decode_core(qkv_cache: Tensor, seq_len: int, rq_row: Tensor, gkv: Tensor, w_rout: Tensor,
                 b_rout: Tensor, g_local: Tensor, g_remote: Tensor, *, n_heads: int, latent_heads: int,
                 window: int, local_block_size: int, latent_tokens: int,
