@@ -93,8 +93,10 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
   L.drow = take(sizeof(float) * BTd);
   L.dlat = take(sizeof(float) * (size_t)rows * g.Ld);
   L.dlat_tok = take(sizeof(float) * (size_t)g.B * g.T * g.Ld);
-  L.dg_part = take(sizeof(float) * (size_t)L.n_gate_cta * 2 * g.hd);
-  L.dg_sum = take(sizeof(float) * 2 * g.hd);
+  // dg partials: [n_gate_cta][2 hd] (SIMT gate) or [gate_bwd_ctas][hd + 65 H] (tensor-core gate)
+  const size_t dg_tc = (size_t)g.B * cdiv(g.T, 128) * (g.hd + 65 * g.H);
+  L.dg_part = take(sizeof(float) * std::max((size_t)L.n_gate_cta * 2 * g.hd, dg_tc));
+  L.dg_sum = take(sizeof(float) * (size_t)std::max(2 * g.hd, g.hd + 65 * g.H));
   L.dw_part = take(sizeof(float) * (size_t)L.n_split_w * g.d * (g.Ld + 1));
   L.dgkv_part = take(sizeof(float) * (size_t)L.n_split_lat * g.B * g.Nc * 2 * g.Ld);
   L.total = off;
@@ -220,21 +222,27 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
   if (rc) return rc;
   }
   {
-  prof::Scope ps(prof::REDUCE, s, 3);
+  prof::Scope ps(prof::REDUCE, s, tc ? 4 : 3);
   rc = check_launch(launch_reduce_rows(dw_part, L.n_split_w, (int64_t)g.d * g.Ld, a->dw_rout, s), "reduce_dw");
   if (rc) return rc;
   rc = check_launch(launch_reduce_rows(dw_part + (size_t)L.n_split_w * g.d * g.Ld, L.n_split_w, g.d, a->db_rout, s),
                     "reduce_db");
   if (rc) return rc;
-  // dg partials are [cta][2*hd] (local half, remote half)
-  rc = check_launch(launch_reduce_rows(dg_part, n_dg, 2 * g.hd, dg_sum, s), "reduce_dg");
+  // dg partials: SIMT [cta][2*hd] (local half, remote half); tensor-core
+  // [cta][hd + 65 H] (local, then the S1/S0 sums dg_remote is linear in)
+  const int dg_n = tc ? sm100::gate_dg_floats(g) : 2 * g.hd;
+  rc = check_launch(launch_reduce_rows(dg_part, n_dg, dg_n, dg_sum, s), "reduce_dg");
   if (rc) return rc;
   rc = check_launch(cudaMemcpyAsync(a->dg_local, dg_sum, sizeof(float) * g.hd, cudaMemcpyDeviceToDevice, s),
                     "copy dg_local");
   if (rc) return rc;
-  rc = check_launch(cudaMemcpyAsync(a->dg_remote, dg_sum + g.hd, sizeof(float) * g.hd,
-                                    cudaMemcpyDeviceToDevice, s),
-                    "copy dg_remote");
+  if (tc)
+    rc = check_launch(sm100::launch_gate_dgr_finalize(g, dg_sum, a->w_rout, a->b_rout, a->dg_remote, s),
+                      "gate_dgr_finalize");
+  else
+    rc = check_launch(cudaMemcpyAsync(a->dg_remote, dg_sum + g.hd, sizeof(float) * g.hd,
+                                      cudaMemcpyDeviceToDevice, s),
+                      "copy dg_remote");
   }
   if (rc) return rc;
   prof::Scope ps(prof::LATENT_BWD, s, 2);

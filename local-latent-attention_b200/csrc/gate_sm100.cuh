@@ -22,6 +22,42 @@ template <int G>
 constexpr int gate_max_heads() { return G == 2 ? 32 : 24; }  // per-head ds rows kept in shared memory
 constexpr int kGateMaxHeads = 32;
 
+// floats per CTA in dg_part: dg_local [hd], then S1_h [64] and S0_h per head
+__host__ __device__ constexpr int gate_dg_stride(int hd, int H) { return hd + H * 65; }
+
+// dg_remote[c] = -sum_h (sum_e S1_h[e] W[h*hd + c, e] + S0_h b[h*hd + c])
+// from the reduced gate partials (dg_sum + hd). Thread (c, head half).
+__global__ void __launch_bounds__(256) gate_dgr_finalize_kernel(Geom g, const float* __restrict__ dg_sum,
+                                                                const bf16* __restrict__ w_rout,
+                                                                const float* __restrict__ b_rout,
+                                                                float* __restrict__ dg_remote) {
+  __shared__ float part[256];
+  const int HD = g.hd, H = g.H;
+  const float* s1 = dg_sum + HD;
+  for (int c0 = 0; c0 < HD; c0 += 128) {
+    const int c = c0 + (threadIdx.x & 127), half = threadIdx.x >> 7;
+    float v = 0.f;
+    if (c < HD) {
+      for (int h = half; h < H; h += 2) {
+        const uint4* wrow = reinterpret_cast<const uint4*>(w_rout + ((int64_t)h * HD + c) * 64);
+        const float* sh = s1 + h * 65;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float wv[8];
+          unpack8(__ldg(wrow + q), wv);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) v = fmaf(sh[q * 8 + k], wv[k], v);
+        }
+        v = fmaf(sh[64], b_rout[(int64_t)h * HD + c], v);
+      }
+    }
+    part[threadIdx.x] = v;
+    __syncthreads();
+    if (threadIdx.x < 128 && c < HD) dg_remote[c] = -(part[threadIdx.x] + part[threadIdx.x + 128]);
+    __syncthreads();
+  }
+}
+
 template <int HD, int G = 2>
 struct GbLayout {
   static constexpr int TILE = BM * HD * 2;         // 128 rows x HD bf16 (HD/64 panels of 16 KB)
@@ -348,7 +384,7 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) LLATTN_TRACE_K(3, 60);
-  const int64_t part = ((int64_t)b * gridDim.x + blockIdx.x) * 2 * HD;
+  const int64_t part = ((int64_t)b * gridDim.x + blockIdx.x) * gate_dg_stride(HD, H);
   // dg_local partial [cta][0, HD): summed over the compute warps
   for (int e = threadIdx.x; e < HD; e += blockDim.x) {
     float v = 0.f;
@@ -356,44 +392,36 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
     for (int w8 = 0; w8 < 4 * G; ++w8) v += red[w8 * HD + e];
     dg_part[part + e] = v;
   }
-  // dg_remote partial [cta][HD, 2HD): S1_h[e] = sum_rows ds lat[row, e] and
-  // S0_h into the (now idle) local_out tile buffer, then -sum_h S1_h W_h^T + S0_h b_h
-  float* s1 = reinterpret_cast<float*>(smem + L::LT);  // [H][64], then S0 at [H*64 + h]
+  // dg_remote is linear in S1_h[e] = sum_rows ds lat[row, e] and
+  // S0_h = sum_rows ds: their per-CTA partials go to [cta][HD + h*65 + e]
+  // (e = 64: S0) and gate_dgr_finalize_kernel applies W_h, b_h once to the
+  // sums. Thread = (head, 4 consecutive e), 4 independent accumulators.
   const bool all_ok = !*abort;
-  for (int idx = threadIdx.x; idx < H * 65; idx += blockDim.x) {
-    const int h = idx / 65, e = idx % 65;
-    float v = 0.f;
+  for (int idx = threadIdx.x; idx < H * 16; idx += blockDim.x) {
+    const int h = idx >> 4, e0 = (idx & 15) * 4;
+    const int c = e0 >> 3, k0 = (e0 & 7) * 2;  // 16-byte chunk, byte offset in it
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, s0 = 0.f;
     if (all_ok) {
-      if (e < 64) {
-        const int c = e >> 3, k = e & 7;
-#pragma unroll 4
-        for (int r = 0; r < BM; ++r) {
-          const bf16* lrow = reinterpret_cast<const bf16*>(smem + L::LAT + r * 128 + ((c ^ (r & 7)) * 16));
-          v = fmaf(dsh[h * BM + r], __bfloat162float(lrow[k]), v);
-        }
-      } else {
-#pragma unroll 4
-        for (int r = 0; r < BM; ++r) v += dsh[h * BM + r];
+      const float* dh = dsh + h * BM;
+#pragma unroll 8
+      for (int r = 0; r < BM; ++r) {
+        const uint2 lv = *reinterpret_cast<const uint2*>(smem + L::LAT + r * 128 + ((c ^ (r & 7)) * 16) + k0);
+        const float dsv = dh[r];
+        const float2 l01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lv.x));
+        const float2 l23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lv.y));
+        a0 = fmaf(dsv, l01.x, a0);
+        a1 = fmaf(dsv, l01.y, a1);
+        a2 = fmaf(dsv, l23.x, a2);
+        a3 = fmaf(dsv, l23.y, a3);
+        s0 += dsv;
       }
     }
-    s1[h * 65 + e] = v;
-  }
-  __syncthreads();
-  for (int c = threadIdx.x; c < HD; c += blockDim.x) {
-    float v = 0.f;
-    for (int h = 0; h < H; ++h) {
-      const uint4* wrow = reinterpret_cast<const uint4*>(w_rout + ((int64_t)h * HD + c) * 64);
-      const float* sh = s1 + h * 65;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float wv[8];
-        unpack8(__ldg(wrow + q), wv);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) v = fmaf(sh[q * 8 + k], wv[k], v);
-      }
-      v = fmaf(sh[64], __ldg(b_rout + (int64_t)h * HD + c), v);
-    }
-    dg_part[part + HD + c] = -v;
+    float* o = dg_part + part + HD + h * 65;
+    o[e0] = a0;  // rows of 65 floats: not 16-byte aligned
+    o[e0 + 1] = a1;
+    o[e0 + 2] = a2;
+    o[e0 + 3] = a3;
+    if (e0 == 0) o[64] = s0;
   }
   if (warp == 1) {
     __syncwarp();

@@ -252,6 +252,13 @@ cudaError_t gate_bwd_hd(const Geom& g, const GateBwd& a, cudaStream_t s) {
 }  // namespace
 
 int gate_bwd_ctas(const Geom& g) { return g.B * cdiv(g.T, BM); }
+int gate_dg_floats(const Geom& g) { return gate_dg_stride(g.hd, g.H); }
+
+cudaError_t launch_gate_dgr_finalize(const Geom& g, const float* dg_sum, const void* w_rout, const float* b_rout,
+                                     float* dg_remote, cudaStream_t s) {
+  gate_dgr_finalize_kernel<<<1, 256, 0, s>>>(g, dg_sum, static_cast<const bf16*>(w_rout), b_rout, dg_remote);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_gate_bwd(const Geom& g, const GateBwd& a, cudaStream_t s) {
   // one head group per CTA, two CTAs per SM, unless the heads' ds rows do not fit

@@ -37,12 +37,18 @@ cudaError_t launch_local_dkv(const Geom& g, const void* qkv, const void* dl, con
 
 // Gate / r_out backward on tensor cores (needs gate_fusable): writes dl
 // (bf16 [B,T,d]), delta [B,H,T], dr (bf16 [B,T,d]), dlat_tok (fp32 [B,T,64])
-// and dg_part ([gate_bwd_ctas][2*hd], dg_local half then dg_remote half).
+// and dg_part ([gate_bwd_ctas][gate_dg_floats]).
 struct GateBwd {
   const void* local_out; const void* lat; const void* w_rout; const float* b_rout; const float* g_local;
   const float* g_remote; const void* dmixed; void* dl; float* delta; void* dr; float* dlat_tok; float* dg_part;
 };
 int gate_bwd_ctas(const Geom& g);
+// floats per gate CTA in dg_part: dg_local [hd], then per head S1_h [64] =
+// sum_t ds lat[t] and S0_h = sum_t ds, from which dg_remote follows linearly
+int gate_dg_floats(const Geom& g);
+// dg_remote [hd] from the CTA-summed dg partials (dg_sum [gate_dg_floats])
+cudaError_t launch_gate_dgr_finalize(const Geom& g, const float* dg_sum, const void* w_rout, const float* b_rout,
+                                     float* dg_remote, cudaStream_t s);
 cudaError_t launch_gate_bwd(const Geom& g, const GateBwd& a, cudaStream_t s);
 // dW_rout / db_rout partials over n_split token ranges: dw_part [n_split][d*64],
 // db_part [n_split][d]; dr bf16 [B*T, d] (d a multiple of 64), lat [B,Tq,64].
