@@ -46,7 +46,7 @@ struct FwdPPLayout {
   static constexpr int X = X_OVER_Q ? QA : V + NST * KTILE;
   static constexpr int CST = X_OVER_Q ? V + NST * KTILE : X + (PAIR ? 2 : 1) * XS;
   static constexpr int BAR = CST + 3 * HD * 4;  // b_rout[h], g_local, g_remote (hd floats each)
-  static constexpr int BYTES = BAR + 256;
+  static constexpr int BYTES = BAR + 320;  // PP_NB barriers, TMEM slot, abort flag
   static constexpr int TMEM_COLS = PAIR ? 512 : 256;
   static constexpr int O_BASE = PAIR ? 256 : 128;  // O_x at O_BASE + x * hd
   static constexpr int THREADS = PAIR ? 320 : 192;
@@ -57,10 +57,10 @@ struct FwdPPLayout {
 
 // per group g: S[2], P[2] (softmax arrivals), O[2] (PV done) — one barrier
 // per buffer, so a group running a tile ahead never makes a parity wait
-// ambiguous — plus LW (remote operands written) and R; shared: Q, K[2],
-// V[2], KVE[2]
+// ambiguous — plus LW (remote operands written) and R; shared: Q, K / V
+// loaded and K / V stage free per ring stage
 enum {
-  PP_Q = 0, PP_K = 1, PP_V = 4, PP_KVE = 7,  // K, V, KVE: + stage (3)
+  PP_Q = 0, PP_K = 1, PP_V = 4, PP_VE = 7,  // K, V loaded, V stage free: + stage (3)
   PP_LW = 10,  // + g
   PP_S = 12,   // + 2*g + buffer
   PP_P = 16,   // + 2*g + buffer
@@ -68,7 +68,8 @@ enum {
   PP_R = 24,   // + g
   PP_EP = 26,  // + g: epilogue tiles staged
   PP_SD = 28,  // group A's S MMAs done (!PAIR: Q free for the remote operands)
-  PP_NB = 29
+  PP_KE = 29,  // + stage (3): K stage free (its tile's S MMAs done)
+  PP_NB = 32
 };
 
 // The running max of a row is only moved (and O rescaled) when the new
@@ -129,7 +130,8 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
     for (int s = 0; s < L::NST; ++s) {
       mbar_init(&bars[PP_K + s], 1);
       mbar_init(&bars[PP_V + s], 1);
-      mbar_init(&bars[PP_KVE + s], 1);
+      mbar_init(&bars[PP_VE + s], 1);
+      mbar_init(&bars[PP_KE + s], 1);
     }
     for (int x = 0; x < 4; ++x) {
       mbar_init(&bars[PP_S + x], 1);
@@ -184,18 +186,27 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
         tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QA, q0, h, b);
         if (PAIR) tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QB, q0 + BM, h, b);
       }
-      for (int j = 0; j < nk; ++j) {
+      // K stages free once their tile's S MMAs are done, V stages once its
+      // PV MMAs are: K tiles are issued one tile ahead of V tiles, so a K
+      // load never waits behind a PV
+      int issued_v = 0;
+      auto load_kv = [&](int j, bool is_k) -> bool {
         const int s = j % L::NST;
-        if (j >= L::NST && !mbar_wait(&bars[PP_KVE + s], ((j / L::NST) - 1) & 1, abort, &g_fault_word)) {
+        if (j >= L::NST &&
+            !mbar_wait(&bars[(is_k ? PP_KE : PP_VE) + s], ((j / L::NST) - 1) & 1, abort, &g_fault_word))
+          return false;
+        const int bar = (is_k ? PP_K : PP_V) + s;
+        mbar_expect_tx(&bars[bar], L::KTILE);
+        tma_load_tile(&tm_kv, &bars[bar], smem + (is_k ? L::K : L::V) + s * L::KTILE, kbase + j * BNK,
+                      (is_k ? 1 : 2) * g.H + h, b);
+        if (is_k) issued = j + 1; else issued_v = j + 1;
+        return true;
+      };
+      for (int j = 0; j <= nk; ++j) {
+        if ((j < nk && !load_kv(j, true)) || (j >= 1 && !load_kv(j - 1, false))) {
           raise_fault(kFaultProducer, abort);
           break;
         }
-        const int k0 = kbase + j * BNK;
-        mbar_expect_tx(&bars[PP_K + s], L::KTILE);
-        tma_load_tile(&tm_kv, &bars[PP_K + s], smem + L::K + s * L::KTILE, k0, g.H + h, b);
-        mbar_expect_tx(&bars[PP_V + s], L::KTILE);
-        tma_load_tile(&tm_kv, &bars[PP_V + s], smem + L::V + s * L::KTILE, k0, 2 * g.H + h, b);
-        issued = j + 1;
       }
       if (fuse && L::X_OVER_Q && !*abort) {  // the remote operands go over Q once its S MMAs are done
         if (mbar_wait(&bars[PP_SD], 0, abort, &g_fault_word))
@@ -210,10 +221,10 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
         if (nk > 0) mbar_wait(&bars[PP_Q], 0, &none, &gnone, 100000000ull);
         if (fuse)
           for (int x = 0; x < (PAIR ? 2 : 1); ++x) mbar_wait(&bars[PP_LW + x], 0, &none, &gnone, 100000000ull);
-        for (int j = issued - L::NST < 0 ? 0 : issued - L::NST; j < issued; ++j) {
+        for (int j = issued - L::NST < 0 ? 0 : issued - L::NST; j < issued; ++j)
           mbar_wait(&bars[PP_K + j % L::NST], (j / L::NST) & 1, &none, &gnone, 100000000ull);
+        for (int j = issued_v - L::NST < 0 ? 0 : issued_v - L::NST; j < issued_v; ++j)
           mbar_wait(&bars[PP_V + j % L::NST], (j / L::NST) & 1, &none, &gnone, 100000000ull);
-        }
       }
     }
   } else if (warp == 1) {
@@ -230,14 +241,15 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
       //           reads P_x(i-2) from those columns, issued (i <= npv + 1)
       //   PV_x(i): P_x(i) landed and V tile loaded
       //   R_x: after the group's last PV, once its lat / W_rout rows are in
-      // A K/V stage is released (KVE commit) once every group using the tile
-      // has issued its PV for it; releases happen in tile order.
+      // A K stage is released (KE commit) once every group using the tile has
+      // issued its S for it, a V stage (VE) once they have issued its PV;
+      // releases happen in tile order.
       int ns[2] = {0, 0}, npv[2] = {0, 0};
       bool r_done[2] = {false, false};
       const int nx[2] = {tA.n(), has_b ? tB.n() : 0};
       const int first[2] = {tA.first, tB.first};
       const bool grp_on[2] = {true, has_b};
-      int released = 0;  // tiles whose stage was released
+      int released = 0, k_released = 0;  // tiles whose V / K stage was released
       if (nk > 0) ok = mbar_wait(&bars[PP_Q], 0, abort, &g_fault_word);
       LLATTN_TRACE_K(1, 2);
       uint64_t t_last = globaltimer_ns();
@@ -302,7 +314,19 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
           }
           if (npv[x] < nx[x] || (fuse && !r_done[x])) all_done = false;
         }
-        // release K/V stages in tile order
+        // release K stages in tile order once every group using the tile
+        // has issued its S MMAs, V stages once they have issued their PV
+        while (k_released < nk) {
+          const int j = k_released;
+          bool used_done = true;
+#pragma unroll
+          for (int x = 0; x < 2; ++x)
+            if (grp_on[x] && j >= first[x] && j < first[x] + nx[x] && ns[x] <= j - first[x]) used_done = false;
+          if (!used_done) break;
+          mma_commit(&bars[PP_KE + j % L::NST]);
+          ++k_released;
+          progress = true;
+        }
         while (released < nk) {
           const int j = released;
           bool used_done = true;
@@ -310,11 +334,11 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
           for (int x = 0; x < 2; ++x)
             if (grp_on[x] && j >= first[x] && j < first[x] + nx[x] && npv[x] <= j - first[x]) used_done = false;
           if (!used_done) break;
-          mma_commit(&bars[PP_KVE + j % L::NST]);
+          mma_commit(&bars[PP_VE + j % L::NST]);
           ++released;
           progress = true;
         }
-        if (all_done && released == nk) break;
+        if (all_done && released == nk && k_released == nk) break;
         if (progress) {
           t_last = globaltimer_ns();
           spin = 0;
