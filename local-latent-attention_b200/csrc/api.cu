@@ -246,11 +246,20 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
   }
   if (rc) return rc;
   prof::Scope ps(prof::LATENT_BWD, s, 2);
-  rc = check_launch(launch_latent_bwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv),
-                                         a->lat_lse, dlat, static_cast<T*>(a->drq), dgkv_part, L.n_split_lat, s),
-                    "latent_bwd");
+  // tensor-core latent backward for bf16 with head dim 32 and <= 64 chunks;
+  // its row splits are 128-row tiles, at most the SIMT kernel's 64-row count
+  const bool lat_tc = sizeof(T) == 2 && sm100::latent_tc_ok(g);
+  const int n_split_lat = lat_tc ? std::min(sm100::latent_tc_splits(g), L.n_split_lat) : L.n_split_lat;
+  if (lat_tc)
+    rc = check_launch(sm100::launch_latent_bwd_tc(g, a->rq, a->gkv, a->lat_lse, dlat, a->drq, dgkv_part,
+                                                  n_split_lat, s),
+                      "latent_bwd_sm100");
+  else
+    rc = check_launch(launch_latent_bwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv),
+                                           a->lat_lse, dlat, static_cast<T*>(a->drq), dgkv_part, n_split_lat, s),
+                      "latent_bwd");
   if (rc) return rc;
-  return check_launch(launch_latent_reduce<T>(g, dgkv_part, L.n_split_lat, static_cast<T*>(a->dgkv), s),
+  return check_launch(launch_latent_reduce<T>(g, dgkv_part, n_split_lat, static_cast<T*>(a->dgkv), s),
                       "latent_reduce");
 }
 

@@ -1,0 +1,305 @@
+// Backward of the latent branch on the tensor cores (included by
+// local_sm100.cu), for latent head dim 32 and at most 64 chunks (one key
+// tile), bf16 activations. Math as the SIMT kernel of latent.cu: with
+// P = softmax(lat_scale rq.gk) over chunks j < qid(r) (models.py:361-375),
+// dP = dlat.gv, delta = sum_j P dP, dS = P (dP - delta):
+//   drq = lat_scale dS gk,  dgk = lat_scale dS^T rq,  dgv = P^T dlat.
+//
+// CTA = (row split, latent head, b); it walks the 128-row tiles
+// rb = split + k * n_split of its (b, head). Warps 0-3: thread = row = TMEM
+// lane (operand rows in, softmax, drq out); warp 4: TMEM allocation and the
+// single MMA-issuing thread. Per tile:
+//   1. S = rq gk^T and dP = dlat gv^T as kind::tf32 MMAs (fp32 operands: dlat
+//      keeps 11 mantissa bits, since dP - delta cancels when the pooled values
+//      are close; rq and gk are bf16 values, exact in tf32)
+//   2. the threads form P, delta, dS in fp32; dS goes to TMEM as bf16 (A of
+//      the drq MMA) and both dS and P to shared memory as bf16
+//   3. drq = dS [gk | gv] (N = 64, the gv half unused) with A from TMEM, and
+//      D2 += [rq | dlat]^T [dS | P] over the tile's rows (M = 128, N = 128,
+//      both operands MN-major): rows e < 32 x columns j < 64 are dgk^T / lat_scale,
+//      rows 32 + e x columns 64 + j are dgv^T. D2 stays in TMEM across the
+//      CTA's tiles and is written once as the CTA's partial.
+// Everything within a tile is sequential; two CTAs per SM overlap each other.
+
+struct LatTcLayout {
+  static constexpr int AS = 0;              // rq fp32 [128 rows][32] (K-major, tf32)
+  static constexpr int AD = AS + 16384;     // dlat fp32 [128][32]
+  static constexpr int X = AD + 16384;      // [128 rows][rq bf16 32 | dlat bf16 32] (MN-major A of D2)
+  static constexpr int BP = X + 16384;      // dS bf16 [128 rows][64 keys], then P at BP + 16384
+  static constexpr int GK = BP + 32768;     // gk fp32 [64 keys][32]
+  static constexpr int GV = GK + 8192;      // gv fp32 [64][32]
+  static constexpr int GKV = GV + 8192;     // [64 keys][gk bf16 32 | gv bf16 32] (MN-major B of drq)
+  static constexpr int BAR = GKV + 8192;
+  static constexpr int BYTES = BAR + 128;
+  static_assert(BYTES + 1024 <= 113 * 1024, "two CTAs per SM");
+};
+
+enum { LT_A = 0, LT_S = 1, LT_P = 2, LT_T = 3, LT_NB = 4 };
+
+__device__ __forceinline__ uint4* lat_chunk(uint8_t* tile, int row, int c) {  // 16-byte chunk c of a 128-byte row
+  return reinterpret_cast<uint4*>(tile + row * 128 + ((c ^ (row & 7)) * 16));
+}
+
+__global__ void __launch_bounds__(160, 2)
+    latent_bwd_tc_kernel(Geom g, const bf16* __restrict__ rq, const bf16* __restrict__ gkv,
+                         const float* __restrict__ lat_lse, const float* __restrict__ dlat, bf16* __restrict__ drq,
+                         float* __restrict__ part, int n_split) {
+  using L = LatTcLayout;
+  extern __shared__ __align__(1024) uint8_t smem_lat_tc[];
+  uint8_t* smem = smem_lat_tc;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + LT_NB);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  if (smem_u32(smem) & 1023u) {
+    if (threadIdx.x == 0) atomicOr(&g_fault_word, kFaultEpilogue);
+    return;
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, tid = threadIdx.x;
+  const int split = blockIdx.x, lh = blockIdx.y, b = blockIdx.z;
+  const int n_rb = cdiv(g.Tq, BM);
+  const int n_tiles = split < n_rb ? (n_rb - 1 - split) / n_split + 1 : 0;
+
+  if (tid == 0) {
+    mbar_init(&bars[LT_A], BM);
+    mbar_init(&bars[LT_S], 1);
+    mbar_init(&bars[LT_P], BM);
+    mbar_init(&bars[LT_T], 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  // chunk keys / values of (b, lh): thread = (key, half of the 32 dims)
+  if (tid < BM) {
+    const int key = tid >> 1, e0 = (tid & 1) * 16;
+    uint4 k2[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, v2[2] = {k2[0], k2[1]};
+    if (key < g.Nc) {
+      const uint4* kp = reinterpret_cast<const uint4*>(gkv + ((int64_t)(b * g.Nc + key) * 2 * g.Lh + lh) * 32 + e0);
+      const uint4* vp =
+          reinterpret_cast<const uint4*>(gkv + ((int64_t)(b * g.Nc + key) * 2 * g.Lh + g.Lh + lh) * 32 + e0);
+      k2[0] = kp[0];
+      k2[1] = kp[1];
+      v2[0] = vp[0];
+      v2[1] = vp[1];
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      float kf[8], vf[8];
+      unpack8(k2[q], kf);
+      unpack8(v2[q], vf);
+      const int c = (e0 >> 2) + 2 * q;  // fp32 chunks of 4
+      *lat_chunk(smem + L::GK, key, c) = make_uint4(__float_as_uint(kf[0]), __float_as_uint(kf[1]),
+                                                    __float_as_uint(kf[2]), __float_as_uint(kf[3]));
+      *lat_chunk(smem + L::GK, key, c + 1) = make_uint4(__float_as_uint(kf[4]), __float_as_uint(kf[5]),
+                                                        __float_as_uint(kf[6]), __float_as_uint(kf[7]));
+      *lat_chunk(smem + L::GV, key, c) = make_uint4(__float_as_uint(vf[0]), __float_as_uint(vf[1]),
+                                                    __float_as_uint(vf[2]), __float_as_uint(vf[3]));
+      *lat_chunk(smem + L::GV, key, c + 1) = make_uint4(__float_as_uint(vf[4]), __float_as_uint(vf[5]),
+                                                        __float_as_uint(vf[6]), __float_as_uint(vf[7]));
+      *lat_chunk(smem + L::GKV, key, (e0 >> 3) + q) = k2[q];       // gk bf16: chunks 0-3
+      *lat_chunk(smem + L::GKV, key, 4 + (e0 >> 3) + q) = v2[q];   // gv bf16: chunks 4-7
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM: S [0,64) (then drq / the unused dS gv product), dP [64,128) with dS
+  // bf16 over [64,96), D2 [128,256)
+  const uint32_t tS = tmem, tP = tmem + 64, tD2 = tmem + 128;
+
+  if (warp == 4) {
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t id1 = idesc_tf32_f32(BM, 64);
+      constexpr uint32_t idQ = idesc_bf16_f32(BM, 64, false, true);   // dS [gk | gv]
+      constexpr uint32_t id2 = idesc_bf16_f32(BM, 128, true, true);   // [rq | dlat]^T [dS | P]
+      const uint64_t das = desc_sw128(smem_u32(smem + L::AS), 16, 1024);
+      const uint64_t dad = desc_sw128(smem_u32(smem + L::AD), 16, 1024);
+      const uint64_t dgk = desc_sw128(smem_u32(smem + L::GK), 16, 1024);
+      const uint64_t dgv = desc_sw128(smem_u32(smem + L::GV), 16, 1024);
+      const uint64_t dkv = desc_sw128(smem_u32(smem + L::GKV), 8192, 1024);
+      // M = 128 reads a second 64-row panel of A 16 KB on (the dS tile): the
+      // D2 rows it produces (64-127) are never read
+      const uint64_t dx = desc_sw128(smem_u32(smem + L::X), 16384, 1024);
+      const uint64_t dbp = desc_sw128(smem_u32(smem + L::BP), 16384, 1024);
+      bool ok = true;
+      for (int n = 0; ok && n < n_tiles; ++n) {
+        if (!(ok = mbar_wait(&bars[LT_A], n & 1, abort, &g_fault_word))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_tf32(tS, desc_add(das, kk * 32), desc_add(dgk, kk * 32), id1, kk > 0);
+          mma_tf32(tP, desc_add(dad, kk * 32), desc_add(dgv, kk * 32), id1, kk > 0);
+        }
+        mma_commit(&bars[LT_S]);
+        if (!(ok = mbar_wait(&bars[LT_P], n & 1, abort, &g_fault_word))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(tS, tP + kk * 8, desc_add(dkv, kk * 2048), idQ, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk)
+          mma_bf16(tD2, desc_add(dx, kk * 2048), desc_add(dbp, kk * 2048), id2, (n > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&bars[LT_T]);
+      }
+      if (!ok) raise_fault(kFaultMma, abort);
+    }
+  } else {
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    const float sc2 = g.lat_scale * kLog2e;
+    const int ldh = 32;
+    uint4 pre_q[4], pre_d[8];  // next tile's rq (bf16) / dlat (fp32) row
+    float pre_lse = INFINITY;
+    auto fetch = [&](int n) {
+      const int r = (split + n * n_split) * BM + tid;
+      if (n < n_tiles && r < g.Tq) {
+        const uint4* qp = reinterpret_cast<const uint4*>(rq + ((int64_t)(b * g.Tq + r) * g.Lh + lh) * ldh);
+        const uint4* dp = reinterpret_cast<const uint4*>(dlat + (int64_t)(b * g.Tq + r) * g.Ld + lh * ldh);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pre_q[i] = __ldg(qp + i);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pre_d[i] = __ldg(dp + i);
+        pre_lse = __ldg(lat_lse + (int64_t)(b * g.Lh + lh) * g.Tq + r) * kLog2e;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pre_q[i] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pre_d[i] = make_uint4(0, 0, 0, 0);
+        pre_lse = INFINITY;
+      }
+    };
+    fetch(0);
+    bool ok = true;
+    for (int n = 0; n < n_tiles; ++n) {
+      const int r = (split + n * n_split) * BM + tid;
+      const bool valid = r < g.Tq;
+      const int qid = valid ? row_qid(g, r) : 0;
+      const float lse2 = pre_lse;
+      // operands of this tile (the previous tile's MMAs finished reading them)
+      if (n > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[LT_T], (n - 1) & 1, abort, &g_fault_word));
+        if (!ok) break;
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) *lat_chunk(smem + L::AD, tid, c) = pre_d[c];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float f[8];
+        unpack8(pre_q[i], f);
+        *lat_chunk(smem + L::AS, tid, 2 * i) = make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]),
+                                                          __float_as_uint(f[2]), __float_as_uint(f[3]));
+        *lat_chunk(smem + L::AS, tid, 2 * i + 1) = make_uint4(__float_as_uint(f[4]), __float_as_uint(f[5]),
+                                                              __float_as_uint(f[6]), __float_as_uint(f[7]));
+        *lat_chunk(smem + L::X, tid, i) = pre_q[i];
+        const float4 d0 = *reinterpret_cast<const float4*>(&pre_d[2 * i]);
+        const float4 d1 = *reinterpret_cast<const float4*>(&pre_d[2 * i + 1]);
+        *lat_chunk(smem + L::X, tid, 4 + i) = make_uint4(pack_bf16(d0.x, d0.y), pack_bf16(d0.z, d0.w),
+                                                         pack_bf16(d1.x, d1.y), pack_bf16(d1.z, d1.w));
+      }
+      fence_async_smem();
+      mbar_arrive(&bars[LT_A]);
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[LT_S], n & 1, abort, &g_fault_word));
+      if (!ok) break;
+      tc_fence_after();
+      // P and dP of this row: keys in two halves of 32
+      float p[64], dp[64];
+      {
+        uint32_t rs[32], rp[32];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          tmem_ld32(tS + lane_off + hh * 32, rs);
+          tmem_ld32(tP + lane_off + hh * 32, rp);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int j = hh * 32 + i;
+            p[j] = j < qid ? fast_exp2(fmaf(__uint_as_float(rs[i]), sc2, -lse2)) : 0.f;
+            dp[j] = __uint_as_float(rp[i]);
+          }
+        }
+      }
+      float delta = 0.f;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) delta = fmaf(p[j], dp[j], delta);
+      uint32_t pk[32], pp[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        pk[i] = pack_bf16(p[2 * i] * (dp[2 * i] - delta), p[2 * i + 1] * (dp[2 * i + 1] - delta));
+        pp[i] = pack_bf16(p[2 * i], p[2 * i + 1]);
+      }
+      {
+        uint32_t lo[16], hi[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          lo[i] = pk[i];
+          hi[i] = pk[16 + i];
+        }
+        tmem_st16(tP + lane_off, lo);
+        tmem_st16(tP + lane_off + 16, hi);
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        *lat_chunk(smem + L::BP, tid, c) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        *lat_chunk(smem + L::BP + 16384, tid, c) = make_uint4(pp[4 * c], pp[4 * c + 1], pp[4 * c + 2], pp[4 * c + 3]);
+      }
+      tmem_st_wait();
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars[LT_P]);
+      fetch(n + 1);  // next tile's rows load during this tile's MMAs
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[LT_T], n & 1, abort, &g_fault_word));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t rq32[32];
+      tmem_ld32(tS + lane_off, rq32);
+      tmem_ld_wait();
+      if (valid) {
+        uint4* dst = reinterpret_cast<uint4*>(drq + ((int64_t)(b * g.Tq + r) * g.Lh + lh) * ldh);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          dst[c] = make_uint4(pack_bf16(__uint_as_float(rq32[8 * c]) * g.lat_scale,
+                                        __uint_as_float(rq32[8 * c + 1]) * g.lat_scale),
+                              pack_bf16(__uint_as_float(rq32[8 * c + 2]) * g.lat_scale,
+                                        __uint_as_float(rq32[8 * c + 3]) * g.lat_scale),
+                              pack_bf16(__uint_as_float(rq32[8 * c + 4]) * g.lat_scale,
+                                        __uint_as_float(rq32[8 * c + 5]) * g.lat_scale),
+                              pack_bf16(__uint_as_float(rq32[8 * c + 6]) * g.lat_scale,
+                                        __uint_as_float(rq32[8 * c + 7]) * g.lat_scale));
+      }
+    }
+    if (!ok) raise_fault(kFaultSoftmax, abort);
+    // this CTA's dgk / dgv partial: warp 0 holds D2 rows e (dgk^T), warp 1
+    // rows 32 + e (dgv^T); partial layout [split][b][key][2][Ld]
+    if (warp < 2) {
+      float* my_part = part + ((int64_t)split * g.B + b) * g.Nc * 2 * g.Ld + lh * ldh + lane;
+      const float mul = warp == 0 ? g.lat_scale : 1.f;
+      const bool have = ok && n_tiles > 0 && !*abort;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t v[32];
+        if (have) {
+          tmem_ld32(tD2 + lane_off + warp * 64 + hh * 32, v);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = hh * 32 + i;
+          if (key < g.Nc) my_part[(int64_t)(2 * key + warp) * g.Ld] = __uint_as_float(v[i]) * mul;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}

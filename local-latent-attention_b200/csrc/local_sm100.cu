@@ -72,6 +72,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 #include "local_sm100_fwd_pp.cuh"
 #include "local_sm100_bwd.cuh"
 #include "gate_sm100.cuh"
+#include "latent_sm100.cuh"
 
 // ---------------------------------------------------------------------------
 // host side
@@ -285,6 +286,24 @@ cudaError_t launch_rout_dw(const Geom& g, const void* dr, const void* lat, float
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.d, 128), n_split);
   rout_dw_tc_kernel<<<grid, 192, smem, s>>>(tm, tl, g, static_cast<const bf16*>(lat), dw_part, db_part, n_split);
+  return cudaGetLastError();
+}
+
+bool latent_tc_ok(const Geom& g) { return g.ldh == 32 && g.Nc <= 64 && g.Tq >= 1; }
+
+int latent_tc_splits(const Geom& g) { return std::max(1, std::min(cdiv(g.Tq, BM), (2 * sm_count()) / (g.B * g.Lh))); }
+
+cudaError_t launch_latent_bwd_tc(const Geom& g, const void* rq, const void* gkv, const float* lat_lse,
+                                 const float* dlat, void* drq, float* part, int n_split, cudaStream_t s) {
+  if (!latent_tc_ok(g)) return cudaErrorNotSupported;
+  if (((uintptr_t)rq & 15) || ((uintptr_t)gkv & 15) || ((uintptr_t)dlat & 15) || ((uintptr_t)drq & 15))
+    return cudaErrorMisalignedAddress;
+  const int smem = LatTcLayout::BYTES;  // the kernel's shared memory is 1024-byte aligned
+  cudaError_t e = cudaFuncSetAttribute(latent_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(n_split, g.Lh, g.B);
+  latent_bwd_tc_kernel<<<grid, 160, smem, s>>>(g, static_cast<const bf16*>(rq), static_cast<const bf16*>(gkv),
+                                               lat_lse, dlat, static_cast<bf16*>(drq), part, n_split);
   return cudaGetLastError();
 }
 

@@ -42,6 +42,13 @@ struct GateBwd {
   const void* local_out; const void* lat; const void* w_rout; const float* b_rout; const float* g_local;
   const float* g_remote; const void* dmixed; void* dl; float* delta; void* dr; float* dlat_tok; float* dg_part;
 };
+// Latent backward on tensor cores (latent head dim 32, at most 64 chunks,
+// bf16): drq and per-split dgk/dgv partials [n_split][B][Nc][2][Ld] as the
+// SIMT kernel writes them; n_split = latent_tc_splits(g) row splits.
+bool latent_tc_ok(const Geom& g);
+int latent_tc_splits(const Geom& g);
+cudaError_t launch_latent_bwd_tc(const Geom& g, const void* rq, const void* gkv, const float* lat_lse,
+                                 const float* dlat, void* drq, float* part, int n_split, cudaStream_t s);
 int gate_bwd_ctas(const Geom& g);
 // floats per gate CTA in dg_part: dg_local [hd], then per head S1_h [64] =
 // sum_t ds lat[t] and S0_h = sum_t ds, from which dg_remote follows linearly

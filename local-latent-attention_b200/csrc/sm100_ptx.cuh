@@ -7,8 +7,9 @@
 //   smem desc: [0,14) start>>4, [16,30) leading-byte-offset>>4,
 //              [32,46) stride-byte-offset>>4, [46,48) version = 1,
 //              [49,52) base offset = 0, [61,64) layout (2 = 128-byte swizzle)
-//   idesc:     [4,6) D format (1 = f32), [7,10) A format (1 = bf16),
-//              [10,13) B format (1 = bf16), bit 15 A MN-major, bit 16 B MN-major,
+//   idesc:     [4,6) D format (1 = f32), [7,10) A format (1 = bf16; 2 = tf32
+//              under .kind::tf32), [10,13) B format (same codes), bit 15 A
+//              MN-major, bit 16 B MN-major,
 //              [17,23) N>>3, [24,29) M>>4
 #pragma once
 
@@ -253,6 +254,17 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// kind::tf32: fp32 operands in shared memory read as tf32 (one K=8 step
+// spans 32 bytes of a K-major row), fp32 accumulation
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Same with A read from TMEM (K-major: lane = row of A, 32-bit column c
 // holds elements 2c (low half) and 2c+1; one K=16 step spans 8 columns).
 __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
@@ -294,6 +306,11 @@ __device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t byte_off) { re
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn, bool b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// kind::tf32 instruction descriptor: A and B format 2 (tf32), D f32, both K-major
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // 2^x with the SFU's approximate exp2 (ex2.approx.ftz): ~2 ulp, denormal
