@@ -111,7 +111,10 @@ int run_fwd(const Geom& g, const llattn_fwd_args* a, cudaStream_t s) {
   int rc;
   {
     prof::Scope ps(prof::LATENT_FWD, s);
-    rc = check_launch(launch_latent_fwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv),
+    if (sizeof(T) == 2 && sm100::latent_tc_ok(g))  // tensor cores: bf16, head dim 32, <= 64 chunks
+      rc = check_launch(sm100::launch_latent_fwd_tc(g, a->rq, a->gkv, a->lat, a->lat_lse, s), "latent_fwd_sm100");
+    else
+      rc = check_launch(launch_latent_fwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv),
                                              static_cast<T*>(a->lat), a->lat_lse, s),
                         "latent_fwd");
   }

@@ -303,3 +303,190 @@ __global__ void __launch_bounds__(160, 2)
     tmem_dealloc(tmem, 256);
   }
 }
+
+// Forward of the latent branch on the tensor cores (same conditions): per
+// 128-row tile, S = rq gk^T (bf16 operands, fp32 accumulation), the
+// threads mask chunks j >= qid(r), take the row max and P = 2^(S sc - max) in
+// fp32 (the normaliser l sums the fp32 P), and write P as bf16 over the S
+// columns; lat = (P [gk | gv]) / l from the gv half, lat_lse = max + ln l
+// (INFINITY and lat = 0 for rows that see no chunk, models.py:366-373).
+struct LatFwdTcLayout {
+  static constexpr int AQ = 0;              // rq bf16 [128 rows][32] in 128-byte rows (first 64 bytes)
+  static constexpr int GKV = AQ + 16384;    // [64 keys][gk bf16 32 | gv bf16 32]
+  static constexpr int BAR = GKV + 8192;
+  static constexpr int BYTES = BAR + 128;
+};
+
+__global__ void __launch_bounds__(160)
+    latent_fwd_tc_kernel(Geom g, const bf16* __restrict__ rq, const bf16* __restrict__ gkv, bf16* __restrict__ lat,
+                         float* __restrict__ lat_lse, int n_split) {
+  using L = LatFwdTcLayout;
+  extern __shared__ __align__(1024) uint8_t smem_latf_tc[];
+  uint8_t* smem = smem_latf_tc;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + LT_NB);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  if (smem_u32(smem) & 1023u) {
+    if (threadIdx.x == 0) atomicOr(&g_fault_word, kFaultEpilogue);
+    return;
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, tid = threadIdx.x;
+  const int split = blockIdx.x, lh = blockIdx.y, b = blockIdx.z;
+  const int n_rb = cdiv(g.Tq, BM);
+  const int n_tiles = split < n_rb ? (n_rb - 1 - split) / n_split + 1 : 0;
+
+  if (tid == 0) {
+    mbar_init(&bars[LT_A], BM);
+    mbar_init(&bars[LT_S], 1);
+    mbar_init(&bars[LT_P], BM);
+    mbar_init(&bars[LT_T], 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, 128);
+    tmem_relinquish();
+  }
+  if (tid < BM) {  // chunk keys / values of (b, lh): thread = (key, half of the 32 dims)
+    const int key = tid >> 1, e0 = (tid & 1) * 16;
+    uint4 k2[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, v2[2] = {k2[0], k2[1]};
+    if (key < g.Nc) {
+      const uint4* kp = reinterpret_cast<const uint4*>(gkv + ((int64_t)(b * g.Nc + key) * 2 * g.Lh + lh) * 32 + e0);
+      const uint4* vp =
+          reinterpret_cast<const uint4*>(gkv + ((int64_t)(b * g.Nc + key) * 2 * g.Lh + g.Lh + lh) * 32 + e0);
+      k2[0] = kp[0];
+      k2[1] = kp[1];
+      v2[0] = vp[0];
+      v2[1] = vp[1];
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      *lat_chunk(smem + L::GKV, key, (e0 >> 3) + q) = k2[q];
+      *lat_chunk(smem + L::GKV, key, 4 + (e0 >> 3) + q) = v2[q];
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 64;  // S [0,64) with P bf16 over [0,32); P [gk | gv] at [64,128)
+
+  if (warp == 4) {
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(BM, 64, false, false);  // rq gk^T
+      constexpr uint32_t idO = idesc_bf16_f32(BM, 64, false, true);   // P [gk | gv]
+      const uint64_t daq = desc_sw128(smem_u32(smem + L::AQ), 16, 1024);
+      const uint64_t dk = desc_sw128(smem_u32(smem + L::GKV), 16, 1024);
+      const uint64_t dkv = desc_sw128(smem_u32(smem + L::GKV), 8192, 1024);
+      bool ok = true;
+      for (int n = 0; ok && n < n_tiles; ++n) {
+        if (!(ok = mbar_wait(&bars[LT_A], n & 1, abort, &g_fault_word))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) mma_bf16(tS, desc_add(daq, kk * 32), desc_add(dk, kk * 32), idS, kk > 0);
+        mma_commit(&bars[LT_S]);
+        if (!(ok = mbar_wait(&bars[LT_P], n & 1, abort, &g_fault_word))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(tO, tS + kk * 8, desc_add(dkv, kk * 2048), idO, kk > 0);
+        mma_commit(&bars[LT_T]);
+      }
+      if (!ok) raise_fault(kFaultMma, abort);
+    }
+  } else {
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    const float sc2 = g.lat_scale * kLog2e;
+    uint4 pre_q[4];
+    auto fetch = [&](int n) {
+      const int r = (split + n * n_split) * BM + tid;
+      if (n < n_tiles && r < g.Tq) {
+        const uint4* qp = reinterpret_cast<const uint4*>(rq + ((int64_t)(b * g.Tq + r) * g.Lh + lh) * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pre_q[i] = __ldg(qp + i);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pre_q[i] = make_uint4(0, 0, 0, 0);
+      }
+    };
+    fetch(0);
+    bool ok = true;
+    for (int n = 0; n < n_tiles; ++n) {
+      const int r = (split + n * n_split) * BM + tid;
+      const bool valid = r < g.Tq;
+      const int qid = valid ? row_qid(g, r) : 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) *lat_chunk(smem + L::AQ, tid, i) = pre_q[i];
+      fence_async_smem();
+      mbar_arrive(&bars[LT_A]);
+      fetch(n + 1);
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[LT_S], n & 1, abort, &g_fault_word));
+      if (!ok) break;
+      tc_fence_after();
+      float s[64];
+      {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tS + lane_off, r0);
+        tmem_ld32(tS + lane_off + 32, r1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          s[i] = i < qid ? __uint_as_float(r0[i]) * sc2 : -INFINITY;
+          s[32 + i] = 32 + i < qid ? __uint_as_float(r1[i]) * sc2 : -INFINITY;
+        }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) mx = fmaxf(mx, s[j]);
+      const float mb = qid > 0 ? mx : 0.f;
+      float l = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float p0 = 2 * i < qid ? fast_exp2(s[2 * i] - mb) : 0.f;
+        const float p1 = 2 * i + 1 < qid ? fast_exp2(s[2 * i + 1] - mb) : 0.f;
+        l += p0 + p1;
+        pk[i] = pack_bf16(p0, p1);
+      }
+      {
+        uint32_t lo[16], hi[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          lo[i] = pk[i];
+          hi[i] = pk[16 + i];
+        }
+        tmem_st16(tS + lane_off, lo);
+        tmem_st16(tS + lane_off + 16, hi);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars[LT_P]);
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[LT_T], n & 1, abort, &g_fault_word));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t o[32];
+      tmem_ld32(tO + lane_off + 32, o);  // the gv half
+      tmem_ld_wait();
+      if (valid) {
+        const float inv = qid > 0 ? 1.f / l : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(lat + (int64_t)(b * g.Tq + r) * g.Ld + lh * 32);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          dst[c] = make_uint4(pack_bf16(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
+                              pack_bf16(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
+                              pack_bf16(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
+                              pack_bf16(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
+        lat_lse[(int64_t)(b * g.Lh + lh) * g.Tq + r] = qid > 0 ? (mb + log2f(l)) * kLn2 : INFINITY;
+      }
+    }
+    if (!ok) raise_fault(kFaultSoftmax, abort);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}

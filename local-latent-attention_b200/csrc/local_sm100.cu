@@ -307,6 +307,21 @@ cudaError_t launch_latent_bwd_tc(const Geom& g, const void* rq, const void* gkv,
   return cudaGetLastError();
 }
 
+cudaError_t launch_latent_fwd_tc(const Geom& g, const void* rq, const void* gkv, void* lat, float* lat_lse,
+                                 cudaStream_t s) {
+  if (!latent_tc_ok(g)) return cudaErrorNotSupported;
+  if (((uintptr_t)rq & 15) || ((uintptr_t)gkv & 15) || ((uintptr_t)lat & 15)) return cudaErrorMisalignedAddress;
+  const int smem = LatFwdTcLayout::BYTES;  // the kernel's shared memory is 1024-byte aligned
+  cudaError_t e = cudaFuncSetAttribute(latent_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  // up to four CTAs per SM (128 TMEM columns each)
+  const int n_split = std::max(1, std::min(cdiv(g.Tq, BM), (4 * sm_count()) / (g.B * g.Lh)));
+  dim3 grid(n_split, g.Lh, g.B);
+  latent_fwd_tc_kernel<<<grid, 160, smem, s>>>(g, static_cast<const bf16*>(rq), static_cast<const bf16*>(gkv),
+                                               static_cast<bf16*>(lat), lat_lse, n_split);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_dlat_rowsum(const Geom& g, const float* dlat_tok, float* dlat, cudaStream_t s) {
   const int64_t n = (int64_t)g.B * g.Tq * 64;
   dlat_rowsum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(g, dlat_tok, dlat);

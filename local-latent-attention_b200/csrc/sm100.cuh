@@ -49,6 +49,9 @@ bool latent_tc_ok(const Geom& g);
 int latent_tc_splits(const Geom& g);
 cudaError_t launch_latent_bwd_tc(const Geom& g, const void* rq, const void* gkv, const float* lat_lse,
                                  const float* dlat, void* drq, float* part, int n_split, cudaStream_t s);
+// Latent forward on tensor cores (same conditions): lat [B,Tq,Ld], lat_lse [B,Lh,Tq]
+cudaError_t launch_latent_fwd_tc(const Geom& g, const void* rq, const void* gkv, void* lat, float* lat_lse,
+                                 cudaStream_t s);
 int gate_bwd_ctas(const Geom& g);
 // floats per gate CTA in dg_part: dg_local [hd], then per head S1_h [64] =
 // sum_t ds lat[t] and S0_h = sum_t ds, from which dg_remote follows linearly
