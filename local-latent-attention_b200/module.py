@@ -9,9 +9,10 @@ same forward math (models.py:307-462). The projections stay cuBLAS GEMMs;
 pooling and everything between the projections run in the custom ops of
 ``ops.py``. On CUDA the block runs as one autograd node
 (``ops.BlockFunction``) whose backward fuses the gradient accumulation and
-bias reductions around those GEMMs; with profiling on, or parameters of
-another dtype than the input, or under autocast, it runs layer by layer
-under autograd.
+bias reductions around those GEMMs (under autocast, on the input and
+weights cast to the autocast dtype); with profiling on, or parameters of
+another dtype than the input outside autocast, it runs layer by layer under
+autograd.
 
 ``build_attention(config)`` is the module switch of models.py:465-488: with
 ``config.use_triton_kernel`` set it returns this module.
@@ -145,15 +146,23 @@ class LocalLatentAttentionB200(nn.Module):
             raise NotImplementedError("LocalLatentAttentionB200 does not implement attention dropout")
         B, T, d = x.shape
         prof = self.profile_enabled and x.is_cuda
-        if (x.is_cuda and not prof and not torch.is_autocast_enabled("cuda")
-                and all(p.dtype == x.dtype for p in self.parameters())):
-            return ops.BlockFunction.apply(
-                x, self.qkv_proj.weight, self.qkv_proj.bias, self.rq_proj.weight, self.rq_proj.bias,
-                self.rkv_proj.weight, self.rkv_proj.bias, self.r_out.weight, self.r_out.bias,
-                self.gate_local.weight, self.gate_remote.weight, self.out.weight, self.out.bias,
-                (self.n_heads, self.latent_heads, self.window, self.local_block_size, self.latent_tokens,
-                 self.latent_query_block_size, self.gate_bias))
-        # per-layer path: profiling (events between the stages), mixed dtypes, autocast
+        if x.is_cuda and not prof:
+            params = (self.qkv_proj.weight, self.qkv_proj.bias, self.rq_proj.weight, self.rq_proj.bias,
+                      self.rkv_proj.weight, self.rkv_proj.bias, self.r_out.weight, self.r_out.bias,
+                      self.gate_local.weight, self.gate_remote.weight, self.out.weight, self.out.bias)
+            cfg = (self.n_heads, self.latent_heads, self.window, self.local_block_size, self.latent_tokens,
+                   self.latent_query_block_size, self.gate_bias)
+            if torch.is_autocast_enabled("cuda"):
+                # what autocast does to each linear layer, once for the block:
+                # input and weights cast to the autocast dtype (autograd casts
+                # the gradients back), the block itself run without autocast
+                dt = torch.get_autocast_dtype("cuda")
+                if dt in (torch.bfloat16, torch.float32):
+                    with torch.autocast("cuda", enabled=False):
+                        return ops.BlockFunction.apply(x.to(dt), *(p.to(dt) for p in params), cfg)
+            elif all(p.dtype == x.dtype for p in params):
+                return ops.BlockFunction.apply(x, *params, cfg)
+        # per-layer path: profiling (events between the stages), mixed dtypes
         if prof:
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
             ev[0].record()

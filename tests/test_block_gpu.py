@@ -91,3 +91,36 @@ def test_block_function_matches_per_layer_autograd(case, dtype):
     assert rel_err(fused[1], dx_ref) < TOL[dtype]
     for k in fused[2]:
         assert rel_err(fused[2][k], g_ref[k]) < TOL[dtype], k
+
+
+def test_block_function_under_autocast_matches_per_layer():
+    """fp32 parameters under bf16 autocast (the LM's training setup): the
+    fused node on cast inputs/weights against autocast over the layers."""
+    import llattn_b200
+
+    B, T, cfg = make_cfg(CASES["tokenwise"])
+    m = llattn_b200.LocalLatentAttentionB200(model_config(cfg))
+    m.load_state_dict(O.init_params(cfg, 0))
+    m = m.cuda()
+    gen = torch.Generator().manual_seed(4)
+    x = torch.randn(B, T, cfg.d_model, generator=gen).cuda()
+    gy = torch.randn(B, T, cfg.d_model, generator=gen).cuda()
+
+    def run():
+        xx = x.clone().requires_grad_(True)
+        m.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = m(xx)
+        y.float().backward(gy)
+        return y.detach(), xx.grad, {k: p.grad.detach().clone() for k, p in m.named_parameters()}
+
+    fused = run()
+    m.set_profile(True)
+    layered = run()
+    m.set_profile(False)
+    assert fused[0].dtype == layered[0].dtype == torch.bfloat16
+    assert rel_err(fused[0], layered[0]) < 1e-2
+    assert fused[1].dtype == torch.float32 and rel_err(fused[1], layered[1]) < 1e-2
+    for k in fused[2]:
+        assert fused[2][k].dtype == torch.float32
+        assert rel_err(fused[2][k], layered[2][k]) < 1e-2, k
