@@ -26,35 +26,40 @@ constexpr int kGateMaxHeads = 32;
 __host__ __device__ constexpr int gate_dg_stride(int hd, int H) { return hd + H * 65; }
 
 // dg_remote[c] = -sum_h (sum_e S1_h[e] W[h*hd + c, e] + S0_h b[h*hd + c])
-// from the reduced gate partials (dg_sum + hd). Thread (c, head half).
+// from the reduced gate partials (dg_sum + hd). Block = 16 columns; its 256
+// threads = 16 columns x 16 slices of the (head, 8-wide e chunk) pairs,
+// summed over the slices in a fixed order.
 __global__ void __launch_bounds__(256) gate_dgr_finalize_kernel(Geom g, const float* __restrict__ dg_sum,
                                                                 const bf16* __restrict__ w_rout,
                                                                 const float* __restrict__ b_rout,
                                                                 float* __restrict__ dg_remote) {
-  __shared__ float part[256];
+  __shared__ float part[16][17];
   const int HD = g.hd, H = g.H;
   const float* s1 = dg_sum + HD;
-  for (int c0 = 0; c0 < HD; c0 += 128) {
-    const int c = c0 + (threadIdx.x & 127), half = threadIdx.x >> 7;
-    float v = 0.f;
-    if (c < HD) {
-      for (int h = half; h < H; h += 2) {
-        const uint4* wrow = reinterpret_cast<const uint4*>(w_rout + ((int64_t)h * HD + c) * 64);
-        const float* sh = s1 + h * 65;
+  const int cl = threadIdx.x & 15, sl = threadIdx.x >> 4;
+  const int c = blockIdx.x * 16 + cl;
+  float v = 0.f;
+  if (c < HD) {
+    for (int it = sl; it < H * 9; it += 16) {  // per head: 8 chunks of W_h[c, :] and the bias term
+      const int h = it / 9, q = it % 9;
+      const float* sh = s1 + h * 65;
+      if (q < 8) {
+        float wv[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(w_rout + ((int64_t)h * HD + c) * 64) + q), wv);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float wv[8];
-          unpack8(__ldg(wrow + q), wv);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) v = fmaf(sh[q * 8 + k], wv[k], v);
-        }
+        for (int k = 0; k < 8; ++k) v = fmaf(sh[q * 8 + k], wv[k], v);
+      } else {
         v = fmaf(sh[64], b_rout[(int64_t)h * HD + c], v);
       }
     }
-    part[threadIdx.x] = v;
-    __syncthreads();
-    if (threadIdx.x < 128 && c < HD) dg_remote[c] = -(part[threadIdx.x] + part[threadIdx.x + 128]);
-    __syncthreads();
+  }
+  part[sl][cl] = v;
+  __syncthreads();
+  if (sl == 0 && c < HD) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) t += part[k][cl];
+    dg_remote[c] = -t;
   }
 }
 

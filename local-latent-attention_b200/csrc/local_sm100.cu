@@ -257,7 +257,7 @@ int gate_dg_floats(const Geom& g) { return gate_dg_stride(g.hd, g.H); }
 
 cudaError_t launch_gate_dgr_finalize(const Geom& g, const float* dg_sum, const void* w_rout, const float* b_rout,
                                      float* dg_remote, cudaStream_t s) {
-  gate_dgr_finalize_kernel<<<1, 256, 0, s>>>(g, dg_sum, static_cast<const bf16*>(w_rout), b_rout, dg_remote);
+  gate_dgr_finalize_kernel<<<cdiv(g.hd, 16), 256, 0, s>>>(g, dg_sum, static_cast<const bf16*>(w_rout), b_rout, dg_remote);
   return cudaGetLastError();
 }
 
