@@ -298,7 +298,6 @@ def run_ours(args):
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    _lib.profile_enable(True)
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -308,10 +307,17 @@ def run_ours(args):
     e1.record()
     torch.cuda.synchronize()
     barrier()
-    kern = _lib.profile_read()
-    _lib.profile_enable(False)
     clk = clocks.stop()
     ms = e0.elapsed_time(e1) / args.steps
+    # per-kernel times from a separate pass of the same steps with the
+    # library's event profiler on (its events cost time: not in `ms`)
+    _lib.profile_enable(True)
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    kern = _lib.profile_read()
+    _lib.profile_enable(False)
 
     # end to end through the public module: each step's x and upstream grad
     # copied in from pinned host memory and its dx copied back, pipelined
@@ -500,7 +506,6 @@ def run_lm(args):
     clocks = ClockSampler(device.index)
     clocks.start()
     time.sleep(0.3)
-    _lib.profile_enable(True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
@@ -508,10 +513,16 @@ def run_lm(args):
     e1.record()
     torch.cuda.synchronize()
     D.barrier()
-    kern = _lib.profile_read()
-    _lib.profile_enable(False)
     clk = clocks.stop()
     ms = e0.elapsed_time(e1) / args.steps
+    # per-kernel times from a separate profiled pass (the profiler's events cost time)
+    _lib.profile_enable(True)
+    for _ in range(args.steps):
+        train_step(model, opt, ids, tgt)
+    torch.cuda.synchronize()
+    D.barrier()
+    kern = _lib.profile_read()
+    _lib.profile_enable(False)
     # end to end: the step's tokens copied from pinned host memory, loss read back
     loss_h = torch.empty((), dtype=torch.float32).pin_memory()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -584,8 +595,9 @@ def run_decode(args):
     gen = torch.Generator().manual_seed(0)
     T0 = T - 1
     steps = args.steps + args.warmup
-    x = torch.randn(B, T0 + steps, cfg.d_model, generator=gen).to(device=dev, dtype=torch.bfloat16)
-    cache = m.new_decode_cache(T0 + steps)
+    # room for the timed steps and then a profiled pass of as many steps
+    x = torch.randn(B, T0 + steps + args.steps, cfg.d_model, generator=gen).to(device=dev, dtype=torch.bfloat16)
+    cache = m.new_decode_cache(T0 + steps + args.steps)
     m.prefill(x[:, :T0], cache)
     for i in range(args.warmup):
         m.decode(x[:, T0 + i:T0 + i + 1], cache)
@@ -593,17 +605,21 @@ def run_decode(args):
     clocks = ClockSampler(0)
     clocks.start()
     time.sleep(0.3)
-    _lib.profile_enable(True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(args.warmup, steps):
         y = m.decode(x[:, T0 + i:T0 + i + 1], cache)
     e1.record()
     torch.cuda.synchronize()
-    kern = _lib.profile_read()
-    _lib.profile_enable(False)
     clk = clocks.stop()
     ms = e0.elapsed_time(e1) / args.steps
+    # per-kernel times from the next steps with the profiler on (its events cost time)
+    _lib.profile_enable(True)
+    for i in range(steps, steps + args.steps):
+        m.decode(x[:, T0 + i:T0 + i + 1], cache)
+    torch.cuda.synchronize()
+    kern = _lib.profile_read()
+    _lib.profile_enable(False)
     # end to end: the new token's input from pinned host memory, its output row back
     xh = x[:, -1:].cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
