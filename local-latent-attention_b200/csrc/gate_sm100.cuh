@@ -72,7 +72,8 @@ struct GbLayout {
   static constexpr int DM = LT + G * TILE;         // per group: dmixed tile, overwritten by dR
   static constexpr int RED = DM + G * TILE;        // 4G warps x HD floats (dg_local partials)
   static constexpr int DSH = RED + 4 * G * HD * 4; // [max heads][128] gate grad ds per head and row
-  static constexpr int BAR = DSH + gate_max_heads<G>() * BM * 4;
+  static constexpr int CST = DSH + gate_max_heads<G>() * BM * 4;  // g_local, g_remote, then b_rout[h] per group
+  static constexpr int BAR = CST + (2 + G) * HD * 4;
   static constexpr int BYTES = BAR + 256;
   static constexpr int THREADS = 64 + 128 * G;
   static constexpr int TMEM_COLS = G == 2 ? 512 : 256;
@@ -243,26 +244,31 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
 #pragma unroll
       for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(d + ((c ^ (row & 7)) * 16)) = src[c];
     }
-    auto write_w = [&](int h) {  // into this group's W buffer
+    float* cgl = reinterpret_cast<float*>(smem + L::CST);  // g_local [HD], g_remote [HD]
+    float* cbh = cgl + (2 + grp) * HD;                      // this group's b_rout[h]
+    auto write_w = [&](int h) {  // into this group's W buffer, and b_rout[h]
       if (row < HD) {
         const uint4* src = reinterpret_cast<const uint4*>(w_rout + ((int64_t)h * HD + row) * 64);
         uint8_t* d = smem + L::W + grp * HD * 128 + row * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(d + ((c ^ (row & 7)) * 16)) = src[c];
+        cbh[row] = b_rout[(int64_t)h * HD + row];
       }
       fence_async_smem();
       mbar_arrive(&bars[GB_W + grp]);
     };
     float* wred = red + (warp - 2) * HD;  // lane owns columns cc*32+lane
     for (int e = lane; e < HD; e += 32) wred[e] = 0.f;
+    if (grp == 0 && row < HD) {
+      cgl[row] = gl[row];
+      cgl[HD + row] = gr[row];
+    }
     bool ok = true;
     if (grp < H) write_w(grp);
     // tile rows: 16-byte chunk c of this row sits at panel c/8, slot (c%8)^(row%8)
     auto chunk_ptr = [&](uint8_t* tile, int c) -> uint4* {
       return reinterpret_cast<uint4*>(tile + (c >> 3) * (BM * 128) + row * 128 + (((c & 7) ^ (row & 7)) * 16));
     };
-    const float4* gl4 = reinterpret_cast<const float4*>(gl);
-    const float4* gr4 = reinterpret_cast<const float4*>(gr);
     for (int h = grp; h < H; h += G) {
       const int n = h / G;  // this group's n-th head
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_R + grp], n & 1, abort, &g_fault_word));
@@ -273,9 +279,16 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
       const uint32_t tR = tmem + grp * HD + lane_off;
       uint8_t* lt = smem + L::LT + grp * L::TILE;
       uint8_t* dmt = smem + L::DM + grp * L::TILE;
-      const float4* bh4 = reinterpret_cast<const float4*>(b_rout + (int64_t)h * HD);
-      // pass 1: gate logits and dw
-      float sl = 0.f, sr = 0.f, dw = 0.f;
+      // b_rout[h] (and at the first head the gate vectors), written by the
+      // group's threads before they arrived on GB_W: that phase completing
+      // publishes them (a bounded wait, unlike a named barrier)
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_W + grp], n & 1, abort, &g_fault_word));
+      if (!ok) break;
+      const float4* bh4 = reinterpret_cast<const float4*>(cbh);
+      const float4* gl4 = reinterpret_cast<const float4*>(cgl);
+      const float4* gr4 = reinterpret_cast<const float4*>(cgl + HD);
+      // pass 1: gate logits and dw, two columns per f32x2 operation
+      uint64_t sl2 = 0, sr2 = 0, dw2 = 0;
 #pragma unroll 1
       for (int cc = 0; cc < HD / 32; ++cc) {
         uint32_t rr[32];
@@ -283,65 +296,69 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
         tmem_ld_wait();
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          float lv[8], mv[8];
-          unpack8(*chunk_ptr(lt, cc * 4 + q), lv);
-          unpack8(*chunk_ptr(dmt, cc * 4 + q), mv);
+          const uint4 lq = *chunk_ptr(lt, cc * 4 + q), mq = *chunk_ptr(dmt, cc * 4 + q);
+          const uint32_t lw[4] = {lq.x, lq.y, lq.z, lq.w}, mw[4] = {mq.x, mq.y, mq.z, mq.w};
 #pragma unroll
           for (int i4 = 0; i4 < 2; ++i4) {
             const int c4 = (cc * 32 + q * 8) / 4 + i4;
-            const float4 bb = __ldg(bh4 + c4), ga = __ldg(gl4 + c4), gb = __ldg(gr4 + c4);
-            const float bv[4] = {bb.x, bb.y, bb.z, bb.w}, gav[4] = {ga.x, ga.y, ga.z, ga.w};
-            const float gbv[4] = {gb.x, gb.y, gb.z, gb.w};
+            const float4 bb = bh4[c4], ga = gl4[c4], gb = gr4[c4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int i = i4 * 4 + k;
-              const float rv = __uint_as_float(rr[q * 8 + i]) + bv[k];
-              sl = fmaf(lv[i], gav[k], sl);
-              sr = fmaf(rv, gbv[k], sr);
-              dw = fmaf(mv[i], lv[i] - rv, dw);
+            for (int k = 0; k < 2; ++k) {
+              const int pi = i4 * 2 + k;  // column pair within the chunk
+              const uint64_t l2 = bf2_to_f2(lw[pi]), m2 = bf2_to_f2(mw[pi]);
+              const uint64_t r2 = f2_add(f2_pack(__uint_as_float(rr[q * 8 + 2 * pi]), __uint_as_float(rr[q * 8 + 2 * pi + 1])),
+                                         k ? f2_pack(bb.z, bb.w) : f2_pack(bb.x, bb.y));
+              sl2 = f2_fma(l2, k ? f2_pack(ga.z, ga.w) : f2_pack(ga.x, ga.y), sl2);
+              sr2 = f2_fma(r2, k ? f2_pack(gb.z, gb.w) : f2_pack(gb.x, gb.y), sr2);
+              dw2 = f2_fma(m2, f2_sub(l2, r2), dw2);
             }
           }
         }
       }
       if (row == 0 && h < 12) LLATTN_TRACE_K(3, 26 + h);
-      const float x = sl + g.gate_bias - sr;
+      float sla, slb, sra, srb, dwa, dwb;
+      f2_unpack(sl2, sla, slb);
+      f2_unpack(sr2, sra, srb);
+      f2_unpack(dw2, dwa, dwb);
+      const float x = (sla + slb) + g.gate_bias - (sra + srb);
       const float w = 1.f / (1.f + expf(-x));
       const float wr = 1.f / (1.f + expf(x));
-      const float ds = valid ? dw * w * wr : 0.f;
+      const float ds = valid ? (dwa + dwb) * w * wr : 0.f;
       dsh[h * BM + row] = ds;
       // pass 2: dL over local_out and dR over dmixed in the tiles (same
-      // thread, same bytes, after reading them), D = dL.L, dg_local partial
-      float dsum = 0.f;
+      // thread, same bytes, after reading them), D = dL.L, dg_local partial.
+      // Rows past T (the next sequence's rows in the 2-D load) have ds = 0
+      // and their dL / dR are clipped by the 3-D store maps.
+      const uint64_t w2 = f2_pack(w, w), wr2 = f2_pack(wr, wr), ds2 = f2_pack(ds, ds), nds2 = f2_pack(-ds, -ds);
+      uint64_t dsum2 = 0;
 #pragma unroll 1
       for (int cc = 0; cc < HD / 32; ++cc) {
         float al[32];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          float lv[8], mv[8];
           uint4* lp = chunk_ptr(lt, cc * 4 + q);
           uint4* mp = chunk_ptr(dmt, cc * 4 + q);
-          unpack8(*lp, lv);
-          unpack8(*mp, mv);
+          const uint4 lq = *lp, mq = *mp;
+          const uint32_t lw[4] = {lq.x, lq.y, lq.z, lq.w}, mw[4] = {mq.x, mq.y, mq.z, mq.w};
           uint32_t pdl[4], pdr[4];
 #pragma unroll
           for (int i4 = 0; i4 < 2; ++i4) {
             const int c4 = (cc * 32 + q * 8) / 4 + i4;
-            const float4 ga = __ldg(gl4 + c4), gb = __ldg(gr4 + c4);
-            const float gav[4] = {ga.x, ga.y, ga.z, ga.w}, gbv[4] = {gb.x, gb.y, gb.z, gb.w};
+            const float4 ga = gl4[c4], gb = gr4[c4];
 #pragma unroll
-            for (int k = 0; k < 4; k += 2) {
-              float dlv[2], drv[2];
-#pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                const int i = i4 * 4 + k + u;
-                const float a = __bfloat162float(__float2bfloat16_rn(w * mv[i] + ds * gav[k + u]));
-                dlv[u] = valid ? a : 0.f;
-                dsum = fmaf(a, lv[i], dsum);
-                drv[u] = valid ? wr * mv[i] - ds * gbv[k + u] : 0.f;
-                al[q * 8 + i] = ds * lv[i];
-              }
-              pdl[(i4 * 4 + k) / 2] = pack_bf16(dlv[0], dlv[1]);
-              pdr[(i4 * 4 + k) / 2] = pack_bf16(drv[0], drv[1]);
+            for (int k = 0; k < 2; ++k) {
+              const int pi = i4 * 2 + k;
+              const uint64_t l2 = bf2_to_f2(lw[pi]), m2 = bf2_to_f2(mw[pi]);
+              const uint64_t dl2 = f2_fma(w2, m2, f2_mul(ds2, k ? f2_pack(ga.z, ga.w) : f2_pack(ga.x, ga.y)));
+              const uint64_t dr2 = f2_fma(wr2, m2, f2_mul(nds2, k ? f2_pack(gb.z, gb.w) : f2_pack(gb.x, gb.y)));
+              float a0, a1, r0, r1;
+              f2_unpack(dl2, a0, a1);
+              f2_unpack(dr2, r0, r1);
+              pdl[pi] = pack_bf16(a0, a1);
+              pdr[pi] = pack_bf16(r0, r1);
+              // D from the stored (bf16-rounded) dL
+              dsum2 = f2_fma(bf2_to_f2(pdl[pi]), l2, dsum2);
+              f2_unpack(f2_mul(ds2, l2), al[q * 8 + 2 * pi], al[q * 8 + 2 * pi + 1]);
             }
           }
           *lp = make_uint4(pdl[0], pdl[1], pdl[2], pdl[3]);
@@ -349,6 +366,9 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
         }
         wred[cc * 32 + lane] += butterfly32(al, lane);
       }
+      float dsa, dsb;
+      f2_unpack(dsum2, dsa, dsb);
+      const float dsum = dsa + dsb;
       if (valid) delta[((int64_t)b * H + h) * g.T + t] = dsum;
       fence_async_smem();
       tc_fence_before();

@@ -353,6 +353,12 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
 }
 
 // 8 bf16 (one 16-byte chunk) -> 8 floats
+// bf16 pair (low element in the low half) -> packed f32x2 (exact: a bf16 is
+// the high half of its fp32)
+__device__ __forceinline__ uint64_t bf2_to_f2(uint32_t u) {
+  return f2_pack(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+
 __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
