@@ -70,8 +70,8 @@ int make_geom(const llattn_dims* d, Geom* g) {
 
 // Backward workspace, every region 256-byte aligned.
 struct BwdLayout {
-  size_t dl, delta, drow, dlat, dlat_tok, dg_part, dg_sum, dw_part, dgkv_part, total;
-  int gate_tok, n_gate_cta, n_split_w, n_split_lat;
+  size_t dl, delta, drow, dlat, dlat_tok, dg_part, dg_sum, dw_part, dgkv_part, drq_part, total;
+  int gate_tok, n_gate_cta, n_split_w, n_split_lat, n_kg_lat;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -85,6 +85,12 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
   L.n_split_w = std::max(1, std::min(cdiv(g.B * g.T, 64), (2 * 148) / cdiv(g.d, 128)));
   // row splits of the latent backward: (b, latent head, split) CTAs, about two per SM
   L.n_split_lat = std::max(1, std::min(cdiv(g.Tq, 64), (2 * 148) / (g.B * g.Lh)));
+  // SIMT latent backward with several 64-key tiles and too few row splits
+  // to fill the GPU: split the key tiles of each row split over CTAs
+  {
+    const int base = g.B * g.Lh * L.n_split_lat, n_kt = cdiv(g.Nc, 64);
+    L.n_kg_lat = (n_kt > 1 && base < 148) ? std::max(1, std::min(n_kt, (2 * 148) / base)) : 1;
+  }
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
   const size_t BTd = (size_t)g.B * g.T * g.d;
@@ -98,7 +104,8 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
   L.dg_part = take(sizeof(float) * std::max((size_t)L.n_gate_cta * 2 * g.hd, dg_tc));
   L.dg_sum = take(sizeof(float) * (size_t)std::max(2 * g.hd, g.hd + 65 * g.H));
   L.dw_part = take(sizeof(float) * (size_t)L.n_split_w * g.d * (g.Ld + 1));
-  L.dgkv_part = take(sizeof(float) * (size_t)L.n_split_lat * g.B * g.Nc * 2 * g.Ld);
+  L.dgkv_part = take(sizeof(float) * (size_t)L.n_split_lat * L.n_kg_lat * g.B * g.Nc * 2 * g.Ld);
+  L.drq_part = take(L.n_kg_lat > 1 ? sizeof(float) * (size_t)L.n_kg_lat * g.B * g.Tq * g.Ld : 0);
   L.total = off;
   return L;
 }
@@ -248,21 +255,23 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
                       "copy dg_remote");
   }
   if (rc) return rc;
-  prof::Scope ps(prof::LATENT_BWD, s, 2);
   // tensor-core latent backward for bf16 with head dim 32 and <= 64 chunks;
   // its row splits are 128-row tiles, at most the SIMT kernel's 64-row count
   const bool lat_tc = sizeof(T) == 2 && sm100::latent_tc_ok(g);
   const int n_split_lat = lat_tc ? std::min(sm100::latent_tc_splits(g), L.n_split_lat) : L.n_split_lat;
+  const int n_kg_lat = lat_tc || g.Nc <= 64 ? 1 : L.n_kg_lat;
+  prof::Scope ps(prof::LATENT_BWD, s, n_kg_lat > 1 ? 3 : 2);
   if (lat_tc)
     rc = check_launch(sm100::launch_latent_bwd_tc(g, a->rq, a->gkv, a->lat_lse, dlat, a->drq, dgkv_part,
                                                   n_split_lat, s),
                       "latent_bwd_sm100");
   else
     rc = check_launch(launch_latent_bwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv),
-                                           a->lat_lse, dlat, static_cast<T*>(a->drq), dgkv_part, n_split_lat, s),
+                                           a->lat_lse, dlat, static_cast<T*>(a->drq), dgkv_part, n_split_lat,
+                                           n_kg_lat, reinterpret_cast<float*>(ws + L.drq_part), s),
                       "latent_bwd");
   if (rc) return rc;
-  return check_launch(launch_latent_reduce<T>(g, dgkv_part, n_split_lat, static_cast<T*>(a->dgkv), s),
+  return check_launch(launch_latent_reduce<T>(g, dgkv_part, n_split_lat * n_kg_lat, static_cast<T*>(a->dgkv), s),
                       "latent_reduce");
 }
 

@@ -99,11 +99,14 @@ cudaError_t launch_reduce_parts(const float* part, int n_part, int64_t n, To* ou
 template <typename T>
 cudaError_t launch_latent_fwd(const Geom& g, const T* rq, const T* gkv, T* lat, float* lat_lse,
                               cudaStream_t s);
-// Latent backward: drq (direct) and per-row-split partials of dgk/dgv
-// ([n_split][B][Nc][2][Ld], every entry written).
+// Latent backward: drq and per-CTA partials of dgk/dgv ([n_split * n_kg][B][Nc][2][Ld],
+// every entry written). n_kg > 1 (more than one 64-key tile) splits the key
+// tiles of each row split over n_kg CTAs; their drq goes through drq_part
+// ([n_kg][B][Tq][Ld] fp32) and a fixed-order sum.
 template <typename T>
 cudaError_t launch_latent_bwd(const Geom& g, const T* rq, const T* gkv, const float* lat_lse,
-                              const float* dlat, T* drq, float* dgkv_part, int n_split, cudaStream_t s);
+                              const float* dlat, T* drq, float* dgkv_part, int n_split, int n_kg, float* drq_part,
+                              cudaStream_t s);
 // One decode step (decode.cu): qkv cache [B, cache_len, 3, H, hd] with rows
 // 0..T-1 filled, rq_row [B, Ld], gkv [B, Nc, 2, Ld] -> out [B, d] (row T-1).
 template <typename T>

@@ -56,7 +56,8 @@ __global__ void __launch_bounds__(256, 2) latent_bwd_kernel(Geom g, const T* __r
                                                          const T* __restrict__ gkv,
                                                          const float* __restrict__ lat_lse,
                                                          const float* __restrict__ dlat, T* __restrict__ drq,
-                                                         float* __restrict__ part, int n_split) {
+                                                         float* __restrict__ part, int n_split, int n_kg,
+                                                         float* __restrict__ drq_part) {
   using S = LatBwdSmem<L>;
   constexpr int LS = S::LS, PS = S::PS, EQ = L / 4;
   extern __shared__ float4 smem_lat4[];
@@ -64,12 +65,17 @@ __global__ void __launch_bounds__(256, 2) latent_bwd_kernel(Geom g, const T* __r
   float *s_rq = sm + S::RQ, *s_dl = sm + S::DL, *s_k = sm + S::K, *s_v = sm + S::V;
   float *s_p = sm + S::P, *s_ds = sm + S::DS, *s_lse = sm + S::LSE, *s_delta = sm + S::DELTA;
   int* s_qid = reinterpret_cast<int*>(sm + S::QID);
-  const int b = blockIdx.z, lh = blockIdx.y, split = blockIdx.x;
+  // blockIdx.x = row split * n_kg + key group: with n_kg > 1 (several key
+  // tiles, too few row splits to fill the GPU) every CTA of a row split sums
+  // delta over all keys (pass 1) but forms dS, drq and dgk/dgv only for the
+  // key tiles kt = key group (mod n_kg); its drq goes to drq_part[key group]
+  // (fp32), summed by a fixed-order reduce.
+  const int b = blockIdx.z, lh = blockIdx.y, split = blockIdx.x / n_kg, kgrp = blockIdx.x % n_kg;
   const int tid = threadIdx.x;
   const float sc2 = g.lat_scale * kLatLog2e;
   const int rg = tid >> 4, kg = tid & 15;  // S / dP block: rows 4rg + i, keys kg + 16u
   const int own = tid >> 2, eq = tid & 3;  // drq row / dgk,dgv key, and its e-quarter
-  float* my_part = part + ((int64_t)split * g.B + b) * g.Nc * 2 * g.Ld + lh * g.ldh;
+  float* my_part = part + ((int64_t)blockIdx.x * g.B + b) * g.Nc * 2 * g.Ld + lh * g.ldh;
 
   // this CTA's partial slice starts at zero (same thread mapping as the adds)
   if (!ONE)
@@ -201,8 +207,8 @@ __global__ void __launch_bounds__(256, 2) latent_bwd_kernel(Geom g, const T* __r
     float aq[EQ];
 #pragma unroll
     for (int u = 0; u < EQ; ++u) aq[u] = 0.f;
-    // pass 2: dS; drq; dgk, dgv
-    for (int kt = 0; kt < n_kt; ++kt) {
+    // pass 2: dS; drq; dgk, dgv (this CTA's key tiles)
+    for (int kt = kgrp; kt < n_kt; kt += n_kg) {
       const int j0 = kt * kLatKeys;
       __syncthreads();
       if (!ONE && n_kt > 1) {  // one tile: its P, dP are still in s_p / s_ds
@@ -281,7 +287,13 @@ __global__ void __launch_bounds__(256, 2) latent_bwd_kernel(Geom g, const T* __r
 #pragma unroll
       for (int u = 0; u < EQ; ++u) {
         const int e = eq * EQ + u;
-        if (e < g.ldh) drq[((int64_t)(b * g.Tq + r) * g.Lh + lh) * g.ldh + e] = from_f<T>(aq[u] * g.lat_scale);
+        if (e < g.ldh) {
+          const int64_t o = ((int64_t)(b * g.Tq + r) * g.Lh + lh) * g.ldh + e;
+          if (n_kg > 1)
+            drq_part[(int64_t)kgrp * g.B * g.Tq * g.Ld + o] = aq[u] * g.lat_scale;
+          else
+            drq[o] = from_f<T>(aq[u] * g.lat_scale);
+        }
       }
     }
   }
@@ -481,14 +493,17 @@ cudaError_t latent_fwd_l(const Geom& g, const T* rq, const T* gkv, T* lat, float
 
 template <typename T, int L>
 cudaError_t latent_bwd_l(const Geom& g, const T* rq, const T* gkv, const float* lse, const float* dlat, T* drq,
-                         float* part, int n_split, cudaStream_t s) {
+                         float* part, int n_split, int n_kg, float* drq_part, cudaStream_t s) {
   const int sm = (int)sizeof(float) * LatBwdSmem<L>::FLOATS;
   auto k = g.Nc <= kLatKeys ? latent_bwd_kernel<T, L, true> : latent_bwd_kernel<T, L, false>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   if (e != cudaSuccess) return e;
-  dim3 grid(n_split, g.Lh, g.B);
-  k<<<grid, 256, sm, s>>>(g, rq, gkv, lse, dlat, drq, part, n_split);
-  return cudaGetLastError();
+  if (g.Nc <= kLatKeys) n_kg = 1;  // one key tile: nothing to split
+  dim3 grid(n_split * n_kg, g.Lh, g.B);
+  k<<<grid, 256, sm, s>>>(g, rq, gkv, lse, dlat, drq, part, n_split, n_kg, drq_part);
+  cudaError_t e2 = cudaGetLastError();
+  if (e2 != cudaSuccess || n_kg == 1) return e2;
+  return launch_reduce_parts<T>(drq_part, n_kg, (int64_t)g.B * g.Tq * g.Ld, drq, s);
 }
 
 }  // namespace
@@ -504,11 +519,11 @@ cudaError_t launch_latent_fwd(const Geom& g, const T* rq, const T* gkv, T* lat, 
 
 template <typename T>
 cudaError_t launch_latent_bwd(const Geom& g, const T* rq, const T* gkv, const float* lat_lse, const float* dlat,
-                              T* drq, float* dgkv_part, int n_split, cudaStream_t s) {
-  if (g.ldh <= 8) return latent_bwd_l<T, 8>(g, rq, gkv, lat_lse, dlat, drq, dgkv_part, n_split, s);
-  if (g.ldh <= 16) return latent_bwd_l<T, 16>(g, rq, gkv, lat_lse, dlat, drq, dgkv_part, n_split, s);
-  if (g.ldh <= 32) return latent_bwd_l<T, 32>(g, rq, gkv, lat_lse, dlat, drq, dgkv_part, n_split, s);
-  return latent_bwd_l<T, 64>(g, rq, gkv, lat_lse, dlat, drq, dgkv_part, n_split, s);
+                              T* drq, float* dgkv_part, int n_split, int n_kg, float* drq_part, cudaStream_t s) {
+  if (g.ldh <= 8) return latent_bwd_l<T, 8>(g, rq, gkv, lat_lse, dlat, drq, dgkv_part, n_split, n_kg, drq_part, s);
+  if (g.ldh <= 16) return latent_bwd_l<T, 16>(g, rq, gkv, lat_lse, dlat, drq, dgkv_part, n_split, n_kg, drq_part, s);
+  if (g.ldh <= 32) return latent_bwd_l<T, 32>(g, rq, gkv, lat_lse, dlat, drq, dgkv_part, n_split, n_kg, drq_part, s);
+  return latent_bwd_l<T, 64>(g, rq, gkv, lat_lse, dlat, drq, dgkv_part, n_split, n_kg, drq_part, s);
 }
 
 template <typename T>
@@ -536,9 +551,9 @@ template cudaError_t launch_reduce_parts<bf16>(const float*, int, int64_t, bf16*
 template cudaError_t launch_latent_fwd<float>(const Geom&, const float*, const float*, float*, float*, cudaStream_t);
 template cudaError_t launch_latent_fwd<bf16>(const Geom&, const bf16*, const bf16*, bf16*, float*, cudaStream_t);
 template cudaError_t launch_latent_bwd<float>(const Geom&, const float*, const float*, const float*, const float*,
-                                              float*, float*, int, cudaStream_t);
+                                              float*, float*, int, int, float*, cudaStream_t);
 template cudaError_t launch_latent_bwd<bf16>(const Geom&, const bf16*, const bf16*, const float*, const float*,
-                                             bf16*, float*, int, cudaStream_t);
+                                             bf16*, float*, int, int, float*, cudaStream_t);
 template cudaError_t launch_latent_reduce<float>(const Geom&, const float*, int, float*, cudaStream_t);
 template cudaError_t launch_latent_reduce<bf16>(const Geom&, const float*, int, bf16*, cudaStream_t);
 
