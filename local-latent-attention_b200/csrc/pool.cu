@@ -174,6 +174,9 @@ constexpr int vec_width() { return 16 / (int)sizeof(T); }
 
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
+// threads per block for n column groups: up to 256, no idle warps when n < 256
+inline int col_threads(int64_t n) { return n >= 256 ? 256 : (int)((n + 31) / 32 * 32); }
+
 }  // namespace
 
 template <typename T>
@@ -183,11 +186,13 @@ cudaError_t launch_pool_fwd(const Geom& g, int mode, const T* x, T* out, int64_t
   const int size = chunks ? g.cs : g.qbs;
   constexpr int V = vec_width<T>();
   if (d % V == 0 && aligned16(x) && aligned16(out)) {
-    dim3 grid((unsigned)cdiv((int)(d / V), 256), rows, g.B);
-    pool_fwd_kernel<T, V><<<grid, 256, 0, s>>>(x, out, g.T, d, rows, size, chunks ? 0 : 1);
+    const int nt = col_threads(d / V);
+    dim3 grid((unsigned)cdiv((int)(d / V), nt), rows, g.B);
+    pool_fwd_kernel<T, V><<<grid, nt, 0, s>>>(x, out, g.T, d, rows, size, chunks ? 0 : 1);
   } else {
-    dim3 grid((unsigned)cdiv((int)d, 256), rows, g.B);
-    pool_fwd_kernel<T, 1><<<grid, 256, 0, s>>>(x, out, g.T, d, rows, size, chunks ? 0 : 1);
+    const int nt = col_threads(d);
+    dim3 grid((unsigned)cdiv((int)d, nt), rows, g.B);
+    pool_fwd_kernel<T, 1><<<grid, nt, 0, s>>>(x, out, g.T, d, rows, size, chunks ? 0 : 1);
   }
   return cudaGetLastError();
 }
@@ -200,11 +205,13 @@ cudaError_t launch_pool_bwd(const Geom& g, int mode, const T* dout, T* dx, int64
   const int size = chunks ? g.cs : g.qbs;
   constexpr int V = vec_width<T>();
   if (d % V == 0 && aligned16(dout) && aligned16(dx)) {
-    dim3 grid((unsigned)cdiv((int)(d / V), 256), g.T, g.B);
-    pool_bwd_kernel<T, V><<<grid, 256, 0, s>>>(dout, dx, g.T, d, rows, size, chunks ? 0 : 1, accumulate);
+    const int nt = col_threads(d / V);
+    dim3 grid((unsigned)cdiv((int)(d / V), nt), g.T, g.B);
+    pool_bwd_kernel<T, V><<<grid, nt, 0, s>>>(dout, dx, g.T, d, rows, size, chunks ? 0 : 1, accumulate);
   } else {
-    dim3 grid((unsigned)cdiv((int)d, 256), g.T, g.B);
-    pool_bwd_kernel<T, 1><<<grid, 256, 0, s>>>(dout, dx, g.T, d, rows, size, chunks ? 0 : 1, accumulate);
+    const int nt = col_threads(d);
+    dim3 grid((unsigned)cdiv((int)d, nt), g.T, g.B);
+    pool_bwd_kernel<T, 1><<<grid, nt, 0, s>>>(dout, dx, g.T, d, rows, size, chunks ? 0 : 1, accumulate);
   }
   return cudaGetLastError();
 }
