@@ -5,8 +5,11 @@
  *
  * Plain C: device pointers, sizes and a stream handle. No torch types.
  * The caller owns every buffer (outputs, saved tensors and the backward
- * workspace); the library never allocates or frees device memory and keeps
- * no device state between calls. Every entry point returns 0 on success and
+ * workspace); the library never allocates or frees device memory on its
+ * launch paths. Its only global state: the device fault word of the
+ * tensor-core kernels and its host-mapped mirror (one pinned 64-byte host
+ * allocation per process, made by the first launching call), and the fixed
+ * scratch array of llattn_bwd_noalloc. Every entry point returns 0 on success and
  * a nonzero llattn_status otherwise; llattn_last_error() then describes the
  * failure (thread-local string). Argument errors are detected on the host
  * before any launch.
@@ -55,7 +58,7 @@ typedef enum llattn_status {
   LLATTN_ERR_ALIGN = 2,     /* pointer not aligned as the kernel requires   */
   LLATTN_ERR_LAUNCH = 3,    /* cudaLaunch / cudaFuncSetAttribute failure    */
   LLATTN_ERR_WORKSPACE = 4, /* workspace too small                          */
-  LLATTN_ERR_DEVICE = 5     /* device-side check failed (debug builds)      */
+  LLATTN_ERR_DEVICE = 5     /* a kernel recorded a device-side fault        */
 } llattn_status;
 
 /* Block hyper-parameters: the ModelConfig fields the block reads
@@ -186,12 +189,22 @@ typedef enum llattn_pool_mode {
 LLATTN_API int llattn_version(void);
 LLATTN_API const char* llattn_last_error(void);
 
-/* Device fault word of the current device (0 = none): set by a tensor-core
- * kernel whose bounded wait on a barrier ran out, after which that kernel
- * abandoned its work and returned. Synchronises with the device; for tests
- * and diagnostics, not for the hot path. reset != 0 clears it. No
- * counterpart in the reference (its Triton kernels have no waits). */
+/* Fault bits (0 = none): set by a tensor-core kernel whose bounded wait on
+ * a barrier ran out, after which that kernel abandoned its work and returned
+ * (and every kernel launched after it on the device exits at once). The
+ * kernels also set a host-mapped copy of the word, which llattn_fwd,
+ * llattn_bwd, llattn_bwd_noalloc and llattn_decode test before launching:
+ * once it is set they return LLATTN_ERR_DEVICE (like an asynchronous CUDA
+ * error, the fault shows at the next call) until it is cleared. This
+ * function returns the device word of the current device or'd with the host
+ * copy; it synchronises with the device, so it is for tests and
+ * diagnostics, not for the hot path. reset != 0 clears both. No counterpart
+ * in the reference (its Triton kernels have no waits). */
 LLATTN_API unsigned llattn_fault_status(int reset);
+/* Sets bits in the host-mapped fault word without touching the GPU: the
+ * host-side fault injection with which tests check that a recorded fault
+ * makes the launching entry points fail. No counterpart in the reference. */
+LLATTN_API int llattn_fault_inject_host(unsigned bits);
 
 /* Fills *out from *dims. Returns LLATTN_ERR_ARG for inconsistent dims. */
 LLATTN_API int llattn_geometry(const llattn_dims* dims, llattn_geom* out);
@@ -237,8 +250,14 @@ LLATTN_API int llattn_bwd(const llattn_bwd_args* args, void* stream);
  * llattn_bwd_workspace_bytes exceeds that are rejected with
  * LLATTN_ERR_WORKSPACE (one 8192-token sequence of d_model 256 in bf16 needs
  * 21 MiB and fits; a 16 x 2048-token batch of d_model 1536 needs 307 MiB and
- * does not). The first call on each device looks up the array's device address (with that device current), so make that first call before
- * any stream capture. All calls on a device share the one array: calls that
+ * does not). The first call on each device looks up the array's device
+ * address (with that device current) and caches it, so make that first call
+ * before any stream capture; the cached address does not survive
+ * cudaDeviceReset. The stream must belong to the current device (else
+ * LLATTN_ERR_ARG). The array is reserved when the library's device code
+ * first loads on a device (at context creation under
+ * CUDA_MODULE_LOADING=EAGER): a device without 32 MiB free then yields
+ * LLATTN_ERR_WORKSPACE. All calls on a device share the one array: calls that
  * can overlap on the GPU (different streams, or other threads) race and
  * corrupt each other's results — serialise them. Nothing in it needs clearing
  * between calls; it allocates and frees nothing. */

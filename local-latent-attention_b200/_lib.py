@@ -20,7 +20,7 @@ EXPORTED = (
     "llattn_version", "llattn_last_error", "llattn_fault_status", "llattn_geometry", "llattn_bwd_workspace_bytes",
     "llattn_pool_fwd", "llattn_pool_bwd", "llattn_fwd", "llattn_bwd", "llattn_bwd_noalloc", "llattn_decode",
     "llattn_profile_enable", "llattn_profile_read", "llattn_profile_name", "llattn_colsum_workspace_bytes",
-    "llattn_colsum",
+    "llattn_colsum", "llattn_fault_inject_host",
 )
 
 
@@ -81,6 +81,8 @@ def lib() -> ctypes.CDLL:
         L.llattn_last_error.restype = ctypes.c_char_p
         L.llattn_fault_status.argtypes = [ctypes.c_int]
         L.llattn_fault_status.restype = ctypes.c_uint
+        L.llattn_fault_inject_host.argtypes = [ctypes.c_uint]
+        L.llattn_fault_inject_host.restype = ctypes.c_int
         L.llattn_geometry.argtypes = [ctypes.POINTER(Dims), ctypes.POINTER(Geom)]
         L.llattn_geometry.restype = ctypes.c_int
         L.llattn_bwd_workspace_bytes.argtypes = [ctypes.POINTER(Dims)]

@@ -1,6 +1,8 @@
 // C ABI of libllattn (declared in include/llattn.h): host-side validation,
-// geometry, backward workspace layout and kernel dispatch. No allocation, no
-// host synchronisation, no global device state.
+// geometry, backward workspace layout and kernel dispatch. No device
+// allocation and no host synchronisation on the launch paths. Global state:
+// the device fault word of the tensor-core kernels, its host-mapped mirror
+// (one pinned word per process) and the scratch array of llattn_bwd_noalloc.
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -65,6 +67,7 @@ int make_geom(const llattn_dims* d, Geom* g) {
   g->gate_bias = d->gate_bias;
   g->scale = 1.0f / sqrtf((float)g->hd);
   g->lat_scale = 1.0f / sqrtf((float)g->ldh);
+  g->fault_host = nullptr;
   return LLATTN_OK;
 }
 
@@ -111,6 +114,49 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
 }
 
 bool al(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+// Host-mapped fault word: a tensor-core kernel whose bounded wait runs out
+// sets it (besides the device word that stops the other CTAs), and every
+// launching entry point tests it first, without synchronising. A fault thus
+// surfaces as LLATTN_ERR_DEVICE at the next call, the way CUDA reports an
+// asynchronous error, instead of later calls silently returning the outputs
+// of kernels that exit at once on the sticky device word.
+std::mutex g_fault_mu;
+volatile unsigned* g_fault_host = nullptr;
+
+volatile unsigned* fault_host_word() {
+  std::lock_guard<std::mutex> lk(g_fault_mu);
+  if (!g_fault_host) {
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, 64, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    *static_cast<volatile unsigned*>(p) = 0u;
+    g_fault_host = static_cast<volatile unsigned*>(p);
+  }
+  return g_fault_host;
+}
+
+// Before a launch: attach the mirror to the geometry and refuse to run once
+// a fault has been recorded (cleared by llattn_fault_status(1)).
+int fault_gate(Geom* g) {
+  volatile unsigned* w = fault_host_word();
+  if (!w) return fail(LLATTN_ERR_LAUNCH, "cannot allocate the host-mapped fault word");
+  const unsigned bits = *w;
+  if (bits)
+    return fail(LLATTN_ERR_DEVICE,
+                "an earlier tensor-core launch gave up on a barrier wait (fault bits 0x%x); its outputs and "
+                "those of the launches queued after it are invalid. llattn_fault_status(1) clears the fault",
+                bits);
+  void* dp = nullptr;
+  if (cudaHostGetDevicePointer(&dp, const_cast<unsigned*>(w), 0) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LLATTN_ERR_LAUNCH, "the fault word is not mapped for the current device");
+  }
+  g->fault_host = static_cast<volatile unsigned*>(dp);
+  return LLATTN_OK;
+}
 
 template <typename T>
 int run_fwd(const Geom& g, const llattn_fwd_args* a, cudaStream_t s) {
@@ -284,7 +330,22 @@ extern "C" {
 
 int llattn_version(void) { return LLATTN_VERSION; }
 
-unsigned llattn_fault_status(int reset) { return sm100::read_fault_word(reset != 0); }
+unsigned llattn_fault_status(int reset) {
+  unsigned v = sm100::read_fault_word(reset != 0);
+  volatile unsigned* w = fault_host_word();
+  if (w) {
+    v |= *w;
+    if (reset) *w = 0u;
+  }
+  return v;
+}
+
+int llattn_fault_inject_host(unsigned bits) {
+  volatile unsigned* w = fault_host_word();
+  if (!w) return fail(LLATTN_ERR_LAUNCH, "cannot allocate the host-mapped fault word");
+  *w |= bits;
+  return LLATTN_OK;
+}
 
 const char* llattn_last_error(void) { return g_err; }
 
@@ -364,6 +425,7 @@ int llattn_fwd(const llattn_fwd_args* a, void* stream) {
   if (!a->qkv || !a->rq || !a->gkv || !a->w_rout || !a->b_rout || !a->g_local || !a->g_remote || !a->mixed ||
       !a->local_out || !a->lse || !a->lat || !a->lat_lse)
     return fail(LLATTN_ERR_ARG, "llattn_fwd: NULL pointer in args");
+  if ((rc = fault_gate(&g))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a->dims.dtype == LLATTN_BF16) return run_fwd<bf16>(g, a, s);
   return run_fwd<float>(g, a, s);
@@ -380,6 +442,7 @@ int llattn_decode(const llattn_decode_args* a, void* stream) {
   if (a->cache_len < a->dims.seq_len)
     return fail(LLATTN_ERR_ARG, "llattn_decode: cache_len %lld < seq_len %d", (long long)a->cache_len,
                 a->dims.seq_len);
+  if ((rc = fault_gate(&g))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   prof::Scope ps(prof::DECODE, s);
   if (a->dims.dtype == LLATTN_BF16)
@@ -407,6 +470,7 @@ int llattn_bwd(const llattn_bwd_args* a, void* stream) {
     return fail(LLATTN_ERR_WORKSPACE, "llattn_bwd: workspace of %zu bytes needed, %zu given", need,
                 a->workspace_bytes);
   if (!al(a->workspace, 256)) return fail(LLATTN_ERR_ALIGN, "llattn_bwd: workspace must be 256-byte aligned");
+  if ((rc = fault_gate(&g))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a->dims.dtype == LLATTN_BF16) return run_bwd<bf16>(g, a, s);
   return run_bwd<float>(g, a, s);
@@ -435,6 +499,19 @@ int llattn_bwd_noalloc(const llattn_bwd_args* a, void* stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return fail(LLATTN_ERR_LAUNCH, "llattn_bwd_noalloc: no usable current device");
+  if (stream) {
+    // the scratch address is the current device's copy of the array: a
+    // stream of another device would run the kernels on that device with
+    // a pointer into this one's memory
+    int sdev = -1;
+    if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(LLATTN_ERR_ARG, "llattn_bwd_noalloc: cannot query the stream's device");
+    }
+    if (sdev != dev)
+      return fail(LLATTN_ERR_ARG, "llattn_bwd_noalloc: stream belongs to device %d, current device is %d", sdev,
+                  dev);
+  }
   void* ptr = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
@@ -444,6 +521,16 @@ int llattn_bwd_noalloc(const llattn_bwd_args* a, void* stream) {
       cudaError_t e = cudaGetSymbolAddress(&g_noalloc_ptr[dev], g_bwd_noalloc_scratch);
       if (e != cudaSuccess) {
         g_noalloc_ptr[dev] = nullptr;
+        cudaGetLastError();
+        // the array is reserved when the library's module loads on the
+        // device (first use under lazy loading): that load fails when the
+        // device has no 32 MiB left, e.g. under a caching allocator
+        if (e == cudaErrorMemoryAllocation)
+          return fail(LLATTN_ERR_WORKSPACE,
+                      "llattn_bwd_noalloc: device %d has no room for the library's fixed %u-byte scratch array "
+                      "(reserved when the library first loads on the device); free device memory first or use "
+                      "llattn_bwd with a caller-provided workspace",
+                      dev, (unsigned)LLATTN_BWD_NOALLOC_SCRATCH_BYTES);
         return fail(LLATTN_ERR_LAUNCH, "llattn_bwd_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
       }
     }

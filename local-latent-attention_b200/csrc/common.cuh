@@ -23,6 +23,9 @@ struct Geom {
   float gate_bias;
   float scale;      // 1/sqrt(hd)
   float lat_scale;  // 1/sqrt(ldh)
+  // host-mapped fault word (pinned, zero-copy): set by a kernel that gave up
+  // on a bounded wait; nullptr disables the mirror
+  volatile unsigned* fault_host;
 };
 
 __host__ __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }

@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
       for (int h = H - G < 0 ? 0 : H - G; ok && h < H; ++h) ok = store_head(h);
       tma_store_wait_read();
       if (!ok) {
-        raise_fault(kFaultProducer, abort);
+        raise_fault(g, kFaultProducer, abort);
         volatile int none = 0;
         volatile unsigned gnone = 0;
         for (int h = issued - G < 0 ? 0 : issued - G; h < issued; ++h)
@@ -229,7 +229,7 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
         mma_commit(&bars[GB_DL + s]);
         if (h + G < H && !(ok = issue_r(h + G))) break;
       }
-      if (!ok) raise_fault(kFaultMma, abort);
+      if (!ok) raise_fault(g, kFaultMma, abort);
     }
   } else if (warp >= 2) {
     const int grp = (warp - 2) >> 2;
@@ -382,12 +382,12 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
         write_w(h + G);
       }
     }
-    if (!ok) raise_fault(kFaultSoftmax, abort);
+    if (!ok) raise_fault(g, kFaultSoftmax, abort);
     if (grp == 0) {
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars[GB_DL + ((H - 1) % G)], ((H - 1) / G) & 1, abort,
                                                      &g_fault_word));
       if (!ok) {
-        raise_fault(kFaultEpilogue, abort);
+        raise_fault(g, kFaultEpilogue, abort);
       } else {
         tc_fence_after();
 #pragma unroll
@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(192, 2)
       for (int i = 0; i < nch; ++i) {
         const int s = i % DW_ST;
         if (i >= DW_ST && !mbar_wait(&bars[DW_E + s], ((i / DW_ST) - 1) & 1, abort, &g_fault_word)) {
-          raise_fault(kFaultProducer, abort);
+          raise_fault(g, kFaultProducer, abort);
           break;
         }
         mbar_expect_tx(&bars[DW_FA + s], 16384 + (lat_tma ? 8192 : 0));
@@ -565,7 +565,7 @@ __global__ void __launch_bounds__(192, 2)
         mma_commit(&bars[DW_E + s]);
       }
       mma_commit(&bars[DW_DONE]);
-      if (!ok) raise_fault(kFaultMma, abort);
+      if (!ok) raise_fault(g, kFaultMma, abort);
     }
   } else {
     const int tid = threadIdx.x - 64;  // 0..127
@@ -594,11 +594,11 @@ __global__ void __launch_bounds__(192, 2)
         fence_async_smem();
         mbar_arrive(&bars[DW_FB + s]);
       }
-      if (!ok) raise_fault(kFaultSoftmax, abort);
+      if (!ok) raise_fault(g, kFaultSoftmax, abort);
     }
     if (ok && nch > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars[DW_DONE], 0, abort, &g_fault_word));
     if (!ok) {
-      raise_fault(kFaultEpilogue, abort);
+      raise_fault(g, kFaultEpilogue, abort);
     } else {
       tc_fence_after();
       const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;

@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(160, 2)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + LT_NB);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   if (smem_u32(smem) & 1023u) {
-    if (threadIdx.x == 0) atomicOr(&g_fault_word, kFaultEpilogue);
+    if (threadIdx.x == 0) raise_fault(g, kFaultEpilogue, nullptr);
     return;
   }
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, tid = threadIdx.x;
@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(160, 2)
           mma_bf16(tD2, desc_add(dx, kk * 2048), desc_add(dbp, kk * 2048), id2, (n > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&bars[LT_T]);
       }
-      if (!ok) raise_fault(kFaultMma, abort);
+      if (!ok) raise_fault(g, kFaultMma, abort);
     }
   } else {
     const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(160, 2)
                                         __uint_as_float(rq32[8 * c + 7]) * g.lat_scale));
       }
     }
-    if (!ok) raise_fault(kFaultSoftmax, abort);
+    if (!ok) raise_fault(g, kFaultSoftmax, abort);
     // this CTA's dgk / dgv partial: warp 0 holds D2 rows e (dgk^T), warp 1
     // rows 32 + e (dgv^T); partial layout [split][b][key][2][Ld]
     if (warp < 2) {
@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(160)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + LT_NB);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   if (smem_u32(smem) & 1023u) {
-    if (threadIdx.x == 0) atomicOr(&g_fault_word, kFaultEpilogue);
+    if (threadIdx.x == 0) raise_fault(g, kFaultEpilogue, nullptr);
     return;
   }
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, tid = threadIdx.x;
@@ -393,7 +393,7 @@ __global__ void __launch_bounds__(160)
         for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(tO, tS + kk * 8, desc_add(dkv, kk * 2048), idO, kk > 0);
         mma_commit(&bars[LT_T]);
       }
-      if (!ok) raise_fault(kFaultMma, abort);
+      if (!ok) raise_fault(g, kFaultMma, abort);
     }
   } else {
     const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(160)
         lat_lse[(int64_t)(b * g.Lh + lh) * g.Tq + r] = qid > 0 ? (mb + log2f(l)) * kLn2 : INFINITY;
       }
     }
-    if (!ok) raise_fault(kFaultSoftmax, abort);
+    if (!ok) raise_fault(g, kFaultSoftmax, abort);
   }
   tc_fence_before();
   __syncthreads();

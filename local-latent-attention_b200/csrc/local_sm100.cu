@@ -60,9 +60,17 @@ enum Fault : unsigned {
   kFaultProducer = 1u, kFaultMma = 2u, kFaultSoftmax = 4u, kFaultEpilogue = 8u,
 };
 
-__device__ __forceinline__ void raise_fault(unsigned bit, volatile int* abort) {
+// Records the fault in the device word (which stops every other wait at
+// once), in the host-mapped word the entry points test before each launch
+// (so the op fails loudly instead of returning abandoned outputs), and in
+// this CTA's abort flag.
+__device__ __forceinline__ void raise_fault(const Geom& g, unsigned bit, volatile int* abort) {
   atomicOr(&g_fault_word, bit);
-  *abort = 1;
+  if (g.fault_host) {
+    *g.fault_host |= bit;
+    __threadfence_system();
+  }
+  if (abort) *abort = 1;
 }
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {

@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(320, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + DP_NB);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   if (smem_u32(smem) & 1023u) {  // the swizzled layouts need 1024-byte alignment
-    if (threadIdx.x == 0) atomicOr(&g_fault_word, kFaultEpilogue);
+    if (threadIdx.x == 0) raise_fault(g, kFaultEpilogue, nullptr);
     return;
   }
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       if (!ok) {
-        raise_fault(kFaultProducer, abort);
+        raise_fault(g, kFaultProducer, abort);
         // let the copies already issued land before the CTA can exit
         volatile int none = 0;
         volatile unsigned gnone = 0;
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(320, 1)
         cur = nx;
         ++jj;
       }
-      if (!ok) raise_fault(kFaultMma, abort);
+      if (!ok) raise_fault(g, kFaultMma, abort);
     }
   } else {
     // warps 2..9: row = TMEM lane = query; warps w and w+4 share a lane
@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       ok = __all_sync(0xffffffffu, ok);
     }
-    if (!ok) raise_fault(kFaultSoftmax, abort);
+    if (!ok) raise_fault(g, kFaultSoftmax, abort);
   }
   tc_fence_before();
   __syncthreads();
@@ -438,7 +438,7 @@ __global__ void __launch_bounds__(320, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + KV_NB);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   if (smem_u32(smem) & 1023u) {  // the swizzled layouts need 1024-byte alignment
-    if (threadIdx.x == 0) atomicOr(&g_fault_word, kFaultEpilogue);
+    if (threadIdx.x == 0) raise_fault(g, kFaultEpilogue, nullptr);
     return;
   }
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -507,7 +507,7 @@ __global__ void __launch_bounds__(320, 1)
         q += t.nq;
       }
       if (!ok) {
-        raise_fault(kFaultProducer, abort);
+        raise_fault(g, kFaultProducer, abort);
         // let the copies already issued land before the CTA can exit
         volatile int none = 0;
         volatile unsigned gnone = 0;
@@ -580,7 +580,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         q += t.nq;
       }
-      if (!ok) raise_fault(kFaultMma, abort);
+      if (!ok) raise_fault(g, kFaultMma, abort);
     }
   } else {
     // warps 2..9: row = TMEM lane = key; warps w and w+4 split the columns
@@ -727,7 +727,7 @@ __global__ void __launch_bounds__(320, 1)
       if (!ok) break;
       q += t.nq;
     }
-    if (!ok) raise_fault(kFaultSoftmax, abort);
+    if (!ok) raise_fault(g, kFaultSoftmax, abort);
   }
   tc_fence_before();
   __syncthreads();

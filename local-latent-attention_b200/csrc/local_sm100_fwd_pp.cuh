@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + PP_NB);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   if (smem_u32(smem) & 1023u) {
-    if (threadIdx.x == 0) atomicOr(&g_fault_word, kFaultEpilogue);
+    if (threadIdx.x == 0) raise_fault(g, kFaultEpilogue, nullptr);
     return;
   }
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
       };
       for (int j = 0; j <= nk; ++j) {
         if ((j < nk && !load_kv(j, true)) || (j >= 1 && !load_kv(j - 1, false))) {
-          raise_fault(kFaultProducer, abort);
+          raise_fault(g, kFaultProducer, abort);
           break;
         }
       }
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
         if (mbar_wait(&bars[PP_SD], 0, abort, &g_fault_word))
           load_remote();
         else
-          raise_fault(kFaultProducer, abort);
+          raise_fault(g, kFaultProducer, abort);
       }
       if (*abort) {
         // let the copies already issued land before the CTA can exit
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
           if (*abort || g_fault_word || globaltimer_ns() - t_last > 1000000000ull) ok = false;
         }
       }
-      if (!ok) raise_fault(kFaultMma, abort);
+      if (!ok) raise_fault(g, kFaultMma, abort);
     }
   } else {
     const int grp = (warp - 2) >> 2;  // 0: tile A, 1: tile B
@@ -461,7 +461,7 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
         mbar_arrive(&bars[PP_P + 2 * grp + (i & 1)]);
         if (row == 0) LLATTN_TRACE_K(1, 16 + grp * 24 + i);
       }
-      if (!ok) raise_fault(kFaultSoftmax, abort);
+      if (!ok) raise_fault(g, kFaultSoftmax, abort);
       if (ok && fuse && L::X_OVER_Q) {
         ok = __all_sync(0xffffffffu, mbar_wait(&bars[PP_SD], 0, abort, &g_fault_word));
         if (ok) write_lat_rows();
@@ -476,7 +476,7 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
       }
       if (row == 0) LLATTN_TRACE_K(1, 52 + 2 * grp);
       if (!ok) {
-        raise_fault(kFaultEpilogue, abort);
+        raise_fault(g, kFaultEpilogue, abort);
       } else {
         tc_fence_after();
         const int nk_here = n_mine;
@@ -558,7 +558,7 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
               LLATTN_TRACE_K(1, 62 + grp);
               tma_store_wait_read();
             } else {
-              raise_fault(kFaultEpilogue, abort);
+              raise_fault(g, kFaultEpilogue, abort);
             }
           }
         } else {

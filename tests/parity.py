@@ -1,9 +1,10 @@
 """Shared helpers of the parity tests: seeded inputs, the oracle run (CPU) and
 the B200 run of the same block, and the error metric.
 
-Error metric, per tensor: max|a - b| / max|b| (relative to the reference's
-largest magnitude). Tolerances (from the parity target): 1e-4 for float32
-activations, 2e-2 for bfloat16.
+Error metrics, per tensor, both held to the same tolerance: max|a - b| /
+max|b| (relative to the reference's largest magnitude) and the
+Frobenius-relative ||a - b||_F / ||b||_F. Tolerances (from the parity
+target): 1e-4 for float32 activations, 2e-2 for bfloat16.
 """
 
 from __future__ import annotations
@@ -20,6 +21,12 @@ def rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
     b = b.detach().double().cpu()
     denom = b.abs().max().item()
     return (a - b).abs().max().item() / max(denom, 1e-30)
+
+
+def frob_err(a: torch.Tensor, b: torch.Tensor) -> float:
+    a = a.detach().double().cpu()
+    b = b.detach().double().cpu()
+    return (a - b).norm().item() / max(b.norm().item(), 1e-30)
 
 
 def make_cfg(dims: dict) -> tuple[int, int, O.BlockCfg]:
@@ -68,9 +75,11 @@ def b200_block(params: dict, x: torch.Tensor, g: torch.Tensor, cfg, gate_bias=0.
 def compare(got, ref, tol: float, label: str = "") -> dict:
     y, dx, grads = got
     ry, rdx, rgrads = ref
-    errs = {"y": rel_err(y, ry), "dx": rel_err(dx, rdx)}
+    errs = {"y": rel_err(y, ry), "dx": rel_err(dx, rdx),
+            "y/frob": frob_err(y, ry), "dx/frob": frob_err(dx, rdx)}
     for k in rgrads:
         errs[k] = rel_err(grads[k], rgrads[k])
+        errs[k + "/frob"] = frob_err(grads[k], rgrads[k])
     bad = {k: v for k, v in errs.items() if not (v <= tol)}
     assert not bad, f"{label}: relative errors above {tol}: {bad}"
     return errs

@@ -136,3 +136,26 @@ def test_local_bwd_tc_matches_simt(case):
                 assert rel_err(x, y) < 2e-2, (sname, rel_err(x, y))
         else:
             assert rel_err(a.float(), b_.float()) < 2e-2, (name, rel_err(a.float(), b_.float()))
+
+
+def test_recorded_fault_fails_later_launches_until_cleared():
+    """A fault recorded in the host-mapped fault word (injected on the host:
+    no GPU wait is made to run out) makes the launching entry points fail
+    with LLATTN_ERR_DEVICE, so the op raises instead of returning outputs of
+    abandoned kernels; clearing the word restores normal launches."""
+    from llattn_b200 import _lib
+
+    L = _lib.lib()
+    inp = _inputs(1, 300, 2, 64)
+    ref = _run_fwd(inp, 2, 2, 128, 256, 32, 0, False)
+    assert _fault() == 0
+    assert L.llattn_fault_inject_host(4) == 0
+    try:
+        with pytest.raises(RuntimeError, match="status 5"):
+            _run_fwd(inp, 2, 2, 128, 256, 32, 0, False)
+    finally:
+        assert _fault() == 4  # reads and clears both words
+    again = _run_fwd(inp, 2, 2, 128, 256, 32, 0, False)
+    for a, b in zip(again, ref):
+        assert torch.equal(a, b)
+    assert _fault() == 0

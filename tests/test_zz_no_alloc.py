@@ -63,16 +63,41 @@ def _run(entry, inp, fwd, dm, cfg, with_workspace):
     return outs
 
 
+def _near_full_T(dtype, **kw):
+    """Largest T whose backward workspace still fits the fixed scratch: the
+    case that puts the last workspace region at the end of the array."""
+    from llattn_b200 import _lib
+
+    H, Lh, hd, ldh, W, LBS, Nl, QB = (kw[k] for k in ("H", "Lh", "hd", "ldh", "W", "LBS", "Nl", "QB"))
+    code = _lib.BF16 if dtype == torch.bfloat16 else _lib.F32
+    need = lambda T: _lib.lib().llattn_bwd_workspace_bytes(
+        ctypes.byref(_lib.make_dims(kw["B"], T, H, hd, Lh, ldh, W, LBS, Nl, QB, code, 0.0)))
+    lo, hi = 1, 65535
+    while lo < hi:  # the workspace grows with T
+        mid = (lo + hi + 1) // 2
+        lo, hi = (mid, hi) if need(mid) <= _lib.BWD_NOALLOC_SCRATCH_BYTES else (lo, mid - 1)
+    assert _lib.BWD_NOALLOC_SCRATCH_BYTES - need(lo) < 64 * 1024, "workspace not within 64 KiB of the scratch"
+    return lo
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_noalloc_bwd_matches_workspace_bwd_twice(dtype):
+    """Two calls in a row on different dims. The first fills the scratch almost
+    to its end, with block-pooled queries and more than 64 latent chunks (the
+    paths with the most workspace regions); the second, smaller call then
+    runs over what the first left behind. Each must give exactly the bytes of
+    llattn_bwd with a fresh caller workspace (the backward is deterministic)."""
     from llattn_b200 import _lib
 
     L = _lib.lib()
-    for seed in (0, 1):  # two calls in a row; the second reuses the scratch left by the first
-        inp, fwd, dm, cfg = _case(dtype, seed=seed)
+    big = dict(B=1, H=2, hd=128, Lh=2, ldh=32, Nl=128, W=256, LBS=256, QB=64)
+    T_big = _near_full_T(dtype, **big)
+    for kw in (dict(big, T=T_big), dict(T=777, seed=1)):
+        inp, fwd, dm, cfg = _case(dtype, **kw)
         ref = _run(L.llattn_bwd, inp, fwd, dm, cfg, True)
         got = _run(L.llattn_bwd_noalloc, inp, fwd, dm, cfg, False)
         for a, b in zip(got, ref):
+            assert torch.equal(a, b), f"T={kw['T']}: max diff {(a.float() - b.float()).abs().max().item()}"
             assert rel_err(a.float(), b.float()) <= TOL[dtype]
 
 
