@@ -42,8 +42,8 @@ int make_geom(const llattn_dims* d, Geom* g) {
     return fail(LLATTN_ERR_ARG, "n_heads >= 1 and 1 <= head_dim <= 128 required (head_dim=%d)", d->head_dim);
   if (d->latent_heads < 1 || d->latent_head_dim < 1 || d->latent_head_dim > 64)
     return fail(LLATTN_ERR_ARG, "latent_heads >= 1 and 1 <= latent_head_dim <= 64 required");
-  if (d->latent_heads * d->latent_head_dim > 128)
-    return fail(LLATTN_ERR_ARG, "latent_d_model = %d exceeds 128", d->latent_heads * d->latent_head_dim);
+  if (d->latent_heads * d->latent_head_dim > 4096)
+    return fail(LLATTN_ERR_ARG, "latent_d_model = %d exceeds 4096", d->latent_heads * d->latent_head_dim);
   if (d->window < 1) return fail(LLATTN_ERR_ARG, "local_window must be positive");
   if (d->latent_tokens < 1) return fail(LLATTN_ERR_ARG, "latent_tokens must be positive");
   if (d->dtype != LLATTN_F32 && d->dtype != LLATTN_BF16) return fail(LLATTN_ERR_ARG, "unknown dtype %d", d->dtype);
@@ -73,7 +73,7 @@ int make_geom(const llattn_dims* d, Geom* g) {
 
 // Backward workspace, every region 256-byte aligned.
 struct BwdLayout {
-  size_t dl, delta, drow, dlat, dlat_tok, dg_part, dg_sum, dw_part, dgkv_part, drq_part, total;
+  size_t dl, delta, drow, drow_half, dlat, dlat_tok, dg_part, dg_sum, dw_part, dgkv_part, drq_part, total;
   int gate_tok, n_gate_cta, n_split_w, n_split_lat, n_kg_lat;
 };
 
@@ -99,12 +99,16 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
   const size_t BTd = (size_t)g.B * g.T * g.d;
   L.dl = take(BTd * elt);
   L.delta = take(sizeof(float) * g.B * g.H * g.T);
-  L.drow = take(sizeof(float) * BTd);
+  // fp32 dremote (SIMT), bf16 dR (fused tensor-core path), or the general
+  // path's bf16 remote rows [B*Tq, d] and, from drow_half on, its dR rows
+  L.drow_half = align256(sizeof(bf16) * (size_t)g.B * g.Tq * g.d);
+  L.drow = take(std::max(sizeof(float) * BTd, 2 * L.drow_half));
   L.dlat = take(sizeof(float) * (size_t)rows * g.Ld);
   L.dlat_tok = take(sizeof(float) * (size_t)g.B * g.T * g.Ld);
   // dg partials: [n_gate_cta][2 hd] (SIMT gate) or [gate_bwd_ctas][hd + 65 H] (tensor-core gate)
   const size_t dg_tc = (size_t)g.B * cdiv(g.T, 128) * (g.hd + 65 * g.H);
-  L.dg_part = take(sizeof(float) * std::max((size_t)L.n_gate_cta * 2 * g.hd, dg_tc));
+  const size_t dg_rm = (size_t)g.B * std::max(cdiv(g.T, 16), g.Tq) * 2 * g.hd;  // general path's gate CTAs
+  L.dg_part = take(sizeof(float) * std::max(std::max((size_t)L.n_gate_cta * 2 * g.hd, dg_tc), dg_rm));
   L.dg_sum = take(sizeof(float) * (size_t)std::max(2 * g.hd, g.hd + 65 * g.H));
   L.dw_part = take(sizeof(float) * (size_t)L.n_split_w * g.d * (g.Ld + 1));
   L.dgkv_part = take(sizeof(float) * (size_t)L.n_split_lat * L.n_kg_lat * g.B * g.Nc * 2 * g.Ld);
@@ -158,10 +162,57 @@ int fault_gate(Geom* g) {
   return LLATTN_OK;
 }
 
+// The general tensor-core path needs 16-byte rows for the GEMM's copies.
+bool general_ok(const Geom& g) { return g.Ld % 8 == 0 && g.d % 8 == 0 && g.hd % 4 == 0; }
+
+// The SIMT r_out / gate kernels hold at most 128 latent columns per row.
+int simt_gate_check(const Geom& g) {
+  if (g.Ld > 128)
+    return fail(LLATTN_ERR_ARG,
+                "latent_d_model = %d > 128 needs the tensor-core path (bf16 activations, head_dim 64 or 128, "
+                "latent_d_model a multiple of 8)",
+                g.Ld);
+  return LLATTN_OK;
+}
+
+// Tensor-core path for geometries the fused gate epilogue does not hold
+// (latent_d_model != 64, or more than 32 heads): local forward without the
+// epilogue, remote = lat W_rout^T + b_rout by the tensor-core GEMM written
+// into the rows of `mixed` the gate kernel reads them from, then gate and
+// mix in place.
+int run_fwd_general(const Geom& g, const llattn_fwd_args* a, cudaStream_t s) {
+  int rc;
+  {
+    prof::Scope ps(prof::LOCAL_FWD, s);
+    sm100::GateEpilogue ep{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    rc = check_launch(sm100::launch_local_fwd(g, a->qkv, a->local_out, a->lse, ep, s), "local_fwd_sm100");
+  }
+  if (rc) return rc;
+  prof::Scope ps(prof::GATE_FWD, s, 2);
+  sm100::GemmOut o{};
+  o.C = a->mixed;
+  o.ldc = g.d;
+  o.out_bf16 = 1;
+  o.bias = a->b_rout;
+  o.rows_per_group = g.Tq;
+  o.group_stride = g.T;
+  o.row_step = g.qbs;
+  rc = check_launch(sm100::launch_gemm(g, g.B * g.Tq, g.d, g.Ld, a->lat, g.Ld, 0, a->w_rout, g.Ld, 0, o, 1, s),
+                    "remote_gemm");
+  if (rc) return rc;
+  return check_launch(launch_gate_mix_rmem(g, static_cast<const bf16*>(a->local_out), a->g_local, a->g_remote,
+                                           static_cast<bf16*>(a->mixed), s),
+                      "gate_mix");
+}
+
 template <typename T>
 int run_fwd(const Geom& g, const llattn_fwd_args* a, cudaStream_t s) {
   const T* qkv = static_cast<const T*>(a->qkv);
+  const bool tc = sm100::fwd_supported(g, sizeof(T));
+  const bool fused = tc && sm100::gate_fusable(g);
+  const bool general = tc && !fused && general_ok(g);
   int rc;
+  if (!fused && !general && (rc = simt_gate_check(g))) return rc;
   {
     prof::Scope ps(prof::LATENT_FWD, s);
     if (sizeof(T) == 2 && sm100::latent_tc_ok(g))  // tensor cores: bf16, head dim 32, <= 64 chunks
@@ -172,8 +223,7 @@ int run_fwd(const Geom& g, const llattn_fwd_args* a, cudaStream_t s) {
                         "latent_fwd");
   }
   if (rc) return rc;
-  const bool tc = sm100::fwd_supported(g, sizeof(T));
-  const bool fused = tc && sm100::gate_fusable(g);
+  if (general) return run_fwd_general(g, a, s);
   {
   prof::Scope ps(prof::LOCAL_FWD, s);
   if (tc) {
@@ -195,6 +245,7 @@ int run_fwd(const Geom& g, const llattn_fwd_args* a, cudaStream_t s) {
 
 template <typename T>
 int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
+  int rc0;
   const BwdLayout L = bwd_layout(g, sizeof(T));
   char* ws = static_cast<char*>(a->workspace);
   T* dl = reinterpret_cast<T*>(ws + L.dl);
@@ -209,9 +260,65 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
   const T* w_rout = static_cast<const T*>(a->w_rout);
 
   const bool tc = sm100::bwd_supported(g, sizeof(T)) && sm100::gate_fusable(g);
+  const bool general =
+      sizeof(T) == 2 && sm100::bwd_supported(g, sizeof(T)) && !sm100::gate_fusable(g) && general_ok(g);
+  if (!tc && !general && (rc0 = simt_gate_check(g))) return rc0;
   int n_dg = L.n_gate_cta;
   int rc;
-  if (tc) {
+  if (general) {
+    // remote rows recomputed by the GEMM, the gate backward on them, the
+    // local backward, then dlat = dR W_rout, dW_rout = dR^T lat and db_rout
+    // (column sums) by the GEMM, with dR per query row (summed over each
+    // query block for block-pooled queries)
+    bf16* rem = reinterpret_cast<bf16*>(ws + L.drow);
+    bf16* dr = reinterpret_cast<bf16*>(ws + L.drow + L.drow_half);
+    const int rows = g.B * g.Tq;
+    n_dg = gate_rmem_ctas(g);
+    {
+      prof::Scope ps(prof::GATE_BWD, s, 2);
+      sm100::GemmOut o{};
+      o.C = rem;
+      o.ldc = g.d;
+      o.out_bf16 = 1;
+      o.bias = a->b_rout;
+      rc = check_launch(sm100::launch_gemm(g, rows, g.d, g.Ld, a->lat, g.Ld, 0, a->w_rout, g.Ld, 0, o, 1, s),
+                        "remote_gemm");
+      if (rc) return rc;
+      rc = check_launch(launch_gate_bwd_rmem(g, static_cast<const bf16*>(a->local_out), rem, a->g_local,
+                                             a->g_remote, static_cast<const bf16*>(a->dmixed),
+                                             reinterpret_cast<bf16*>(dl), delta, dr, dg_part, s),
+                        "gate_bwd_rmem");
+    }
+    if (rc) return rc;
+    {
+      prof::Scope ps(prof::LOCAL_DQ, s);
+      rc = check_launch(sm100::launch_local_dq(g, a->qkv, dl, a->lse, delta, a->dqkv, s), "local_dq_sm100");
+    }
+    if (rc) return rc;
+    {
+      prof::Scope ps(prof::LOCAL_DKV, s);
+      rc = check_launch(sm100::launch_local_dkv(g, a->qkv, dl, a->lse, delta, a->dqkv, s), "local_dkv_sm100");
+    }
+    if (rc) return rc;
+    {
+      prof::Scope ps(prof::ROUT_BWD, s, 2);
+      sm100::GemmOut o{};
+      o.C = dlat;
+      o.ldc = g.Ld;
+      rc = check_launch(sm100::launch_gemm(g, rows, g.Ld, g.d, dr, g.d, 0, a->w_rout, g.Ld, 1, o, 1, s),
+                        "dlat_gemm");
+      if (rc) return rc;
+      sm100::GemmOut w{};
+      w.C = dw_part;
+      w.ldc = g.Ld;
+      w.split_stride = (int64_t)g.d * g.Ld;
+      w.colsum = dw_part + (size_t)L.n_split_w * g.d * g.Ld;
+      w.colsum_split = g.d;
+      rc = check_launch(sm100::launch_gemm(g, g.d, g.Ld, rows, dr, g.d, 1, a->lat, g.Ld, 1, w, L.n_split_w, s),
+                        "dw_gemm");
+      if (rc) return rc;
+    }
+  } else if (tc) {
     // tensor-core path: gate backward (also dlat, dR bf16, dg partials), then
     // the local backward, then the dW_rout / db_rout GEMM from dR
     bf16* dr = reinterpret_cast<bf16*>(drow);
@@ -286,7 +393,7 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
   if (rc) return rc;
   // dg partials: SIMT [cta][2*hd] (local half, remote half); tensor-core
   // [cta][hd + 65 H] (local, then the S1/S0 sums dg_remote is linear in)
-  const int dg_n = tc ? sm100::gate_dg_floats(g) : 2 * g.hd;
+  const int dg_n = tc ? sm100::gate_dg_floats(g) : 2 * g.hd;  // general: the SIMT format
   rc = check_launch(launch_reduce_rows(dg_part, n_dg, dg_n, dg_sum, s), "reduce_dg");
   if (rc) return rc;
   rc = check_launch(cudaMemcpyAsync(a->dg_local, dg_sum, sizeof(float) * g.hd, cudaMemcpyDeviceToDevice, s),

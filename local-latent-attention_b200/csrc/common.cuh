@@ -139,6 +139,17 @@ cudaError_t launch_gate_bwd(const Geom& g, const T* local_out, const T* lat, con
 template <typename T>
 cudaError_t launch_rout_bwd(const Geom& g, const float* drow, const T* lat, const T* w_rout,
                             float* dlat, float* dw_part, int n_split, cudaStream_t s);
+// Gate and mix with the remote projection precomputed (bf16; see gate.cu):
+// forward in place over `mixed`, which holds the remote rows on entry (token
+// t's at row t, query block r's at row r * qbs); backward with the remote
+// rows rem [B*Tq, d], writing dl, delta, dr (per token, or per query block
+// summed over its tokens) and gate_rmem_ctas(g) partials [2 hd] of dg.
+int gate_rmem_ctas(const Geom& g);
+cudaError_t launch_gate_mix_rmem(const Geom& g, const bf16* local_out, const float* g_local, const float* g_remote,
+                                 bf16* mixed, cudaStream_t s);
+cudaError_t launch_gate_bwd_rmem(const Geom& g, const bf16* local_out, const bf16* rem, const float* g_local,
+                                 const float* g_remote, const bf16* dmixed, bf16* dl, float* delta, bf16* dr,
+                                 float* dg_part, cudaStream_t s);
 cudaError_t launch_reduce_rows(const float* part, int n_part, int64_t n, float* out,
                                cudaStream_t s);
 

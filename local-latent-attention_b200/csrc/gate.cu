@@ -273,7 +273,203 @@ cudaError_t rout_bwd_lm(const Geom& g, const float* drow, const T* lat, const T*
   return cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------------------
+// Gate and mix with the remote projection precomputed (bf16, any latent
+// width): the tensor-core GEMM writes remote = lat W_rout^T + b_rout, these
+// kernels do the per-(token, head) gate arithmetic, one warp per (token,
+// head) pair with 4 elements per lane (head_dim <= 128, a multiple of 4).
+// A CTA covers RM_TOK tokens (token-wise latent queries) or one query block
+// (block-pooled ones); warp w takes the heads h = w mod 8 of every token, so
+// a head's running sums stay in one warp and the order of every sum is fixed.
+
+constexpr int RM_WARPS = 8, RM_TOK = 16;
+
+__device__ __forceinline__ void ld4(const bf16* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  v[0] = __uint_as_float(u.x << 16);
+  v[1] = __uint_as_float(u.x & 0xffff0000u);
+  v[2] = __uint_as_float(u.y << 16);
+  v[3] = __uint_as_float(u.y & 0xffff0000u);
+}
+__device__ __forceinline__ void st4(bf16* p, const float (&v)[4]) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&a);
+  u.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+// mixed holds the remote rows on entry: token t's at row t (token-wise), or
+// query block r's at the block's first row r * qbs (read by this CTA alone,
+// into shared memory, before any of the block's rows is overwritten).
+__global__ void __launch_bounds__(RM_WARPS * 32) gate_mix_rmem_kernel(Geom g, const bf16* __restrict__ local_out,
+                                                                     const float* __restrict__ gl,
+                                                                     const float* __restrict__ gr,
+                                                                     bf16* __restrict__ mixed) {
+  extern __shared__ __align__(16) bf16 srem[];  // block-pooled queries: the block's remote row [d]
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, b = blockIdx.y;
+  const bool pooled = g.qbs > 1;
+  const int ta = pooled ? blockIdx.x * g.qbs : blockIdx.x * RM_TOK;
+  const int tb = min(g.T, ta + (pooled ? g.qbs : RM_TOK));
+  if (pooled) {
+    const uint4* src = reinterpret_cast<const uint4*>(mixed + ((int64_t)b * g.T + ta) * g.d);
+    for (int i = threadIdx.x; i < g.d / 8; i += blockDim.x) reinterpret_cast<uint4*>(srem)[i] = src[i];
+    __syncthreads();
+  }
+  const int e = 4 * lane;
+  const bool on = e < g.hd;
+  float vgl[4] = {0.f, 0.f, 0.f, 0.f}, vgr[4] = {0.f, 0.f, 0.f, 0.f};
+  if (on) {
+    const float4 a = *reinterpret_cast<const float4*>(gl + e), c = *reinterpret_cast<const float4*>(gr + e);
+    vgl[0] = a.x; vgl[1] = a.y; vgl[2] = a.z; vgl[3] = a.w;
+    vgr[0] = c.x; vgr[1] = c.y; vgr[2] = c.z; vgr[3] = c.w;
+  }
+  for (int t = ta; t < tb; ++t) {
+    const int64_t row = (int64_t)b * g.T + t;
+    for (int h = warp; h < g.H; h += RM_WARPS) {
+      const int64_t o = row * g.d + (int64_t)h * g.hd + e;
+      float L[4] = {0.f, 0.f, 0.f, 0.f}, R[4] = {0.f, 0.f, 0.f, 0.f};
+      if (on) {
+        ld4(local_out + o, L);
+        ld4(pooled ? srem + h * g.hd + e : mixed + o, R);
+      }
+      float sl = 0.f, sr = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        sl = fmaf(L[k], vgl[k], sl);
+        sr = fmaf(R[k], vgr[k], sr);
+      }
+      sl = warp_sum(sl);
+      sr = warp_sum(sr);
+      // both weights directly: 1 - w would lose the small one when the gate saturates
+      const float x = sl + g.gate_bias - sr;
+      const float w = 1.f / (1.f + expf(-x)), wr = 1.f / (1.f + expf(x));
+      if (on) {
+        float m[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) m[k] = w * L[k] + wr * R[k];
+        st4(mixed + o, m);
+      }
+    }
+  }
+}
+
+// Backward with the remote rows R [B*Tq, d] precomputed. Writes dl (bf16),
+// the local backward's row term D = dl.local, the gradient of the remote
+// projection's output (bf16; per token, or summed over each query block when
+// the queries are block-pooled: the rows the r_out GEMMs take) and per-CTA
+// gate partials dg_part[cta] = [sum ds local (hd), -sum ds remote (hd)].
+__global__ void __launch_bounds__(RM_WARPS * 32) gate_bwd_rmem_kernel(
+    Geom g, const bf16* __restrict__ local_out, const bf16* __restrict__ rem, const float* __restrict__ gl,
+    const float* __restrict__ gr, const bf16* __restrict__ dmixed, bf16* __restrict__ dl,
+    float* __restrict__ delta, bf16* __restrict__ dr, float* __restrict__ dg_part) {
+  extern __shared__ __align__(16) float sgb[];  // [RM_WARPS][2 hd] partials, then (pooled) dR sums [d]
+  float* sred = sgb;
+  float* sdr = sgb + RM_WARPS * 2 * g.hd;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, b = blockIdx.y;
+  const bool pooled = g.qbs > 1;
+  const int ta = pooled ? blockIdx.x * g.qbs : blockIdx.x * RM_TOK;
+  const int tb = min(g.T, ta + (pooled ? g.qbs : RM_TOK));
+  const int e = 4 * lane;
+  const bool on = e < g.hd;
+  float vgl[4] = {0.f, 0.f, 0.f, 0.f}, vgr[4] = {0.f, 0.f, 0.f, 0.f};
+  if (on) {
+    const float4 a = *reinterpret_cast<const float4*>(gl + e), c = *reinterpret_cast<const float4*>(gr + e);
+    vgl[0] = a.x; vgl[1] = a.y; vgl[2] = a.z; vgl[3] = a.w;
+    vgr[0] = c.x; vgr[1] = c.y; vgr[2] = c.z; vgr[3] = c.w;
+  }
+  float agl[4] = {0.f, 0.f, 0.f, 0.f}, agr[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int h = warp; h < g.H; h += RM_WARPS) {
+    float dsum[4] = {0.f, 0.f, 0.f, 0.f};  // pooled: this head's dR summed over the block
+    for (int t = ta; t < tb; ++t) {
+      const int64_t row = (int64_t)b * g.T + t;
+      const int64_t o = row * g.d + (int64_t)h * g.hd + e;
+      const int64_t orem = ((int64_t)b * g.Tq + t / g.qbs) * g.d + (int64_t)h * g.hd + e;
+      float L[4] = {0.f, 0.f, 0.f, 0.f}, R[4] = {0.f, 0.f, 0.f, 0.f}, dm[4] = {0.f, 0.f, 0.f, 0.f};
+      if (on) {
+        ld4(local_out + o, L);
+        ld4(rem + orem, R);
+        ld4(dmixed + o, dm);
+      }
+      float sl = 0.f, sr = 0.f, dw = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        sl = fmaf(L[k], vgl[k], sl);
+        sr = fmaf(R[k], vgr[k], sr);
+        dw = fmaf(dm[k], L[k] - R[k], dw);
+      }
+      sl = warp_sum(sl);
+      sr = warp_sum(sr);
+      dw = warp_sum(dw);
+      const float x = sl + g.gate_bias - sr;
+      const float w = 1.f / (1.f + expf(-x)), wr = 1.f / (1.f + expf(x));
+      const float ds = dw * w * wr;
+      float dlv[4], drv[4], dd = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        dlv[k] = __bfloat162float(__float2bfloat16_rn(w * dm[k] + ds * vgl[k]));
+        dd = fmaf(dlv[k], L[k], dd);
+        drv[k] = wr * dm[k] - ds * vgr[k];
+        agl[k] = fmaf(ds, L[k], agl[k]);
+        agr[k] = fmaf(-ds, R[k], agr[k]);
+      }
+      dd = warp_sum(dd);
+      if (on) {
+        st4(dl + o, dlv);
+        if (pooled) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) dsum[k] += drv[k];
+        } else {
+          st4(dr + o, drv);
+        }
+      }
+      if (lane == 0) delta[((int64_t)b * g.H + h) * g.T + t] = dd;
+    }
+    if (pooled && on) st4(dr + ((int64_t)b * g.Tq + blockIdx.x) * g.d + (int64_t)h * g.hd + e, dsum);
+  }
+  if (on) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      sred[warp * 2 * g.hd + e + k] = agl[k];
+      sred[warp * 2 * g.hd + g.hd + e + k] = agr[k];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 2 * g.hd; i += blockDim.x) {
+    float a = 0.f;
+    for (int w = 0; w < RM_WARPS; ++w) a += sred[w * 2 * g.hd + i];
+    dg_part[((int64_t)b * gridDim.x + blockIdx.x) * 2 * g.hd + i] = a;
+  }
+  (void)sdr;
+}
+
 }  // namespace
+
+int gate_rmem_ctas(const Geom& g) { return g.B * (g.qbs > 1 ? g.Tq : cdiv(g.T, RM_TOK)); }
+
+cudaError_t launch_gate_mix_rmem(const Geom& g, const bf16* local_out, const float* g_local, const float* g_remote,
+                                 bf16* mixed, cudaStream_t s) {
+  const size_t sm = g.qbs > 1 ? sizeof(bf16) * g.d : 0;
+  if (sm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(gate_mix_rmem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid(g.qbs > 1 ? g.Tq : cdiv(g.T, RM_TOK), g.B);
+  gate_mix_rmem_kernel<<<grid, RM_WARPS * 32, sm, s>>>(g, local_out, g_local, g_remote, mixed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gate_bwd_rmem(const Geom& g, const bf16* local_out, const bf16* rem, const float* g_local,
+                                 const float* g_remote, const bf16* dmixed, bf16* dl, float* delta, bf16* dr,
+                                 float* dg_part, cudaStream_t s) {
+  const size_t sm = sizeof(float) * RM_WARPS * 2 * g.hd;
+  dim3 grid(g.qbs > 1 ? g.Tq : cdiv(g.T, RM_TOK), g.B);
+  gate_bwd_rmem_kernel<<<grid, RM_WARPS * 32, sm, s>>>(g, local_out, rem, g_local, g_remote, dmixed, dl, delta, dr,
+                                                       dg_part);
+  return cudaGetLastError();
+}
+
 
 template <typename T>
 cudaError_t launch_gate_fwd(const Geom& g, const T* local_out, const T* lat, const T* w_rout,

@@ -165,8 +165,8 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
         if (!mbar_wait(&bars[GB_DR + grp], n & 1, abort, &g_fault_word)) return false;
 #pragma unroll
         for (int p = 0; p < HD / 64; ++p) {
-          tma_store_3d(&tm_dl, smem + L::LT + grp * L::TILE + p * (BM * 128), h * HD + p * 64, t0, b);
-          tma_store_3d(&tm_dr, smem + L::DM + grp * L::TILE + p * (BM * 128), h * HD + p * 64, t0, b);
+          tma_store_4d(&tm_dl, smem + L::LT + grp * L::TILE + p * (BM * 128), p * 64, h, t0, b);
+          tma_store_4d(&tm_dr, smem + L::DM + grp * L::TILE + p * (BM * 128), p * 64, h, t0, b);
         }
         tma_store_commit();
         return true;
@@ -182,8 +182,8 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
         mbar_expect_tx(&bars[GB_F + grp], 2 * L::TILE);
 #pragma unroll
         for (int p = 0; p < HD / 64; ++p) {
-          tma_load_2d(&tm_lo, &bars[GB_F + grp], smem + L::LT + grp * L::TILE + p * (BM * 128), h * HD + p * 64, row0);
-          tma_load_2d(&tm_dm, &bars[GB_F + grp], smem + L::DM + grp * L::TILE + p * (BM * 128), h * HD + p * 64, row0);
+          tma_load_4d(&tm_lo, &bars[GB_F + grp], smem + L::LT + grp * L::TILE + p * (BM * 128), p * 64, h, row0, 0);
+          tma_load_4d(&tm_dm, &bars[GB_F + grp], smem + L::DM + grp * L::TILE + p * (BM * 128), p * 64, h, row0, 0);
         }
         issued = h + 1;
       }
@@ -247,12 +247,14 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
     float* cgl = reinterpret_cast<float*>(smem + L::CST);  // g_local [HD], g_remote [HD]
     float* cbh = cgl + (2 + grp) * HD;                      // this group's b_rout[h]
     auto write_w = [&](int h) {  // into this group's W buffer, and b_rout[h]
-      if (row < HD) {
-        const uint4* src = reinterpret_cast<const uint4*>(w_rout + ((int64_t)h * HD + row) * 64);
+      if (row < HD) {  // rows past a padded head_dim are zero
+        const bool real = row < g.hd;
+        const uint4* src = reinterpret_cast<const uint4*>(w_rout + ((int64_t)h * g.hd + (real ? row : 0)) * 64);
         uint8_t* d = smem + L::W + grp * HD * 128 + row * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(d + ((c ^ (row & 7)) * 16)) = src[c];
-        cbh[row] = b_rout[(int64_t)h * HD + row];
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(d + ((c ^ (row & 7)) * 16)) = real ? src[c] : make_uint4(0u, 0u, 0u, 0u);
+        cbh[row] = real ? b_rout[(int64_t)h * g.hd + row] : 0.f;
       }
       fence_async_smem();
       mbar_arrive(&bars[GB_W + grp]);
@@ -260,8 +262,8 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
     float* wred = red + (warp - 2) * HD;  // lane owns columns cc*32+lane
     for (int e = lane; e < HD; e += 32) wred[e] = 0.f;
     if (grp == 0 && row < HD) {
-      cgl[row] = gl[row];
-      cgl[HD + row] = gr[row];
+      cgl[row] = row < g.hd ? gl[row] : 0.f;
+      cgl[HD + row] = row < g.hd ? gr[row] : 0.f;
     }
     bool ok = true;
     if (grp < H) write_w(grp);
@@ -409,9 +411,9 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) LLATTN_TRACE_K(3, 60);
-  const int64_t part = ((int64_t)b * gridDim.x + blockIdx.x) * gate_dg_stride(HD, H);
+  const int64_t part = ((int64_t)b * gridDim.x + blockIdx.x) * gate_dg_stride(g.hd, H);
   // dg_local partial [cta][0, HD): summed over the compute warps
-  for (int e = threadIdx.x; e < HD; e += blockDim.x) {
+  for (int e = threadIdx.x; e < g.hd; e += blockDim.x) {
     float v = 0.f;
 #pragma unroll
     for (int w8 = 0; w8 < 4 * G; ++w8) v += red[w8 * HD + e];
@@ -441,7 +443,7 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
         s0 += dsv;
       }
     }
-    float* o = dg_part + part + HD + h * 65;
+    float* o = dg_part + part + g.hd + h * 65;
     o[e0] = a0;  // rows of 65 floats: not 16-byte aligned
     o[e0 + 1] = a1;
     o[e0 + 2] = a2;

@@ -81,6 +81,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 #include "local_sm100_bwd.cuh"
 #include "gate_sm100.cuh"
 #include "latent_sm100.cuh"
+#include "gemm_sm100.cuh"
 
 // ---------------------------------------------------------------------------
 // host side
@@ -113,24 +114,6 @@ bool make_rows_map(CUtensorMap* map, const void* base, int B, int T, int slots_x
   return r == CUDA_SUCCESS;
 }
 
-// [B, T, S, H, hd] bf16 viewed as 5-D (64, T, hd/64, S*H, B) with box
-// (64, rows, hd/64, 1, 1): one copy brings a whole rows x hd tile in the
-// panel-major 128-byte-swizzled layout the MMA descriptors expect (panel p at
-// p * rows * 128 bytes). Fewer, larger copies: the TMA issue rate, not
-// bandwidth, bounds a stream of 8 KB boxes.
-bool make_panel_map(CUtensorMap* map, const void* base, int B, int T, int slots_x_heads, int hd, int rows) {
-  auto enc = get_encode();
-  if (!enc) return false;
-  const cuuint64_t row_stride = (cuuint64_t)slots_x_heads * hd * 2;
-  cuuint64_t dims[5] = {64, (cuuint64_t)T, (cuuint64_t)(hd / 64), (cuuint64_t)slots_x_heads, (cuuint64_t)B};
-  cuuint64_t strides[4] = {row_stride, 128, (cuuint64_t)hd * 2, (cuuint64_t)T * row_stride};
-  cuuint32_t box[5] = {64, (cuuint32_t)rows, (cuuint32_t)(hd / 64), 1, 1};
-  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // LLATTN_FORCE_SIMT=1 routes bf16 through the SIMT kernels (used by the tests
 // to compare the two implementations of the same math).
 // bf16 matrix [rows, cols] (cols contiguous) with box (64 cols, box_rows rows).
@@ -139,6 +122,19 @@ bool make_2d_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// bf16 matrix [rows, cols] with row stride ld elements, box (64 cols, box_rows rows).
+bool make_ld_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
   cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
@@ -169,12 +165,13 @@ template <int HD>
 cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, const GateEpilogue& ep,
                    cudaStream_t s) {
   CUtensorMap tq, tkv;
-  if (!make_panel_map(&tq, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_panel_map(&tkv, qkv, g.B, g.T, 3 * g.H, HD, 64))
+  if (!make_rows_map(&tq, qkv, g.B, g.T, 3 * g.H, g.hd, 128) || !make_rows_map(&tkv, qkv, g.B, g.T, 3 * g.H, g.hd, 64))
     return cudaErrorInvalidValue;
   // two query tiles per CTA (ping-pong), one CTA per SM; the fused epilogue
   // stores local_out and mixed through 3-D maps (d, T, B) that clip at T
   CUtensorMap tlo, tmx, tlat, tw;
-  if (!make_btd_map(&tlo, local_out, g.B, g.T, g.d) || !make_btd_map(&tmx, ep.mixed ? ep.mixed : local_out, g.B, g.T, g.d))
+  if (!make_rows_map(&tlo, local_out, g.B, g.T, g.H, g.hd, 128) ||
+      !make_rows_map(&tmx, ep.mixed ? ep.mixed : local_out, g.B, g.T, g.H, g.hd, 128))
     return cudaErrorInvalidValue;
   // remote-tile operands: lat rows [B, Tq, 64] (box 64 x 128 rows) and the
   // head's W_rout slice [d, 64] (box 64 x hd rows); unused without the fusion
@@ -212,8 +209,8 @@ template <int HD>
 cudaError_t dq_hd(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta, void* dqkv,
                   cudaStream_t s) {
   CUtensorMap q128, q64, do128, st;
-  if (!make_panel_map(&q128, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_panel_map(&q64, qkv, g.B, g.T, 3 * g.H, HD, 64) ||
-      !make_panel_map(&do128, dl, g.B, g.T, g.H, HD, 128) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, HD, 128))
+  if (!make_rows_map(&q128, qkv, g.B, g.T, 3 * g.H, g.hd, 128) || !make_rows_map(&q64, qkv, g.B, g.T, 3 * g.H, g.hd, 64) ||
+      !make_rows_map(&do128, dl, g.B, g.T, g.H, g.hd, 128) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, g.hd, 128))
     return cudaErrorInvalidValue;
   // persistent: one CTA per SM walks the (h, query tile, b) units
   const int smem = DqpLayout<HD>::BYTES;  // the kernel's shared memory is 1024-byte aligned
@@ -229,8 +226,8 @@ template <int HD>
 cudaError_t dkv_hd(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta, void* dqkv,
                    cudaStream_t s) {
   CUtensorMap q128, q64, do64, st;
-  if (!make_panel_map(&q128, qkv, g.B, g.T, 3 * g.H, HD, 128) || !make_panel_map(&q64, qkv, g.B, g.T, 3 * g.H, HD, 64) ||
-      !make_panel_map(&do64, dl, g.B, g.T, g.H, HD, 64) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, HD, 128))
+  if (!make_rows_map(&q128, qkv, g.B, g.T, 3 * g.H, g.hd, 128) || !make_rows_map(&q64, qkv, g.B, g.T, 3 * g.H, g.hd, 64) ||
+      !make_rows_map(&do64, dl, g.B, g.T, g.H, g.hd, 64) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, g.hd, 128))
     return cudaErrorInvalidValue;
   const int smem = DkvLayout<HD>::BYTES;  // the kernel's shared memory is 1024-byte aligned
   cudaError_t e = cudaFuncSetAttribute(local_dkv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -244,9 +241,11 @@ cudaError_t dkv_hd(const Geom& g, const void* qkv, const void* dl, const float* 
 template <int HD, int G>
 cudaError_t gate_bwd_hd(const Geom& g, const GateBwd& a, cudaStream_t s) {
   CUtensorMap tlo, tdm, tdl, tdr;
-  if (!make_2d_map(&tlo, a.local_out, (int64_t)g.B * g.T, g.d, 128) ||
-      !make_2d_map(&tdm, a.dmixed, (int64_t)g.B * g.T, g.d, 128) || !make_btd_map(&tdl, a.dl, g.B, g.T, g.d) ||
-      !make_btd_map(&tdr, a.dr, g.B, g.T, g.d))
+  // per-head 4-D maps (hd, H, rows, B): a padded head_dim's extra columns
+  // are zero-filled on load and clipped on store
+  if (!make_rows_map(&tlo, a.local_out, 1, g.B * g.T, g.H, g.hd, 128) ||
+      !make_rows_map(&tdm, a.dmixed, 1, g.B * g.T, g.H, g.hd, 128) ||
+      !make_rows_map(&tdl, a.dl, g.B, g.T, g.H, g.hd, 128) || !make_rows_map(&tdr, a.dr, g.B, g.T, g.H, g.hd, 128))
     return cudaErrorInvalidValue;
   const int smem = GbLayout<HD, G>::BYTES + 1024;
   cudaError_t e = cudaFuncSetAttribute(gate_bwd_tc_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -259,6 +258,42 @@ cudaError_t gate_bwd_hd(const Geom& g, const GateBwd& a, cudaStream_t s) {
 }
 
 }  // namespace
+
+cudaError_t launch_gemm(const Geom& g, int M, int N, int K, const void* A, int64_t lda, int a_mn, const void* B,
+                        int64_t ldb, int b_mn, const GemmOut& o, int splits, cudaStream_t s) {
+  if (M < 1 || N < 1 || K < 1 || splits < 1) return cudaErrorInvalidValue;
+  if (((uintptr_t)A & 15) || ((uintptr_t)B & 15) || (lda % 8) || (ldb % 8)) return cudaErrorMisalignedAddress;
+  CUtensorMap ta, tb;
+  // K-major: [rows, K] tiles of 128 rows x 64 K; MN-major: [K, MN] panels of 64 MN x 64 K rows
+  if (!(a_mn ? make_ld_map(&ta, A, K, M, lda, 64) : make_ld_map(&ta, A, M, K, lda, 128)) ||
+      !(b_mn ? make_ld_map(&tb, B, K, N, ldb, 64) : make_ld_map(&tb, B, N, K, ldb, 128)))
+    return cudaErrorInvalidValue;
+  GemmArgs p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.a_mn = a_mn;
+  p.b_mn = b_mn;
+  p.k_per_split = cdiv(cdiv(K, splits), 64) * 64;
+  p.bias = o.bias;
+  p.C = o.C;
+  p.ldc = o.ldc;
+  p.c_bf16 = o.out_bf16;
+  p.c_split = o.split_stride;
+  p.rows_per_group = o.rows_per_group > 0 ? o.rows_per_group : M;
+  p.group_stride = o.group_stride;
+  p.row_step = o.row_step > 0 ? o.row_step : 1;
+  p.colsum = o.colsum;
+  p.colsum_split = o.colsum_split;
+  const int smem = GemmLayout::BYTES + 1024;
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  // every split runs (one whose K range is empty writes zeros): callers sum
+  // exactly `splits` partials
+  dim3 grid(cdiv(N, 128), cdiv(M, 128), splits);
+  gemm_tc_kernel<<<grid, 192, smem, s>>>(ta, tb, g, p);
+  return cudaGetLastError();
+}
 
 int gate_bwd_ctas(const Geom& g) { return g.B * cdiv(g.T, BM); }
 int gate_dg_floats(const Geom& g) { return gate_dg_stride(g.hd, g.H); }
@@ -337,7 +372,10 @@ cudaError_t launch_dlat_rowsum(const Geom& g, const float* dlat_tok, float* dlat
 }
 
 bool fwd_supported(const Geom& g, int elt_bytes) {
-  return !force_simt() && elt_bytes == 2 && (g.hd == 64 || g.hd == 128) && get_encode() != nullptr;
+  // head_dim 64, or 64 < hd <= 128 run as 128-wide tiles (the copies zero-fill
+  // the columns past hd; 16-byte rows need hd % 8 == 0)
+  const bool hd_ok = g.hd == 64 || (g.hd > 64 && g.hd <= 128 && g.hd % 8 == 0);
+  return !force_simt() && elt_bytes == 2 && hd_ok && get_encode() != nullptr;
 }
 
 bool bwd_supported(const Geom& g, int elt_bytes) { return fwd_supported(g, elt_bytes); }

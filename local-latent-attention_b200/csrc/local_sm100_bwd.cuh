@@ -132,16 +132,16 @@ __global__ void __launch_bounds__(320, 1)
         // buffer qb: free once unit n-2's dQ store has read its staging
         if (n >= 2 && !(ok = mbar_wait(&bars[DP_QE + qb], ((n >> 1) - 1) & 1, abort, &g_fault_word))) break;
         mbar_expect_tx(&bars[DP_Q + qb], 2 * L::QTILE);
-        tma_load_tile(&tm_qkv128, &bars[DP_Q + qb], smem + qb * L::QD + L::Q, t.q0, t.h, t.b);
-        tma_load_tile(&tm_do128, &bars[DP_Q + qb], smem + qb * L::QD + L::DO, t.q0, t.h, t.b);
+        tma_load_tile<HD / 64, BM>(&tm_qkv128, &bars[DP_Q + qb], smem + qb * L::QD + L::Q, t.q0, t.h, t.b);
+        tma_load_tile<HD / 64, BM>(&tm_do128, &bars[DP_Q + qb], smem + qb * L::QD + L::DO, t.q0, t.h, t.b);
         issued_q = n + 1;
         for (int j = 0; j < t.nk; ++j, ++jj) {
           const int s = jj % NKS;
           if (jj >= NKS && !(ok = mbar_wait(&bars[DP_KVE + s], ((jj / NKS) - 1) & 1, abort, &g_fault_word))) break;
           const int k0 = t.kbase + j * BNK;
           mbar_expect_tx(&bars[DP_KV + s], 2 * L::KTILE);
-          tma_load_tile(&tm_qkv64, &bars[DP_KV + s], smem + L::K + s * L::KV, k0, g.H + t.h, t.b);
-          tma_load_tile(&tm_qkv64, &bars[DP_KV + s], smem + L::V + s * L::KV, k0, 2 * g.H + t.h, t.b);
+          tma_load_tile<HD / 64, 64>(&tm_qkv64, &bars[DP_KV + s], smem + L::K + s * L::KV, k0, g.H + t.h, t.b);
+          tma_load_tile<HD / 64, 64>(&tm_qkv64, &bars[DP_KV + s], smem + L::V + s * L::KV, k0, 2 * g.H + t.h, t.b);
           issued_kv = jj + 1;
         }
       }
@@ -489,8 +489,8 @@ __global__ void __launch_bounds__(320, 1)
         if (gq >= NQS && !mbar_wait(&bars[KV_QDE + s], ((gq / NQS) - 1) & 1, abort, &g_fault_word)) return false;
         const int t0 = t.tfirst + i * BNQ;
         mbar_expect_tx(&bars[KV_QD + s], 2 * L::QTILE);
-        tma_load_tile(&tm_qkv64, &bars[KV_QD + s], smem + L::Q + s * L::QTILE, t0, t.h, t.b);
-        tma_load_tile(&tm_do64, &bars[KV_QD + s], smem + L::DO + s * L::QTILE, t0, t.h, t.b);
+        tma_load_tile<HD / 64, 64>(&tm_qkv64, &bars[KV_QD + s], smem + L::Q + s * L::QTILE, t0, t.h, t.b);
+        tma_load_tile<HD / 64, 64>(&tm_do64, &bars[KV_QD + s], smem + L::DO + s * L::QTILE, t0, t.h, t.b);
         issued_q = gq + 1;
         return true;
       };
@@ -500,8 +500,8 @@ __global__ void __launch_bounds__(320, 1)
         const int kb = n & 1;
         if (n >= 2 && !(ok = mbar_wait(&bars[KV_KVE + kb], ((n >> 1) - 1) & 1, abort, &g_fault_word))) break;
         mbar_expect_tx(&bars[KV_KV + kb], 2 * L::KTILE);
-        tma_load_tile(&tm_qkv128, &bars[KV_KV + kb], smem + kb * L::KV + L::K, t.k0, g.H + t.h, t.b);
-        tma_load_tile(&tm_qkv128, &bars[KV_KV + kb], smem + kb * L::KV + L::V, t.k0, 2 * g.H + t.h, t.b);
+        tma_load_tile<HD / 64, BM>(&tm_qkv128, &bars[KV_KV + kb], smem + kb * L::KV + L::K, t.k0, g.H + t.h, t.b);
+        tma_load_tile<HD / 64, BM>(&tm_qkv128, &bars[KV_KV + kb], smem + kb * L::KV + L::V, t.k0, 2 * g.H + t.h, t.b);
         issued_kv = n + 1;
         for (int i = 0; ok && i < t.nq; ++i) ok = load_qd(t, i);
         q += t.nq;

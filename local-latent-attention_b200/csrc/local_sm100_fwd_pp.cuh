@@ -171,20 +171,20 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
 #pragma unroll
         for (int x = 0; x < (PAIR ? 2 : 1); ++x) {
           uint8_t* xr = smem + L::X + x * L::XS;
-          mbar_expect_tx(&bars[PP_LW + x], HD * 128 + (lat_tma ? BM * 128 : 0) + (x == 0 ? 3 * HD * 4 : 0));
-          tma_load_2d(&tm_w, &bars[PP_LW + x], xr + BM * 128, 0, h * HD);
+          mbar_expect_tx(&bars[PP_LW + x], HD * 128 + (lat_tma ? BM * 128 : 0) + (x == 0 ? 3 * g.hd * 4 : 0));
+          tma_load_2d(&tm_w, &bars[PP_LW + x], xr + BM * 128, 0, h * g.hd);
           if (lat_tma) tma_load_3d(&tm_lat, &bars[PP_LW + x], xr, 0, q0 + x * BM, b);
         }
         float* cst = reinterpret_cast<float*>(smem + L::CST);
-        bulk_load(cst, ep.b_rout + (int64_t)h * HD, HD * 4, &bars[PP_LW + 0]);
-        bulk_load(cst + HD, ep.g_local, HD * 4, &bars[PP_LW + 0]);
-        bulk_load(cst + 2 * HD, ep.g_remote, HD * 4, &bars[PP_LW + 0]);
+        bulk_load(cst, ep.b_rout + (int64_t)h * g.hd, g.hd * 4, &bars[PP_LW + 0]);
+        bulk_load(cst + HD, ep.g_local, g.hd * 4, &bars[PP_LW + 0]);
+        bulk_load(cst + 2 * HD, ep.g_remote, g.hd * 4, &bars[PP_LW + 0]);
       };
       if (fuse && !L::X_OVER_Q) load_remote();
       if (nk > 0) {
         mbar_expect_tx(&bars[PP_Q], (PAIR ? 2 : 1) * L::QTILE);
-        tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QA, q0, h, b);
-        if (PAIR) tma_load_tile(&tm_q, &bars[PP_Q], smem + L::QB, q0 + BM, h, b);
+        tma_load_tile<HD / 64, BM>(&tm_q, &bars[PP_Q], smem + L::QA, q0, h, b);
+        if (PAIR) tma_load_tile<HD / 64, BM>(&tm_q, &bars[PP_Q], smem + L::QB, q0 + BM, h, b);
       }
       // K stages free once their tile's S MMAs are done, V stages once its
       // PV MMAs are: K tiles are issued one tile ahead of V tiles, so a K
@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
           return false;
         const int bar = (is_k ? PP_K : PP_V) + s;
         mbar_expect_tx(&bars[bar], L::KTILE);
-        tma_load_tile(&tm_kv, &bars[bar], smem + (is_k ? L::K : L::V) + s * L::KTILE, kbase + j * BNK,
+        tma_load_tile<HD / 64, BNK>(&tm_kv, &bars[bar], smem + (is_k ? L::K : L::V) + s * L::KTILE, kbase + j * BNK,
                       (is_k ? 1 : 2) * g.H + h, b);
         if (is_k) issued = j + 1; else issued_v = j + 1;
         return true;
@@ -366,6 +366,13 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
     // block-pooled latent queries: this row's lat row (token-wise ones and
     // W_rout come by TMA); with the operands over Q, after its S MMAs
     auto write_lat_rows = [&]() {
+      // padded head_dim: the per-column constants past hd are zero (the bulk
+      // copies bring hd of them), so padded columns add nothing to the logits
+      if (grp == 0 && row < HD - g.hd) {
+        cst[g.hd + row] = 0.f;
+        cst[HD + g.hd + row] = 0.f;
+        cst[2 * HD + g.hd + row] = 0.f;
+      }
       if (g.qbs != 1) {
         const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(ep.lat) +
                                                           ((int64_t)b * g.Tq + (valid ? t / g.qbs : 0)) * 64);
@@ -481,7 +488,7 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
         tc_fence_after();
         const int nk_here = n_mine;
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        bf16* dst = local_out + ((int64_t)b * g.T + (valid ? t : 0)) * g.d + (int64_t)h * HD;
+        bf16* dst = local_out + ((int64_t)b * g.T + (valid ? t : 0)) * g.d + (int64_t)h * g.hd;
         if (fuse) {
           // pass 1 over TMEM: gate logits of local = bf16(O / l) and
           // remote = R + b; pass 2: local (over this group's Q tile) and
@@ -551,8 +558,8 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
             if (mbar_wait(&bars[PP_EP + grp], 0, abort, &g_fault_word)) {
 #pragma unroll
               for (int p = 0; p < HD / 64; ++p) {
-                tma_store_3d(&tm_lo, ltile + p * (BM * 128), h * HD + p * 64, q0 + grp * BM, b);
-                tma_store_3d(&tm_mx, mtile + p * (BM * 128), h * HD + p * 64, q0 + grp * BM, b);
+                tma_store_4d(&tm_lo, ltile + p * (BM * 128), p * 64, h, q0 + grp * BM, b);
+                tma_store_4d(&tm_mx, mtile + p * (BM * 128), p * 64, h, q0 + grp * BM, b);
               }
               tma_store_commit();
               LLATTN_TRACE_K(1, 62 + grp);
@@ -579,8 +586,9 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
             if (valid) {
 #pragma unroll
               for (int q = 0; q < 4; ++q)
-                *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) =
-                    make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                if (cc * 32 + q * 8 < g.hd)  // padded head_dim: columns past hd are not stored
+                  *reinterpret_cast<uint4*>(dst + cc * 32 + q * 8) =
+                      make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
             }
           }
         }

@@ -66,6 +66,26 @@ cudaError_t launch_rout_dw(const Geom& g, const void* dr, const void* lat, float
                            int n_split, cudaStream_t s);
 cudaError_t launch_dlat_rowsum(const Geom& g, const float* dlat_tok, float* dlat, cudaStream_t s);
 
+// C[M, N] = A[M, K] B[N, K]^T on the tensor cores (bf16 operands, fp32
+// accumulation); a_mn / b_mn: operand stored [K, M] / [K, N] (MN-major)
+// instead of [M, K] / [N, K]; lda / ldb: row strides in elements (multiples
+// of 8). Output row m goes to row (m / rows_per_group) * group_stride +
+// (m % rows_per_group) * row_step of C (rows_per_group 0: plain rows). K is
+// split over `splits` CTAs along z, split z writing C + z * split_stride;
+// colsum (optional, fp32 [splits][M] at colsum_split apart) = sum_k A[m, k].
+struct GemmOut {
+  void* C;
+  int64_t ldc;
+  int out_bf16;
+  int64_t split_stride;
+  const float* bias;
+  int rows_per_group, group_stride, row_step;
+  float* colsum;
+  int64_t colsum_split;
+};
+cudaError_t launch_gemm(const Geom& g, int M, int N, int K, const void* A, int64_t lda, int a_mn, const void* B,
+                        int64_t ldb, int b_mn, const GemmOut& o, int splits, cudaStream_t s);
+
 // Reads (and optionally clears) the device fault word of the current device:
 // bits set by a tensor-core kernel whose bounded wait ran out.
 unsigned read_fault_word(bool reset);

@@ -110,20 +110,18 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* ba
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
-// One tile of `rows` token rows x hd columns in panel-major 128-byte-swizzled
-// layout (panel p = columns [64p, 64p+64) at p * rows * 128 bytes) from a 5-D
-// map (64, T, hd/64, slots*heads, B): one copy for all panels.
-__device__ __forceinline__ void tma_load_5d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1,
-                                            int c2, int c3, int c4) {
-  asm volatile(
-      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
-      : "memory");
-}
+// A tile of ROWS token rows x (64 NP) columns of one (slot, head) from a
+// 4-D map (hd, slots*heads, T, B) with box (64, 1, ROWS, 1): NP copies, panel
+// p (columns [64p, 64p + 64)) at p * ROWS * 128 bytes, the panel-major
+// 128-byte-swizzled layout the MMA descriptors expect. Columns at or past
+// the map's head_dim are zero-filled, so a head_dim between 64 and 128 (88,
+// 96, ...) runs as a 128-wide tile whose extra columns add nothing.
+template <int NP, int ROWS>
 __device__ __forceinline__ void tma_load_tile(const CUtensorMap* map, uint64_t* bar, void* dst, int row, int slot_head,
                                               int b) {
-  tma_load_5d(map, bar, dst, 0, row, 0, slot_head, b);
+#pragma unroll
+  for (int p = 0; p < NP; ++p)
+    tma_load_4d(map, bar, static_cast<uint8_t*>(dst) + p * ROWS * 128, 64 * p, slot_head, row, b);
 }
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1) {
   asm volatile(

@@ -86,6 +86,75 @@ BF16_CASES = [
 ]
 
 
+# latent widths the fused gate epilogue does not hold (the reference's
+# training presets use latent_d_model 512 / 384 with 8 latent heads,
+# train.py:71-92) and more than 32 heads: the general tensor-core path
+# (local kernels without the fused epilogue, remote / dlat / dW_rout on the
+# tensor-core GEMM, gate kernels on the precomputed remote rows).
+GENERAL_CASES = [
+    dict(B=2, T=700, d_model=256, n_heads=2, local_window=128, latent_tokens=32, latent_d_model=512,
+         latent_heads=8),
+    dict(B=1, T=1000, d_model=512, n_heads=4, local_window=256, latent_tokens=64, latent_d_model=384,
+         latent_heads=8),
+    dict(B=2, T=515, d_model=256, n_heads=4, local_window=64, latent_tokens=32, latent_d_model=128,
+         latent_heads=2, latent_query_block_size=64),
+    dict(B=1, T=1337, d_model=512, n_heads=4, local_window=300, local_block_size=200, latent_tokens=48,
+         latent_d_model=384, latent_heads=8, latent_query_block_size=16),
+    dict(B=1, T=600, d_model=40 * 64, n_heads=40, local_window=128, latent_tokens=16, latent_d_model=64,
+         latent_heads=2),
+    dict(B=2, T=333, d_model=256, n_heads=2, local_window=100, latent_tokens=16, latent_d_model=200,
+         latent_heads=4, latent_query_block_size=7),
+]
+
+
+# head_dim between 64 and 128 (the presets: 1408 / 16 = 88, 1536 / 16 = 96):
+# the tensor-core kernels run 128-wide tiles whose extra columns the copies
+# zero-fill and the stores clip
+PADDED_HD_CASES = [
+    dict(B=2, T=600, d_model=2 * 88, n_heads=2, local_window=128, latent_tokens=32, latent_d_model=64,
+         latent_heads=2),
+    dict(B=1, T=1000, d_model=4 * 96, n_heads=4, local_window=256, latent_tokens=64, latent_d_model=64,
+         latent_heads=2, latent_query_block_size=32),
+    dict(B=1, T=777, d_model=3 * 72, n_heads=3, local_window=300, local_block_size=200, latent_tokens=16,
+         latent_d_model=64, latent_heads=2),
+    dict(B=2, T=515, d_model=2 * 120, n_heads=2, local_window=64, latent_tokens=32, latent_d_model=128,
+         latent_heads=4),
+]
+
+
+@pytest.mark.parametrize("idx", range(len(PADDED_HD_CASES)))
+def test_block_bf16_padded_head_dim(idx):
+    print(_block_case(dict(PADDED_HD_CASES[idx]), oracle_dtype=torch.float32))
+
+
+# the reference's training presets (train.py:71-92) at full width, one
+# 2048-token sequence: 0.55b (d1408 H16 -> hd 88, latent 512 over 8 heads)
+# and 0.60b (d1536 H16 -> hd 96, latent 384 over 8 heads -> 48 per head)
+PRESETS = {
+    "0.55b": dict(B=1, T=2048, d_model=1408, n_heads=16, local_window=256, latent_tokens=64, latent_d_model=512,
+                  latent_heads=8),
+    "0.60b": dict(B=1, T=2048, d_model=1536, n_heads=16, local_window=256, latent_tokens=64, latent_d_model=384,
+                  latent_heads=8),
+}
+
+
+@pytest.mark.parametrize("name", sorted(PRESETS))
+def test_block_bf16_reference_presets(name):
+    print(_block_case(dict(PRESETS[name]), oracle_dtype=torch.float32))
+
+
+@pytest.mark.parametrize("idx", range(len(GENERAL_CASES)))
+def test_block_bf16_general_latent_width(idx):
+    print(_block_case(dict(GENERAL_CASES[idx]), oracle_dtype=torch.float32))
+
+
+@pytest.mark.parametrize("bias", [8.0, -8.0])
+def test_block_bf16_general_saturated_gate(bias):
+    dims = dict(B=2, T=600, d_model=256, n_heads=2, local_window=128, latent_tokens=32, latent_d_model=512,
+                latent_heads=8, latent_query_block_size=32)
+    print(_block_case(dims, gate_bias=bias, oracle_dtype=torch.float32))
+
+
 @pytest.mark.parametrize("idx", range(len(BF16_CASES)))
 def test_block_bf16_shapes(idx):
     dims = dict(BF16_CASES[idx])

@@ -57,6 +57,8 @@ FWD_CASES = [
     (2, 129, 2, 128, 16, 32),
     (1, 1, 1, 128, 4, 256),
     (1, 4096, 2, 128, 512, 256),
+    (1, 700, 2, 88, 256, 256),
+    (2, 333, 3, 96, 64, 128),
 ]
 
 
@@ -116,6 +118,8 @@ BWD_CASES = [
     (2, 129, 2, 128, 16, 32),
     (1, 1, 1, 128, 4, 256),
     (1, 4096, 2, 128, 512, 256),
+    (1, 700, 2, 88, 256, 256),
+    (2, 333, 3, 96, 64, 128),
 ]
 
 
