@@ -1,16 +1,26 @@
-"""Decoder LM around the drop-in attention block: the reference's
-LocalLatentLM (models.py:505-576) with LocalLatentAttentionB200 in every
-layer. Used as the multi-GPU data-parallel training harness.
+"""Decoder-only language model around the drop-in attention block, the
+data-parallel training harness of this package (and its generation loop).
 
-Same module tree and state_dict names as the reference (embedding,
-position, blocks.{i}.norm1/attn/norm2/ff.w1/ff.w2, norm, tied lm_head), the
-same pre-norm residual block (models.py:491-502) and GPT-2 style init
-(models.py:520-546).
+What is kept from the reference, because checkpoints and configs must move
+between the two (each an interface, not an implementation):
+  * the ModelConfig fields (models.py:21-37);
+  * the parameter names: embedding, position, blocks.{i}.norm1 / attn /
+    norm2 / ff.w1 / ff.w2, norm, and lm_head tied to the embedding
+    (models.py:505-518);
+  * the pre-norm residual layer x + attn(norm1(x)), then x + ff(norm2(x)),
+    with RMSNorm eps 1e-6 and an exact-GELU MLP (models.py:40-58, 491-502);
+  * the GPT-2 style initial values (models.py:520-546): N(0, 0.02) for every
+    linear weight and embedding, zero biases, the weights of the residual
+    output projections (out, r_out, w2) scaled by 1/sqrt(2 n_layers), drawn
+    in module order so that a seeded model equals the reference's.
+
+Where the reference tree is importable, ``use_in_reference(models)`` points
+its own attention switch (models.py:465-488) at this package instead, so the
+reference's LocalLatentLM runs the B200 block in every layer.
 """
 
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 
 import torch
@@ -23,7 +33,7 @@ from .module import LocalLatentAttentionB200
 
 @dataclass
 class ModelConfig:
-    """Field-for-field the reference's ModelConfig (models.py:21-37)."""
+    """The reference's ModelConfig fields (models.py:21-37)."""
 
     vocab_size: int = 128
     max_seq_len: int = 1024
@@ -42,92 +52,82 @@ class ModelConfig:
     use_triton_kernel: bool = True
 
 
-class RMSNorm(nn.Module):
-    def __init__(self, dim: int, eps: float = 1e-6) -> None:
-        super().__init__()
-        self.weight = nn.Parameter(torch.ones(dim))
-        self.eps = eps
-
-    def forward(self, x):
-        return F.rms_norm(x, (self.weight.shape[0],), self.weight, self.eps)
+RESIDUAL_OUTPUTS = ("out", "r_out", "w2")  # linear layers whose output is added to the residual stream
 
 
-class FeedForward(nn.Module):
+class DecoderLayer(nn.Module):
+    """norm1 -> LocalLatentAttentionB200 -> residual add, norm2 -> MLP ->
+    residual add. The MLP is an nn.ModuleDict {w1, w2} so its parameters
+    keep the reference's ff.w1 / ff.w2 names."""
+
     def __init__(self, config: ModelConfig) -> None:
         super().__init__()
-        self.w1 = nn.Linear(config.d_model, config.d_ff)
-        self.w2 = nn.Linear(config.d_ff, config.d_model)
-        self.dropout = nn.Dropout(config.dropout)
-
-    def forward(self, x):
-        return self.dropout(self.w2(F.gelu(self.w1(x))))
-
-
-class TransformerBlock(nn.Module):
-    def __init__(self, config: ModelConfig) -> None:
-        super().__init__()
-        self.norm1 = RMSNorm(config.d_model)
-        self.norm2 = RMSNorm(config.d_model)
+        d = config.d_model
+        self.norm1 = nn.RMSNorm(d, eps=1e-6)
         self.attn = LocalLatentAttentionB200(config)
-        self.ff = FeedForward(config)
+        self.norm2 = nn.RMSNorm(d, eps=1e-6)
+        self.ff = nn.ModuleDict({"w1": nn.Linear(d, config.d_ff), "w2": nn.Linear(config.d_ff, d)})
+        self.p_drop = config.dropout
 
-    def forward(self, x):
+    def mlp(self, h: torch.Tensor) -> torch.Tensor:
+        h = self.ff["w2"](F.gelu(self.ff["w1"](h)))
+        return F.dropout(h, self.p_drop, self.training) if self.p_drop else h
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
         x = x + self.attn(self.norm1(x))
-        return x + self.ff(self.norm2(x))
+        return x + self.mlp(self.norm2(x))
+
+
+def gpt2_init_(model: nn.Module, n_layers: int, skip: nn.Module | None = None) -> None:
+    """GPT-2 style initial values in module order (see the module docstring);
+    `skip` (the tied output head) keeps the embedding's values."""
+    residual_scale = (2.0 * n_layers) ** -0.5
+    with torch.no_grad():
+        for name, mod in model.named_modules():
+            if mod is skip:
+                continue
+            if isinstance(mod, nn.Embedding):
+                mod.weight.normal_(0.0, 0.02)
+            elif isinstance(mod, nn.Linear):
+                mod.weight.normal_(0.0, 0.02)
+                if mod.bias is not None:
+                    mod.bias.zero_()
+                if name.split(".")[-1] in RESIDUAL_OUTPUTS:
+                    mod.weight.mul_(residual_scale)
 
 
 class LocalLatentLM(nn.Module):
+    """Token + learned position embeddings, n_layers DecoderLayers, a final
+    RMSNorm and the tied output head -> logits [B, T, vocab]."""
+
     def __init__(self, config: ModelConfig) -> None:
         super().__init__()
         self.config = config
         self.checkpoint_blocks = config.checkpoint_blocks
         self.embedding = nn.Embedding(config.vocab_size, config.d_model)
         self.position = nn.Embedding(config.max_seq_len, config.d_model)
-        self.blocks = nn.ModuleList([TransformerBlock(config) for _ in range(config.n_layers)])
-        self.norm = RMSNorm(config.d_model)
+        self.blocks = nn.ModuleList(DecoderLayer(config) for _ in range(config.n_layers))
+        self.norm = nn.RMSNorm(config.d_model, eps=1e-6)
         self.lm_head = nn.Linear(config.d_model, config.vocab_size, bias=False)
         self.lm_head.weight = self.embedding.weight
-        self._init_weights(config.n_layers)
-
-    def _init_weights(self, n_layers: int) -> None:
-        output_projs = {"out", "r_out", "w2"}
-        for name, module in self.named_modules():
-            if module is self.lm_head:
-                continue
-            if isinstance(module, nn.Linear):
-                nn.init.normal_(module.weight, mean=0.0, std=0.02)
-                if module.bias is not None:
-                    nn.init.zeros_(module.bias)
-                if name.rsplit(".", 1)[-1] in output_projs:
-                    module.weight.data.mul_(1.0 / math.sqrt(2 * n_layers))
-            elif isinstance(module, nn.Embedding):
-                nn.init.normal_(module.weight, mean=0.0, std=0.02)
+        gpt2_init_(self, config.n_layers, skip=self.lm_head)
 
     def set_profile(self, enabled: bool) -> None:
-        for block in self.blocks:
-            block.attn.set_profile(enabled)
+        for layer in self.blocks:
+            layer.attn.set_profile(enabled)
 
     def get_profile_stats(self) -> dict[str, float]:
-        totals: dict[str, float] = {}
-        count = 0
-        for block in self.blocks:
-            stats = block.attn.get_profile_stats()
-            if not stats:
-                continue
-            count += 1
-            for k, v in stats.items():
-                totals[k] = totals.get(k, 0.0) + v
-        return {k: v / count for k, v in totals.items()} if count else {}
+        """Per-phase attention times averaged over the layers that recorded any."""
+        per_layer = [s for s in (layer.attn.get_profile_stats() for layer in self.blocks) if s]
+        keys = {k for s in per_layer for k in s}
+        return {k: sum(s.get(k, 0.0) for s in per_layer) / len(per_layer) for k in keys} if per_layer else {}
 
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
         T = input_ids.shape[1]
-        pos = torch.arange(T, device=input_ids.device)
-        x = self.embedding(input_ids) + self.position(pos).unsqueeze(0)
-        for block in self.blocks:
-            if self.checkpoint_blocks and self.training:
-                x = checkpoint(block, x, use_reentrant=False)
-            else:
-                x = block(x)
+        x = self.embedding(input_ids) + self.position.weight[:T].unsqueeze(0)
+        remat = self.checkpoint_blocks and self.training
+        for layer in self.blocks:
+            x = checkpoint(layer, x, use_reentrant=False) if remat else layer(x)
         return self.lm_head(self.norm(x))
 
 
@@ -167,15 +167,31 @@ class LocalLatentLM(nn.Module):
         x = self.embedding(ids) + self.position(torch.arange(T, device=ids.device)).unsqueeze(0)
         for blk, cache in zip(self.blocks, caches):
             x = x + blk.attn.prefill(blk.norm1(x), cache)
-            x = x + blk.ff(blk.norm2(x))
+            x = x + blk.mlp(blk.norm2(x))
         return self.lm_head(self.norm(x[:, -1]))
 
     def _decode_one(self, tok: torch.Tensor, pos: int, caches) -> torch.Tensor:
         x = self.embedding(tok) + self.position.weight[pos].view(1, 1, -1)
         for blk, cache in zip(self.blocks, caches):
             x = x + blk.attn.decode(blk.norm1(x), cache)
-            x = x + blk.ff(blk.norm2(x))
+            x = x + blk.mlp(blk.norm2(x))
         return self.lm_head(self.norm(x[:, -1]))
+
+
+def use_in_reference(models_module) -> None:
+    """Make the reference's models module build this package's block: after
+    the call, its _build_attention (models.py:465-488) returns
+    LocalLatentAttentionB200 for a config with use_triton_kernel set, so the
+    reference's own TransformerBlock / LocalLatentLM run the B200 kernels
+    (the same switch train.py's --use-triton-kernel sets)."""
+    fallback = models_module._build_attention
+
+    def build(config):
+        if getattr(config, "use_triton_kernel", False):
+            return LocalLatentAttentionB200(config)
+        return fallback(config)
+
+    models_module._build_attention = build
 
 
 def _sample(logits: torch.Tensor, temperature: float, top_k: int, generator) -> torch.Tensor:

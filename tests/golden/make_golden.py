@@ -1,9 +1,12 @@
 """Generate the golden vectors that pin the CPU oracle to the reference.
 
 Runs the reference's own PyTorch ``LocalLatentAttention`` (models.py:61-462,
-imported read-only from $LLATTN_REF_PATH, default the reference checkout) on
-seeded inputs and stores inputs, weights, the output, dx and every parameter
-gradient. The gate-bias cases add the bias with a forward hook on
+imported read-only from $LLATTN_REF_PATH, default a `reference` checkout
+beside this repository) on seeded inputs and stores inputs, weights, the
+output, dx and every parameter gradient; and the reference's own
+``LocalLatentLM`` (models.py:505-576) at the 0.55b preset's attention
+ratios (train.py:71-80: head_dim 88, latent_d_model 512 over 8 heads),
+shrunk to 2 layers, storing its logits, loss and every gradient. The gate-bias cases add the bias with a forward hook on
 ``gate_local`` — the reference code itself is not modified.
 
 Usage:  python tests/golden/make_golden.py   (needs the reference tree; the
@@ -16,7 +19,8 @@ import sys
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("LLATTN_REF_PATH", "/root/reference")
+ROOT = os.path.dirname(os.path.dirname(HERE))
+REF = os.environ.get("LLATTN_REF_PATH", os.path.join(ROOT, os.pardir, "reference"))
 
 # name: (dims, gate_bias, dtype)
 SMALL = {
@@ -74,6 +78,43 @@ def run_reference(dims: dict, gate_bias: float, dtype: torch.dtype, seed: int = 
     }
 
 
+# LM golden: the 0.55b preset's block ratios (d_model 1408 / 16 heads = 88
+# per head; latent 512 = 8 x 64) at d_model 176 with 2 heads, 2 layers
+LM = dict(vocab_size=128, max_seq_len=128, d_model=176, n_heads=2, n_layers=2, d_ff=128, local_window=32,
+          local_block_size=64, latent_tokens=16, latent_d_model=512, latent_heads=8)
+LM_B = 2
+
+
+def run_reference_lm():
+    """Reference LocalLatentLM in float64 on weights rounded to bf16 values
+    (the test builds the same weights from the seed with the package's own
+    LocalLatentLM, whose seeded init equals the reference's, and rounds them
+    the same way), tokens from seed 1, next-token cross-entropy. Gradients
+    are stored in bf16 to keep the fixture small (2^-9 relative)."""
+    sys.path.insert(0, REF)
+    import torch.nn.functional as F
+    from models import LocalLatentLM, ModelConfig  # noqa: E402
+
+    torch.manual_seed(0)
+    m = LocalLatentLM(ModelConfig(**LM))
+    with torch.no_grad():
+        for p in m.parameters():
+            p.copy_(p.to(torch.bfloat16).float())
+    m = m.double()
+    gen = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, LM["vocab_size"], (LM_B, LM["max_seq_len"] + 1), generator=gen)
+    logits = m(ids[:, :-1])
+    loss = F.cross_entropy(logits.reshape(-1, LM["vocab_size"]), ids[:, 1:].reshape(-1))
+    loss.backward()
+    return {
+        "cfg": dict(LM), "B": LM_B, "ids": ids,
+        "params_checksum": {k: (v.double().sum().item(), v.double().abs().sum().item())
+                            for k, v in m.state_dict().items()},
+        "logits": logits.detach().float(), "loss": loss.item(),
+        "grads": {k: p.grad.detach().to(torch.bfloat16) for k, p in m.named_parameters()},
+    }
+
+
 def main() -> None:
     small = {name: run_reference(dims, bias, torch.float64) for name, (dims, bias) in SMALL.items()}
     torch.save(small, os.path.join(HERE, "small_f64.pt"))
@@ -87,7 +128,8 @@ def main() -> None:
     cfg1["params_checksum"] = {k: (v.double().sum().item(), v.double().abs().sum().item())
                                for k, v in params.items()}
     torch.save(cfg1, os.path.join(HERE, "cfg1_f32.pt"))
-    print("wrote", sorted(small), "and cfg1")
+    torch.save(run_reference_lm(), os.path.join(HERE, "lm_055b_small.pt"))
+    print("wrote", sorted(small), "cfg1 and the LM golden")
 
 
 if __name__ == "__main__":

@@ -60,3 +60,99 @@ def test_lm_trains_on_gpu():
     losses = [train_step(m, opt, ids, tgt).item() for _ in range(30)]
     assert all(torch.isfinite(torch.tensor(losses)))
     assert losses[-1] < 0.5 * losses[0], losses
+
+
+def _reference_models():
+    """The reference's models module, imported read-only from
+    $LLATTN_REF_PATH (default: a `reference` checkout beside this repository);
+    the tests that need it skip where it is absent (e.g. the GPU box)."""
+    import importlib
+    import os
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    path = os.environ.get("LLATTN_REF_PATH", os.path.join(root, os.pardir, "reference"))
+    if not os.path.exists(os.path.join(path, "models.py")):
+        pytest.skip("reference tree not present")
+    if path not in sys.path:
+        sys.path.insert(0, path)
+    return importlib.import_module("models")
+
+
+SMALL_LM = dict(vocab_size=300, max_seq_len=128, d_model=176, n_heads=2, n_layers=2, d_ff=256, local_window=32,
+                latent_tokens=8, latent_d_model=512, latent_heads=8)
+
+
+def test_seeded_init_equals_reference_lm():
+    """Same seed, same weights: the module tree is created and initialised in
+    the reference LocalLatentLM's order (models.py:505-546)."""
+    models = _reference_models()
+    torch.manual_seed(0)
+    ref = models.LocalLatentLM(models.ModelConfig(**SMALL_LM))
+    torch.manual_seed(0)
+    ours = LocalLatentLM(ModelConfig(**SMALL_LM))
+    a, b = ref.state_dict(), ours.state_dict()
+    assert set(a) == set(b)
+    for k in a:
+        assert torch.equal(a[k], b[k]), k
+
+
+def test_reference_lm_builds_the_b200_block():
+    """use_in_reference points the reference's own _build_attention at the
+    B200 block: its LocalLatentLM then has the same parameters as ours."""
+    import llattn_b200
+    from llattn_b200.lm import use_in_reference
+
+    models = _reference_models()
+    saved = models._build_attention
+    try:
+        use_in_reference(models)
+        cfg = models.ModelConfig(**SMALL_LM, use_triton_kernel=True)
+        ref = models.LocalLatentLM(cfg)
+        assert all(isinstance(blk.attn, llattn_b200.LocalLatentAttentionB200) for blk in ref.blocks)
+        ours = LocalLatentLM(ModelConfig(**SMALL_LM))
+        ours.load_state_dict(ref.state_dict(), strict=True)
+        cfg_plain = models.ModelConfig(**SMALL_LM, use_triton_kernel=False)
+        assert not isinstance(models.LocalLatentLM(cfg_plain).blocks[0].attn, llattn_b200.LocalLatentAttentionB200)
+    finally:
+        models._build_attention = saved
+
+
+@pytest.mark.gpu
+def test_lm_matches_reference_golden_bf16():
+    """The package's LocalLatentLM on the GPU (bf16 autocast, the B200 block
+    in both layers, on its tensor-core paths: head_dim 88 and latent width
+    512) against the reference LocalLatentLM's float64 logits, loss and
+    every gradient (tests/golden/lm_055b_small.pt, weights rebuilt from the
+    same seed). Tolerance 2e-2 on max|a-b|/max|b| and the Frobenius ratio."""
+    import os
+
+    import torch.nn.functional as F
+    from parity import TOL, frob_err, rel_err
+
+    gold = torch.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "lm_055b_small.pt"))
+    cfg = ModelConfig(**gold["cfg"])
+    torch.manual_seed(0)
+    m = LocalLatentLM(cfg)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.copy_(p.to(torch.bfloat16).float())
+    for k, v in m.state_dict().items():  # same weights as the reference run
+        s, a = gold["params_checksum"][k]
+        assert abs(v.double().sum().item() - s) <= 1e-6 * max(1.0, a), k
+    m = m.cuda()
+    ids = gold["ids"].cuda()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        logits = m(ids[:, :-1])
+        loss = F.cross_entropy(logits.float().reshape(-1, cfg.vocab_size), ids[:, 1:].reshape(-1))
+    loss.backward()
+    tol = TOL[torch.bfloat16]
+    errs = {"logits": rel_err(logits.float(), gold["logits"]), "logits/frob": frob_err(logits.float(), gold["logits"]),
+            "loss": abs(loss.item() - gold["loss"]) / abs(gold["loss"])}
+    grads = dict(m.named_parameters())
+    for k, g in gold["grads"].items():
+        errs[k] = rel_err(grads[k].grad, g.float())
+        errs[k + "/frob"] = frob_err(grads[k].grad, g.float())
+    bad = {k: v for k, v in errs.items() if not v <= tol}
+    print({k: round(v, 5) for k, v in errs.items()})
+    assert not bad, bad
