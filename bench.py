@@ -1,7 +1,8 @@
 """Benchmark of the LocalLatentAttention block on B200 (one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config cfg2|cfg3|cfg1] [--no-cpu-baseline]
+                    [--config cfg2|cfg3|cfg1|p055|p060] [--no-cpu-baseline]
+                    [--no-lm] [--no-presets] [--lm-steps S]
 
 A step is one forward + backward of the drop-in block (LocalLatentAttentionB200:
 cuBLAS projections + the libllattn kernels) over one batch of the configured
@@ -9,26 +10,38 @@ shape, bf16, with a seeded synthetic input and upstream gradient. Default
 workload: cfg2 (B16 T2048 d1536 H12 W256 Nl64 Ld64 Lh2, token-wise latent
 queries). Under torchrun each rank runs its own batch (weak scaling) and
 all-reduces the block's parameter gradients with NCCL (all_reduce_mean), the
-data-parallel exchange of the reference's DDP training.
+data-parallel exchange of the reference's DDP training. `value` is the whole
+job's tokens/s (all ranks); `value_per_gpu` divides it by the GPU count.
 
 Keys beyond the base contract:
   e2e           same metric through the public module API with the step's
                 inputs (x, upstream grad) copied from pinned host memory and
-                dx copied back, inside the timed region
+                dx copied back, inside the timed region; copy_ms_per_step is
+                the same copies alone on the same streams (all ranks at
+                once), the host-link bound of the e2e figure
+  sustained     the same step repeated for >= 2 s of device time, with its
+                own clock samples (the K-step figure is a burst)
   roofline      dominant kernel: its algorithmic FLOPs (local branch: 4*hd*P
                 per launch, P = visible query/key pairs) and bytes per launch;
                 the bound is the roof whose ideal time is longer; achieved =
-                that amount over the kernel's CUDA-event time in the timed
-                region, against MEASURED_PEAKS.json; traffic = DRAM bytes per
-                launch from the committed full-size ncu capture
+                that amount over the kernel's CUDA-event time, against
+                MEASURED_PEAKS.json; traffic = DRAM bytes per launch from the
+                committed ncu capture (profiles/traffic.json)
+  local_branch  local fwd + bwd kernels against the dense-bf16 peak
   cpu_baseline  the CPU oracle (a restatement of the reference PyTorch block)
                 on the host cores, bounded sample
   kernels       per-kernel-group event times (ms per step) and launch counts
+  presets       the block at the reference's training presets (train.py:71-92:
+                0.55b d1408 H16 hd88 latent 512/8 heads, 0.60b d1536 H16 hd96
+                latent 384/8 heads) at B16 x T2048, with their kernel groups
+  lm            cfg4: the LocalLatentLM training step (24 layers, d1536, B16 x
+                T2048 per GPU, AdamW, DDP) at the same N, its own e2e
   clocks        nvidia-smi samples taken during the timed region
 
---impl reference times the reference's CPU implementation of the path (the
-oracle port of models.py's LocalLatentAttention, autocast bf16, all host
-threads) on a bounded sample; under torchrun only rank 0 runs it.
+--impl reference times the reference's CPU implementation of the path on a
+bounded sample: its own LocalLatentAttention (models.py) when the reference
+is installed in baseline/_ref, else the oracle port; under torchrun only rank
+0 runs it.
 """
 
 from __future__ import annotations
@@ -52,8 +65,14 @@ CONFIGS = {
                  latent_tokens=64, latent_d_model=64, latent_heads=2, latent_query_block_size=0),
     "cfg3": dict(B=2, T=16384, d_model=1024, n_heads=8, local_window=512, local_block_size=256,
                  latent_tokens=256, latent_d_model=64, latent_heads=2, latent_query_block_size=64),
+    # the block of the reference's training presets (train.py:71-92) at the cfg2 batch
+    "p055": dict(B=16, T=2048, d_model=1408, n_heads=16, local_window=256, local_block_size=256,
+                 latent_tokens=64, latent_d_model=512, latent_heads=8, latent_query_block_size=0),
+    "p060": dict(B=16, T=2048, d_model=1536, n_heads=16, local_window=256, local_block_size=256,
+                 latent_tokens=64, latent_d_model=384, latent_heads=8, latent_query_block_size=0),
 }
-METRIC = "llattn fwd+bwd tokens/s/GPU (bf16, T=2048)"
+METRIC = "llattn fwd+bwd tokens/s, whole job over n_gpus (bf16, T=2048)"
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
 
 def parse():
@@ -69,6 +88,10 @@ def parse():
     p.add_argument("--workload", default="block", choices=["block", "lm", "decode"],
                    help="block: the attention block fwd+bwd (default); lm: cfg4 LM training step")
     p.add_argument("--layers", type=int, default=24, help="lm: decoder layers (cfg4: 24)")
+    p.add_argument("--lm-steps", type=int, default=10, help="timed steps of the LM object in the block run")
+    p.add_argument("--no-lm", action="store_true", help="leave the cfg4 LM measurement out of the block run")
+    p.add_argument("--no-presets", action="store_true", help="leave the preset-shape block points out")
+    p.add_argument("--sustain-seconds", type=float, default=2.0)
     return p.parse_args()
 
 
@@ -107,26 +130,56 @@ def config_json(name, n_gpus):
 # ---------------------------------------------------------------------------
 # CPU legs (oracle = restatement of the reference PyTorch block)
 
-def cpu_time_block(name, seconds, steps=None, warmup=1):
-    import torch
+def reference_models():
+    """The reference's own models module if it is installed in baseline/_ref
+    (the reference tree has no setup.py / pyproject, so `pip install --target`
+    cannot install it; __graft_entry__.build() places its unmodified models.py
+    there instead), else None."""
+    path = os.path.join(REF_DIR, "models.py")
+    if not os.path.exists(path):
+        return None
+    import importlib.util
 
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import llattn_oracle as O
+    spec = importlib.util.spec_from_file_location("llattn_reference_models", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def cpu_time_block(name, seconds, steps=None, warmup=1):
+    """Median time of one fwd+bwd of one sequence of the config on the host
+    cores (autocast bf16, all threads): the reference's own module when
+    installed, else the oracle restatement of it."""
+    import torch
 
     fields = {k: v for k, v in CONFIGS[name].items() if k not in ("B", "T")}
     T = CONFIGS[name]["T"]
-    cfg = O.BlockCfg(**fields)
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     Bs = 1  # bounded sample: one sequence of the workload per iteration
-    params = {k: v.requires_grad_(True) for k, v in O.init_params(cfg, 0).items()}
+    ref = reference_models()
+    torch.manual_seed(0)
+    if ref is not None:
+        kind = "reference"
+        m = ref.LocalLatentAttention(ref.ModelConfig(**fields))
+        fwd = m
+        what = "the reference's own models.py LocalLatentAttention"
+    else:
+        kind = "port"
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import llattn_oracle as O
+
+        cfg = O.BlockCfg(**fields)
+        params = {k: v.requires_grad_(True) for k, v in O.init_params(cfg, 0).items()}
+        fwd = lambda xx: O.block_forward(params, xx, cfg)  # noqa: E731
+        what = "oracle restatement of models.py LocalLatentAttention"
     gen = torch.Generator().manual_seed(1)
-    x = torch.randn(Bs, T, cfg.d_model, generator=gen).requires_grad_(True)
-    g = torch.randn(Bs, T, cfg.d_model, generator=gen)
+    x = torch.randn(Bs, T, fields["d_model"], generator=gen).requires_grad_(True)
+    g = torch.randn(Bs, T, fields["d_model"], generator=gen)
 
     def one():
         with torch.autocast("cpu", dtype=torch.bfloat16):
-            y = O.block_forward(params, x, cfg)
+            y = fwd(x)
         y.float().backward(g)
 
     for _ in range(warmup):
@@ -142,16 +195,16 @@ def cpu_time_block(name, seconds, steps=None, warmup=1):
         if steps is None and time.perf_counter() - t_start > seconds and len(times) >= 2:
             break
     per = statistics.median(times)
-    sample = (f"{len(times)} iterations of 1 x {T}-token sequence of {name} (oracle restatement of "
-              f"models.py LocalLatentAttention, autocast bf16, fwd+bwd), median")
-    return Bs * T / per, threads, sample, per
+    sample = (f"{len(times)} iterations of 1 x {T}-token sequence of {name} ({what}, autocast bf16, "
+              f"fwd+bwd), median")
+    return Bs * T / per, threads, sample, per, kind
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    tok_s, threads, sample, per = cpu_time_block(args.config, 0, steps=args.steps, warmup=args.warmup)
+    tok_s, threads, sample, per, kind = cpu_time_block(args.config, 0, steps=args.steps, warmup=args.warmup)
     import platform
 
     cpu = platform.processor() or "cpu"
@@ -169,7 +222,7 @@ def run_reference(args):
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded randn)",
            "config": config_json(args.config, 1),
            "cpu_baseline": {"value": round(tok_s, 1), "unit": "tokens/s", "cores": threads,
-                            "kind": "port", "sample": sample, "cpu": cpu},
+                            "kind": kind, "sample": sample, "cpu": cpu},
            "e2e": {"value": round(tok_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
@@ -371,13 +424,67 @@ def run_ours(args):
     ms_e2e = e2e_run(args.steps)
     barrier()
 
-    t = torch.tensor([ms, ms_e2e], device=dev, dtype=torch.float64)
+    # the e2e step's copies alone (H2D of x and the upstream grad, D2H of a
+    # dx-sized buffer, on the same two streams, every rank at once): the
+    # host-link bound of the e2e figure
+    def copy_run(n):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(comp)
+        h2d.wait_event(start)
+        d2h.wait_event(start)
+        for i in range(n):
+            k = i % 2
+            with torch.cuda.stream(h2d):
+                xs[k].data.copy_(x_h, non_blocking=True)
+                gs[k].copy_(g_h, non_blocking=True)
+            with torch.cuda.stream(d2h):
+                dxh[k].copy_(gs[1 - k], non_blocking=True)
+        ev_in[0].record(h2d)
+        ev_out[0].record(d2h)
+        comp.wait_event(ev_in[0])
+        comp.wait_event(ev_out[0])
+        end.record(comp)
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / n
+
+    copy_run(2)
+    barrier()
+    ms_copy = copy_run(args.steps)
+    barrier()
+
+    # sustained: the same step repeated for >= sustain_seconds of device time
+    n_sus = max(args.steps, min(20000, math.ceil(args.sustain_seconds * 1e3 / max(ms, 1e-3))))
+    clocks_sus = ClockSampler(local)
+    clocks_sus.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(n_sus):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk_sus = clocks_sus.stop()
+    ms_sus = e0.elapsed_time(e1) / n_sus
+
+    t = torch.tensor([ms, ms_e2e, ms_copy, ms_sus], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e = t.tolist()
+    ms, ms_e2e, ms_copy, ms_sus = t.tolist()
     tokens = B * T * world
     value = tokens / (ms / 1e3)
     e2e_value = tokens / (ms_e2e / 1e3)
+
+    presets = None
+    if rank == 0 and not args.no_presets and args.config in ("cfg2",):
+        presets = {name: measure_block_point(name, dev, args.steps) for name in ("p055", "p060")}
+    barrier()
+    del m, params, x, g, xs, gs, flat
+    torch.cuda.empty_cache()
+    lm = None
+    if not args.no_lm and args.config == "cfg2":
+        lm = measure_lm(args, world, rank, dev)
 
     if rank != 0:
         if world > 1:
@@ -438,39 +545,108 @@ def run_ours(args):
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        tok_s, threads, sample, _ = cpu_time_block(args.config, args.cpu_seconds)
-        cpu = {"value": round(tok_s, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+        tok_s, threads, sample, _, kind = cpu_time_block(args.config, args.cpu_seconds)
+        cpu = {"value": round(tok_s, 1), "unit": "tokens/s", "cores": threads, "kind": kind,
                "sample": sample}
 
     launches = int(sum(v[1] for v in kern.values()))
     out = {
-        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "metric": METRIC, "value": round(value, 1), "value_per_gpu": round(value / world, 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded randn inputs and upstream grad; reference default init)",
         "config": config_json(args.config, world),
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": 2 * x_h.numel() * 2, "d2h_bytes_per_step": dx_h.numel() * 2,
-                "ms_per_step": round(ms_e2e, 4)},
+                "ms_per_step": round(ms_e2e, 4), "copy_ms_per_step": round(ms_copy, 4),
+                "copy_bound_frac": round(ms_copy / ms_e2e, 4)},
+        "sustained": {"steps": n_sus, "seconds": round(ms_sus * n_sus / 1e3, 3), "ms_per_step": round(ms_sus, 4),
+                      "value": round(tokens / (ms_sus / 1e3), 1), "clocks": clk_sus},
         "roofline": roof,
         "local_branch": local_branch,
         "cpu_baseline": cpu,
         "gpu_launches": launches,
         "kernels": {k: {"ms_per_step": round(v[0], 4), "launches_per_step": v[1]} for k, v in per_step.items()},
         "clocks": clk,
+        "presets": presets,
+        "lm": lm,
     }
     print(json.dumps(out), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
+def measure_block_point(name, dev, steps, warmup=3):
+    """One GPU's block fwd+bwd at a config (no gradient exchange): K steps
+    timed with CUDA events, then a profiled pass for the kernel groups.
+    local_backward names the local-branch backward that ran: tcgen05 (the
+    dq / dk,dv tensor-core kernels) or simt."""
+    import torch
+
+    from llattn_b200 import _lib
+
+    B, T, cfg = block_cfg(name)
+    m = seeded_module(cfg, dev)
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(B, T, cfg.d_model, generator=gen).to(device=dev, dtype=torch.bfloat16).requires_grad_(True)
+    g = torch.randn(B, T, cfg.d_model, generator=gen).to(device=dev, dtype=torch.bfloat16)
+
+    def step():
+        x.grad = None
+        for p in m.parameters():
+            p.grad = None
+        m(x).backward(g)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    _lib.profile_enable(True)
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize()
+    kern = _lib.profile_read()
+    _lib.profile_enable(False)
+    c = CONFIGS[name]
+    return {"config": {k: c[k] for k in ("B", "T", "d_model", "n_heads", "latent_d_model", "latent_heads")},
+            "head_dim": c["d_model"] // c["n_heads"], "ms_per_step": round(ms, 4),
+            "value": round(B * T / (ms / 1e3), 1), "unit": "tokens/s",
+            "local_backward": "tcgen05" if kern.get("local_dq", (0, 0))[1] > 0 and kern.get("local_bwd", (0, 0))[1] == 0
+            else "simt",
+            "kernels": {k: {"ms_per_step": round(v[0] / steps, 4), "launches_per_step": v[1] / steps}
+                        for k, v in kern.items() if v[1] > 0}}
+
+
 LM_METRIC = "LM train tok/s (bf16, T=2048, cfg4 0.55B-class, AdamW, DDP)"
 
 
 def run_lm(args):
+    """--workload lm: the cfg4 LM training step alone, as its own JSON line."""
+    import torch
+
+    from llattn_b200 import dist as D
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    device = D.setup_distributed("nccl") if world > 1 else torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    out = measure_lm(args, world, D.get_rank(), device, steps=args.steps)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+    D.cleanup_distributed()
+
+
+def measure_lm(args, world, rank, device, steps=None):
     """cfg4: LocalLatentLM (24 x d1536 H12 W256 Nl64 Ld64, d_ff 4096, V32000,
     tied embeddings), B16 x T2048 per GPU, bf16 autocast, fused AdamW, DDP
-    gradient all-reduce over NCCL (bucketed, overlapping the backward)."""
+    gradient all-reduce over NCCL (bucketed, overlapping the backward; the
+    process group must exist when world > 1). Returns the measurement on
+    rank 0, None elsewhere."""
     import torch
     import torch.distributed as dist
 
@@ -479,11 +655,9 @@ def run_lm(args):
     from llattn_b200 import dist as D
     from llattn_b200.lm import LocalLatentLM, ModelConfig, build_optimizer, train_step
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    device = D.setup_distributed("nccl") if world > 1 else torch.device("cuda", 0)
-    torch.cuda.set_device(device)
-    rank = D.get_rank()
-    B = args.batch or 16
+    steps = steps or args.lm_steps
+    warmup = max(3, min(args.warmup, 5))
+    B = (args.batch if args.workload == "lm" else 0) or 16
     T = 2048
     cfg = ModelConfig(vocab_size=32000, max_seq_len=T, d_model=1536, n_heads=12, n_layers=args.layers, d_ff=4096,
                       local_window=256, latent_tokens=64, latent_d_model=64, latent_heads=2)
@@ -498,8 +672,7 @@ def run_lm(args):
     data_h = torch.randint(0, cfg.vocab_size, (B, T + 1), generator=gen, dtype=torch.int64).pin_memory()
     data = data_h.to(device)
     ids, tgt = data[:, :-1].contiguous(), data[:, 1:].contiguous()
-
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         train_step(model, opt, ids, tgt)
     torch.cuda.synchronize()
     D.barrier()
@@ -508,16 +681,16 @@ def run_lm(args):
     time.sleep(0.3)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         loss = train_step(model, opt, ids, tgt)
     e1.record()
     torch.cuda.synchronize()
     D.barrier()
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = e0.elapsed_time(e1) / steps
     # per-kernel times from a separate profiled pass (the profiler's events cost time)
     _lib.profile_enable(True)
-    for _ in range(args.steps):
+    for _ in range(steps):
         train_step(model, opt, ids, tgt)
     torch.cuda.synchronize()
     D.barrier()
@@ -527,13 +700,13 @@ def run_lm(args):
     loss_h = torch.empty((), dtype=torch.float32).pin_memory()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         data.copy_(data_h, non_blocking=True)
         loss = train_step(model, opt, data[:, :-1], data[:, 1:])
         loss_h.copy_(loss, non_blocking=True)
     e3.record()
     torch.cuda.synchronize()
-    ms_e2e = e2.elapsed_time(e3) / args.steps
+    ms_e2e = e2.elapsed_time(e3) / steps
     t = torch.tensor([ms, ms_e2e], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -550,10 +723,11 @@ def run_lm(args):
         n_nonemb = n_params - cfg.vocab_size * cfg.d_model - T * cfg.d_model
         flops_tok = 6 * n_nonemb + 6 * cfg.vocab_size * cfg.d_model
         ach = flops_tok * tokens / (ms / 1e3) / 1e12
-        per_step = {k: (v[0] / args.steps, v[1] / args.steps) for k, v in kern.items() if v[1] > 0}
+        per_step = {k: (v[0] / steps, v[1] / steps) for k, v in kern.items() if v[1] > 0}
         out = {
-            "metric": LM_METRIC, "value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "metric": LM_METRIC, "value": round(tokens / (ms / 1e3), 1),
+            "value_per_gpu": round(tokens / world / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded uniform tokens in [0, 32000))",
             "config": {"workload": "LocalLatentLM training step (cfg4)", "model": "LocalLatentLM 0.55B-class",
@@ -570,8 +744,8 @@ def run_lm(args):
             "final_loss": float(loss.item()),
             "clocks": clk,
         }
-        print(json.dumps(out), flush=True)
-    D.cleanup_distributed()
+        return out
+    return None
 
 
 def run_decode(args):
