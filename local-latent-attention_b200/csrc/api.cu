@@ -215,7 +215,7 @@ int run_fwd(const Geom& g, const llattn_fwd_args* a, cudaStream_t s) {
   if (!fused && !general && (rc = simt_gate_check(g))) return rc;
   {
     prof::Scope ps(prof::LATENT_FWD, s);
-    if (sizeof(T) == 2 && sm100::latent_tc_ok(g))  // tensor cores: bf16, head dim 32, <= 64 chunks
+    if (sizeof(T) == 2 && sm100::latent_tc_ok(g))  // tensor cores: bf16, head dim <= 64, <= 64 chunks
       rc = check_launch(sm100::launch_latent_fwd_tc(g, a->rq, a->gkv, a->lat, a->lat_lse, s), "latent_fwd_sm100");
     else
       rc = check_launch(launch_latent_fwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv),
@@ -408,7 +408,7 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
                       "copy dg_remote");
   }
   if (rc) return rc;
-  // tensor-core latent backward for bf16 with head dim 32 and <= 64 chunks;
+  // tensor-core latent backward for bf16 with head dim <= 64 and <= 64 chunks;
   // its row splits are 128-row tiles, at most the SIMT kernel's 64-row count
   const bool lat_tc = sizeof(T) == 2 && sm100::latent_tc_ok(g);
   const int n_split_lat = lat_tc ? std::min(sm100::latent_tc_splits(g), L.n_split_lat) : L.n_split_lat;

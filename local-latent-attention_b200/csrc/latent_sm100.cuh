@@ -1,8 +1,10 @@
 // Backward of the latent branch on the tensor cores (included by
-// local_sm100.cu), for latent head dim 32 and at most 64 chunks (one key
-// tile), bf16 activations. Math as the SIMT kernel of latent.cu: with
-// P = softmax(lat_scale rq.gk) over chunks j < qid(r) (models.py:361-375),
-// dP = dlat.gv, delta = sum_j P dP, dS = P (dP - delta):
+// local_sm100.cu), for at most 64 chunks (one key tile), bf16 activations and
+// latent head dims up to 64: LDH = 32, or 64 for 32 < ldh <= 64 (ldh a
+// multiple of 8; the columns past ldh are zero in every operand). Math as
+// the SIMT kernel of latent.cu: with P = softmax(lat_scale rq.gk) over chunks
+// j < qid(r) (models.py:361-375), dP = dlat.gv, delta = sum_j P dP,
+// dS = P (dP - delta):
 //   drq = lat_scale dS gk,  dgk = lat_scale dS^T rq,  dgv = P^T dlat.
 //
 // CTA = (row split, latent head, b); it walks the 128-row tiles
@@ -14,24 +16,30 @@
 //      are close; rq and gk are bf16 values, exact in tf32)
 //   2. the threads form P, delta, dS in fp32; dS goes to TMEM as bf16 (A of
 //      the drq MMA) and both dS and P to shared memory as bf16
-//   3. drq = dS [gk | gv] (N = 64, the gv half unused) with A from TMEM, and
-//      D2 += [rq | dlat]^T [dS | P] over the tile's rows (M = 128, N = 128,
-//      both operands MN-major): rows e < 32 x columns j < 64 are dgk^T / lat_scale,
-//      rows 32 + e x columns 64 + j are dgv^T. D2 stays in TMEM across the
-//      CTA's tiles and is written once as the CTA's partial.
+//   3. drq = dS gk with A from TMEM, and D2 += [rq | dlat]^T [dS | P] over
+//      the tile's rows (M = 128, N = 128, both operands MN-major): rows
+//      e < LDH x columns j < 64 are dgk^T / lat_scale, rows LDH + e x columns
+//      64 + j are dgv^T (LDH = 32: rows 64-127 come from unrelated bytes and
+//      are never read). D2 stays in TMEM across the CTA's tiles and is
+//      written once as the CTA's partial.
 // Everything within a tile is sequential; two CTAs per SM overlap each other.
 
+template <int LDH>
 struct LatTcLayout {
-  static constexpr int AS = 0;              // rq fp32 [128 rows][32] (K-major, tf32)
-  static constexpr int AD = AS + 16384;     // dlat fp32 [128][32]
-  static constexpr int X = AD + 16384;      // [128 rows][rq bf16 32 | dlat bf16 32] (MN-major A of D2)
-  static constexpr int BP = X + 16384;      // dS bf16 [128 rows][64 keys], then P at BP + 16384
-  static constexpr int GK = BP + 32768;     // gk fp32 [64 keys][32]
-  static constexpr int GV = GK + 8192;      // gv fp32 [64][32]
-  static constexpr int GKV = GV + 8192;     // [64 keys][gk bf16 32 | gv bf16 32] (MN-major B of drq)
-  static constexpr int BAR = GKV + 8192;
+  static constexpr int FP = LDH / 32;           // 128-byte panels of an fp32 row
+  static constexpr int AS = 0;                  // rq fp32 [128 rows][LDH] (K-major, tf32), FP panels of 16 KB
+  static constexpr int AD = AS + FP * 16384;    // dlat fp32 [128][LDH]
+  // [128 rows][rq bf16 | dlat bf16] (MN-major A of D2): LDH 32 one 128-byte
+  // row, LDH 64 a rq panel and a dlat panel of 16 KB
+  static constexpr int X = AD + FP * 16384;
+  static constexpr int BP = X + (LDH == 64 ? 32768 : 16384);  // dS bf16 [128 rows][64 keys], then P at +16 KB
+  static constexpr int GK = BP + 32768;         // gk fp32 [64 keys][LDH], FP panels of 8 KB
+  static constexpr int GV = GK + FP * 8192;     // gv fp32 [64][LDH]
+  static constexpr int GKB = GV + FP * 8192;    // gk bf16 [64 keys][LDH] in 128-byte rows (MN-major B of drq)
+  static constexpr int BAR = GKB + 8192;
   static constexpr int BYTES = BAR + 128;
-  static_assert(BYTES + 1024 <= 113 * 1024, "two CTAs per SM");
+  static_assert(LDH == 64 || BYTES + 1024 <= 113 * 1024, "two CTAs per SM");
+  static_assert(BYTES + 1024 <= 227 * 1024, "shared memory");
 };
 
 enum { LT_A = 0, LT_S = 1, LT_P = 2, LT_T = 3, LT_NB = 4 };
@@ -39,12 +47,18 @@ enum { LT_A = 0, LT_S = 1, LT_P = 2, LT_T = 3, LT_NB = 4 };
 __device__ __forceinline__ uint4* lat_chunk(uint8_t* tile, int row, int c) {  // 16-byte chunk c of a 128-byte row
   return reinterpret_cast<uint4*>(tile + row * 128 + ((c ^ (row & 7)) * 16));
 }
+// chunk c (16 bytes) of a row that spans several 128-byte panels of `rows` rows
+__device__ __forceinline__ uint4* lat_pchunk(uint8_t* tile, int rows, int row, int c) {
+  return lat_chunk(tile + (c >> 3) * rows * 128, row, c & 7);
+}
 
-__global__ void __launch_bounds__(160, 2)
+template <int LDH>
+__global__ void __launch_bounds__(160, LDH == 32 ? 2 : 1)
     latent_bwd_tc_kernel(Geom g, const bf16* __restrict__ rq, const bf16* __restrict__ gkv,
                          const float* __restrict__ lat_lse, const float* __restrict__ dlat, bf16* __restrict__ drq,
                          float* __restrict__ part, int n_split) {
-  using L = LatTcLayout;
+  using L = LatTcLayout<LDH>;
+  constexpr int NQ = LDH / 8, ND = LDH / 4;  // 16-byte chunks of a bf16 / fp32 row
   extern __shared__ __align__(1024) uint8_t smem_lat_tc[];
   uint8_t* smem = smem_lat_tc;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
@@ -58,6 +72,7 @@ __global__ void __launch_bounds__(160, 2)
   const int split = blockIdx.x, lh = blockIdx.y, b = blockIdx.z;
   const int n_rb = cdiv(g.Tq, BM);
   const int n_tiles = split < n_rb ? (n_rb - 1 - split) / n_split + 1 : 0;
+  const int ldh = g.ldh;  // <= LDH, a multiple of 8: chunks past it are zero
 
   if (tid == 0) {
     mbar_init(&bars[LT_A], BM);
@@ -72,74 +87,72 @@ __global__ void __launch_bounds__(160, 2)
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
-  // chunk keys / values of (b, lh): thread = (key, half of the 32 dims)
+  // chunk keys / values of (b, lh): thread = (key, half of the LDH dims)
   if (tid < BM) {
-    const int key = tid >> 1, e0 = (tid & 1) * 16;
-    uint4 k2[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, v2[2] = {k2[0], k2[1]};
-    if (key < g.Nc) {
-      const uint4* kp = reinterpret_cast<const uint4*>(gkv + ((int64_t)(b * g.Nc + key) * 2 * g.Lh + lh) * 32 + e0);
-      const uint4* vp =
-          reinterpret_cast<const uint4*>(gkv + ((int64_t)(b * g.Nc + key) * 2 * g.Lh + g.Lh + lh) * 32 + e0);
-      k2[0] = kp[0];
-      k2[1] = kp[1];
-      v2[0] = vp[0];
-      v2[1] = vp[1];
-    }
+    const int key = tid >> 1, c0 = (tid & 1) * (NQ / 2);  // first bf16 chunk of this half
+    const bf16* kp = gkv + ((int64_t)(b * g.Nc + key) * 2 * g.Lh + lh) * ldh;
+    const bf16* vp = gkv + ((int64_t)(b * g.Nc + key) * 2 * g.Lh + g.Lh + lh) * ldh;
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
+    for (int q = 0; q < NQ / 2; ++q) {
+      const int c = c0 + q;  // bf16 chunk: elements 8c .. 8c+7
+      const bool on = key < g.Nc && 8 * c < ldh;
+      const uint4 k2 = on ? reinterpret_cast<const uint4*>(kp)[c] : make_uint4(0, 0, 0, 0);
+      const uint4 v2 = on ? reinterpret_cast<const uint4*>(vp)[c] : make_uint4(0, 0, 0, 0);
       float kf[8], vf[8];
-      unpack8(k2[q], kf);
-      unpack8(v2[q], vf);
-      const int c = (e0 >> 2) + 2 * q;  // fp32 chunks of 4
-      *lat_chunk(smem + L::GK, key, c) = make_uint4(__float_as_uint(kf[0]), __float_as_uint(kf[1]),
-                                                    __float_as_uint(kf[2]), __float_as_uint(kf[3]));
-      *lat_chunk(smem + L::GK, key, c + 1) = make_uint4(__float_as_uint(kf[4]), __float_as_uint(kf[5]),
-                                                        __float_as_uint(kf[6]), __float_as_uint(kf[7]));
-      *lat_chunk(smem + L::GV, key, c) = make_uint4(__float_as_uint(vf[0]), __float_as_uint(vf[1]),
-                                                    __float_as_uint(vf[2]), __float_as_uint(vf[3]));
-      *lat_chunk(smem + L::GV, key, c + 1) = make_uint4(__float_as_uint(vf[4]), __float_as_uint(vf[5]),
-                                                        __float_as_uint(vf[6]), __float_as_uint(vf[7]));
-      *lat_chunk(smem + L::GKV, key, (e0 >> 3) + q) = k2[q];       // gk bf16: chunks 0-3
-      *lat_chunk(smem + L::GKV, key, 4 + (e0 >> 3) + q) = v2[q];   // gv bf16: chunks 4-7
+      unpack8(k2, kf);
+      unpack8(v2, vf);
+      *lat_pchunk(smem + L::GK, 64, key, 2 * c) = make_uint4(__float_as_uint(kf[0]), __float_as_uint(kf[1]),
+                                                             __float_as_uint(kf[2]), __float_as_uint(kf[3]));
+      *lat_pchunk(smem + L::GK, 64, key, 2 * c + 1) = make_uint4(__float_as_uint(kf[4]), __float_as_uint(kf[5]),
+                                                                 __float_as_uint(kf[6]), __float_as_uint(kf[7]));
+      *lat_pchunk(smem + L::GV, 64, key, 2 * c) = make_uint4(__float_as_uint(vf[0]), __float_as_uint(vf[1]),
+                                                             __float_as_uint(vf[2]), __float_as_uint(vf[3]));
+      *lat_pchunk(smem + L::GV, 64, key, 2 * c + 1) = make_uint4(__float_as_uint(vf[4]), __float_as_uint(vf[5]),
+                                                                 __float_as_uint(vf[6]), __float_as_uint(vf[7]));
+      *lat_chunk(smem + L::GKB, key, c) = k2;
     }
+    if (LDH == 32)  // the drq MMA reads 64 columns of gk bf16: the upper half is zero
+#pragma unroll
+      for (int q = 0; q < 2; ++q) *lat_chunk(smem + L::GKB, key, 4 + (tid & 1) * 2 + q) = make_uint4(0, 0, 0, 0);
   }
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM: S [0,64) (then drq / the unused dS gv product), dP [64,128) with dS
-  // bf16 over [64,96), D2 [128,256)
+  // TMEM: S [0,64) (then drq), dP [64,128) with dS bf16 over [64,96), D2 [128,256)
   const uint32_t tS = tmem, tP = tmem + 64, tD2 = tmem + 128;
 
   if (warp == 4) {
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t id1 = idesc_tf32_f32(BM, 64);
-      constexpr uint32_t idQ = idesc_bf16_f32(BM, 64, false, true);   // dS [gk | gv]
+      constexpr uint32_t idQ = idesc_bf16_f32(BM, 64, false, true);   // dS gk
       constexpr uint32_t id2 = idesc_bf16_f32(BM, 128, true, true);   // [rq | dlat]^T [dS | P]
       const uint64_t das = desc_sw128(smem_u32(smem + L::AS), 16, 1024);
       const uint64_t dad = desc_sw128(smem_u32(smem + L::AD), 16, 1024);
       const uint64_t dgk = desc_sw128(smem_u32(smem + L::GK), 16, 1024);
       const uint64_t dgv = desc_sw128(smem_u32(smem + L::GV), 16, 1024);
-      const uint64_t dkv = desc_sw128(smem_u32(smem + L::GKV), 8192, 1024);
-      // M = 128 reads a second 64-row panel of A 16 KB on (the dS tile): the
-      // D2 rows it produces (64-127) are never read
+      const uint64_t dkb = desc_sw128(smem_u32(smem + L::GKB), 8192, 1024);
+      // LDH 32: M = 128 reads a second 64-row panel of A 16 KB on (the dS
+      // tile): the D2 rows it produces (64-127) are never read
       const uint64_t dx = desc_sw128(smem_u32(smem + L::X), 16384, 1024);
       const uint64_t dbp = desc_sw128(smem_u32(smem + L::BP), 16384, 1024);
       bool ok = true;
       for (int n = 0; ok && n < n_tiles; ++n) {
         if (!(ok = mbar_wait(&bars[LT_A], n & 1, abort, &g_fault_word))) break;
         tc_fence_after();
+        // K steps of 8 fp32 (32 bytes); panels of 32 fp32 at 16 KB (A) / 8 KB (B)
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          mma_tf32(tS, desc_add(das, kk * 32), desc_add(dgk, kk * 32), id1, kk > 0);
-          mma_tf32(tP, desc_add(dad, kk * 32), desc_add(dgv, kk * 32), id1, kk > 0);
+        for (int kk = 0; kk < LDH / 8; ++kk) {
+          const uint32_t ao = (kk / 4) * 16384 + (kk % 4) * 32, bo = (kk / 4) * 8192 + (kk % 4) * 32;
+          mma_tf32(tS, desc_add(das, ao), desc_add(dgk, bo), id1, kk > 0);
+          mma_tf32(tP, desc_add(dad, ao), desc_add(dgv, bo), id1, kk > 0);
         }
         mma_commit(&bars[LT_S]);
         if (!(ok = mbar_wait(&bars[LT_P], n & 1, abort, &g_fault_word))) break;
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(tS, tP + kk * 8, desc_add(dkv, kk * 2048), idQ, kk > 0);
+        for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(tS, tP + kk * 8, desc_add(dkb, kk * 2048), idQ, kk > 0);
 #pragma unroll
         for (int kk = 0; kk < BM / 16; ++kk)
           mma_bf16(tD2, desc_add(dx, kk * 2048), desc_add(dbp, kk * 2048), id2, (n > 0 || kk > 0) ? 1u : 0u);
@@ -150,26 +163,18 @@ __global__ void __launch_bounds__(160, 2)
   } else {
     const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
     const float sc2 = g.lat_scale * kLog2e;
-    const int ldh = 32;
-    uint4 pre_q[4], pre_d[8];  // next tile's rq (bf16) / dlat (fp32) row
+    uint4 pre_q[NQ], pre_d[ND];  // next tile's rq (bf16) / dlat (fp32) row
     float pre_lse = INFINITY;
     auto fetch = [&](int n) {
       const int r = (split + n * n_split) * BM + tid;
-      if (n < n_tiles && r < g.Tq) {
-        const uint4* qp = reinterpret_cast<const uint4*>(rq + ((int64_t)(b * g.Tq + r) * g.Lh + lh) * ldh);
-        const uint4* dp = reinterpret_cast<const uint4*>(dlat + (int64_t)(b * g.Tq + r) * g.Ld + lh * ldh);
+      const bool on = n < n_tiles && r < g.Tq;
+      const uint4* qp = reinterpret_cast<const uint4*>(rq + ((int64_t)(b * g.Tq + (on ? r : 0)) * g.Lh + lh) * ldh);
+      const uint4* dp = reinterpret_cast<const uint4*>(dlat + (int64_t)(b * g.Tq + (on ? r : 0)) * g.Ld + lh * ldh);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) pre_q[i] = __ldg(qp + i);
+      for (int i = 0; i < NQ; ++i) pre_q[i] = (on && 8 * i < ldh) ? __ldg(qp + i) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) pre_d[i] = __ldg(dp + i);
-        pre_lse = __ldg(lat_lse + (int64_t)(b * g.Lh + lh) * g.Tq + r) * kLog2e;
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) pre_q[i] = make_uint4(0, 0, 0, 0);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) pre_d[i] = make_uint4(0, 0, 0, 0);
-        pre_lse = INFINITY;
-      }
+      for (int i = 0; i < ND; ++i) pre_d[i] = (on && 4 * i < ldh) ? __ldg(dp + i) : make_uint4(0, 0, 0, 0);
+      pre_lse = on ? __ldg(lat_lse + (int64_t)(b * g.Lh + lh) * g.Tq + r) * kLog2e : INFINITY;
     };
     fetch(0);
     bool ok = true;
@@ -184,20 +189,20 @@ __global__ void __launch_bounds__(160, 2)
         if (!ok) break;
       }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) *lat_chunk(smem + L::AD, tid, c) = pre_d[c];
+      for (int c = 0; c < ND; ++c) *lat_pchunk(smem + L::AD, BM, tid, c) = pre_d[c];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < NQ; ++i) {
         float f[8];
         unpack8(pre_q[i], f);
-        *lat_chunk(smem + L::AS, tid, 2 * i) = make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]),
-                                                          __float_as_uint(f[2]), __float_as_uint(f[3]));
-        *lat_chunk(smem + L::AS, tid, 2 * i + 1) = make_uint4(__float_as_uint(f[4]), __float_as_uint(f[5]),
-                                                              __float_as_uint(f[6]), __float_as_uint(f[7]));
-        *lat_chunk(smem + L::X, tid, i) = pre_q[i];
+        *lat_pchunk(smem + L::AS, BM, tid, 2 * i) = make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]),
+                                                               __float_as_uint(f[2]), __float_as_uint(f[3]));
+        *lat_pchunk(smem + L::AS, BM, tid, 2 * i + 1) = make_uint4(__float_as_uint(f[4]), __float_as_uint(f[5]),
+                                                                   __float_as_uint(f[6]), __float_as_uint(f[7]));
+        *lat_pchunk(smem + L::X, BM, tid, i) = pre_q[i];
         const float4 d0 = *reinterpret_cast<const float4*>(&pre_d[2 * i]);
         const float4 d1 = *reinterpret_cast<const float4*>(&pre_d[2 * i + 1]);
-        *lat_chunk(smem + L::X, tid, 4 + i) = make_uint4(pack_bf16(d0.x, d0.y), pack_bf16(d0.z, d0.w),
-                                                         pack_bf16(d1.x, d1.y), pack_bf16(d1.z, d1.w));
+        *lat_pchunk(smem + L::X, BM, tid, NQ + i) = make_uint4(pack_bf16(d0.x, d0.y), pack_bf16(d0.z, d0.w),
+                                                               pack_bf16(d1.x, d1.y), pack_bf16(d1.z, d1.w));
       }
       fence_async_smem();
       mbar_arrive(&bars[LT_A]);
@@ -254,43 +259,51 @@ __global__ void __launch_bounds__(160, 2)
       if (!ok) break;
       tc_fence_after();
       uint32_t rq32[32];
-      tmem_ld32(tS + lane_off, rq32);
-      tmem_ld_wait();
-      if (valid) {
-        uint4* dst = reinterpret_cast<uint4*>(drq + ((int64_t)(b * g.Tq + r) * g.Lh + lh) * ldh);
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          dst[c] = make_uint4(pack_bf16(__uint_as_float(rq32[8 * c]) * g.lat_scale,
-                                        __uint_as_float(rq32[8 * c + 1]) * g.lat_scale),
-                              pack_bf16(__uint_as_float(rq32[8 * c + 2]) * g.lat_scale,
-                                        __uint_as_float(rq32[8 * c + 3]) * g.lat_scale),
-                              pack_bf16(__uint_as_float(rq32[8 * c + 4]) * g.lat_scale,
-                                        __uint_as_float(rq32[8 * c + 5]) * g.lat_scale),
-                              pack_bf16(__uint_as_float(rq32[8 * c + 6]) * g.lat_scale,
-                                        __uint_as_float(rq32[8 * c + 7]) * g.lat_scale));
+      for (int hh = 0; hh < LDH / 32; ++hh) {
+        tmem_ld32(tS + lane_off + hh * 32, rq32);
+        tmem_ld_wait();
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(drq + ((int64_t)(b * g.Tq + r) * g.Lh + lh) * ldh + hh * 32);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if (hh * 32 + 8 * c < ldh)
+              dst[c] = make_uint4(pack_bf16(__uint_as_float(rq32[8 * c]) * g.lat_scale,
+                                            __uint_as_float(rq32[8 * c + 1]) * g.lat_scale),
+                                  pack_bf16(__uint_as_float(rq32[8 * c + 2]) * g.lat_scale,
+                                            __uint_as_float(rq32[8 * c + 3]) * g.lat_scale),
+                                  pack_bf16(__uint_as_float(rq32[8 * c + 4]) * g.lat_scale,
+                                            __uint_as_float(rq32[8 * c + 5]) * g.lat_scale),
+                                  pack_bf16(__uint_as_float(rq32[8 * c + 6]) * g.lat_scale,
+                                            __uint_as_float(rq32[8 * c + 7]) * g.lat_scale));
+        }
       }
     }
     if (!ok) raise_fault(g, kFaultSoftmax, abort);
-    // this CTA's dgk / dgv partial: warp 0 holds D2 rows e (dgk^T), warp 1
-    // rows 32 + e (dgv^T); partial layout [split][b][key][2][Ld]
-    if (warp < 2) {
-      float* my_part = part + ((int64_t)split * g.B + b) * g.Nc * 2 * g.Ld + lh * ldh + lane;
-      const float mul = warp == 0 ? g.lat_scale : 1.f;
+    // this CTA's dgk / dgv partial: D2 row m = 32 warp + lane is dgk^T row e
+    // for m < LDH and dgv^T row m - LDH after it (LDH 32: rows >= 64 unused);
+    // partial layout [split][b][key][2][Ld]
+    const int m = 32 * warp + lane, which = m / LDH, e = m % LDH;
+    if (which < 2) {
+      float* my_part = part + ((int64_t)split * g.B + b) * g.Nc * 2 * g.Ld + lh * ldh + e;
+      const float mul = which == 0 ? g.lat_scale : 1.f;
       const bool have = ok && n_tiles > 0 && !*abort;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t v[32];
         if (have) {
-          tmem_ld32(tD2 + lane_off + warp * 64 + hh * 32, v);
+          tmem_ld32(tD2 + lane_off + which * 64 + hh * 32, v);
           tmem_ld_wait();
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = 0u;
         }
+        if (e < ldh) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = hh * 32 + i;
-          if (key < g.Nc) my_part[(int64_t)(2 * key + warp) * g.Ld] = __uint_as_float(v[i]) * mul;
+          for (int i = 0; i < 32; ++i) {
+            const int key = hh * 32 + i;
+            if (key < g.Nc) my_part[(int64_t)(2 * key + which) * g.Ld] = __uint_as_float(v[i]) * mul;
+          }
         }
       }
     }
@@ -308,19 +321,23 @@ __global__ void __launch_bounds__(160, 2)
 // 128-row tile, S = rq gk^T (bf16 operands, fp32 accumulation), the
 // threads mask chunks j >= qid(r), take the row max and P = 2^(S sc - max) in
 // fp32 (the normaliser l sums the fp32 P), and write P as bf16 over the S
-// columns; lat = (P [gk | gv]) / l from the gv half, lat_lse = max + ln l
-// (INFINITY and lat = 0 for rows that see no chunk, models.py:366-373).
+// columns; lat = (P gv) / l, lat_lse = max + ln l (INFINITY and lat = 0 for
+// rows that see no chunk, models.py:366-373). gk and gv sit in 128-byte rows
+// (columns past ldh zero): K-major B of the score MMA and MN-major B of P gv.
 struct LatFwdTcLayout {
-  static constexpr int AQ = 0;              // rq bf16 [128 rows][32] in 128-byte rows (first 64 bytes)
-  static constexpr int GKV = AQ + 16384;    // [64 keys][gk bf16 32 | gv bf16 32]
-  static constexpr int BAR = GKV + 8192;
+  static constexpr int AQ = 0;              // rq bf16 [128 rows][<= 64] in 128-byte rows
+  static constexpr int GK = AQ + 16384;     // gk bf16 [64 keys][<= 64]
+  static constexpr int GV = GK + 8192;      // gv bf16 [64 keys][<= 64]
+  static constexpr int BAR = GV + 8192;
   static constexpr int BYTES = BAR + 128;
 };
 
+template <int LDH>
 __global__ void __launch_bounds__(160)
     latent_fwd_tc_kernel(Geom g, const bf16* __restrict__ rq, const bf16* __restrict__ gkv, bf16* __restrict__ lat,
                          float* __restrict__ lat_lse, int n_split) {
   using L = LatFwdTcLayout;
+  constexpr int NQ = LDH / 8;
   extern __shared__ __align__(1024) uint8_t smem_latf_tc[];
   uint8_t* smem = smem_latf_tc;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
@@ -334,6 +351,7 @@ __global__ void __launch_bounds__(160)
   const int split = blockIdx.x, lh = blockIdx.y, b = blockIdx.z;
   const int n_rb = cdiv(g.Tq, BM);
   const int n_tiles = split < n_rb ? (n_rb - 1 - split) / n_split + 1 : 0;
+  const int ldh = g.ldh;
 
   if (tid == 0) {
     mbar_init(&bars[LT_A], BM);
@@ -348,22 +366,16 @@ __global__ void __launch_bounds__(160)
     tmem_alloc(tmem_slot, 128);
     tmem_relinquish();
   }
-  if (tid < BM) {  // chunk keys / values of (b, lh): thread = (key, half of the 32 dims)
-    const int key = tid >> 1, e0 = (tid & 1) * 16;
-    uint4 k2[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, v2[2] = {k2[0], k2[1]};
-    if (key < g.Nc) {
-      const uint4* kp = reinterpret_cast<const uint4*>(gkv + ((int64_t)(b * g.Nc + key) * 2 * g.Lh + lh) * 32 + e0);
-      const uint4* vp =
-          reinterpret_cast<const uint4*>(gkv + ((int64_t)(b * g.Nc + key) * 2 * g.Lh + g.Lh + lh) * 32 + e0);
-      k2[0] = kp[0];
-      k2[1] = kp[1];
-      v2[0] = vp[0];
-      v2[1] = vp[1];
-    }
+  if (tid < BM) {  // chunk keys / values of (b, lh): thread = (key, half of the row's 8 chunks)
+    const int key = tid >> 1, c0 = (tid & 1) * 4;
+    const bf16* kp = gkv + ((int64_t)(b * g.Nc + key) * 2 * g.Lh + lh) * ldh;
+    const bf16* vp = gkv + ((int64_t)(b * g.Nc + key) * 2 * g.Lh + g.Lh + lh) * ldh;
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      *lat_chunk(smem + L::GKV, key, (e0 >> 3) + q) = k2[q];
-      *lat_chunk(smem + L::GKV, key, 4 + (e0 >> 3) + q) = v2[q];
+    for (int q = 0; q < 4; ++q) {
+      const int c = c0 + q;
+      const bool on = key < g.Nc && 8 * c < ldh;
+      *lat_chunk(smem + L::GK, key, c) = on ? reinterpret_cast<const uint4*>(kp)[c] : make_uint4(0, 0, 0, 0);
+      *lat_chunk(smem + L::GV, key, c) = on ? reinterpret_cast<const uint4*>(vp)[c] : make_uint4(0, 0, 0, 0);
     }
   }
   fence_async_smem();
@@ -371,26 +383,27 @@ __global__ void __launch_bounds__(160)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 64;  // S [0,64) with P bf16 over [0,32); P [gk | gv] at [64,128)
+  const uint32_t tS = tmem, tO = tmem + 64;  // S [0,64) with P bf16 over [0,32); P gv at [64,128)
 
   if (warp == 4) {
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t idS = idesc_bf16_f32(BM, 64, false, false);  // rq gk^T
-      constexpr uint32_t idO = idesc_bf16_f32(BM, 64, false, true);   // P [gk | gv]
+      constexpr uint32_t idO = idesc_bf16_f32(BM, 64, false, true);   // P gv
       const uint64_t daq = desc_sw128(smem_u32(smem + L::AQ), 16, 1024);
-      const uint64_t dk = desc_sw128(smem_u32(smem + L::GKV), 16, 1024);
-      const uint64_t dkv = desc_sw128(smem_u32(smem + L::GKV), 8192, 1024);
+      const uint64_t dk = desc_sw128(smem_u32(smem + L::GK), 16, 1024);
+      const uint64_t dv = desc_sw128(smem_u32(smem + L::GV), 8192, 1024);
       bool ok = true;
       for (int n = 0; ok && n < n_tiles; ++n) {
         if (!(ok = mbar_wait(&bars[LT_A], n & 1, abort, &g_fault_word))) break;
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 2; ++kk) mma_bf16(tS, desc_add(daq, kk * 32), desc_add(dk, kk * 32), idS, kk > 0);
+        for (int kk = 0; kk < LDH / 16; ++kk)
+          mma_bf16(tS, desc_add(daq, kk * 32), desc_add(dk, kk * 32), idS, kk > 0);
         mma_commit(&bars[LT_S]);
         if (!(ok = mbar_wait(&bars[LT_P], n & 1, abort, &g_fault_word))) break;
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(tO, tS + kk * 8, desc_add(dkv, kk * 2048), idO, kk > 0);
+        for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(tO, tS + kk * 8, desc_add(dv, kk * 2048), idO, kk > 0);
         mma_commit(&bars[LT_T]);
       }
       if (!ok) raise_fault(g, kFaultMma, abort);
@@ -398,17 +411,13 @@ __global__ void __launch_bounds__(160)
   } else {
     const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
     const float sc2 = g.lat_scale * kLog2e;
-    uint4 pre_q[4];
+    uint4 pre_q[NQ];
     auto fetch = [&](int n) {
       const int r = (split + n * n_split) * BM + tid;
-      if (n < n_tiles && r < g.Tq) {
-        const uint4* qp = reinterpret_cast<const uint4*>(rq + ((int64_t)(b * g.Tq + r) * g.Lh + lh) * 32);
+      const bool on = n < n_tiles && r < g.Tq;
+      const uint4* qp = reinterpret_cast<const uint4*>(rq + ((int64_t)(b * g.Tq + (on ? r : 0)) * g.Lh + lh) * ldh);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) pre_q[i] = __ldg(qp + i);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) pre_q[i] = make_uint4(0, 0, 0, 0);
-      }
+      for (int i = 0; i < NQ; ++i) pre_q[i] = (on && 8 * i < ldh) ? __ldg(qp + i) : make_uint4(0, 0, 0, 0);
     };
     fetch(0);
     bool ok = true;
@@ -417,7 +426,7 @@ __global__ void __launch_bounds__(160)
       const bool valid = r < g.Tq;
       const int qid = valid ? row_qid(g, r) : 0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) *lat_chunk(smem + L::AQ, tid, i) = pre_q[i];
+      for (int i = 0; i < NQ; ++i) *lat_chunk(smem + L::AQ, tid, i) = pre_q[i];
       fence_async_smem();
       mbar_arrive(&bars[LT_A]);
       fetch(n + 1);
@@ -465,20 +474,24 @@ __global__ void __launch_bounds__(160)
       ok = __all_sync(0xffffffffu, mbar_wait(&bars[LT_T], n & 1, abort, &g_fault_word));
       if (!ok) break;
       tc_fence_after();
-      uint32_t o[32];
-      tmem_ld32(tO + lane_off + 32, o);  // the gv half
-      tmem_ld_wait();
-      if (valid) {
-        const float inv = qid > 0 ? 1.f / l : 0.f;
-        uint4* dst = reinterpret_cast<uint4*>(lat + (int64_t)(b * g.Tq + r) * g.Ld + lh * 32);
+      const float inv = qid > 0 ? 1.f / l : 0.f;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          dst[c] = make_uint4(pack_bf16(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
-                              pack_bf16(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
-                              pack_bf16(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
-                              pack_bf16(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
-        lat_lse[(int64_t)(b * g.Lh + lh) * g.Tq + r] = qid > 0 ? (mb + log2f(l)) * kLn2 : INFINITY;
+      for (int hh = 0; hh < LDH / 32; ++hh) {
+        uint32_t o[32];
+        tmem_ld32(tO + lane_off + hh * 32, o);
+        tmem_ld_wait();
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(lat + (int64_t)(b * g.Tq + r) * g.Ld + lh * ldh + hh * 32);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if (hh * 32 + 8 * c < ldh)
+              dst[c] = make_uint4(pack_bf16(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
+                                  pack_bf16(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
+                                  pack_bf16(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
+                                  pack_bf16(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
+        }
       }
+      if (valid) lat_lse[(int64_t)(b * g.Lh + lh) * g.Tq + r] = qid > 0 ? (mb + log2f(l)) * kLn2 : INFINITY;
     }
     if (!ok) raise_fault(g, kFaultSoftmax, abort);
   }

@@ -332,7 +332,11 @@ cudaError_t launch_rout_dw(const Geom& g, const void* dr, const void* lat, float
   return cudaGetLastError();
 }
 
-bool latent_tc_ok(const Geom& g) { return g.ldh == 32 && g.Nc <= 64 && g.Tq >= 1; }
+// latent head dim 32, or up to 64 as 64-wide tiles (ldh a multiple of 8,
+// the columns past it zero); one 64-chunk key tile
+bool latent_tc_ok(const Geom& g) {
+  return !force_simt() && g.ldh <= 64 && g.ldh % 8 == 0 && g.Nc <= 64 && g.Tq >= 1;
+}
 
 int latent_tc_splits(const Geom& g) { return std::max(1, std::min(cdiv(g.Tq, BM), (2 * sm_count()) / (g.B * g.Lh))); }
 
@@ -341,13 +345,16 @@ cudaError_t launch_latent_bwd_tc(const Geom& g, const void* rq, const void* gkv,
   if (!latent_tc_ok(g)) return cudaErrorNotSupported;
   if (((uintptr_t)rq & 15) || ((uintptr_t)gkv & 15) || ((uintptr_t)dlat & 15) || ((uintptr_t)drq & 15))
     return cudaErrorMisalignedAddress;
-  const int smem = LatTcLayout::BYTES;  // the kernel's shared memory is 1024-byte aligned
-  cudaError_t e = cudaFuncSetAttribute(latent_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
   dim3 grid(n_split, g.Lh, g.B);
-  latent_bwd_tc_kernel<<<grid, 160, smem, s>>>(g, static_cast<const bf16*>(rq), static_cast<const bf16*>(gkv),
-                                               lat_lse, dlat, static_cast<bf16*>(drq), part, n_split);
-  return cudaGetLastError();
+  auto run = [&](auto kern, int smem) -> cudaError_t {  // the kernel's shared memory is 1024-byte aligned
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, 160, smem, s>>>(g, static_cast<const bf16*>(rq), static_cast<const bf16*>(gkv), lat_lse, dlat,
+                                 static_cast<bf16*>(drq), part, n_split);
+    return cudaGetLastError();
+  };
+  if (g.ldh <= 32) return run(latent_bwd_tc_kernel<32>, LatTcLayout<32>::BYTES);
+  return run(latent_bwd_tc_kernel<64>, LatTcLayout<64>::BYTES);
 }
 
 cudaError_t launch_latent_fwd_tc(const Geom& g, const void* rq, const void* gkv, void* lat, float* lat_lse,
@@ -355,13 +362,14 @@ cudaError_t launch_latent_fwd_tc(const Geom& g, const void* rq, const void* gkv,
   if (!latent_tc_ok(g)) return cudaErrorNotSupported;
   if (((uintptr_t)rq & 15) || ((uintptr_t)gkv & 15) || ((uintptr_t)lat & 15)) return cudaErrorMisalignedAddress;
   const int smem = LatFwdTcLayout::BYTES;  // the kernel's shared memory is 1024-byte aligned
-  cudaError_t e = cudaFuncSetAttribute(latent_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  auto kern = g.ldh <= 32 ? latent_fwd_tc_kernel<32> : latent_fwd_tc_kernel<64>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   // up to four CTAs per SM (128 TMEM columns each)
   const int n_split = std::max(1, std::min(cdiv(g.Tq, BM), (4 * sm_count()) / (g.B * g.Lh)));
   dim3 grid(n_split, g.Lh, g.B);
-  latent_fwd_tc_kernel<<<grid, 160, smem, s>>>(g, static_cast<const bf16*>(rq), static_cast<const bf16*>(gkv),
-                                               static_cast<bf16*>(lat), lat_lse, n_split);
+  kern<<<grid, 160, smem, s>>>(g, static_cast<const bf16*>(rq), static_cast<const bf16*>(gkv),
+                               static_cast<bf16*>(lat), lat_lse, n_split);
   return cudaGetLastError();
 }
 

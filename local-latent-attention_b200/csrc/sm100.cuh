@@ -42,7 +42,7 @@ struct GateBwd {
   const void* local_out; const void* lat; const void* w_rout; const float* b_rout; const float* g_local;
   const float* g_remote; const void* dmixed; void* dl; float* delta; void* dr; float* dlat_tok; float* dg_part;
 };
-// Latent backward on tensor cores (latent head dim 32, at most 64 chunks,
+// Latent backward on tensor cores (latent head dim <= 64, at most 64 chunks,
 // bf16): drq and per-split dgk/dgv partials [n_split][B][Nc][2][Ld] as the
 // SIMT kernel writes them; n_split = latent_tc_splits(g) row splits.
 bool latent_tc_ok(const Geom& g);
