@@ -39,7 +39,7 @@
 extern "C" {
 #endif
 
-#define LLATTN_VERSION 1
+#define LLATTN_VERSION 2
 
 #if defined(__GNUC__)
 #define LLATTN_API __attribute__((visibility("default")))
@@ -147,7 +147,11 @@ typedef struct llattn_decode_args {
  * and dmixed [B, T, H*hd] dtype. Outputs (all fully overwritten):
  *   dqkv [B, T, 3, H, hd] dtype, drq [B, Tq, Lh, ldh] dtype,
  *   dgkv [B, Nc, 2, Lh, ldh] dtype, dw_rout [H*hd, Lh*ldh] fp32,
- *   db_rout [H*hd] fp32, dg_local [hd] fp32, dg_remote [hd] fp32.
+ *   db_rout [H*hd] fp32, dg_local [hd] fp32, dg_remote [hd] fp32, and
+ *   (optional, NULL to skip) db_qkv [3*H*hd] fp32 = the column sums of dqkv,
+ *   the bias gradient of qkv_proj (models.py:80), which the tensor-core
+ *   kernels take from the tiles they already hold instead of re-reading dqkv
+ *   (fp32 sums of the unrounded values, fixed order).
  * workspace: device buffer of at least llattn_bwd_workspace_bytes(&dims)
  * bytes, 256-byte aligned; its contents need no initialisation. */
 typedef struct llattn_bwd_args {
@@ -173,6 +177,7 @@ typedef struct llattn_bwd_args {
   float* dg_remote;
   void* workspace;
   size_t workspace_bytes;
+  float* db_qkv; /* since LLATTN_VERSION 2 */
 } llattn_bwd_args;
 
 /* Pool modes of llattn_pool_fwd / llattn_pool_bwd. */

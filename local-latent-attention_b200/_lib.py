@@ -56,7 +56,7 @@ class BwdArgs(ctypes.Structure):
                 ("lse", _fp), ("lat", _vp), ("lat_lse", _fp), ("dmixed", _vp), ("dqkv", _vp),
                 ("drq", _vp), ("dgkv", _vp), ("dw_rout", _fp), ("db_rout", _fp),
                 ("dg_local", _fp), ("dg_remote", _fp), ("workspace", _vp),
-                ("workspace_bytes", ctypes.c_size_t)]
+                ("workspace_bytes", ctypes.c_size_t), ("db_qkv", _fp)]
 
 
 class DecodeArgs(ctypes.Structure):

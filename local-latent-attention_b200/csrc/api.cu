@@ -73,7 +73,7 @@ int make_geom(const llattn_dims* d, Geom* g) {
 
 // Backward workspace, every region 256-byte aligned.
 struct BwdLayout {
-  size_t dl, delta, drow, drow_half, dlat, dlat_tok, dg_part, dg_sum, dw_part, dgkv_part, drq_part, total;
+  size_t dl, delta, drow, drow_half, dlat, dlat_tok, dg_part, dg_sum, dw_part, dgkv_part, drq_part, dbqkv, total;
   int gate_tok, n_gate_cta, n_split_w, n_split_lat, n_kg_lat;
 };
 
@@ -113,6 +113,8 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
   L.dw_part = take(sizeof(float) * (size_t)L.n_split_w * g.d * (g.Ld + 1));
   L.dgkv_part = take(sizeof(float) * (size_t)L.n_split_lat * L.n_kg_lat * g.B * g.Nc * 2 * g.Ld);
   L.drq_part = take(L.n_kg_lat > 1 ? sizeof(float) * (size_t)L.n_kg_lat * g.B * g.Tq * g.Ld : 0);
+  // qkv_proj bias gradient: the column-sum kernel's split partials
+  L.dbqkv = take(sizeof(float) * 3 * (size_t)g.d * colsum_splits((int64_t)g.B * g.T, 3 * g.d, elt));
   L.total = off;
   return L;
 }
@@ -413,6 +415,7 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
   const bool lat_tc = sizeof(T) == 2 && sm100::latent_tc_ok(g);
   const int n_split_lat = lat_tc ? std::min(sm100::latent_tc_splits(g), L.n_split_lat) : L.n_split_lat;
   const int n_kg_lat = lat_tc || g.Nc <= 64 ? 1 : L.n_kg_lat;
+  {
   prof::Scope ps(prof::LATENT_BWD, s, n_kg_lat > 1 ? 3 : 2);
   if (lat_tc)
     rc = check_launch(sm100::launch_latent_bwd_tc(g, a->rq, a->gkv, a->lat_lse, dlat, a->drq, dgkv_part,
@@ -424,8 +427,14 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
                                            n_kg_lat, reinterpret_cast<float*>(ws + L.drq_part), s),
                       "latent_bwd");
   if (rc) return rc;
-  return check_launch(launch_latent_reduce<T>(g, dgkv_part, n_split_lat * n_kg_lat, static_cast<T*>(a->dgkv), s),
-                      "latent_reduce");
+  rc = check_launch(launch_latent_reduce<T>(g, dgkv_part, n_split_lat * n_kg_lat, static_cast<T*>(a->dgkv), s),
+                    "latent_reduce");
+  }
+  if (rc || !a->db_qkv) return rc;
+  prof::Scope pc(prof::COLSUM, s, 2);
+  return check_launch(launch_colsum<T, float>(static_cast<const T*>(a->dqkv), (int64_t)g.B * g.T, 3 * (int64_t)g.d,
+                                              reinterpret_cast<float*>(ws + L.dbqkv), a->db_qkv, s),
+                      "colsum_dbqkv");
 }
 
 }  // namespace
@@ -520,8 +529,10 @@ int llattn_colsum(const void* g, int64_t rows, int64_t cols, int dtype, void* ou
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   prof::Scope ps(prof::COLSUM, s, 2);
   if (dtype == LLATTN_BF16)
-    return check_launch(launch_colsum<bf16>((const bf16*)g, rows, cols, (float*)workspace, (bf16*)out, s), "colsum");
-  return check_launch(launch_colsum<float>((const float*)g, rows, cols, (float*)workspace, (float*)out, s), "colsum");
+    return check_launch(launch_colsum<bf16, bf16>((const bf16*)g, rows, cols, (float*)workspace, (bf16*)out, s),
+                        "colsum");
+  return check_launch(launch_colsum<float, float>((const float*)g, rows, cols, (float*)workspace, (float*)out, s),
+                      "colsum");
 }
 
 int llattn_fwd(const llattn_fwd_args* a, void* stream) {

@@ -94,8 +94,8 @@ cudaError_t launch_pool_bwd(const Geom& g, int mode, const T* dout, T* dx, int64
 // colsum_splits(rows, cols, sizeof(T)) x cols floats
 int colsum_splits(int64_t rows, int64_t cols, int elem_bytes);
 int sm_count();  // SMs of the current device
-template <typename T>
-cudaError_t launch_colsum(const T* g, int64_t rows, int64_t cols, float* part, T* out, cudaStream_t s);
+template <typename T, typename To = T>
+cudaError_t launch_colsum(const T* g, int64_t rows, int64_t cols, float* part, To* out, cudaStream_t s);
 template <typename To>
 cudaError_t launch_reduce_parts(const float* part, int n_part, int64_t n, To* out, cudaStream_t s);
 

@@ -84,21 +84,6 @@ struct GbLayout {
 // L/dmixed tiles loaded
 enum { GB_W = 0, GB_R = 2, GB_DR = 4, GB_DL = 6, GB_F = 8, GB_NB = 10 };
 
-// Sum of v[c] over the 32 lanes for column c = lane (recursive halving).
-__device__ __forceinline__ float butterfly32(float (&v)[32], int lane) {
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    const bool up = lane & off;
-#pragma unroll
-    for (int i = 0; i < off; ++i) {
-      const float send = up ? v[i] : v[i + off];
-      const float keep = up ? v[i + off] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-  }
-  return v[0];
-}
-
 // Warps: 0 = TMA producer (tiles in, dL/dR tiles out), 1 = TMEM + MMA issuer,
 // 2-5 = group 0 (even heads), 6-9 = group 1 (odd heads); in a group thread =
 // token row = TMEM lane.

@@ -138,7 +138,15 @@ __global__ void __launch_bounds__(256) colsum_part_kernel(const T* __restrict__ 
   for (int i = 0; i < V; ++i) acc[i] = 0.f;
   if (col < cols) {
     int64_t r = r0 + rl;
-    for (; r + 24 < r1; r += 32) {  // four rows in flight per thread
+    for (; r + 56 < r1; r += 64) {  // eight rows in flight per thread
+      float v[8][V];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) Vec<T, V>::load(g + (r + 8 * k) * cols + col, v[k]);
+#pragma unroll
+      for (int i = 0; i < V; ++i)
+        acc[i] += ((v[0][i] + v[1][i]) + (v[2][i] + v[3][i])) + ((v[4][i] + v[5][i]) + (v[6][i] + v[7][i]));
+    }
+    for (; r + 24 < r1; r += 32) {
       float v0[V], v1[V], v2[V], v3[V];
       Vec<T, V>::load(g + r * cols + col, v0);
       Vec<T, V>::load(g + (r + 8) * cols + col, v1);
@@ -247,8 +255,8 @@ int colsum_occupancy(K kernel) {
   return occ;
 }
 
-template <typename T>
-cudaError_t launch_colsum(const T* g, int64_t rows, int64_t cols, float* part, T* out, cudaStream_t s) {
+template <typename T, typename To>
+cudaError_t launch_colsum(const T* g, int64_t rows, int64_t cols, float* part, To* out, cudaStream_t s) {
   constexpr int V = vec_width<T>();
   const bool vec = cols % V == 0 && aligned16(g);
   const int gx = vec ? cdiv((int)(cols / V), 32) : cdiv((int)cols, 32);
@@ -264,11 +272,12 @@ cudaError_t launch_colsum(const T* g, int64_t rows, int64_t cols, float* part, T
     colsum_part_kernel<T, 1><<<dim3(gx, splits), 256, 0, s>>>(g, rows, cols, per, part);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return launch_reduce_parts<T>(part, splits, cols, out, s);
+  return launch_reduce_parts<To>(part, splits, cols, out, s);
 }
 
-template cudaError_t launch_colsum<float>(const float*, int64_t, int64_t, float*, float*, cudaStream_t);
-template cudaError_t launch_colsum<bf16>(const bf16*, int64_t, int64_t, float*, bf16*, cudaStream_t);
+template cudaError_t launch_colsum<float, float>(const float*, int64_t, int64_t, float*, float*, cudaStream_t);
+template cudaError_t launch_colsum<bf16, bf16>(const bf16*, int64_t, int64_t, float*, bf16*, cudaStream_t);
+template cudaError_t launch_colsum<bf16, float>(const bf16*, int64_t, int64_t, float*, float*, cudaStream_t);
 template cudaError_t launch_pool_fwd<float>(const Geom&, int, const float*, float*, int64_t, cudaStream_t);
 template cudaError_t launch_pool_fwd<bf16>(const Geom&, int, const bf16*, bf16*, int64_t, cudaStream_t);
 template cudaError_t launch_pool_bwd<float>(const Geom&, int, const float*, float*, int64_t, int, cudaStream_t);

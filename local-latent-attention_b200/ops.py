@@ -208,7 +208,7 @@ def attn_bwd(dmixed: Tensor, qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tenso
              g_local: Tensor, g_remote: Tensor, local_out: Tensor, lse: Tensor, lat: Tensor,
              lat_lse: Tensor, n_heads: int, latent_heads: int, window: int, local_block: int,
              latent_tokens: int, query_block: int,
-             gate_bias: float) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+             gate_bias: float) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
     dims = _core_dims(qkv, w_rout, n_heads, latent_heads, window, local_block, latent_tokens,
                       query_block, gate_bias)
     _require(dmixed.shape == local_out.shape and dmixed.dtype == qkv.dtype and dmixed.is_contiguous(),
@@ -222,15 +222,16 @@ def attn_bwd(dmixed: Tensor, qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tenso
     db = torch.empty(d, dtype=torch.float32, **kw)
     dgl = torch.empty(hd, dtype=torch.float32, **kw)
     dgr = torch.empty(hd, dtype=torch.float32, **kw)
+    dbqkv = torch.empty(3 * d, dtype=torch.float32, **kw)
     ws_bytes = _lib.lib().llattn_bwd_workspace_bytes(ctypes.byref(dims))
     ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, **kw)
     args = _lib.BwdArgs(dims, _ptr(qkv), _ptr(rq), _ptr(gkv), _ptr(w_rout), _ptr(b_rout),
                         _ptr(g_local), _ptr(g_remote), _ptr(local_out), _ptr(lse), _ptr(lat),
                         _ptr(lat_lse), _ptr(dmixed), _ptr(dqkv), _ptr(drq), _ptr(dgkv), _ptr(dw),
-                        _ptr(db), _ptr(dgl), _ptr(dgr), _ptr(ws), ws.numel())
+                        _ptr(db), _ptr(dgl), _ptr(dgr), _ptr(ws), ws.numel(), _ptr(dbqkv))
     with torch.cuda.device(qkv.device):
         _lib.check(_lib.lib().llattn_bwd(ctypes.byref(args), _stream(qkv)), "llattn_bwd")
-    return dqkv, drq, dgkv, dw, db, dgl, dgr
+    return dqkv, drq, dgkv, dw, db, dgl, dgr, dbqkv
 
 
 @attn_bwd.register_fake
@@ -239,7 +240,8 @@ def _attn_bwd_fake(dmixed, qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, loca
     f32 = torch.float32
     return (torch.empty_like(qkv), torch.empty_like(rq), torch.empty_like(gkv),
             w_rout.new_empty(w_rout.shape, dtype=f32), b_rout.new_empty(b_rout.shape, dtype=f32),
-            g_local.new_empty(g_local.shape, dtype=f32), g_remote.new_empty(g_remote.shape, dtype=f32))
+            g_local.new_empty(g_local.shape, dtype=f32), g_remote.new_empty(g_remote.shape, dtype=f32),
+            qkv.new_empty(qkv.shape[-1], dtype=f32))
 
 
 def _attn_setup(ctx, inputs, output):
@@ -255,7 +257,7 @@ def _attn_backward(ctx, dmixed, _d_local, _d_lse, _d_lat, _d_lat_lse):
     qkv = saved[0]
     if dmixed is None:
         dmixed = torch.zeros_like(saved[7])
-    dqkv, drq, dgkv, dw, db, dgl, dgr = attn_bwd(dmixed.to(qkv.dtype).contiguous(), *saved, *ctx.cfg)
+    dqkv, drq, dgkv, dw, db, dgl, dgr, _ = attn_bwd(dmixed.to(qkv.dtype).contiguous(), *saved, *ctx.cfg)
     return (dqkv, drq, dgkv, dw.to(saved[3].dtype), db, dgl, dgr) + (None,) * 7
 
 
@@ -371,7 +373,7 @@ class BlockFunction(torch.autograd.Function):
             g[11] = torch.mm(dy2.t(), mixed.view(M, d))
         if need[12]:
             g[12] = colsum(dy2)
-        dqkv, drq, dgkv, dw_rout, db_rout, dgl, dgr = attn_bwd(
+        dqkv, drq, dgkv, dw_rout, db_rout, dgl, dgr, db_qkv = attn_bwd(
             dmixed.view(B, T, d), qkv, rq, gkv, w_rout, b_rout_f, gl, gr, local_out, lse, lat, lat_lse,
             n_heads, latent_heads, window, local_block, latent_tokens, query_block, float(gate_bias))
         dqkv2 = dqkv.view(M, 3 * d)
@@ -389,8 +391,8 @@ class BlockFunction(torch.autograd.Function):
             g[0] = dx
         if need[1]:
             g[1] = torch.mm(dqkv2.t(), x2)
-        if need[2]:
-            g[2] = colsum(dqkv2)
+        if need[2]:  # column sums of dqkv, taken by the library's backward from the tiles it holds
+            g[2] = db_qkv.to(dqkv.dtype)
         if need[3]:
             g[3] = torch.mm(drq2.t(), x2 if qsrc is None else qsrc.view(-1, d))
         if need[4]:

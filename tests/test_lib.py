@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
     L = _lib.lib()
     for name in declared_symbols():
         assert hasattr(L, name), name
-    assert L.llattn_version() == 1
+    assert L.llattn_version() == 2
 
 
 @pytest.mark.parametrize("T,Nl,QB,W,LBS", [

@@ -130,7 +130,8 @@ def test_local_bwd_tc_matches_simt(case):
     _, gt = _run_fwd_bwd(inp, H, 2, W, LBS, 32, 0, False)
     assert _fault() == 0
     _, gr = _run_fwd_bwd(inp, H, 2, W, LBS, 32, 0, True)
-    names = ["dqkv", "drq", "dgkv", "dw_rout", "db_rout", "dg_local", "dg_remote"]
+    names = ["dqkv", "drq", "dgkv", "dw_rout", "db_rout", "dg_local", "dg_remote", "db_qkv"]
+    assert len(gt) == len(names)
     d = H * hd
     for name, a, b_ in zip(names, gt, gr):
         if name == "dqkv":

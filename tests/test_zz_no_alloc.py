@@ -48,15 +48,15 @@ def _run(entry, inp, fwd, dm, cfg, with_workspace):
     dims = _lib.make_dims(B, T, H, hd, Lh, ldh, W, LBS, Nl, QB, code, 0.0)
     outs = [torch.empty_like(qkv), torch.empty_like(inp["rq"]), torch.empty_like(inp["gkv"]),
             torch.empty(inp["w"].shape, device="cuda"), torch.empty(H * hd, device="cuda"),
-            torch.empty(hd, device="cuda"), torch.empty(hd, device="cuda")]
+            torch.empty(hd, device="cuda"), torch.empty(hd, device="cuda"), torch.empty(3 * H * hd, device="cuda")]
     ws = None
     if with_workspace:
         n = _lib.lib().llattn_bwd_workspace_bytes(ctypes.byref(dims))
         ws = torch.empty(n, dtype=torch.uint8, device="cuda")
     p = lambda t: t.data_ptr()
     args = _lib.BwdArgs(dims, p(qkv), p(inp["rq"]), p(inp["gkv"]), p(inp["w"]), p(inp["b"]), p(inp["gl"]),
-                        p(inp["gr"]), p(fwd[1]), p(fwd[2]), p(fwd[3]), p(fwd[4]), p(dm), *[p(o) for o in outs],
-                        p(ws) if ws is not None else None, ws.numel() if ws is not None else 0)
+                        p(inp["gr"]), p(fwd[1]), p(fwd[2]), p(fwd[3]), p(fwd[4]), p(dm), *[p(o) for o in outs[:7]],
+                        p(ws) if ws is not None else None, ws.numel() if ws is not None else 0, p(outs[7]))
     rc = entry(ctypes.byref(args), torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert rc == 0, _lib.lib().llattn_last_error().decode()
