@@ -355,8 +355,10 @@ def run_ours(args):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
+    t_host = time.perf_counter()
     for _ in range(args.steps):
         step()
+    host_ms = (time.perf_counter() - t_host) * 1e3 / args.steps  # CPU time to issue a step
     e1.record()
     torch.cuda.synchronize()
     barrier()
@@ -553,6 +555,7 @@ def run_ours(args):
     out = {
         "metric": METRIC, "value": round(value, 1), "value_per_gpu": round(value / world, 1), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "host_issue_ms_per_step": round(host_ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded randn inputs and upstream grad; reference default init)",
         "config": config_json(args.config, world),

@@ -121,6 +121,35 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
 
 bool al(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
 
+std::mutex g_attr_mu;
+struct AttrEntry {
+  const void* kernel;
+  int dev, bytes;
+};
+AttrEntry g_attr[512];
+int g_n_attr = 0;
+
+}  // namespace
+
+cudaError_t set_smem_attr(const void* kernel, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  for (int i = 0; i < g_n_attr; ++i)
+    if (g_attr[i].kernel == kernel && g_attr[i].dev == dev) {
+      if (g_attr[i].bytes >= bytes) return cudaSuccess;
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      if (e == cudaSuccess) g_attr[i].bytes = bytes;
+      return e;
+    }
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && g_n_attr < 512) g_attr[g_n_attr++] = {kernel, dev, bytes};
+  return e;
+}
+
+namespace {
+
 // Host-mapped fault word: a tensor-core kernel whose bounded wait runs out
 // sets it (besides the device word that stops the other CTAs), and every
 // launching entry point tests it first, without synchronising. A fault thus

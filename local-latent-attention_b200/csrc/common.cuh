@@ -30,6 +30,17 @@ struct Geom {
 
 __host__ __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
 
+// cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, bytes) only when
+// this (kernel, device) has not been given at least `bytes` yet: the
+// attribute is per-device state of the function, so the call (a driver
+// round trip) is made once per kernel instance and device instead of on
+// every launch. Thread-safe (api.cu).
+cudaError_t set_smem_attr(const void* kernel, int bytes);
+template <typename K>
+cudaError_t set_smem_once(K kernel, int bytes) {
+  return set_smem_attr(reinterpret_cast<const void*>(kernel), bytes);
+}
+
 // First key visible from query t (inclusive); the last is t-1. Mask of
 // models.py:245-292: 0 < t-j <= W and j >= max(0, qs(t)-W+1), where qs(t) is
 // the first row of t's bsL-block.

@@ -187,7 +187,7 @@ cudaError_t launch_decode(const Geom& g, int64_t cache_len, const T* qkv, const 
   const size_t smem = sizeof(float) * ((size_t)cap + (3 + kDecThreads / 32) * g.hd + g.Ld + 32);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = set_smem_once(decode_kernel<T>, (int)smem);
     if (e != cudaSuccess) return e;
   }
   dim3 grid(g.H, g.B);

@@ -260,8 +260,7 @@ template <typename T, int LM>
 cudaError_t rout_bwd_lm(const Geom& g, const float* drow, const T* lat, const T* w_rout, float* dlat,
                         float* dw_part, int n_split, cudaStream_t s) {
   const size_t sm = sizeof(float) * (32 * 65 + 64 * (LM + 1));
-  cudaError_t e = cudaFuncSetAttribute(rout_dlat_kernel<LM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sm);
+  cudaError_t e = set_smem_once(rout_dlat_kernel<LM>, (int)sm);
   if (e != cudaSuccess) return e;
   const int n_rows = g.B * g.Tq;
   rout_dlat_kernel<LM><<<cdiv(n_rows, 32), 256, sm, s>>>(g, drow, w_rout, sizeof(T) == 2, dlat);
@@ -452,7 +451,7 @@ cudaError_t launch_gate_mix_rmem(const Geom& g, const bf16* local_out, const flo
                                  bf16* mixed, cudaStream_t s) {
   const size_t sm = g.qbs > 1 ? sizeof(bf16) * g.d : 0;
   if (sm > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(gate_mix_rmem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    cudaError_t e = set_smem_once(gate_mix_rmem_kernel, (int)sm);
     if (e != cudaSuccess) return e;
   }
   dim3 grid(g.qbs > 1 ? g.Tq : cdiv(g.T, RM_TOK), g.B);
@@ -476,7 +475,7 @@ cudaError_t launch_gate_fwd(const Geom& g, const T* local_out, const T* lat, con
                             const float* b_rout, const float* g_local, const float* g_remote, T* mixed,
                             cudaStream_t s) {
   const size_t sm = sizeof(float) * (2 * g.d + g.Ld + 2 * g.H);
-  cudaError_t e = cudaFuncSetAttribute(gate_fwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  cudaError_t e = set_smem_once(gate_fwd_kernel<T>, (int)sm);
   if (e != cudaSuccess) return e;
   dim3 grid(g.T, g.B);
   gate_fwd_kernel<T><<<grid, NT, sm, s>>>(g, local_out, lat, w_rout, b_rout, g_local, g_remote, mixed);
@@ -489,7 +488,7 @@ cudaError_t launch_gate_bwd(const Geom& g, const T* local_out, const T* lat, con
                             const T* dmixed, T* dl, float* delta, float* drow, float* dg_part,
                             int tok_per_cta, cudaStream_t s) {
   const size_t sm = sizeof(float) * (3 * g.d + g.Ld + g.H);
-  cudaError_t e = cudaFuncSetAttribute(gate_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  cudaError_t e = set_smem_once(gate_bwd_kernel<T>, (int)sm);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.T, tok_per_cta), g.B);
   gate_bwd_kernel<T><<<grid, NT, sm, s>>>(g, local_out, lat, w_rout, b_rout, g_local, g_remote, dmixed, dl,

@@ -484,7 +484,7 @@ __global__ void __launch_bounds__(256) reduce_parts_kernel(const float* __restri
 template <typename T, int L>
 cudaError_t latent_fwd_l(const Geom& g, const T* rq, const T* gkv, T* lat, float* lse, cudaStream_t s) {
   const int sm = (int)sizeof(float) * LatBwdSmem<L>::FLOATS;
-  cudaError_t e = cudaFuncSetAttribute(latent_fwd_blocked_kernel<T, L>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  cudaError_t e = set_smem_once(latent_fwd_blocked_kernel<T, L>, sm);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.Tq, kLatRows), g.Lh, g.B);
   latent_fwd_blocked_kernel<T, L><<<grid, 256, sm, s>>>(g, rq, gkv, lat, lse);
@@ -496,7 +496,7 @@ cudaError_t latent_bwd_l(const Geom& g, const T* rq, const T* gkv, const float* 
                          float* part, int n_split, int n_kg, float* drq_part, cudaStream_t s) {
   const int sm = (int)sizeof(float) * LatBwdSmem<L>::FLOATS;
   auto k = g.Nc <= kLatKeys ? latent_bwd_kernel<T, L, true> : latent_bwd_kernel<T, L, false>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  cudaError_t e = set_smem_once(k, sm);
   if (e != cudaSuccess) return e;
   if (g.Nc <= kLatKeys) n_kg = 1;  // one key tile: nothing to split
   dim3 grid(n_split * n_kg, g.Lh, g.B);

@@ -259,8 +259,7 @@ __global__ void __launch_bounds__(NT) local_dkv_simt_kernel(Geom g, const T* __r
 template <typename T, int HD>
 cudaError_t fwd_hd(const Geom& g, const T* qkv, T* out, float* lse, cudaStream_t s) {
   const size_t sm = sizeof(float) * ((QT + 2 * KT) * (HD + 1) + QT * (KT + 1));
-  cudaError_t e = cudaFuncSetAttribute(local_fwd_simt_kernel<T, HD>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  cudaError_t e = set_smem_once(local_fwd_simt_kernel<T, HD>, (int)sm);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.T, QT), g.H, g.B);
   local_fwd_simt_kernel<T, HD><<<grid, NT, sm, s>>>(g, qkv, out, lse);
@@ -272,11 +271,9 @@ cudaError_t bwd_hd(const Geom& g, const T* qkv, const T* dl, const float* lse, c
                    T* dqkv, cudaStream_t s) {
   const size_t sm1 = sizeof(float) * ((2 * QT + 2 * KT) * (HD + 1) + QT * (KT + 1));
   const size_t sm2 = sizeof(float) * ((2 * QT + 2 * KT) * (HD + 1) + 2 * KT * (QT + 1) + 3 * QT);
-  cudaError_t e = cudaFuncSetAttribute(local_dq_simt_kernel<T, HD>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
+  cudaError_t e = set_smem_once(local_dq_simt_kernel<T, HD>, (int)sm1);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(local_dkv_simt_kernel<T, HD>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2);
+  e = set_smem_once(local_dkv_simt_kernel<T, HD>, (int)sm2);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.T, QT), g.H, g.B);
   local_dq_simt_kernel<T, HD><<<grid, NT, sm1, s>>>(g, qkv, dl, lse, delta, dqkv);

@@ -17,6 +17,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "sm100.cuh"
@@ -114,6 +115,58 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
+// Encoded tensor maps, cached by their full description (base address,
+// sizes, strides, box, swizzle, L2 promotion): a training loop re-launches
+// with the same buffers, and the maps are plain host data, so a hit skips
+// the driver call. Direct-mapped, 1024 entries, under a mutex.
+struct MapKey {
+  const void* base;
+  cuuint64_t dims[5], strides[4];
+  cuuint32_t box[5];
+  int rank, swz, l2;
+  bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+
+CUresult encode_cached(CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims,
+                       const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swz,
+                       CUtensorMapL2promotion l2) {
+  auto enc = get_encode();
+  if (!enc) return CUDA_ERROR_NOT_SUPPORTED;
+  MapKey k;
+  std::memset(&k, 0, sizeof(k));
+  k.base = base;
+  for (int i = 0; i < rank; ++i) {
+    k.dims[i] = dims[i];
+    k.box[i] = box[i];
+    if (i + 1 < rank) k.strides[i] = strides[i];
+  }
+  k.rank = rank;
+  k.swz = (int)swz;
+  k.l2 = (int)l2;
+  uint64_t h = 1469598103934665603ull;  // FNV-1a over the key bytes
+  const unsigned char* p = reinterpret_cast<const unsigned char*>(&k);
+  for (size_t i = 0; i < sizeof(k); ++i) h = (h ^ p[i]) * 1099511628211ull;
+  static std::mutex mu;
+  static MapKey keys[1024];
+  static CUtensorMap maps[1024];
+  static bool used[1024];
+  const int slot = (int)(h % 1024);
+  std::lock_guard<std::mutex> lk(mu);
+  if (used[slot] && keys[slot] == k) {
+    *map = maps[slot];
+    return CUDA_SUCCESS;
+  }
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_SUCCESS) {
+    keys[slot] = k;
+    maps[slot] = *map;
+    used[slot] = true;
+  }
+  return r;
+}
+
 // [B, T, S, H, hd] bf16 viewed as 4-D (hd, S*H, T, B); box (64, 1, rows, 1).
 bool make_rows_map(CUtensorMap* map, const void* base, int B, int T, int slots_x_heads, int hd, int rows = 128) {
   auto enc = get_encode();
@@ -123,9 +176,7 @@ bool make_rows_map(CUtensorMap* map, const void* base, int B, int T, int slots_x
                            (cuuint64_t)T * slots_x_heads * hd * 2};
   cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_cached(map, 4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   return r == CUDA_SUCCESS;
 }
 
@@ -139,9 +190,7 @@ bool make_2d_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
   cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
   cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return encode_cached(map, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B) == CUDA_SUCCESS;
 }
 
 // bf16 matrix [rows, cols] with row stride ld elements, box (64 cols, box_rows rows).
@@ -152,9 +201,7 @@ bool make_ld_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
   cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
   cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return encode_cached(map, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B) == CUDA_SUCCESS;
 }
 
 // bf16 [B, T, d] as 3-D (d, T, B), box (64, 128, 1), 128-byte swizzle.
@@ -165,9 +212,7 @@ bool make_btd_map(CUtensorMap* map, const void* base, int B, int T, int d) {
   cuuint64_t strides[2] = {(cuuint64_t)d * 2, (cuuint64_t)T * d * 2};
   cuuint32_t box[3] = {64, 128, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return encode_cached(map, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE) == CUDA_SUCCESS;
 }
 
 
@@ -204,14 +249,14 @@ cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, 
   }();
   if (pair) {
     const int smem = FwdPPLayout<HD, true>::BYTES;
-    cudaError_t e = cudaFuncSetAttribute(local_fwd_pp_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = set_smem_once(local_fwd_pp_kernel<HD, true>, smem);
     if (e != cudaSuccess) return e;
     dim3 grid(g.H, cdiv(g.T, 2 * BM), g.B);
     local_fwd_pp_kernel<HD, true><<<grid, FwdPPLayout<HD, true>::THREADS, smem, s>>>(
         tq, tkv, tlo, tmx, tlat, tw, g, static_cast<bf16*>(local_out), lse, ep);
   } else {
     const int smem = FwdPPLayout<HD, false>::BYTES;
-    cudaError_t e = cudaFuncSetAttribute(local_fwd_pp_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = set_smem_once(local_fwd_pp_kernel<HD, false>, smem);
     if (e != cudaSuccess) return e;
     dim3 grid(g.H, cdiv(g.T, BM), g.B);
     local_fwd_pp_kernel<HD, false><<<grid, FwdPPLayout<HD, false>::THREADS, smem, s>>>(
@@ -229,7 +274,7 @@ cudaError_t dq_hd(const Geom& g, const void* qkv, const void* dl, const float* l
     return cudaErrorInvalidValue;
   // persistent: one CTA per SM walks the (h, query tile, b) units
   const int smem = DqpLayout<HD>::BYTES;  // the kernel's shared memory is 1024-byte aligned
-  cudaError_t e = cudaFuncSetAttribute(local_dq_persist_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = set_smem_once(local_dq_persist_kernel<HD>, smem);
   if (e != cudaSuccess) return e;
   const int n_units = g.H * cdiv(g.T, BM) * g.B;
   local_dq_persist_kernel<HD><<<std::min(n_units, sm_count()), 320, smem, s>>>(q128, q64, do128, st, g, lse, delta,
@@ -245,7 +290,7 @@ cudaError_t dkv_hd(const Geom& g, const void* qkv, const void* dl, const float* 
       !make_rows_map(&do64, dl, g.B, g.T, g.H, g.hd, 64) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, g.hd, 128))
     return cudaErrorInvalidValue;
   const int smem = DkvLayout<HD>::BYTES;  // the kernel's shared memory is 1024-byte aligned
-  cudaError_t e = cudaFuncSetAttribute(local_dkv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = set_smem_once(local_dkv_tc_kernel<HD>, smem);
   if (e != cudaSuccess) return e;
   // persistent: one CTA per SM walks the (h, key tile, b) units
   const int n_units = g.H * cdiv(g.T, BM) * g.B;
@@ -263,7 +308,7 @@ cudaError_t gate_bwd_hd(const Geom& g, const GateBwd& a, cudaStream_t s) {
       !make_rows_map(&tdl, a.dl, g.B, g.T, g.H, g.hd, 128) || !make_rows_map(&tdr, a.dr, g.B, g.T, g.H, g.hd, 128))
     return cudaErrorInvalidValue;
   const int smem = GbLayout<HD, G>::BYTES + 1024;
-  cudaError_t e = cudaFuncSetAttribute(gate_bwd_tc_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = set_smem_once(gate_bwd_tc_kernel<HD, G>, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.T, BM), g.B);
   gate_bwd_tc_kernel<HD, G><<<grid, GbLayout<HD, G>::THREADS, smem, s>>>(
@@ -301,7 +346,7 @@ cudaError_t launch_gemm(const Geom& g, int M, int N, int K, const void* A, int64
   p.colsum = o.colsum;
   p.colsum_split = o.colsum_split;
   const int smem = GemmLayout::BYTES + 1024;
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = set_smem_once(gemm_tc_kernel, smem);
   if (e != cudaSuccess) return e;
   // every split runs (one whose K range is empty writes zeros): callers sum
   // exactly `splits` partials
@@ -340,7 +385,7 @@ cudaError_t launch_rout_dw(const Geom& g, const void* dr, const void* lat, float
     tl = tm;
   }
   const int smem = DwLayout::BYTES + 1024;  // < 113 KB: two CTAs per SM
-  cudaError_t e = cudaFuncSetAttribute(rout_dw_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = set_smem_once(rout_dw_tc_kernel, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(cdiv(g.d, 128), n_split);
   rout_dw_tc_kernel<<<grid, 192, smem, s>>>(tm, tl, g, static_cast<const bf16*>(lat), dw_part, db_part, n_split);
@@ -362,7 +407,7 @@ cudaError_t launch_latent_bwd_tc(const Geom& g, const void* rq, const void* gkv,
     return cudaErrorMisalignedAddress;
   dim3 grid(n_split, g.Lh, g.B);
   auto run = [&](auto kern, int smem) -> cudaError_t {  // the kernel's shared memory is 1024-byte aligned
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = set_smem_once(kern, smem);
     if (e != cudaSuccess) return e;
     kern<<<grid, 160, smem, s>>>(g, static_cast<const bf16*>(rq), static_cast<const bf16*>(gkv), lat_lse, dlat,
                                  static_cast<bf16*>(drq), part, n_split);
@@ -378,7 +423,7 @@ cudaError_t launch_latent_fwd_tc(const Geom& g, const void* rq, const void* gkv,
   if (((uintptr_t)rq & 15) || ((uintptr_t)gkv & 15) || ((uintptr_t)lat & 15)) return cudaErrorMisalignedAddress;
   const int smem = LatFwdTcLayout::BYTES;  // the kernel's shared memory is 1024-byte aligned
   auto kern = g.ldh <= 32 ? latent_fwd_tc_kernel<32> : latent_fwd_tc_kernel<64>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = set_smem_once(kern, smem);
   if (e != cudaSuccess) return e;
   // up to four CTAs per SM (128 TMEM columns each)
   const int n_split = std::max(1, std::min(cdiv(g.Tq, BM), (4 * sm_count()) / (g.B * g.Lh)));

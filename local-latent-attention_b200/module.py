@@ -24,6 +24,7 @@ from dataclasses import dataclass
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 from torch import Tensor
 
 from . import ops
@@ -110,15 +111,18 @@ class LocalLatentAttentionB200(nn.Module):
                          ("gate_mix_ms", 0.0)):
                 self.profile_totals[k] = self.profile_totals.get(k, 0.0) + v
             for k, v in geo.items():
-                self.profile_totals[k] = self.profile_totals.get(k, 0.0) + v
+                self.profile_totals[k] = self.profile_totals.get(k, 0.0) + float(v)
             self.profile_steps += 1
         self._profile_events = []
 
     def get_profile_stats(self) -> dict[str, float]:
-        """Same keys as the reference. The fused op times local + latent +
-        gate together: its time is reported as local_attention_ms and the
-        latent/gate entries are 0. gate_mean is not computed (NaN): the fused
-        op does not materialise the gate weights."""
+        """Same keys as the reference (models.py:136-157). The fused op runs
+        local + latent + gate as one library call: its time is reported as
+        local_attention_ms and the latent / gate entries are 0 (per-kernel
+        times come from the library's event profiler, llattn_profile_*).
+        gate_mean is the mean local gate weight w_l over tokens and heads,
+        recomputed in profile mode from the op's saved tensors (the fused
+        kernels never materialise the weights)."""
         if not self.profile_enabled:
             return {}
         self._drain_profile()
@@ -133,7 +137,7 @@ class LocalLatentAttentionB200(nn.Module):
             "profile_local_attention_ms": t["local_attention_ms"] / n,
             "profile_latent_attention_ms": t["latent_attention_ms"] / n,
             "profile_gate_mix_ms": t["gate_mix_ms"] / n,
-            "profile_gate_mean": float("nan"),
+            "profile_gate_mean": t["gate_mean"] / n,
             "profile_seq_len": t["seq_len"] / n,
             "profile_local_block_size": t["local_block_size"] / n,
             "profile_latent_count": t["latent_count"] / n,
@@ -189,13 +193,37 @@ class LocalLatentAttentionB200(nn.Module):
         y = self.out(mixed)
         if prof:
             ev[4].record()
+            gate_mean = self._gate_mean(qkv, rq, gkv)  # after the timed phases
             geo = ops.geometry(T, self.latent_tokens, self.latent_query_block_size, self.window,
                                self.local_block_size)
             self._profile_events.append((ev, {
-                "seq_len": T, "local_block_size": geo["local_span"],
+                "gate_mean": gate_mean, "seq_len": T, "local_block_size": geo["local_span"],
                 "latent_count": geo["n_chunks"], "chunk_size": geo["chunk"],
                 "latent_query_block_size": geo["qblock"]}))
         return y
+
+    @torch.no_grad()
+    def _gate_mean(self, qkv: Tensor, rq: Tensor, gkv: Tensor) -> Tensor:
+        """Mean of w_l = sigmoid(local.g_l + gate_bias - remote.g_r) (the
+        weight of models.py:424-437), from the core op's saved local output
+        and latent rows: profile mode only. Returned as a device scalar."""
+        dt = qkv.dtype
+        outs = ops.attn_fwd(qkv.contiguous(), rq.to(dt).contiguous(), gkv.to(dt).contiguous(),
+                            self.r_out.weight.to(dt).contiguous(), self.r_out.bias.float().contiguous(),
+                            self.gate_local.weight.float().reshape(-1).contiguous(),
+                            self.gate_remote.weight.float().reshape(-1).contiguous(), self.n_heads,
+                            self.latent_heads, self.window, self.local_block_size, self.latent_tokens,
+                            self.latent_query_block_size, float(self.gate_bias))
+        local_out, lat = outs[1], outs[3]
+        B, T, d = local_out.shape
+        remote = F.linear(lat.float(), self.r_out.weight.float(), self.r_out.bias.float())
+        qbs = ops.geometry(T, self.latent_tokens, self.latent_query_block_size)["qblock"]
+        if qbs > 1:
+            remote = remote.repeat_interleave(qbs, dim=1)[:, :T]
+        hd = d // self.n_heads
+        sl = local_out.float().view(B, T, self.n_heads, hd) @ self.gate_local.weight.float().reshape(-1)
+        sr = remote.view(B, T, self.n_heads, hd) @ self.gate_remote.weight.float().reshape(-1)
+        return torch.sigmoid(sl + self.gate_bias - sr).mean()
 
     # --- incremental generation ------------------------------------------
 

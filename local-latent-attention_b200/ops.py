@@ -287,6 +287,7 @@ def llattn_attention(qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tensor, b_rou
 # --------------------------------------------------------------------------
 # whole block: projections, pooling, attention core, output projection
 
+@torch.library.custom_op("llattn_b200::colsum", mutates_args=(), device_types="cuda")
 def colsum(g: Tensor) -> Tensor:
     """Column sums of a contiguous [rows, cols] CUDA tensor, in its dtype with
     fp32 accumulation in a fixed order: the bias gradient of a linear layer
@@ -304,16 +305,26 @@ def colsum(g: Tensor) -> Tensor:
     return out
 
 
-def pool_bwd_accumulate_(dx: Tensor, dpooled: Tensor, latent_tokens: int, query_block: int, mode: int) -> Tensor:
+@colsum.register_fake
+def _colsum_fake(g):
+    return g.new_empty(g.shape[1])
+
+
+@torch.library.custom_op("llattn_b200::pool_bwd_accumulate", mutates_args=("dx",), device_types="cuda")
+def pool_bwd_accumulate_(dx: Tensor, dpooled: Tensor, latent_tokens: int, query_block: int, pool_mode: int) -> None:
     """dx [B,T,d] += the pooling gradient of dpooled [B,rows,d] (in place)."""
     _require(dx.is_contiguous() and dpooled.is_contiguous() and dx.dtype == dpooled.dtype,
              "pool_bwd_accumulate_ expects contiguous tensors of one dtype")
     B, T, d = dx.shape
     dims = _lib.make_dims(B, T, latent_tokens=latent_tokens, query_block=query_block, dtype=_dtype_code(dx))
     with torch.cuda.device(dx.device):
-        _lib.check(_lib.lib().llattn_pool_bwd(ctypes.byref(dims), mode | _lib.POOL_ACCUMULATE, _ptr(dpooled),
+        _lib.check(_lib.lib().llattn_pool_bwd(ctypes.byref(dims), pool_mode | _lib.POOL_ACCUMULATE, _ptr(dpooled),
                                               _ptr(dx), d, _stream(dx)), "llattn_pool_bwd")
-    return dx
+
+
+@pool_bwd_accumulate_.register_fake
+def _pool_bwd_accumulate_fake(dx, dpooled, latent_tokens, query_block, pool_mode):
+    return None
 
 
 class BlockFunction(torch.autograd.Function):

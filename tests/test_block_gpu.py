@@ -13,6 +13,7 @@ from __future__ import annotations
 import pytest
 import torch
 
+import llattn_b200
 import llattn_oracle as O
 from parity import TOL, make_cfg, model_config, oracle_block, rel_err
 
@@ -50,7 +51,8 @@ def test_pool_bwd_accumulate(mode):
     dp = torch.randn(B, rows, d, generator=gen, device="cpu").cuda()
     dx0 = torch.randn(B, T, d, generator=gen, device="cpu").cuda()
     want = dx0 + ops.pool_bwd(dp, T, Nl, qb if mode == "qblocks" else 0, m)
-    got = ops.pool_bwd_accumulate_(dx0.clone(), dp, Nl, qb if mode == "qblocks" else 0, m)
+    got = dx0.clone()
+    ops.pool_bwd_accumulate_(got, dp, Nl, qb if mode == "qblocks" else 0, m)
     assert torch.allclose(got, want, rtol=0, atol=1e-6)
 
 
@@ -124,3 +126,50 @@ def test_block_function_under_autocast_matches_per_layer():
     for k in fused[2]:
         assert fused[2][k].dtype == torch.float32
         assert rel_err(fused[2][k], layered[2][k]) < 1e-2, k
+
+
+def test_block_under_torch_compile_matches_eager():
+    """torch.compile over the drop-in block (aot_eager: FakeTensor tracing of
+    the custom ops, their register_fake / register_autograd entries and the
+    autograd graph, with the library kernels as the executed ops) gives the
+    eager outputs and gradients."""
+    B, T, cfg = make_cfg(CASES["tokenwise"])
+    m = llattn_b200.LocalLatentAttentionB200(model_config(cfg))
+    m.load_state_dict(O.init_params(cfg, 0))
+    m = m.cuda().to(torch.bfloat16)
+    gen = torch.Generator().manual_seed(5)
+    x = torch.randn(B, T, cfg.d_model, generator=gen).to(torch.bfloat16).cuda()
+    gy = torch.randn(B, T, cfg.d_model, generator=gen).to(torch.bfloat16).cuda()
+
+    def run(fn):
+        xx = x.clone().requires_grad_(True)
+        m.zero_grad(set_to_none=True)
+        y = fn(xx)
+        y.backward(gy)
+        return y.detach(), xx.grad, {k: p.grad.detach().clone() for k, p in m.named_parameters()}
+
+    eager = run(m)
+    compiled = run(torch.compile(m, backend="aot_eager", fullgraph=True))
+    assert torch.equal(eager[0], compiled[0])
+    assert torch.equal(eager[1], compiled[1])
+    for k in eager[2]:
+        assert torch.equal(eager[2][k], compiled[2][k]), k
+
+
+@pytest.mark.parametrize("bias", [0.0, 8.0, -8.0])
+def test_profile_stats_gate_mean(bias):
+    """Profile mode fills the reference's keys; gate_mean is the mean local
+    gate weight (models.py:450), near 1 / 0 when the gate bias saturates it."""
+    B, T, cfg = make_cfg(CASES["tokenwise"])
+    m = llattn_b200.LocalLatentAttentionB200(model_config(cfg)).cuda().to(torch.bfloat16)
+    m.gate_bias = bias
+    m.set_profile(True)
+    x = torch.randn(B, T, cfg.d_model, device="cuda", dtype=torch.bfloat16)
+    m(x)
+    st = m.get_profile_stats()
+    m.set_profile(False)
+    assert st["profile_local_latent_total_ms"] > 0 and 0.0 < st["profile_gate_mean"] < 1.0
+    if bias > 0:
+        assert st["profile_gate_mean"] > 0.99
+    elif bias < 0:
+        assert st["profile_gate_mean"] < 0.01

@@ -1,5 +1,7 @@
 """Host-side checks of the drop-in module and ops (CPU only)."""
 
+from types import SimpleNamespace
+
 import pytest
 import torch
 
@@ -99,3 +101,39 @@ def test_visible_pairs_matches_oracle_count():
 
     for T, W, lbs in [(2048, 256, 256), (512, 128, 256), (16384, 512, 256), (37, 12, 16), (1, 4, 4), (300, 64, 32)]:
         assert visible_pairs(T, W, lbs) == O.local_pairs(T, W, lbs)
+
+
+def test_fake_tensor_trace_of_the_block():
+    """The custom ops' fake implementations (register_fake) let the whole
+    block trace without a GPU: forward and backward of the drop-in module on
+    FakeTensor CUDA inputs give the real op's shapes and dtypes. This is what
+    torch.compile relies on (the reference's Triton path forbids compile,
+    train.py:694-695)."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    import llattn_b200
+
+    cfg = SimpleNamespace(d_model=176, n_heads=2, local_window=32, local_block_size=64, latent_tokens=16,
+                          latent_d_model=512, latent_heads=8, latent_query_block_size=0, dropout=0.0, n_layers=1,
+                          use_triton_kernel=True)
+    m = llattn_b200.LocalLatentAttentionB200(cfg)
+    with FakeTensorMode() as fm:
+        params = {k: fm.from_tensor(v).to(device="cuda", dtype=torch.bfloat16).requires_grad_(True)
+                  for k, v in m.named_parameters()}
+        x = torch.empty(2, 300, 176, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        y = torch.func.functional_call(m, params, (x,))
+        assert y.shape == x.shape and y.dtype == torch.bfloat16 and y.device.type == "cuda"
+        # the backward op's fake (autograd's engine itself needs a device to run)
+        B, T, d, Ld, hd = 2, 300, 176, 512, 88
+        bf = dict(device="cuda", dtype=torch.bfloat16)
+        f32 = dict(device="cuda", dtype=torch.float32)
+        qkv = torch.empty(B, T, 3 * d, **bf)
+        outs = torch.ops.llattn_b200.attn_fwd(qkv, torch.empty(B, T, Ld, **bf), torch.empty(B, 16, 2 * Ld, **bf),
+                                              torch.empty(d, Ld, **bf), torch.empty(d, **f32),
+                                              torch.empty(hd, **f32), torch.empty(hd, **f32), 2, 8, 32, 64, 16, 0, 0.0)
+        grads = torch.ops.llattn_b200.attn_bwd(outs[0], qkv, torch.empty(B, T, Ld, **bf),
+                                               torch.empty(B, 16, 2 * Ld, **bf), torch.empty(d, Ld, **bf),
+                                               torch.empty(d, **f32), torch.empty(hd, **f32), torch.empty(hd, **f32),
+                                               *outs[1:], 2, 8, 32, 64, 16, 0, 0.0)
+        want = [(B, T, 3 * d), (B, T, Ld), (B, 16, 2 * Ld), (d, Ld), (d,), (hd,), (hd,), (3 * d,)]
+        assert [tuple(g.shape) for g in grads] == want
