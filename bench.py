@@ -335,7 +335,12 @@ def run_ours(args):
         y = m(xx)
         y.backward(gg)
         if world > 1:
-            # data-parallel exchange: one flat bucket, all_reduce_mean
+            # data-parallel exchange: one flat bucket, all_reduce_mean. The
+            # block is one autograd node, so its gradients all appear at the
+            # end of its backward: there is nothing left to overlap the
+            # exchange with inside the step (DDP over the block measured
+            # slower: 2.50 vs 2.42 ms at N=2); the LM below overlaps DDP
+            # buckets with the earlier layers' backward
             torch.cat([p.grad.reshape(-1) for p in params], out=flat)
             D.all_reduce_mean(flat)
 
