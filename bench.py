@@ -36,6 +36,9 @@ Keys beyond the base contract:
                 latent 384/8 heads) at B16 x T2048, with their kernel groups
   lm            cfg4: the LocalLatentLM training step (24 layers, d1536, B16 x
                 T2048 per GPU, AdamW, DDP) at the same N, its own e2e
+  lm_0.55b      the same step for the reference's 0.55b preset (22 layers,
+                d1408, H16, latent 512 over 8 heads), with vs_published = per-GPU
+                tok/s over the reference's published 108k tok/s/GPU (H200)
   clocks        nvidia-smi samples taken during the timed region
 
 --impl reference times the reference's CPU implementation of the path on a
@@ -489,9 +492,11 @@ def run_ours(args):
     barrier()
     del m, params, x, g, xs, gs, flat
     torch.cuda.empty_cache()
-    lm = None
+    lm = lm055 = None
     if not args.no_lm and args.config == "cfg2":
         lm = measure_lm(args, world, rank, dev)
+        torch.cuda.empty_cache()
+        lm055 = measure_lm(args, world, rank, dev, shape="0.55b")
 
     if rank != 0:
         if world > 1:
@@ -578,6 +583,7 @@ def run_ours(args):
         "clocks": clk,
         "presets": presets,
         "lm": lm,
+        "lm_0.55b": lm055,
     }
     print(json.dumps(out), flush=True)
     if world > 1:
@@ -649,7 +655,17 @@ def run_lm(args):
     D.cleanup_distributed()
 
 
-def measure_lm(args, world, rank, device, steps=None):
+# LM shapes: cfg4 and the reference's 0.55b training preset
+# (train.py:71-80), whose LM throughput the reference publishes (
+# 108k tok/s/GPU, 1 H200, torch.compile, batch 16 x 2048, PyTorch attention)
+LM_SHAPES = {
+    "cfg4": dict(d_model=1536, n_heads=12, n_layers=24, d_ff=4096, latent_d_model=64, latent_heads=2),
+    "0.55b": dict(d_model=1408, n_heads=16, n_layers=22, d_ff=4096, latent_d_model=512, latent_heads=8),
+}
+LM_PUBLISHED = {"0.55b": 108000.0}
+
+
+def measure_lm(args, world, rank, device, steps=None, shape="cfg4"):
     """cfg4: LocalLatentLM (24 x d1536 H12 W256 Nl64 Ld64, d_ff 4096, V32000,
     tied embeddings), B16 x T2048 per GPU, bf16 autocast, fused AdamW, DDP
     gradient all-reduce over NCCL (bucketed, overlapping the backward; the
@@ -667,8 +683,10 @@ def measure_lm(args, world, rank, device, steps=None):
     warmup = max(3, min(args.warmup, 5))
     B = (args.batch if args.workload == "lm" else 0) or 16
     T = 2048
-    cfg = ModelConfig(vocab_size=32000, max_seq_len=T, d_model=1536, n_heads=12, n_layers=args.layers, d_ff=4096,
-                      local_window=256, latent_tokens=64, latent_d_model=64, latent_heads=2)
+    sh = dict(LM_SHAPES[shape])
+    if shape == "cfg4":
+        sh["n_layers"] = args.layers
+    cfg = ModelConfig(vocab_size=32000, max_seq_len=T, local_window=256, latent_tokens=64, **sh)
     torch.manual_seed(0)  # identical init on every rank (DDP also broadcasts rank 0's)
     model = LocalLatentLM(cfg).to(device)
     n_params = sum(p.numel() for p in model.parameters())
@@ -738,7 +756,10 @@ def measure_lm(args, world, rank, device, steps=None):
             "steps": steps, "warmup": warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded uniform tokens in [0, 32000))",
-            "config": {"workload": "LocalLatentLM training step (cfg4)", "model": "LocalLatentLM 0.55B-class",
+            "vs_published": (round(tokens / world / (ms / 1e3) / LM_PUBLISHED[shape], 3)
+                             if shape in LM_PUBLISHED else None),
+            "config": {"workload": f"LocalLatentLM training step ({shape})", "model": f"LocalLatentLM {shape}",
+                       "d_model": cfg.d_model, "n_heads": cfg.n_heads, "latent_d_model": cfg.latent_d_model,
                        "n_layers": cfg.n_layers, "params": n_params, "global_batch": B * world, "seq_len": T,
                        "parallelism": f"dp{world}", "l2": "inputs and activations larger than L2"},
             "e2e": {"value": round(tokens / (ms_e2e / 1e3), 1), "unit": "tokens/s",
