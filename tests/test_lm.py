@@ -156,3 +156,72 @@ def test_lm_matches_reference_golden_bf16():
     bad = {k: v for k, v in errs.items() if not v <= tol}
     print({k: round(v, 5) for k, v in errs.items()})
     assert not bad, bad
+
+
+def _installed_reference_models():
+    """The reference's models.py as installed in baseline/_ref (placed there by
+    __graft_entry__.build(), travels with the working tree); skip where absent."""
+    import importlib.util
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    path = os.path.join(root, "baseline", "_ref", "models.py")
+    if not os.path.exists(path):
+        pytest.skip("reference not installed in baseline/_ref")
+    spec = importlib.util.spec_from_file_location("llattn_installed_reference_models", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+@pytest.mark.gpu
+def test_reference_lm_runs_the_b200_block_at_cfg4_width():
+    """The reference's own LocalLatentLM (models.py:505-576), built through its
+    own _build_attention switched to the B200 block (use_in_reference), at the
+    cfg4 width (d1536 H12 W256 Nl64 Ld64, d_ff 4096, vocab 32000; 2 layers,
+    B2 x T512), trains on the GPU under bf16 autocast and matches the same
+    model with the reference's PyTorch attention in fp32: logits, loss and
+    every gradient within 2e-2 (max-norm and Frobenius)."""
+    import torch.nn.functional as F
+    from parity import TOL, frob_err, rel_err
+
+    from llattn_b200.lm import use_in_reference
+
+    models = _installed_reference_models()
+    shape = dict(vocab_size=32000, max_seq_len=512, d_model=1536, n_heads=12, n_layers=2, d_ff=4096,
+                 local_window=256, latent_tokens=64, latent_d_model=64, latent_heads=2)
+    torch.manual_seed(0)
+    ref = models.LocalLatentLM(models.ModelConfig(**shape, use_triton_kernel=False))
+    with torch.no_grad():
+        for p in ref.parameters():
+            p.copy_(p.to(torch.bfloat16).float())
+    saved = models._build_attention
+    try:
+        use_in_reference(models)
+        ours = models.LocalLatentLM(models.ModelConfig(**shape, use_triton_kernel=True))
+    finally:
+        models._build_attention = saved
+    ours.load_state_dict(ref.state_dict())
+    gen = torch.Generator().manual_seed(3)
+    ids = torch.randint(0, shape["vocab_size"], (2, 513), generator=gen).cuda()
+    V = shape["vocab_size"]
+
+    ref = ref.cuda()
+    logits_r = ref(ids[:, :-1])
+    loss_r = F.cross_entropy(logits_r.reshape(-1, V), ids[:, 1:].reshape(-1))
+    loss_r.backward()
+    ours = ours.cuda()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        logits = ours(ids[:, :-1])
+        loss = F.cross_entropy(logits.float().reshape(-1, V), ids[:, 1:].reshape(-1))
+    loss.backward()
+    tol = TOL[torch.bfloat16]
+    errs = {"logits": rel_err(logits.float(), logits_r), "logits/frob": frob_err(logits.float(), logits_r),
+            "loss": abs(loss.item() - loss_r.item()) / abs(loss_r.item())}
+    gr = dict(ref.named_parameters())
+    for k, p in ours.named_parameters():
+        errs[k] = rel_err(p.grad, gr[k].grad)
+        errs[k + "/frob"] = frob_err(p.grad, gr[k].grad)
+    bad = {k: v for k, v in errs.items() if not v <= tol}
+    print(max(errs.values()))
+    assert not bad, bad
