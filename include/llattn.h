@@ -76,9 +76,20 @@ typedef struct llattn_dims {
   int32_t query_block;     /* latent_query_block_size; <= 1 = token-wise  */
   int32_t dtype;           /* llattn_dtype of activations                 */
   float gate_bias;         /* added to the local gate logit (0 = reference) */
+  /* Sequence shards (since LLATTN_VERSION 2; both 0 = a whole sequence): the
+   * call's row 0 is global position seq_offset of a total_len-token
+   * sequence. The local block span, latent chunking and query blocks follow
+   * total_len; masks and chunk ids follow global positions; gkv holds every
+   * chunk of the whole sequence. The buffers must hold every key the rows'
+   * outputs need (a shard plus a left halo of at least window rows, the
+   * halo rows' own outputs being unused); seq_offset is a multiple of the
+   * query block for block-pooled queries. */
+  int32_t seq_offset;
+  int32_t total_len;
 } llattn_dims;
 
-/* Quantities derived from llattn_dims exactly as models.py derives them. */
+/* Quantities derived from llattn_dims exactly as models.py derives them
+ * (chunk / local_span / qblock from total_len; n_qrows over this call's rows). */
 typedef struct llattn_geom {
   int32_t chunk;        /* cs  = ceil(T / min(Nl, T))          models.py:175-183 */
   int32_t n_chunks;     /* Nc  = ceil(T / cs)                                  */

@@ -49,6 +49,11 @@ int make_geom(const llattn_dims* d, Geom* g) {
   if (d->dtype != LLATTN_F32 && d->dtype != LLATTN_BF16) return fail(LLATTN_ERR_ARG, "unknown dtype %d", d->dtype);
   if ((int64_t)d->n_heads * d->head_dim > (1 << 20)) return fail(LLATTN_ERR_ARG, "d_model too large");
   const int T = d->seq_len;
+  const int TT = d->total_len > 0 ? d->total_len : T;
+  if (d->seq_offset < 0 || (int64_t)d->seq_offset + T > TT)
+    return fail(LLATTN_ERR_ARG, "seq_offset %d + seq_len %d exceeds total_len %d", d->seq_offset, T, TT);
+  g->off = d->seq_offset;
+  g->T_total = TT;
   g->B = d->batch;
   g->T = T;
   g->H = d->n_heads;
@@ -58,11 +63,13 @@ int make_geom(const llattn_dims* d, Geom* g) {
   g->ldh = d->latent_head_dim;
   g->Ld = d->latent_heads * d->latent_head_dim;
   g->W = d->window;
-  g->bsL = std::min(T, std::max(d->window, d->local_block));
-  const int target = std::min(d->latent_tokens, T);
-  g->cs = cdiv(T, target);
-  g->Nc = cdiv(T, g->cs);
-  g->qbs = d->query_block > 1 ? std::min(T, d->query_block) : 1;
+  g->bsL = std::min(TT, std::max(d->window, d->local_block));
+  const int target = std::min(d->latent_tokens, TT);
+  g->cs = cdiv(TT, target);
+  g->Nc = cdiv(TT, g->cs);
+  g->qbs = d->query_block > 1 ? std::min(TT, d->query_block) : 1;
+  if (g->off % g->qbs)
+    return fail(LLATTN_ERR_ARG, "seq_offset %d must be a multiple of the query block %d", g->off, g->qbs);
   g->Tq = cdiv(T, g->qbs);
   g->gate_bias = d->gate_bias;
   g->scale = 1.0f / sqrtf((float)g->hd);

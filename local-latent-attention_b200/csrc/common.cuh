@@ -20,6 +20,11 @@ using bf16 = __nv_bfloat16;
 struct Geom {
   int B, T, H, hd, d, Lh, ldh, Ld;
   int W, bsL, cs, Nc, qbs, Tq;
+  // sequence shards: row 0 of this call is global position `off` of a
+  // sequence of `T_total` tokens; bsL, cs, Nc and qbs follow T_total, the
+  // masks and chunk ids follow global positions (off = 0, T_total = T for
+  // a whole sequence)
+  int off, T_total;
   float gate_bias;
   float scale;      // 1/sqrt(hd)
   float lat_scale;  // 1/sqrt(ldh)
@@ -45,11 +50,22 @@ cudaError_t set_smem_once(K kernel, int bytes) {
 // models.py:245-292: 0 < t-j <= W and j >= max(0, qs(t)-W+1), where qs(t) is
 // the first row of t's bsL-block.
 __host__ __device__ __forceinline__ int local_lo(const Geom& g, int t) {
-  int qs = (t / g.bsL) * g.bsL;
-  int lo = t - g.W;
+  const int tg = t + g.off;  // global position
+  int qs = (tg / g.bsL) * g.bsL;
+  int lo = tg - g.W;
   int lo2 = qs - g.W + 1;
   lo = lo > lo2 ? lo : lo2;
+  lo = (lo > 0 ? lo : 0) - g.off;  // back to this call's rows (a shard holds the keys it needs)
   return lo > 0 ? lo : 0;
+}
+
+// Last query (inclusive, this call's rows) that sees key j: t - j <= W and t
+// before the end of the bsL-block holding global position j + W - 1.
+__host__ __device__ __forceinline__ int local_hi(const Geom& g, int j) {
+  const int jg = j + g.off;
+  const int a = jg + g.W, bnd = ((jg + g.W - 1) / g.bsL + 1) * g.bsL - 1;
+  const int hi = (a < bnd ? a : bnd) - g.off;
+  return hi < g.T - 1 ? hi : g.T - 1;
 }
 
 __host__ __device__ __forceinline__ bool local_visible(const Geom& g, int t, int j) {
@@ -59,7 +75,7 @@ __host__ __device__ __forceinline__ bool local_visible(const Geom& g, int t, int
 // Latent chunk count visible from latent query row r (chunks j < qid(r)),
 // models.py:208-212, 227-229, 363-365.
 __host__ __device__ __forceinline__ int row_qid(const Geom& g, int r) {
-  int t = r * g.qbs;
+  int t = g.off + r * g.qbs;
   int c = t / g.cs;
   return c < g.Nc - 1 ? c : g.Nc - 1;
 }

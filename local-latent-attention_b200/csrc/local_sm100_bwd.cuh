@@ -598,7 +598,7 @@ __global__ void __launch_bounds__(320, 1)
       const bool valid = j < g.T;
       // queries that see key j form one range: t in (j, j+W] with qs(t) <= j+W-1,
       // i.e. t < the end of the bsL-block holding j+W-1 (mask of models.py:286-292)
-      const int t_hi = min(min(j + g.W, ((j + g.W - 1) / g.bsL + 1) * g.bsL - 1), g.T - 1);  // inclusive
+      const int t_hi = local_hi(g, j);  // inclusive
       const float* lse_b = lse + ((int64_t)t.b * g.H + t.h) * g.T;
       const float* d_b = delta + ((int64_t)t.b * g.H + t.h) * g.T;
       // this lane's -lse*log2(e) / D for the next query tile, loaded one tile ahead

@@ -28,14 +28,17 @@ _DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
 
 
 def geometry(seq_len: int, latent_tokens: int, query_block: int, window: int = 1,
-             local_block: int = 256) -> dict:
+             local_block: int = 256, total_len: int = 0) -> dict:
     """Derived sizes, as models.py derives them (cs/Nc :175-183, bsL :249,
-    bs/Tq :216-219). Pure Python so fake tensors need no library call."""
-    target = min(latent_tokens, seq_len)
-    cs = math.ceil(seq_len / target)
-    qbs = min(seq_len, query_block) if query_block > 1 else 1
-    return {"chunk": cs, "n_chunks": math.ceil(seq_len / cs),
-            "local_span": min(seq_len, max(window, local_block)),
+    bs/Tq :216-219). Pure Python so fake tensors need no library call. For a
+    shard of a total_len-token sequence the chunking, block span and query
+    block follow total_len and n_qrows counts the shard's query rows."""
+    TT = total_len if total_len > 0 else seq_len
+    target = min(latent_tokens, TT)
+    cs = math.ceil(TT / target)
+    qbs = min(TT, query_block) if query_block > 1 else 1
+    return {"chunk": cs, "n_chunks": math.ceil(TT / cs),
+            "local_span": min(TT, max(window, local_block)),
             "qblock": qbs, "n_qrows": math.ceil(seq_len / qbs)}
 
 
@@ -141,14 +144,16 @@ def pool_query_blocks(x: Tensor, latent_tokens: int, query_block: int) -> Tensor
 # fused attention core: local + latent + r_out + gate + mix
 
 def _core_dims(qkv: Tensor, w_rout: Tensor, n_heads: int, latent_heads: int, window: int,
-               local_block: int, latent_tokens: int, query_block: int, gate_bias: float):
+               local_block: int, latent_tokens: int, query_block: int, gate_bias: float,
+               seq_offset: int = 0, total_len: int = 0):
     B, T, three_d = qkv.shape
     d = three_d // 3
     _require(three_d == 3 * d and d % n_heads == 0, "qkv last dim must be 3 * n_heads * head_dim")
     Ld = w_rout.shape[1]
     _require(Ld % latent_heads == 0, "latent_d_model must be divisible by latent_heads")
     return _lib.make_dims(B, T, n_heads, d // n_heads, latent_heads, Ld // latent_heads, window,
-                          local_block, latent_tokens, query_block, _dtype_code(qkv), gate_bias)
+                          local_block, latent_tokens, query_block, _dtype_code(qkv), gate_bias,
+                          seq_offset, total_len)
 
 
 def _check_core_inputs(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, dims, geo):
@@ -171,10 +176,11 @@ def _check_core_inputs(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, dims, ge
 def attn_fwd(qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tensor, b_rout: Tensor,
              g_local: Tensor, g_remote: Tensor, n_heads: int, latent_heads: int, window: int,
              local_block: int, latent_tokens: int, query_block: int,
-             gate_bias: float) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+             gate_bias: float, seq_offset: int = 0,
+             total_len: int = 0) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
     dims = _core_dims(qkv, w_rout, n_heads, latent_heads, window, local_block, latent_tokens,
-                      query_block, gate_bias)
-    geo = geometry(dims.seq_len, latent_tokens, query_block, window, local_block)
+                      query_block, gate_bias, seq_offset, total_len)
+    geo = geometry(dims.seq_len, latent_tokens, query_block, window, local_block, total_len)
     _check_core_inputs(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, dims, geo)
     B, T, H = dims.batch, dims.seq_len, dims.n_heads
     d, Ld, Tq = H * dims.head_dim, w_rout.shape[1], geo["n_qrows"]
@@ -194,10 +200,10 @@ def attn_fwd(qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tensor, b_rout: Tenso
 
 @attn_fwd.register_fake
 def _attn_fwd_fake(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, n_heads, latent_heads, window,
-                   local_block, latent_tokens, query_block, gate_bias):
+                   local_block, latent_tokens, query_block, gate_bias, seq_offset=0, total_len=0):
     B, T, three_d = qkv.shape
     d = three_d // 3
-    Tq = geometry(T, latent_tokens, query_block)["n_qrows"]
+    Tq = geometry(T, latent_tokens, query_block, total_len=total_len)["n_qrows"]
     f32 = torch.float32
     return (qkv.new_empty(B, T, d), qkv.new_empty(B, T, d), qkv.new_empty(B, n_heads, T, dtype=f32),
             qkv.new_empty(B, Tq, w_rout.shape[1]), qkv.new_empty(B, latent_heads, Tq, dtype=f32))
@@ -207,10 +213,10 @@ def _attn_fwd_fake(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, n_heads, lat
 def attn_bwd(dmixed: Tensor, qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tensor, b_rout: Tensor,
              g_local: Tensor, g_remote: Tensor, local_out: Tensor, lse: Tensor, lat: Tensor,
              lat_lse: Tensor, n_heads: int, latent_heads: int, window: int, local_block: int,
-             latent_tokens: int, query_block: int,
-             gate_bias: float) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+             latent_tokens: int, query_block: int, gate_bias: float, seq_offset: int = 0,
+             total_len: int = 0) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
     dims = _core_dims(qkv, w_rout, n_heads, latent_heads, window, local_block, latent_tokens,
-                      query_block, gate_bias)
+                      query_block, gate_bias, seq_offset, total_len)
     _require(dmixed.shape == local_out.shape and dmixed.dtype == qkv.dtype and dmixed.is_contiguous(),
              "dmixed must be a contiguous [B, T, d] tensor of the activation dtype")
     d, hd = dims.n_heads * dims.head_dim, dims.head_dim
@@ -258,7 +264,7 @@ def _attn_backward(ctx, dmixed, _d_local, _d_lse, _d_lat, _d_lat_lse):
     if dmixed is None:
         dmixed = torch.zeros_like(saved[7])
     dqkv, drq, dgkv, dw, db, dgl, dgr, _ = attn_bwd(dmixed.to(qkv.dtype).contiguous(), *saved, *ctx.cfg)
-    return (dqkv, drq, dgkv, dw.to(saved[3].dtype), db, dgl, dgr) + (None,) * 7
+    return (dqkv, drq, dgkv, dw.to(saved[3].dtype), db, dgl, dgr) + (None,) * 9
 
 
 attn_fwd.register_autograd(_attn_backward, setup_context=_attn_setup)

@@ -95,3 +95,19 @@ def test_bwd_rejects_small_workspace():
     args.workspace_bytes = 16
     assert _lib.lib().llattn_bwd(ctypes.byref(args), None) == 4
     assert "workspace" in _lib.lib().llattn_last_error().decode()
+
+
+def test_shard_offset_validation():
+    """Sequence shards: geometry follows total_len, bad offsets are rejected on the host."""
+    from llattn_b200 import _lib
+
+    g = _lib.Geom()
+    L = _lib.lib()
+    # offset + length beyond the total, and an offset off the query-block grid, are rejected
+    bad = _lib.make_dims(1, 100, 1, 64, 1, 32, 16, 256, 8, 0, _lib.BF16, 0.0, 950, 1000)
+    assert L.llattn_geometry(ctypes.byref(bad), ctypes.byref(g)) == 1
+    bad = _lib.make_dims(1, 100, 1, 64, 1, 32, 16, 256, 8, 64, _lib.BF16, 0.0, 100, 1000)
+    assert L.llattn_geometry(ctypes.byref(bad), ctypes.byref(g)) == 1
+    ok = _lib.make_dims(1, 128, 1, 64, 1, 32, 16, 256, 8, 64, _lib.BF16, 0.0, 128, 1000)
+    assert L.llattn_geometry(ctypes.byref(ok), ctypes.byref(g)) == 0
+    assert (g.chunk, g.n_chunks, g.qblock, g.n_qrows) == (125, 8, 64, 2)
