@@ -207,8 +207,9 @@ __global__ void __launch_bounds__(GbLayout<HD, G>::THREADS, G == 1 ? 2 : 1)
         tc_fence_after();
         const uint64_t dda = desc_sw128(smem_u32(smem + L::DM + s * L::TILE), 16, 1024);
         const uint64_t dwm = desc_sw128(smem_u32(smem + L::W + s * HD * 128), 0, 1024);
+        // K steps past a padded head_dim would multiply zero-filled columns: skipped
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk)
+        for (int kk = 0; kk < HD / 16 && kk * 16 < g.hd; ++kk)
           mma_bf16(tDL, desc_add(dda, (kk / 4) * (BM * 128) + (kk % 4) * 32), desc_add(dwm, kk * 2048), idL,
                    (h > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&bars[GB_DL + s]);

@@ -194,8 +194,9 @@ __global__ void __launch_bounds__(320, 1)
         const uint64_t dq = desc_add(dq0, qb * L::QD), ddo = desc_add(ddo0, qb * L::QD);
         const uint64_t dk = desc_add(dk0, sk * L::KV), dv = desc_add(dv0, sk * L::KV);
         const uint32_t tS = tmem + s * BNK, tP = tmem + 128 + s * BNK;
+        // K steps past a padded head_dim would multiply zero-filled columns: skipped
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
+        for (int kk = 0; kk < HD / 16 && kk * 16 < g.hd; ++kk) {
           const uint32_t aoff = (kk / 4) * L::QPANEL + (kk % 4) * 32;
           const uint32_t boff = (kk / 4) * L::KPANEL + (kk % 4) * 32;
           mma_bf16(tS, desc_add(dq, aoff), desc_add(dk, boff), idSP, kk > 0);
@@ -532,8 +533,9 @@ __global__ void __launch_bounds__(320, 1)
         const uint64_t dq = desc_sw128(smem_u32(smem + L::Q + sq * L::QTILE), 16, 1024);
         const uint64_t ddo = desc_sw128(smem_u32(smem + L::DO + sq * L::QTILE), 16, 1024);
         const uint32_t tS = tmem + s * BNQ, tP = tmem + 128 + s * BNQ;
+        // K steps past a padded head_dim would multiply zero-filled columns: skipped
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
+        for (int kk = 0; kk < HD / 16 && kk * 16 < g.hd; ++kk) {
           const uint32_t aoff = (kk / 4) * L::KPANEL + (kk % 4) * 32;
           const uint32_t boff = (kk / 4) * L::QPANEL + (kk % 4) * 32;
           mma_bf16(tS, desc_add(dk0, aoff), desc_add(dq, boff), idSP, kk > 0);

@@ -272,8 +272,9 @@ __global__ void __launch_bounds__(FwdPPLayout<HD, PAIR>::THREADS, PAIR ? 1 : 2)
               const uint64_t dka = desc_sw128(smem_u32(smem + L::K + st * L::KTILE), 16, 1024);
               const uint32_t dst = tmem + x * 128 + (ns[x] & 1) * BNK;
               const uint64_t dqa = x ? dqb0 : dqa0;
+              // K steps past a padded head_dim would multiply zero-filled columns: skipped
 #pragma unroll
-              for (int kk = 0; kk < HD / 16; ++kk)
+              for (int kk = 0; kk < HD / 16 && kk * 16 < g.hd; ++kk)
                 mma_bf16(dst, desc_add(dqa, (kk / 4) * L::QPANEL + (kk % 4) * 32),
                          desc_add(dka, (kk / 4) * L::KPANEL + (kk % 4) * 32), idS, kk > 0);
               mma_commit(&bars[PP_S + 2 * x + (ns[x] & 1)]);
