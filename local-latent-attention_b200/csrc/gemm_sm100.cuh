@@ -177,12 +177,24 @@ __global__ void __launch_bounds__(192, 2)
         }
         if (!row_ok) continue;
         float v[32];
-#pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const int n = nc + q;
-          v[q] = __uint_as_float(r[q]) + ((p.bias && n < p.N) ? __ldg(p.bias + n) : 0.f);
-        }
         const bool full = nc + 32 <= p.N && vec;
+        if (p.bias && full && ((reinterpret_cast<uintptr_t>(p.bias + nc) & 15) == 0)) {
+          const float4* b4 = reinterpret_cast<const float4*>(p.bias + nc);  // 8 vector loads, not 32
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 bb = __ldg(b4 + q);
+            v[4 * q] = __uint_as_float(r[4 * q]) + bb.x;
+            v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + bb.y;
+            v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + bb.z;
+            v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb.w;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) {
+            const int n = nc + q;
+            v[q] = __uint_as_float(r[q]) + ((p.bias && n < p.N) ? __ldg(p.bias + n) : 0.f);
+          }
+        }
         if (p.c_bf16) {
           bf16* dst = static_cast<bf16*>(p.C) + (int64_t)split * p.c_split + orow * p.ldc + nc;
           if (full) {
