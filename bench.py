@@ -35,7 +35,12 @@ Keys beyond the base contract:
                 0.55b d1408 H16 hd88 latent 512/8 heads, 0.60b d1536 H16 hd96
                 latent 384/8 heads) at B16 x T2048, with their kernel groups
   lm            cfg4: the LocalLatentLM training step (24 layers, d1536, B16 x
-                T2048 per GPU, AdamW, DDP) at the same N, its own e2e
+                T2048 per GPU, AdamW, DDP) at the same N, its own e2e; each
+                decoder layer under torch.compile (inductor fuses the norms,
+                MLP activation, residual adds and casts; the attention is the
+                library's kernels, opaque custom ops in the graph), as the
+                reference's published LM numbers use torch.compile;
+                --lm-compile 0 for the eager harness
   lm_0.55b      the same step for the reference's 0.55b preset (22 layers,
                 d1408, H16, latent 512 over 8 heads), with vs_published = per-GPU
                 tok/s over the reference's published 108k tok/s/GPU (H200)
@@ -95,6 +100,9 @@ def parse():
     p.add_argument("--no-lm", action="store_true", help="leave the cfg4 LM measurement out of the block run")
     p.add_argument("--no-presets", action="store_true", help="leave the preset-shape block points out")
     p.add_argument("--sustain-seconds", type=float, default=2.0)
+    p.add_argument("--lm-compile", type=int, default=1,
+                   help="lm: 1 (default) = torch.compile each decoder layer (norms, MLP, residuals fused by inductor; the "
+                        "attention stays the library's kernels, opaque custom ops in the graph)")
     return p.parse_args()
 
 
@@ -690,6 +698,11 @@ def measure_lm(args, world, rank, device, steps=None, shape="cfg4"):
     torch.manual_seed(0)  # identical init on every rank (DDP also broadcasts rank 0's)
     model = LocalLatentLM(cfg).to(device)
     n_params = sum(p.numel() for p in model.parameters())
+    t_compile = None
+    if args.lm_compile:
+        t0 = time.perf_counter()
+        for i, layer in enumerate(model.blocks):
+            model.blocks[i] = torch.compile(layer, fullgraph=True)
     if world > 1:
         model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[device.index], bucket_cap_mb=100,
                                                           gradient_as_bucket_view=True)
@@ -701,6 +714,8 @@ def measure_lm(args, world, rank, device, steps=None, shape="cfg4"):
     for _ in range(warmup):
         train_step(model, opt, ids, tgt)
     torch.cuda.synchronize()
+    if args.lm_compile:
+        t_compile = time.perf_counter() - t0
     D.barrier()
     clocks = ClockSampler(device.index)
     clocks.start()
@@ -771,6 +786,8 @@ def measure_lm(args, world, rank, device, steps=None, shape="cfg4"):
             "gpu_launches": int(sum(v[1] for v in kern.values())),
             "kernels": {k: {"ms_per_step": round(v[0], 4), "launches_per_step": v[1]} for k, v in per_step.items()},
             "final_loss": float(loss.item()),
+            "compiled_layers": bool(args.lm_compile),
+            "compile_and_warmup_s": round(t_compile, 1) if t_compile is not None else None,
             "clocks": clk,
         }
         return out

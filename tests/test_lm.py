@@ -225,3 +225,33 @@ def test_reference_lm_runs_the_b200_block_at_cfg4_width():
     bad = {k: v for k, v in errs.items() if not v <= tol}
     print(max(errs.values()))
     assert not bad, bad
+
+
+@pytest.mark.gpu
+def test_compiled_layers_match_eager_training_step():
+    """Each decoder layer under torch.compile (the bench's LM setting: the
+    B200 attention as opaque custom ops inside inductor's graph) gives the
+    eager layer's loss and gradients within 2e-2."""
+    import copy
+
+    from parity import TOL, rel_err
+
+    torch.manual_seed(0)
+    eager = LocalLatentLM(small_cfg()).cuda()
+    comp = copy.deepcopy(eager)
+    for i, layer in enumerate(comp.blocks):
+        comp.blocks[i] = torch.compile(layer, fullgraph=True)
+    gen = torch.Generator().manual_seed(0)
+    seq = torch.randint(0, 512, (2, 129), generator=gen).cuda()
+    ids, tgt = seq[:, :-1], seq[:, 1:]
+    losses, grads = [], []
+    for m in (eager, comp):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits = m(ids)
+            loss = torch.nn.functional.cross_entropy(logits.float().reshape(-1, 512), tgt.reshape(-1))
+        loss.backward()
+        losses.append(loss.item())
+        grads.append({k.replace("._orig_mod", ""): p.grad for k, p in m.named_parameters()})
+    assert abs(losses[0] - losses[1]) <= 1e-2 * abs(losses[0])
+    for k, g in grads[0].items():
+        assert rel_err(grads[1][k], g) <= TOL[torch.bfloat16], k
