@@ -31,6 +31,8 @@ Keys beyond the base contract:
   cpu_baseline  the CPU oracle (a restatement of the reference PyTorch block)
                 on the host cores, bounded sample
   kernels       per-kernel-group event times (ms per step) and launch counts
+  graphed       the same step captured once as a CUDA graph and replayed
+                (1 GPU): the launch-overhead-free time, for small shapes
   presets       the block at the reference's training presets (train.py:71-92:
                 0.55b d1408 H16 hd88 latent 512/8 heads, 0.60b d1536 H16 hd96
                 latent 384/8 heads) at B16 x T2048, with their kernel groups
@@ -390,6 +392,35 @@ def run_ours(args):
     kern = _lib.profile_read()
     _lib.profile_enable(False)
 
+    # the same step captured once as a CUDA graph and replayed (the library
+    # is capture-safe after its first call: no allocation, no host sync, cached
+    # tensor maps and attributes): what a launch-bound shape gains from graphs
+    graphed = None
+    if world == 1:
+        try:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    step()
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step()
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ms_g = e0.elapsed_time(e1) / args.steps
+            graphed = {"ms_per_step": round(ms_g, 4), "value": round(B * T / (ms_g / 1e3), 1)}
+            del graph
+        except Exception as ex:  # reported, not fatal: the eager figure above is the measurement
+            graphed = {"error": repr(ex)[:200]}
+
     # end to end through the public module: each step's x and upstream grad
     # copied in from pinned host memory and its dx copied back, pipelined
     # over two input/output buffers so that the copies of steps i+1 / i-1
@@ -589,6 +620,7 @@ def run_ours(args):
         "gpu_launches": launches,
         "kernels": {k: {"ms_per_step": round(v[0], 4), "launches_per_step": v[1]} for k, v in per_step.items()},
         "clocks": clk,
+        "graphed": graphed,
         "presets": presets,
         "lm": lm,
         "lm_0.55b": lm055,
