@@ -695,9 +695,10 @@ def run_lm(args):
     D.cleanup_distributed()
 
 
-# LM shapes: cfg4 and the reference's 0.55b training preset
-# (train.py:71-80), whose LM throughput the reference publishes (
-# 108k tok/s/GPU, 1 H200, torch.compile, batch 16 x 2048, PyTorch attention)
+# LM shapes: cfg4 (the benchmark's LM config) and the reference's 0.55b
+# training preset (train.py:71-80), whose LM throughput the reference
+# publishes (README.md:254-257: 108k tok/s/GPU, 1 H200, torch.compile, batch
+# 16 x 2048, PyTorch attention)
 LM_SHAPES = {
     "cfg4": dict(d_model=1536, n_heads=12, n_layers=24, d_ff=4096, latent_d_model=64, latent_heads=2),
     "0.55b": dict(d_model=1408, n_heads=16, n_layers=22, d_ff=4096, latent_d_model=512, latent_heads=8),
