@@ -736,6 +736,7 @@ def measure_lm(args, world, rank, device, steps=None, shape="cfg4"):
         t0 = time.perf_counter()
         for i, layer in enumerate(model.blocks):
             model.blocks[i] = torch.compile(layer, fullgraph=True)
+        model.loss_head = torch.compile(model.loss_head, fullgraph=True)  # norm, tied head, fp32 CE
     if world > 1:
         model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[device.index], bucket_cap_mb=100,
                                                           gradient_as_bucket_view=True)

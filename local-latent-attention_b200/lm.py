@@ -122,13 +122,22 @@ class LocalLatentLM(nn.Module):
         keys = {k for s in per_layer for k in s}
         return {k: sum(s.get(k, 0.0) for s in per_layer) / len(per_layer) for k in keys} if per_layer else {}
 
-    def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
+    def forward(self, input_ids: torch.Tensor, targets: torch.Tensor | None = None) -> torch.Tensor:
+        """Logits [B, T, vocab]; with `targets` [B, T], the mean next-token
+        cross-entropy instead (computed in fp32 by `self.loss_head`, which a
+        caller may replace by a compiled version of itself)."""
         T = input_ids.shape[1]
         x = self.embedding(input_ids) + self.position.weight[:T].unsqueeze(0)
         remat = self.checkpoint_blocks and self.training
         for layer in self.blocks:
             x = checkpoint(layer, x, use_reentrant=False) if remat else layer(x)
+        if targets is not None:
+            return self.loss_head(x, targets)
         return self.lm_head(self.norm(x))
+
+    def loss_head(self, x: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        logits = self.lm_head(self.norm(x))
+        return F.cross_entropy(logits.float().reshape(-1, logits.shape[-1]), targets.reshape(-1))
 
 
     # --- generation ---------------------------------------------------------
@@ -221,8 +230,7 @@ def train_step(model: nn.Module, optimizer, ids: torch.Tensor, targets: torch.Te
     """One optimiser step: bf16 autocast forward, cross-entropy, backward
     (DDP all-reduces the grads), clip, AdamW. Returns the loss (on device)."""
     with torch.autocast(device_type=ids.device.type, dtype=autocast_dtype):
-        logits = model(ids)
-        loss = F.cross_entropy(logits.float().reshape(-1, logits.shape[-1]), targets.reshape(-1))
+        loss = model(ids, targets)
     loss.backward()
     torch.nn.utils.clip_grad_norm_(model.parameters(), grad_clip)
     optimizer.step()
