@@ -237,3 +237,193 @@ __global__ void __launch_bounds__(192, 2)
     tmem_dealloc(tmem, 256);
   }
 }
+
+// Persistent variant (no column sums): one CTA per SM slot walks the output
+// tiles t = blockIdx.x + k * gridDim.x (N tiles fastest, so the CTAs running
+// together share A rows in L2). The shared-memory ring continues across
+// tiles, so the next tile's loads start while this tile's MMAs run, and the
+// accumulator is double-buffered in TMEM (two 128-column buffers): the
+// epilogue of tile k reads one buffer while the MMAs of tile k+1 fill the
+// other. Barriers: ring full / empty per stage, accumulator full / empty per
+// buffer.
+enum { GP_F = 0, GP_E = 3, GP_AF = 6, GP_AE = 8, GP_NB = 10 };
+
+__global__ void __launch_bounds__(192, 2)
+    gemm_tc_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                              Geom g, GemmArgs p) {
+  using L = GemmLayout;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + GP_NB);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n_nt = cdiv(p.N, 128), n_tiles = n_nt * cdiv(p.M, 128);
+  const int nk = cdiv(p.K, 64);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < L::ST; ++s) {
+      mbar_init(&bars[GP_F + s], 1);
+      mbar_init(&bars[GP_E + s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars[GP_AF + b], 1);
+      mbar_init(&bars[GP_AE + b], 128);
+    }
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // accumulator buffer b at [128 b, 128 b + 128)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_a);
+      prefetch_tmap(&tm_b);
+      int it = 0, issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
+        const int n0 = (t % n_nt) * 128, m0 = (t / n_nt) * 128;
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int s = it % L::ST, k0 = i * 64;
+          if (it >= L::ST && !(ok = mbar_wait(&bars[GP_E + s], ((it / L::ST) - 1) & 1, abort, &g_fault_word)))
+            break;
+          mbar_expect_tx(&bars[GP_F + s], 2 * L::TILE);
+          uint8_t* sa = smem + L::A + s * L::TILE;
+          uint8_t* sb = smem + L::B + s * L::TILE;
+          if (p.a_mn) {
+            tma_load_2d(&tm_a, &bars[GP_F + s], sa, m0, k0);
+            tma_load_2d(&tm_a, &bars[GP_F + s], sa + L::TILE / 2, m0 + 64, k0);
+          } else {
+            tma_load_2d(&tm_a, &bars[GP_F + s], sa, k0, m0);
+          }
+          if (p.b_mn) {
+            tma_load_2d(&tm_b, &bars[GP_F + s], sb, n0, k0);
+            tma_load_2d(&tm_b, &bars[GP_F + s], sb + L::TILE / 2, n0 + 64, k0);
+          } else {
+            tma_load_2d(&tm_b, &bars[GP_F + s], sb, k0, n0);
+          }
+          issued = it + 1;
+        }
+      }
+      if (!ok) {
+        raise_fault(g, kFaultProducer, abort);
+        volatile int none = 0;  // let the copies already issued land before the CTA can exit
+        volatile unsigned gnone = 0;
+        for (int i = issued - L::ST < 0 ? 0 : issued - L::ST; i < issued; ++i)
+          mbar_wait(&bars[GP_F + i % L::ST], (i / L::ST) & 1, &none, &gnone, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id = idesc_bf16_f32(128, 128, p.a_mn != 0, p.b_mn != 0);
+      const uint32_t a_step = p.a_mn ? 2048 : 32, b_step = p.b_mn ? 2048 : 32;
+      const uint32_t a_lbo = p.a_mn ? L::TILE / 2 : 16, b_lbo = p.b_mn ? L::TILE / 2 : 16;
+      int it = 0, k = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++k) {
+        const int buf = k & 1;
+        // the epilogue has read this buffer's previous tile (k - 2)
+        if (k >= 2 && !(ok = mbar_wait(&bars[GP_AE + buf], ((k >> 1) - 1) & 1, abort, &g_fault_word))) break;
+        tc_fence_after();
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int s = it % L::ST;
+          if (!(ok = mbar_wait(&bars[GP_F + s], (it / L::ST) & 1, abort, &g_fault_word))) break;
+          tc_fence_after();
+          const uint64_t da = desc_sw128(smem_u32(smem + L::A + s * L::TILE), a_lbo, 1024);
+          const uint64_t db = desc_sw128(smem_u32(smem + L::B + s * L::TILE), b_lbo, 1024);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16(tmem + 128 * buf, desc_add(da, kk * a_step), desc_add(db, kk * b_step), id,
+                     (i > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&bars[GP_E + s]);
+        }
+        if (!ok) break;
+        mma_commit(&bars[GP_AF + buf]);
+      }
+      if (!ok) raise_fault(g, kFaultMma, abort);
+    }
+  } else {
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const bool vec = (p.ldc % 8) == 0;
+    int k = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++k) {
+      const int buf = k & 1, n0 = (t % n_nt) * 128, m0 = (t / n_nt) * 128;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[GP_AF + buf], (k >> 1) & 1, abort, &g_fault_word));
+      if (!ok) break;
+      tc_fence_after();
+      const int m = m0 + 32 * (warp & 3) + lane;
+      const bool row_ok = m < p.M;
+      const int64_t orow = row_ok ? (int64_t)(m / p.rows_per_group) * p.group_stride +
+                                        (int64_t)(m % p.rows_per_group) * p.row_step
+                                  : 0;
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        const int nc = n0 + cc * 32;
+        if (nc >= p.N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld32(tmem + 128 * buf + lane_off + cc * 32, r);
+        tmem_ld_wait();
+        if (!row_ok) continue;
+        float v[32];
+        const bool full = nc + 32 <= p.N && vec;
+        if (p.bias && full && ((reinterpret_cast<uintptr_t>(p.bias + nc) & 15) == 0)) {
+          const float4* b4 = reinterpret_cast<const float4*>(p.bias + nc);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 bb = __ldg(b4 + q);
+            v[4 * q] = __uint_as_float(r[4 * q]) + bb.x;
+            v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + bb.y;
+            v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + bb.z;
+            v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb.w;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) {
+            const int n = nc + q;
+            v[q] = __uint_as_float(r[q]) + ((p.bias && n < p.N) ? __ldg(p.bias + n) : 0.f);
+          }
+        }
+        if (p.c_bf16) {
+          bf16* dst = static_cast<bf16*>(p.C) + orow * p.ldc + nc;
+          if (full) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              reinterpret_cast<uint4*>(dst)[q] =
+                  make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]), pack_bf16(v[8 * q + 2], v[8 * q + 3]),
+                             pack_bf16(v[8 * q + 4], v[8 * q + 5]), pack_bf16(v[8 * q + 6], v[8 * q + 7]));
+          } else {
+            for (int q = 0; q < 32 && nc + q < p.N; ++q) dst[q] = __float2bfloat16_rn(v[q]);
+          }
+        } else {
+          float* dst = static_cast<float*>(p.C) + orow * p.ldc + nc;
+          if (full && (p.ldc % 4) == 0) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          } else {
+            for (int q = 0; q < 32 && nc + q < p.N; ++q) dst[q] = v[q];
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars[GP_AE + buf]);  // this buffer may take the tile after next
+    }
+    if (!ok) raise_fault(g, kFaultEpilogue, abort);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}

@@ -346,6 +346,14 @@ cudaError_t launch_gemm(const Geom& g, int M, int N, int K, const void* A, int64
   p.colsum = o.colsum;
   p.colsum_split = o.colsum_split;
   const int smem = GemmLayout::BYTES + 1024;
+  if (!o.colsum && splits == 1 && K > 0) {
+    // persistent: two CTAs per SM walk the output tiles, double-buffered accumulators
+    cudaError_t e = set_smem_once(gemm_tc_persistent_kernel, smem);
+    if (e != cudaSuccess) return e;
+    const int n_tiles = cdiv(N, 128) * cdiv(M, 128);
+    gemm_tc_persistent_kernel<<<std::min(n_tiles, 2 * sm_count()), 192, smem, s>>>(ta, tb, g, p);
+    return cudaGetLastError();
+  }
   cudaError_t e = set_smem_once(gemm_tc_kernel, smem);
   if (e != cudaSuccess) return e;
   // every split runs (one whose K range is empty writes zeros): callers sum
