@@ -18,6 +18,8 @@
  *   llattn_pool_fwd / llattn_pool_bwd
  *       LocalLatentAttention._pool_to_latents      models.py:159-214
  *       LocalLatentAttention._pool_query_blocks    models.py:216-230
+ *   llattn_pool_proj_fwd / llattn_pool_proj_bwd
+ *       the pooling with rkv_proj / rq_proj       models.py:159-230, 333-347
  *   llattn_fwd
  *       kernels/llattn_op.py:34-84   _call_fwd (launch of llattn_fwd_kernel)
  *       with the math of models.py:232-305 (local) and :355-438 (latent,
@@ -235,6 +237,26 @@ LLATTN_API int llattn_pool_fwd(const llattn_dims* dims, int mode, const void* x,
  * LLATTN_POOL_ACCUMULATE). */
 LLATTN_API int llattn_pool_bwd(const llattn_dims* dims, int mode, const void* dpooled,
                     void* dx, int64_t d, void* stream);
+
+/* Pooling fused with the latent projections. The pooled means are linear,
+ * so chunk_mean(x) W_rkv^T + b_rkv = chunk_mean(x W_rkv^T) + b_rkv and
+ * qblock_mean(x) W_rq^T + b_rq = qblock_mean(x W_rq^T) + b_rq: the caller
+ * projects every token once, z = x [W_rkv; W_rq]^T (one GEMM, no bias), and
+ * this pools the 3 Ld-wide rows of z instead of the d-wide rows of x.
+ *   z    [B*T, ldz] dtype: columns [0, 2Ld) = x W_rkv^T, [2Ld, 3Ld) = x W_rq^T
+ *   gkv  [B, Nc, 2Ld] = chunk means of z[:, :2Ld] + b_rkv
+ *   rq   [B, Tq, Ld]  = query-block means of z[:, 2Ld:] + b_rq (the token's
+ *        own row when latent_query_block_size <= 1)
+ * b_rkv [2Ld] / b_rq [Ld] (dtype) may be NULL. Whole sequences only
+ * (seq_offset 0). Replaces the pooling and the two latent Linears of
+ * LocalLatentAttention.forward (models.py:159-230, :333-347). */
+LLATTN_API int llattn_pool_proj_fwd(const llattn_dims* dims, const void* z, int64_t ldz,
+                    const void* b_rkv, const void* b_rq, void* gkv, void* rq, void* stream);
+/* Its gradient with respect to z: dz[:, :2Ld] = dgkv of the token's chunk /
+ * the chunk's count, dz[:, 2Ld:3Ld] = drq of the token's query block / bs
+ * (or the token's own drq). Columns of dz past 3 Ld are left alone. */
+LLATTN_API int llattn_pool_proj_bwd(const llattn_dims* dims, const void* dgkv, const void* drq,
+                    void* dz, int64_t ldz, void* stream);
 
 /* Bias gradient of a linear layer: out[c] = sum_r g[r, c] over a row-major
  * [rows, cols] matrix of dtype (LLATTN_BF16 / LLATTN_F32), fp32

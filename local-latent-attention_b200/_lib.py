@@ -20,7 +20,7 @@ EXPORTED = (
     "llattn_version", "llattn_last_error", "llattn_fault_status", "llattn_geometry", "llattn_bwd_workspace_bytes",
     "llattn_pool_fwd", "llattn_pool_bwd", "llattn_fwd", "llattn_bwd", "llattn_bwd_noalloc", "llattn_decode",
     "llattn_profile_enable", "llattn_profile_read", "llattn_profile_name", "llattn_colsum_workspace_bytes",
-    "llattn_colsum", "llattn_fault_inject_host",
+    "llattn_colsum", "llattn_fault_inject_host", "llattn_pool_proj_fwd", "llattn_pool_proj_bwd",
 )
 
 
@@ -92,6 +92,10 @@ def lib() -> ctypes.CDLL:
             fn = getattr(L, name)
             fn.argtypes = [ctypes.POINTER(Dims), ctypes.c_int, _vp, _vp, ctypes.c_int64, _vp]
             fn.restype = ctypes.c_int
+        L.llattn_pool_proj_fwd.argtypes = [ctypes.POINTER(Dims), _vp, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp]
+        L.llattn_pool_proj_fwd.restype = ctypes.c_int
+        L.llattn_pool_proj_bwd.argtypes = [ctypes.POINTER(Dims), _vp, _vp, _vp, ctypes.c_int64, _vp]
+        L.llattn_pool_proj_bwd.restype = ctypes.c_int
         L.llattn_colsum_workspace_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int]
         L.llattn_colsum_workspace_bytes.restype = ctypes.c_size_t
         L.llattn_colsum.argtypes = [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _vp, _vp, ctypes.c_size_t, _vp]

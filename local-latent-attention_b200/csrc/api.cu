@@ -550,6 +550,42 @@ int llattn_pool_bwd(const llattn_dims* dims, int mode, const void* dpooled, void
   return check_launch(launch_pool_bwd<float>(g, mode, (const float*)dpooled, (float*)dx, d, acc, s), "pool_bwd");
 }
 
+int llattn_pool_proj_fwd(const llattn_dims* dims, const void* z, int64_t ldz, const void* b_rkv, const void* b_rq,
+                         void* gkv, void* rq, void* stream) {
+  Geom g;
+  int rc = make_geom(dims, &g);
+  if (rc) return rc;
+  if (!z || !gkv || !rq) return fail(LLATTN_ERR_ARG, "pool_proj_fwd: NULL pointer");
+  if (g.off != 0 || g.T_total != g.T) return fail(LLATTN_ERR_ARG, "pool_proj_fwd: whole sequences only");
+  if (ldz < 3 * (int64_t)g.Ld) return fail(LLATTN_ERR_ARG, "pool_proj_fwd: ldz %lld < 3 * latent_d_model", (long long)ldz);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  prof::Scope ps(prof::POOL_FWD, s);
+  if (dims->dtype == LLATTN_BF16)
+    return check_launch(launch_pool_proj_fwd<bf16>(g, (const bf16*)z, ldz, (const bf16*)b_rkv, (const bf16*)b_rq,
+                                                   (bf16*)gkv, (bf16*)rq, s),
+                        "pool_proj_fwd");
+  return check_launch(launch_pool_proj_fwd<float>(g, (const float*)z, ldz, (const float*)b_rkv, (const float*)b_rq,
+                                                  (float*)gkv, (float*)rq, s),
+                      "pool_proj_fwd");
+}
+
+int llattn_pool_proj_bwd(const llattn_dims* dims, const void* dgkv, const void* drq, void* dz, int64_t ldz,
+                         void* stream) {
+  Geom g;
+  int rc = make_geom(dims, &g);
+  if (rc) return rc;
+  if (!dgkv || !drq || !dz) return fail(LLATTN_ERR_ARG, "pool_proj_bwd: NULL pointer");
+  if (g.off != 0 || g.T_total != g.T) return fail(LLATTN_ERR_ARG, "pool_proj_bwd: whole sequences only");
+  if (ldz < 3 * (int64_t)g.Ld) return fail(LLATTN_ERR_ARG, "pool_proj_bwd: ldz %lld < 3 * latent_d_model", (long long)ldz);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  prof::Scope ps(prof::POOL_BWD, s);
+  if (dims->dtype == LLATTN_BF16)
+    return check_launch(launch_pool_proj_bwd<bf16>(g, (const bf16*)dgkv, (const bf16*)drq, (bf16*)dz, ldz, s),
+                        "pool_proj_bwd");
+  return check_launch(launch_pool_proj_bwd<float>(g, (const float*)dgkv, (const float*)drq, (float*)dz, ldz, s),
+                      "pool_proj_bwd");
+}
+
 size_t llattn_colsum_workspace_bytes(int64_t rows, int64_t cols, int dtype) {
   if (rows < 1 || cols < 1 || (dtype != LLATTN_BF16 && dtype != LLATTN_F32)) return 0;
   return sizeof(float) * (size_t)colsum_splits(rows, cols, dtype == LLATTN_BF16 ? 2 : 4) * (size_t)cols;

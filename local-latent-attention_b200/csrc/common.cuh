@@ -117,6 +117,11 @@ cudaError_t launch_pool_fwd(const Geom& g, int mode, const T* x, T* out, int64_t
 template <typename T>
 cudaError_t launch_pool_bwd(const Geom& g, int mode, const T* dout, T* dx, int64_t d, int accumulate,
                             cudaStream_t s);
+template <typename T>
+cudaError_t launch_pool_proj_fwd(const Geom& g, const T* z, int64_t ldz, const T* b_rkv, const T* b_rq, T* gkv,
+                                 T* rq, cudaStream_t s);
+template <typename T>
+cudaError_t launch_pool_proj_bwd(const Geom& g, const T* dgkv, const T* drq, T* dz, int64_t ldz, cudaStream_t s);
 // out[c] = sum_r g[r, c] over a row-major [rows, cols] matrix; part holds
 // colsum_splits(rows, cols, sizeof(T)) x cols floats
 int colsum_splits(int64_t rows, int64_t cols, int elem_bytes);

@@ -121,6 +121,93 @@ __global__ void __launch_bounds__(256) pool_bwd_kernel(const T* __restrict__ dou
   Vec<T, V>::store(dst, v);
 }
 
+// Pooling fused with the latent projections (llattn_pool_proj_*). The
+// pooled means are linear, so chunk_mean(x) W^T + b = chunk_mean(x W^T) + b
+// and the same for the query-block means (models.py:159-230, :333-347): the
+// projections run per token as ONE GEMM z = x [W_rkv; W_rq]^T ([B*T, 3Ld],
+// no bias), and these kernels pool the 3Ld-wide rows of z instead of the
+// d-wide rows of x. Part 0 = gkv (columns [0, 2Ld) of z, chunk means over
+// the true count, + b_rkv), part 1 = rq (columns [2Ld, 3Ld), query-block
+// means with zero padding counted, or the token's own row when qbs = 1,
+// + b_rq). Thread = one (output row, 16-byte column group) item.
+struct PoolPart {
+  int col0, cols, rows, size, full_divisor;
+};
+
+template <typename T, int V>
+__global__ void __launch_bounds__(256) pool_proj_fwd_kernel(const T* __restrict__ z, int64_t ldz, int T_, int B,
+                                                            PoolPart p0, PoolPart p1, const T* __restrict__ b0,
+                                                            const T* __restrict__ b1, T* __restrict__ out0,
+                                                            T* __restrict__ out1) {
+  const PoolPart p = blockIdx.y ? p1 : p0;
+  const T* bias = blockIdx.y ? b1 : b0;
+  T* out = blockIdx.y ? out1 : out0;
+  const int ng = p.cols / V;
+  const int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (item >= (int64_t)B * p.rows * ng) return;
+  const int cg = (int)(item % ng);
+  const int64_t br = item / ng;  // b * rows + r
+  const int b = (int)(br / p.rows), r = (int)(br % p.rows);
+  const int t0 = r * p.size, t1 = min(t0 + p.size, T_);
+  const T* src = z + ((int64_t)b * T_ + t0) * ldz + p.col0 + cg * V;
+  float acc[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = 0.f;
+  int t = t0;
+  for (; t + 4 <= t1; t += 4) {  // four rows in flight
+    float v0[V], v1[V], v2[V], v3[V];
+    Vec<T, V>::load(src, v0);
+    Vec<T, V>::load(src + ldz, v1);
+    Vec<T, V>::load(src + 2 * ldz, v2);
+    Vec<T, V>::load(src + 3 * ldz, v3);
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] += (v0[i] + v1[i]) + (v2[i] + v3[i]);
+    src += 4 * ldz;
+  }
+  for (; t < t1; ++t) {
+    float v0[V];
+    Vec<T, V>::load(src, v0);
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] += v0[i];
+    src += ldz;
+  }
+  const float inv = 1.f / (float)(p.full_divisor ? p.size : (t1 - t0));
+  float bv[V];
+  if (bias) {
+    Vec<T, V>::load(bias + cg * V, bv);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) bv[i] = 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = fmaf(acc[i], inv, bv[i]);
+  Vec<T, V>::store(out + br * p.cols + cg * V, acc);
+}
+
+// The gradient of the above with respect to z: dz[b*T + t, col0 + j] =
+// dout[b, row(t), j] / divisor(row(t)); thread = one (token, column group).
+template <typename T, int V>
+__global__ void __launch_bounds__(256) pool_proj_bwd_kernel(const T* __restrict__ d0, const T* __restrict__ d1,
+                                                            T* __restrict__ dz, int64_t ldz, int T_, int B,
+                                                            PoolPart p0, PoolPart p1) {
+  const PoolPart p = blockIdx.y ? p1 : p0;
+  const T* dout = blockIdx.y ? d1 : d0;
+  const int ng = p.cols / V;
+  const int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (item >= (int64_t)B * T_ * ng) return;
+  const int cg = (int)(item % ng);
+  const int64_t bt = item / ng;
+  const int b = (int)(bt / T_), t = (int)(bt % T_);
+  const int r = t / p.size;
+  const int cnt = p.full_divisor ? p.size : (min((r + 1) * p.size, T_) - r * p.size);
+  float v[V];
+  Vec<T, V>::load(dout + ((int64_t)b * p.rows + r) * p.cols + cg * V, v);
+  const float inv = 1.f / (float)cnt;
+#pragma unroll
+  for (int i = 0; i < V; ++i) v[i] *= inv;
+  Vec<T, V>::store(dz + bt * ldz + p.col0 + cg * V, v);
+}
+
 // Column sums of a row-major [rows, cols] matrix (the bias gradient of a
 // linear layer: the sum of its output gradient over tokens), fp32
 // accumulation. Block: 32 column groups of V columns x 8 row lanes; blockIdx.y
@@ -223,6 +310,56 @@ cudaError_t launch_pool_bwd(const Geom& g, int mode, const T* dout, T* dx, int64
   }
   return cudaGetLastError();
 }
+
+namespace {
+void pool_proj_parts(const Geom& g, PoolPart* p0, PoolPart* p1) {
+  *p0 = PoolPart{0, 2 * g.Ld, g.Nc, g.cs, 0};
+  *p1 = PoolPart{2 * g.Ld, g.Ld, g.Tq, g.qbs, 1};
+}
+}  // namespace
+
+template <typename T>
+cudaError_t launch_pool_proj_fwd(const Geom& g, const T* z, int64_t ldz, const T* b_rkv, const T* b_rq, T* gkv,
+                                 T* rq, cudaStream_t s) {
+  PoolPart p0, p1;
+  pool_proj_parts(g, &p0, &p1);
+  constexpr int V = vec_width<T>();
+  const bool vec = g.Ld % V == 0 && ldz % V == 0 && aligned16(z) && aligned16(gkv) && aligned16(rq) &&
+                   (!b_rkv || aligned16(b_rkv)) && (!b_rq || aligned16(b_rq));
+  const int v = vec ? V : 1;
+  const int64_t items = std::max<int64_t>((int64_t)g.B * p0.rows * (p0.cols / v), (int64_t)g.B * p1.rows * (p1.cols / v));
+  dim3 grid((unsigned)((items + 255) / 256), 2);
+  if (vec)
+    pool_proj_fwd_kernel<T, V><<<grid, 256, 0, s>>>(z, ldz, g.T, g.B, p0, p1, b_rkv, b_rq, gkv, rq);
+  else
+    pool_proj_fwd_kernel<T, 1><<<grid, 256, 0, s>>>(z, ldz, g.T, g.B, p0, p1, b_rkv, b_rq, gkv, rq);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_pool_proj_bwd(const Geom& g, const T* dgkv, const T* drq, T* dz, int64_t ldz, cudaStream_t s) {
+  PoolPart p0, p1;
+  pool_proj_parts(g, &p0, &p1);
+  constexpr int V = vec_width<T>();
+  const bool vec = g.Ld % V == 0 && ldz % V == 0 && aligned16(dz) && aligned16(dgkv) && aligned16(drq);
+  const int v = vec ? V : 1;
+  const int64_t items = (int64_t)g.B * g.T * (p0.cols / v);  // part 0 is the wider one
+  dim3 grid((unsigned)((items + 255) / 256), 2);
+  if (vec)
+    pool_proj_bwd_kernel<T, V><<<grid, 256, 0, s>>>(dgkv, drq, dz, ldz, g.T, g.B, p0, p1);
+  else
+    pool_proj_bwd_kernel<T, 1><<<grid, 256, 0, s>>>(dgkv, drq, dz, ldz, g.T, g.B, p0, p1);
+  return cudaGetLastError();
+}
+
+template cudaError_t launch_pool_proj_fwd<float>(const Geom&, const float*, int64_t, const float*, const float*,
+                                                 float*, float*, cudaStream_t);
+template cudaError_t launch_pool_proj_fwd<bf16>(const Geom&, const bf16*, int64_t, const bf16*, const bf16*, bf16*,
+                                                bf16*, cudaStream_t);
+template cudaError_t launch_pool_proj_bwd<float>(const Geom&, const float*, const float*, float*, int64_t,
+                                                 cudaStream_t);
+template cudaError_t launch_pool_proj_bwd<bf16>(const Geom&, const bf16*, const bf16*, bf16*, int64_t,
+                                                cudaStream_t);
 
 // SMs of the current device, cached per device
 int sm_count() {

@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+from typing import Optional
 
 import torch
 from torch import Tensor
@@ -128,6 +129,70 @@ def _pool_backward(ctx, grad):
 
 
 pool_fwd.register_autograd(_pool_backward, setup_context=_pool_setup)
+
+
+# Pooling fused with the latent projections (llattn_pool_proj_fwd/bwd): z =
+# x [W_rkv; W_rq]^T per token, then the chunk / query-block means of z's rows.
+
+def _pp_dims(B, T, latent_heads, latent_d_model, latent_tokens, query_block, t):
+    return _lib.make_dims(B, T, latent_heads=latent_heads, latent_head_dim=latent_d_model // latent_heads,
+                          latent_tokens=latent_tokens, query_block=query_block, dtype=_dtype_code(t))
+
+
+@torch.library.custom_op("llattn_b200::pool_proj_fwd", mutates_args=(), device_types="cuda")
+def pool_proj_fwd(z: Tensor, b_rkv: Optional[Tensor], b_rq: Optional[Tensor], batch: int, latent_heads: int,
+                  latent_tokens: int, query_block: int) -> tuple[Tensor, Tensor]:
+    """z [B*T, 3Ld] (x W_rkv^T | x W_rq^T, no bias) -> gkv [B, Nc, 2Ld] (chunk
+    means + b_rkv), rq [B, Tq, Ld] (query-block means or the rows, + b_rq)."""
+    _require(z.dim() == 2 and z.stride(1) == 1 and z.is_cuda, "pool_proj_fwd expects a row-major 2-D CUDA tensor")
+    _require(z.shape[1] % 3 == 0 and z.shape[0] % batch == 0, "pool_proj_fwd: z must be [B*T, 3*latent_d_model]")
+    Ld, T = z.shape[1] // 3, z.shape[0] // batch
+    geo = geometry(T, latent_tokens, query_block)
+    gkv = torch.empty(batch, geo["n_chunks"], 2 * Ld, dtype=z.dtype, device=z.device)
+    rq = torch.empty(batch, geo["n_qrows"], Ld, dtype=z.dtype, device=z.device)
+    for b in (b_rkv, b_rq):
+        _require(b is None or (b.is_contiguous() and b.dtype == z.dtype), "pool_proj_fwd: biases must match z")
+    dims = _pp_dims(batch, T, latent_heads, Ld, latent_tokens, query_block, z)
+    with torch.cuda.device(z.device):
+        _lib.check(_lib.lib().llattn_pool_proj_fwd(ctypes.byref(dims), _ptr(z), z.stride(0),
+                                                   _ptr(b_rkv) if b_rkv is not None else None,
+                                                   _ptr(b_rq) if b_rq is not None else None, _ptr(gkv), _ptr(rq),
+                                                   _stream(z)), "llattn_pool_proj_fwd")
+    return gkv, rq
+
+
+@pool_proj_fwd.register_fake
+def _pool_proj_fwd_fake(z, b_rkv, b_rq, batch, latent_heads, latent_tokens, query_block):
+    Ld, T = z.shape[1] // 3, z.shape[0] // batch
+    geo = geometry(T, latent_tokens, query_block)
+    return z.new_empty(batch, geo["n_chunks"], 2 * Ld), z.new_empty(batch, geo["n_qrows"], Ld)
+
+
+@torch.library.custom_op("llattn_b200::pool_proj_bwd", mutates_args=(), device_types="cuda")
+def pool_proj_bwd(dgkv: Tensor, drq: Tensor, seq_len: int, latent_heads: int, latent_tokens: int,
+                  query_block: int) -> Tensor:
+    """dgkv [B, Nc, 2Ld], drq [B, Tq, Ld] -> dz [B*T, 3Ld], the gradient of
+    pool_proj_fwd with respect to z."""
+    _require(dgkv.is_contiguous() and drq.is_contiguous() and dgkv.dtype == drq.dtype,
+             "pool_proj_bwd expects contiguous gradients of one dtype")
+    B, Ld = dgkv.shape[0], drq.shape[-1]
+    dz = torch.empty(B * seq_len, 3 * Ld, dtype=dgkv.dtype, device=dgkv.device)
+    dims = _pp_dims(B, seq_len, latent_heads, Ld, latent_tokens, query_block, dgkv)
+    with torch.cuda.device(dgkv.device):
+        _lib.check(_lib.lib().llattn_pool_proj_bwd(ctypes.byref(dims), _ptr(dgkv), _ptr(drq), _ptr(dz), dz.stride(0),
+                                                   _stream(dgkv)), "llattn_pool_proj_bwd")
+    return dz
+
+
+@pool_proj_bwd.register_fake
+def _pool_proj_bwd_fake(dgkv, drq, seq_len, latent_heads, latent_tokens, query_block):
+    return dgkv.new_empty(dgkv.shape[0] * seq_len, 3 * drq.shape[-1])
+
+
+# the per-token latent projections cost 3 * 2 M d 3Ld FLOPs over the step
+# against the pooled ones' 2 M d Ld plus the x reads of the pooling: they pay
+# for small latent widths only
+POOL_PROJ_MAX_LATENT = 128
 
 
 def pool_chunks(x: Tensor, latent_tokens: int) -> Tensor:
@@ -356,10 +421,18 @@ class BlockFunction(torch.autograd.Function):
         x = x.contiguous()
         F = torch.nn.functional
         qkv = F.linear(x, w_qkv, b_qkv)
-        pooled = pool_fwd(x, latent_tokens, 0, _lib.POOL_CHUNKS)
-        gkv = F.linear(pooled, w_rkv, b_rkv)
-        qsrc = pool_fwd(x, latent_tokens, query_block, _lib.POOL_QBLOCKS) if query_block > 1 else None
-        rq = F.linear(x if qsrc is None else qsrc, w_rq, b_rq)
+        Ld = w_rq.shape[0]
+        w_z = None
+        if Ld <= POOL_PROJ_MAX_LATENT:  # one GEMM for both latent projections, then pool their rows
+            w_z = torch.cat([w_rkv, w_rq])
+            z = torch.mm(x.view(B * T, d), w_z.t())
+            gkv, rq = pool_proj_fwd(z, b_rkv, b_rq, B, latent_heads, latent_tokens, query_block)
+            pooled = qsrc = None
+        else:
+            pooled = pool_fwd(x, latent_tokens, 0, _lib.POOL_CHUNKS)
+            gkv = F.linear(pooled, w_rkv, b_rkv)
+            qsrc = pool_fwd(x, latent_tokens, query_block, _lib.POOL_QBLOCKS) if query_block > 1 else None
+            rq = F.linear(x if qsrc is None else qsrc, w_rq, b_rq)
         b_rout_f = b_rout.float().contiguous()
         gl = g_local.float().reshape(-1).contiguous()
         gr = g_remote.float().reshape(-1).contiguous()
@@ -368,7 +441,7 @@ class BlockFunction(torch.autograd.Function):
             latent_tokens, query_block, float(gate_bias))
         y = F.linear(mixed, w_out, b_out)
         ctx.save_for_backward(x, qkv, pooled, qsrc, rq, gkv, mixed, local_out, lse, lat, lat_lse, w_qkv, w_rq,
-                              w_rkv, w_rout, b_rout_f, gl, gr, w_out)
+                              w_rkv, w_rout, b_rout_f, gl, gr, w_out, w_z)
         ctx.cfg = cfg
         ctx.dtypes = (b_rout.dtype, g_local.dtype, g_local.shape, g_remote.dtype, g_remote.shape)
         return y
@@ -376,12 +449,12 @@ class BlockFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         (x, qkv, pooled, qsrc, rq, gkv, mixed, local_out, lse, lat, lat_lse, w_qkv, w_rq, w_rkv, w_rout,
-         b_rout_f, gl, gr, w_out) = ctx.saved_tensors
+         b_rout_f, gl, gr, w_out, w_z) = ctx.saved_tensors
         n_heads, latent_heads, window, local_block, latent_tokens, query_block, gate_bias = ctx.cfg
         b_rout_dt, gl_dt, gl_shape, gr_dt, gr_shape = ctx.dtypes
         need = ctx.needs_input_grad
         B, T, d = x.shape
-        M = B * T
+        M, Ld = B * T, w_rq.shape[0]
         dy2 = dy.to(x.dtype).contiguous().view(M, d)
         x2 = x.view(M, d)
         g = [None] * 14
@@ -396,7 +469,14 @@ class BlockFunction(torch.autograd.Function):
         dqkv2 = dqkv.view(M, 3 * d)
         drq2 = drq.view(-1, drq.shape[-1])
         dgkv2 = dgkv.view(-1, dgkv.shape[-1])
-        if need[0]:
+        dz = None
+        if w_z is not None and (need[0] or need[3] or need[5]):
+            dz = pool_proj_bwd(dgkv.contiguous(), drq.contiguous(), T, latent_heads, latent_tokens, query_block)
+        if need[0] and dz is not None:  # x's latent gradients: one beta=1 GEMM into the qkv_proj one
+            dx = torch.mm(dqkv2, w_qkv)
+            dx.addmm_(dz, w_z)
+            g[0] = dx.view(B, T, d)
+        elif need[0]:
             dx = torch.mm(dqkv2, w_qkv)
             if qsrc is None:
                 dx.addmm_(drq2, w_rq)
@@ -410,11 +490,15 @@ class BlockFunction(torch.autograd.Function):
             g[1] = torch.mm(dqkv2.t(), x2)
         if need[2]:  # column sums of dqkv, taken by the library's backward from the tiles it holds
             g[2] = db_qkv.to(dqkv.dtype)
-        if need[3]:
+        if dz is not None and (need[3] or need[5]):
+            dw_z = torch.mm(dz.t(), x2)  # [dW_rkv; dW_rq]
+            g[3] = dw_z[2 * Ld:] if need[3] else None
+            g[5] = dw_z[:2 * Ld] if need[5] else None
+        if need[3] and dz is None:
             g[3] = torch.mm(drq2.t(), x2 if qsrc is None else qsrc.view(-1, d))
         if need[4]:
             g[4] = colsum(drq2)
-        if need[5]:
+        if need[5] and dz is None:
             g[5] = torch.mm(dgkv2.t(), pooled.view(-1, d))
         if need[6]:
             g[6] = colsum(dgkv2)

@@ -81,9 +81,10 @@ def test_block_function_matches_per_layer_autograd(case, dtype):
     m.set_profile(True)  # per-layer path
     layered = _run(m, x, gy)
     m.set_profile(False)
-    # same forward kernels and GEMMs
-    assert torch.equal(fused[0], layered[0])
+    # the fused node pools the projected rows (llattn_pool_proj), the layers
+    # project the pooled rows: equal up to rounding
     tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert rel_err(fused[0], layered[0]) < tol, "y"
     assert rel_err(fused[1], layered[1]) < tol, "dx"
     for k in fused[2]:
         assert rel_err(fused[2][k], layered[2][k]) < tol, k
