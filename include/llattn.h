@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define LLATTN_VERSION 2
+#define LLATTN_VERSION 3
 
 #if defined(__GNUC__)
 #define LLATTN_API __attribute__((visibility("default")))
@@ -88,6 +88,13 @@ typedef struct llattn_dims {
    * query block for block-pooled queries. */
   int32_t seq_offset;
   int32_t total_len;
+  /* Row strides in elements (since LLATTN_VERSION 3; 0 = 3 * d_model, a
+   * contiguous [B, T, 3d]): the qkv rows read by llattn_fwd / llattn_bwd and
+   * the dqkv rows written by llattn_bwd may sit in a wider row-major buffer
+   * (the qkv_proj output beside other per-token projections of one GEMM).
+   * >= 3 d; a multiple of 8 for bf16 when not 3 d (16-byte TMA strides). */
+  int32_t qkv_row_stride;
+  int32_t dqkv_row_stride;
 } llattn_dims;
 
 /* Quantities derived from llattn_dims exactly as models.py derives them
@@ -248,7 +255,8 @@ LLATTN_API int llattn_pool_bwd(const llattn_dims* dims, int mode, const void* dp
  *   rq   [B, Tq, Ld]  = query-block means of z[:, 2Ld:] + b_rq (the token's
  *        own row when latent_query_block_size <= 1)
  * b_rkv [2Ld] / b_rq [Ld] (dtype) may be NULL. Whole sequences only
- * (seq_offset 0). Replaces the pooling and the two latent Linears of
+ * (seq_offset 0), latent_d_model <= 128 (past that, projecting every token
+ * costs more than pooling x first). Replaces the pooling and the two latent Linears of
  * LocalLatentAttention.forward (models.py:159-230, :333-347). */
 LLATTN_API int llattn_pool_proj_fwd(const llattn_dims* dims, const void* z, int64_t ldz,
                     const void* b_rkv, const void* b_rq, void* gkv, void* rq, void* stream);

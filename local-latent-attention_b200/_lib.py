@@ -32,6 +32,7 @@ class Dims(ctypes.Structure):
         ("local_block", ctypes.c_int32), ("latent_tokens", ctypes.c_int32),
         ("query_block", ctypes.c_int32), ("dtype", ctypes.c_int32), ("gate_bias", ctypes.c_float),
         ("seq_offset", ctypes.c_int32), ("total_len", ctypes.c_int32),
+        ("qkv_row_stride", ctypes.c_int32), ("dqkv_row_stride", ctypes.c_int32),
     ]
 
 
@@ -142,10 +143,11 @@ def check(rc: int, what: str) -> None:
 
 def make_dims(batch, seq_len, n_heads=1, head_dim=1, latent_heads=1, latent_head_dim=1,
               window=1, local_block=256, latent_tokens=1, query_block=0, dtype=F32,
-              gate_bias=0.0, seq_offset=0, total_len=0) -> Dims:
+              gate_bias=0.0, seq_offset=0, total_len=0, qkv_row_stride=0, dqkv_row_stride=0) -> Dims:
     return Dims(int(batch), int(seq_len), int(n_heads), int(head_dim), int(latent_heads),
                 int(latent_head_dim), int(window), int(local_block), int(latent_tokens),
-                int(query_block), int(dtype), float(gate_bias), int(seq_offset), int(total_len))
+                int(query_block), int(dtype), float(gate_bias), int(seq_offset), int(total_len),
+                int(qkv_row_stride), int(dqkv_row_stride))
 
 
 def geometry(dims: Dims) -> Geom:

@@ -71,6 +71,13 @@ int make_geom(const llattn_dims* d, Geom* g) {
   if (g->off % g->qbs)
     return fail(LLATTN_ERR_ARG, "seq_offset %d must be a multiple of the query block %d", g->off, g->qbs);
   g->Tq = cdiv(T, g->qbs);
+  const int d3 = 3 * d->n_heads * d->head_dim;
+  g->ldq = d->qkv_row_stride > 0 ? d->qkv_row_stride : d3;
+  g->ldd = d->dqkv_row_stride > 0 ? d->dqkv_row_stride : d3;
+  if (g->ldq < d3 || g->ldd < d3)
+    return fail(LLATTN_ERR_ARG, "qkv / dqkv row strides (%d, %d) below 3 * d_model = %d", g->ldq, g->ldd, d3);
+  if (d->dtype == LLATTN_BF16 && ((g->ldq != d3 && g->ldq % 8) || (g->ldd != d3 && g->ldd % 8)))
+    return fail(LLATTN_ERR_ARG, "bf16 qkv / dqkv row strides must be multiples of 8");
   g->gate_bias = d->gate_bias;
   g->scale = 1.0f / sqrtf((float)g->hd);
   g->lat_scale = 1.0f / sqrtf((float)g->ldh);
@@ -469,7 +476,7 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
   if (rc || !a->db_qkv) return rc;
   prof::Scope pc(prof::COLSUM, s, 2);
   return check_launch(launch_colsum<T, float>(static_cast<const T*>(a->dqkv), (int64_t)g.B * g.T, 3 * (int64_t)g.d,
-                                              reinterpret_cast<float*>(ws + L.dbqkv), a->db_qkv, s),
+                                              reinterpret_cast<float*>(ws + L.dbqkv), a->db_qkv, s, g.ldd),
                       "colsum_dbqkv");
 }
 
@@ -558,6 +565,7 @@ int llattn_pool_proj_fwd(const llattn_dims* dims, const void* z, int64_t ldz, co
   if (!z || !gkv || !rq) return fail(LLATTN_ERR_ARG, "pool_proj_fwd: NULL pointer");
   if (g.off != 0 || g.T_total != g.T) return fail(LLATTN_ERR_ARG, "pool_proj_fwd: whole sequences only");
   if (ldz < 3 * (int64_t)g.Ld) return fail(LLATTN_ERR_ARG, "pool_proj_fwd: ldz %lld < 3 * latent_d_model", (long long)ldz);
+  if (g.Ld > 128) return fail(LLATTN_ERR_ARG, "pool_proj_fwd: latent_d_model %d > 128", g.Ld);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   prof::Scope ps(prof::POOL_FWD, s);
   if (dims->dtype == LLATTN_BF16)
@@ -577,6 +585,7 @@ int llattn_pool_proj_bwd(const llattn_dims* dims, const void* dgkv, const void* 
   if (!dgkv || !drq || !dz) return fail(LLATTN_ERR_ARG, "pool_proj_bwd: NULL pointer");
   if (g.off != 0 || g.T_total != g.T) return fail(LLATTN_ERR_ARG, "pool_proj_bwd: whole sequences only");
   if (ldz < 3 * (int64_t)g.Ld) return fail(LLATTN_ERR_ARG, "pool_proj_bwd: ldz %lld < 3 * latent_d_model", (long long)ldz);
+  if (g.Ld > 128) return fail(LLATTN_ERR_ARG, "pool_proj_bwd: latent_d_model %d > 128", g.Ld);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   prof::Scope ps(prof::POOL_BWD, s);
   if (dims->dtype == LLATTN_BF16)

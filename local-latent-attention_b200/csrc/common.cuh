@@ -25,6 +25,9 @@ struct Geom {
   // masks and chunk ids follow global positions (off = 0, T_total = T for
   // a whole sequence)
   int off, T_total;
+  // row strides (elements) of qkv (read) and dqkv (written): 3d unless the
+  // rows sit in a wider buffer
+  int ldq, ldd;
   float gate_bias;
   float scale;      // 1/sqrt(hd)
   float lat_scale;  // 1/sqrt(ldh)
@@ -127,7 +130,8 @@ cudaError_t launch_pool_proj_bwd(const Geom& g, const T* dgkv, const T* drq, T* 
 int colsum_splits(int64_t rows, int64_t cols, int elem_bytes);
 int sm_count();  // SMs of the current device
 template <typename T, typename To = T>
-cudaError_t launch_colsum(const T* g, int64_t rows, int64_t cols, float* part, To* out, cudaStream_t s);
+cudaError_t launch_colsum(const T* g, int64_t rows, int64_t cols, float* part, To* out, cudaStream_t s,
+                          int64_t ld = 0);  // ld: row stride in elements (0 = cols)
 template <typename To>
 cudaError_t launch_reduce_parts(const float* part, int n_part, int64_t n, To* out, cudaStream_t s);
 

@@ -41,7 +41,7 @@ __global__ void __launch_bounds__(NT) local_fwd_simt_kernel(Geom g, const T* __r
   float(*sp)[KT + 1] = reinterpret_cast<float(*)[KT + 1]>(sv + KT);
   const int q0 = blockIdx.x * QT, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, i = tid / 4, c = tid % 4;
-  const int64_t rs = 3LL * g.d;
+  const int64_t rs = g.ldq;  // qkv row stride
   const T* qb = qkv + (int64_t)b * g.T * rs + (int64_t)h * g.hd;
   load_rows<T, HD>(sq, qb, rs, q0, QT, g.T, g.hd, g.scale);
 
@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(NT) local_dq_simt_kernel(Geom g, const T* __re
   float(*sds)[KT + 1] = reinterpret_cast<float(*)[KT + 1]>(sv + KT);
   const int q0 = blockIdx.x * QT, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, i = tid / 4, c = tid % 4;
-  const int64_t rs = 3LL * g.d;
+  const int64_t rs = g.ldq;  // qkv row stride
   const T* qb = qkv + (int64_t)b * g.T * rs + (int64_t)h * g.hd;
   load_rows<T, HD>(sq, qb, rs, q0, QT, g.T, g.hd, g.scale);
   load_rows<T, HD>(sdo, dl + (int64_t)b * g.T * g.d + (int64_t)h * g.hd, g.d, q0, QT, g.T, g.hd, 1.f);
@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(NT) local_dq_simt_kernel(Geom g, const T* __re
     }
   }
   if (t < g.T) {
-    T* dst = dqkv + ((int64_t)b * g.T + t) * rs + (int64_t)h * g.hd;
+    T* dst = dqkv + ((int64_t)b * g.T + t) * g.ldd + (int64_t)h * g.hd;
 #pragma unroll
     for (int u = 0; u < HD / 4; ++u) {
       const int e = c + 4 * u;
@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(NT) local_dkv_simt_kernel(Geom g, const T* __r
   int* slo = reinterpret_cast<int*>(sd + QT);
   const int j0 = blockIdx.x * KT, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, jr = tid / 4, c = tid % 4;
-  const int64_t rs = 3LL * g.d;
+  const int64_t rs = g.ldq;  // qkv row stride
   const T* qb = qkv + (int64_t)b * g.T * rs + (int64_t)h * g.hd;
   const T* db = dl + (int64_t)b * g.T * g.d + (int64_t)h * g.hd;
   const float* lse_b = lse + ((int64_t)b * g.H + h) * g.T;
@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(NT) local_dkv_simt_kernel(Geom g, const T* __r
     }
   }
   if (j < g.T) {
-    T* dst = dqkv + ((int64_t)b * g.T + j) * rs + (int64_t)h * g.hd;
+    T* dst = dqkv + ((int64_t)b * g.T + j) * g.ldd + (int64_t)h * g.hd;
 #pragma unroll
     for (int u = 0; u < HD / 4; ++u) {
       const int e = c + 4 * u;

@@ -168,12 +168,14 @@ CUresult encode_cached(CUtensorMap* map, int rank, const void* base, const cuuin
 }
 
 // [B, T, S, H, hd] bf16 viewed as 4-D (hd, S*H, T, B); box (64, 1, rows, 1).
-bool make_rows_map(CUtensorMap* map, const void* base, int B, int T, int slots_x_heads, int hd, int rows = 128) {
+// row_elems: elements between consecutive token rows (0 = slots_x_heads * hd)
+bool make_rows_map(CUtensorMap* map, const void* base, int B, int T, int slots_x_heads, int hd, int rows = 128,
+                   int64_t row_elems = 0) {
   auto enc = get_encode();
   if (!enc) return false;
+  const cuuint64_t row = (cuuint64_t)(row_elems > 0 ? row_elems : (int64_t)slots_x_heads * hd) * 2;
   cuuint64_t dims[4] = {(cuuint64_t)hd, (cuuint64_t)slots_x_heads, (cuuint64_t)T, (cuuint64_t)B};
-  cuuint64_t strides[3] = {(cuuint64_t)hd * 2, (cuuint64_t)slots_x_heads * hd * 2,
-                           (cuuint64_t)T * slots_x_heads * hd * 2};
+  cuuint64_t strides[3] = {(cuuint64_t)hd * 2, row, (cuuint64_t)T * row};
   cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = encode_cached(map, 4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
@@ -225,7 +227,8 @@ template <int HD>
 cudaError_t fwd_hd(const Geom& g, const void* qkv, void* local_out, float* lse, const GateEpilogue& ep,
                    cudaStream_t s) {
   CUtensorMap tq, tkv;
-  if (!make_rows_map(&tq, qkv, g.B, g.T, 3 * g.H, g.hd, 128) || !make_rows_map(&tkv, qkv, g.B, g.T, 3 * g.H, g.hd, 64))
+  if (!make_rows_map(&tq, qkv, g.B, g.T, 3 * g.H, g.hd, 128, g.ldq) ||
+      !make_rows_map(&tkv, qkv, g.B, g.T, 3 * g.H, g.hd, 64, g.ldq))
     return cudaErrorInvalidValue;
   // two query tiles per CTA (ping-pong), one CTA per SM; the fused epilogue
   // stores local_out and mixed through 3-D maps (d, T, B) that clip at T
@@ -269,8 +272,10 @@ template <int HD>
 cudaError_t dq_hd(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta, void* dqkv,
                   cudaStream_t s) {
   CUtensorMap q128, q64, do128, st;
-  if (!make_rows_map(&q128, qkv, g.B, g.T, 3 * g.H, g.hd, 128) || !make_rows_map(&q64, qkv, g.B, g.T, 3 * g.H, g.hd, 64) ||
-      !make_rows_map(&do128, dl, g.B, g.T, g.H, g.hd, 128) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, g.hd, 128))
+  if (!make_rows_map(&q128, qkv, g.B, g.T, 3 * g.H, g.hd, 128, g.ldq) ||
+      !make_rows_map(&q64, qkv, g.B, g.T, 3 * g.H, g.hd, 64, g.ldq) ||
+      !make_rows_map(&do128, dl, g.B, g.T, g.H, g.hd, 128) ||
+      !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, g.hd, 128, g.ldd))
     return cudaErrorInvalidValue;
   // persistent: one CTA per SM walks the (h, query tile, b) units
   const int smem = DqpLayout<HD>::BYTES;  // the kernel's shared memory is 1024-byte aligned
@@ -286,8 +291,10 @@ template <int HD>
 cudaError_t dkv_hd(const Geom& g, const void* qkv, const void* dl, const float* lse, const float* delta, void* dqkv,
                    cudaStream_t s) {
   CUtensorMap q128, q64, do64, st;
-  if (!make_rows_map(&q128, qkv, g.B, g.T, 3 * g.H, g.hd, 128) || !make_rows_map(&q64, qkv, g.B, g.T, 3 * g.H, g.hd, 64) ||
-      !make_rows_map(&do64, dl, g.B, g.T, g.H, g.hd, 64) || !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, g.hd, 128))
+  if (!make_rows_map(&q128, qkv, g.B, g.T, 3 * g.H, g.hd, 128, g.ldq) ||
+      !make_rows_map(&q64, qkv, g.B, g.T, 3 * g.H, g.hd, 64, g.ldq) ||
+      !make_rows_map(&do64, dl, g.B, g.T, g.H, g.hd, 64) ||
+      !make_rows_map(&st, dqkv, g.B, g.T, 3 * g.H, g.hd, 128, g.ldd))
     return cudaErrorInvalidValue;
   const int smem = DkvLayout<HD>::BYTES;  // the kernel's shared memory is 1024-byte aligned
   cudaError_t e = set_smem_once(local_dkv_tc_kernel<HD>, smem);

@@ -130,46 +130,70 @@ __global__ void __launch_bounds__(256) pool_bwd_kernel(const T* __restrict__ dou
 // the true count, + b_rkv), part 1 = rq (columns [2Ld, 3Ld), query-block
 // means with zero padding counted, or the token's own row when qbs = 1,
 // + b_rq). Thread = one (output row, 16-byte column group) item.
+// Block layout: the part's ng = cols / V column groups (ng <= 256) x slots =
+// 256 / ng thread slots; `split` slots share one output row's tokens (token
+// t0 + k*split + sub for slot sub) and are summed in shared memory in a fixed
+// order, rpb = slots / split output rows per block.
 struct PoolPart {
-  int col0, cols, rows, size, full_divisor;
+  int col0, cols, rows, size, full_divisor, split, rpb, blocks;
 };
 
 template <typename T, int V>
-__global__ void __launch_bounds__(256) pool_proj_fwd_kernel(const T* __restrict__ z, int64_t ldz, int T_, int B,
+__global__ void __launch_bounds__(256) pool_proj_fwd_kernel(const T* __restrict__ z, int ldz, int T_, int B,
                                                             PoolPart p0, PoolPart p1, const T* __restrict__ b0,
                                                             const T* __restrict__ b1, T* __restrict__ out0,
                                                             T* __restrict__ out1) {
+  __shared__ float red[256 * V];
   const PoolPart p = blockIdx.y ? p1 : p0;
+  if ((int)blockIdx.x >= p.blocks) return;
   const T* bias = blockIdx.y ? b1 : b0;
   T* out = blockIdx.y ? out1 : out0;
   const int ng = p.cols / V;
-  const int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (item >= (int64_t)B * p.rows * ng) return;
-  const int cg = (int)(item % ng);
-  const int64_t br = item / ng;  // b * rows + r
-  const int b = (int)(br / p.rows), r = (int)(br % p.rows);
-  const int t0 = r * p.size, t1 = min(t0 + p.size, T_);
-  const T* src = z + ((int64_t)b * T_ + t0) * ldz + p.col0 + cg * V;
+  const int cg = threadIdx.x % ng, slot = threadIdx.x / ng;
+  const int slots = 256 / ng;
+  const int rr = slot / p.split, sub = slot % p.split;
+  const int br = blockIdx.x * p.rpb + rr;  // b * rows + r
+  const bool live = slot < slots && rr < p.rpb && br < B * p.rows;
   float acc[V];
 #pragma unroll
   for (int i = 0; i < V; ++i) acc[i] = 0.f;
-  int t = t0;
-  for (; t + 4 <= t1; t += 4) {  // four rows in flight
-    float v0[V], v1[V], v2[V], v3[V];
-    Vec<T, V>::load(src, v0);
-    Vec<T, V>::load(src + ldz, v1);
-    Vec<T, V>::load(src + 2 * ldz, v2);
-    Vec<T, V>::load(src + 3 * ldz, v3);
+  int t0 = 0, t1 = 0;
+  if (live) {
+    const int b = br / p.rows, r = br % p.rows;
+    t0 = r * p.size;
+    t1 = min(t0 + p.size, T_);
+    const T* src = z + ((size_t)b * T_ + t0 + sub) * ldz + p.col0 + cg * V;
+    const size_t step = (size_t)p.split * ldz;
+    int t = t0 + sub;
+    for (; t + 3 * p.split < t1; t += 4 * p.split) {  // four rows in flight
+      float v0[V], v1[V], v2[V], v3[V];
+      Vec<T, V>::load(src, v0);
+      Vec<T, V>::load(src + step, v1);
+      Vec<T, V>::load(src + 2 * step, v2);
+      Vec<T, V>::load(src + 3 * step, v3);
 #pragma unroll
-    for (int i = 0; i < V; ++i) acc[i] += (v0[i] + v1[i]) + (v2[i] + v3[i]);
-    src += 4 * ldz;
+      for (int i = 0; i < V; ++i) acc[i] += (v0[i] + v1[i]) + (v2[i] + v3[i]);
+      src += 4 * step;
+    }
+    for (; t < t1; t += p.split) {
+      float v0[V];
+      Vec<T, V>::load(src, v0);
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] += v0[i];
+      src += step;
+    }
   }
-  for (; t < t1; ++t) {
-    float v0[V];
-    Vec<T, V>::load(src, v0);
+  if (p.split > 1) {
 #pragma unroll
-    for (int i = 0; i < V; ++i) acc[i] += v0[i];
-    src += ldz;
+    for (int i = 0; i < V; ++i) red[threadIdx.x * V + i] = acc[i];
+    __syncthreads();
+    if (!live || sub != 0) return;
+    for (int k = 1; k < p.split; ++k) {
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] += red[(threadIdx.x + k * ng) * V + i];
+    }
+  } else if (!live) {
+    return;
   }
   const float inv = 1.f / (float)(p.full_divisor ? p.size : (t1 - t0));
   float bv[V];
@@ -181,31 +205,31 @@ __global__ void __launch_bounds__(256) pool_proj_fwd_kernel(const T* __restrict_
   }
 #pragma unroll
   for (int i = 0; i < V; ++i) acc[i] = fmaf(acc[i], inv, bv[i]);
-  Vec<T, V>::store(out + br * p.cols + cg * V, acc);
+  Vec<T, V>::store(out + (size_t)br * p.cols + cg * V, acc);
 }
 
 // The gradient of the above with respect to z: dz[b*T + t, col0 + j] =
-// dout[b, row(t), j] / divisor(row(t)); thread = one (token, column group).
+// dout[b, row(t), j] / divisor(row(t)); thread = one (token, column group),
+// 32-bit indexing (the host checks B*T*ng < 2^31).
 template <typename T, int V>
 __global__ void __launch_bounds__(256) pool_proj_bwd_kernel(const T* __restrict__ d0, const T* __restrict__ d1,
-                                                            T* __restrict__ dz, int64_t ldz, int T_, int B,
+                                                            T* __restrict__ dz, int ldz, int T_, int B,
                                                             PoolPart p0, PoolPart p1) {
   const PoolPart p = blockIdx.y ? p1 : p0;
   const T* dout = blockIdx.y ? d1 : d0;
-  const int ng = p.cols / V;
-  const int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (item >= (int64_t)B * T_ * ng) return;
-  const int cg = (int)(item % ng);
-  const int64_t bt = item / ng;
-  const int b = (int)(bt / T_), t = (int)(bt % T_);
-  const int r = t / p.size;
+  const unsigned ng = (unsigned)(p.cols / V);
+  const unsigned item = blockIdx.x * blockDim.x + threadIdx.x;
+  if (item >= (unsigned)B * (unsigned)T_ * ng) return;
+  const unsigned cg = item % ng, bt = item / ng;
+  const unsigned b = bt / (unsigned)T_, t = bt % (unsigned)T_;
+  const int r = (int)t / p.size;
   const int cnt = p.full_divisor ? p.size : (min((r + 1) * p.size, T_) - r * p.size);
   float v[V];
-  Vec<T, V>::load(dout + ((int64_t)b * p.rows + r) * p.cols + cg * V, v);
+  Vec<T, V>::load(dout + ((size_t)b * p.rows + r) * p.cols + cg * V, v);
   const float inv = 1.f / (float)cnt;
 #pragma unroll
   for (int i = 0; i < V; ++i) v[i] *= inv;
-  Vec<T, V>::store(dz + bt * ldz + p.col0 + cg * V, v);
+  Vec<T, V>::store(dz + (size_t)bt * ldz + p.col0 + cg * V, v);
 }
 
 // Column sums of a row-major [rows, cols] matrix (the bias gradient of a
@@ -214,7 +238,8 @@ __global__ void __launch_bounds__(256) pool_proj_bwd_kernel(const T* __restrict_
 // takes a contiguous row range and writes its fp32 partial row to part[y].
 template <typename T, int V>
 __global__ void __launch_bounds__(256) colsum_part_kernel(const T* __restrict__ g, int64_t rows, int64_t cols,
-                                                          int64_t rows_per_split, float* __restrict__ part) {
+                                                          int64_t ld, int64_t rows_per_split,
+                                                          float* __restrict__ part) {
   __shared__ float red[8][32 * V + 1];
   const int cg = threadIdx.x & 31, rl = threadIdx.x >> 5;
   const int64_t col = ((int64_t)blockIdx.x * 32 + cg) * V;
@@ -228,23 +253,23 @@ __global__ void __launch_bounds__(256) colsum_part_kernel(const T* __restrict__ 
     for (; r + 56 < r1; r += 64) {  // eight rows in flight per thread
       float v[8][V];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) Vec<T, V>::load(g + (r + 8 * k) * cols + col, v[k]);
+      for (int k = 0; k < 8; ++k) Vec<T, V>::load(g + (r + 8 * k) * ld + col, v[k]);
 #pragma unroll
       for (int i = 0; i < V; ++i)
         acc[i] += ((v[0][i] + v[1][i]) + (v[2][i] + v[3][i])) + ((v[4][i] + v[5][i]) + (v[6][i] + v[7][i]));
     }
     for (; r + 24 < r1; r += 32) {
       float v0[V], v1[V], v2[V], v3[V];
-      Vec<T, V>::load(g + r * cols + col, v0);
-      Vec<T, V>::load(g + (r + 8) * cols + col, v1);
-      Vec<T, V>::load(g + (r + 16) * cols + col, v2);
-      Vec<T, V>::load(g + (r + 24) * cols + col, v3);
+      Vec<T, V>::load(g + r * ld + col, v0);
+      Vec<T, V>::load(g + (r + 8) * ld + col, v1);
+      Vec<T, V>::load(g + (r + 16) * ld + col, v2);
+      Vec<T, V>::load(g + (r + 24) * ld + col, v3);
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] += (v0[i] + v1[i]) + (v2[i] + v3[i]);
     }
     for (; r < r1; r += 8) {
       float v0[V];
-      Vec<T, V>::load(g + r * cols + col, v0);
+      Vec<T, V>::load(g + r * ld + col, v0);
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] += v0[i];
     }
@@ -312,43 +337,52 @@ cudaError_t launch_pool_bwd(const Geom& g, int mode, const T* dout, T* dx, int64
 }
 
 namespace {
-void pool_proj_parts(const Geom& g, PoolPart* p0, PoolPart* p1) {
-  *p0 = PoolPart{0, 2 * g.Ld, g.Nc, g.cs, 0};
-  *p1 = PoolPart{2 * g.Ld, g.Ld, g.Tq, g.qbs, 1};
+// column groups of v elements; split / rows per block as described at the kernel
+PoolPart pool_part(int col0, int cols, int rows, int size, int full_divisor, int v, int B) {
+  PoolPart p{col0, cols, rows, size, full_divisor, 1, 1, 0};
+  const int slots = 256 / (cols / v);
+  int split = 1;
+  while (split * 2 <= slots && split * 2 <= size) split *= 2;
+  p.split = split;
+  p.rpb = slots / split;
+  p.blocks = cdiv(B * rows, p.rpb);
+  return p;
 }
 }  // namespace
 
 template <typename T>
 cudaError_t launch_pool_proj_fwd(const Geom& g, const T* z, int64_t ldz, const T* b_rkv, const T* b_rq, T* gkv,
                                  T* rq, cudaStream_t s) {
-  PoolPart p0, p1;
-  pool_proj_parts(g, &p0, &p1);
   constexpr int V = vec_width<T>();
   const bool vec = g.Ld % V == 0 && ldz % V == 0 && aligned16(z) && aligned16(gkv) && aligned16(rq) &&
                    (!b_rkv || aligned16(b_rkv)) && (!b_rq || aligned16(b_rq));
   const int v = vec ? V : 1;
-  const int64_t items = std::max<int64_t>((int64_t)g.B * p0.rows * (p0.cols / v), (int64_t)g.B * p1.rows * (p1.cols / v));
-  dim3 grid((unsigned)((items + 255) / 256), 2);
+  if (2 * g.Ld / v > 256 || ldz > INT32_MAX || (int64_t)g.B * g.T * ldz >= ((int64_t)1 << 40))
+    return cudaErrorInvalidValue;
+  const PoolPart p0 = pool_part(0, 2 * g.Ld, g.Nc, g.cs, 0, v, g.B);
+  const PoolPart p1 = pool_part(2 * g.Ld, g.Ld, g.Tq, g.qbs, 1, v, g.B);
+  dim3 grid((unsigned)std::max(p0.blocks, p1.blocks), 2);
   if (vec)
-    pool_proj_fwd_kernel<T, V><<<grid, 256, 0, s>>>(z, ldz, g.T, g.B, p0, p1, b_rkv, b_rq, gkv, rq);
+    pool_proj_fwd_kernel<T, V><<<grid, 256, 0, s>>>(z, (int)ldz, g.T, g.B, p0, p1, b_rkv, b_rq, gkv, rq);
   else
-    pool_proj_fwd_kernel<T, 1><<<grid, 256, 0, s>>>(z, ldz, g.T, g.B, p0, p1, b_rkv, b_rq, gkv, rq);
+    pool_proj_fwd_kernel<T, 1><<<grid, 256, 0, s>>>(z, (int)ldz, g.T, g.B, p0, p1, b_rkv, b_rq, gkv, rq);
   return cudaGetLastError();
 }
 
 template <typename T>
 cudaError_t launch_pool_proj_bwd(const Geom& g, const T* dgkv, const T* drq, T* dz, int64_t ldz, cudaStream_t s) {
-  PoolPart p0, p1;
-  pool_proj_parts(g, &p0, &p1);
   constexpr int V = vec_width<T>();
   const bool vec = g.Ld % V == 0 && ldz % V == 0 && aligned16(dz) && aligned16(dgkv) && aligned16(drq);
   const int v = vec ? V : 1;
-  const int64_t items = (int64_t)g.B * g.T * (p0.cols / v);  // part 0 is the wider one
+  const int64_t items = (int64_t)g.B * g.T * (2 * g.Ld / v);  // part 0 is the wider one
+  if (items >= ((int64_t)1 << 31) || ldz > INT32_MAX) return cudaErrorInvalidValue;
+  const PoolPart p0{0, 2 * g.Ld, g.Nc, g.cs, 0, 1, 1, 0};
+  const PoolPart p1{2 * g.Ld, g.Ld, g.Tq, g.qbs, 1, 1, 1, 0};
   dim3 grid((unsigned)((items + 255) / 256), 2);
   if (vec)
-    pool_proj_bwd_kernel<T, V><<<grid, 256, 0, s>>>(dgkv, drq, dz, ldz, g.T, g.B, p0, p1);
+    pool_proj_bwd_kernel<T, V><<<grid, 256, 0, s>>>(dgkv, drq, dz, (int)ldz, g.T, g.B, p0, p1);
   else
-    pool_proj_bwd_kernel<T, 1><<<grid, 256, 0, s>>>(dgkv, drq, dz, ldz, g.T, g.B, p0, p1);
+    pool_proj_bwd_kernel<T, 1><<<grid, 256, 0, s>>>(dgkv, drq, dz, (int)ldz, g.T, g.B, p0, p1);
   return cudaGetLastError();
 }
 
@@ -393,9 +427,10 @@ int colsum_occupancy(K kernel) {
 }
 
 template <typename T, typename To>
-cudaError_t launch_colsum(const T* g, int64_t rows, int64_t cols, float* part, To* out, cudaStream_t s) {
+cudaError_t launch_colsum(const T* g, int64_t rows, int64_t cols, float* part, To* out, cudaStream_t s, int64_t ld) {
   constexpr int V = vec_width<T>();
-  const bool vec = cols % V == 0 && aligned16(g);
+  if (ld <= 0) ld = cols;
+  const bool vec = cols % V == 0 && ld % V == 0 && aligned16(g);
   const int gx = vec ? cdiv((int)(cols / V), 32) : cdiv((int)cols, 32);
   // one wave: as many row splits as fit resident beside the column groups
   static const int occ_v = colsum_occupancy(colsum_part_kernel<T, V>);
@@ -404,17 +439,17 @@ cudaError_t launch_colsum(const T* g, int64_t rows, int64_t cols, float* part, T
   const int splits = std::max(1, std::min(colsum_splits(rows, cols, (int)sizeof(T)), sms * occ / gx));
   const int64_t per = (rows + splits - 1) / splits;
   if (vec)
-    colsum_part_kernel<T, V><<<dim3(gx, splits), 256, 0, s>>>(g, rows, cols, per, part);
+    colsum_part_kernel<T, V><<<dim3(gx, splits), 256, 0, s>>>(g, rows, cols, ld, per, part);
   else
-    colsum_part_kernel<T, 1><<<dim3(gx, splits), 256, 0, s>>>(g, rows, cols, per, part);
+    colsum_part_kernel<T, 1><<<dim3(gx, splits), 256, 0, s>>>(g, rows, cols, ld, per, part);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   return launch_reduce_parts<To>(part, splits, cols, out, s);
 }
 
-template cudaError_t launch_colsum<float, float>(const float*, int64_t, int64_t, float*, float*, cudaStream_t);
-template cudaError_t launch_colsum<bf16, bf16>(const bf16*, int64_t, int64_t, float*, bf16*, cudaStream_t);
-template cudaError_t launch_colsum<bf16, float>(const bf16*, int64_t, int64_t, float*, float*, cudaStream_t);
+template cudaError_t launch_colsum<float, float>(const float*, int64_t, int64_t, float*, float*, cudaStream_t, int64_t);
+template cudaError_t launch_colsum<bf16, bf16>(const bf16*, int64_t, int64_t, float*, bf16*, cudaStream_t, int64_t);
+template cudaError_t launch_colsum<bf16, float>(const bf16*, int64_t, int64_t, float*, float*, cudaStream_t, int64_t);
 template cudaError_t launch_pool_fwd<float>(const Geom&, int, const float*, float*, int64_t, cudaStream_t);
 template cudaError_t launch_pool_fwd<bf16>(const Geom&, int, const bf16*, bf16*, int64_t, cudaStream_t);
 template cudaError_t launch_pool_bwd<float>(const Geom&, int, const float*, float*, int64_t, int, cudaStream_t);

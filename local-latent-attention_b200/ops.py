@@ -184,6 +184,28 @@ def pool_proj_bwd(dgkv: Tensor, drq: Tensor, seq_len: int, latent_heads: int, la
     return dz
 
 
+@torch.library.custom_op("llattn_b200::pool_proj_bwd_into_", mutates_args=("buf",), device_types="cuda")
+def pool_proj_bwd_into_(buf: Tensor, dgkv: Tensor, drq: Tensor, col0: int, latent_heads: int, latent_tokens: int,
+                        query_block: int) -> None:
+    """pool_proj_bwd written into columns [col0, col0 + 3Ld) of a row-major
+    [B*T, W] buffer (beside the other per-token gradients held there)."""
+    _require(buf.dim() == 2 and buf.is_contiguous() and buf.dtype == dgkv.dtype, "buf must be a contiguous [B*T, W]")
+    _require(dgkv.is_contiguous() and drq.is_contiguous() and dgkv.dtype == drq.dtype,
+             "pool_proj_bwd expects contiguous gradients of one dtype")
+    B, Ld = dgkv.shape[0], drq.shape[-1]
+    _require(col0 >= 0 and col0 + 3 * Ld <= buf.shape[1] and buf.shape[0] % B == 0, "pool_proj_bwd_into_: bad columns")
+    dims = _pp_dims(B, buf.shape[0] // B, latent_heads, Ld, latent_tokens, query_block, dgkv)
+    with torch.cuda.device(buf.device):
+        _lib.check(_lib.lib().llattn_pool_proj_bwd(ctypes.byref(dims), _ptr(dgkv), _ptr(drq),
+                                                   buf.data_ptr() + col0 * buf.element_size(), buf.stride(0),
+                                                   _stream(buf)), "llattn_pool_proj_bwd")
+
+
+@pool_proj_bwd_into_.register_fake
+def _pool_proj_bwd_into_fake(buf, dgkv, drq, col0, latent_heads, latent_tokens, query_block):
+    return None
+
+
 @pool_proj_bwd.register_fake
 def _pool_proj_bwd_fake(dgkv, drq, seq_len, latent_heads, latent_tokens, query_block):
     return dgkv.new_empty(dgkv.shape[0] * seq_len, 3 * drq.shape[-1])
@@ -193,6 +215,13 @@ def _pool_proj_bwd_fake(dgkv, drq, seq_len, latent_heads, latent_tokens, query_b
 # against the pooled ones' 2 M d Ld plus the x reads of the pooling: they pay
 # for small latent widths only
 POOL_PROJ_MAX_LATENT = 128
+
+
+def _fused_projections(x: Tensor, d: int, Ld: int) -> bool:
+    """Whether BlockFunction runs qkv_proj and the latent projections as one
+    GEMM: small latent widths, and (bf16) 16-byte row strides for the tensor
+    maps of the wide rows."""
+    return Ld <= POOL_PROJ_MAX_LATENT and (x.dtype != torch.bfloat16 or (3 * d + 3 * Ld) % 8 == 0)
 
 
 def pool_chunks(x: Tensor, latent_tokens: int) -> Tensor:
@@ -208,9 +237,20 @@ def pool_query_blocks(x: Tensor, latent_tokens: int, query_block: int) -> Tensor
 # --------------------------------------------------------------------------
 # fused attention core: local + latent + r_out + gate + mix
 
+def _row_stride(t: Tensor) -> int:
+    """Row stride of a [B, T, C] tensor whose rows may sit in a wider
+    row-major buffer (t = buf[..., :C]); 0 when t is contiguous."""
+    if t.is_contiguous():
+        return 0
+    B, T, C = t.shape
+    ok = t.stride(2) == 1 and t.stride(1) >= C and (B == 1 or t.stride(0) == T * t.stride(1))
+    _require(ok, "qkv must be contiguous or a column slice [..., :3d] of a row-major [B, T, W] buffer")
+    return t.stride(1)
+
+
 def _core_dims(qkv: Tensor, w_rout: Tensor, n_heads: int, latent_heads: int, window: int,
                local_block: int, latent_tokens: int, query_block: int, gate_bias: float,
-               seq_offset: int = 0, total_len: int = 0):
+               seq_offset: int = 0, total_len: int = 0, dqkv_row_stride: int = 0):
     B, T, three_d = qkv.shape
     d = three_d // 3
     _require(three_d == 3 * d and d % n_heads == 0, "qkv last dim must be 3 * n_heads * head_dim")
@@ -218,7 +258,7 @@ def _core_dims(qkv: Tensor, w_rout: Tensor, n_heads: int, latent_heads: int, win
     _require(Ld % latent_heads == 0, "latent_d_model must be divisible by latent_heads")
     return _lib.make_dims(B, T, n_heads, d // n_heads, latent_heads, Ld // latent_heads, window,
                           local_block, latent_tokens, query_block, _dtype_code(qkv), gate_bias,
-                          seq_offset, total_len)
+                          seq_offset, total_len, _row_stride(qkv), dqkv_row_stride)
 
 
 def _check_core_inputs(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, dims, geo):
@@ -233,7 +273,7 @@ def _check_core_inputs(qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, dims, ge
     ):
         _require(tuple(t.shape) == shape, f"{name} has shape {tuple(t.shape)}, expected {shape}")
         _require(t.dtype == want, f"{name} has dtype {t.dtype}, expected {want}")
-        _require(t.is_contiguous(), f"{name} must be contiguous")
+        _require(t is qkv or t.is_contiguous(), f"{name} must be contiguous")
         _require(t.device == qkv.device, f"{name} is on {t.device}, expected {qkv.device}")
 
 
@@ -279,14 +319,20 @@ def attn_bwd(dmixed: Tensor, qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tenso
              g_local: Tensor, g_remote: Tensor, local_out: Tensor, lse: Tensor, lat: Tensor,
              lat_lse: Tensor, n_heads: int, latent_heads: int, window: int, local_block: int,
              latent_tokens: int, query_block: int, gate_bias: float, seq_offset: int = 0,
-             total_len: int = 0) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+             total_len: int = 0,
+             dqkv_cols: int = 0) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """The backward of attn_fwd. dqkv_cols > 3d returns dqkv as the first 3d
+    columns of a [B, T, dqkv_cols] buffer (the rest unwritten), for a caller
+    that puts other per-token gradients beside it."""
+    B, T, three_d = qkv.shape
+    wide = dqkv_cols > three_d
     dims = _core_dims(qkv, w_rout, n_heads, latent_heads, window, local_block, latent_tokens,
-                      query_block, gate_bias, seq_offset, total_len)
+                      query_block, gate_bias, seq_offset, total_len, dqkv_cols if wide else 0)
     _require(dmixed.shape == local_out.shape and dmixed.dtype == qkv.dtype and dmixed.is_contiguous(),
              "dmixed must be a contiguous [B, T, d] tensor of the activation dtype")
     d, hd = dims.n_heads * dims.head_dim, dims.head_dim
     kw = dict(device=qkv.device)
-    dqkv = torch.empty_like(qkv)
+    dqkv = torch.empty(B, T, dqkv_cols if wide else three_d, dtype=qkv.dtype, **kw)
     drq = torch.empty_like(rq)
     dgkv = torch.empty_like(gkv)
     dw = torch.empty(w_rout.shape, dtype=torch.float32, **kw)
@@ -307,9 +353,11 @@ def attn_bwd(dmixed: Tensor, qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tenso
 
 @attn_bwd.register_fake
 def _attn_bwd_fake(dmixed, qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, local_out, lse, lat,
-                   lat_lse, *cfg):
+                   lat_lse, n_heads, latent_heads, window, local_block, latent_tokens, query_block, gate_bias,
+                   seq_offset=0, total_len=0, dqkv_cols=0):
     f32 = torch.float32
-    return (torch.empty_like(qkv), torch.empty_like(rq), torch.empty_like(gkv),
+    B, T, three_d = qkv.shape
+    return (qkv.new_empty(B, T, max(dqkv_cols, three_d)), torch.empty_like(rq), torch.empty_like(gkv),
             w_rout.new_empty(w_rout.shape, dtype=f32), b_rout.new_empty(b_rout.shape, dtype=f32),
             g_local.new_empty(g_local.shape, dtype=f32), g_remote.new_empty(g_remote.shape, dtype=f32),
             qkv.new_empty(qkv.shape[-1], dtype=f32))
@@ -420,15 +468,20 @@ class BlockFunction(torch.autograd.Function):
         B, T, d = x.shape
         x = x.contiguous()
         F = torch.nn.functional
-        qkv = F.linear(x, w_qkv, b_qkv)
         Ld = w_rq.shape[0]
-        w_z = None
-        if Ld <= POOL_PROJ_MAX_LATENT:  # one GEMM for both latent projections, then pool their rows
-            w_z = torch.cat([w_rkv, w_rq])
-            z = torch.mm(x.view(B * T, d), w_z.t())
-            gkv, rq = pool_proj_fwd(z, b_rkv, b_rq, B, latent_heads, latent_tokens, query_block)
+        w_cat = None
+        if _fused_projections(x, d, Ld):
+            # one GEMM for qkv_proj and the per-token latent projections:
+            # [qkv | x W_rkv^T | x W_rq^T], whose last 3 Ld columns are pooled
+            w_cat = torch.cat([w_qkv, w_rkv, w_rq])
+            b_cat = torch.cat([b_qkv, b_qkv.new_zeros(3 * Ld)])
+            full = F.linear(x, w_cat, b_cat)
+            qkv = full[..., :3 * d]
+            gkv, rq = pool_proj_fwd(full.view(B * T, -1)[:, 3 * d:], b_rkv, b_rq, B, latent_heads, latent_tokens,
+                                    query_block)
             pooled = qsrc = None
         else:
+            qkv = F.linear(x, w_qkv, b_qkv)
             pooled = pool_fwd(x, latent_tokens, 0, _lib.POOL_CHUNKS)
             gkv = F.linear(pooled, w_rkv, b_rkv)
             qsrc = pool_fwd(x, latent_tokens, query_block, _lib.POOL_QBLOCKS) if query_block > 1 else None
@@ -441,7 +494,7 @@ class BlockFunction(torch.autograd.Function):
             latent_tokens, query_block, float(gate_bias))
         y = F.linear(mixed, w_out, b_out)
         ctx.save_for_backward(x, qkv, pooled, qsrc, rq, gkv, mixed, local_out, lse, lat, lat_lse, w_qkv, w_rq,
-                              w_rkv, w_rout, b_rout_f, gl, gr, w_out, w_z)
+                              w_rkv, w_rout, b_rout_f, gl, gr, w_out, w_cat)
         ctx.cfg = cfg
         ctx.dtypes = (b_rout.dtype, g_local.dtype, g_local.shape, g_remote.dtype, g_remote.shape)
         return y
@@ -449,7 +502,7 @@ class BlockFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         (x, qkv, pooled, qsrc, rq, gkv, mixed, local_out, lse, lat, lat_lse, w_qkv, w_rq, w_rkv, w_rout,
-         b_rout_f, gl, gr, w_out, w_z) = ctx.saved_tensors
+         b_rout_f, gl, gr, w_out, w_cat) = ctx.saved_tensors
         n_heads, latent_heads, window, local_block, latent_tokens, query_block, gate_bias = ctx.cfg
         b_rout_dt, gl_dt, gl_shape, gr_dt, gr_shape = ctx.dtypes
         need = ctx.needs_input_grad
@@ -463,43 +516,48 @@ class BlockFunction(torch.autograd.Function):
             g[11] = torch.mm(dy2.t(), mixed.view(M, d))
         if need[12]:
             g[12] = colsum(dy2)
+        fused = w_cat is not None
         dqkv, drq, dgkv, dw_rout, db_rout, dgl, dgr, db_qkv = attn_bwd(
             dmixed.view(B, T, d), qkv, rq, gkv, w_rout, b_rout_f, gl, gr, local_out, lse, lat, lat_lse,
-            n_heads, latent_heads, window, local_block, latent_tokens, query_block, float(gate_bias))
-        dqkv2 = dqkv.view(M, 3 * d)
+            n_heads, latent_heads, window, local_block, latent_tokens, query_block, float(gate_bias), 0, 0,
+            w_cat.shape[0] if fused else 0)
         drq2 = drq.view(-1, drq.shape[-1])
         dgkv2 = dgkv.view(-1, dgkv.shape[-1])
-        dz = None
-        if w_z is not None and (need[0] or need[3] or need[5]):
-            dz = pool_proj_bwd(dgkv.contiguous(), drq.contiguous(), T, latent_heads, latent_tokens, query_block)
-        if need[0] and dz is not None:  # x's latent gradients: one beta=1 GEMM into the qkv_proj one
-            dx = torch.mm(dqkv2, w_qkv)
-            dx.addmm_(dz, w_z)
-            g[0] = dx.view(B, T, d)
-        elif need[0]:
-            dx = torch.mm(dqkv2, w_qkv)
-            if qsrc is None:
-                dx.addmm_(drq2, w_rq)
-            dx = dx.view(B, T, d)
-            if qsrc is not None:
-                pool_bwd_accumulate_(dx, torch.mm(drq2, w_rq).view(B, -1, d), latent_tokens, query_block,
-                                     _lib.POOL_QBLOCKS)
-            pool_bwd_accumulate_(dx, torch.mm(dgkv2, w_rkv).view(B, -1, d), latent_tokens, 0, _lib.POOL_CHUNKS)
-            g[0] = dx
-        if need[1]:
-            g[1] = torch.mm(dqkv2.t(), x2)
+        if fused:
+            # [dqkv | dz] in one buffer: x's gradient is one GEMM against
+            # [W_qkv; W_rkv; W_rq] and the three weight gradients one GEMM
+            dfull = dqkv.view(M, -1)
+            pool_proj_bwd_into_(dfull, dgkv, drq, 3 * d, latent_heads, latent_tokens, query_block)
+            if need[0]:
+                g[0] = torch.mm(dfull, w_cat).view(B, T, d)
+            if need[1] or need[3] or need[5]:
+                dw_cat = torch.mm(dfull.t(), x2)
+                g[1] = dw_cat[:3 * d] if need[1] else None
+                g[5] = dw_cat[3 * d:3 * d + 2 * Ld] if need[5] else None
+                g[3] = dw_cat[3 * d + 2 * Ld:] if need[3] else None
+        else:
+            dqkv2 = dqkv.view(M, 3 * d)
+            if need[0]:
+                dx = torch.mm(dqkv2, w_qkv)
+                if qsrc is None:
+                    dx.addmm_(drq2, w_rq)
+                dx = dx.view(B, T, d)
+                if qsrc is not None:
+                    pool_bwd_accumulate_(dx, torch.mm(drq2, w_rq).view(B, -1, d), latent_tokens, query_block,
+                                         _lib.POOL_QBLOCKS)
+                pool_bwd_accumulate_(dx, torch.mm(dgkv2, w_rkv).view(B, -1, d), latent_tokens, 0,
+                                     _lib.POOL_CHUNKS)
+                g[0] = dx
+            if need[1]:
+                g[1] = torch.mm(dqkv2.t(), x2)
+            if need[3]:
+                g[3] = torch.mm(drq2.t(), x2 if qsrc is None else qsrc.view(-1, d))
+            if need[5]:
+                g[5] = torch.mm(dgkv2.t(), pooled.view(-1, d))
         if need[2]:  # column sums of dqkv, taken by the library's backward from the tiles it holds
             g[2] = db_qkv.to(dqkv.dtype)
-        if dz is not None and (need[3] or need[5]):
-            dw_z = torch.mm(dz.t(), x2)  # [dW_rkv; dW_rq]
-            g[3] = dw_z[2 * Ld:] if need[3] else None
-            g[5] = dw_z[:2 * Ld] if need[5] else None
-        if need[3] and dz is None:
-            g[3] = torch.mm(drq2.t(), x2 if qsrc is None else qsrc.view(-1, d))
         if need[4]:
             g[4] = colsum(drq2)
-        if need[5] and dz is None:
-            g[5] = torch.mm(dgkv2.t(), pooled.view(-1, d))
         if need[6]:
             g[6] = colsum(dgkv2)
         g[7] = dw_rout.to(w_rout.dtype) if need[7] else None

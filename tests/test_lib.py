@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
     L = _lib.lib()
     for name in declared_symbols():
         assert hasattr(L, name), name
-    assert L.llattn_version() == 2
+    assert L.llattn_version() == 3
 
 
 @pytest.mark.parametrize("T,Nl,QB,W,LBS", [
@@ -50,6 +50,8 @@ def test_geometry_matches_reference_formulas(T, Nl, QB, W, LBS):
     (dict(seq_len=0), "seq_len"), (dict(head_dim=256), "head_dim"), (dict(window=0), "local_window"),
     (dict(latent_tokens=0), "latent_tokens"), (dict(dtype=7), "dtype"),
     (dict(latent_head_dim=128), "latent_head_dim"),
+    (dict(qkv_row_stride=95), "row strides"), (dict(dqkv_row_stride=64), "row strides"),
+    (dict(qkv_row_stride=100, dtype=1), "multiples of 8"), (dict(dqkv_row_stride=97, dtype=1), "multiples of 8"),
 ])
 def test_bad_dims_are_rejected_on_the_host(bad, msg):
     kw = dict(batch=2, seq_len=64, n_heads=2, head_dim=16, latent_heads=2, latent_head_dim=4,
@@ -61,6 +63,16 @@ def test_bad_dims_are_rejected_on_the_host(bad, msg):
     assert rc == 1
     assert msg in _lib.lib().llattn_last_error().decode()
     assert _lib.lib().llattn_bwd_workspace_bytes(ctypes.byref(dims)) == 0
+
+
+def test_wide_row_strides_are_accepted():
+    """qkv / dqkv rows inside a wider buffer (3d = 96 here): any stride >= 3d
+    in fp32, a multiple of 8 in bf16."""
+    L = _lib.lib()
+    g = _lib.Geom()
+    for ld, dt in ((96, _lib.F32), (97, _lib.F32), (104, _lib.BF16), (96 + 192, _lib.BF16)):
+        dims = _lib.make_dims(2, 64, 2, 16, 2, 4, 8, 16, 8, dtype=dt, qkv_row_stride=ld, dqkv_row_stride=ld)
+        assert L.llattn_geometry(ctypes.byref(dims), ctypes.byref(g)) == 0, (ld, dt)
 
 
 def test_entry_points_reject_null_args_without_launching():

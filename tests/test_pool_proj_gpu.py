@@ -108,3 +108,5 @@ def test_pool_proj_rejects_bad_args():
     assert L.llattn_pool_proj_fwd(ctypes.byref(dims), p, 100, None, None, p, p, None) == 1  # ldz < 3 Ld
     assert L.llattn_pool_proj_fwd(ctypes.byref(dims), None, 192, None, None, p, p, None) == 1
     assert L.llattn_pool_proj_bwd(ctypes.byref(dims), p, p, p, 191, None) == 1
+    wide = _lib.make_dims(1, 64, latent_heads=4, latent_head_dim=64, latent_tokens=8, dtype=_lib.F32)
+    assert L.llattn_pool_proj_fwd(ctypes.byref(wide), p, 768, None, None, p, p, None) == 1  # Ld 256 > 128

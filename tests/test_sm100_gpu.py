@@ -164,3 +164,52 @@ def test_recorded_fault_fails_later_launches_until_cleared():
     for a, b in zip(again, ref):
         assert torch.equal(a, b)
     assert _fault() == 0
+
+
+STRIDE_CASES = [
+    # B, T, H, hd, Lh, ldh, force_simt, dtype
+    (2, 300, 2, 128, 2, 32, False, torch.bfloat16),
+    (2, 257, 3, 64, 2, 32, False, torch.bfloat16),
+    (1, 300, 2, 88, 2, 32, False, torch.bfloat16),   # padded head_dim
+    (1, 200, 2, 64, 4, 64, False, torch.bfloat16),   # latent_d_model 256: the general path
+    (2, 150, 2, 32, 2, 16, True, torch.bfloat16),    # SIMT kernels
+    (2, 150, 2, 32, 2, 16, False, torch.float32),
+]
+
+
+@pytest.mark.parametrize("case", STRIDE_CASES)
+def test_wide_qkv_and_dqkv_rows_match_contiguous(case):
+    """qkv read from, and dqkv written into, the first 3d columns of a wider
+    row-major buffer (llattn_dims.qkv_row_stride / dqkv_row_stride): the
+    same bits as with contiguous rows, and the extra columns untouched."""
+    B, T, H, hd, Lh, ldh, simt, dt = case
+    d, Ld, extra = H * hd, Lh * ldh, 24
+    W, LBS, Nl = 64, 128, 16
+    inp = _inputs(B, T, H, hd, Lh, ldh, Nl)
+    dev = {k: v.cuda().to(dt if k in ("qkv", "rq", "gkv", "w") else torch.float32) for k, v in inp.items()}
+    wide = torch.full((B, T, 3 * d + extra), 7.0, dtype=dt, device="cuda")
+    wide[..., :3 * d] = dev["qkv"]
+    qkv_view = wide[..., :3 * d]
+    cfg = (H, Lh, W, LBS, Nl, 0, 0.0)
+    os.environ["LLATTN_FORCE_SIMT"] = "1" if simt else "0"
+    try:
+        ref = torch.ops.llattn_b200.attn_fwd(dev["qkv"], dev["rq"], dev["gkv"], dev["w"], dev["b"], dev["gl"],
+                                             dev["gr"], *cfg)
+        got = torch.ops.llattn_b200.attn_fwd(qkv_view, dev["rq"], dev["gkv"], dev["w"], dev["b"], dev["gl"],
+                                             dev["gr"], *cfg)
+        dm = torch.randn(B, T, d, generator=torch.Generator().manual_seed(3)).to("cuda", dt)
+        saved = lambda q, o: (q, dev["rq"], dev["gkv"], dev["w"], dev["b"], dev["gl"], dev["gr"], o[1], o[2],  # noqa: E731
+                              o[3], o[4])
+        bref = torch.ops.llattn_b200.attn_bwd(dm, *saved(dev["qkv"], ref), *cfg)
+        bgot = torch.ops.llattn_b200.attn_bwd(dm, *saved(qkv_view, got), *cfg, 0, 0, 3 * d + extra)
+        torch.cuda.synchronize()
+    finally:
+        os.environ["LLATTN_FORCE_SIMT"] = "0"
+    assert _fault() == 0
+    for a, b in zip(ref, got):
+        assert torch.equal(a, b)
+    assert bgot[0].shape == (B, T, 3 * d + extra)
+    assert torch.equal(bgot[0][..., :3 * d], bref[0])
+    for a, b in zip(bref[1:], bgot[1:]):
+        assert torch.equal(a, b)
+    assert torch.equal(wide[..., 3 * d:], torch.full_like(wide[..., 3 * d:], 7.0))
