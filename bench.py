@@ -501,8 +501,13 @@ def run_ours(args):
     ms_copy = copy_run(args.steps)
     barrier()
 
-    # sustained: the same step repeated for >= sustain_seconds of device time
-    n_sus = max(args.steps, min(20000, math.ceil(args.sustain_seconds * 1e3 / max(ms, 1e-3))))
+    # sustained: the same step repeated for >= sustain_seconds of device time.
+    # The step count comes from the slowest rank's ms so that every rank runs
+    # the same number of steps (each step holds a gradient all-reduce)
+    ms_all = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_all, op=dist.ReduceOp.MAX)
+    n_sus = max(args.steps, min(20000, math.ceil(args.sustain_seconds * 1e3 / max(ms_all.item(), 1e-3))))
     clocks_sus = ClockSampler(local)
     clocks_sus.start()
     time.sleep(0.3)
