@@ -324,8 +324,12 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    numa_cpus = None
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
+        # each rank's pinned buffers on its GPU's NUMA node (the N ranks'
+        # host copies otherwise meet on one socket's memory and link)
+        numa_cpus = D.bind_to_gpu_numa(local)
 
     B, T, cfg = block_cfg(args.config)
     if args.batch:
@@ -616,7 +620,8 @@ def run_ours(args):
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": 2 * x_h.numel() * 2, "d2h_bytes_per_step": dx_h.numel() * 2,
                 "ms_per_step": round(ms_e2e, 4), "copy_ms_per_step": round(ms_copy, 4),
-                "copy_bound_frac": round(ms_copy / ms_e2e, 4)},
+                "copy_bound_frac": round(ms_copy / ms_e2e, 4),
+                "rank0_cpus": None if numa_cpus is None else f"{len(numa_cpus)} cpus bound to GPU {local}'s NUMA node"},
         "sustained": {"steps": n_sus, "seconds": round(ms_sus * n_sus / 1e3, 3), "ms_per_step": round(ms_sus, 4),
                       "value": round(tokens / (ms_sus / 1e3), 1), "clocks": clk_sus},
         "roofline": roof,

@@ -113,3 +113,39 @@ def unwrap(model: torch.nn.Module) -> torch.nn.Module:
             inner = inner.module
             continue
         return inner
+
+
+def mask_to_cpus(words, bits_per_word: int = 64) -> list[int]:
+    """CPU ids set in an NVML affinity mask (a list of words, CPU 0 = bit 0
+    of word 0)."""
+    return [w * bits_per_word + b for w, word in enumerate(words) for b in range(bits_per_word) if (int(word) >> b) & 1]
+
+
+def bind_to_gpu_numa(device_index: int, nvml=None) -> list[int] | None:
+    """Pin this process to the CPUs that NVML reports as local to the GPU
+    (nvmlDeviceGetCpuAffinity), so that host memory it allocates afterwards
+    (pinned staging buffers) lands on the GPU's NUMA node and its host-device
+    copies do not cross the socket link. Changes only this process's CPU
+    affinity, never a GPU setting. Returns the CPUs bound to, or None (NVML
+    or the affinity call unavailable: nothing changed)."""
+    try:
+        if nvml is None:
+            import pynvml as nvml
+        props = torch.cuda.get_device_properties(device_index)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        nvml.nvmlInit()
+        try:
+            handle = nvml.nvmlDeviceGetHandleByPciBusId(bus)
+            n_cpu = os.cpu_count() or 1
+            words = nvml.nvmlDeviceGetCpuAffinity(handle, (n_cpu + 63) // 64)
+        finally:
+            nvml.nvmlShutdown()
+        cpus = [c for c in mask_to_cpus(words) if c < n_cpu]
+        allowed = os.sched_getaffinity(0)
+        cpus = [c for c in cpus if c in allowed]
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return cpus
+    except Exception:  # noqa: BLE001 - best effort: no NVML, no PCI ids, no permission
+        return None

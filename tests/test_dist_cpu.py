@@ -123,3 +123,47 @@ def test_helpers_outside_torchrun():
     D.barrier()
     dev = D.setup_distributed("gloo")
     assert dev.type in ("cpu", "cuda")
+
+
+def test_numa_mask_decoding_and_fake_nvml_binding(monkeypatch):
+    """bind_to_gpu_numa: decodes NVML's CPU mask, binds the process to those
+    CPUs (restored after the test), and is a no-op when NVML fails."""
+    import os
+    import types
+
+    from llattn_b200 import dist as D
+
+    assert D.mask_to_cpus([0b1011]) == [0, 1, 3]
+    assert D.mask_to_cpus([0, 1]) == [64]
+    allowed = sorted(os.sched_getaffinity(0))
+    props = types.SimpleNamespace(pci_domain_id=0, pci_bus_id=0x1b, pci_device_id=0)
+    monkeypatch.setattr("torch.cuda.get_device_properties", lambda i: props)
+    seen = {}
+
+    class FakeNvml:
+        def nvmlInit(self):
+            pass
+
+        def nvmlShutdown(self):
+            pass
+
+        def nvmlDeviceGetHandleByPciBusId(self, bus):
+            seen["bus"] = bus
+            return "h"
+
+        def nvmlDeviceGetCpuAffinity(self, handle, n):
+            return [1 << allowed[0]] + [0] * (n - 1)
+
+    try:
+        assert D.bind_to_gpu_numa(0, nvml=FakeNvml()) == [allowed[0]]
+        assert seen["bus"] == "00000000:1b:00.0"
+        assert os.sched_getaffinity(0) == {allowed[0]}
+    finally:
+        os.sched_setaffinity(0, allowed)
+
+    class Broken(FakeNvml):
+        def nvmlDeviceGetHandleByPciBusId(self, bus):
+            raise RuntimeError("no such device")
+
+    assert D.bind_to_gpu_numa(0, nvml=Broken()) is None
+    assert sorted(os.sched_getaffinity(0)) == allowed
