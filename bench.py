@@ -324,12 +324,13 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    numa_cpus = None
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
-        # each rank's pinned buffers on its GPU's NUMA node (the N ranks'
-        # host copies otherwise meet on one socket's memory and link)
-        numa_cpus = D.bind_to_gpu_numa(local)
+    # each rank's pinned buffers on its GPU's NUMA node (host copies from the
+    # far socket's memory cross the socket link, and the N ranks' copies
+    # otherwise meet on one socket); the CPU baseline gets the whole host back
+    all_cpus = os.sched_getaffinity(0)
+    numa_cpus = D.bind_to_gpu_numa(local)
 
     B, T, cfg = block_cfg(args.config)
     if args.batch:
@@ -605,7 +606,10 @@ def run_ours(args):
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
+        os.sched_setaffinity(0, all_cpus)
         tok_s, threads, sample, _, kind = cpu_time_block(args.config, args.cpu_seconds)
+        if numa_cpus:
+            os.sched_setaffinity(0, numa_cpus)
         cpu = {"value": round(tok_s, 1), "unit": "tokens/s", "cores": threads, "kind": kind,
                "sample": sample}
 
