@@ -123,3 +123,24 @@ def test_shard_offset_validation():
     ok = _lib.make_dims(1, 128, 1, 64, 1, 32, 16, 256, 8, 64, _lib.BF16, 0.0, 128, 1000)
     assert L.llattn_geometry(ctypes.byref(ok), ctypes.byref(g)) == 0
     assert (g.chunk, g.n_chunks, g.qblock, g.n_qrows) == (125, 8, 64, 2)
+
+
+def test_pool_proj_rejects_bad_args_on_the_host():
+    """llattn_pool_proj_fwd / _bwd validate before launching (no GPU needed):
+    NULL pointers, ldz below 3 * latent_d_model, latent_d_model above 128,
+    sequence shards."""
+    L = _lib.lib()
+    p = ctypes.c_void_p(16)  # never dereferenced: every case fails validation first
+    ok = _lib.make_dims(1, 64, latent_heads=2, latent_head_dim=32, latent_tokens=8, dtype=_lib.BF16)
+    cases = [
+        (ok, None, 192, "NULL"),
+        (ok, p, 100, "ldz"),
+        (_lib.make_dims(1, 64, latent_heads=4, latent_head_dim=64, latent_tokens=8, dtype=_lib.BF16), p, 768, "> 128"),
+        (_lib.make_dims(1, 64, latent_heads=2, latent_head_dim=32, latent_tokens=8, dtype=_lib.BF16,
+                        seq_offset=0, total_len=128), p, 192, "whole sequences"),
+    ]
+    for dims, z, ldz, msg in cases:
+        assert L.llattn_pool_proj_fwd(ctypes.byref(dims), z, ldz, None, None, p, p, None) == 1
+        assert msg in L.llattn_last_error().decode(), (msg, L.llattn_last_error())
+        assert L.llattn_pool_proj_bwd(ctypes.byref(dims), z, p, p, ldz, None) == 1
+        assert msg in L.llattn_last_error().decode(), (msg, L.llattn_last_error())
