@@ -319,11 +319,12 @@ def attn_bwd(dmixed: Tensor, qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tenso
              g_local: Tensor, g_remote: Tensor, local_out: Tensor, lse: Tensor, lat: Tensor,
              lat_lse: Tensor, n_heads: int, latent_heads: int, window: int, local_block: int,
              latent_tokens: int, query_block: int, gate_bias: float, seq_offset: int = 0,
-             total_len: int = 0,
-             dqkv_cols: int = 0) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+             total_len: int = 0, dqkv_cols: int = 0,
+             want_db_qkv: bool = True) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
     """The backward of attn_fwd. dqkv_cols > 3d returns dqkv as the first 3d
     columns of a [B, T, dqkv_cols] buffer (the rest unwritten), for a caller
-    that puts other per-token gradients beside it."""
+    that puts other per-token gradients beside it; want_db_qkv=False skips
+    the qkv bias gradient (the last output is then left unwritten)."""
     B, T, three_d = qkv.shape
     wide = dqkv_cols > three_d
     dims = _core_dims(qkv, w_rout, n_heads, latent_heads, window, local_block, latent_tokens,
@@ -345,7 +346,7 @@ def attn_bwd(dmixed: Tensor, qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tenso
     args = _lib.BwdArgs(dims, _ptr(qkv), _ptr(rq), _ptr(gkv), _ptr(w_rout), _ptr(b_rout),
                         _ptr(g_local), _ptr(g_remote), _ptr(local_out), _ptr(lse), _ptr(lat),
                         _ptr(lat_lse), _ptr(dmixed), _ptr(dqkv), _ptr(drq), _ptr(dgkv), _ptr(dw),
-                        _ptr(db), _ptr(dgl), _ptr(dgr), _ptr(ws), ws.numel(), _ptr(dbqkv))
+                        _ptr(db), _ptr(dgl), _ptr(dgr), _ptr(ws), ws.numel(), _ptr(dbqkv) if want_db_qkv else 0)
     with torch.cuda.device(qkv.device):
         _lib.check(_lib.lib().llattn_bwd(ctypes.byref(args), _stream(qkv)), "llattn_bwd")
     return dqkv, drq, dgkv, dw, db, dgl, dgr, dbqkv
@@ -354,7 +355,7 @@ def attn_bwd(dmixed: Tensor, qkv: Tensor, rq: Tensor, gkv: Tensor, w_rout: Tenso
 @attn_bwd.register_fake
 def _attn_bwd_fake(dmixed, qkv, rq, gkv, w_rout, b_rout, g_local, g_remote, local_out, lse, lat,
                    lat_lse, n_heads, latent_heads, window, local_block, latent_tokens, query_block, gate_bias,
-                   seq_offset=0, total_len=0, dqkv_cols=0):
+                   seq_offset=0, total_len=0, dqkv_cols=0, want_db_qkv=True):
     f32 = torch.float32
     B, T, three_d = qkv.shape
     return (qkv.new_empty(B, T, max(dqkv_cols, three_d)), torch.empty_like(rq), torch.empty_like(gkv),
@@ -376,7 +377,9 @@ def _attn_backward(ctx, dmixed, _d_local, _d_lse, _d_lat, _d_lat_lse):
     qkv = saved[0]
     if dmixed is None:
         dmixed = torch.zeros_like(saved[7])
-    dqkv, drq, dgkv, dw, db, dgl, dgr, _ = attn_bwd(dmixed.to(qkv.dtype).contiguous(), *saved, *ctx.cfg)
+    # (the qkv bias gradient belongs to the caller's qkv projection: not asked for)
+    dqkv, drq, dgkv, dw, db, dgl, dgr, _ = attn_bwd(dmixed.to(qkv.dtype).contiguous(), *saved, *ctx.cfg,
+                                                    want_db_qkv=False)
     return (dqkv, drq, dgkv, dw.to(saved[3].dtype), db, dgl, dgr) + (None,) * 9
 
 
@@ -520,7 +523,7 @@ class BlockFunction(torch.autograd.Function):
         dqkv, drq, dgkv, dw_rout, db_rout, dgl, dgr, db_qkv = attn_bwd(
             dmixed.view(B, T, d), qkv, rq, gkv, w_rout, b_rout_f, gl, gr, local_out, lse, lat, lat_lse,
             n_heads, latent_heads, window, local_block, latent_tokens, query_block, float(gate_bias), 0, 0,
-            w_cat.shape[0] if fused else 0)
+            w_cat.shape[0] if fused else 0, not fused)
         drq2 = drq.view(-1, drq.shape[-1])
         dgkv2 = dgkv.view(-1, dgkv.shape[-1])
         if fused:
@@ -530,6 +533,17 @@ class BlockFunction(torch.autograd.Function):
             pool_proj_bwd_into_(dfull, dgkv, drq, 3 * d, latent_heads, latent_tokens, query_block)
             if need[0]:
                 g[0] = torch.mm(dfull, w_cat).view(B, T, d)
+            if need[2] or need[4] or need[6]:
+                # the bias gradients as one column sum over the buffer (for
+                # rkv: sum_t dgkv[c(t)] / cnt(c), the chunk gradients summed).
+                # Block-pooled queries count zero padding, so a ragged last
+                # block's bias gradient is its whole drq row, not the
+                # n_valid / bs share its tokens carry in dz: rq's own sum then
+                db_cat = colsum(dfull)
+                g[2] = db_cat[:3 * d] if need[2] else None
+                g[6] = db_cat[3 * d:3 * d + 2 * Ld] if need[6] else None
+                if need[4]:
+                    g[4] = db_cat[3 * d + 2 * Ld:] if query_block <= 1 else colsum(drq2)
             if need[1] or need[3] or need[5]:
                 dw_cat = torch.mm(dfull.t(), x2)
                 g[1] = dw_cat[:3 * d] if need[1] else None
@@ -554,12 +568,12 @@ class BlockFunction(torch.autograd.Function):
                 g[3] = torch.mm(drq2.t(), x2 if qsrc is None else qsrc.view(-1, d))
             if need[5]:
                 g[5] = torch.mm(dgkv2.t(), pooled.view(-1, d))
-        if need[2]:  # column sums of dqkv, taken by the library's backward from the tiles it holds
-            g[2] = db_qkv.to(dqkv.dtype)
-        if need[4]:
-            g[4] = colsum(drq2)
-        if need[6]:
-            g[6] = colsum(dgkv2)
+            if need[2]:  # column sums of dqkv, taken by the library's backward
+                g[2] = db_qkv.to(dqkv.dtype)
+            if need[4]:
+                g[4] = colsum(drq2)
+            if need[6]:
+                g[6] = colsum(dgkv2)
         g[7] = dw_rout.to(w_rout.dtype) if need[7] else None
         g[8] = db_rout.to(b_rout_dt) if need[8] else None
         g[9] = dgl.to(gl_dt).view(gl_shape) if need[9] else None
