@@ -260,7 +260,7 @@ int run_fwd(const Geom& g, const llattn_fwd_args* a, cudaStream_t s) {
   if (!fused && !general && (rc = simt_gate_check(g))) return rc;
   {
     prof::Scope ps(prof::LATENT_FWD, s);
-    if (sizeof(T) == 2 && sm100::latent_tc_ok(g))  // tensor cores: bf16, head dim <= 64, <= 64 chunks
+    if (sizeof(T) == 2 && sm100::latent_tc_fwd_ok(g))  // tensor cores: bf16, head dim <= 64, <= 512 chunks
       rc = check_launch(sm100::launch_latent_fwd_tc(g, a->rq, a->gkv, a->lat, a->lat_lse, s), "latent_fwd_sm100");
     else
       rc = check_launch(launch_latent_fwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv),

@@ -503,3 +503,241 @@ __global__ void __launch_bounds__(160)
     tmem_dealloc(tmem, 128);
   }
 }
+
+// Forward of the latent branch on the tensor cores for 64 < Nc <= 512 chunks
+// (bf16, latent head dim <= 64 as above). All of (b, head)'s chunk keys and
+// values sit in shared memory (128-byte rows, 64 KB each at 512 chunks). Per
+// 128-row tile with nkt = ceil(qid(last row) / 64) key tiles, two passes over
+// the key tiles, each tile S = rq gk^T (M128 x N64, bf16, fp32 accumulation)
+// in one of two TMEM buffers so that the next tile's MMA overlaps this
+// tile's softmax:
+//   pass 1: the row max of the masked S sc (chunks j < qid(r));
+//   pass 2: P = 2^(S sc - max) (masked, fp32; l sums it), P as bf16 over the
+//           S columns, O += P gv_tile (A from TMEM) accumulated in TMEM.
+// lat = O / l, lat_lse = max + ln l; rows that see no chunk write 0 and
+// INFINITY (models.py:366-373). Recomputing S costs one small MMA per tile
+// and keeps P exactly the fp32 value the normaliser sums, as in the 64-chunk
+// kernel.
+struct LatFwdLongLayout {
+  static constexpr int AQ = 0;  // rq bf16 [128 rows][<= 64] in 128-byte rows
+  static constexpr int GK = 16384;
+  __host__ __device__ static constexpr int nc_pad(int nc) { return (nc + 63) / 64 * 64; }
+  __host__ __device__ static constexpr int gv(int nc) { return GK + nc_pad(nc) * 128; }
+  __host__ __device__ static constexpr int bar(int nc) { return GK + 2 * nc_pad(nc) * 128; }
+  __host__ __device__ static constexpr int bytes(int nc) { return bar(nc) + 128; }
+};
+enum { LL_A = 0, LL_S = 1, LL_F = 3, LL_O = 5, LL_NB = 6 };
+
+template <int LDH>
+__global__ void __launch_bounds__(160, 1)
+    latent_fwd_tc_long_kernel(Geom g, const bf16* __restrict__ rq, const bf16* __restrict__ gkv,
+                              bf16* __restrict__ lat, float* __restrict__ lat_lse, int n_split) {
+  using L = LatFwdLongLayout;
+  constexpr int NQ = LDH / 8;
+  extern __shared__ __align__(1024) uint8_t smem_latl_tc[];
+  uint8_t* smem = smem_latl_tc;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::bar(g.Nc));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + LL_NB);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  if (smem_u32(smem) & 1023u) {
+    if (threadIdx.x == 0) raise_fault(g, kFaultEpilogue, nullptr);
+    return;
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, tid = threadIdx.x;
+  const int split = blockIdx.x, lh = blockIdx.y, b = blockIdx.z;
+  const int n_rb = cdiv(g.Tq, BM);
+  const int n_tiles = split < n_rb ? (n_rb - 1 - split) / n_split + 1 : 0;
+  const int ldh = g.ldh;
+  const int nc_pad = L::nc_pad(g.Nc);
+  uint8_t* sgk = smem + L::GK;
+  uint8_t* sgv = smem + L::gv(g.Nc);
+  // key tiles a row tile needs: the chunks its last row sees
+  auto tile_nkt = [&](int n) {
+    const int rlast = min((split + n * n_split) * BM + BM - 1, g.Tq - 1);
+    return cdiv(row_qid(g, rlast), 64);
+  };
+
+  if (tid == 0) {
+    mbar_init(&bars[LL_A], BM);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[LL_S + s], 1);
+      mbar_init(&bars[LL_F + s], BM);
+    }
+    mbar_init(&bars[LL_O], 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  // chunk keys / values of (b, lh), 16-byte chunk (key, c); zero past Nc / ldh
+  for (int idx = tid; idx < nc_pad * 8; idx += blockDim.x) {
+    const int key = idx >> 3, c = idx & 7;
+    const bool on = key < g.Nc && 8 * c < ldh;
+    const int64_t base = ((int64_t)(b * g.Nc + (on ? key : 0)) * 2 * g.Lh + lh) * ldh;
+    *lat_chunk(sgk, key, c) = on ? reinterpret_cast<const uint4*>(gkv + base)[c] : make_uint4(0, 0, 0, 0);
+    *lat_chunk(sgv, key, c) =
+        on ? reinterpret_cast<const uint4*>(gkv + base + (int64_t)g.Lh * ldh)[c] : make_uint4(0, 0, 0, 0);
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tO = tmem + 128;  // S buffers at [0,64) and [64,128) (P bf16 over the first 32 of each)
+
+  if (warp == 4) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(BM, 64, false, false);  // rq gk^T
+      constexpr uint32_t idO = idesc_bf16_f32(BM, 64, false, true);   // P gv
+      const uint64_t daq = desc_sw128(smem_u32(smem + L::AQ), 16, 1024);
+      const uint64_t dk = desc_sw128(smem_u32(sgk), 16, 1024);
+      const uint64_t dv = desc_sw128(smem_u32(sgv), 8192, 1024);
+      bool ok = true;
+      int it = 0, no = 0;  // items (S tiles) issued so far, tiles with an O
+      // S of item q (key tile kt) into buffer q&1, once item q-2 has left it
+      auto issue_s = [&](int q, int kt) -> bool {
+        if (q >= 2 && !mbar_wait(&bars[LL_F + (q & 1)], ((q - 2) >> 1) & 1, abort, &g_fault_word)) return false;
+        tc_fence_after();
+        const uint32_t tS = tmem + (q & 1) * 64;
+#pragma unroll
+        for (int kk = 0; kk < LDH / 16; ++kk)
+          mma_bf16(tS, desc_add(daq, kk * 32), desc_add(dk, kt * 8192 + kk * 32), idS, kk > 0);
+        mma_commit(&bars[LL_S + (q & 1)]);
+        return true;
+      };
+      for (int n = 0; ok && n < n_tiles; ++n) {
+        // the rows are staged (and the previous tile's O has been read)
+        if (!(ok = mbar_wait(&bars[LL_A], n & 1, abort, &g_fault_word))) break;
+        const int nkt = tile_nkt(n), N = 2 * nkt;
+        if (N == 0) continue;
+        if (!(ok = issue_s(it, 0))) break;
+        for (int i = 0; ok && i < N; ++i) {
+          const int q = it + i;
+          if (i + 1 < N && !(ok = issue_s(q + 1, (i + 1) % nkt))) break;
+          if (i >= nkt) {  // pass 2: P of item q written -> O += P gv
+            if (!(ok = mbar_wait(&bars[LL_F + (q & 1)], (q >> 1) & 1, abort, &g_fault_word))) break;
+            tc_fence_after();
+            const int kt = i - nkt;
+            const uint32_t tP = tmem + (q & 1) * 64;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16_ts(tO, tP + kk * 8, desc_add(dv, kt * 8192 + kk * 2048), idO, (i > nkt || kk > 0) ? 1u : 0u);
+          }
+        }
+        if (!ok) break;
+        mma_commit(&bars[LL_O]);
+        it += N;
+        ++no;
+      }
+      if (!ok) raise_fault(g, kFaultMma, abort);
+    }
+  } else {
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    const float sc2 = g.lat_scale * kLog2e;
+    uint4 pre_q[NQ];
+    auto fetch = [&](int n) {
+      const int r = (split + n * n_split) * BM + tid;
+      const bool on = n < n_tiles && r < g.Tq;
+      const uint4* qp = reinterpret_cast<const uint4*>(rq + ((int64_t)(b * g.Tq + (on ? r : 0)) * g.Lh + lh) * ldh);
+#pragma unroll
+      for (int i = 0; i < NQ; ++i) pre_q[i] = (on && 8 * i < ldh) ? __ldg(qp + i) : make_uint4(0, 0, 0, 0);
+    };
+    fetch(0);
+    bool ok = true;
+    int it = 0, no = 0;
+    for (int n = 0; n < n_tiles; ++n) {
+      const int r = (split + n * n_split) * BM + tid;
+      const bool valid = r < g.Tq;
+      const int qid = valid ? row_qid(g, r) : 0;
+#pragma unroll
+      for (int i = 0; i < NQ; ++i) *lat_chunk(smem + L::AQ, tid, i) = pre_q[i];
+      fence_async_smem();
+      mbar_arrive(&bars[LL_A]);
+      fetch(n + 1);
+      const int nkt = tile_nkt(n), N = 2 * nkt;
+      float m = -INFINITY, mb = 0.f, l = 0.f;
+      for (int i = 0; i < N; ++i) {
+        const int q = it + i, kt = i < nkt ? i : i - nkt;
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[LL_S + (q & 1)], (q >> 1) & 1, abort, &g_fault_word));
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t tS = tmem + lane_off + (q & 1) * 64;
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tS, r0);
+        tmem_ld32(tS + 32, r1);
+        tmem_ld_wait();
+        const int c_hi = qid - kt * 64;  // columns c < c_hi are visible
+        if (i < nkt) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            if (c < c_hi) m = fmaxf(m, __uint_as_float(r0[c]) * sc2);
+            if (32 + c < c_hi) m = fmaxf(m, __uint_as_float(r1[c]) * sc2);
+          }
+        } else {
+          if (i == nkt) mb = qid > 0 ? m : 0.f;
+          uint32_t lo[16], hi[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float p0 = 2 * c < c_hi ? fast_exp2(__uint_as_float(r0[2 * c]) * sc2 - mb) : 0.f;
+            const float p1 = 2 * c + 1 < c_hi ? fast_exp2(__uint_as_float(r0[2 * c + 1]) * sc2 - mb) : 0.f;
+            const float p2 = 32 + 2 * c < c_hi ? fast_exp2(__uint_as_float(r1[2 * c]) * sc2 - mb) : 0.f;
+            const float p3 = 33 + 2 * c < c_hi ? fast_exp2(__uint_as_float(r1[2 * c + 1]) * sc2 - mb) : 0.f;
+            l += (p0 + p1) + (p2 + p3);
+            lo[c] = pack_bf16(p0, p1);
+            hi[c] = pack_bf16(p2, p3);
+          }
+          tmem_st16(tS, lo);
+          tmem_st16(tS + 16, hi);
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        mbar_arrive(&bars[LL_F + (q & 1)]);
+      }
+      if (!ok) break;
+      it += N;
+      const float inv = qid > 0 ? 1.f / l : 0.f;
+      if (N > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars[LL_O], no & 1, abort, &g_fault_word));
+        if (!ok) break;
+        ++no;
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int hh = 0; hh < LDH / 32; ++hh) {
+        uint32_t o[32];
+        if (N > 0) {
+          tmem_ld32(tO + lane_off + hh * 32, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] = 0u;
+        }
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(lat + (int64_t)(b * g.Tq + r) * g.Ld + lh * ldh + hh * 32);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if (hh * 32 + 8 * c < ldh)
+              dst[c] = make_uint4(pack_bf16(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
+                                  pack_bf16(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
+                                  pack_bf16(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
+                                  pack_bf16(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
+        }
+      }
+      // O has been read: the next tile's first P gv may overwrite it (the
+      // MMA thread waits for LL_A, which these threads arrive on next)
+      tc_fence_before();
+      if (valid) lat_lse[(int64_t)(b * g.Lh + lh) * g.Tq + r] = qid > 0 ? (mb + log2f(l)) * kLn2 : INFINITY;
+    }
+    if (!ok) raise_fault(g, kFaultSoftmax, abort);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}

@@ -432,10 +432,28 @@ cudaError_t launch_latent_bwd_tc(const Geom& g, const void* rq, const void* gkv,
   return run(latent_bwd_tc_kernel<64>, LatTcLayout<64>::BYTES);
 }
 
+// forward: up to 512 chunks (more than 64: the two-pass kernel over 64-key tiles)
+bool latent_tc_fwd_ok(const Geom& g) {
+  return !force_simt() && g.ldh <= 64 && g.ldh % 8 == 0 && g.Nc <= 512 && g.Tq >= 1;
+}
+
 cudaError_t launch_latent_fwd_tc(const Geom& g, const void* rq, const void* gkv, void* lat, float* lat_lse,
                                  cudaStream_t s) {
-  if (!latent_tc_ok(g)) return cudaErrorNotSupported;
+  if (!latent_tc_fwd_ok(g)) return cudaErrorNotSupported;
   if (((uintptr_t)rq & 15) || ((uintptr_t)gkv & 15) || ((uintptr_t)lat & 15)) return cudaErrorMisalignedAddress;
+  if (g.Nc > 64) {
+    auto kern = g.ldh <= 32 ? latent_fwd_tc_long_kernel<32> : latent_fwd_tc_long_kernel<64>;
+    // the attribute covers the largest key set; a launch asks for at least
+    // 80 KB so that no more than two CTAs (256 TMEM columns each) share an SM
+    cudaError_t e = set_smem_once(kern, LatFwdLongLayout::bytes(512));
+    if (e != cudaSuccess) return e;
+    const int smem = std::max(LatFwdLongLayout::bytes(g.Nc), 80 * 1024);
+    const int n_split = std::max(1, std::min(cdiv(g.Tq, BM), (2 * sm_count()) / (g.B * g.Lh)));
+    dim3 grid(n_split, g.Lh, g.B);
+    kern<<<grid, 160, smem, s>>>(g, static_cast<const bf16*>(rq), static_cast<const bf16*>(gkv),
+                                 static_cast<bf16*>(lat), lat_lse, n_split);
+    return cudaGetLastError();
+  }
   const int smem = LatFwdTcLayout::BYTES;  // the kernel's shared memory is 1024-byte aligned
   auto kern = g.ldh <= 32 ? latent_fwd_tc_kernel<32> : latent_fwd_tc_kernel<64>;
   cudaError_t e = set_smem_once(kern, smem);

@@ -49,7 +49,9 @@ bool latent_tc_ok(const Geom& g);
 int latent_tc_splits(const Geom& g);
 cudaError_t launch_latent_bwd_tc(const Geom& g, const void* rq, const void* gkv, const float* lat_lse,
                                  const float* dlat, void* drq, float* part, int n_split, cudaStream_t s);
-// Latent forward on tensor cores (same conditions): lat [B,Tq,Ld], lat_lse [B,Lh,Tq]
+// Latent forward on tensor cores (bf16, latent head dim <= 64, up to 512
+// chunks): lat [B,Tq,Ld], lat_lse [B,Lh,Tq]
+bool latent_tc_fwd_ok(const Geom& g);
 cudaError_t launch_latent_fwd_tc(const Geom& g, const void* rq, const void* gkv, void* lat, float* lat_lse,
                                  cudaStream_t s);
 int gate_bwd_ctas(const Geom& g);
