@@ -87,8 +87,9 @@ int make_geom(const llattn_dims* d, Geom* g) {
 
 // Backward workspace, every region 256-byte aligned.
 struct BwdLayout {
-  size_t dl, delta, drow, drow_half, dlat, dlat_tok, dg_part, dg_sum, dw_part, dgkv_part, drq_part, dbqkv, total;
-  int gate_tok, n_gate_cta, n_split_w, n_split_lat, n_kg_lat;
+  size_t dl, delta, drow, drow_half, dlat, dlat_tok, dg_part, dg_sum, dw_part, dgkv_part, drq_part, lat_delta, dbqkv,
+      total;
+  int gate_tok, n_gate_cta, n_split_w, n_split_lat, n_kg_lat, n_split_keys;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -108,6 +109,9 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
     const int base = g.B * g.Lh * L.n_split_lat, n_kt = cdiv(g.Nc, 64);
     L.n_kg_lat = (n_kt > 1 && base < 148) ? std::max(1, std::min(n_kt, (2 * 148) / base)) : 1;
   }
+  // row splits of the tensor-core latent keys kernel (64 < Nc <= 512): one
+  // CTA per SM, about two waves of (128-key tile, split, latent head, b)
+  L.n_split_keys = std::max(1, std::min(cdiv(g.Tq, 64), (2 * 148) / (g.B * g.Lh * cdiv(g.Nc, 128))));
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off += align256(bytes); return o; };
   const size_t BTd = (size_t)g.B * g.T * g.d;
@@ -125,8 +129,11 @@ BwdLayout bwd_layout(const Geom& g, int elt) {
   L.dg_part = take(sizeof(float) * std::max(std::max((size_t)L.n_gate_cta * 2 * g.hd, dg_tc), dg_rm));
   L.dg_sum = take(sizeof(float) * (size_t)std::max(2 * g.hd, g.hd + 65 * g.H));
   L.dw_part = take(sizeof(float) * (size_t)L.n_split_w * g.d * (g.Ld + 1));
-  L.dgkv_part = take(sizeof(float) * (size_t)L.n_split_lat * L.n_kg_lat * g.B * g.Nc * 2 * g.Ld);
+  const bool long_lat = g.Nc > 64;
+  L.dgkv_part = take(sizeof(float) * (size_t)std::max(L.n_split_lat * L.n_kg_lat, long_lat ? L.n_split_keys : 0) *
+                     g.B * g.Nc * 2 * g.Ld);
   L.drq_part = take(L.n_kg_lat > 1 ? sizeof(float) * (size_t)L.n_kg_lat * g.B * g.Tq * g.Ld : 0);
+  L.lat_delta = take(long_lat ? sizeof(float) * (size_t)g.B * g.Lh * g.Tq : 0);
   // qkv_proj bias gradient: the column-sum kernel's split partials
   L.dbqkv = take(sizeof(float) * 3 * (size_t)g.d * colsum_splits((int64_t)g.B * g.T, 3 * g.d, elt));
   L.total = off;
@@ -456,14 +463,22 @@ int run_bwd(const Geom& g, const llattn_bwd_args* a, cudaStream_t s) {
   // tensor-core latent backward for bf16 with head dim <= 64 and <= 64 chunks;
   // its row splits are 128-row tiles, at most the SIMT kernel's 64-row count
   const bool lat_tc = sizeof(T) == 2 && sm100::latent_tc_ok(g);
-  const int n_split_lat = lat_tc ? std::min(sm100::latent_tc_splits(g), L.n_split_lat) : L.n_split_lat;
-  const int n_kg_lat = lat_tc || g.Nc <= 64 ? 1 : L.n_kg_lat;
+  // past 64 chunks: the tensor-core rows / keys kernels (up to 512 chunks)
+  const bool lat_tc_long = sizeof(T) == 2 && !lat_tc && sm100::latent_tc_long_ok(g);
+  const int n_split_lat = lat_tc ? std::min(sm100::latent_tc_splits(g), L.n_split_lat)
+                                 : lat_tc_long ? L.n_split_keys : L.n_split_lat;
+  const int n_kg_lat = lat_tc || lat_tc_long || g.Nc <= 64 ? 1 : L.n_kg_lat;
   {
-  prof::Scope ps(prof::LATENT_BWD, s, n_kg_lat > 1 ? 3 : 2);
+  prof::Scope ps(prof::LATENT_BWD, s, n_kg_lat > 1 || lat_tc_long ? 3 : 2);
   if (lat_tc)
     rc = check_launch(sm100::launch_latent_bwd_tc(g, a->rq, a->gkv, a->lat_lse, dlat, a->drq, dgkv_part,
                                                   n_split_lat, s),
                       "latent_bwd_sm100");
+  else if (lat_tc_long)
+    rc = check_launch(sm100::launch_latent_bwd_tc_long(g, a->rq, a->gkv, a->lat_lse, dlat, a->drq,
+                                                       reinterpret_cast<float*>(ws + L.lat_delta), dgkv_part,
+                                                       n_split_lat, s),
+                      "latent_bwd_sm100_long");
   else
     rc = check_launch(launch_latent_bwd<T>(g, static_cast<const T*>(a->rq), static_cast<const T*>(a->gkv),
                                            a->lat_lse, dlat, static_cast<T*>(a->drq), dgkv_part, n_split_lat,

@@ -432,6 +432,41 @@ cudaError_t launch_latent_bwd_tc(const Geom& g, const void* rq, const void* gkv,
   return run(latent_bwd_tc_kernel<64>, LatTcLayout<64>::BYTES);
 }
 
+// backward past one key tile: 64 < Nc <= 512 (the rows / keys kernel pair)
+bool latent_tc_long_ok(const Geom& g) {
+  return !force_simt() && g.ldh <= 64 && g.ldh % 8 == 0 && g.Nc > 64 && g.Nc <= 512 && g.Tq >= 1;
+}
+
+cudaError_t launch_latent_bwd_tc_long(const Geom& g, const void* rq, const void* gkv, const float* lat_lse,
+                                      const float* dlat, void* drq, float* delta, float* part, int n_split_keys,
+                                      cudaStream_t s) {
+  if (!latent_tc_long_ok(g)) return cudaErrorNotSupported;
+  if (((uintptr_t)rq & 15) || ((uintptr_t)gkv & 15) || ((uintptr_t)dlat & 15) || ((uintptr_t)drq & 15))
+    return cudaErrorMisalignedAddress;
+  const bf16* rq_ = static_cast<const bf16*>(rq);
+  const bf16* gkv_ = static_cast<const bf16*>(gkv);
+  // rows: 512 TMEM columns a CTA, so at least 116 KB of shared memory (one CTA per SM)
+  {
+    auto kern = g.ldh <= 32 ? latent_bwd_rows_tc_kernel<32> : latent_bwd_rows_tc_kernel<64>;
+    const int cap = std::max(LatBwdRowsLayout::bytes(512), 116 * 1024);
+    cudaError_t e = set_smem_once(kern, cap);
+    if (e != cudaSuccess) return e;
+    const int smem = std::max(LatBwdRowsLayout::bytes(g.Nc), 116 * 1024);
+    const int n_split = std::max(1, std::min(cdiv(g.Tq, BM), (2 * sm_count()) / (g.B * g.Lh)));
+    dim3 grid(n_split, g.Lh, g.B);
+    kern<<<grid, 160, smem, s>>>(g, rq_, gkv_, lat_lse, dlat, static_cast<bf16*>(drq), delta, n_split);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  {
+    auto kern = g.ldh <= 32 ? latent_bwd_keys_tc_kernel<32> : latent_bwd_keys_tc_kernel<64>;
+    cudaError_t e = set_smem_once(kern, LatBwdKeysLayout::LAUNCH);
+    if (e != cudaSuccess) return e;
+    dim3 grid(cdiv(g.Nc, BM) * n_split_keys, g.Lh, g.B);
+    kern<<<grid, 160, LatBwdKeysLayout::LAUNCH, s>>>(g, rq_, gkv_, lat_lse, dlat, delta, part, n_split_keys);
+    return cudaGetLastError();
+  }
+}
+
 // forward: up to 512 chunks (more than 64: the two-pass kernel over 64-key tiles)
 bool latent_tc_fwd_ok(const Geom& g) {
   return !force_simt() && g.ldh <= 64 && g.ldh % 8 == 0 && g.Nc <= 512 && g.Tq >= 1;

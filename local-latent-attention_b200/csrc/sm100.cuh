@@ -49,6 +49,13 @@ bool latent_tc_ok(const Geom& g);
 int latent_tc_splits(const Geom& g);
 cudaError_t launch_latent_bwd_tc(const Geom& g, const void* rq, const void* gkv, const float* lat_lse,
                                  const float* dlat, void* drq, float* part, int n_split, cudaStream_t s);
+// Latent backward on tensor cores for 64 < Nc <= 512 (bf16, latent head dim
+// <= 64): a rows kernel (drq, and delta [B,Lh,Tq] fp32 into `delta`) then a
+// keys kernel (dgk/dgv partials [n_split_keys][B][Nc][2][Ld] into `part`)
+bool latent_tc_long_ok(const Geom& g);
+cudaError_t launch_latent_bwd_tc_long(const Geom& g, const void* rq, const void* gkv, const float* lat_lse,
+                                      const float* dlat, void* drq, float* delta, float* part, int n_split_keys,
+                                      cudaStream_t s);
 // Latent forward on tensor cores (bf16, latent head dim <= 64, up to 512
 // chunks): lat [B,Tq,Ld], lat_lse [B,Lh,Tq]
 bool latent_tc_fwd_ok(const Geom& g);

@@ -95,3 +95,28 @@ def test_latent_fwd_tc_long(case):
     assert torch.equal(fin, torch.isfinite(lse))
     if fin.any():
         assert (lse[fin] - simt[4][fin]).abs().max().item() < 1e-3
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_latent_bwd_tc_long(case):
+    """Every gradient of the block op, tensor-core latent kernels against the
+    SIMT ones (which the parity suite holds to the oracle)."""
+    B, T, Nl, ldh, Lh, QB = case
+    inp = _inputs(B, T, Nl, ldh, Lh, QB)
+    _, gt = _run(inp, Lh, Nl, QB, False, backward=True)
+    assert _fault() == 0
+    _, gr = _run(inp, Lh, Nl, QB, True, backward=True)
+    names = ["dqkv", "drq", "dgkv", "dw_rout", "db_rout", "dg_local", "dg_remote", "db_qkv"]
+    for name, a, b_ in zip(names, gt, gr):
+        a, b_ = a.float(), b_.float()
+        assert rel_err(a, b_) < TOL[torch.bfloat16], (name, rel_err(a, b_))
+        assert frob_err(a, b_) < TOL[torch.bfloat16], (name, frob_err(a, b_))
+
+
+def test_latent_bwd_tc_long_deterministic():
+    inp = _inputs(1, 8192, 512, 32, 2, 0)
+    _, g1 = _run(inp, 2, 512, 0, False, backward=True)
+    _, g2 = _run(inp, 2, 512, 0, False, backward=True)
+    assert _fault() == 0
+    for a, b_ in zip(g1, g2):
+        assert torch.equal(a, b_)

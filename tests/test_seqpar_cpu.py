@@ -48,7 +48,9 @@ def _worker(rank, world, port, q):
         sums = dnnf.all_reduce(sums)
         w = torch.randn(sums.shape, generator=torch.Generator().manual_seed(1))
         (sums * w).sum().backward()
-        q.put((rank, fwd_ok, mine.grad, sums.detach(), counts, x.grad))
+        # by value (numpy): a tensor would travel as a shared-memory handle
+        # that is gone once this process exits
+        q.put((rank, fwd_ok, *(t.detach().numpy().copy() for t in (mine.grad, sums, counts, x.grad))))
         dist.destroy_process_group()
     except Exception as e:  # pragma: no cover - reported to the parent
         q.put((rank, repr(e)))
@@ -67,7 +69,7 @@ def test_halo_exchange_and_chunk_sums_two_ranks():
     for _ in range(world):
         item = q.get(timeout=120)
         assert len(item) > 2, item
-        res[item[0]] = item[1:]
+        res[item[0]] = (item[1], *(torch.from_numpy(a) for a in item[2:]))
     for p in ps:
         p.join(timeout=60)
     B, T, C, h, Nl = 2, 40, 6, 7, 6

@@ -116,7 +116,9 @@ def _sp_worker(rank, world, port, q):
             yf.backward(g)
             gf = torch.cat([p.grad.float().reshape(-1) for p in m.parameters()])
             out = out + (yf.detach().cpu(), xf.grad.cpu(), gf.cpu())
-        q.put((rank,) + out)
+        # by value (numpy): a tensor would travel as a shared-memory handle
+        # that is gone once this process exits
+        q.put((rank,) + tuple(t.float().numpy().copy() for t in out))
         dist.destroy_process_group()
     except Exception as e:  # pragma: no cover - reported to the parent
         import traceback
@@ -147,7 +149,7 @@ def test_sequence_parallel_two_gpus_equals_one_device():
     for _ in range(world):
         item = q.get(timeout=300)
         assert len(item) > 2, item[1]
-        res[item[0]] = item[1:]
+        res[item[0]] = tuple(torch.from_numpy(a) for a in item[1:])
     for p in ps:
         p.join(timeout=60)
     yf, dxf, gf = res[0][3:]
