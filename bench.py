@@ -1,7 +1,7 @@
 """Benchmark of the LocalLatentAttention block on B200 (one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config cfg2|cfg3|cfg1|p055|p060] [--no-cpu-baseline]
+                    [--config cfg2|cfg3|cfg1|cfg5_nl512|p055|p060] [--no-cpu-baseline]
                     [--no-lm] [--no-presets] [--lm-steps S]
 
 A step is one forward + backward of the drop-in block (LocalLatentAttentionB200:
@@ -75,6 +75,10 @@ CONFIGS = {
                  latent_tokens=64, latent_d_model=64, latent_heads=2, latent_query_block_size=0),
     "cfg3": dict(B=2, T=16384, d_model=1024, n_heads=8, local_window=512, local_block_size=256,
                  latent_tokens=256, latent_d_model=64, latent_heads=2, latent_query_block_size=64),
+    # the shape sweep's 512-latent corner (B*T = 32k, 8 heads of 128, the wide
+    # window): the point where the latent branch is largest
+    "cfg5_nl512": dict(B=4, T=8192, d_model=1024, n_heads=8, local_window=1024, local_block_size=256,
+                       latent_tokens=512, latent_d_model=64, latent_heads=2, latent_query_block_size=0),
     # the block of the reference's training presets (train.py:71-92) at the cfg2 batch
     "p055": dict(B=16, T=2048, d_model=1408, n_heads=16, local_window=256, local_block_size=256,
                  latent_tokens=64, latent_d_model=512, latent_heads=8, latent_query_block_size=0),
