@@ -144,3 +144,19 @@ def test_pool_proj_rejects_bad_args_on_the_host():
         assert msg in L.llattn_last_error().decode(), (msg, L.llattn_last_error())
         assert L.llattn_pool_proj_bwd(ctypes.byref(dims), z, p, p, ldz, None) == 1
         assert msg in L.llattn_last_error().decode(), (msg, L.llattn_last_error())
+
+
+@pytest.mark.parametrize("T,Nl,QB", [(8192, 512, 0), (16384, 256, 64), (1000, 100, 0)])
+def test_workspace_holds_the_long_latent_regions(T, Nl, QB):
+    """Past 64 chunks the tensor-core latent backward needs delta [B, Lh, Tq]
+    fp32 and one dgk/dgv partial [B, Nc, 2, Ld] per row split of its keys
+    kernel (splits: about two waves of (128-key tile, split, head, b) CTAs
+    on 148 SMs); the workspace must hold both beside everything else."""
+    B, Lh, ldh = 4, 2, 32
+    dims = _lib.make_dims(B, T, 8, 128, Lh, ldh, 1024, 256, Nl, QB, _lib.BF16)
+    g = _lib.geometry(dims)
+    nc, tq, Ld = g.n_chunks, g.n_qrows, Lh * ldh
+    assert nc > 64
+    splits = max(1, min(-(-tq // 64), (2 * 148) // (B * Lh * -(-nc // 128))))
+    need = 4 * B * Lh * tq + 4 * splits * B * nc * 2 * Ld
+    assert _lib.lib().llattn_bwd_workspace_bytes(ctypes.byref(dims)) >= need
