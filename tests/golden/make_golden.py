@@ -46,6 +46,13 @@ SMALL = {
     "more_latents_than_T": (dict(B=1, T=20, d_model=16, n_heads=2, local_window=5,
                                  local_block_size=8, latent_tokens=64, latent_d_model=8,
                                  latent_heads=2), 0.0),
+    # more than one 64-chunk key tile (100 chunks of 3 tokens; 150 chunks of 2
+    # with query blocks of 8 and a 48-wide latent head)
+    "many_chunks": (dict(B=1, T=300, d_model=32, n_heads=2, local_window=16, local_block_size=32,
+                         latent_tokens=100, latent_d_model=64, latent_heads=2), 0.0),
+    "many_chunks_qblocks": (dict(B=2, T=300, d_model=32, n_heads=2, local_window=16, local_block_size=32,
+                                 latent_tokens=150, latent_d_model=48, latent_heads=1,
+                                 latent_query_block_size=8), 0.0),
 }
 
 CFG1 = dict(B=2, T=512, d_model=256, n_heads=4, local_window=128, local_block_size=256,
