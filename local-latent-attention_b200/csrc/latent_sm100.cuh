@@ -1,5 +1,9 @@
-// Backward of the latent branch on the tensor cores (included by
-// local_sm100.cu), for at most 64 chunks (one key tile), bf16 activations and
+// Latent-branch kernels on the tensor cores (included by local_sm100.cu),
+// bf16 activations, latent head dims up to 64: for at most 64 chunks a
+// backward and a forward that hold one key tile; past 64 chunks (up to 512)
+// a two-pass forward and a rows / keys backward pair, further down.
+//
+// Backward for at most 64 chunks (one key tile), bf16 activations and
 // latent head dims up to 64: LDH = 32, or 64 for 32 < ldh <= 64 (ldh a
 // multiple of 8; the columns past ldh are zero in every operand). Math as
 // the SIMT kernel of latent.cu: with P = softmax(lat_scale rq.gk) over chunks

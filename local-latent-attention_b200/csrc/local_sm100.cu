@@ -1,10 +1,12 @@
 // Tensor-core (tcgen05 + TMA) kernels of the local branch and of the
 // r_out / gate backward for bf16 activations on sm_100a, and their host-side
 // launchers (tensor maps, shared-memory sizing). The kernels live in:
-//   local_sm100_fwd_pp.cuh  forward, two 128-query tiles per CTA, fused
-//                           remote projection + gate + mix epilogue
+//   local_sm100_fwd_pp.cuh  forward, one 128-query tile per CTA and two CTAs
+//                           per SM (two tiles per CTA with LLATTN_FWD_PAIR=1),
+//                           fused remote projection + gate + mix epilogue
 //   local_sm100_bwd.cuh     dq (units of query tiles) and dk/dv (units of key tiles), persistent
 //   gate_sm100.cuh          gate / r_out backward and the dW_rout GEMM
+//   latent_sm100.cuh        latent attention forward / backward (up to 512 chunks)
 // Windowed causal mask of the reference (models.py:232-305): key j is
 // visible from query t iff 0 < t-j <= W and j >= qs(t) - W + 1.
 //
