@@ -20,10 +20,13 @@ CASES = [
     (torch.bfloat16, 1536, 2, 128, 256, 256, 32, 2, 32, 0),   # fused gate epilogue
     (torch.bfloat16, 1536, 2, 88, 300, 200, 40, 8, 64, 64),   # padded head dim, general path, query blocks
     (torch.float32, 1200, 2, 64, 128, 256, 16, 2, 16, 0),     # exact SIMT path
+    (torch.bfloat16, 1536, 2, 128, 256, 256, 200, 2, 32, 0),  # 192 chunks: the tensor-core long-latent kernels
+    (torch.bfloat16, 1536, 2, 64, 128, 256, 300, 1, 64, 64),  # 256 chunks with query blocks
 ]
 
 
-@pytest.mark.parametrize("case", CASES, ids=["bf16-fused", "bf16-general-qb", "fp32"])
+@pytest.mark.parametrize("case", CASES, ids=["bf16-fused", "bf16-general-qb", "fp32", "bf16-long-latent",
+                                             "bf16-long-latent-qb"])
 def test_shards_with_halo_equal_the_whole_sequence(case):
     from llattn_b200.seqpar import halo_rows
 
