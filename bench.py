@@ -33,6 +33,9 @@ Keys beyond the base contract:
   kernels       per-kernel-group event times (ms per step) and launch counts
   graphed       the same step captured once as a CUDA graph and replayed
                 (1 GPU): the launch-overhead-free time, for small shapes
+  configs       cfg3 (B2 T16384, 256 chunks, query blocks of 64) and cfg5_nl512
+                (B4 T8192 W1024, 512 chunks) measured the same way, with their
+                kernel groups (rank 0, 1 GPU each)
   presets       the block at the reference's training presets (train.py:71-92:
                 0.55b d1408 H16 hd88 latent 512/8 heads, 0.60b d1536 H16 hd96
                 latent 384/8 heads) at B16 x T2048, with their kernel groups
@@ -539,9 +542,11 @@ def run_ours(args):
     value = tokens / (ms / 1e3)
     e2e_value = tokens / (ms_e2e / 1e3)
 
-    presets = None
+    presets = sweep = None
     if rank == 0 and not args.no_presets and args.config in ("cfg2",):
         presets = {name: measure_block_point(name, dev, args.steps) for name in ("p055", "p060")}
+        # the long-context and 512-latent configs beside the headline one
+        sweep = {name: measure_block_point(name, dev, args.steps) for name in ("cfg3", "cfg5_nl512")}
     barrier()
     del m, params, x, g, xs, gs, flat
     torch.cuda.empty_cache()
@@ -640,6 +645,7 @@ def run_ours(args):
         "clocks": clk,
         "graphed": graphed,
         "presets": presets,
+        "configs": sweep,
         "lm": lm,
         "lm_0.55b": lm055,
     }
